@@ -1,0 +1,62 @@
+"""tcgen05 BF16 GEMM vs an fp32 torch reference (all tile configs)."""
+import pytest
+import torch
+
+from vllm_sm70_b200.ops import linear
+
+pytestmark = pytest.mark.gpu
+
+CFGS = {"n256": 0, "n128": 1, "swap16": 2, "swap32": 3, "swap64": 4}
+
+
+def _ref(a, w):
+    return a.float() @ w.float().t()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 4096), (300, 1000, 520),
+                                   (1, 4096, 4096), (17, 6144, 4096), (64, 384, 128),
+                                   (1024, 1024, 1024)])
+@pytest.mark.parametrize("cfg", list(CFGS))
+def test_gemm_configs(b200_ops, M, N, K, cfg, rel_err):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    if cfg.startswith("swap") and M > int(cfg[4:]) * 8:
+        pytest.skip("swap configs target small M")
+    out = linear.gemm(a, w, cfg=CFGS[cfg])
+    torch.cuda.synchronize()
+    ref = _ref(a, w)
+    assert rel_err(out, ref) < 1e-2, (M, N, K, cfg)
+
+
+def test_gemm_auto_and_strided(b200_ops, rel_err):
+    torch.manual_seed(1)
+    big = torch.randn(64, 4096 + 64, device="cuda", dtype=torch.bfloat16)
+    a = big[:, :4096]  # leading dim 4160
+    w = torch.randn(2048, 4096, device="cuda", dtype=torch.bfloat16) * 0.02
+    out = linear.gemm(a, w)
+    assert rel_err(out, _ref(a, w)) < 1e-2
+
+
+@pytest.mark.parametrize("M", [1, 40, 256, 777])
+def test_gemm_silu_mul(b200_ops, M, rel_err):
+    torch.manual_seed(2)
+    K, N = 512, 768
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wg = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    wu = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    wi = linear.interleave_gate_up(wg, wu)
+    out = linear.gemm_silu_mul(a, wi)
+    g = a.float() @ wg.float().t()
+    u = a.float() @ wu.float().t()
+    ref = g * torch.sigmoid(g) * u
+    assert rel_err(out, ref) < 2e-2
+
+
+def test_gemm_deterministic(b200_ops):
+    torch.manual_seed(3)
+    a = torch.randn(512, 1024, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(2048, 1024, device="cuda", dtype=torch.bfloat16)
+    o1 = linear.gemm(a, w)
+    o2 = linear.gemm(a, w)
+    assert torch.equal(o1, o2)

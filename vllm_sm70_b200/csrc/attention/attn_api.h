@@ -1,0 +1,29 @@
+// Host API of the paged attention kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+struct AttnArgs {
+  const void* q;        // [T, Hq, D] bf16, token stride q_stride_t elements
+  const void* k_cache;  // [num_blocks, Hkv, block_size, D] bf16
+  const void* v_cache;
+  void* out;            // [T, Hq, D] bf16, token stride o_stride_t elements
+  const int* block_table;  // [num_seqs, max_blocks]
+  const int* seq_lens;     // [num_seqs]
+  const int* cu_q;         // [num_seqs + 1]
+  const float* sinks;      // [Hq] or nullptr
+  float* part_o;           // split-KV partial outputs [splits, T, Hq, D] (decode only)
+  float* part_ml;          // [splits, T, Hq, 2]
+  int num_seqs, num_tokens, Hq, Hkv, head_dim, block_size, max_blocks;
+  int max_q_len;  // max tokens per sequence in this batch (grid sizing)
+  int window;     // sliding window (0 = full)
+  int q_stride_t, o_stride_t;
+  float scale;
+  bool decode;     // use the decode (1-warp, split-KV) variant
+  int num_splits;  // decode split-KV factor (1 = none)
+};
+
+void paged_attention_launch(const AttnArgs& a, cudaStream_t stream);
+
+}  // namespace b200

@@ -1,0 +1,465 @@
+// Paged flash attention over a block table (prefill, chunked prefill, decode,
+// spec-verify), GQA-packed: one CTA serves one KV head of one sequence and
+// packs (query token x query head of the group) into the MMA row dimension,
+// so each K/V tile is read once for the whole GQA group.
+//
+//   q        [T, Hq, D]                       bf16 (RoPE already applied)
+//   k_cache  [num_blocks, Hkv, BS, D]          bf16 (head-major inside a block:
+//   v_cache  [num_blocks, Hkv, BS, D]          one (block, head) is BS*D contiguous)
+//   block_table [num_seqs, max_blocks] int32, seq_lens [num_seqs] int32 (context
+//   length including this step's tokens), cu_q [num_seqs + 1] int32.
+//   Query token j of sequence s sits at absolute position seq_len - q_len + j and
+//   attends keys [max(0, pos - window + 1), pos]. Optional per-head sink logits
+//   join the softmax denominator.
+//
+// Prefill variant: 4 warps x 16 rows, K/V tiles of 64 keys shared through smem.
+// Decode variant: 1 warp x 16 rows, tiles of 32 keys, the key range split over
+// grid.z with a deterministic (index-order) combine kernel when splits > 1.
+//
+// Math on mma.sync.m16n8k16 (bf16 in, fp32 acc) with ldmatrix from XOR-swizzled
+// smem; online softmax in base 2. The decode path is HBM-bound (K/V bytes), so
+// the legacy MMA rate is not its limiter.
+//
+// Reference parity: Flash-V100 paged decode / prefill / verify
+// (sm70/csrc/flash_v100/flash_decode_paged.cu:640-860,1421-1528,2061-2450;
+// fused_mha_forward_paged.cu:357; verify_decode.cu:133-368), which uses
+// m8n8k4/WMMA on sm_70 and an LBNHC cache; here the cache is [blk, Hkv, BS, D].
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "attention/attn_api.h"
+
+namespace b200 {
+namespace {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
+  const int sz = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                            uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                  uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Byte offset of 16-byte chunk `ch` of row `r` in a swizzled tile whose rows
+// hold D bf16 (D/8 chunks).
+template <int D>
+__device__ __forceinline__ uint32_t swz(int r, int ch) {
+  return (uint32_t)(r * (D * 2) + ((ch ^ (r & 7)) << 4));
+}
+
+struct Params {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  __nv_bfloat16* out;
+  const int* block_table;
+  const int* seq_lens;
+  const int* cu_q;
+  const float* sinks;     // [Hq] or nullptr
+  float* part_o;          // [splits, T, Hq, D] (decode split-KV) or nullptr
+  float* part_ml;         // [splits, T, Hq, 2]
+  int num_seqs, Hq, Hkv, block_size, max_blocks, window;
+  int q_stride_t, o_stride_t;  // element strides between tokens
+  float scale_log2;            // softmax scale * log2(e)
+  int num_splits;              // decode split-KV
+  int rows_per_seq_max;        // max over seqs of q_len*G (grid sizing)
+};
+
+// One "worker" = NW warps sharing one K/V pipeline and owning 16*NW rows.
+template <int D, int KT, int NW, int STAGES, bool DECODE>
+__global__ void __launch_bounds__(NW * 32)
+paged_attn_kernel(const Params p) {
+  constexpr int ROWS = 16 * NW;
+  constexpr int CH = D / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + ROWS * D * 2;  // STAGES x (K tile, V tile)
+  constexpr int kTileBytes = KT * D * 2;
+
+  const int seq = blockIdx.y;
+  const int kvh = blockIdx.z % p.Hkv;
+  const int split = DECODE ? blockIdx.z / p.Hkv : 0;
+  const int G = p.Hq / p.Hkv;
+  const int q0 = p.cu_q[seq];
+  const int q_len = p.cu_q[seq + 1] - q0;
+  const int seq_len = p.seq_lens[seq];
+  const int rows_total = q_len * G;
+  const int n_row_tiles = (rows_total + ROWS - 1) / ROWS;
+  // Later row tiles carry more causal work: schedule them first.
+  const int rt = DECODE ? blockIdx.x : (int)gridDim.x - 1 - (int)blockIdx.x;
+  if (rt >= n_row_tiles || q_len == 0) return;
+  const int row0 = rt * ROWS;
+
+  const int tid = threadIdx.x;
+  const int warp = tid / 32;
+  const int lane = tid % 32;
+
+  // Key range for this CTA.
+  const int first_pos = seq_len - q_len + row0 / G;
+  const int last_row = min(row0 + ROWS, rows_total) - 1;
+  const int last_pos = seq_len - q_len + last_row / G;
+  int k_begin = 0;
+  if (p.window > 0) k_begin = max(0, first_pos - p.window + 1);
+  int k_end = last_pos + 1;  // exclusive
+  if (DECODE && p.num_splits > 1) {
+    const int span = k_end - k_begin;
+    const int per = ((span + p.num_splits - 1) / p.num_splits + KT - 1) / KT * KT;
+    const int b = k_begin + split * per;
+    const int e = min(k_end, b + per);
+    k_begin = b;
+    k_end = e;
+  }
+  k_begin = (k_begin / KT) * KT;
+  const int n_tiles = k_end > k_begin ? (k_end - k_begin + KT - 1) / KT : 0;
+
+  // ---- load Q rows (row r -> token r / G, head r % G) into smem
+  for (int c = tid; c < ROWS * CH; c += NW * 32) {
+    const int r = c / CH, ch = c % CH;
+    const int gr = row0 + r;
+    const bool valid = gr < rows_total;
+    const int tok = valid ? gr / G : 0;
+    const int h = kvh * G + (valid ? gr % G : 0);
+    const __nv_bfloat16* src = p.q + (size_t)(q0 + tok) * p.q_stride_t + (size_t)h * D + ch * 8;
+    cp_async_16(smem_addr(sQ) + swz<D>(r, ch), valid ? (const void*)src : (const void*)p.q, valid);
+  }
+  cp_async_commit();
+
+  const int* bt = p.block_table + (size_t)seq * p.max_blocks;
+  auto load_tile = [&](int tile, int buf) {
+    const int kbase = k_begin + tile * KT;
+    uint8_t* sK = sKV + buf * 2 * kTileBytes;
+    uint8_t* sV = sK + kTileBytes;
+    for (int c = tid; c < KT * CH; c += NW * 32) {
+      const int r = c / CH, ch = c % CH;
+      const int key = kbase + r;
+      const bool valid = key < k_end;
+      size_t off = 0;
+      if (valid) {
+        const int blk = bt[key / p.block_size];
+        off = (((size_t)blk * p.Hkv + kvh) * p.block_size + key % p.block_size) * D + ch * 8;
+      }
+      cp_async_16(smem_addr(sK) + swz<D>(r, ch), p.k_cache + off, valid);
+      cp_async_16(smem_addr(sV) + swz<D>(r, ch), p.v_cache + off, valid);
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < n_tiles) load_tile(s, s);
+    cp_async_commit();
+  }
+
+  // Q fragments for this warp's 16 rows.
+  cp_async_wait<STAGES - 1>();
+  __syncthreads();
+  uint32_t qf[D / 16][4];
+  {
+    const int r = warp * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int ch = kk * 2 + lane / 16;
+      ldmatrix_x4(smem_addr(sQ) + swz<D>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    }
+  }
+
+  // Row bookkeeping: this thread holds rows (g) and (g + 8) of the warp tile.
+  const int g = lane / 4, t4 = lane % 4;
+  int row_pos[2];
+  bool row_valid[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int gr = row0 + warp * 16 + g + h * 8;
+    row_valid[h] = gr < rows_total;
+    row_pos[h] = seq_len - q_len + (row_valid[h] ? gr / G : 0);
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int buf = tile % STAGES;
+    {
+      const int nt = tile + STAGES - 1;
+      if (nt < n_tiles) load_tile(nt, nt % STAGES);
+      cp_async_commit();
+    }
+    cp_async_wait<STAGES - 1>();
+    __syncthreads();
+    const uint8_t* sK = sKV + buf * 2 * kTileBytes;
+    const uint8_t* sV = sK + kTileBytes;
+    const int kbase = k_begin + tile * KT;
+
+    // S = Q K^T : 16 rows x KT keys per warp
+    float s[KT / 8][4];
+#pragma unroll
+    for (int n = 0; n < KT / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int n2 = 0; n2 < KT / 16; ++n2) {
+        const int key = n2 * 16 + (lane % 8) + (lane / 16) * 8;
+        const int ch = kk * 2 + (lane / 8) % 2;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(smem_addr(sK) + swz<D>(key, ch), b0, b1, b2, b3);
+        mma_bf16(s[2 * n2], qf[kk], b0, b1);
+        mma_bf16(s[2 * n2 + 1], qf[kk], b2, b3);
+      }
+    }
+
+    // Mask + online softmax (base 2).
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < KT / 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e / 2;
+        const int key = kbase + n * 8 + t4 * 2 + (e & 1);
+        bool ok = row_valid[h] && key <= row_pos[h] && key < k_end;
+        if (p.window > 0) ok = ok && key > row_pos[h] - p.window;
+        const float v = ok ? s[n][e] * p.scale_log2 : -INFINITY;
+        s[n][e] = v;
+        mx[h] = fmaxf(mx[h], v);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2));
+      const float m_new = fmaxf(m_run[h], mx[h]);
+      corr[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[h] - m_new);
+      m_run[h] = m_new;
+      l_run[h] *= corr[h];
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= corr[0];
+      o[i][1] *= corr[0];
+      o[i][2] *= corr[1];
+      o[i][3] *= corr[1];
+    }
+    uint32_t pf[KT / 16][4];
+#pragma unroll
+    for (int n = 0; n < KT / 8; ++n) {
+      float e4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e / 2;
+        e4[e] = (m_run[h] == -INFINITY) ? 0.f : exp2f(s[n][e] - m_run[h]);
+        l_run[h] += e4[e];
+      }
+      const int kk = n / 2, hi = n % 2;
+      pf[kk][hi * 2 + 0] = pack2(e4[0], e4[1]);
+      pf[kk][hi * 2 + 1] = pack2(e4[2], e4[3]);
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < KT / 16; ++kk) {
+#pragma unroll
+      for (int d2 = 0; d2 < D / 16; ++d2) {
+        const int key = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+        const int ch = d2 * 2 + lane / 16;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(smem_addr(sV) + swz<D>(key, ch), b0, b1, b2, b3);
+        mma_bf16(o[2 * d2], pf[kk], b0, b1);
+        mma_bf16(o[2 * d2 + 1], pf[kk], b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // Row sums across the 4 threads of a quad.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffff, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffff, l_run[h], 2);
+  }
+
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (!row_valid[h]) continue;
+    const int gr = row0 + warp * 16 + g + h * 8;
+    const int tok = gr / G;
+    const int head = kvh * G + gr % G;
+    if (DECODE && p.num_splits > 1) {
+      const size_t T = (size_t)p.cu_q[p.num_seqs];
+      const size_t base = ((size_t)split * T + (q0 + tok)) * p.Hq + head;
+      float* dst = p.part_o + base * D;
+      const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        const int d = i * 8 + t4 * 2;
+        *reinterpret_cast<float2*>(dst + d) = make_float2(o[i][2 * h] * inv, o[i][2 * h + 1] * inv);
+      }
+      if (t4 == 0) {
+        p.part_ml[base * 2 + 0] = m_run[h];
+        p.part_ml[base * 2 + 1] = l_run[h];
+      }
+    } else {
+      float denom = l_run[h];
+      if (p.sinks != nullptr) {
+        const float sk = p.sinks[head] * 1.4426950408889634f;  // to base 2
+        const float m = m_run[h];
+        if (m == -INFINITY) {
+          denom = 1.f;  // only the sink: output 0
+        } else {
+          denom += exp2f(sk - m);
+        }
+      }
+      const float inv = denom > 0.f ? 1.f / denom : 0.f;
+      __nv_bfloat16* dst = p.out + (size_t)(q0 + tok) * p.o_stride_t + (size_t)head * D;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        const int d = i * 8 + t4 * 2;
+        *reinterpret_cast<uint32_t*>(dst + d) = pack2(o[i][2 * h] * inv, o[i][2 * h + 1] * inv);
+      }
+    }
+  }
+}
+
+// Merge split-KV partials in split order (deterministic).
+template <int D>
+__global__ void combine_splits_kernel(const Params p, int T) {
+  const int tok = blockIdx.x;
+  const int head = blockIdx.y;
+  const int d = threadIdx.x;
+  float m = -INFINITY;
+  for (int s = 0; s < p.num_splits; ++s) {
+    const size_t base = ((size_t)s * T + tok) * p.Hq + head;
+    const float l = p.part_ml[base * 2 + 1];
+    if (l > 0.f) m = fmaxf(m, p.part_ml[base * 2]);
+  }
+  float denom = 0.f;
+  for (int s = 0; s < p.num_splits; ++s) {
+    const size_t base = ((size_t)s * T + tok) * p.Hq + head;
+    const float l = p.part_ml[base * 2 + 1];
+    if (l > 0.f) denom += l * exp2f(p.part_ml[base * 2] - m);
+  }
+  if (p.sinks != nullptr && m != -INFINITY) denom += exp2f(p.sinks[head] * 1.4426950408889634f - m);
+  const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  for (int dd = d; dd < D; dd += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < p.num_splits; ++s) {
+      const size_t base = ((size_t)s * T + tok) * p.Hq + head;
+      const float l = p.part_ml[base * 2 + 1];
+      if (l > 0.f) acc += p.part_o[base * D + dd] * l * exp2f(p.part_ml[base * 2] - m);
+    }
+    p.out[(size_t)tok * p.o_stride_t + (size_t)head * D + dd] = __float2bfloat16_rn(acc * inv);
+  }
+}
+
+template <int D, int KT, int NW, int STAGES, bool DECODE>
+void launch_attn(const Params& p, cudaStream_t stream) {
+  constexpr int ROWS = 16 * NW;
+  constexpr int smem = ROWS * D * 2 + STAGES * 2 * KT * D * 2;
+  auto kernel = paged_attn_kernel<D, KT, NW, STAGES, DECODE>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  const int row_tiles = (p.rows_per_seq_max + ROWS - 1) / ROWS;
+  dim3 grid(row_tiles, p.num_seqs, p.Hkv * (DECODE ? p.num_splits : 1));
+  kernel<<<grid, NW * 32, smem, stream>>>(p);
+}
+
+}  // namespace
+
+void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
+  if (a.Hq % a.Hkv != 0) throw std::runtime_error("paged_attention: Hq % Hkv != 0");
+  if (a.block_size % 8 != 0) throw std::runtime_error("paged_attention: block_size % 8 != 0");
+  Params p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  p.k_cache = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
+  p.v_cache = reinterpret_cast<const __nv_bfloat16*>(a.v_cache);
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.block_table = a.block_table;
+  p.seq_lens = a.seq_lens;
+  p.cu_q = a.cu_q;
+  p.sinks = a.sinks;
+  p.part_o = a.part_o;
+  p.part_ml = a.part_ml;
+  p.num_seqs = a.num_seqs;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.block_size = a.block_size;
+  p.max_blocks = a.max_blocks;
+  p.window = a.window;
+  p.q_stride_t = a.q_stride_t;
+  p.o_stride_t = a.o_stride_t;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.num_splits = a.decode ? (a.num_splits > 0 ? a.num_splits : 1) : 1;
+  p.rows_per_seq_max = a.max_q_len * (a.Hq / a.Hkv);
+  if (p.num_splits > 1 && (a.part_o == nullptr || a.part_ml == nullptr))
+    throw std::runtime_error("paged_attention: split-KV needs partial buffers");
+  if (a.head_dim == 128) {
+    if (a.decode)
+      launch_attn<128, 32, 1, 3, true>(p, stream);
+    else
+      launch_attn<128, 64, 4, 2, false>(p, stream);
+  } else if (a.head_dim == 256) {
+    if (a.decode)
+      launch_attn<256, 32, 1, 2, true>(p, stream);
+    else
+      launch_attn<256, 32, 4, 2, false>(p, stream);
+  } else if (a.head_dim == 64) {
+    if (a.decode)
+      launch_attn<64, 32, 1, 3, true>(p, stream);
+    else
+      launch_attn<64, 64, 4, 2, false>(p, stream);
+  } else {
+    throw std::runtime_error("paged_attention: head_dim must be 64, 128 or 256");
+  }
+  if (p.num_splits > 1) {
+    dim3 grid(a.num_tokens, a.Hq);
+    if (a.head_dim == 128) combine_splits_kernel<128><<<grid, 128, 0, stream>>>(p, a.num_tokens);
+    else if (a.head_dim == 256) combine_splits_kernel<256><<<grid, 128, 0, stream>>>(p, a.num_tokens);
+    else combine_splits_kernel<64><<<grid, 64, 0, stream>>>(p, a.num_tokens);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("paged_attention launch: ") + cudaGetErrorString(e));
+}
+
+}  // namespace b200

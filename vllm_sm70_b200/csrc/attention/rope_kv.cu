@@ -1,0 +1,140 @@
+// Fused (optional per-head q/k RMSNorm) + NeoX RoPE + paged KV-cache write.
+//
+// qkv [T, (Hq + 2 Hkv) * D] bf16 is the QKV projection output. In place, q and
+// k are normalised (when q_norm / k_norm are given) and rotated; k and v are
+// then written to k_cache / v_cache [num_blocks, Hkv, BS, D] at
+// slot_mapping[t] = block * BS + offset (negative slot: token not cached).
+// The attention kernel reads q straight from qkv with a token stride of
+// (Hq + 2 Hkv) * D, so no separate q buffer is written.
+//
+// One warp per (token, head); D/64 rotation pairs per lane.
+//
+// Reference parity: the Triton q/k-norm + RoPE + KV writer
+// (sm70/vllm_sm70/flint/qk_norm_rope_kv.py:55-148), here as a CUDA kernel.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <stdexcept>
+
+#include "ops_api.h"
+
+namespace b200 {
+namespace {
+
+template <int D>
+__global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, const int64_t* __restrict__ pos,
+                               const float* __restrict__ cos_sin, __nv_bfloat16* __restrict__ kc,
+                               __nv_bfloat16* __restrict__ vc, const int64_t* __restrict__ slots,
+                               const __nv_bfloat16* __restrict__ q_norm,
+                               const __nv_bfloat16* __restrict__ k_norm, int T, int Hq, int Hkv,
+                               int BS, float eps, int rot_dim) {
+  constexpr int P = D / 64;  // pairs per lane (first-half index i, second-half i + D/2)
+  const int warps_per_block = blockDim.x / 32;
+  const int gw = blockIdx.x * warps_per_block + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int heads = Hq + 2 * Hkv;
+  const int t = gw / heads;
+  const int h = gw % heads;
+  if (t >= T) return;
+  const size_t row = (size_t)t * heads * D;
+  __nv_bfloat16* hp = qkv + row + (size_t)h * D;
+  const bool is_q = h < Hq;
+  const bool is_k = !is_q && h < Hq + Hkv;
+  const bool is_v = h >= Hq + Hkv;
+  const int64_t slot = slots ? slots[t] : -1;
+
+  float a[P], b[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int i = lane + 32 * j;
+    a[j] = __bfloat162float(hp[i]);
+    b[j] = __bfloat162float(hp[i + D / 2]);
+  }
+  if (!is_v) {
+    const __nv_bfloat16* nw = is_q ? q_norm : k_norm;
+    if (nw != nullptr) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < P; ++j) ss += a[j] * a[j] + b[j] * b[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+      const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        const int i = lane + 32 * j;
+        a[j] = __bfloat162float(__float2bfloat16_rn(a[j] * inv)) * __bfloat162float(nw[i]);
+        b[j] = __bfloat162float(__float2bfloat16_rn(b[j] * inv)) * __bfloat162float(nw[i + D / 2]);
+      }
+    }
+    // NeoX rotation over the first rot_dim dims (pairs i, i + rot_dim/2).
+    const int half = rot_dim / 2;
+    const float* cs = cos_sin + (size_t)pos[t] * rot_dim;
+    if (rot_dim == D) {
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        const int i = lane + 32 * j;
+        const float c = cs[i], s = cs[half + i];
+        const float x1 = a[j], x2 = b[j];
+        a[j] = x1 * c - x2 * s;
+        b[j] = x2 * c + x1 * s;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int i = lane + 32 * j;
+      hp[i] = __float2bfloat16_rn(a[j]);
+      hp[i + D / 2] = __float2bfloat16_rn(b[j]);
+    }
+    if (rot_dim != D) {
+      // Partial rotary (rot_dim < D): rotate pairs (i, i + half) for i < half.
+      __syncwarp();
+      for (int i = lane; i < half; i += 32) {
+        const float c = cs[i], s = cs[half + i];
+        const float x1 = __bfloat162float(hp[i]), x2 = __bfloat162float(hp[i + half]);
+        hp[i] = __float2bfloat16_rn(x1 * c - x2 * s);
+        hp[i + half] = __float2bfloat16_rn(x2 * c + x1 * s);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        const int i = lane + 32 * j;
+        a[j] = __bfloat162float(hp[i]);
+        b[j] = __bfloat162float(hp[i + D / 2]);
+      }
+    }
+  }
+  if ((is_k || is_v) && slot >= 0) {
+    const int kvh = is_k ? h - Hq : h - Hq - Hkv;
+    const int64_t blk = slot / BS, off = slot % BS;
+    __nv_bfloat16* dst = (is_k ? kc : vc) + ((blk * Hkv + kvh) * BS + off) * D;
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int i = lane + 32 * j;
+      dst[i] = __float2bfloat16_rn(a[j]);
+      dst[i + D / 2] = __float2bfloat16_rn(b[j]);
+    }
+  }
+}
+
+}  // namespace
+
+void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, void* k_cache,
+                          void* v_cache, const int64_t* slots, const void* q_norm,
+                          const void* k_norm, int T, int Hq, int Hkv, int D, int BS, float eps,
+                          int rot_dim, cudaStream_t stream) {
+  if (T <= 0) return;
+  const long warps = (long)T * (Hq + 2 * Hkv);
+  const int wpb = 8;
+  const long blocks = (warps + wpb - 1) / wpb;
+#define B200_ROPE(DD)                                                                           \
+  rope_kv_kernel<DD><<<blocks, wpb * 32, 0, stream>>>(                                          \
+      (__nv_bfloat16*)qkv, pos, cos_sin, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slots, \
+      (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, T, Hq, Hkv, BS, eps, rot_dim)
+  if (D == 128) B200_ROPE(128);
+  else if (D == 256) B200_ROPE(256);
+  else if (D == 64) B200_ROPE(64);
+  else throw std::runtime_error("rope_kv_write: head_dim must be 64, 128 or 256");
+#undef B200_ROPE
+}
+
+}  // namespace b200

@@ -1,0 +1,259 @@
+// torch.ops._b200_C: the op registry of the B200 kernel library.
+//
+// Reference parity: TORCH_LIBRARY(_sm70_C) + abi_version
+// (sm70/csrc/torch_bindings_sm70.cpp:16-40). Each area adds a FRAGMENT; this
+// file holds the core ops (GEMM, norm, RoPE/KV, attention, sampling, misc).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+#include <torch/torch.h>
+
+#include "ops_api.h"
+
+namespace b200 {
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+#define CHECK_ROWMAJOR(x) \
+  TORCH_CHECK((x).dim() == 2 && (x).stride(1) == 1, #x " must be 2-D with unit inner stride")
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+int64_t abi_version() { return kAbiVersion; }
+
+void init_device(int64_t device) { (void)device_status_ptr((int)device); }
+
+int64_t read_status(int64_t device, bool clear) {
+  unsigned int* p = device_status_ptr((int)device);
+  unsigned int v = 0;
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  C10_CUDA_CHECK(cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost));
+  if (clear && v) C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(v)));
+  return (int64_t)v;
+}
+
+void gemm_bf16_out(at::Tensor& out, const at::Tensor& a, const at::Tensor& w, int64_t cfg) {
+  CHECK_CUDA(a); CHECK_CUDA(w); CHECK_CUDA(out);
+  CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out);
+  CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(a.size(1) == w.size(1), "gemm_bf16: K mismatch");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0), "gemm_bf16: out shape");
+  c10::cuda::CUDAGuard g(a.device());
+  gemm_bf16_launch(a.data_ptr(), w.data_ptr(), out.data_ptr(), (int)a.size(0), (int)w.size(0),
+                   (int)a.size(1), (int)a.stride(0), (int)w.stride(0), (int)out.stride(0), kEpiNone,
+                   (int)cfg, device_status_ptr(a.get_device()), cur_stream());
+}
+
+at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& w, int64_t cfg) {
+  auto out = at::empty({a.size(0), w.size(0)}, a.options());
+  gemm_bf16_out(out, a, w, cfg);
+  return out;
+}
+
+// w_interleaved rows are [gate 64 | up 64] blocks (prepare with
+// interleave_gate_up); output has w.size(0) / 2 columns.
+void gemm_bf16_silu_mul_out(at::Tensor& out, const at::Tensor& a, const at::Tensor& w,
+                            int64_t cfg) {
+  CHECK_CUDA(a); CHECK_CUDA(w); CHECK_CUDA(out);
+  CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out);
+  CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(a.size(1) == w.size(1), "gemm_bf16_silu_mul: K mismatch");
+  TORCH_CHECK(w.size(0) % 128 == 0, "gemm_bf16_silu_mul: N must be a multiple of 128");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0) / 2,
+              "gemm_bf16_silu_mul: out shape");
+  c10::cuda::CUDAGuard g(a.device());
+  const int M = (int)a.size(0), N = (int)w.size(0), K = (int)a.size(1);
+  int c = (int)cfg;
+  if (c < 0) c = gemm_bf16_pick_config(M, N, K, kEpiSiluMul, 148);
+  if (c != kCfgN128 && c != kCfgN256) {
+    // Small-M configs do not fuse the activation: GEMM then silu_mul.
+    auto tmp = at::empty({a.size(0), w.size(0)}, a.options());
+    gemm_bf16_launch(a.data_ptr(), w.data_ptr(), tmp.data_ptr(), M, N, K, (int)a.stride(0),
+                     (int)w.stride(0), (int)tmp.stride(0), kEpiNone, c,
+                     device_status_ptr(a.get_device()), cur_stream());
+    // De-interleave on the fly is not supported by silu_mul: callers that
+    // reach here use the block layout, so undo it with a view.
+    auto t4 = tmp.view({M, N / 128, 2, 64});
+    auto gate = t4.select(2, 0).reshape({M, N / 2});
+    auto up = t4.select(2, 1).reshape({M, N / 2});
+    auto gu = at::cat({gate, up}, 1);
+    silu_mul_launch(out.data_ptr(), gu.data_ptr(), M, N / 2, (int)gu.stride(0),
+                    (int)out.stride(0), cur_stream());
+    return;
+  }
+  gemm_bf16_launch(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, (int)a.stride(0),
+                   (int)w.stride(0), (int)out.stride(0), kEpiSiluMul, c,
+                   device_status_ptr(a.get_device()), cur_stream());
+}
+
+int64_t gemm_bf16_config(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  return gemm_bf16_pick_config((int)M, (int)N, (int)K, (int)epi, 148);
+}
+
+void rms_norm(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, double eps) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(out);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "rms_norm: 2-D rows");
+  c10::cuda::CUDAGuard g(x.device());
+  rms_norm_launch(out.data_ptr(), (int)out.stride(0), x.data_ptr(), (int)x.stride(0), w.data_ptr(),
+                  (int)x.size(0), (int)x.size(1), (float)eps, cur_stream());
+}
+
+void fused_add_rms_norm(at::Tensor& x, at::Tensor& residual, const at::Tensor& w, double eps) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(residual); CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && residual.stride(1) == 1,
+              "fused_add_rms_norm: 2-D rows");
+  TORCH_CHECK(x.sizes() == residual.sizes(), "fused_add_rms_norm: shape mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  fused_add_rms_norm_launch(x.data_ptr(), (int)x.stride(0), residual.data_ptr(),
+                            (int)residual.stride(0), w.data_ptr(), (int)x.size(0), (int)x.size(1),
+                            (float)eps, cur_stream());
+}
+
+void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& cos_sin,
+                   at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor& slot_mapping,
+                   int64_t num_q_heads, int64_t num_kv_heads, const c10::optional<at::Tensor>& q_norm,
+                   const c10::optional<at::Tensor>& k_norm, double eps) {
+  CHECK_CUDA(qkv); CHECK_BF16(qkv); CHECK_BF16(k_cache); CHECK_BF16(v_cache);
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slot_mapping.scalar_type() == at::kLong,
+              "rope_kv_write: positions / slot_mapping must be int64");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin fp32");
+  TORCH_CHECK(qkv.is_contiguous() && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "rope_kv_write: contiguous tensors required");
+  TORCH_CHECK(k_cache.dim() == 4, "k_cache must be [blocks, Hkv, BS, D]");
+  const int T = (int)qkv.size(0);
+  const int D = (int)k_cache.size(3);
+  const int BS = (int)k_cache.size(2);
+  TORCH_CHECK(qkv.size(1) == (num_q_heads + 2 * num_kv_heads) * D, "rope_kv_write: qkv width");
+  TORCH_CHECK(positions.numel() >= T && slot_mapping.numel() >= T, "rope_kv_write: lengths");
+  c10::cuda::CUDAGuard g(qkv.device());
+  rope_kv_write_launch(qkv.data_ptr(), positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
+                       k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr<int64_t>(),
+                       q_norm ? q_norm->data_ptr() : nullptr, k_norm ? k_norm->data_ptr() : nullptr,
+                       T, (int)num_q_heads, (int)num_kv_heads, D, BS, (float)eps,
+                       (int)cos_sin.size(1), cur_stream());
+}
+
+void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                     const at::Tensor& v_cache, const at::Tensor& block_table,
+                     const at::Tensor& seq_lens, const at::Tensor& cu_q, int64_t max_q_len,
+                     double scale, int64_t window, const c10::optional<at::Tensor>& sinks,
+                     bool decode, int64_t num_splits, const c10::optional<at::Tensor>& part_o,
+                     const c10::optional<at::Tensor>& part_ml) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(out); CHECK_BF16(k_cache); CHECK_BF16(v_cache);
+  TORCH_CHECK(q.dim() == 3 && out.dim() == 3, "paged_attention: q/out must be [T, H, D]");
+  TORCH_CHECK(q.stride(2) == 1 && q.stride(1) == q.size(2), "paged_attention: q head layout");
+  TORCH_CHECK(out.stride(2) == 1 && out.stride(1) == out.size(2), "paged_attention: out layout");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "paged_attention: caches must be contiguous [blocks, Hkv, BS, D]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  cu_q.scalar_type() == at::kInt,
+              "paged_attention: int32 metadata");
+  TORCH_CHECK(block_table.is_contiguous() && seq_lens.is_contiguous() && cu_q.is_contiguous(),
+              "paged_attention: contiguous metadata");
+  TORCH_CHECK(q.stride(0) % 8 == 0, "paged_attention: q token stride must be 16B aligned");
+  AttnArgs a{};
+  a.q = q.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.out = out.data_ptr();
+  a.block_table = block_table.data_ptr<int>();
+  a.seq_lens = seq_lens.data_ptr<int>();
+  a.cu_q = cu_q.data_ptr<int>();
+  a.sinks = sinks ? sinks->data_ptr<float>() : nullptr;
+  a.part_o = part_o ? part_o->data_ptr<float>() : nullptr;
+  a.part_ml = part_ml ? part_ml->data_ptr<float>() : nullptr;
+  a.num_seqs = (int)seq_lens.size(0);
+  a.num_tokens = (int)q.size(0);
+  a.Hq = (int)q.size(1);
+  a.Hkv = (int)k_cache.size(1);
+  a.head_dim = (int)q.size(2);
+  a.block_size = (int)k_cache.size(2);
+  a.max_blocks = (int)block_table.size(1);
+  a.max_q_len = (int)max_q_len;
+  a.window = (int)window;
+  a.q_stride_t = (int)q.stride(0);
+  a.o_stride_t = (int)out.stride(0);
+  a.scale = (float)scale;
+  a.decode = decode;
+  a.num_splits = (int)num_splits;
+  if (a.num_splits > 1) {
+    TORCH_CHECK(part_o && part_ml, "split-KV decode needs part_o / part_ml");
+    TORCH_CHECK(part_o->numel() >= (int64_t)a.num_splits * a.num_tokens * a.Hq * a.head_dim,
+                "part_o too small");
+    TORCH_CHECK(part_ml->numel() >= (int64_t)a.num_splits * a.num_tokens * a.Hq * 2,
+                "part_ml too small");
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  paged_attention_launch(a, cur_stream());
+}
+
+void argmax(at::Tensor& ids, const c10::optional<at::Tensor>& vals, const at::Tensor& logits,
+            int64_t id_offset) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "argmax: 2-D logits");
+  TORCH_CHECK(ids.scalar_type() == at::kInt, "argmax: ids int32");
+  const bool bf = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf || logits.scalar_type() == at::kFloat, "argmax: bf16 or fp32 logits");
+  c10::cuda::CUDAGuard g(logits.device());
+  argmax_launch(logits.data_ptr(), bf, (int)logits.size(0), (int)logits.size(1),
+                (int)logits.stride(0), ids.data_ptr<int>(),
+                vals ? vals->data_ptr<float>() : nullptr, (int)id_offset, cur_stream());
+}
+
+void silu_mul(at::Tensor& out, const at::Tensor& x) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "silu_mul: 2-D rows");
+  c10::cuda::CUDAGuard g(x.device());
+  silu_mul_launch(out.data_ptr(), x.data_ptr(), (int)x.size(0), (int)(x.size(1) / 2),
+                  (int)x.stride(0), (int)out.stride(0), cur_stream());
+}
+
+void embedding(at::Tensor& out, const at::Tensor& ids, const at::Tensor& table,
+               int64_t vocab_start) {
+  CHECK_CUDA(ids); CHECK_BF16(table); CHECK_BF16(out);
+  TORCH_CHECK(ids.scalar_type() == at::kLong, "embedding: ids int64");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous(), "embedding: contiguous");
+  c10::cuda::CUDAGuard g(ids.device());
+  embedding_launch(out.data_ptr(), ids.data_ptr<int64_t>(), table.data_ptr(), (int)ids.numel(),
+                   (int)table.size(1), vocab_start, vocab_start + table.size(0), cur_stream());
+}
+
+}  // namespace
+}  // namespace b200
+
+TORCH_LIBRARY(_b200_C, m) {
+  m.def("abi_version() -> int", &b200::abi_version);
+  m.def("init_device(int device) -> ()", &b200::init_device);
+  m.def("read_status(int device, bool clear) -> int", &b200::read_status);
+  m.def("gemm_bf16(Tensor a, Tensor w, int cfg=-1) -> Tensor");
+  m.def("gemm_bf16_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
+  m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
+  m.def("gemm_bf16_config(int M, int N, int K, int epi) -> int", &b200::gemm_bf16_config);
+  m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
+  m.def("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()");
+  m.def(
+      "rope_kv_write(Tensor(a!) qkv, Tensor positions, Tensor cos_sin, Tensor(b!) k_cache, "
+      "Tensor(c!) v_cache, Tensor slot_mapping, int num_q_heads, int num_kv_heads, "
+      "Tensor? q_norm, Tensor? k_norm, float eps) -> ()");
+  m.def(
+      "paged_attention(Tensor(a!) out, Tensor q, Tensor k_cache, Tensor v_cache, "
+      "Tensor block_table, Tensor seq_lens, Tensor cu_q, int max_q_len, float scale, int window, "
+      "Tensor? sinks, bool decode, int num_splits, Tensor? part_o, Tensor? part_ml) -> ()");
+  m.def("argmax(Tensor(a!) ids, Tensor(b!)? vals, Tensor logits, int id_offset) -> ()");
+  m.def("silu_mul(Tensor(a!) out, Tensor x) -> ()");
+  m.def("embedding(Tensor(a!) out, Tensor ids, Tensor table, int vocab_start) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
+  m.impl("gemm_bf16", &b200::gemm_bf16);
+  m.impl("gemm_bf16_out", &b200::gemm_bf16_out);
+  m.impl("gemm_bf16_silu_mul_out", &b200::gemm_bf16_silu_mul_out);
+  m.impl("rms_norm", &b200::rms_norm);
+  m.impl("fused_add_rms_norm", &b200::fused_add_rms_norm);
+  m.impl("rope_kv_write", &b200::rope_kv_write);
+  m.impl("paged_attention", &b200::paged_attention);
+  m.impl("argmax", &b200::argmax);
+  m.impl("silu_mul", &b200::silu_mul);
+  m.impl("embedding", &b200::embedding);
+}

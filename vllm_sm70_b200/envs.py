@@ -1,0 +1,133 @@
+"""Single registry of ``VLLM_B200_*`` environment variables.
+
+Reference parity: ``sm70/vllm_sm70/envs.py:34-115`` (getter kinds) and
+``:118-396`` (sections), ``:410-420`` (merge into ``vllm.envs``).
+
+Getter kinds (same semantics as the reference):
+
+* kill switch -- only ``"0"`` acts (turns a fused path OFF); any other value,
+  or unset, leaves the default. The environment can never ENABLE something
+  the typed config disabled.
+* opt-in      -- only ``"1"`` acts (turns an experimental path ON).
+* debug       -- ``"1"`` enables extra logging / checks.
+* tuning      -- free-form string passed through to the native library.
+* path        -- a filesystem path or unset.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from typing import Callable
+
+
+@dataclass(frozen=True)
+class EnvVar:
+    name: str
+    kind: str  # kill | optin | debug | tuning | path | int
+    default: object
+    section: str
+    doc: str
+
+    def get(self):
+        raw = os.environ.get(self.name)
+        if self.kind == "kill":
+            return False if raw == "0" else bool(self.default)
+        if self.kind == "optin":
+            return True if raw == "1" else bool(self.default)
+        if self.kind == "debug":
+            return raw == "1"
+        if self.kind == "int":
+            try:
+                return int(raw) if raw is not None else self.default
+            except ValueError:
+                return self.default
+        return raw if raw is not None else self.default
+
+
+_REGISTRY: dict[str, EnvVar] = {}
+
+
+def _reg(name, kind, default, section, doc):
+    _REGISTRY[name] = EnvVar(name, kind, default, section, doc)
+
+
+# -- plugin ---------------------------------------------------------------
+_reg("VLLM_B200_PLUGIN_STRICT", "kill", True, "plugin",
+     "Fail fast when a plugin area fails to register (0 = warn only).")
+_reg("VLLM_B200_PLUGIN_DEBUG", "debug", False, "plugin", "Verbose plugin logging.")
+_reg("VLLM_B200_SKIP_EXT", "optin", False, "plugin",
+     "Do not load _b200_C (CPU-only tests).")
+# -- kernels (kill switches back to the baseline path) --------------------
+_reg("VLLM_B200_GEMM", "kill", True, "kernels", "tcgen05 BF16 GEMM (0 = torch.matmul).")
+_reg("VLLM_B200_GEMM_SILU_EPILOGUE", "kill", True, "kernels",
+     "Fuse SiLU*up into the gate_up GEMM epilogue.")
+_reg("VLLM_B200_ATTN", "kill", True, "kernels", "Paged attention kernels (0 = SDPA reference).")
+_reg("VLLM_B200_ROPE_KV", "kill", True, "kernels", "Fused RoPE + KV-cache write kernel.")
+_reg("VLLM_B200_FP8_GEMM", "kill", True, "kernels", "Block-FP8 tcgen05 GEMM.")
+_reg("VLLM_B200_AWQ_GEMM", "kill", True, "kernels", "AWQ int4 GEMM.")
+_reg("VLLM_B200_NVFP4_GEMM", "kill", True, "kernels", "NVFP4 GEMM.")
+_reg("VLLM_B200_MOE", "kill", True, "kernels", "Grouped expert GEMM + router kernels.")
+_reg("VLLM_B200_ROUTER", "kill", True, "kernels", "Fused MoE router (U3 provider).")
+_reg("VLLM_B200_SAMPLER", "kill", True, "kernels", "Hidden-state sampler (U4 provider).")
+_reg("VLLM_B200_GREEDY_FASTPATH", "kill", True, "kernels", "Vocab-parallel greedy top-1.")
+_reg("VLLM_B200_GDN", "kill", True, "kernels", "Gated-DeltaNet kernels.")
+# -- collectives ----------------------------------------------------------
+_reg("VLLM_B200_FUSED_AR_RMSNORM", "kill", True, "comm",
+     "Fused all-reduce + residual + RMSNorm over NVLink peer memory (0 = NCCL + norm).")
+_reg("VLLM_B200_FUSED_GEMM_RS", "kill", True, "comm", "Fused GEMM -> reduce-scatter.")
+_reg("VLLM_B200_FUSED_AG_GEMM", "kill", True, "comm", "Fused all-gather -> GEMM.")
+_reg("VLLM_B200_FUSED_EP_A2A", "kill", True, "comm", "Fused EP dispatch / combine.")
+_reg("VLLM_B200_NVLS", "optin", False, "comm", "Use NVLS multimem reductions where supported.")
+_reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
+     "Bound (ms) for every device-side flag wait in fused collectives.")
+# -- runtime --------------------------------------------------------------
+_reg("VLLM_B200_CUDA_GRAPHS", "kill", True, "runtime", "Capture decode steps in CUDA graphs.")
+_reg("VLLM_B200_GRAPH_MAX_BS", "int", 512, "runtime", "Largest captured decode batch.")
+_reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tuning.")
+_reg("VLLM_B200_GEMM_LUT_PATH", "path", None, "runtime", "Tuned GEMM config table to import.")
+_reg("VLLM_B200_GEMM_LUT_EXPORT_PATH", "path", None, "runtime", "Where to export the table.")
+_reg("VLLM_B200_GEMM_LUT_STRICT", "optin", False, "runtime",
+     "Refuse a LUT whose manifest does not match this build / GPU.")
+
+
+def get(name: str):
+    return _REGISTRY[name].get()
+
+
+def registry() -> dict[str, EnvVar]:
+    return dict(_REGISTRY)
+
+
+def sections() -> dict[str, list[str]]:
+    out: dict[str, list[str]] = {}
+    for v in _REGISTRY.values():
+        out.setdefault(v.section, []).append(v.name)
+    return out
+
+
+def compile_factors() -> dict[str, object]:
+    """Values that change generated code / graphs; hashed into cache keys."""
+    return {k: v.get() for k, v in sorted(_REGISTRY.items()) if v.kind in ("kill", "optin")}
+
+
+def merge_into_vllm() -> int:
+    """Expose the getters through ``vllm.envs`` (when vLLM is importable) so
+    its environment validation and compile hashing see them. Returns the
+    number of names merged (0 without vLLM)."""
+    try:
+        import vllm.envs as venvs  # type: ignore
+    except Exception:  # noqa: BLE001 - vLLM is optional for the core library
+        return 0
+    table = getattr(venvs, "environment_variables", None)
+    if not isinstance(table, dict):
+        return 0
+    n = 0
+    for name, var in _REGISTRY.items():
+        if name not in table:
+            table[name] = _getter(var)
+            n += 1
+    return n
+
+
+def _getter(var: EnvVar) -> Callable[[], object]:
+    return lambda: var.get()

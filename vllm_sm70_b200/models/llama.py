@@ -1,0 +1,208 @@
+"""Llama-family dense decoder (Llama-3.x; Qwen3-dense with q/k-norm) on the
+B200 kernels, tensor-parallel over the TP group.
+
+Per layer (T tokens):
+  x   = fused_add_rms_norm(x, residual)                  # residual += x
+  qkv = gemm(x, Wqkv)                                     # tcgen05
+  rope_kv_write(qkv -> q rotated in place, K/V -> paged cache)
+  a   = paged_attention(q view of qkv)                    # GQA-packed
+  o   = gemm(a, Wo)          -- TP: all-reduce fused with the next norm
+  h   = gemm_silu_mul(norm(o + residual), Wgate_up)       # SiLU*up in epilogue
+  x   = gemm(h, Wdown)       -- TP: all-reduce fused with the next norm
+
+Reference parity: the reference's dense path is the Flint layer stack
+(``sm70/vllm_sm70/models/flint_sm70/model.py:145-482``) through upstream
+vLLM Column/RowParallel layers; here the model class owns its TP layers so
+the row-parallel all-reduce can be fused with the residual add + RMSNorm
+(the reference's K17, ``sm70/vllm_sm70/ar_rms_fusion.py:105-433``).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+from ..parallel import comm, state as pstate
+from .config import ModelConfig
+from .layers import AttnMeta, DenseLinear, GateUpLinear, KVCache
+
+
+def _shard(n: int, tp: int, rank: int) -> slice:
+    assert n % tp == 0, (n, tp)
+    k = n // tp
+    return slice(rank * k, (rank + 1) * k)
+
+
+class LlamaModel:
+    def __init__(self, cfg: ModelConfig, device: torch.device, dtype=torch.bfloat16,
+                 ps: pstate.ParallelState | None = None):
+        self.cfg = cfg
+        self.device = device
+        self.dtype = dtype
+        self.ps = ps or pstate.get()
+        tp = self.ps.tp_size
+        assert cfg.num_heads % tp == 0, "num_heads must divide by TP"
+        self.hq = cfg.num_heads // tp
+        self.hkv = max(1, cfg.num_kv_heads // tp)
+        self.kv_replicated = cfg.num_kv_heads < tp
+        self.d = cfg.head_dim
+        self.inter = cfg.intermediate_size // tp
+        assert cfg.vocab_size % tp == 0 or True
+        self.vocab_local = math.ceil(cfg.vocab_size / tp)
+        self.vocab_start = self.ps.tp_rank * self.vocab_local
+        self.layers: list[dict] = []
+        self.scale = 1.0 / math.sqrt(self.d)
+        self.cos_sin = None
+        self.embed = None
+        self.lm_head = None
+        self.final_norm = None
+
+    # ------------------------------------------------------------------ weights
+    def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
+        """Random-init weights of the configured shapes (TP-local shards)."""
+        cfg, dev, dt = self.cfg, self.device, self.dtype
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 7919 + self.ps.tp_rank)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std).to(dt)
+
+        h = cfg.hidden_size
+        self.embed = rnd(self.vocab_local, h)
+        self.lm_head = self.embed if cfg.tie_embeddings else rnd(self.vocab_local, h)
+        self.final_norm = torch.ones(h, device=dev, dtype=dt)
+        qkv_out = (self.hq + 2 * self.hkv) * self.d
+        self.layers = []
+        for _ in range(cfg.num_layers):
+            L = {
+                "in_norm": torch.ones(h, device=dev, dtype=dt),
+                "post_norm": torch.ones(h, device=dev, dtype=dt),
+                "qkv": DenseLinear(rnd(qkv_out, h)),
+                "o": DenseLinear(rnd(h, self.hq * self.d)),
+                "gate_up": GateUpLinear(rnd(self.inter, h), rnd(self.inter, h)),
+                "down": DenseLinear(rnd(h, self.inter)),
+            }
+            if cfg.qk_norm:
+                L["q_norm"] = torch.ones(self.d, device=dev, dtype=dt)
+                L["k_norm"] = torch.ones(self.d, device=dev, dtype=dt)
+            self.layers.append(L)
+        self._init_rope()
+
+    def load_hf_state(self, get_tensor) -> None:
+        """Load from an HF Llama checkpoint; ``get_tensor(name)`` returns the
+        full (unsharded) tensor. Shards for this TP rank are cut here."""
+        cfg, dev, dt = self.cfg, self.device, self.dtype
+        tp, r = self.ps.tp_size, self.ps.tp_rank
+
+        def t(name):
+            return get_tensor(name).to(device=dev, dtype=dt)
+
+        vs = slice(r * self.vocab_local, (r + 1) * self.vocab_local)
+        emb = t("model.embed_tokens.weight")
+        pad = self.vocab_local * tp - emb.shape[0]
+        if pad:
+            emb = torch.cat([emb, emb.new_zeros(pad, emb.shape[1])])
+        self.embed = emb[vs].contiguous()
+        if cfg.tie_embeddings:
+            self.lm_head = self.embed
+        else:
+            lm = t("lm_head.weight")
+            if pad:
+                lm = torch.cat([lm, lm.new_zeros(pad, lm.shape[1])])
+            self.lm_head = lm[vs].contiguous()
+        self.final_norm = t("model.norm.weight")
+        qs = _shard(cfg.num_heads * self.d, tp, r)
+        if self.kv_replicated:
+            kvh = r * cfg.num_kv_heads // tp
+            ks = slice(kvh * self.d, (kvh + 1) * self.d)
+        else:
+            ks = _shard(cfg.num_kv_heads * self.d, tp, r)
+        is_ = _shard(cfg.intermediate_size, tp, r)
+        self.layers = []
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            q = t(p + "self_attn.q_proj.weight")[qs]
+            k = t(p + "self_attn.k_proj.weight")[ks]
+            v = t(p + "self_attn.v_proj.weight")[ks]
+            L = {
+                "in_norm": t(p + "input_layernorm.weight"),
+                "post_norm": t(p + "post_attention_layernorm.weight"),
+                "qkv": DenseLinear(torch.cat([q, k, v], 0)),
+                "o": DenseLinear(t(p + "self_attn.o_proj.weight")[:, qs]),
+                "gate_up": GateUpLinear(t(p + "mlp.gate_proj.weight")[is_],
+                                        t(p + "mlp.up_proj.weight")[is_]),
+                "down": DenseLinear(t(p + "mlp.down_proj.weight")[:, is_]),
+            }
+            if cfg.qk_norm:
+                L["q_norm"] = t(p + "self_attn.q_norm.weight")
+                L["k_norm"] = t(p + "self_attn.k_norm.weight")
+            self.layers.append(L)
+        self._init_rope()
+
+    def _init_rope(self) -> None:
+        rot = int(self.d * self.cfg.partial_rotary_factor)
+        self.cos_sin = ops.attention.rope_cos_sin(rot, self.cfg.max_position, self.cfg.rope_theta,
+                                                  self.cfg.rope_scaling, device=self.device)
+
+    def weight_bytes(self) -> int:
+        n = self.embed.numel() * 2 + (0 if self.cfg.tie_embeddings else self.lm_head.numel() * 2)
+        for L in self.layers:
+            n += sum(L[k].weight_bytes() for k in ("qkv", "o", "gate_up", "down"))
+        return n
+
+    # ------------------------------------------------------------------ forward
+    def embed_tokens(self, ids: torch.Tensor) -> torch.Tensor:
+        out = torch.empty(ids.shape[0], self.cfg.hidden_size, device=ids.device, dtype=self.dtype)
+        if ids.is_cuda:
+            torch.ops._b200_C.embedding(out, ids, self.embed, self.vocab_start)
+        else:
+            loc = ids - self.vocab_start
+            ok = (loc >= 0) & (loc < self.embed.shape[0])
+            out.copy_(self.embed[loc.clamp(0, self.embed.shape[0] - 1)] * ok[:, None])
+        if self.ps.tp_size > 1:
+            pstate.tp_all_reduce(out)
+        return out
+
+    def forward(self, ids: torch.Tensor, meta: AttnMeta, kv: KVCache) -> torch.Tensor:
+        cfg = self.cfg
+        eps = cfg.rms_eps
+        T = ids.shape[0]
+        residual = self.embed_tokens(ids)
+        x = ops.rms_norm(residual, self.layers[0]["in_norm"], eps)
+        attn_out = torch.empty(T, self.hq, self.d, device=ids.device, dtype=self.dtype)
+        for li, L in enumerate(self.layers):
+            if li > 0:
+                comm.all_reduce_add_rms_norm(x, residual, L["in_norm"], eps)
+            qkv = L["qkv"].forward(x)
+            ops.rope_kv_write(qkv, meta.positions, self.cos_sin, kv.k[li], kv.v[li],
+                              meta.slot_mapping, self.hq, self.hkv, L.get("q_norm"),
+                              L.get("k_norm"), eps)
+            q = qkv.view(T, self.hq + 2 * self.hkv, self.d)[:, : self.hq]
+            ops.paged_attention(attn_out, q, kv.k[li], kv.v[li], meta.block_table,
+                                meta.seq_lens, meta.cu_q, meta.max_q_len, self.scale, 0, None,
+                                meta.decode, meta.num_splits, meta.part_o, meta.part_ml)
+            o = L["o"].forward(attn_out.view(T, self.hq * self.d))
+            comm.all_reduce_add_rms_norm(o, residual, L["post_norm"], eps)
+            h = L["gate_up"].forward(o)
+            x = L["down"].forward(h)
+        comm.all_reduce_add_rms_norm(x, residual, self.final_norm, eps)
+        return x
+
+    def greedy(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Vocab-parallel greedy sampling: local LM-head GEMM + argmax, then a
+        rank-order merge of (value, id) pairs. Returns int32 ids ``[rows]``."""
+        logits = ops.gemm(hidden, self.lm_head)
+        if self.ps.tp_size == 1:
+            ids, _ = ops.argmax(logits[:, : self.cfg.vocab_size])
+            return ids
+        # Padded vocab rows (vocab not divisible by TP) are excluded.
+        nvalid = max(1, min(self.vocab_local, self.cfg.vocab_size - self.vocab_start))
+        ids, vals = ops.argmax(logits[:, :nvalid], id_offset=self.vocab_start)
+        return comm.greedy_merge(vals, ids)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        lg = ops.gemm(hidden, self.lm_head)
+        if self.ps.tp_size > 1:
+            lg = pstate.tp_all_gather(lg, dim=1)
+        return lg[:, : self.cfg.vocab_size]

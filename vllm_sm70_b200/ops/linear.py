@@ -1,0 +1,92 @@
+"""BF16 GEMM wrappers over the tcgen05 kernel (``_b200_C::gemm_bf16*``).
+
+Reference parity: the TurboMind f16 ops ``sm70_f16_gemm{,_out}`` and the
+gated-SiLU epilogue (``sm70/csrc/turbomind/ops/tm_f16_sm70.cu:351-365``,
+wrappers ``sm70/vllm_sm70/ops/tm.py:35-50``). On B200 the weight needs no
+repack for the plain GEMM (the kernel TMA-loads K-major rows directly); the
+fused SiLU epilogue wants the gate/up rows interleaved in 64-row blocks,
+produced once at load time by :func:`interleave_gate_up`.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _ext, envs
+
+GATE_UP_BLOCK = 64
+
+
+def _use_native(t: torch.Tensor) -> bool:
+    if not t.is_cuda:
+        return False
+    if not envs.get("VLLM_B200_GEMM"):
+        return False
+    _ext.require()
+    return True
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+         cfg: int = -1) -> torch.Tensor:
+    """``x[M, K] @ w[N, K].T`` in bf16 with fp32 accumulation."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    if _use_native(x):
+        torch.ops._b200_C.gemm_bf16_out(out, x, w, cfg)
+    else:
+        out.copy_((x.float() @ w.float().t()).to(out.dtype))
+    return out
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """Stack gate/up rows as [g0..g63, u0..u63, g64..g127, u64..u127, ...]."""
+    n, k = w_gate.shape
+    assert w_up.shape == (n, k) and n % GATE_UP_BLOCK == 0, (w_gate.shape, w_up.shape)
+    g = w_gate.reshape(n // GATE_UP_BLOCK, GATE_UP_BLOCK, k)
+    u = w_up.reshape(n // GATE_UP_BLOCK, GATE_UP_BLOCK, k)
+    return torch.stack([g, u], dim=1).reshape(2 * n, k).contiguous()
+
+
+def deinterleave_gate_up(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    n2, k = w.shape
+    v = w.reshape(n2 // (2 * GATE_UP_BLOCK), 2, GATE_UP_BLOCK, k)
+    return v[:, 0].reshape(n2 // 2, k), v[:, 1].reshape(n2 // 2, k)
+
+
+def silu_mul_ref(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    g = gate.float()
+    return (g * torch.sigmoid(g) * up.float()).to(gate.dtype)
+
+
+def gemm_silu_mul(x: torch.Tensor, w_interleaved: torch.Tensor,
+                  out: torch.Tensor | None = None, cfg: int = -1) -> torch.Tensor:
+    """``silu(x @ w_gate.T) * (x @ w_up.T)`` with the activation fused in the
+    GEMM epilogue. ``w_interleaved`` comes from :func:`interleave_gate_up`."""
+    n = w_interleaved.shape[0] // 2
+    if out is None:
+        out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
+    if _use_native(x) and envs.get("VLLM_B200_GEMM_SILU_EPILOGUE"):
+        torch.ops._b200_C.gemm_bf16_silu_mul_out(out, x, w_interleaved, cfg)
+        return out
+    wg, wu = deinterleave_gate_up(w_interleaved)
+    if _use_native(x):
+        gu = torch.empty(x.shape[0], 2 * n, dtype=x.dtype, device=x.device)
+        gemm(x, torch.cat([wg, wu], 0), out=gu)
+        torch.ops._b200_C.silu_mul(out, gu)
+        return out
+    g = x.float() @ wg.float().t()
+    u = x.float() @ wu.float().t()
+    out.copy_((g * torch.sigmoid(g) * u).to(out.dtype))
+    return out
+
+
+def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x = [gate | up]`` -> ``silu(gate) * up``."""
+    n = x.shape[-1] // 2
+    if out is None:
+        out = torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
+    if x.is_cuda:
+        _ext.require()
+        torch.ops._b200_C.silu_mul(out, x)
+    else:
+        out.copy_(silu_mul_ref(x[..., :n], x[..., n:]))
+    return out

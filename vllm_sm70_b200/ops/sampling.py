@@ -1,0 +1,60 @@
+"""Greedy (argmax) sampling and the vocab-parallel top-1 merge.
+
+Tie order (shared by the kernel, this oracle and the rank merge): NaN first,
+then the larger value, then the lower token id. Reference parity:
+``sm70/vllm_sm70/sample_greedy.py:74-328`` (per-rank argmax -> all-gather of
+(value, id) pairs) and ``sm70/csrc/custom_ar/top1_custom_ar.cu:52-101``.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _ext
+
+
+def argmax_ref(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    x = logits.float()
+    nan = torch.isnan(x)
+    has_nan = nan.any(-1)
+    # First NaN index for rows with NaN; else the first max index.
+    first_nan = torch.where(nan, torch.arange(x.shape[-1], device=x.device), x.shape[-1]).min(-1)
+    mx = torch.where(nan, torch.full_like(x, float("-inf")), x).max(-1)
+    is_max = torch.where(nan, False, x == mx.values[:, None])
+    first_max = torch.where(is_max, torch.arange(x.shape[-1], device=x.device),
+                            x.shape[-1]).min(-1).values
+    ids = torch.where(has_nan, first_nan.values, first_max).to(torch.int32)
+    vals = torch.where(has_nan, torch.full_like(mx.values, float("nan")), mx.values)
+    return ids, vals
+
+
+def argmax(logits: torch.Tensor, id_offset: int = 0,
+           ids: torch.Tensor | None = None,
+           vals: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    rows = logits.shape[0]
+    if ids is None:
+        ids = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    if vals is None:
+        vals = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    if logits.is_cuda:
+        _ext.require()
+        torch.ops._b200_C.argmax(ids, vals, logits, id_offset)
+    else:
+        i, v = argmax_ref(logits)
+        ids.copy_(i + id_offset)
+        vals.copy_(v)
+    return ids, vals
+
+
+def merge_rank_top1(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    """``vals/ids [world, rows]`` (rank order) -> global greedy ids ``[rows]``
+    under the same tie order (NaN first, max value, lowest id)."""
+    v = vals.float()
+    nan = torch.isnan(v)
+    key_nan = torch.where(nan, ids.to(torch.int64), torch.iinfo(torch.int64).max)
+    any_nan = nan.any(0)
+    nan_pick = key_nan.min(0).values
+    vm = torch.where(nan, torch.full_like(v, float("-inf")), v)
+    mx = vm.max(0).values
+    cand = torch.where((vm == mx[None]) & ~nan, ids.to(torch.int64), torch.iinfo(torch.int64).max)
+    pick = cand.min(0).values
+    return torch.where(any_nan, nan_pick, pick).to(torch.int32)
