@@ -1,0 +1,310 @@
+"""Headline benchmark: output tokens/s of the Llama-3.1-8B-shaped workload.
+
+Workload: Llama-3.1-8B shapes, random-init bf16 weights
+(std 0.02), 256 requests with uniform-random prompt ids of length 1024, 256
+greedy output tokens each (ignore EOS), tensor-parallel over N GPUs of one
+node. One bench "step" is the whole workload: prefill of all 256 prompts and
+255 decode steps, through the public ``LLM.generate`` API.
+
+    python bench.py --gpus 1 --steps 3 --warmup 3
+    torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference ...   # upstream vLLM + the reference plugin
+
+``value`` is device time (CUDA events on the launching stream, barrier +
+synchronize on both sides, max over ranks); ``e2e`` is the host wall clock of
+the same ``generate`` calls (pinned prompt upload + output download included).
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "output tok/s (box, max over ranks) at 1/2/4/8 B200; p50 TTFT/TPOT"
+MODEL = "Llama-3.1-8B-shaped (32L, h4096, 32q/8kv, d128, ffn14336, vocab128256)"
+N_REQ, PROMPT, OUT = 256, 1024, 256
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this config
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", ",".join(map(str, self.gpus))],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001 - clocks are best-effort metadata
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        load = [s for s in sm if s > 500] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist_setup():
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    return world, rank
+
+
+def _max_over_ranks(x: float) -> float:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def _barrier():
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def make_prompts(seed: int = 1234):
+    """Fresh uniform-random prompt ids. Every warm-up and timed step uses a new
+    seed, so no step can be served from a prefix cache of an earlier one."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, 128000, (N_REQ, PROMPT), generator=g, dtype=torch.int64)
+
+
+# ----------------------------------------------------------------------------- ours
+def run_ours(args) -> dict:
+    sys.path.insert(0, str(ROOT))
+    from vllm_sm70_b200.engine import LLM, SamplingParams
+    from vllm_sm70_b200.parallel import state as pstate
+    from vllm_sm70_b200.utils import launch_count
+
+    world, rank = _dist_setup()
+    ps = pstate.init(tp_size=args.gpus if world > 1 else 1)
+    llm = LLM("llama-3.1-8b", tensor_parallel_size=ps.tp_size, max_num_seqs=N_REQ,
+              max_model_len=PROMPT + OUT, block_size=args.block_size,
+              max_num_batched_tokens=args.chunk, load_format="dummy", seed=0)
+    warm = [make_prompts(1000 + i).pin_memory() for i in range(args.warmup)]
+    timed = [make_prompts(2000 + i).pin_memory() for i in range(args.steps)]
+    prompts = timed[0]
+    sp = SamplingParams(max_tokens=OUT, temperature=0.0, ignore_eos=True)
+    for w in warm:
+        llm.generate(w, sp)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    launch_count.reset()
+    _barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    ev0.record()
+    ttft, tpot = [], []
+    outs = None
+    for i in range(args.steps):
+        outs = llm.generate(timed[i], sp)
+        st = llm.last_stats
+        ttft += st.ttft_ms
+        tpot += st.tpot_ms
+    ev1.record()
+    torch.cuda.synchronize()
+    _barrier()
+    wall = time.perf_counter() - w0
+    dev_ms = ev0.elapsed_time(ev1)
+    launches = launch_count.total()
+    clocks = sampler.stop() if sampler else None
+    dev_ms = _max_over_ranks(dev_ms)
+    wall = _max_over_ranks(wall)
+    n_out = sum(len(o.output_token_ids) for o in outs) * args.steps
+    value = n_out / (dev_ms / 1e3)
+    e2e = n_out / wall
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 2),
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 3),
+        "dtype": "bf16", "data": "synthetic (uniform-random prompt ids, random-init weights std 0.02)",
+        "config": {"model": MODEL, "global_batch": N_REQ, "seq_len": PROMPT,
+                   "output_len": OUT, "parallelism": f"tp{args.gpus}",
+                   "l2": "inputs larger than L2 (16 GB of weights streamed per step)",
+                   "block_size": args.block_size, "prefill_chunk_tokens": args.chunk},
+        "p50_ttft_ms": round(statistics.median(ttft), 1) if ttft else None,
+        "p50_tpot_ms": round(statistics.median(tpot), 3) if tpot else None,
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": int(prompts.numel() * prompts.element_size()),
+                "d2h_bytes_per_step": int(N_REQ * OUT * 4)},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    llm.shutdown()
+    pstate.shutdown()
+    return res
+
+
+# ----------------------------------------------------------------------------- reference
+def _write_hf_config(d: Path):
+    cfg = {
+        "architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": 4096,
+        "intermediate_size": 14336, "num_attention_heads": 32, "num_key_value_heads": 8,
+        "num_hidden_layers": 32, "head_dim": 128, "vocab_size": 128256, "rms_norm_eps": 1e-5,
+        "rope_theta": 500000.0, "max_position_embeddings": 131072, "torch_dtype": "bfloat16",
+        "rope_scaling": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                         "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+        "bos_token_id": 128000, "eos_token_id": 128001, "tie_word_embeddings": False,
+        "hidden_act": "silu", "initializer_range": 0.02,
+    }
+    (d / "config.json").write_text(json.dumps(cfg))
+
+
+def run_reference(args) -> dict:
+    world, rank = _dist_setup()
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "vllm_sm70").exists():
+        line = {"impl": "reference", "unavailable": "baseline/_ref not installed"}
+        print(json.dumps(line))
+        return line
+    sys.path.insert(0, str(ref))
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    try:
+        import vllm_sm70  # noqa: F401  (the reference plugin; inert unless every GPU is sm_70)
+        from vllm import LLM, SamplingParams
+        from vllm.inputs import TokensPrompt
+    except Exception as e:  # noqa: BLE001
+        line = {"impl": "reference", "unavailable": f"import failed: {type(e).__name__}: {e}"}
+        print(json.dumps(line))
+        return line
+    d = Path(tempfile.mkdtemp(prefix="ref_llama8b_"))
+    _write_hf_config(d)
+    kw = dict(model=str(d), load_format="dummy", dtype="bfloat16", skip_tokenizer_init=True,
+              max_num_seqs=N_REQ, max_model_len=PROMPT + OUT, seed=0,
+              tensor_parallel_size=args.gpus, gpu_memory_utilization=0.85)
+    if world > 1:
+        kw["distributed_executor_backend"] = "external_launcher"
+    llm = LLM(**kw)
+    def tp(seed):
+        return [TokensPrompt(prompt_token_ids=row.tolist()) for row in make_prompts(seed)]
+
+    warm = [tp(1000 + i) for i in range(args.warmup)]
+    timed = [tp(2000 + i) for i in range(args.steps)]
+    sp = SamplingParams(max_tokens=OUT, temperature=0.0, ignore_eos=True)
+    for w in warm:
+        llm.generate(w, sp, use_tqdm=False)
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    _barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    ev0.record()
+    ttft, tpot = [], []
+    n_out = 0
+    for i in range(args.steps):
+        outs = llm.generate(timed[i], sp, use_tqdm=False)
+        for o in outs:
+            n_out += len(o.outputs[0].token_ids)
+            m = getattr(o, "metrics", None)
+            if m is not None and getattr(m, "first_token_latency", None) is not None:
+                ttft.append(m.first_token_latency * 1e3)
+    ev1.record()
+    torch.cuda.synchronize()
+    _barrier()
+    wall = time.perf_counter() - w0
+    dev_ms = _max_over_ranks(ev0.elapsed_time(ev1))
+    wall = _max_over_ranks(wall)
+    clocks = sampler.stop() if sampler else None
+    value = n_out / (dev_ms / 1e3)
+    res = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / args.steps, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random prompt ids, dummy weights)",
+        "config": {"model": MODEL, "global_batch": N_REQ, "seq_len": PROMPT, "output_len": OUT,
+                   "parallelism": f"tp{args.gpus}",
+                   "stack": "upstream vLLM (image) + vllm_sm70 plugin from baseline/_ref"},
+        "p50_ttft_ms": round(statistics.median(ttft), 1) if ttft else None,
+        "e2e": {"value": round(n_out / wall, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": N_REQ * PROMPT * 8, "d2h_bytes_per_step": N_REQ * OUT * 4},
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    return res
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--block-size", type=int, default=16)
+    ap.add_argument("--chunk", type=int, default=16384, help="prefill tokens per chunk")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        print("warning: --warmup < 3 does not meet the timing rules", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -28,6 +28,9 @@ def b200_ops():
     major, minor = torch.cuda.get_device_capability()
     assert (major, minor) == (10, 0), f"expected sm_100 (B200), got sm_{major}{minor}"
     torch.ops._b200_C.init_device(torch.cuda.current_device())
+    from vllm_sm70_b200.ops import linear
+
+    linear.configure_workspace(torch.cuda.current_device())
     return torch.ops._b200_C
 
 

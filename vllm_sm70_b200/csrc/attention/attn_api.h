@@ -22,6 +22,7 @@ struct AttnArgs {
   float scale;
   bool decode;     // use the decode (1-warp, split-KV) variant
   int num_splits;  // decode split-KV factor (1 = none)
+  long long kv_block_stride = 0;  // elements between cache blocks (0 = Hkv*BS*D, packed)
 };
 
 void paged_attention_launch(const AttnArgs& a, cudaStream_t stream);

@@ -95,22 +95,32 @@ struct Params {
   const float* sinks;     // [Hq] or nullptr
   float* part_o;          // [splits, T, Hq, D] (decode split-KV) or nullptr
   float* part_ml;         // [splits, T, Hq, 2]
-  int num_seqs, Hq, Hkv, block_size, max_blocks, window;
+  int num_seqs, Hq, Hkv, block_size, block_shift, max_blocks, window;
+  long long kv_block_stride;   // elements between consecutive cache blocks
   int q_stride_t, o_stride_t;  // element strides between tokens
   float scale_log2;            // softmax scale * log2(e)
   int num_splits;              // decode split-KV
   int rows_per_seq_max;        // max over seqs of q_len*G (grid sizing)
 };
 
-// One "worker" = NW warps sharing one K/V pipeline and owning 16*NW rows.
+constexpr int kBtCache = 512;  // block ids cached in smem per window
+
+// Prefill (DECODE=false): NW warps, each owns 16 query rows; all warps walk
+// every key of each shared K/V tile.
+// Decode (DECODE=true): the CTA owns 16 rows (GQA group x query tokens); the
+// NW warps split every K/V tile by keys (KT/NW each) and merge their softmax
+// states in warp order at the end.
 template <int D, int KT, int NW, int STAGES, bool DECODE>
 __global__ void __launch_bounds__(NW * 32)
 paged_attn_kernel(const Params p) {
-  constexpr int ROWS = 16 * NW;
+  constexpr int ROWS = DECODE ? 16 : 16 * NW;
+  constexpr int KW = DECODE ? KT / NW : KT;  // keys per warp per tile
+  static_assert(KW % 16 == 0, "keys per warp must be a multiple of 16");
   constexpr int CH = D / 8;  // 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + ROWS * D * 2;  // STAGES x (K tile, V tile)
+  int* sBT = reinterpret_cast<int*>(smem + ROWS * D * 2);
+  uint8_t* sKV = smem + ROWS * D * 2 + kBtCache * 4;  // STAGES x (K tile, V tile)
   constexpr int kTileBytes = KT * D * 2;
 
   const int seq = blockIdx.y;
@@ -130,6 +140,8 @@ paged_attn_kernel(const Params p) {
   const int tid = threadIdx.x;
   const int warp = tid / 32;
   const int lane = tid % 32;
+  const int key_off = DECODE ? warp * KW : 0;
+  const int warp_row0 = DECODE ? 0 : warp * 16;
 
   // Key range for this CTA.
   const int first_pos = seq_len - q_len + row0 / G;
@@ -161,24 +173,46 @@ paged_attn_kernel(const Params p) {
   }
   cp_async_commit();
 
+  // Block ids of the key range, cached in smem window by window so the K/V
+  // address computation never waits on a global load.
   const int* bt = p.block_table + (size_t)seq * p.max_blocks;
+  const int blk_first = k_begin >> p.block_shift;
+  const int blk_last = k_end > 0 ? (k_end - 1) >> p.block_shift : 0;
+  int bt_base = -kBtCache;
+  auto refill_bt = [&](int first_blk) {
+    __syncthreads();
+    for (int i = tid; i < kBtCache; i += NW * 32) {
+      const int b = first_blk + i;
+      sBT[i] = b <= blk_last ? __ldg(bt + b) : 0;
+    }
+    __syncthreads();
+  };
+  const long long head_off = (long long)kvh * p.block_size * D;
   auto load_tile = [&](int tile, int buf) {
     const int kbase = k_begin + tile * KT;
+    const int kb_last = min(kbase + KT, k_end) - 1;
+    if ((kb_last >> p.block_shift) >= bt_base + kBtCache) {  // uniform across the CTA
+      bt_base = kbase >> p.block_shift;
+      refill_bt(bt_base);
+    }
     uint8_t* sK = sKV + buf * 2 * kTileBytes;
     uint8_t* sV = sK + kTileBytes;
+#pragma unroll 4
     for (int c = tid; c < KT * CH; c += NW * 32) {
       const int r = c / CH, ch = c % CH;
       const int key = kbase + r;
       const bool valid = key < k_end;
-      size_t off = 0;
+      long long off = 0;
       if (valid) {
-        const int blk = bt[key / p.block_size];
-        off = (((size_t)blk * p.Hkv + kvh) * p.block_size + key % p.block_size) * D + ch * 8;
+        const int blk = sBT[(key >> p.block_shift) - bt_base];
+        off = (long long)blk * p.kv_block_stride + head_off +
+              (long long)(key & (p.block_size - 1)) * D + ch * 8;
       }
       cp_async_16(smem_addr(sK) + swz<D>(r, ch), p.k_cache + off, valid);
       cp_async_16(smem_addr(sV) + swz<D>(r, ch), p.v_cache + off, valid);
     }
   };
+  (void)blk_first;
 
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
@@ -191,7 +225,7 @@ paged_attn_kernel(const Params p) {
   __syncthreads();
   uint32_t qf[D / 16][4];
   {
-    const int r = warp * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+    const int r = warp_row0 + (lane % 8) + ((lane / 8) % 2) * 8;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const int ch = kk * 2 + lane / 16;
@@ -205,7 +239,7 @@ paged_attn_kernel(const Params p) {
   bool row_valid[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int gr = row0 + warp * 16 + g + h * 8;
+    const int gr = row0 + warp_row0 + g + h * 8;
     row_valid[h] = gr < rows_total;
     row_pos[h] = seq_len - q_len + (row_valid[h] ? gr / G : 0);
   }
@@ -227,17 +261,17 @@ paged_attn_kernel(const Params p) {
     __syncthreads();
     const uint8_t* sK = sKV + buf * 2 * kTileBytes;
     const uint8_t* sV = sK + kTileBytes;
-    const int kbase = k_begin + tile * KT;
+    const int kbase = k_begin + tile * KT + key_off;
 
-    // S = Q K^T : 16 rows x KT keys per warp
-    float s[KT / 8][4];
+    // S = Q K^T : 16 rows x KW keys per warp
+    float s[KW / 8][4];
 #pragma unroll
-    for (int n = 0; n < KT / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < KW / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
 #pragma unroll
-      for (int n2 = 0; n2 < KT / 16; ++n2) {
-        const int key = n2 * 16 + (lane % 8) + (lane / 16) * 8;
+      for (int n2 = 0; n2 < KW / 16; ++n2) {
+        const int key = key_off + n2 * 16 + (lane % 8) + (lane / 16) * 8;
         const int ch = kk * 2 + (lane / 8) % 2;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(smem_addr(sK) + swz<D>(key, ch), b0, b1, b2, b3);
@@ -249,7 +283,7 @@ paged_attn_kernel(const Params p) {
     // Mask + online softmax (base 2).
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int n = 0; n < KT / 8; ++n) {
+    for (int n = 0; n < KW / 8; ++n) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int h = e / 2;
@@ -278,9 +312,9 @@ paged_attn_kernel(const Params p) {
       o[i][2] *= corr[1];
       o[i][3] *= corr[1];
     }
-    uint32_t pf[KT / 16][4];
+    uint32_t pf[KW / 16][4];
 #pragma unroll
-    for (int n = 0; n < KT / 8; ++n) {
+    for (int n = 0; n < KW / 8; ++n) {
       float e4[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -294,10 +328,10 @@ paged_attn_kernel(const Params p) {
     }
     // O += P V
 #pragma unroll
-    for (int kk = 0; kk < KT / 16; ++kk) {
+    for (int kk = 0; kk < KW / 16; ++kk) {
 #pragma unroll
       for (int d2 = 0; d2 < D / 16; ++d2) {
-        const int key = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+        const int key = key_off + kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
         const int ch = d2 * 2 + lane / 16;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(smem_addr(sV) + swz<D>(key, ch), b0, b1, b2, b3);
@@ -316,10 +350,71 @@ paged_attn_kernel(const Params p) {
     l_run[h] += __shfl_xor_sync(0xffffffff, l_run[h], 2);
   }
 
+  if constexpr (DECODE && NW > 1) {
+    // Merge the warps' partial softmax states in warp order through smem
+    // (the K/V ring is idle now).
+    __syncthreads();
+    float* sO = reinterpret_cast<float*>(sKV);            // [NW][16][D]
+    float* sM = sO + NW * 16 * D;                          // [NW][16]
+    float* sL = sM + NW * 16;                              // [NW][16]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = g + h * 8;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        const int d = i * 8 + t4 * 2;
+        sO[(warp * 16 + r) * D + d] = o[i][2 * h];
+        sO[(warp * 16 + r) * D + d + 1] = o[i][2 * h + 1];
+      }
+      if (t4 == 0) {
+        sM[warp * 16 + r] = m_run[h];
+        sL[warp * 16 + r] = l_run[h];
+      }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < 16 * D; idx += NW * 32) {
+      const int r = idx / D, d = idx % D;
+      const int gr = row0 + r;
+      if (gr >= rows_total) continue;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) M = fmaxf(M, sM[w * 16 + r]);
+      float L = 0.f, acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float mw = sM[w * 16 + r];
+        const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+        L += sL[w * 16 + r] * sc;
+        acc += sO[(w * 16 + r) * D + d] * sc;
+      }
+      const int tok = gr / G;
+      const int head = kvh * G + gr % G;
+      if (p.num_splits > 1) {
+        const size_t T = (size_t)p.cu_q[p.num_seqs];
+        const size_t base = ((size_t)split * T + (q0 + tok)) * p.Hq + head;
+        p.part_o[base * D + d] = L > 0.f ? acc / L : 0.f;
+        if (d == 0) {
+          p.part_ml[base * 2 + 0] = M;
+          p.part_ml[base * 2 + 1] = L;
+        }
+      } else {
+        float denom = L;
+        if (p.sinks != nullptr) {
+          if (M == -INFINITY) denom = 1.f;
+          else denom += exp2f(p.sinks[head] * 1.4426950408889634f - M);
+        }
+        const float inv = denom > 0.f ? 1.f / denom : 0.f;
+        p.out[(size_t)(q0 + tok) * p.o_stride_t + (size_t)head * D + d] =
+            __float2bfloat16_rn(acc * inv);
+      }
+    }
+    return;
+  }
+
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     if (!row_valid[h]) continue;
-    const int gr = row0 + warp * 16 + g + h * 8;
+    const int gr = row0 + warp_row0 + g + h * 8;
     const int tok = gr / G;
     const int head = kvh * G + gr % G;
     if (DECODE && p.num_splits > 1) {
@@ -391,8 +486,10 @@ __global__ void combine_splits_kernel(const Params p, int T) {
 
 template <int D, int KT, int NW, int STAGES, bool DECODE>
 void launch_attn(const Params& p, cudaStream_t stream) {
-  constexpr int ROWS = 16 * NW;
-  constexpr int smem = ROWS * D * 2 + STAGES * 2 * KT * D * 2;
+  constexpr int ROWS = DECODE ? 16 : 16 * NW;
+  constexpr int smem = ROWS * D * 2 + kBtCache * 4 + STAGES * 2 * KT * D * 2;
+  static_assert(!DECODE || STAGES * 2 * KT * D * 2 >= (NW * 16 * D + NW * 32) * 4,
+                "decode merge buffer must fit in the K/V ring");
   auto kernel = paged_attn_kernel<D, KT, NW, STAGES, DECODE>;
   static bool attr = false;
   if (!attr) {
@@ -408,7 +505,8 @@ void launch_attn(const Params& p, cudaStream_t stream) {
 
 void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   if (a.Hq % a.Hkv != 0) throw std::runtime_error("paged_attention: Hq % Hkv != 0");
-  if (a.block_size % 8 != 0) throw std::runtime_error("paged_attention: block_size % 8 != 0");
+  if (a.block_size < 8 || (a.block_size & (a.block_size - 1)) != 0)
+    throw std::runtime_error("paged_attention: block_size must be a power of two >= 8");
   Params p;
   p.q = reinterpret_cast<const __nv_bfloat16*>(a.q);
   p.k_cache = reinterpret_cast<const __nv_bfloat16*>(a.k_cache);
@@ -424,6 +522,9 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   p.Hq = a.Hq;
   p.Hkv = a.Hkv;
   p.block_size = a.block_size;
+  p.block_shift = __builtin_ctz(a.block_size);
+  p.kv_block_stride = a.kv_block_stride > 0 ? a.kv_block_stride
+                                            : (long long)a.Hkv * a.block_size * a.head_dim;
   p.max_blocks = a.max_blocks;
   p.window = a.window;
   p.q_stride_t = a.q_stride_t;
@@ -435,17 +536,17 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
     throw std::runtime_error("paged_attention: split-KV needs partial buffers");
   if (a.head_dim == 128) {
     if (a.decode)
-      launch_attn<128, 32, 1, 3, true>(p, stream);
+      launch_attn<128, 64, 4, 3, true>(p, stream);
     else
       launch_attn<128, 64, 4, 2, false>(p, stream);
   } else if (a.head_dim == 256) {
     if (a.decode)
-      launch_attn<256, 32, 1, 2, true>(p, stream);
+      launch_attn<256, 64, 4, 2, true>(p, stream);
     else
       launch_attn<256, 32, 4, 2, false>(p, stream);
   } else if (a.head_dim == 64) {
     if (a.decode)
-      launch_attn<64, 32, 1, 3, true>(p, stream);
+      launch_attn<64, 64, 4, 3, true>(p, stream);
     else
       launch_attn<64, 64, 4, 2, false>(p, stream);
   } else {

@@ -27,7 +27,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, const int64_t* _
                                __nv_bfloat16* __restrict__ vc, const int64_t* __restrict__ slots,
                                const __nv_bfloat16* __restrict__ q_norm,
                                const __nv_bfloat16* __restrict__ k_norm, int T, int Hq, int Hkv,
-                               int BS, float eps, int rot_dim) {
+                               int BS, float eps, int rot_dim, long long blk_stride) {
   constexpr int P = D / 64;  // pairs per lane (first-half index i, second-half i + D/2)
   const int warps_per_block = blockDim.x / 32;
   const int gw = blockIdx.x * warps_per_block + threadIdx.x / 32;
@@ -106,7 +106,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, const int64_t* _
   if ((is_k || is_v) && slot >= 0) {
     const int kvh = is_k ? h - Hq : h - Hq - Hkv;
     const int64_t blk = slot / BS, off = slot % BS;
-    __nv_bfloat16* dst = (is_k ? kc : vc) + ((blk * Hkv + kvh) * BS + off) * D;
+    __nv_bfloat16* dst = (is_k ? kc : vc) + blk * blk_stride + ((long long)kvh * BS + off) * D;
 #pragma unroll
     for (int j = 0; j < P; ++j) {
       const int i = lane + 32 * j;
@@ -121,7 +121,8 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, const int64_t* _
 void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, void* k_cache,
                           void* v_cache, const int64_t* slots, const void* q_norm,
                           const void* k_norm, int T, int Hq, int Hkv, int D, int BS, float eps,
-                          int rot_dim, cudaStream_t stream) {
+                          int rot_dim, long long blk_stride, cudaStream_t stream) {
+  if (blk_stride <= 0) blk_stride = (long long)Hkv * BS * D;
   if (T <= 0) return;
   const long warps = (long)T * (Hq + 2 * Hkv);
   const int wpb = 8;
@@ -129,7 +130,8 @@ void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, v
 #define B200_ROPE(DD)                                                                           \
   rope_kv_kernel<DD><<<blocks, wpb * 32, 0, stream>>>(                                          \
       (__nv_bfloat16*)qkv, pos, cos_sin, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slots, \
-      (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, T, Hq, Hkv, BS, eps, rot_dim)
+      (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, T, Hq, Hkv, BS, eps, rot_dim, \
+      blk_stride)
   if (D == 128) B200_ROPE(128);
   else if (D == 256) B200_ROPE(256);
   else if (D == 64) B200_ROPE(64);

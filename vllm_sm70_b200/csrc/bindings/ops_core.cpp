@@ -22,6 +22,27 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 int64_t abi_version() { return kAbiVersion; }
 
+// cfg < 0: auto plan (tile + split-K). splits > 0 forces the split factor
+// (used by tests); the split path needs the configured per-device workspace.
+void launch_gemm(at::Tensor& out, const at::Tensor& a, const at::Tensor& w, int epi, int64_t cfg,
+                 int64_t splits) {
+  const int dev = a.get_device();
+  const int M = (int)a.size(0), N = (int)w.size(0), K = (int)a.size(1);
+  int c = (int)cfg, s = (int)splits;
+  if (c < 0) {
+    int nsm = 0;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    GemmPlan p = gemm_bf16_plan(M, N, K, epi, nsm);
+    c = p.cfg;
+    if (s <= 0) s = p.splits;
+  }
+  if (s <= 0) s = 1;
+  gemm_bf16_launch_split(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, (int)a.stride(0),
+                         (int)w.stride(0), (int)out.stride(0), epi, c, s, gemm_ws_ptr(dev),
+                         gemm_workspace_bytes(dev), gemm_counters_ptr(dev),
+                         gemm_n_counters(dev), device_status_ptr(dev), cur_stream());
+}
+
 void init_device(int64_t device) { (void)device_status_ptr((int)device); }
 
 int64_t read_status(int64_t device, bool clear) {
@@ -33,22 +54,31 @@ int64_t read_status(int64_t device, bool clear) {
   return (int64_t)v;
 }
 
-void gemm_bf16_out(at::Tensor& out, const at::Tensor& a, const at::Tensor& w, int64_t cfg) {
+void gemm_bf16_out(at::Tensor& out, const at::Tensor& a, const at::Tensor& w, int64_t cfg,
+                   int64_t splits) {
   CHECK_CUDA(a); CHECK_CUDA(w); CHECK_CUDA(out);
   CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out);
   CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(w); CHECK_ROWMAJOR(out);
   TORCH_CHECK(a.size(1) == w.size(1), "gemm_bf16: K mismatch");
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0), "gemm_bf16: out shape");
   c10::cuda::CUDAGuard g(a.device());
-  gemm_bf16_launch(a.data_ptr(), w.data_ptr(), out.data_ptr(), (int)a.size(0), (int)w.size(0),
-                   (int)a.size(1), (int)a.stride(0), (int)w.stride(0), (int)out.stride(0), kEpiNone,
-                   (int)cfg, device_status_ptr(a.get_device()), cur_stream());
+  launch_gemm(out, a, w, kEpiNone, cfg, splits);
 }
 
 at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& w, int64_t cfg) {
   auto out = at::empty({a.size(0), w.size(0)}, a.options());
-  gemm_bf16_out(out, a, w, cfg);
+  gemm_bf16_out(out, a, w, cfg, 0);
   return out;
+}
+
+void gemm_configure_workspace_op(int64_t device, int64_t ws_bytes, int64_t n_counters) {
+  gemm_configure_workspace((int)device, (size_t)ws_bytes, (int)n_counters);
+}
+
+std::vector<int64_t> gemm_bf16_plan_op(int64_t M, int64_t N, int64_t K, int64_t epi,
+                                       int64_t num_sm) {
+  GemmPlan p = gemm_bf16_plan((int)M, (int)N, (int)K, (int)epi, (int)num_sm);
+  return {p.cfg, p.splits};
 }
 
 // w_interleaved rows are [gate 64 | up 64] blocks (prepare with
@@ -63,28 +93,7 @@ void gemm_bf16_silu_mul_out(at::Tensor& out, const at::Tensor& a, const at::Tens
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0) / 2,
               "gemm_bf16_silu_mul: out shape");
   c10::cuda::CUDAGuard g(a.device());
-  const int M = (int)a.size(0), N = (int)w.size(0), K = (int)a.size(1);
-  int c = (int)cfg;
-  if (c < 0) c = gemm_bf16_pick_config(M, N, K, kEpiSiluMul, 148);
-  if (c != kCfgN128 && c != kCfgN256) {
-    // Small-M configs do not fuse the activation: GEMM then silu_mul.
-    auto tmp = at::empty({a.size(0), w.size(0)}, a.options());
-    gemm_bf16_launch(a.data_ptr(), w.data_ptr(), tmp.data_ptr(), M, N, K, (int)a.stride(0),
-                     (int)w.stride(0), (int)tmp.stride(0), kEpiNone, c,
-                     device_status_ptr(a.get_device()), cur_stream());
-    // De-interleave on the fly is not supported by silu_mul: callers that
-    // reach here use the block layout, so undo it with a view.
-    auto t4 = tmp.view({M, N / 128, 2, 64});
-    auto gate = t4.select(2, 0).reshape({M, N / 2});
-    auto up = t4.select(2, 1).reshape({M, N / 2});
-    auto gu = at::cat({gate, up}, 1);
-    silu_mul_launch(out.data_ptr(), gu.data_ptr(), M, N / 2, (int)gu.stride(0),
-                    (int)out.stride(0), cur_stream());
-    return;
-  }
-  gemm_bf16_launch(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, (int)a.stride(0),
-                   (int)w.stride(0), (int)out.stride(0), kEpiSiluMul, c,
-                   device_status_ptr(a.get_device()), cur_stream());
+  launch_gemm(out, a, w, kEpiSiluMul, cfg, 0);
 }
 
 int64_t gemm_bf16_config(int64_t M, int64_t N, int64_t K, int64_t epi) {
@@ -118,9 +127,13 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tenso
   TORCH_CHECK(positions.scalar_type() == at::kLong && slot_mapping.scalar_type() == at::kLong,
               "rope_kv_write: positions / slot_mapping must be int64");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin fp32");
-  TORCH_CHECK(qkv.is_contiguous() && k_cache.is_contiguous() && v_cache.is_contiguous(),
-              "rope_kv_write: contiguous tensors required");
-  TORCH_CHECK(k_cache.dim() == 4, "k_cache must be [blocks, Hkv, BS, D]");
+  TORCH_CHECK(qkv.is_contiguous(), "rope_kv_write: contiguous qkv required");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4, "k_cache must be [blocks, Hkv, BS, D]");
+  for (const at::Tensor* c : {&k_cache, &v_cache})
+    TORCH_CHECK(c->stride(3) == 1 && c->stride(2) == c->size(3) &&
+                    c->stride(1) == c->size(2) * c->size(3),
+                "rope_kv_write: cache blocks must be dense [Hkv, BS, D]");
+  TORCH_CHECK(k_cache.stride(0) == v_cache.stride(0), "rope_kv_write: K/V block strides differ");
   const int T = (int)qkv.size(0);
   const int D = (int)k_cache.size(3);
   const int BS = (int)k_cache.size(2);
@@ -131,7 +144,7 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tenso
                        k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr<int64_t>(),
                        q_norm ? q_norm->data_ptr() : nullptr, k_norm ? k_norm->data_ptr() : nullptr,
                        T, (int)num_q_heads, (int)num_kv_heads, D, BS, (float)eps,
-                       (int)cos_sin.size(1), cur_stream());
+                       (int)cos_sin.size(1), k_cache.stride(0), cur_stream());
 }
 
 void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
@@ -144,8 +157,16 @@ void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_c
   TORCH_CHECK(q.dim() == 3 && out.dim() == 3, "paged_attention: q/out must be [T, H, D]");
   TORCH_CHECK(q.stride(2) == 1 && q.stride(1) == q.size(2), "paged_attention: q head layout");
   TORCH_CHECK(out.stride(2) == 1 && out.stride(1) == out.size(2), "paged_attention: out layout");
-  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
-              "paged_attention: caches must be contiguous [blocks, Hkv, BS, D]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4, "paged_attention: caches [blocks, Hkv, BS, D]");
+  // Each (block, head) must be a dense BS x D tile; blocks may be strided
+  // (e.g. K and V interleaved per block in one allocation).
+  for (const at::Tensor* c : {&k_cache, &v_cache}) {
+    TORCH_CHECK(c->stride(3) == 1 && c->stride(2) == c->size(3) &&
+                    c->stride(1) == c->size(2) * c->size(3),
+                "paged_attention: cache blocks must be dense [Hkv, BS, D]");
+    TORCH_CHECK(c->stride(0) % 8 == 0, "paged_attention: cache block stride must be 16B aligned");
+  }
+  TORCH_CHECK(k_cache.stride(0) == v_cache.stride(0), "paged_attention: K/V block strides differ");
   TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
                   cu_q.scalar_type() == at::kInt,
               "paged_attention: int32 metadata");
@@ -177,6 +198,7 @@ void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_c
   a.scale = (float)scale;
   a.decode = decode;
   a.num_splits = (int)num_splits;
+  a.kv_block_stride = k_cache.stride(0);
   if (a.num_splits > 1) {
     TORCH_CHECK(part_o && part_ml, "split-KV decode needs part_o / part_ml");
     TORCH_CHECK(part_o->numel() >= (int64_t)a.num_splits * a.num_tokens * a.Hq * a.head_dim,
@@ -227,7 +249,11 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("init_device(int device) -> ()", &b200::init_device);
   m.def("read_status(int device, bool clear) -> int", &b200::read_status);
   m.def("gemm_bf16(Tensor a, Tensor w, int cfg=-1) -> Tensor");
-  m.def("gemm_bf16_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
+  m.def("gemm_bf16_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1, int splits=0) -> ()");
+  m.def("gemm_configure_workspace(int device, int ws_bytes, int n_counters) -> ()",
+        &b200::gemm_configure_workspace_op);
+  m.def("gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) -> int[]",
+        &b200::gemm_bf16_plan_op);
   m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
   m.def("gemm_bf16_config(int M, int N, int K, int epi) -> int", &b200::gemm_bf16_config);
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");

@@ -19,10 +19,33 @@ enum GemmConfig : int {
   kCfgCount = 5,
 };
 
+struct GemmPlan {
+  int cfg;
+  int splits;  // split-K factor (1 = none); partials reduced in-kernel, fixed order
+};
+
+// Tile config + split-K choice from a wave-quantisation cost model.
+GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm);
+
+// Process-wide split-K workspace (fp32 partials + self-re-arming counters).
+void gemm_configure_workspace(int device, size_t ws_bytes, int n_counters);
+size_t gemm_workspace_bytes(int device);
+float* gemm_ws_ptr(int device);
+int* gemm_counters_ptr(int device);
+int gemm_n_counters(int device);
+
 // C[M, N] = A[M, K] . W[N, K]^T  (bf16 in, fp32 accumulate, bf16 out).
+// cfg < 0: planned automatically (tile + split-K over the configured workspace).
 void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
                       int ldc, int epi, int cfg, unsigned int* err, cudaStream_t stream);
 
 int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm);
+
+// Explicit-workspace variant: splits > 1 needs ws >= tiles*splits*128*BN*4
+// bytes and counters[tiles] zeroed (they are re-armed by the kernel).
+void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,
+                            int ldw, int ldc, int epi, int cfg, int splits, float* ws,
+                            size_t ws_bytes, int* counters, int n_counters, unsigned int* err,
+                            cudaStream_t stream);
 
 }  // namespace b200

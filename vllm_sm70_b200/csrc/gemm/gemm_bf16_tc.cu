@@ -72,7 +72,8 @@ template <int BN, int STAGES, bool SWAP, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     const __grid_constant__ CUtensorMap tmap_q, __nv_bfloat16* __restrict__ C,
-                    int ldc, int p_rows, int q_rows, int K, unsigned int* err) {
+                    int ldc, int p_rows, int q_rows, int K, int splits, float* __restrict__ ws,
+                    int* __restrict__ counters, unsigned int* err) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -84,6 +85,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   uint64_t* done_bar = tempty_bar + 2;       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -91,6 +93,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   const int num_n = (q_rows + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
+  const int kb_per = (num_kb + splits - 1) / splits;
+  const int num_units = num_tiles * splits;
   constexpr uint32_t kTmemCols = 2 * BN;
 
   if (threadIdx.x == 0) {
@@ -125,17 +129,19 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const int t = u / splits, sp = u - t * splits;
         const TileCoord tc = tile_coord(t, num_m, num_n);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err)) {
             *abort_flag = 1;
             break;
           }
-          uint8_t* sp = smem + stage * S::kStageBytes;
+          uint8_t* spp = smem + stage * S::kStageBytes;
           mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-          tma_load_2d(sp, &tmap_p, &full_bar[stage], kb * BK, tc.mb * BM);
-          tma_load_2d(sp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, tc.nb * BN);
+          tma_load_2d(spp, &tmap_p, &full_bar[stage], kb * BK, tc.mb * BM);
+          tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, tc.nb * BN);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -158,7 +164,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x, ++local) {
+        const int t = u / splits, sp = u - t * splits;
+        (void)t;
+        const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, err)) {
@@ -168,20 +177,20 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sp = smem_u32(smem + stage * S::kStageBytes);
-          const uint64_t adesc = umma_desc_sw128(sp);
-          const uint64_t bdesc = umma_desc_sw128(sp + S::kPBytes);
+          const uint32_t spa = smem_u32(smem + stage * S::kStageBytes);
+          const uint64_t adesc = umma_desc_sw128(spa);
+          const uint64_t bdesc = umma_desc_sw128(spa + S::kPBytes);
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             // +32 bytes per K=16 step inside the 128-byte swizzle row.
             umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
-                     (kb | k) != 0);
+                     (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -204,8 +213,11 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
+    const int etid = threadIdx.x - 64;  // 0..127
+    constexpr int CW = BN >= 32 ? 32 : 16;  // columns per tcgen05.ld
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x, ++local) {
+      const int t = u / splits, sp = u - t * splits;
       const TileCoord tc = tile_coord(t, num_m, num_n);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -216,25 +228,96 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       const int i = tc.mb * BM + row_in_tile;  // P row
+      const bool split = splits > 1;
+      // Tile-local fp32 partials of this unit: ws[(t * splits + s)][row][col].
+      float* ws_tile = split ? ws + (size_t)t * splits * (BM * BN) : nullptr;
+
+      if (split) {
+        // Column-group-major layout [BN/4][BM] of float4: the 32 lanes of a
+        // warp (consecutive rows) write 512 contiguous bytes per store.
+        float4* mine = reinterpret_cast<float4*>(ws_tile + (size_t)sp * (BM * BN)) + row_in_tile;
+#pragma unroll 1
+        for (int ch = 0; ch < BN / CW; ++ch) {
+          uint32_t r[32];
+          if constexpr (CW == 32) {
+            tmem_ld_32x32b_x32(t_row + ch * CW, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + ch * CW, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int v = 0; v < CW / 4; ++v)
+            __stcg(mine + (size_t)(ch * (CW / 4) + v) * BM,
+                   make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+        }
+        // The accumulator is in global memory now: release TMEM early.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (etid == 0) {
+          const int old = atomicAdd(&counters[t], 1);
+          const int last = old == splits - 1;
+          if (last) counters[t] = 0;  // re-arm for the next launch
+          *last_flag = last;
+        }
+        named_barrier_sync(1, 128);
+        const int is_last = *last_flag;
+        named_barrier_sync(1, 128);  // last_flag may be rewritten by the next unit
+        if (!is_last) continue;
+        __threadfence();
+      }
+
+      // Fetch 32 (or 16) tile columns of this thread's row: from TMEM, or the
+      // fixed-order (split 0, 1, ...) sum of the partials.
+      auto fetch = [&](int col0, float (&v)[32]) {
+        if (!split) {
+          uint32_t r[32];
+          if constexpr (CW == 32) {
+            tmem_ld_32x32b_x32(t_row + col0, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + col0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] = __uint_as_float(r[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] = 0.f;
+          for (int s2 = 0; s2 < splits; ++s2) {
+            const float4* src = reinterpret_cast<const float4*>(ws_tile + (size_t)s2 * (BM * BN)) +
+                                (size_t)(col0 / 4) * BM + row_in_tile;
+#pragma unroll
+            for (int c4 = 0; c4 < CW / 4; ++c4) {
+              const float4 x = __ldcg(src + (size_t)c4 * BM);
+              v[4 * c4] += x.x;
+              v[4 * c4 + 1] += x.y;
+              v[4 * c4 + 2] += x.z;
+              v[4 * c4 + 3] += x.w;
+            }
+          }
+        }
+      };
+
       if constexpr (EPI == kEpiSiluMul) {
         // Tile columns hold [gate 64 | up 64] blocks; output has BN/2 columns.
 #pragma unroll 1
         for (int blk = 0; blk < BN / 128; ++blk) {
 #pragma unroll 1
           for (int half = 0; half < 2; ++half) {
-            uint32_t g[32], u[32];
-            tmem_ld_32x32b_x32(t_row + blk * 128 + half * 32, g);
-            tmem_ld_32x32b_x32(t_row + blk * 128 + 64 + half * 32, u);
-            tmem_wait_ld();
+            float g[32], uu[32];
+            fetch(blk * 128 + half * 32, g);
+            fetch(blk * 128 + 64 + half * 32, uu);
             const int j0 = tc.nb * (BN / 2) + blk * 64 + half * 32;
             if (i < p_rows) {
               uint32_t packed[16];
 #pragma unroll
               for (int c = 0; c < 16; ++c) {
-                float g0 = __uint_as_float(g[2 * c]), g1 = __uint_as_float(g[2 * c + 1]);
-                float u0 = __uint_as_float(u[2 * c]), u1 = __uint_as_float(u[2 * c + 1]);
-                float o0 = g0 / (1.0f + __expf(-g0)) * u0;
-                float o1 = g1 / (1.0f + __expf(-g1)) * u1;
+                const float g0 = g[2 * c], g1 = g[2 * c + 1];
+                const float o0 = g0 / (1.0f + __expf(-g0)) * uu[2 * c];
+                const float o1 = g1 / (1.0f + __expf(-g1)) * uu[2 * c + 1];
                 packed[c] = pack_bf16x2(o0, o1);
               }
               __nv_bfloat16* dst = C + (size_t)i * ldc + j0;
@@ -250,17 +333,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           }
         }
       } else {
-        constexpr int CW = BN >= 32 ? 32 : 16;  // columns per tcgen05.ld
 #pragma unroll 1
         for (int ch = 0; ch < BN / CW; ++ch) {
-          uint32_t r[32];
-          if constexpr (CW == 32) {
-            tmem_ld_32x32b_x32(t_row + ch * CW, r);
-          } else {
-            uint32_t (&r16)[16] = *reinterpret_cast<uint32_t(*)[16]>(r);
-            tmem_ld_32x32b_x16(t_row + ch * CW, r16);
-          }
-          tmem_wait_ld();
+          float r[32];
+          fetch(ch * CW, r);
           const int j0 = tc.nb * BN + ch * CW;
           if constexpr (!SWAP) {
             if (i < p_rows) {
@@ -269,10 +345,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
               for (int v = 0; v < CW / 8; ++v) {
                 if (j0 + v * 8 + 8 <= q_rows) {
                   uint4 pk;
-                  pk.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-                  pk.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-                  pk.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-                  pk.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+                  pk.x = pack_bf16x2(r[8 * v + 0], r[8 * v + 1]);
+                  pk.y = pack_bf16x2(r[8 * v + 2], r[8 * v + 3]);
+                  pk.z = pack_bf16x2(r[8 * v + 4], r[8 * v + 5]);
+                  pk.w = pack_bf16x2(r[8 * v + 6], r[8 * v + 7]);
                   *reinterpret_cast<uint4*>(dst + v * 8) = pk;
                 }
               }
@@ -284,15 +360,17 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 #pragma unroll
               for (int c = 0; c < CW; ++c) {
                 const int j = j0 + c;
-                if (j < q_rows) C[(size_t)j * ldc + i] = __float2bfloat16_rn(__uint_as_float(r[c]));
+                if (j < q_rows) C[(size_t)j * ldc + i] = __float2bfloat16_rn(r[c]);
               }
             }
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (!split) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      }
     }
   }
 
@@ -304,9 +382,20 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   }
 }
 
+// Process-wide split-K workspace per device (fp32 partial tiles + arrival
+// counters that the last-arriving CTA re-arms). Configured once at start-up.
+struct SplitWorkspace {
+  float* ws = nullptr;
+  size_t ws_bytes = 0;
+  int* counters = nullptr;
+  int n_counters = 0;
+};
+SplitWorkspace g_split_ws[64];
+
 template <int BN, int STAGES, bool SWAP, int EPI>
 void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, int K, int ldp,
-                int ldq, int ldc, unsigned int* err, cudaStream_t stream) {
+                int ldq, int ldc, int splits, float* ws, int* counters, unsigned int* err,
+                cudaStream_t stream) {
   using S = Smem<BN, STAGES>;
   auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI>;
   static bool attr_set = false;  // per instantiation; idempotent if raced
@@ -323,60 +412,161 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
                                 (uint64_t)ldq * 2, BN, BK);
   int dev = 0;
   cudaGetDevice(&dev);
-  const int tiles = ((p_rows + BM - 1) / BM) * ((q_rows + BN - 1) / BN);
-  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  const long units = (long)((p_rows + BM - 1) / BM) * ((q_rows + BN - 1) / BN) * splits;
+  const int grid = units < num_sms(dev) ? (int)units : num_sms(dev);
   kernel<<<grid, kThreads, S::kTotal, stream>>>(tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                                p_rows, q_rows, K, err);
+                                                p_rows, q_rows, K, splits, ws, counters, err);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc launch: ") + cudaGetErrorString(e));
 }
 
+int cfg_bn(int cfg) {
+  switch (cfg) {
+    case kCfgN256: return 256;
+    case kCfgN128: return 128;
+    case kCfgSwap16: return 16;
+    case kCfgSwap32: return 32;
+    case kCfgSwap64: return 64;
+  }
+  return 0;
+}
+bool cfg_swap(int cfg) { return cfg == kCfgSwap16 || cfg == kCfgSwap32 || cfg == kCfgSwap64; }
+
 }  // namespace
 
-int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm) {
-  // Swap-AB for small token counts: the weight fills the 128-row M side.
+GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
+  // Candidate tile shapes: swap-AB (weights on the 128-row side) for small M.
+  int cands[3];
+  int nc = 0;
   if (epi == kEpiNone && M <= 64) {
-    if (M <= 16) return kCfgSwap16;
-    if (M <= 32) return kCfgSwap32;
-    return kCfgSwap64;
+    cands[nc++] = M <= 16 ? kCfgSwap16 : (M <= 32 ? kCfgSwap32 : kCfgSwap64);
+  } else {
+    cands[nc++] = kCfgN256;
+    cands[nc++] = kCfgN128;
   }
-  const long tiles256 = (long)((M + 127) / 128) * ((N + 255) / 256);
-  const long tiles128 = (long)((M + 127) / 128) * ((N + 127) / 128);
-  if (tiles256 >= 2L * num_sm) return kCfgN256;
-  if (tiles128 >= num_sm || epi == kEpiSiluMul) return tiles256 >= num_sm ? kCfgN256 : kCfgN128;
-  return kCfgN128;
+  const int num_kb = (K + 63) / 64;
+  GemmPlan best{cands[0], 1};
+  double best_cost = 1e30;
+  for (int ci = 0; ci < nc; ++ci) {
+    const int cfg = cands[ci];
+    const int bn = cfg_bn(cfg);
+    const bool swap = cfg_swap(cfg);
+    const long p = swap ? N : M, qq = swap ? M : N;
+    const long tiles = ((p + 127) / 128) * ((qq + bn - 1) / bn);
+    for (int s = 1; s <= 8; ++s) {
+      const int kb_per = (num_kb + s - 1) / s;
+      if (s > 1 && kb_per < 4) break;
+      const long units = tiles * s;
+      const long waves = (units + num_sm - 1) / num_sm;
+      // Relative cost model: MMA time per k-block grows with BN, plus a fixed
+      // per-k-block latency share, per-unit prologue/epilogue, and the split
+      // partial-sum traffic.
+      const double per_kb = bn / 256.0 + 0.25;
+      double t_unit = kb_per * per_kb + 3.0;
+      if (s > 1) t_unit += 2.0 + s * (bn / 256.0) * 0.5;
+      const double cost = waves * t_unit;
+      if (cost < best_cost * 0.97) {
+        best_cost = cost;
+        best = {cfg, s};
+      }
+    }
+  }
+  return best;
 }
 
-void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
-                      int ldc, int epi, int cfg, unsigned int* err, cudaStream_t stream) {
+int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm) {
+  return gemm_bf16_plan(M, N, K, epi, num_sm).cfg;
+}
+
+void gemm_configure_workspace(int device, size_t ws_bytes, int n_counters) {
+  SplitWorkspace& w = g_split_ws[device];
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  if (w.ws) cudaFree(w.ws);
+  if (w.counters) cudaFree(w.counters);
+  w = SplitWorkspace{};
+  cudaError_t e = cudaSuccess;
+  if (ws_bytes > 0) e = cudaMalloc(&w.ws, ws_bytes);
+  if (e == cudaSuccess && n_counters > 0) e = cudaMalloc(&w.counters, sizeof(int) * n_counters);
+  if (e == cudaSuccess && n_counters > 0) e = cudaMemset(w.counters, 0, sizeof(int) * n_counters);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("gemm workspace: ") + cudaGetErrorString(e));
+  w.ws_bytes = ws_bytes;
+  w.n_counters = n_counters;
+}
+
+size_t gemm_workspace_bytes(int device) { return g_split_ws[device].ws_bytes; }
+float* gemm_ws_ptr(int device) { return g_split_ws[device].ws; }
+int* gemm_counters_ptr(int device) { return g_split_ws[device].counters; }
+int gemm_n_counters(int device) { return g_split_ws[device].n_counters; }
+
+void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,
+                            int ldw, int ldc, int epi, int cfg, int splits, float* ws,
+                            size_t ws_bytes, int* counters, int n_counters, unsigned int* err,
+                            cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return;
   if (K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0)
     throw std::runtime_error("gemm_bf16: K and leading dims must be multiples of 8");
   if (N % 8 != 0 || ldc % 8 != 0) throw std::runtime_error("gemm_bf16: N, ldc must be multiples of 8");
   int dev = 0;
   cudaGetDevice(&dev);
-  if (cfg < 0) cfg = gemm_bf16_pick_config(M, N, K, epi, num_sms(dev));
+  if (cfg < 0) {
+    GemmPlan pl = gemm_bf16_plan(M, N, K, epi, num_sms(dev));
+    cfg = pl.cfg;
+    if (splits <= 0) splits = pl.splits;
+  }
+  if (splits <= 0) splits = 1;
+  if (epi == kEpiSiluMul && cfg_swap(cfg)) cfg = kCfgN128;
+  const int bn = cfg_bn(cfg);
+  if (bn == 0) throw std::runtime_error("gemm_bf16: unknown config " + std::to_string(cfg));
+  const bool swap = cfg_swap(cfg);
+  const long p = swap ? N : M, qq = swap ? M : N;
+  const long tiles = ((p + 127) / 128) * ((qq + bn - 1) / bn);
+  const int num_kb = (K + 63) / 64;
+  if (splits > num_kb) splits = num_kb;
+  if (splits > 1) {
+    const size_t need = (size_t)tiles * splits * 128 * bn * sizeof(float);
+    if (ws == nullptr || need > ws_bytes || tiles > n_counters) splits = 1;  // no room: no split
+  }
+  float* wsp = splits > 1 ? ws : nullptr;
+  int* cnt = splits > 1 ? counters : nullptr;
   if (epi == kEpiSiluMul) {
     if (N % 128 != 0) throw std::runtime_error("gemm_bf16 silu_mul: N must be a multiple of 128");
     if (cfg == kCfgN256)
-      return launch_cfg<256, 4, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, err, stream);
-    return launch_cfg<128, 6, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, err, stream);
+      return launch_cfg<256, 4, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp,
+                                                    cnt, err, stream);
+    return launch_cfg<128, 6, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp,
+                                                  cnt, err, stream);
   }
   switch (cfg) {
     case kCfgN256:
-      return launch_cfg<256, 4, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, err, stream);
+      return launch_cfg<256, 4, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt,
+                                                 err, stream);
     case kCfgN128:
-      return launch_cfg<128, 6, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, err, stream);
+      return launch_cfg<128, 6, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt,
+                                                 err, stream);
     case kCfgSwap16:
-      return launch_cfg<16, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, err, stream);
+      return launch_cfg<16, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt,
+                                               err, stream);
     case kCfgSwap32:
-      return launch_cfg<32, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, err, stream);
+      return launch_cfg<32, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt,
+                                               err, stream);
     case kCfgSwap64:
-      return launch_cfg<64, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, err, stream);
-    default:
-      throw std::runtime_error("gemm_bf16: unknown config " + std::to_string(cfg));
+      return launch_cfg<64, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt,
+                                               err, stream);
   }
+}
+
+void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
+                      int ldc, int epi, int cfg, unsigned int* err, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const SplitWorkspace& w = g_split_ws[dev];
+  gemm_bf16_launch_split(A, W, C, M, N, K, lda, ldw, ldc, epi, cfg, cfg < 0 ? 0 : 1, w.ws,
+                         w.ws_bytes, w.counters, w.n_counters, err, stream);
 }
 
 }  // namespace b200

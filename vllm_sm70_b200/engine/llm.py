@@ -1,0 +1,251 @@
+"""``LLM``: the offline-inference entry point of the runtime.
+
+    llm = LLM("llama-3.1-8b", tensor_parallel_size=1, load_format="dummy")
+    outs = llm.generate(prompt_token_ids, SamplingParams(max_tokens=256, ignore_eos=True))
+
+Scheduling: requests are admitted while a batch slot and the KV blocks for
+``prompt + max_tokens`` are free; admitted prompts are prefilled in chunks
+of at most ``max_num_batched_tokens`` tokens (long prompts are split across
+chunks, the attention kernel reads the cached prefix), then all running
+requests decode together in CUDA-graph steps until the next request
+finishes; finished requests release their slot and blocks and waiting ones
+are admitted. Under ``torchrun`` every rank constructs the same ``LLM`` and
+runs the same schedule (decisions depend only on rank-uniform inputs).
+
+Reference parity: the reference serves through upstream vLLM ``LLM`` /
+``vllm serve``; this in-repo runner is the engine the B200
+kernels and fused collectives run under (also exposed to vLLM through the
+platform plugin, ``vllm_sm70_b200.integration``).
+"""
+from __future__ import annotations
+
+import math
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+import torch
+
+from ..models import build_model
+from ..models.config import ModelConfig, resolve
+from ..parallel import state as pstate
+from .model_runner import ModelRunner
+from .sampling_params import RequestOutput, SamplingParams
+
+
+@dataclass
+class _Req:
+    rid: int
+    prompt: torch.Tensor           # int64 CPU
+    params: SamplingParams
+    slot: int = -1
+    blocks: torch.Tensor | None = None
+    prefilled: int = 0
+    generated: int = 0
+    done: bool = False
+    out: list = field(default_factory=list)
+    t_first: float | None = None
+    t_last: float | None = None
+
+
+@dataclass
+class GenerateStats:
+    prefill_ms: float = 0.0
+    decode_ms: float = 0.0
+    total_ms: float = 0.0
+    decode_steps: int = 0
+    ttft_ms: list = field(default_factory=list)
+    tpot_ms: list = field(default_factory=list)
+
+
+class LLM:
+    def __init__(self, model: str | ModelConfig | dict = "llama-3.1-8b",
+                 tensor_parallel_size: int | None = None, max_num_seqs: int = 256,
+                 max_model_len: int = 4096, block_size: int = 16,
+                 max_num_batched_tokens: int = 16384, gpu_memory_utilization: float = 0.90,
+                 load_format: str = "dummy", seed: int = 0, enforce_eager: bool = False,
+                 dtype=torch.bfloat16, num_kv_blocks: int | None = None):
+        self.cfg: ModelConfig = resolve(model)
+        ps = pstate.get() if pstate._STATE is not None else None
+        if ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
+            ps = pstate.init(tp_size=tensor_parallel_size)
+        self.ps = ps
+        self.device = ps.device
+        self.max_num_batched_tokens = max_num_batched_tokens
+        self.model = build_model(self.cfg, self.device, dtype, ps)
+        if load_format == "dummy":
+            self.model.init_dummy(seed=seed)
+        else:
+            from ..models.loader import load_checkpoint
+
+            load_checkpoint(self.model, model)
+        if self.device.type == "cuda":
+            from .. import _ext
+
+            _ext.require()
+            from ..ops import linear as _linear
+
+            torch.ops._b200_C.init_device(self.device.index or 0)
+            _linear.configure_workspace(self.device.index or 0)
+            torch.cuda.synchronize()
+        if num_kv_blocks is None:
+            num_kv_blocks = self._size_kv(max_num_seqs, max_model_len, block_size,
+                                          gpu_memory_utilization)
+        num_sms = (torch.cuda.get_device_properties(self.device).multi_processor_count
+                   if self.device.type == "cuda" else 148)
+        self.runner = ModelRunner(self.model, max_num_seqs, max_model_len, block_size,
+                                  num_kv_blocks, self.device, use_graphs=not enforce_eager,
+                                  num_sms=num_sms)
+        self.runner.capture()
+        self.last_stats: GenerateStats | None = None
+
+    def shutdown(self) -> None:
+        """Release CUDA graphs (they may hold NCCL work) before the process
+        group is destroyed."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize()
+        self.runner.release_graphs()
+
+    def _size_kv(self, max_num_seqs, max_model_len, block_size, util) -> int:
+        m = self.model
+        n_attn = len(getattr(m, "attn_layer_ids", range(self.cfg.num_layers)))
+        per_block = 2 * n_attn * m.hkv * block_size * m.d * 2
+        need = max_num_seqs * math.ceil(max_model_len / block_size) + 1
+        if self.device.type != "cuda":
+            return min(need, 4096)
+        free, total = torch.cuda.mem_get_info(self.device)
+        T = self.max_num_batched_tokens
+        h = self.cfg.hidden_size
+        act = T * (2 * h + 3 * max(self.cfg.intermediate_size, 1) // max(self.ps.tp_size, 1)
+                   + (m.hq + 2 * m.hkv) * m.d * 2) * 2 * 2
+        reserve = act + (4 << 30) + int((1 - util) * total)
+        budget = max(0, free - reserve)
+        return int(max(2, min(need, budget // per_block)))
+
+    # ------------------------------------------------------------------ API
+    def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
+                 collect_stats: bool = True) -> list[RequestOutput]:
+        if sampling_params is None:
+            sampling_params = SamplingParams()
+        if isinstance(prompt_token_ids, torch.Tensor):
+            prompts = [row for row in prompt_token_ids.to(torch.int64)]
+        else:
+            prompts = [torch.as_tensor(p, dtype=torch.int64) for p in prompt_token_ids]
+        params = (sampling_params if isinstance(sampling_params, list)
+                  else [sampling_params] * len(prompts))
+        for p in params:
+            if not p.greedy:
+                raise NotImplementedError("temperature sampling: use greedy (temperature=0) "
+                                          "or the hidden-state sampler in serving mode")
+        reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
+        runner = self.runner
+        bs = runner.block_size
+        waiting = deque(reqs)
+        running: list[_Req] = []
+        free_slots = list(range(runner.B - 1, -1, -1))
+        stats = GenerateStats()
+        cuda = self.device.type == "cuda"
+        ev = (lambda: torch.cuda.Event(enable_timing=True)) if cuda else None
+        t0 = ev() if cuda else None
+        if cuda:
+            t0.record()
+        wall0 = time.perf_counter()
+        pending_first: list[tuple[object, list[_Req]]] = []
+        decode_events: list[tuple[object, list[_Req], int]] = []
+
+        while waiting or running:
+            # ---- admission
+            admitted: list[_Req] = []
+            while waiting and free_slots:
+                r = waiting[0]
+                L = r.prompt.numel()
+                total = L + r.params.max_tokens
+                if total > runner.max_model_len:
+                    raise ValueError(f"request {r.rid}: {total} tokens > max_model_len")
+                nblk = math.ceil(total / bs)
+                if runner.alloc.num_free() < nblk:
+                    break
+                waiting.popleft()
+                r.slot = free_slots.pop()
+                r.blocks = runner.alloc.allocate(nblk)
+                runner.set_block_row(r.slot, r.blocks)
+                admitted.append(r)
+            if not admitted and not running:
+                raise RuntimeError("cannot admit any request: KV cache too small")
+            # ---- chunked prefill of the admitted prompts
+            queue = deque(admitted)
+            while queue:
+                budget = self.max_num_batched_tokens
+                pieces, finishing = [], []
+                while queue and budget > 0:
+                    r = queue[0]
+                    n = min(budget, r.prompt.numel() - r.prefilled)
+                    last = r.prefilled + n == r.prompt.numel()
+                    pieces.append((r.slot, r.prompt[r.prefilled:r.prefilled + n], r.prefilled,
+                                   last, r.prompt.numel()))
+                    r.prefilled += n
+                    budget -= n
+                    if last:
+                        queue.popleft()
+                        finishing.append(r)
+                runner.prefill(pieces)
+                for r in finishing:
+                    r.generated = 1
+                if cuda and finishing:
+                    e = ev()
+                    e.record()
+                    pending_first.append((e, finishing))
+                running.extend(finishing)
+            # ---- decode until the next request finishes
+            live = [r for r in running if not r.done]
+            finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+            if not finished_now:
+                steps = min(r.params.max_tokens - r.generated for r in live)
+                n_rows = max(r.slot for r in live) + 1
+                runner.decode(n_rows, steps)
+                stats.decode_steps += steps
+                for r in live:
+                    r.generated += steps
+                finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+                if cuda:
+                    e = ev()
+                    e.record()
+                    decode_events.append((e, finished_now, steps))
+            # ---- retire
+            if finished_now:
+                slots = [r.slot for r in finished_now]
+                runner.deactivate(slots)
+                outs = runner.out_tokens[torch.tensor(slots, device=self.device)]
+                outs_h = outs.to("cpu", non_blocking=False)
+                for r, row in zip(finished_now, outs_h):
+                    r.out = row[: r.params.max_tokens].tolist()
+                    r.done = True
+                    runner.alloc.free(r.blocks)
+                    free_slots.append(r.slot)
+                running = [r for r in running if not r.done]
+        if cuda:
+            t_end = ev()
+            t_end.record()
+            t_end.synchronize()
+            for e, rs in pending_first:
+                ms = t0.elapsed_time(e)
+                for r in rs:
+                    r.t_first = ms
+            for e, rs, _ in decode_events:
+                ms = t0.elapsed_time(e)
+                for r in rs:
+                    r.t_last = ms
+            stats.total_ms = t0.elapsed_time(t_end)
+        else:
+            stats.total_ms = (time.perf_counter() - wall0) * 1e3
+        outs = []
+        for r in reqs:
+            if r.t_first is not None:
+                stats.ttft_ms.append(r.t_first)
+                if r.t_last is not None and len(r.out) > 1:
+                    stats.tpot_ms.append((r.t_last - r.t_first) / (len(r.out) - 1))
+            outs.append(RequestOutput(r.rid, r.prompt.tolist(), r.out, True,
+                                      None if r.t_first is None else r.t_first / 1e3,
+                                      None if not stats.tpot_ms else stats.tpot_ms[-1] / 1e3))
+        self.last_stats = stats
+        return outs

@@ -1,0 +1,210 @@
+"""Model runner: paged KV cache, device-resident decode state, chunked
+prefill, and CUDA-graph-captured decode steps.
+
+Decode metadata never leaves the device. Per batch slot the runner keeps
+``seq_lens``, ``active``, the block-table row, the next input id and the
+output cursor; a decode step derives positions / slot mappings from them,
+runs the model, samples, appends the token to ``out_tokens`` and advances
+the counters -- all inside one CUDA graph, so a step costs one graph launch
+and no host<->device traffic. Blocks for ``prompt + max_tokens`` are
+reserved at admission, so the block table is static while a request decodes.
+Padded graph rows (``active == 0``) read and write only the reserved scratch
+block 0.
+
+Reference parity: upstream vLLM ``GPUModelRunner`` + the reference's graph
+policy (``sm70/vllm_sm70/graph_policy.py:64-110``: capture sizes, decode-only
+FULL graphs) and its lesson that host metadata building becomes the
+bottleneck (``docs/history/sm70_flint_tp2_pcie.md:716-730``).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import envs
+from ..utils import launch_count
+from ..models.layers import AttnMeta, KVCache
+from .block_manager import build_prefill_meta, make_allocator
+
+
+def default_capture_sizes(max_bs: int) -> list[int]:
+    sizes = [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512]
+    out = [s for s in sizes if s < max_bs] + [max_bs]
+    return sorted(set(out))
+
+
+class ModelRunner:
+    def __init__(self, model, max_num_seqs: int, max_model_len: int, block_size: int,
+                 num_blocks: int, device: torch.device, use_graphs: bool = True,
+                 num_sms: int = 148):
+        self.model = model
+        self.cfg = model.cfg
+        self.device = device
+        self.B = max_num_seqs
+        self.block_size = block_size
+        self.max_model_len = max_model_len
+        self.max_blocks = math.ceil(max_model_len / block_size)
+        self.num_blocks = num_blocks
+        self.num_sms = num_sms
+        self.kv = KVCache.allocate(self.cfg.num_layers, num_blocks, model.hkv, block_size,
+                                   model.d, dtype=model.dtype, device=device,
+                                   layers=getattr(model, "attn_layer_ids", None))
+        self.alloc = make_allocator(num_blocks, reserved=1)
+        B, dev = self.B, device
+        self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.seq_lens = torch.ones(B, dtype=torch.int32, device=dev)
+        self.active = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.block_table = torch.zeros(B, self.max_blocks, dtype=torch.int32, device=dev)
+        self.cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
+        self.out_cap = max_model_len
+        self.out_tokens = torch.zeros(B, self.out_cap, dtype=torch.int32, device=dev)
+        self.out_pos = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.row_base = torch.arange(B, dtype=torch.int64, device=dev) * self.out_cap
+        self.bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32).pin_memory() \
+            if dev.type == "cuda" else torch.zeros(B, self.max_blocks, dtype=torch.int32)
+        self.use_graphs = use_graphs and dev.type == "cuda" and envs.get("VLLM_B200_CUDA_GRAPHS")
+        self.capture_sizes = default_capture_sizes(B)
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: dict[int, int] = {}
+        self.split_bufs: dict[int, tuple] = {}
+        self.pool = None
+
+    # ------------------------------------------------------------ block tables
+    def set_block_row(self, slot: int, blocks: torch.Tensor) -> None:
+        n = blocks.numel()
+        self.bt_host[slot].zero_()
+        self.bt_host[slot, :n] = blocks
+        self.block_table[slot].copy_(self.bt_host[slot], non_blocking=True)
+
+    # ------------------------------------------------------------ decode
+    def _splits_for(self, b: int) -> int:
+        work = b * self.model.hkv
+        return max(1, min(16, math.ceil(2 * self.num_sms / max(work, 1))))
+
+    def _split_buffers(self, b: int):
+        if b not in self.split_bufs:
+            ns = self._splits_for(b)
+            if ns > 1:
+                po = torch.empty(ns, b, self.model.hq, self.model.d, device=self.device)
+                pml = torch.empty(ns, b, self.model.hq, 2, device=self.device)
+            else:
+                po = pml = None
+            self.split_bufs[b] = (ns, po, pml)
+        return self.split_bufs[b]
+
+    def _decode_body(self, b: int) -> None:
+        bs = self.block_size
+        sl = self.seq_lens[:b]
+        pos = sl.to(torch.int64) - 1
+        bt = self.block_table[:b]
+        blk = torch.gather(bt, 1, (pos // bs).unsqueeze(1)).squeeze(1).to(torch.int64)
+        slots = blk * bs + pos % bs
+        ns, po, pml = self._split_buffers(b)
+        meta = AttnMeta(positions=pos, slot_mapping=slots, block_table=bt, seq_lens=sl,
+                        cu_q=self.cu_q[: b + 1], max_q_len=1, decode=True, num_splits=ns,
+                        part_o=po, part_ml=pml)
+        h = self.model.forward(self.ids[:b], meta, self.kv)
+        nxt = self.model.greedy(h)
+        self.ids[:b].copy_(nxt)
+        self.out_tokens.view(-1).index_copy_(0, self.row_base[:b] + self.out_pos[:b], nxt)
+        act = self.active[:b]
+        self.out_pos[:b] += act
+        self.seq_lens[:b] += act
+
+    def bucket(self, n_rows: int) -> int:
+        for s in self.capture_sizes:
+            if s >= n_rows:
+                return s
+        raise ValueError(f"batch {n_rows} exceeds max_num_seqs {self.B}")
+
+    def capture(self, sizes: list[int] | None = None) -> None:
+        """Capture decode graphs (call at start-up, with no active requests)."""
+        if not self.use_graphs:
+            return
+        sizes = sizes or self.capture_sizes
+        assert int(self.active.sum()) == 0, "capture needs an idle runner"
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for b in sizes:
+                self._decode_body(b)  # warm-up: allocators, GEMM attributes
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+        for b in sorted(sizes, reverse=True):
+            g = torch.cuda.CUDAGraph()
+            before = launch_count.total()
+            with torch.cuda.graph(g, pool=self.pool):
+                self._decode_body(b)
+            self.graph_launches[b] = launch_count.total() - before
+            self.graphs[b] = g
+        torch.cuda.synchronize()
+        # Capture/warm-up touched padded rows only; reset their counters.
+        self.out_pos.zero_()
+        self.seq_lens.fill_(1)
+
+    def decode(self, n_rows: int, steps: int) -> None:
+        b = self.bucket(n_rows)
+        g = self.graphs.get(b)
+        for _ in range(steps):
+            if g is not None:
+                g.replay()
+            else:
+                self._decode_body(b)
+        if g is not None:
+            launch_count.add(self.graph_launches[b] * steps)
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        self.pool = None
+
+    # ------------------------------------------------------------ prefill
+    def prefill(self, pieces: list[tuple[int, torch.Tensor, int, bool, int]]) -> None:
+        """``pieces``: (slot, token ids [n] int64 CPU, ctx_start, is_last, total_len)."""
+        dev = self.device
+        S = len(pieces)
+        toks = torch.cat([p[1] for p in pieces])
+        q_len = torch.tensor([p[1].numel() for p in pieces], dtype=torch.int32)
+        ctx = torch.tensor([p[2] for p in pieces], dtype=torch.int32)
+        slots_idx = [p[0] for p in pieces]
+        bt_rows = self.bt_host[slots_idx]
+        pos, slot_map = build_prefill_meta(bt_rows, ctx, q_len, self.block_size)
+        seq_lens = ctx + q_len
+        cu = torch.zeros(S + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(q_len, 0)
+        pin = dev.type == "cuda"
+
+        def h2d(t):
+            return (t.pin_memory() if pin else t).to(dev, non_blocking=True)
+
+        ids_d = h2d(toks)
+        meta = AttnMeta(positions=h2d(pos), slot_mapping=h2d(slot_map),
+                        block_table=h2d(bt_rows), seq_lens=h2d(seq_lens), cu_q=h2d(cu),
+                        max_q_len=int(q_len.max()), decode=False)
+        h = self.model.forward(ids_d, meta, self.kv)
+        last = [i for i, p in enumerate(pieces) if p[3]]
+        if not last:
+            return
+        rows = h2d(torch.tensor([int(cu[i + 1]) - 1 for i in last], dtype=torch.int64))
+        nxt = self.model.greedy(h.index_select(0, rows))
+        sidx = h2d(torch.tensor([pieces[i][0] for i in last], dtype=torch.int64))
+        total = h2d(torch.tensor([pieces[i][4] + 1 for i in last], dtype=torch.int32))
+        self.ids.index_copy_(0, sidx, nxt.to(torch.int64))
+        self.seq_lens.index_copy_(0, sidx, total)
+        self.out_tokens.view(-1).index_copy_(0, self.row_base.index_select(0, sidx), nxt)
+        self.out_pos.index_fill_(0, sidx, 1)
+        self.active.index_fill_(0, sidx, 1)
+
+    def deactivate(self, slots: list[int]) -> None:
+        if not slots:
+            return
+        idx = torch.tensor(slots, dtype=torch.int64, device=self.device)
+        self.active.index_fill_(0, idx, 0)
+        self.seq_lens.index_fill_(0, idx, 1)
+        self.out_pos.index_fill_(0, idx, 0)
+        self.block_table.index_fill_(0, idx, 0)
+        for s in slots:
+            self.bt_host[s].zero_()

@@ -24,6 +24,7 @@ import torch
 
 from .. import ops
 from ..parallel import comm, state as pstate
+from ..utils import launch_count
 from .config import ModelConfig
 from .layers import AttnMeta, DenseLinear, GateUpLinear, KVCache
 
@@ -156,6 +157,7 @@ class LlamaModel:
         out = torch.empty(ids.shape[0], self.cfg.hidden_size, device=ids.device, dtype=self.dtype)
         if ids.is_cuda:
             torch.ops._b200_C.embedding(out, ids, self.embed, self.vocab_start)
+            launch_count.add(1)
         else:
             loc = ids - self.vocab_start
             ok = (loc >= 0) & (loc < self.embed.shape[0])

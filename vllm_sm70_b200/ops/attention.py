@@ -17,6 +17,7 @@ import math
 import torch
 
 from .. import _ext, envs
+from ..utils import launch_count
 
 
 # --------------------------------------------------------------------------
@@ -142,6 +143,7 @@ def paged_attention(out: torch.Tensor, q: torch.Tensor, k_cache: torch.Tensor,
         torch.ops._b200_C.paged_attention(out, q, k_cache, v_cache, block_table, seq_lens, cu_q,
                                           max_q_len, scale, window, sinks, decode, num_splits,
                                           part_o, part_ml)
+        launch_count.add(2 if (decode and num_splits > 1) else 1)
         return out
     out.copy_(paged_attention_ref(q, k_cache, v_cache, block_table, seq_lens, cu_q, scale,
                                   window, sinks).to(out.dtype))
@@ -218,6 +220,7 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
         _ext.require()
         torch.ops._b200_C.rope_kv_write(qkv, positions, cos_sin, k_cache, v_cache, slots, hq, hkv,
                                         q_norm, k_norm, eps)
+        launch_count.add(1)
         return
     rope_kv_write_ref(qkv, positions, cos_sin, k_cache, v_cache, slots, hq, hkv, q_norm, k_norm,
                       eps)

@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 
 from .. import _ext, envs
+from ..utils import launch_count
 
 GATE_UP_BLOCK = 64
 
@@ -25,13 +26,38 @@ def _use_native(t: torch.Tensor) -> bool:
     return True
 
 
+DEFAULT_WS_BYTES = 64 << 20
+DEFAULT_WS_COUNTERS = 16384
+_ws_configured: set = set()
+
+
+def configure_workspace(device: int, ws_bytes: int = DEFAULT_WS_BYTES,
+                        n_counters: int = DEFAULT_WS_COUNTERS) -> None:
+    """Allocate the per-device split-K workspace (fp32 partial tiles + arrival
+    counters). Call once at start-up, before any CUDA-graph capture; GEMMs
+    planned with split-K fall back to one split when it is absent or too small.
+    Reference parity: ``sm70_gemm_configure_workspace``
+    (``sm70/csrc/turbomind/ops/gemm_runtime.cpp:825-897``)."""
+    _ext.require()
+    torch.ops._b200_C.gemm_configure_workspace(device, ws_bytes, n_counters)
+    _ws_configured.add(device)
+
+
+def plan(M: int, N: int, K: int, epi: int = 0, num_sm: int = 148) -> tuple[int, int]:
+    """(tile config, split-K) chosen by the native planner."""
+    _ext.require()
+    c, s = torch.ops._b200_C.gemm_bf16_plan(M, N, K, epi, num_sm)
+    return int(c), int(s)
+
+
 def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
-         cfg: int = -1) -> torch.Tensor:
+         cfg: int = -1, splits: int = 0) -> torch.Tensor:
     """``x[M, K] @ w[N, K].T`` in bf16 with fp32 accumulation."""
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
     if _use_native(x):
-        torch.ops._b200_C.gemm_bf16_out(out, x, w, cfg)
+        torch.ops._b200_C.gemm_bf16_out(out, x, w, cfg, splits)
+        launch_count.add(1)
     else:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))
     return out
@@ -66,12 +92,14 @@ def gemm_silu_mul(x: torch.Tensor, w_interleaved: torch.Tensor,
         out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
     if _use_native(x) and envs.get("VLLM_B200_GEMM_SILU_EPILOGUE"):
         torch.ops._b200_C.gemm_bf16_silu_mul_out(out, x, w_interleaved, cfg)
+        launch_count.add(1)
         return out
     wg, wu = deinterleave_gate_up(w_interleaved)
     if _use_native(x):
         gu = torch.empty(x.shape[0], 2 * n, dtype=x.dtype, device=x.device)
         gemm(x, torch.cat([wg, wu], 0), out=gu)
         torch.ops._b200_C.silu_mul(out, gu)
+        launch_count.add(1)
         return out
     g = x.float() @ wg.float().t()
     u = x.float() @ wu.float().t()
@@ -87,6 +115,7 @@ def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     if x.is_cuda:
         _ext.require()
         torch.ops._b200_C.silu_mul(out, x)
+        launch_count.add(1)
     else:
         out.copy_(silu_mul_ref(x[..., :n], x[..., n:]))
     return out

@@ -9,6 +9,7 @@ from __future__ import annotations
 import torch
 
 from .. import _ext
+from ..utils import launch_count
 
 
 def rms_norm_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -24,6 +25,7 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
     if x.is_cuda:
         _ext.require()
         torch.ops._b200_C.rms_norm(out, x, w, eps)
+        launch_count.add(1)
     else:
         out.copy_(rms_norm_ref(x, w, eps))
     return out
@@ -35,6 +37,7 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
     if x.is_cuda:
         _ext.require()
         torch.ops._b200_C.fused_add_rms_norm(x, residual, w, eps)
+        launch_count.add(1)
         return
     s = (x.float() + residual.float()).to(x.dtype)
     residual.copy_(s)

@@ -10,6 +10,7 @@ from __future__ import annotations
 import torch
 
 from .. import _ext
+from ..utils import launch_count
 
 
 def argmax_ref(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -38,6 +39,7 @@ def argmax(logits: torch.Tensor, id_offset: int = 0,
     if logits.is_cuda:
         _ext.require()
         torch.ops._b200_C.argmax(ids, vals, logits, id_offset)
+        launch_count.add(1)
     else:
         i, v = argmax_ref(logits)
         ids.copy_(i + id_offset)

@@ -1,0 +1,55 @@
+"""TP/EP communication entry points used by the models.
+
+Each entry point has two paths:
+
+* fused -- one kernel over symmetric (peer-mapped) memory that performs the
+  collective and the following compute (``parallel/symm.py`` +
+  ``csrc/comm/*``), selected when the symmetric workspace is set up and the
+  kill switch is on;
+* baseline -- NCCL through ``torch.distributed`` followed by the unfused op.
+
+The path choice depends only on rank-uniform inputs (config, env, shapes),
+so every rank enters the same collective -- the reference's rule
+(``sm70/vllm_sm70/sample.py:230-271``, ``sample_greedy.py:171-205``).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import envs, ops
+from . import state as pstate
+
+_fused = {"ar_rmsnorm": None}
+
+
+def set_fused_ar_rmsnorm(impl) -> None:
+    """Install the fused all-reduce + add + RMSNorm implementation (callable
+    ``impl(x, residual, w, eps) -> bool``; False = not admitted, use NCCL)."""
+    _fused["ar_rmsnorm"] = impl
+
+
+def all_reduce_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                            eps: float) -> None:
+    """In place: ``x <- allreduce_tp(x)``; ``residual += x``; ``x <- rmsnorm(residual) w``."""
+    st = pstate.get()
+    if st.tp_size > 1:
+        impl = _fused["ar_rmsnorm"]
+        if impl is not None and envs.get("VLLM_B200_FUSED_AR_RMSNORM") and impl(x, residual, w, eps):
+            return
+        dist.all_reduce(x, group=st.tp_group)
+    ops.fused_add_rms_norm(x, residual, w, eps)
+
+
+def greedy_merge(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    """Gather per-rank (max value, id) pairs and pick the global top-1 in rank
+    order with the shared tie rule. Reference parity: F12 greedy
+    (``sm70/vllm_sm70/sample_greedy.py:293-328``)."""
+    st = pstate.get()
+    if st.tp_size == 1:
+        return ids
+    rows = ids.shape[0]
+    packed = torch.stack([vals.float(), ids.float()], 0)  # ids < 2^24 are exact in fp32
+    allp = torch.empty(st.tp_size, 2, rows, dtype=torch.float32, device=ids.device)
+    dist.all_gather_into_tensor(allp, packed.contiguous(), group=st.tp_group)
+    return ops.sampling.merge_rank_top1(allp[:, 0], allp[:, 1].to(torch.int64))

@@ -1,0 +1,188 @@
+"""Kernel microbenchmarks (CUDA-event timed, after warm-up).
+
+    python -m vllm_sm70_b200.perf.microbench gemm --M 256 --N 6144 --K 4096
+    python -m vllm_sm70_b200.perf.microbench decode-attn --batch 256 --ctx 1152
+    python -m vllm_sm70_b200.perf.microbench prefill-attn --seqs 16 --len 1024
+    python -m vllm_sm70_b200.perf.microbench all
+
+Each case prints one JSON line with the device time per launch and the
+achieved fraction of the measured roofline (``MEASURED_PEAKS.json`` when
+present: HBM GB/s for bandwidth-bound kernels, bf16 TFLOP/s for GEMMs).
+Inputs are sized above the 126 MB L2 where the case allows, or the L2 is
+flushed between iterations (``--flush``).
+
+Reference parity: ``sm70/tools/bench_fv100_capture.py`` (attention
+microbench) and the reference's per-kernel GB/s tables.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parents[2]
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+_FLUSH = None
+
+
+def flush_l2():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _FLUSH.zero_()
+
+
+def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = False) -> float:
+    """Mean device ms per call (CUDA events on the current stream)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if not flush:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / iters
+    tot = 0.0
+    for _ in range(iters):
+        flush_l2()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        tot += s.elapsed_time(e)
+    return tot / iters
+
+
+def _setup():
+    from .. import _ext
+    from ..ops import linear
+
+    _ext.require()
+    dev = torch.cuda.current_device()
+    torch.ops._b200_C.init_device(dev)
+    linear.configure_workspace(dev)
+
+
+def bench_gemm(M, N, K, cfg=-1, splits=0, iters=20, flush=False, cublas=True):
+    from ..ops import linear
+
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ms = time_fn(lambda: linear.gemm(a, w, out=out, cfg=cfg, splits=splits), iters, flush=flush)
+    pk = peaks()
+    flops = 2.0 * M * N * K
+    byts = 2.0 * (M * K + N * K + M * N)
+    res = {"kernel": "gemm_bf16", "M": M, "N": N, "K": K, "plan": linear.plan(M, N, K),
+           "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1),
+           "gbs": round(byts / ms / 1e6, 1),
+           "frac_tensor": round(flops / ms / 1e9 / pk["bf16_tflops"], 3),
+           "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}
+    if cublas:
+        ms2 = time_fn(lambda: torch.matmul(a, w.t(), out=out), iters, flush=flush)
+        res["cublas_ms"] = round(ms2, 5)
+        res["vs_cublas"] = round(ms2 / ms, 3)
+    return res
+
+
+def bench_decode_attn(batch=256, ctx=1152, hq=32, hkv=8, d=128, bs=16, splits=1, iters=20):
+    from ..ops import attention as A
+
+    nb = batch * math.ceil(ctx / bs)
+    kc = torch.randn(nb, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.randperm(nb, device="cuda", dtype=torch.int32).view(batch, -1)
+    sl = torch.full((batch,), ctx, device="cuda", dtype=torch.int32)
+    cu = torch.arange(batch + 1, device="cuda", dtype=torch.int32)
+    q = torch.randn(batch, hq, d, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+    po = pml = None
+    if splits > 1:
+        po = torch.empty(splits, batch, hq, d, device="cuda")
+        pml = torch.empty(splits, batch, hq, 2, device="cuda")
+    ms = time_fn(lambda: A.paged_attention(o, q, kc, vc, bt, sl, cu, 1, d ** -0.5, decode=True,
+                                           num_splits=splits, part_o=po, part_ml=pml), iters)
+    byts = batch * ctx * hkv * d * 2 * 2
+    pk = peaks()
+    return {"kernel": "paged_attention_decode", "batch": batch, "ctx": ctx, "hq": hq, "hkv": hkv,
+            "d": d, "block": bs, "splits": splits, "ms": round(ms, 5),
+            "gbs": round(byts / ms / 1e6, 1), "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3),
+            "peaks": pk["src"]}
+
+
+def bench_prefill_attn(seqs=16, length=1024, hq=32, hkv=8, d=128, bs=16, iters=10):
+    from ..ops import attention as A
+
+    nb = seqs * length // bs
+    kc = torch.randn(nb, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.arange(nb, device="cuda", dtype=torch.int32).view(seqs, -1)
+    sl = torch.full((seqs,), length, device="cuda", dtype=torch.int32)
+    cu = torch.arange(seqs + 1, device="cuda", dtype=torch.int32) * length
+    q = torch.randn(seqs * length, hq, d, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+    ms = time_fn(lambda: A.paged_attention(o, q, kc, vc, bt, sl, cu, length, d ** -0.5), iters)
+    flops = seqs * hq * length * length * d * 2.0  # causal: 2 GEMMs x L^2/2 x 2 flop
+    pk = peaks()
+    return {"kernel": "paged_attention_prefill", "seqs": seqs, "len": length, "hq": hq, "hkv": hkv,
+            "d": d, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1),
+            "frac_tensor": round(flops / ms / 1e9 / pk["bf16_tflops"], 3), "peaks": pk["src"]}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["gemm", "decode-attn", "prefill-attn", "all"])
+    ap.add_argument("--M", type=int, default=256)
+    ap.add_argument("--N", type=int, default=6144)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--cfg", type=int, default=-1)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--ctx", type=int, default=1152)
+    ap.add_argument("--seqs", type=int, default=16)
+    ap.add_argument("--len", type=int, default=1024)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--flush", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true")
+    args = ap.parse_args(argv)
+    _setup()
+    out = []
+    if args.case == "gemm":
+        out.append(bench_gemm(args.M, args.N, args.K, args.cfg, args.splits, args.iters,
+                              args.flush, not args.no_cublas))
+    elif args.case == "decode-attn":
+        out.append(bench_decode_attn(args.batch, args.ctx, splits=max(1, args.splits),
+                                     iters=args.iters))
+    elif args.case == "prefill-attn":
+        out.append(bench_prefill_attn(args.seqs, args.len, iters=args.iters))
+    else:
+        for (M, N, K) in [(16384, 6144, 4096), (16384, 4096, 4096), (16384, 28672, 4096),
+                          (16384, 4096, 14336), (256, 6144, 4096), (256, 4096, 4096),
+                          (256, 28672, 4096), (256, 4096, 14336), (256, 128256, 4096),
+                          (1, 4096, 4096), (16, 6144, 4096), (64, 28672, 4096)]:
+            out.append(bench_gemm(M, N, K, iters=args.iters, flush=M <= 256))
+        out.append(bench_decode_attn(256, 1152))
+        out.append(bench_decode_attn(1, 8192, splits=16))
+        out.append(bench_prefill_attn(16, 1024))
+    for r in out:
+        print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
