@@ -32,7 +32,8 @@ import torch
 ROOT = Path(__file__).resolve().parent
 METRIC = "output tok/s (box, max over ranks) at 1/2/4/8 B200; p50 TTFT/TPOT"
 MODEL = "Llama-3.1-8B-shaped (32L, h4096, 32q/8kv, d128, ffn14336, vocab128256)"
-N_REQ, PROMPT, OUT = 256, 1024, 256
+N_REQ, PROMPT, OUT = 256, 1024, 256  # the BASELINE workload; --requests/--prompt-len/
+# --output-len exist only for profiling runs and mark the JSON line "profiling"
 BASELINE_VALUE = None  # BASELINE.md publishes no number for this config
 
 
@@ -297,7 +298,17 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--chunk", type=int, default=16384, help="prefill tokens per chunk")
+    ap.add_argument("--requests", type=int, default=None, help="profiling only")
+    ap.add_argument("--prompt-len", type=int, default=None, help="profiling only")
+    ap.add_argument("--output-len", type=int, default=None, help="profiling only")
     args = ap.parse_args(argv)
+    global N_REQ, PROMPT, OUT
+    if args.requests or args.prompt_len or args.output_len:
+        N_REQ = args.requests or N_REQ
+        PROMPT = args.prompt_len or PROMPT
+        OUT = args.output_len or OUT
+        print("warning: non-default workload; the JSON line is for profiling only",
+              file=sys.stderr)
     if args.warmup < 3:
         print("warning: --warmup < 3 does not meet the timing rules", file=sys.stderr)
     if args.impl == "reference":

@@ -1,0 +1,135 @@
+"""Fused NVLink all-reduce + residual + RMSNorm on 2+ GPUs (spawned ranks,
+bounded join). The fused result must be BITWISE equal to the exact unfused
+reference (all-gather the partials, fp32 sum in rank order, one bf16 round,
+fused_add_rms_norm), across repeated calls, several token counts and CUDA-
+graph replays; a peer that never arrives must end in a recorded timeout,
+not a hang. NVLS is off in every library (NCCL_NVLS_ENABLE=0)."""
+import os
+
+import pytest
+import torch
+
+from . import _mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _world():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    for w in (8, 4, 2):
+        if n >= w:
+            return w
+    return 0
+
+
+def _setup(rank, world):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from vllm_sm70_b200 import _ext
+    from vllm_sm70_b200.parallel import state
+
+    assert _ext.load(), _ext.error()
+    ps = state.init(tp_size=world, timeout_s=60)
+    torch.ops._b200_C.init_device(ps.device.index)
+    return ps
+
+
+def _reference(parts_all, res, w, eps):
+    from vllm_sm70_b200.ops import norm
+
+    tot = parts_all[0].float()
+    for p in parts_all[1:]:
+        tot = tot + p.float()
+    x = tot.to(torch.bfloat16)
+    r = res.clone()
+    norm.fused_add_rms_norm(x, r, w, eps)
+    return x, r
+
+
+def _fused_body(rank, world):
+    import torch.distributed as dist
+
+    from vllm_sm70_b200.parallel import symm, state
+
+    ps = _setup(rank, world)
+    H = 4096
+    f = symm.FusedArRmsNorm(ps, 512, H)
+    dev = ps.device
+    w = (torch.randn(H, device=dev) * 0.5 + 1).to(torch.bfloat16)
+    dist.broadcast(w, 0)
+    for it, T in enumerate([1, 7, 256, 512, 3, 256]):
+        g = torch.Generator(device=dev).manual_seed(100 + it)
+        parts_all = [torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+                     for _ in range(world)]
+        res = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+        st = f.stage_view(T)
+        st.copy_(parts_all[rank])
+        x, r = f(st, res.clone(), w, 1e-5)
+        torch.cuda.synchronize()
+        x_ref, r_ref = _reference(parts_all, res, w, 1e-5)
+        assert torch.equal(r, r_ref), f"residual mismatch T={T}"
+        assert torch.equal(x, x_ref), f"output mismatch T={T}: {(x.float()-x_ref.float()).abs().max()}"
+        assert int(torch.ops._b200_C.read_status(dev.index, True)) == 0
+    # CUDA-graph capture + replay (epoch flags survive replays)
+    T = 64
+    st = f.stage_view(T)
+    resv = f.res_view(T)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        f(st, resv, w, 1e-5)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out, _ = f(st, resv, w, 1e-5)
+    for it in range(5):
+        g = torch.Generator(device=dev).manual_seed(500 + it)
+        parts_all = [torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+                     for _ in range(world)]
+        res = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+        st.copy_(parts_all[rank])
+        resv.copy_(res)
+        graph.replay()
+        torch.cuda.synchronize()
+        x_ref, r_ref = _reference(parts_all, res, w, 1e-5)
+        assert torch.equal(out, x_ref) and torch.equal(resv, r_ref), f"graph replay {it}"
+    del graph
+    torch.cuda.synchronize()
+    dist.barrier()
+    state.shutdown()
+
+
+def test_fused_ar_rmsnorm_bitwise(b200_ops):
+    world = _world()
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    _mp.run(_fused_body, world, timeout=600)
+
+
+def _timeout_body(rank, world):
+    import torch.distributed as dist
+
+    from vllm_sm70_b200.parallel import symm, state
+
+    ps = _setup(rank, world)
+    f = symm.FusedArRmsNorm(ps, 16, 1024)
+    f.timeout_ms = 200
+    w = torch.ones(1024, device=ps.device, dtype=torch.bfloat16)
+    if rank == 0:
+        # Rank 0 enters alone: its wait for the peers' "ready" flags must run
+        # out, set the status word and return (the context stays usable).
+        f(f.stage_view(4), f.res_view(4), w, 1e-5)
+        torch.cuda.synchronize()
+        st = int(torch.ops._b200_C.read_status(ps.device.index, True))
+        assert st == 2, f"expected the peer-timeout status, got {st}"
+        x = torch.ones(4, device=ps.device)
+        assert float(x.sum()) == 4.0  # context still healthy
+    dist.barrier()
+    state.shutdown()
+
+
+def test_fused_ar_rmsnorm_peer_timeout(b200_ops):
+    world = _world()
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    _mp.run(_timeout_body, 2, timeout=300)

@@ -6,7 +6,8 @@ from vllm_sm70_b200.ops import linear
 
 pytestmark = pytest.mark.gpu
 
-CFGS = {"n256": 0, "n128": 1, "swap16": 2, "swap32": 3, "swap64": 4}
+CFGS = {"n256": 0, "n128": 1, "swap16": 2, "swap32": 3, "swap64": 4, "n192": 5, "n96": 6,
+        "n64": 7, "swap128": 8}
 
 
 def _ref(a, w):
@@ -62,11 +63,12 @@ def test_gemm_deterministic(b200_ops):
     assert torch.equal(o1, o2)
 
 
-@pytest.mark.parametrize("cfg", ["n256", "n128", "swap16", "swap64"])
-@pytest.mark.parametrize("splits", [2, 3, 5])
+@pytest.mark.parametrize("cfg", ["n256", "n128", "swap16", "swap64", "n192", "n96", "swap128"])
+@pytest.mark.parametrize("splits", [2, 3, 5, 8])
 def test_gemm_split_k(b200_ops, cfg, splits, rel_err):
     torch.manual_seed(4)
-    M = {"n256": 256, "n128": 200, "swap16": 9, "swap64": 50}[cfg]
+    M = {"n256": 256, "n128": 200, "swap16": 9, "swap64": 50, "n192": 256, "n96": 130,
+         "swap128": 100}[cfg]
     N, K = 1536, 4096 + 64
     a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
@@ -97,3 +99,17 @@ def test_planner_uses_split_for_decode_shapes(b200_ops):
     assert s > 1
     cfg, s = linear.plan(16384, 6144, 4096, 0, 148)
     assert s == 1
+
+
+def test_tuner_installs_plans(b200_ops):
+    from vllm_sm70_b200.engine import warmup
+
+    torch.ops._b200_C.gemm_clear_plans()
+    plans = warmup.tune_shapes([(256, 1536, 1024, 0), (64, 1024, 512, 0), (128, 1024, 512, 1)],
+                               iters=2)
+    assert len(plans) == 3
+    exported = warmup.export_plans()
+    assert sorted(map(tuple, exported)) == sorted(map(tuple, plans))
+    for M, N, K, epi, cfg, sp in plans:
+        assert tuple(torch.ops._b200_C.gemm_bf16_plan(M, N, K, epi, 148)) == (cfg, sp)
+    torch.ops._b200_C.gemm_clear_plans()

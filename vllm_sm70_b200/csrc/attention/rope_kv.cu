@@ -116,7 +116,41 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, const int64_t* _
   }
 }
 
+// Plain K/V scatter into the paged cache (RoPE applied by the caller):
+// one thread per 16-byte chunk of one token's K or V head.
+__global__ void kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+                                long long ldk, long long ldv, __nv_bfloat16* __restrict__ kc,
+                                __nv_bfloat16* __restrict__ vc, const int64_t* __restrict__ slots,
+                                int T, int Hkv, int D, int BS, long long blk_stride) {
+  const long long chunks_per_tok = (long long)Hkv * (D / 8);
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)T * chunks_per_tok * 2;
+  if (idx >= total) return;
+  const bool is_v = idx >= total / 2;
+  const long long j = is_v ? idx - total / 2 : idx;
+  const int t = (int)(j / chunks_per_tok);
+  const int rem = (int)(j % chunks_per_tok);
+  const int h = rem / (D / 8), c = rem % (D / 8);
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  const __nv_bfloat16* src = (is_v ? v + t * ldv : k + t * ldk) + (long long)h * D + c * 8;
+  __nv_bfloat16* dst = (is_v ? vc : kc) + (slot / BS) * blk_stride +
+                       ((long long)h * BS + slot % BS) * D + c * 8;
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+}
+
 }  // namespace
+
+void kv_cache_write_launch(const void* k, const void* v, long long ldk, long long ldv,
+                           void* k_cache, void* v_cache, const int64_t* slots, int T, int Hkv,
+                           int D, int BS, long long blk_stride, cudaStream_t stream) {
+  if (T <= 0) return;
+  const long long total = (long long)T * Hkv * (D / 8) * 2;
+  const int thr = 256;
+  kv_write_kernel<<<(unsigned)((total + thr - 1) / thr), thr, 0, stream>>>(
+      (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, ldk, ldv, (__nv_bfloat16*)k_cache,
+      (__nv_bfloat16*)v_cache, slots, T, Hkv, D, BS, blk_stride);
+}
 
 void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, void* k_cache,
                           void* v_cache, const int64_t* slots, const void* q_norm,

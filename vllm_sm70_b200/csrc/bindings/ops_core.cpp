@@ -9,6 +9,7 @@
 #include <torch/torch.h>
 
 #include "ops_api.h"
+#include "comm/comm_api.h"
 
 namespace b200 {
 namespace {
@@ -73,6 +74,15 @@ at::Tensor gemm_bf16(const at::Tensor& a, const at::Tensor& w, int64_t cfg) {
 
 void gemm_configure_workspace_op(int64_t device, int64_t ws_bytes, int64_t n_counters) {
   gemm_configure_workspace((int)device, (size_t)ws_bytes, (int)n_counters);
+}
+
+void gemm_set_plan_op(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t cfg, int64_t splits) {
+  gemm_set_plan((int)M, (int)N, (int)K, (int)epi, (int)cfg, (int)splits);
+}
+void gemm_clear_plans_op() { gemm_clear_plans(); }
+std::vector<int64_t> gemm_export_plans_op() {
+  auto v = gemm_export_plans();
+  return std::vector<int64_t>(v.begin(), v.end());
 }
 
 std::vector<int64_t> gemm_bf16_plan_op(int64_t M, int64_t N, int64_t K, int64_t epi,
@@ -147,6 +157,26 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tenso
                        (int)cos_sin.size(1), k_cache.stride(0), cur_stream());
 }
 
+void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache,
+                    at::Tensor& v_cache, const at::Tensor& slots) {
+  CHECK_CUDA(k); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(k_cache); CHECK_BF16(v_cache);
+  TORCH_CHECK(k.dim() == 3 && v.dim() == 3 && k.stride(2) == 1 && v.stride(2) == 1 &&
+                  k.stride(1) == k.size(2) && v.stride(1) == v.size(2),
+              "kv_cache_write: k/v must be [T, Hkv, D] with dense heads");
+  TORCH_CHECK(slots.scalar_type() == at::kLong, "kv_cache_write: int64 slot mapping");
+  for (const at::Tensor* c : {&k_cache, &v_cache})
+    TORCH_CHECK(c->dim() == 4 && c->stride(3) == 1 && c->stride(2) == c->size(3) &&
+                    c->stride(1) == c->size(2) * c->size(3),
+                "kv_cache_write: cache blocks must be dense [Hkv, BS, D]");
+  TORCH_CHECK(k.size(2) % 8 == 0 && k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0,
+              "kv_cache_write: 16-byte aligned rows");
+  c10::cuda::CUDAGuard g(k.device());
+  kv_cache_write_launch(k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), k_cache.data_ptr(),
+                        v_cache.data_ptr(), slots.data_ptr<int64_t>(), (int)k.size(0),
+                        (int)k.size(1), (int)k.size(2), (int)k_cache.size(2), k_cache.stride(0),
+                        cur_stream());
+}
+
 void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
                      const at::Tensor& v_cache, const at::Tensor& block_table,
                      const at::Tensor& seq_lens, const at::Tensor& cu_q, int64_t max_q_len,
@@ -210,6 +240,41 @@ void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_c
   paged_attention_launch(a, cur_stream());
 }
 
+// Fused TP all-reduce + residual add + RMSNorm over peer-mapped symmetric
+// buffers (addresses from the symmetric-memory rendezvous, one per rank).
+void ar_rmsnorm(const std::vector<int64_t>& stage_ptrs, const std::vector<int64_t>& res_ptrs,
+                const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& flag_ptrs,
+                int64_t rank, int64_t T, int64_t H, const at::Tensor& w, double eps,
+                int64_t timeout_ms, int64_t grid) {
+  const int W = (int)stage_ptrs.size();
+  TORCH_CHECK(W == 2 || W == 4 || W == 8, "ar_rmsnorm: world size must be 2, 4 or 8");
+  TORCH_CHECK((int)res_ptrs.size() == W && (int)out_ptrs.size() == W && (int)flag_ptrs.size() == W,
+              "ar_rmsnorm: pointer lists must have one entry per rank");
+  TORCH_CHECK(rank >= 0 && rank < W, "ar_rmsnorm: bad rank");
+  CHECK_CUDA(w); CHECK_BF16(w);
+  TORCH_CHECK(w.numel() == H && H % 8 == 0, "ar_rmsnorm: weight size / H % 8");
+  ArRmsNormParams p{};
+  for (int q = 0; q < W; ++q) {
+    p.stage_peer[q] = reinterpret_cast<const __nv_bfloat16*>(stage_ptrs[q]);
+    p.res_peer[q] = reinterpret_cast<__nv_bfloat16*>(res_ptrs[q]);
+    p.out_peer[q] = reinterpret_cast<__nv_bfloat16*>(out_ptrs[q]);
+    p.flags_peer[q] = reinterpret_cast<uint32_t*>(flag_ptrs[q]);
+    TORCH_CHECK((stage_ptrs[q] | res_ptrs[q] | out_ptrs[q]) % 16 == 0, "ar_rmsnorm: 16B alignment");
+  }
+  p.flags_local = p.flags_peer[rank];
+  p.res_local = p.res_peer[rank];
+  p.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.rank = (int)rank;
+  p.world = W;
+  p.T = (int)T;
+  p.H = (int)H;
+  p.eps = (float)eps;
+  p.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  p.err = device_status_ptr(w.get_device());
+  c10::cuda::CUDAGuard g(w.device());
+  ar_rmsnorm_launch(p, (int)grid, cur_stream());
+}
+
 void argmax(at::Tensor& ids, const c10::optional<at::Tensor>& vals, const at::Tensor& logits,
             int64_t id_offset) {
   CHECK_CUDA(logits);
@@ -254,6 +319,10 @@ TORCH_LIBRARY(_b200_C, m) {
         &b200::gemm_configure_workspace_op);
   m.def("gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) -> int[]",
         &b200::gemm_bf16_plan_op);
+  m.def("gemm_set_plan(int M, int N, int K, int epi, int cfg, int splits) -> ()",
+        &b200::gemm_set_plan_op);
+  m.def("gemm_clear_plans() -> ()", &b200::gemm_clear_plans_op);
+  m.def("gemm_export_plans() -> int[]", &b200::gemm_export_plans_op);
   m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
   m.def("gemm_bf16_config(int M, int N, int K, int epi) -> int", &b200::gemm_bf16_config);
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
@@ -266,6 +335,9 @@ TORCH_LIBRARY(_b200_C, m) {
       "paged_attention(Tensor(a!) out, Tensor q, Tensor k_cache, Tensor v_cache, "
       "Tensor block_table, Tensor seq_lens, Tensor cu_q, int max_q_len, float scale, int window, "
       "Tensor? sinks, bool decode, int num_splits, Tensor? part_o, Tensor? part_ml) -> ()");
+  m.def("ar_rmsnorm(int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, int[] flag_ptrs, int rank, "
+        "int T, int H, Tensor w, float eps, int timeout_ms, int grid) -> ()");
+  m.def("kv_cache_write(Tensor k, Tensor v, Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor slots) -> ()");
   m.def("argmax(Tensor(a!) ids, Tensor(b!)? vals, Tensor logits, int id_offset) -> ()");
   m.def("silu_mul(Tensor(a!) out, Tensor x) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor ids, Tensor table, int vocab_start) -> ()");
@@ -280,6 +352,8 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("rope_kv_write", &b200::rope_kv_write);
   m.impl("paged_attention", &b200::paged_attention);
   m.impl("argmax", &b200::argmax);
+  m.impl("kv_cache_write", &b200::kv_cache_write);
+  m.impl("ar_rmsnorm", &b200::ar_rmsnorm);
   m.impl("silu_mul", &b200::silu_mul);
   m.impl("embedding", &b200::embedding);
 }

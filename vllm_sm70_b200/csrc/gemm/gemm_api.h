@@ -2,6 +2,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <vector>
+
 namespace b200 {
 
 enum GemmEpilogue : int {
@@ -16,8 +18,14 @@ enum GemmConfig : int {
   kCfgSwap16 = 2,  // swap-AB: 128 weight rows x 16 tokens
   kCfgSwap32 = 3,
   kCfgSwap64 = 4,
-  kCfgCount = 5,
+  kCfgN192 = 5,    // 128 x 192
+  kCfgN96 = 6,     // 128 x 96
+  kCfgN64 = 7,     // 128 x 64
+  kCfgSwap128 = 8, // swap-AB: 128 weight rows x 128 tokens
+  kCfgCount = 9,
 };
+
+constexpr int kMaxSplits = 8;
 
 struct GemmPlan {
   int cfg;
@@ -26,6 +34,11 @@ struct GemmPlan {
 
 // Tile config + split-K choice from a wave-quantisation cost model.
 GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm);
+
+// Tuned dispatch table (consulted by gemm_bf16_plan before the cost model).
+void gemm_set_plan(int M, int N, int K, int epi, int cfg, int splits);  // cfg < 0 erases
+void gemm_clear_plans();
+std::vector<int> gemm_export_plans();  // flat [M, N, K, epi, cfg, splits] * n
 
 // Process-wide split-K workspace (fp32 partials + self-re-arming counters).
 void gemm_configure_workspace(int device, size_t ws_bytes, int n_counters);

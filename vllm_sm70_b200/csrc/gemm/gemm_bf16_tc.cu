@@ -29,8 +29,11 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <unordered_map>
+#include <vector>
 
 #include "common/ptx.cuh"
 #include "common/tmap.h"
@@ -95,7 +98,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   const int num_kb = (K + BK - 1) / BK;
   const int kb_per = (num_kb + splits - 1) / splits;
   const int num_units = num_tiles * splits;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                                 : (2 * BN <= 256) ? 256 : 512;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -286,16 +290,33 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         } else {
 #pragma unroll
           for (int c = 0; c < CW; ++c) v[c] = 0.f;
-          for (int s2 = 0; s2 < splits; ++s2) {
-            const float4* src = reinterpret_cast<const float4*>(ws_tile + (size_t)s2 * (BM * BN)) +
-                                (size_t)(col0 / 4) * BM + row_in_tile;
+          // Up to 4 splits' partials are requested before any is consumed, so a
+          // chunk costs one L2 round trip per 4 splits; the adds stay in split
+          // order (deterministic).
+          constexpr int RG = EPI == kEpiSiluMul ? 2 : 4;  // splits per load batch
+          for (int s0 = 0; s0 < splits; s0 += RG) {
+            float4 x[RG][CW / 4];
 #pragma unroll
-            for (int c4 = 0; c4 < CW / 4; ++c4) {
-              const float4 x = __ldcg(src + (size_t)c4 * BM);
-              v[4 * c4] += x.x;
-              v[4 * c4 + 1] += x.y;
-              v[4 * c4 + 2] += x.z;
-              v[4 * c4 + 3] += x.w;
+            for (int j = 0; j < RG; ++j) {
+              if (s0 + j < splits) {
+                const float4* src =
+                    reinterpret_cast<const float4*>(ws_tile + (size_t)(s0 + j) * (BM * BN)) +
+                    (size_t)(col0 / 4) * BM + row_in_tile;
+#pragma unroll
+                for (int c4 = 0; c4 < CW / 4; ++c4) x[j][c4] = __ldcg(src + (size_t)c4 * BM);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < RG; ++j) {
+              if (s0 + j < splits) {
+#pragma unroll
+                for (int c4 = 0; c4 < CW / 4; ++c4) {
+                  v[4 * c4] += x[j][c4].x;
+                  v[4 * c4 + 1] += x[j][c4].y;
+                  v[4 * c4 + 2] += x[j][c4].z;
+                  v[4 * c4 + 3] += x[j][c4].w;
+                }
+              }
             }
           }
         }
@@ -421,29 +442,55 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
     throw std::runtime_error(std::string("gemm_bf16_tc launch: ") + cudaGetErrorString(e));
 }
 
-int cfg_bn(int cfg) {
-  switch (cfg) {
-    case kCfgN256: return 256;
-    case kCfgN128: return 128;
-    case kCfgSwap16: return 16;
-    case kCfgSwap32: return 32;
-    case kCfgSwap64: return 64;
+struct CfgInfo {
+  int bn;
+  bool swap;
+};
+constexpr CfgInfo kCfgInfo[kCfgCount] = {
+    {256, false}, {128, false}, {16, true}, {32, true}, {64, true},
+    {192, false}, {96, false},  {64, false}, {128, true},
+};
+
+int cfg_bn(int cfg) { return (cfg >= 0 && cfg < kCfgCount) ? kCfgInfo[cfg].bn : 0; }
+bool cfg_swap(int cfg) { return cfg >= 0 && cfg < kCfgCount && kCfgInfo[cfg].swap; }
+
+// Tuned dispatch table: (M, N, K, epi) -> plan, filled by the warm-up tuner
+// or imported from a LUT file; consulted before the cost model.
+struct PlanKey {
+  int M, N, K, epi;
+  bool operator==(const PlanKey& o) const {
+    return M == o.M && N == o.N && K == o.K && epi == o.epi;
   }
-  return 0;
-}
-bool cfg_swap(int cfg) { return cfg == kCfgSwap16 || cfg == kCfgSwap32 || cfg == kCfgSwap64; }
+};
+struct PlanKeyHash {
+  size_t operator()(const PlanKey& k) const {
+    return ((size_t)k.M * 1000003u) ^ ((size_t)k.N * 10007u) ^ ((size_t)k.K * 131u) ^ k.epi;
+  }
+};
+std::mutex g_plan_mu;
+std::unordered_map<PlanKey, GemmPlan, PlanKeyHash> g_plans;
 
 }  // namespace
 
 GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
+  {
+    std::lock_guard<std::mutex> g(g_plan_mu);
+    auto it = g_plans.find(PlanKey{M, N, K, epi});
+    if (it != g_plans.end()) return it->second;
+  }
   // Candidate tile shapes: swap-AB (weights on the 128-row side) for small M.
-  int cands[3];
+  int cands[8];
   int nc = 0;
   if (epi == kEpiNone && M <= 64) {
     cands[nc++] = M <= 16 ? kCfgSwap16 : (M <= 32 ? kCfgSwap32 : kCfgSwap64);
-  } else {
+  } else if (epi == kEpiSiluMul) {
     cands[nc++] = kCfgN256;
     cands[nc++] = kCfgN128;
+  } else {
+    cands[nc++] = kCfgN256;
+    cands[nc++] = kCfgN192;
+    cands[nc++] = kCfgN128;
+    cands[nc++] = kCfgN96;
   }
   const int num_kb = (K + 63) / 64;
   GemmPlan best{cands[0], 1};
@@ -454,17 +501,17 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
     const bool swap = cfg_swap(cfg);
     const long p = swap ? N : M, qq = swap ? M : N;
     const long tiles = ((p + 127) / 128) * ((qq + bn - 1) / bn);
-    for (int s = 1; s <= 8; ++s) {
+    for (int s = 1; s <= kMaxSplits; ++s) {
       const int kb_per = (num_kb + s - 1) / s;
       if (s > 1 && kb_per < 4) break;
       const long units = tiles * s;
       const long waves = (units + num_sm - 1) / num_sm;
       // Relative cost model: MMA time per k-block grows with BN, plus a fixed
-      // per-k-block latency share, per-unit prologue/epilogue, and the split
-      // partial-sum traffic.
-      const double per_kb = bn / 256.0 + 0.25;
+      // per-k-block latency share (operand traffic), per-unit prologue /
+      // epilogue, and the split partial-sum round trips.
+      const double per_kb = bn / 256.0 + 0.35;
       double t_unit = kb_per * per_kb + 3.0;
-      if (s > 1) t_unit += 2.0 + s * (bn / 256.0) * 0.5;
+      if (s > 1) t_unit += 4.0 + ((s + 3) / 4) * (bn / 256.0) * 2.0;
       const double cost = waves * t_unit;
       if (cost < best_cost * 0.97) {
         best_cost = cost;
@@ -473,6 +520,30 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
     }
   }
   return best;
+}
+
+void gemm_set_plan(int M, int N, int K, int epi, int cfg, int splits) {
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  if (cfg < 0) {
+    g_plans.erase(PlanKey{M, N, K, epi});
+    return;
+  }
+  g_plans[PlanKey{M, N, K, epi}] = GemmPlan{cfg, splits < 1 ? 1 : splits};
+}
+
+void gemm_clear_plans() {
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  g_plans.clear();
+}
+
+std::vector<int> gemm_export_plans() {
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  std::vector<int> out;
+  for (auto& kv : g_plans) {
+    out.insert(out.end(), {kv.first.M, kv.first.N, kv.first.K, kv.first.epi, kv.second.cfg,
+                           kv.second.splits});
+  }
+  return out;
 }
 
 int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm) {
@@ -519,7 +590,8 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
     if (splits <= 0) splits = pl.splits;
   }
   if (splits <= 0) splits = 1;
-  if (epi == kEpiSiluMul && cfg_swap(cfg)) cfg = kCfgN128;
+  if (splits > kMaxSplits) splits = kMaxSplits;
+  if (epi == kEpiSiluMul && cfg != kCfgN256 && cfg != kCfgN128) cfg = kCfgN128;
   const int bn = cfg_bn(cfg);
   if (bn == 0) throw std::runtime_error("gemm_bf16: unknown config " + std::to_string(cfg));
   const bool swap = cfg_swap(cfg);
@@ -541,23 +613,25 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
     return launch_cfg<128, 6, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp,
                                                   cnt, err, stream);
   }
+#define B200_NORMAL(BN_, ST_) \
+  return launch_cfg<BN_, ST_, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, \
+                                               err, stream)
+#define B200_SWAP(BN_, ST_) \
+  return launch_cfg<BN_, ST_, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt, \
+                                              err, stream)
   switch (cfg) {
-    case kCfgN256:
-      return launch_cfg<256, 4, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt,
-                                                 err, stream);
-    case kCfgN128:
-      return launch_cfg<128, 6, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt,
-                                                 err, stream);
-    case kCfgSwap16:
-      return launch_cfg<16, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt,
-                                               err, stream);
-    case kCfgSwap32:
-      return launch_cfg<32, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt,
-                                               err, stream);
-    case kCfgSwap64:
-      return launch_cfg<64, 8, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt,
-                                               err, stream);
+    case kCfgN256: B200_NORMAL(256, 4);
+    case kCfgN192: B200_NORMAL(192, 5);
+    case kCfgN128: B200_NORMAL(128, 6);
+    case kCfgN96: B200_NORMAL(96, 7);
+    case kCfgN64: B200_NORMAL(64, 8);
+    case kCfgSwap16: B200_SWAP(16, 8);
+    case kCfgSwap32: B200_SWAP(32, 8);
+    case kCfgSwap64: B200_SWAP(64, 8);
+    case kCfgSwap128: B200_SWAP(128, 6);
   }
+#undef B200_NORMAL
+#undef B200_SWAP
 }
 
 void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,

@@ -23,6 +23,9 @@ void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, v
                           void* v_cache, const int64_t* slots, const void* q_norm,
                           const void* k_norm, int T, int Hq, int Hkv, int D, int BS, float eps,
                           int rot_dim, long long blk_stride, cudaStream_t stream);
+void kv_cache_write_launch(const void* k, const void* v, long long ldk, long long ldv,
+                           void* k_cache, void* v_cache, const int64_t* slots, int T, int Hkv,
+                           int D, int BS, long long blk_stride, cudaStream_t stream);
 void argmax_launch(const void* logits, bool is_bf16, int rows, int V, int ld, int* ids, float* vals,
                    int id_offset, cudaStream_t stream);
 void silu_mul_launch(void* out, const void* x, int T, int I, int ld_x, int ld_o,

@@ -64,7 +64,8 @@ class LLM:
                  max_model_len: int = 4096, block_size: int = 16,
                  max_num_batched_tokens: int = 16384, gpu_memory_utilization: float = 0.90,
                  load_format: str = "dummy", seed: int = 0, enforce_eager: bool = False,
-                 dtype=torch.bfloat16, num_kv_blocks: int | None = None):
+                 dtype=torch.bfloat16, num_kv_blocks: int | None = None,
+                 tune_gemm: bool = True, gemm_lut_path: str | None = None):
         self.cfg: ModelConfig = resolve(model)
         ps = pstate.get() if pstate._STATE is not None else None
         if ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
@@ -96,6 +97,15 @@ class LLM:
         self.runner = ModelRunner(self.model, max_num_seqs, max_model_len, block_size,
                                   num_kv_blocks, self.device, use_graphs=not enforce_eager,
                                   num_sms=num_sms)
+        if self.device.type == "cuda" and ps.tp_size > 1:
+            from ..parallel import comm, symm
+
+            comm.set_fused_ar_rmsnorm(symm.FusedArRmsNorm(
+                ps, max(max_num_batched_tokens, max_num_seqs), self.cfg.hidden_size))
+        if self.device.type == "cuda" and tune_gemm:
+            from . import warmup
+
+            warmup.engine_warmup(self.model, ps, self.runner.capture_sizes, gemm_lut_path)
         self.runner.capture()
         self.last_stats: GenerateStats | None = None
 
@@ -105,6 +115,9 @@ class LLM:
         if self.device.type == "cuda":
             torch.cuda.synchronize()
         self.runner.release_graphs()
+        from ..parallel import comm
+
+        comm.set_fused_ar_rmsnorm(None)
 
     def _size_kv(self, max_num_seqs, max_model_len, block_size, util) -> int:
         m = self.model

@@ -170,12 +170,13 @@ class LlamaModel:
         cfg = self.cfg
         eps = cfg.rms_eps
         T = ids.shape[0]
-        residual = self.embed_tokens(ids)
+        H = cfg.hidden_size
+        residual = comm.adopt_residual(self.embed_tokens(ids))
         x = ops.rms_norm(residual, self.layers[0]["in_norm"], eps)
         attn_out = torch.empty(T, self.hq, self.d, device=ids.device, dtype=self.dtype)
         for li, L in enumerate(self.layers):
             if li > 0:
-                comm.all_reduce_add_rms_norm(x, residual, L["in_norm"], eps)
+                x, residual = comm.all_reduce_add_rms_norm(x, residual, L["in_norm"], eps)
             qkv = L["qkv"].forward(x)
             ops.rope_kv_write(qkv, meta.positions, self.cos_sin, kv.k[li], kv.v[li],
                               meta.slot_mapping, self.hq, self.hkv, L.get("q_norm"),
@@ -184,11 +185,12 @@ class LlamaModel:
             ops.paged_attention(attn_out, q, kv.k[li], kv.v[li], meta.block_table,
                                 meta.seq_lens, meta.cu_q, meta.max_q_len, self.scale, 0, None,
                                 meta.decode, meta.num_splits, meta.part_o, meta.part_ml)
-            o = L["o"].forward(attn_out.view(T, self.hq * self.d))
-            comm.all_reduce_add_rms_norm(o, residual, L["post_norm"], eps)
-            h = L["gate_up"].forward(o)
-            x = L["down"].forward(h)
-        comm.all_reduce_add_rms_norm(x, residual, self.final_norm, eps)
+            o = L["o"].forward(attn_out.view(T, self.hq * self.d),
+                               out=comm.row_parallel_out(T, H))
+            x, residual = comm.all_reduce_add_rms_norm(o, residual, L["post_norm"], eps)
+            h = L["gate_up"].forward(x)
+            x = L["down"].forward(h, out=comm.row_parallel_out(T, H))
+        x, residual = comm.all_reduce_add_rms_norm(x, residual, self.final_norm, eps)
         return x
 
     def greedy(self, hidden: torch.Tensor) -> torch.Tensor:

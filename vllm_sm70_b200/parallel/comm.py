@@ -24,21 +24,55 @@ _fused = {"ar_rmsnorm": None}
 
 
 def set_fused_ar_rmsnorm(impl) -> None:
-    """Install the fused all-reduce + add + RMSNorm implementation (callable
-    ``impl(x, residual, w, eps) -> bool``; False = not admitted, use NCCL)."""
+    """Install the fused all-reduce + add + RMSNorm implementation (a
+    ``parallel.symm.FusedArRmsNorm`` or None)."""
     _fused["ar_rmsnorm"] = impl
 
 
+def fused_ar_rmsnorm():
+    impl = _fused["ar_rmsnorm"]
+    if impl is None or not envs.get("VLLM_B200_FUSED_AR_RMSNORM"):
+        return None
+    return impl
+
+
+def row_parallel_out(T: int, H: int, dtype=torch.bfloat16, device=None) -> torch.Tensor | None:
+    """Output buffer for a row-parallel GEMM whose result feeds
+    :func:`all_reduce_add_rms_norm`: the fused path's peer-visible stage
+    buffer (so the GEMM writes the collective's input directly), else None."""
+    impl = fused_ar_rmsnorm()
+    if impl is not None and impl.admits(T) and impl.H == H:
+        return impl.stage_view(T)
+    return None
+
+
+def adopt_residual(residual: torch.Tensor) -> torch.Tensor:
+    """Move the residual stream into the fused path's symmetric buffer (once
+    per forward) so the fused kernel updates it in place on every rank."""
+    impl = fused_ar_rmsnorm()
+    T = residual.shape[0]
+    if impl is not None and impl.admits(T) and impl.H == residual.shape[1]:
+        rv = impl.res_view(T)
+        rv.copy_(residual)
+        return rv
+    return residual
+
+
 def all_reduce_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
-                            eps: float) -> None:
-    """In place: ``x <- allreduce_tp(x)``; ``residual += x``; ``x <- rmsnorm(residual) w``."""
+                            eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """``x <- allreduce_tp(x)``; ``residual += x``; ``x <- rmsnorm(residual) w``.
+    Returns ``(x, residual)`` (views of symmetric buffers on the fused path,
+    the updated inputs otherwise)."""
     st = pstate.get()
     if st.tp_size > 1:
-        impl = _fused["ar_rmsnorm"]
-        if impl is not None and envs.get("VLLM_B200_FUSED_AR_RMSNORM") and impl(x, residual, w, eps):
-            return
+        impl = fused_ar_rmsnorm()
+        if impl is not None:
+            r = impl(x, residual, w, eps)
+            if r is not None:
+                return r
         dist.all_reduce(x, group=st.tp_group)
     ops.fused_add_rms_norm(x, residual, w, eps)
+    return x, residual
 
 
 def greedy_merge(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
@@ -50,6 +84,7 @@ def greedy_merge(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
         return ids
     rows = ids.shape[0]
     packed = torch.stack([vals.float(), ids.float()], 0)  # ids < 2^24 are exact in fp32
-    allp = torch.empty(st.tp_size, 2, rows, dtype=torch.float32, device=ids.device)
+    allp = torch.empty(st.tp_size * 2, rows, dtype=torch.float32, device=ids.device)
     dist.all_gather_into_tensor(allp, packed.contiguous(), group=st.tp_group)
+    allp = allp.view(st.tp_size, 2, rows)
     return ops.sampling.merge_rank_top1(allp[:, 0], allp[:, 1].to(torch.int64))

@@ -1,0 +1,98 @@
+"""Symmetric (peer-mapped) workspaces for the fused TP collectives.
+
+Buffers come from ``torch.distributed._symmetric_memory`` (allocation and
+the handle exchange are the plumbing; every kernel that touches them is this
+library's own, with plain NVLink loads/stores -- no library kernel is ever
+handed a peer's memory). Allocation and rendezvous happen once at start-up,
+before any CUDA-graph capture, so captured kernels carry fixed peer
+addresses (the reference's R5 lesson: register at init, never graph
+operands).
+
+``FusedArRmsNorm`` owns three [T_max, H] bf16 buffers per rank (stage =
+row-parallel GEMM output, residual, normalised output) and a signal pad; it
+implements ``all_reduce_add_rms_norm`` for ``T <= T_max`` (rank-uniform
+admission), else defers to NCCL.
+"""
+from __future__ import annotations
+
+import logging
+
+import torch
+import torch.distributed as dist
+
+from .. import envs
+from ..utils import launch_count
+
+logger = logging.getLogger("vllm.b200.symm")
+
+SIGNAL_WORDS = 64  # uint32 words per rank: ready[W], done[W], epoch, done_target
+
+
+class FusedArRmsNorm:
+    def __init__(self, ps, max_tokens: int, hidden: int, dtype=torch.bfloat16,
+                 grid_cap: int = 132):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        assert ps.tp_size in (2, 4, 8), ps.tp_size
+        self.ps = ps
+        self.T_max = max_tokens
+        self.H = hidden
+        self.grid_cap = grid_cap
+        dev = ps.device
+        group = ps.tp_group
+
+        def alloc(n, dt):
+            t = symm_mem.empty(n, dtype=dt, device=dev)
+            h = symm_mem.rendezvous(t, group)
+            return t, h
+
+        self.stage, hs = alloc(max_tokens * hidden, dtype)
+        self.res, hr = alloc(max_tokens * hidden, dtype)
+        self.out, ho = alloc(max_tokens * hidden, dtype)
+        self.flags, hf = alloc(SIGNAL_WORDS, torch.int32)
+        self.flags.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+        self.stage_ptrs = [int(p) for p in hs.buffer_ptrs]
+        self.res_ptrs = [int(p) for p in hr.buffer_ptrs]
+        self.out_ptrs = [int(p) for p in ho.buffer_ptrs]
+        self.flag_ptrs = [int(p) for p in hf.buffer_ptrs]
+        self._handles = (hs, hr, ho, hf)
+        self.timeout_ms = int(envs.get("VLLM_B200_COMM_TIMEOUT_MS"))
+        self.calls = 0
+
+    # Views handed to the model -------------------------------------------------
+    def stage_view(self, T: int) -> torch.Tensor:
+        return self.stage[: T * self.H].view(T, self.H)
+
+    def res_view(self, T: int) -> torch.Tensor:
+        return self.res[: T * self.H].view(T, self.H)
+
+    def out_view(self, T: int) -> torch.Tensor:
+        return self.out[: T * self.H].view(T, self.H)
+
+    def admits(self, T: int) -> bool:
+        return 0 < T <= self.T_max
+
+    def grid(self, T: int) -> int:
+        rows = (T + self.ps.tp_size - 1) // self.ps.tp_size
+        return max(1, min(self.grid_cap, rows))
+
+    def __call__(self, x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float):
+        """Returns (normalised x, residual) as views of the symmetric buffers,
+        or None when not admitted (caller uses NCCL)."""
+        T = x.shape[0]
+        if not self.admits(T) or x.shape[1] != self.H:
+            return None
+        st = self.stage_view(T)
+        if x.data_ptr() != st.data_ptr():
+            st.copy_(x)
+        rv = self.res_view(T)
+        if residual.data_ptr() != rv.data_ptr():
+            rv.copy_(residual)
+        torch.ops._b200_C.ar_rmsnorm(self.stage_ptrs, self.res_ptrs, self.out_ptrs,
+                                     self.flag_ptrs, self.ps.tp_rank, T, self.H, w, eps,
+                                     self.timeout_ms, self.grid(T))
+        launch_count.add(1)
+        self.calls += 1
+        return self.out_view(T), rv

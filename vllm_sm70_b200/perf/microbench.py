@@ -38,10 +38,12 @@ _FLUSH = None
 
 
 def flush_l2():
+    """Evict L2 by READING a 256 MB buffer (a write-based flush leaves L2 full
+    of dirty lines whose write-back would be charged to the timed kernel)."""
     global _FLUSH
     if _FLUSH is None:
-        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    _FLUSH.zero_()
+        _FLUSH = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    _FLUSH.sum()
 
 
 def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = False) -> float:
@@ -160,10 +162,19 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="gemm: time every (cfg, splits)")
     args = ap.parse_args(argv)
     _setup()
     out = []
-    if args.case == "gemm":
+    if args.case == "gemm" and args.sweep:
+        from ..engine import warmup
+
+        for cfg, sp in warmup.candidates(args.M, args.N, args.K, 0):
+            r = bench_gemm(args.M, args.N, args.K, cfg, sp, args.iters, args.flush, False)
+            r["cfg"], r["splits"] = cfg, sp
+            out.append(r)
+        out.append(bench_gemm(args.M, args.N, args.K, -1, 0, args.iters, args.flush, True))
+    elif args.case == "gemm":
         out.append(bench_gemm(args.M, args.N, args.K, args.cfg, args.splits, args.iters,
                               args.flush, not args.no_cublas))
     elif args.case == "decode-attn":
