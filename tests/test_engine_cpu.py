@@ -52,3 +52,19 @@ def test_block_allocator_and_meta():
     assert pos.tolist() == [14, 15, 16, 17, 0, 1]
     # positions 14,15 live in row block 1 (id 2); 16,17 in row block 2 (id 0)
     assert slots.tolist() == [2 * 8 + 6, 2 * 8 + 7, 0, 1, 56, 57]
+
+
+def test_qwen3_moe_tiny_generates_and_is_batch_invariant():
+    from vllm_sm70_b200.models.config import ModelConfig
+
+    cfg = ModelConfig(arch="qwen3_moe", hidden_size=128, num_layers=2, num_heads=4,
+                      num_kv_heads=2, head_dim=32, intermediate_size=256, vocab_size=512,
+                      rope_theta=10000.0, rms_eps=1e-6, max_position=512, qk_norm=True,
+                      num_experts=8, top_k=2, moe_intermediate_size=64)
+    llm = LLM(cfg, max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=64)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (9, 30)]
+    both = llm.generate(prompts, SamplingParams(max_tokens=5))
+    solo = [llm.generate([p], SamplingParams(max_tokens=5))[0] for p in prompts]
+    assert [o.output_token_ids for o in both] == [o.output_token_ids for o in solo]

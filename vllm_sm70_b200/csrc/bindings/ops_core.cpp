@@ -10,6 +10,7 @@
 
 #include "ops_api.h"
 #include "comm/comm_api.h"
+#include "moe/moe_api.h"
 
 namespace b200 {
 namespace {
@@ -108,6 +109,134 @@ void gemm_bf16_silu_mul_out(at::Tensor& out, const at::Tensor& a, const at::Tens
 
 int64_t gemm_bf16_config(int64_t M, int64_t N, int64_t K, int64_t epi) {
   return gemm_bf16_pick_config((int)M, (int)N, (int)K, (int)epi, 148);
+}
+
+WQParams make_wq(int64_t fmt, const at::Tensor& scales, double out_scale) {
+  WQParams q{};
+  q.scale_ld = (int)scales.size(1);
+  q.out_scale = (float)out_scale;
+  TORCH_CHECK(scales.is_cuda() && scales.is_contiguous() && scales.dim() == 2, "wq: scales 2-D");
+  if (fmt == kWFp8) {
+    TORCH_CHECK(scales.scalar_type() == at::kFloat, "fp8: fp32 block scales");
+    q.scales_f32 = scales.data_ptr<float>();
+  } else if (fmt == kWAwq) {
+    TORCH_CHECK(scales.scalar_type() == at::kBFloat16 && scales.size(1) % 2 == 0,
+                "awq: bf16 (scale, -zero*scale) pairs");
+    q.scale_zero = reinterpret_cast<const __nv_bfloat162*>(scales.data_ptr());
+    q.scale_ld = (int)scales.size(1) / 2;
+  } else if (fmt == kWNvfp4) {
+    TORCH_CHECK(scales.element_size() == 1, "nvfp4: e4m3 scales as 1-byte elements");
+    q.scales_u8 = reinterpret_cast<const uint8_t*>(scales.data_ptr());
+  } else {
+    TORCH_CHECK(false, "unknown weight format ", fmt);
+  }
+  return q;
+}
+
+// Weight-only quantised GEMM for M <= 256 (fused dequant in the producer).
+void gemm_wq_out(at::Tensor& out, const at::Tensor& a, const at::Tensor& w_raw, int64_t fmt,
+                 const at::Tensor& scales, double out_scale, int64_t bn, int64_t splits) {
+  CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(out); CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(w_raw.is_cuda() && w_raw.dim() == 2 && w_raw.stride(1) == 1 &&
+                  w_raw.element_size() == 1, "gemm_wq: raw weight must be 2-D bytes");
+  const int M = (int)a.size(0), K = (int)a.size(1), N = (int)w_raw.size(0);
+  const int rb = raw_row_bytes((int)fmt);
+  TORCH_CHECK((int64_t)K * rb / 64 == w_raw.size(1), "gemm_wq: raw width does not match K");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_wq: out shape");
+  TORCH_CHECK(w_raw.stride(0) % 16 == 0, "gemm_wq: raw row stride must be 16B aligned");
+  c10::cuda::CUDAGuard g(a.device());
+  const WQParams q = make_wq(fmt, scales, out_scale);
+  gemm_wq_launch(a.data_ptr(), w_raw.data_ptr(), out.data_ptr(), M, N, K, (int)a.stride(0),
+                 (int)w_raw.stride(0), (int)out.stride(0), (int)fmt, q, (int)bn, (int)splits,
+                 device_status_ptr(a.get_device()), cur_stream());
+}
+
+void dequant_weight(at::Tensor& out, const at::Tensor& w_raw, int64_t fmt, const at::Tensor& scales) {
+  CHECK_BF16(out);
+  TORCH_CHECK(out.is_contiguous() && w_raw.dim() == 2 && w_raw.element_size() == 1,
+              "dequant_weight: shapes");
+  const int N = (int)out.size(0), K = (int)out.size(1);
+  c10::cuda::CUDAGuard g(out.device());
+  const WQParams q = make_wq(fmt, scales, 1.0);
+  dequant_weight_launch(w_raw.data_ptr(), w_raw.stride(0), out.data_ptr(), N, K, (int)fmt, q,
+                        cur_stream());
+}
+
+void moe_topk(at::Tensor& w, at::Tensor& ids, const at::Tensor& logits, int64_t k,
+              bool use_sigmoid, bool renorm, const c10::optional<at::Tensor>& bias) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "moe_topk: 2-D logits");
+  const bool bf = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf || logits.scalar_type() == at::kFloat, "moe_topk: bf16/fp32 logits");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && ids.scalar_type() == at::kInt, "moe_topk: outputs");
+  TORCH_CHECK(w.numel() == logits.size(0) * k && ids.numel() == logits.size(0) * k, "moe_topk: sizes");
+  c10::cuda::CUDAGuard g(logits.device());
+  moe_topk_launch(logits.data_ptr(), bf, (int)logits.stride(0), (int)logits.size(0),
+                  (int)logits.size(1), (int)k, use_sigmoid, renorm,
+                  bias ? bias->data_ptr<float>() : nullptr, w.data_ptr<float>(), ids.data_ptr<int>(),
+                  cur_stream());
+}
+
+// Expert-sort the (token, slot) pairs of experts [e_base, e_base + E).
+void moe_permute(const at::Tensor& ids, int64_t E, int64_t e_base, const c10::optional<at::Tensor>& x,
+                 const c10::optional<at::Tensor>& x_perm, at::Tensor& counts, at::Tensor& offsets,
+                 at::Tensor& rank_scratch, at::Tensor& pos, at::Tensor& src_row) {
+  CHECK_CUDA(ids);
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.dim() == 2 && ids.is_contiguous(), "ids [T, k] int32");
+  const int T = (int)ids.size(0), k = (int)ids.size(1);
+  TORCH_CHECK(counts.numel() >= E && offsets.numel() >= E + 1, "moe_permute: counts/offsets");
+  TORCH_CHECK(rank_scratch.numel() >= T * k && pos.numel() >= T * k && src_row.numel() >= T * k,
+              "moe_permute: scratch sizes");
+  int H = 0;
+  if (x) {
+    CHECK_BF16((*x));
+    TORCH_CHECK(x_perm && x->is_contiguous() && x_perm->is_contiguous(), "moe_permute: x / x_perm");
+    H = (int)x->size(1);
+    TORCH_CHECK(H % 8 == 0 && x_perm->size(1) == H && x_perm->size(0) >= T * k, "moe_permute: H");
+  }
+  c10::cuda::CUDAGuard g(ids.device());
+  moe_permute_launch(ids.data_ptr<int>(), T, k, (int)E, (int)e_base, x ? x->data_ptr() : nullptr, H,
+                     x_perm ? x_perm->data_ptr() : nullptr, counts.data_ptr<int>(),
+                     offsets.data_ptr<int>(), rank_scratch.data_ptr<int>(), pos.data_ptr<int>(),
+                     src_row.data_ptr<int>(), cur_stream());
+}
+
+void moe_combine(at::Tensor& out, const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w,
+                 const c10::optional<at::Tensor>& shared, double shared_scale) {
+  CHECK_CUDA(y); CHECK_BF16(y); CHECK_BF16(out);
+  TORCH_CHECK(pos.scalar_type() == at::kInt && w.scalar_type() == at::kFloat, "moe_combine: types");
+  const int T = (int)pos.size(0), k = (int)pos.size(1), H = (int)out.size(1);
+  TORCH_CHECK(out.is_contiguous() && y.is_contiguous() && y.size(1) == H && H % 2 == 0, "moe_combine");
+  c10::cuda::CUDAGuard g(y.device());
+  moe_combine_launch(y.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), T, k, H,
+                     shared ? shared->data_ptr() : nullptr, (float)shared_scale, out.data_ptr(),
+                     cur_stream());
+}
+
+// Grouped expert GEMM over expert-sorted rows.
+void gemm_grouped_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w_stk, int64_t E,
+                      int64_t N, const at::Tensor& row_off, at::Tensor& tile_off, int64_t fmt,
+                      const c10::optional<at::Tensor>& scales, double out_scale, int64_t bn) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out); CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(row_off.scalar_type() == at::kInt && tile_off.scalar_type() == at::kInt &&
+                  row_off.numel() >= E + 1 && tile_off.numel() >= E + 1, "gemm_grouped: offsets");
+  TORCH_CHECK(w_stk.dim() == 2 && w_stk.stride(1) == 1 && w_stk.size(0) == E * N, "gemm_grouped: W");
+  const int K = (int)x.size(1);
+  WQParams q{};
+  if (fmt != kWBf16) {
+    TORCH_CHECK(scales, "gemm_grouped: quantised weights need scales");
+    q = make_wq(fmt, *scales, out_scale);
+    TORCH_CHECK((int64_t)K * raw_row_bytes((int)fmt) / 64 == w_stk.size(1), "gemm_grouped: raw width");
+  } else {
+    CHECK_BF16(w_stk);
+    TORCH_CHECK(w_stk.size(1) == K, "gemm_grouped: K");
+  }
+  TORCH_CHECK(out.size(0) >= x.size(0) && out.size(1) == N, "gemm_grouped: out shape");
+  c10::cuda::CUDAGuard g(x.device());
+  gemm_grouped_launch(x.data_ptr(), w_stk.data_ptr(), out.data_ptr(), (int)x.size(0), (int)E,
+                      (int)N, K, (int)x.stride(0), (int)w_stk.stride(0), (int)out.stride(0),
+                      row_off.data_ptr<int>(), tile_off.data_ptr<int>(), (int)fmt, q, (int)bn,
+                      device_status_ptr(x.get_device()), cur_stream());
 }
 
 void rms_norm(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, double eps) {
@@ -325,6 +454,16 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("gemm_export_plans() -> int[]", &b200::gemm_export_plans_op);
   m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
   m.def("gemm_bf16_config(int M, int N, int K, int epi) -> int", &b200::gemm_bf16_config);
+  m.def("gemm_wq_out(Tensor(a!) out, Tensor a, Tensor w_raw, int fmt, Tensor scales, "
+        "float out_scale, int bn=0, int splits=0) -> ()");
+  m.def("dequant_weight(Tensor(a!) out, Tensor w_raw, int fmt, Tensor scales) -> ()");
+  m.def("moe_topk(Tensor(a!) w, Tensor(b!) ids, Tensor logits, int k, bool use_sigmoid, bool renorm, "
+        "Tensor? bias) -> ()");
+  m.def("moe_permute(Tensor ids, int E, int e_base, Tensor? x, Tensor(a!)? x_perm, Tensor(b!) counts, "
+        "Tensor(c!) offsets, Tensor(d!) rank_scratch, Tensor(e!) pos, Tensor(f!) src_row) -> ()");
+  m.def("moe_combine(Tensor(a!) out, Tensor y, Tensor pos, Tensor w, Tensor? shared, float shared_scale) -> ()");
+  m.def("gemm_grouped_out(Tensor(a!) out, Tensor x, Tensor w_stk, int E, int N, Tensor row_off, "
+        "Tensor(b!) tile_off, int fmt, Tensor? scales, float out_scale, int bn=0) -> ()");
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
   m.def("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()");
   m.def(
@@ -348,6 +487,12 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("gemm_bf16_out", &b200::gemm_bf16_out);
   m.impl("gemm_bf16_silu_mul_out", &b200::gemm_bf16_silu_mul_out);
   m.impl("rms_norm", &b200::rms_norm);
+  m.impl("moe_topk", &b200::moe_topk);
+  m.impl("moe_permute", &b200::moe_permute);
+  m.impl("moe_combine", &b200::moe_combine);
+  m.impl("gemm_grouped_out", &b200::gemm_grouped_out);
+  m.impl("gemm_wq_out", &b200::gemm_wq_out);
+  m.impl("dequant_weight", &b200::dequant_weight);
   m.impl("fused_add_rms_norm", &b200::fused_add_rms_norm);
   m.impl("rope_kv_write", &b200::rope_kv_write);
   m.impl("paged_attention", &b200::paged_attention);

@@ -1,6 +1,8 @@
 // Host API of the tcgen05 GEMM family (implemented in gemm_*.cu).
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
 
 #include <vector>
 
@@ -26,6 +28,52 @@ enum GemmConfig : int {
 };
 
 constexpr int kMaxSplits = 8;
+
+// Weight formats of the weight-only quantised GEMMs (activations bf16).
+enum WeightFormat : int {
+  kWBf16 = 0,
+  kWFp8 = 1,    // e4m3 [N, K], fp32 scale per 128x128 block: scales_f32[N/128][K/128]
+  kWAwq = 2,    // int4 [N, K/2] (low nibble = even k), per (row, 128-group) bf16x2 (s, -z*s)
+  kWNvfp4 = 3,  // e2m1 [N, K/2] (low nibble = even k), e4m3 scale per (row, 16 k); x out_scale
+};
+
+// Raw bytes of one weight row per 64-wide k-block.
+__host__ __device__ constexpr int raw_row_bytes(int wf) {
+  return wf == kWFp8 ? 64 : (wf == kWBf16 ? 0 : 32);
+}
+
+struct WQParams {
+  const float* scales_f32 = nullptr;                // kWFp8
+  const __nv_bfloat162* scale_zero = nullptr;       // kWAwq
+  const uint8_t* scales_u8 = nullptr;               // kWNvfp4
+  int scale_ld = 0;                                 // elements per scale row
+  float out_scale = 1.f;                            // kWNvfp4 global scale
+};
+
+// Grouped (MoE) GEMM: per-expert tiles read from device arrays.
+struct GroupInfo {
+  const int* tile_off = nullptr;  // [E + 1] tile prefix (filled by the launcher's setup kernel)
+  const int* row_off = nullptr;   // [E + 1] expert row offsets into X (expert-sorted rows)
+  int E = 0;                      // 0 = not grouped
+  int N = 0;                      // weight rows per expert
+};
+
+// C[r, :] = X[r, :] . W_e^T for r in expert e's rows [row_off[e], row_off[e+1]);
+// W stacked [E * N, K] (bf16, or raw quantised rows with stacked scales).
+// Swap-AB tiles (weights on the 128-row side), counts read on the device, so
+// the launch is CUDA-graph capturable. tile_off: int32 scratch [E + 1].
+void gemm_grouped_launch(const void* X, const void* Wstk, void* C, int rows, int E, int N, int K,
+                         int ldx, int ldw, int ldc, const int* row_off, int* tile_off, int wf,
+                         const WQParams& wq, int bn, unsigned int* err, cudaStream_t stream);
+
+void dequant_weight_launch(const void* raw, long long ld_raw, void* out, int N, int K, int wf,
+                           const WQParams& q, cudaStream_t stream);
+
+// C[M, N] = A[M, K] (bf16) . dequant(W)[N, K]^T, M <= 256 (decode shapes),
+// swap-AB tiles with split-K (bn/splits <= 0: automatic).
+void gemm_wq_launch(const void* A, const void* Wraw, void* C, int M, int N, int K, int lda,
+                    int ld_raw, int ldc, int wf, const WQParams& wq, int bn, int splits,
+                    unsigned int* err, cudaStream_t stream);
 
 struct GemmPlan {
   int cfg;

@@ -22,6 +22,15 @@
 // kernel/sm70_884_*.cu) and its gated-SiLU epilogue (types.h:141); the
 // reference computes the same contraction with mma.sync m8n8k4 on sm_70.
 //
+// Weight-only quantised variants (WF != kWBf16, swap-AB only): the producer
+// TMA-loads the raw weight tile (FP8 e4m3 with 128x128 block scales, AWQ int4
+// with g128 scale/zero, or NVFP4 e2m1 with e4m3 16-element block scales) into
+// a staging buffer; four extra dequant warps convert it to the bf16 128-byte-
+// swizzled operand tile (generic-proxy stores + fence.proxy.async) and signal
+// the MMA issuer. W8A16 / W4A16 semantics (the reference's TurboMind fp8 /
+// awq / nvfp4 ops: sm70/csrc/turbomind/ops/tm_fp8_sm70.cu, tm_awq_sm70.cu,
+// tm_nvfp4_sm70.cu).
+//
 // All mbarrier waits are bounded (common/ptx.cuh); on a timeout every role
 // leaves its loop, the MMA issuer drains its outstanding MMAs, the producer
 // drains its outstanding TMA copies, and the CTA frees TMEM before exiting.
@@ -38,6 +47,7 @@
 #include "common/ptx.cuh"
 #include "common/tmap.h"
 #include "gemm/gemm_api.h"
+#include "gemm/dequant.cuh"
 
 namespace b200 {
 namespace {
@@ -45,7 +55,8 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int UMMA_K = 16;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;    // bf16: producer, MMA, 4 epilogue warps
+constexpr int kThreadsQ = 320;   // quantised weights: + 4 dequant warps
 constexpr int kGroupM = 16;  // rasterisation group (M tiles) for L2 reuse
 
 struct TileCoord {
@@ -61,29 +72,70 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n) {
   return {first_m + r % gsize, r / gsize};
 }
 
-template <int BN, int STAGES>
+// Where one tile's operands come from and where its output goes.
+struct UnitCoord {
+  int p_row, q_row;    // TMA row coordinates of the P / Q operands
+  int out_i0, out_j0;  // output index bases along P / Q
+  int p_lim, q_lim;    // exclusive bounds for out_i0 + i / out_j0 + j
+};
+
+template <int BN>
+__device__ __forceinline__ UnitCoord unit_coord(int t, int num_m, int num_n, const GroupInfo& g,
+                                                int p_rows, int q_rows) {
+  if (g.E > 0) {
+    // Grouped (swap-AB): tiles are ordered expert by expert; within an expert,
+    // weight-row blocks vary fastest.
+    int lo = 0, hi = g.E;  // largest e with tile_off[e] <= t
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(g.tile_off + mid) <= t) lo = mid; else hi = mid;
+    }
+    const int e = lo;
+    const int local = t - __ldg(g.tile_off + e);
+    const int nbs = g.N / BM;
+    const int nb = local % nbs, qb = local / nbs;
+    const int r0 = __ldg(g.row_off + e);
+    UnitCoord u;
+    u.p_row = e * g.N + nb * BM;
+    u.q_row = r0 + qb * BN;
+    u.out_i0 = nb * BM;
+    u.out_j0 = u.q_row;
+    u.p_lim = g.N;
+    u.q_lim = __ldg(g.row_off + e + 1);
+    return u;
+  }
+  const TileCoord tc = tile_coord(t, num_m, num_n);
+  return UnitCoord{tc.mb * BM, tc.nb * BN, tc.mb * BM, tc.nb * BN, p_rows, q_rows};
+}
+
+template <int BN, int STAGES, int WF = kWBf16>
 struct Smem {
   static constexpr int kPBytes = BM * BK * 2;
   static constexpr int kQBytes = BN * BK * 2;
-  static constexpr int kStageBytes = kPBytes + kQBytes;
+  static constexpr int kRawBytes = BM * raw_row_bytes(WF);  // weight = P side (swap)
+  static constexpr int kStageBytes = kPBytes + kQBytes + kRawBytes;
   static constexpr int kTileBytes = STAGES * kStageBytes;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = 512;
   static constexpr int kTotal = kTileBytes + kBarBytes + 1024;  // +1024 for manual alignment
 };
 
-template <int BN, int STAGES, bool SWAP, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16>
+__global__ void __launch_bounds__(WF == kWBf16 ? kThreads : kThreadsQ, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     const __grid_constant__ CUtensorMap tmap_q, __nv_bfloat16* __restrict__ C,
                     int ldc, int p_rows, int q_rows, int K, int splits, float* __restrict__ ws,
-                    int* __restrict__ counters, unsigned int* err) {
-  using S = Smem<BN, STAGES>;
+                    int* __restrict__ counters, unsigned int* err, const WQParams wq,
+                    const GroupInfo grp) {
+  static_assert(WF == kWBf16 || SWAP, "quantised weights use the swap-AB (weight = P) form");
+  constexpr bool kQuant = WF != kWBf16;
+  using S = Smem<BN, STAGES, WF>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::kTileBytes);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;  // [2]
+  uint64_t* dq_bar = empty_bar + STAGES;     // [STAGES] dequantised operand ready
+  uint64_t* tfull_bar = dq_bar + STAGES;     // [2]
   uint64_t* tempty_bar = tfull_bar + 2;      // [2]
   uint64_t* done_bar = tempty_bar + 2;       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -97,7 +149,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
   const int kb_per = (num_kb + splits - 1) / splits;
-  const int num_units = num_tiles * splits;
+  const int num_units = grp.E > 0 ? __ldg(grp.tile_off + grp.E) * splits : num_tiles * splits;
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                  : (2 * BN <= 256) ? 256 : 512;
 
@@ -105,6 +157,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
+      mbar_init(&dq_bar[s], 4);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
@@ -135,7 +188,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       long issued = 0;
       for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
         const int t = u / splits, sp = u - t * splits;
-        const TileCoord tc = tile_coord(t, num_m, num_n);
+        const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err)) {
@@ -143,9 +196,18 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             break;
           }
           uint8_t* spp = smem + stage * S::kStageBytes;
-          mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-          tma_load_2d(spp, &tmap_p, &full_bar[stage], kb * BK, tc.mb * BM);
-          tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, tc.nb * BN);
+          if constexpr (kQuant) {
+            // Activations (Q side, bf16) + the raw weight tile; the P operand is
+            // written by the dequant warps.
+            mbar_arrive_expect_tx(&full_bar[stage], S::kQBytes + S::kRawBytes);
+            tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, uc.q_row);
+            tma_load_2d(spp + S::kPBytes + S::kQBytes, &tmap_p, &full_bar[stage],
+                        kb * raw_row_bytes(WF), uc.p_row);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+            tma_load_2d(spp, &tmap_p, &full_bar[stage], kb * BK, uc.p_row);
+            tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, uc.q_row);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -182,7 +244,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, err)) {
+          if (!mbar_wait(kQuant ? &dq_bar[stage] : &full_bar[stage], phase, err)) {
             ok = false;
             break;
           }
@@ -213,16 +275,52 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       mbar_wait(done_bar, 0, err);
     }
     __syncwarp();
+  } else if (kQuant && warp >= 6) {
+    // ------------------------------------------------------------ dequant warps
+    const int dt = threadIdx.x - 192;  // 0..127
+    const int c = dt & 7;              // 16-byte chunk (8 k) of the row
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+      const int t = u / splits, sp = u - t * splits;
+      const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
+      const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, err)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* spp = smem + stage * S::kStageBytes;
+        const uint8_t* raw = spp + S::kPBytes + S::kQBytes;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int r = (dt >> 3) + 16 * j;  // tile row 0..127
+          const int n = uc.p_row + r;        // weight row (stacked for grouped)
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (n < p_rows) v = dequant8<WF>(raw + r * raw_row_bytes(WF), c, wq, n, kb);
+          *reinterpret_cast<uint4*>(spp + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+        }
+        // Generic-proxy smem writes -> visible to the tensor core (async proxy).
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if ((dt & 31) == 0) mbar_arrive(&dq_bar[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
     const int etid = threadIdx.x - 64;  // 0..127
     constexpr int CW = BN >= 32 ? 32 : 16;  // columns per tcgen05.ld
+    const float out_scale = wq.out_scale;
     int local = 0;
     for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x, ++local) {
       const int t = u / splits, sp = u - t * splits;
-      const TileCoord tc = tile_coord(t, num_m, num_n);
+      const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err)) {
@@ -231,7 +329,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       }
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      const int i = tc.mb * BM + row_in_tile;  // P row
+      const int i = uc.out_i0 + row_in_tile;  // output index along P
       const bool split = splits > 1;
       // Tile-local fp32 partials of this unit: ws[(t * splits + s)][row][col].
       float* ws_tile = split ? ws + (size_t)t * splits * (BM * BN) : nullptr;
@@ -286,7 +384,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           }
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < CW; ++c) v[c] = __uint_as_float(r[c]);
+          for (int c = 0; c < CW; ++c) v[c] = __uint_as_float(r[c]) * out_scale;
         } else {
 #pragma unroll
           for (int c = 0; c < CW; ++c) v[c] = 0.f;
@@ -319,6 +417,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
               }
             }
           }
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] *= out_scale;
         }
       };
 
@@ -331,8 +431,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             float g[32], uu[32];
             fetch(blk * 128 + half * 32, g);
             fetch(blk * 128 + 64 + half * 32, uu);
-            const int j0 = tc.nb * (BN / 2) + blk * 64 + half * 32;
-            if (i < p_rows) {
+            const int j0 = (uc.q_row / BN) * (BN / 2) + blk * 64 + half * 32;
+            if (i < uc.p_lim) {
               uint32_t packed[16];
 #pragma unroll
               for (int c = 0; c < 16; ++c) {
@@ -358,13 +458,13 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         for (int ch = 0; ch < BN / CW; ++ch) {
           float r[32];
           fetch(ch * CW, r);
-          const int j0 = tc.nb * BN + ch * CW;
+          const int j0 = uc.out_j0 + ch * CW;
           if constexpr (!SWAP) {
-            if (i < p_rows) {
+            if (i < uc.p_lim) {
               __nv_bfloat16* dst = C + (size_t)i * ldc + j0;
 #pragma unroll
               for (int v = 0; v < CW / 8; ++v) {
-                if (j0 + v * 8 + 8 <= q_rows) {
+                if (j0 + v * 8 + 8 <= uc.q_lim) {
                   uint4 pk;
                   pk.x = pack_bf16x2(r[8 * v + 0], r[8 * v + 1]);
                   pk.y = pack_bf16x2(r[8 * v + 2], r[8 * v + 3]);
@@ -377,11 +477,11 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           } else {
             // Transposed store: lane i holds P row i (an output column);
             // consecutive lanes write consecutive bf16 of one output row.
-            if (i < p_rows) {
+            if (i < uc.p_lim) {
 #pragma unroll
               for (int c = 0; c < CW; ++c) {
                 const int j = j0 + c;
-                if (j < q_rows) C[(size_t)j * ldc + i] = __float2bfloat16_rn(r[c]);
+                if (j < uc.q_lim) C[(size_t)j * ldc + i] = __float2bfloat16_rn(r[c]);
               }
             }
           }
@@ -413,12 +513,13 @@ struct SplitWorkspace {
 };
 SplitWorkspace g_split_ws[64];
 
-template <int BN, int STAGES, bool SWAP, int EPI>
+template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16>
 void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, int K, int ldp,
                 int ldq, int ldc, int splits, float* ws, int* counters, unsigned int* err,
-                cudaStream_t stream) {
-  using S = Smem<BN, STAGES>;
-  auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI>;
+                cudaStream_t stream, const WQParams& wq = WQParams{},
+                const GroupInfo& grp = GroupInfo{}, int grid_units = 0) {
+  using S = Smem<BN, STAGES, WF>;
+  auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI, WF>;
   static bool attr_set = false;  // per instantiation; idempotent if raced
   if (!attr_set) {
     cudaError_t e =
@@ -427,16 +528,28 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
       throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     attr_set = true;
   }
-  CUtensorMap tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, K,
-                                (uint64_t)ldp * 2, BM, BK);
+  CUtensorMap tp;
+  if constexpr (WF == kWBf16) {
+    tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, K, (uint64_t)ldp * 2, BM,
+                      BK);
+  } else {
+    // Raw quantised rows: K * bytes-per-element bytes, box = 128 rows x one k-block.
+    const int rb = raw_row_bytes(WF);
+    tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p_rows, (uint64_t)K * rb / 64,
+                      (uint64_t)ldp, BM, rb, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   CUtensorMap tq = make_tmap_2d(Q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, K,
                                 (uint64_t)ldq * 2, BN, BK);
   int dev = 0;
   cudaGetDevice(&dev);
-  const long units = (long)((p_rows + BM - 1) / BM) * ((q_rows + BN - 1) / BN) * splits;
+  const long units = grid_units > 0 ? grid_units
+                                    : (long)((p_rows + BM - 1) / BM) * ((q_rows + BN - 1) / BN) * splits;
   const int grid = units < num_sms(dev) ? (int)units : num_sms(dev);
-  kernel<<<grid, kThreads, S::kTotal, stream>>>(tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                                p_rows, q_rows, K, splits, ws, counters, err);
+  WQParams q = wq;
+  if (WF == kWBf16) q.out_scale = 1.f;
+  kernel<<<grid, WF == kWBf16 ? kThreads : kThreadsQ, S::kTotal, stream>>>(
+      tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits, ws, counters,
+      err, q, grp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc launch: ") + cudaGetErrorString(e));
@@ -632,6 +745,109 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
   }
 #undef B200_NORMAL
 #undef B200_SWAP
+}
+
+void gemm_wq_launch(const void* A, const void* Wraw, void* C, int M, int N, int K, int lda,
+                    int ld_raw, int ldc, int wf, const WQParams& wq, int bn, int splits,
+                    unsigned int* err, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return;
+  if (K % 128 != 0) throw std::runtime_error("gemm_wq: K must be a multiple of 128");
+  if (lda % 8 != 0 || ldc % 8 != 0 || N % 8 != 0)
+    throw std::runtime_error("gemm_wq: leading dims / N must be multiples of 8");
+  if (M > 256) throw std::runtime_error("gemm_wq: M > 256 uses dequantise + bf16 GEMM");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const SplitWorkspace& w = g_split_ws[dev];
+  if (bn <= 0) bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const long tiles = (long)((N + 127) / 128) * ((M + bn - 1) / bn);
+  const int num_kb = K / 64;
+  if (splits <= 0) {
+    splits = 1;
+    const int sms = num_sms(dev);
+    while (splits < kMaxSplits && tiles * (splits + 1) <= sms && num_kb / (splits + 1) >= 4)
+      ++splits;
+  }
+  if (splits > 1) {
+    const size_t need = (size_t)tiles * splits * 128 * bn * sizeof(float);
+    if (w.ws == nullptr || need > w.ws_bytes || tiles > w.n_counters) splits = 1;
+  }
+  float* wsp = splits > 1 ? w.ws : nullptr;
+  int* cnt = splits > 1 ? w.counters : nullptr;
+#define B200_WQ(BN_, ST_, WF_)                                                                  \
+  return launch_cfg<BN_, ST_, true, kEpiNone, WF_>(Wraw, A, C, N, M, K, ld_raw, lda, ldc, splits, \
+                                                   wsp, cnt, err, stream, wq)
+#define B200_WQ_BN(WF_)                          \
+  switch (bn) {                                  \
+    case 16: B200_WQ(16, 6, WF_);                \
+    case 32: B200_WQ(32, 6, WF_);                \
+    case 64: B200_WQ(64, 5, WF_);                \
+    case 128: B200_WQ(128, 4, WF_);              \
+    case 256: B200_WQ(256, 3, WF_);              \
+    default: throw std::runtime_error("gemm_wq: bad BN"); \
+  }
+  switch (wf) {
+    case kWFp8: B200_WQ_BN(kWFp8);
+    case kWAwq: B200_WQ_BN(kWAwq);
+    case kWNvfp4: B200_WQ_BN(kWNvfp4);
+    default: throw std::runtime_error("gemm_wq: unknown weight format");
+  }
+#undef B200_WQ_BN
+#undef B200_WQ
+}
+
+namespace {
+// tile_off[e + 1] = tile_off[e] + (N / 128) * ceil(count_e / BN), on device.
+__global__ void grouped_tiles_kernel(const int* __restrict__ row_off, int E, int nbs, int bn,
+                                     int* __restrict__ tile_off) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int acc = 0;
+  tile_off[0] = 0;
+  for (int e = 0; e < E; ++e) {
+    const int cnt = row_off[e + 1] - row_off[e];
+    acc += nbs * ((cnt + bn - 1) / bn);
+    tile_off[e + 1] = acc;
+  }
+}
+}  // namespace
+
+void gemm_grouped_launch(const void* X, const void* Wstk, void* C, int rows, int E, int N, int K,
+                         int ldx, int ldw, int ldc, const int* row_off, int* tile_off, int wf,
+                         const WQParams& wq, int bn, unsigned int* err, cudaStream_t stream) {
+  if (rows <= 0 || E <= 0) return;
+  if (N % 128 != 0) throw std::runtime_error("gemm_grouped: N per expert must be a multiple of 128");
+  if (K % 64 != 0) throw std::runtime_error("gemm_grouped: K must be a multiple of 64");
+  if (wf != kWBf16 && K % 128 != 0) throw std::runtime_error("gemm_grouped: quantised K % 128");
+  if (bn <= 0) {
+    const int avg = rows / E;
+    bn = avg <= 16 ? 16 : avg <= 32 ? 32 : avg <= 64 ? 64 : avg <= 128 ? 128 : 256;
+  }
+  grouped_tiles_kernel<<<1, 32, 0, stream>>>(row_off, E, N / 128, bn, tile_off);
+  GroupInfo g{tile_off, row_off, E, N};
+  const int nbs = N / 128;
+  const long max_tiles = (long)nbs * ((rows + bn - 1) / bn + E);
+  const int units = (int)(max_tiles < (1 << 30) ? max_tiles : (1 << 30));
+  const int P = E * N;
+#define B200_G(BN_, ST_, WF_)                                                                   \
+  return launch_cfg<BN_, ST_, true, kEpiNone, WF_>(Wstk, X, C, P, rows, K, ldw, ldx, ldc, 1,       \
+                                                   nullptr, nullptr, err, stream, wq, g, units)
+#define B200_G_BN(WF_, S16, S64, S128, S256)                     \
+  switch (bn) {                                                  \
+    case 16: B200_G(16, S16, WF_);                               \
+    case 32: B200_G(32, S16, WF_);                               \
+    case 64: B200_G(64, S64, WF_);                               \
+    case 128: B200_G(128, S128, WF_);                            \
+    case 256: B200_G(256, S256, WF_);                            \
+    default: throw std::runtime_error("gemm_grouped: bad BN");   \
+  }
+  switch (wf) {
+    case kWBf16: B200_G_BN(kWBf16, 8, 8, 6, 4);
+    case kWFp8: B200_G_BN(kWFp8, 6, 5, 4, 3);
+    case kWAwq: B200_G_BN(kWAwq, 6, 5, 4, 3);
+    case kWNvfp4: B200_G_BN(kWNvfp4, 6, 5, 4, 3);
+    default: throw std::runtime_error("gemm_grouped: unknown weight format");
+  }
+#undef B200_G_BN
+#undef B200_G
 }
 
 void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,

@@ -1,0 +1,18 @@
+// Host API of the MoE routing kernels (moe_route.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+void moe_topk_launch(const void* logits, bool bf16, int ld, int T, int E, int k, bool sigmoid,
+                     bool renorm, const float* bias, float* w, int* ids, cudaStream_t stream);
+
+// ids [T*k] global expert ids; experts [e_base, e_base + E) are local.
+void moe_permute_launch(const int* ids, int T, int k, int E, int e_base, const void* x, int H,
+                        void* x_perm, int* counts, int* offsets, int* rank_scratch, int* pos,
+                        int* src_row, cudaStream_t stream);
+
+void moe_combine_launch(const void* y, const int* pos, const float* w, int T, int k, int H,
+                        const void* shared, float shared_scale, void* out, cudaStream_t stream);
+
+}  // namespace b200

@@ -172,12 +172,13 @@ def model_gemm_shapes(model, Ms: list[int]) -> list[tuple[int, int, int, int]]:
     seen = set()
     for L in model.layers:
         for name, lin in L.items():
-            if not hasattr(lin, "w") or not hasattr(lin, "forward"):
+            w = getattr(lin, "w", None)
+            if not isinstance(w, torch.Tensor) or not hasattr(lin, "forward"):
                 continue
-            if lin.w.dtype != torch.bfloat16:
+            if w.dtype != torch.bfloat16:
                 continue
             epi = EPI_SILU if type(lin).__name__ == "GateUpLinear" else EPI_NONE
-            nk = (lin.w.shape[0], lin.w.shape[1], epi)
+            nk = (w.shape[0], w.shape[1], epi)
             if nk in seen:
                 continue
             seen.add(nk)

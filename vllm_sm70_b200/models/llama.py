@@ -29,6 +29,23 @@ from .config import ModelConfig
 from .layers import AttnMeta, DenseLinear, GateUpLinear, KVCache
 
 
+class _QuantGateUp:
+    """Quantised gate/up projection ([gate | up] rows) followed by SiLU*up."""
+
+    def __init__(self, lin):
+        self.lin = lin
+        self.w = None  # no bf16 weight: the tuner skips this layer
+        self.out_features = lin.out_features // 2
+        self.in_features = lin.in_features
+
+    def forward(self, x, out=None):
+        h = self.lin.forward(x)
+        return ops.silu_mul(h, out=out)
+
+    def weight_bytes(self):
+        return self.lin.weight_bytes()
+
+
 def _shard(n: int, tp: int, rank: int) -> slice:
     assert n % tp == 0, (n, tp)
     k = n // tp
@@ -60,6 +77,26 @@ class LlamaModel:
         self.final_norm = None
 
     # ------------------------------------------------------------------ weights
+    def make_linear(self, w: torch.Tensor) -> "DenseLinear":
+        """Dense bf16 or weight-only quantised linear per ``cfg.quant``."""
+        if self.cfg.quant in ("fp8", "awq", "nvfp4"):
+            from ..ops import quant
+
+            return quant.make_linear(self.cfg.quant, w)
+        return DenseLinear(w.to(self.dtype))
+
+    def make_gate_up(self, wg: torch.Tensor, wu: torch.Tensor):
+        if self.cfg.quant in ("fp8", "awq", "nvfp4"):
+            from ..ops import quant
+
+            return _QuantGateUp(quant.make_linear(self.cfg.quant, torch.cat([wg, wu], 0)))
+        return GateUpLinear(wg.to(self.dtype), wu.to(self.dtype))
+
+    def init_mlp_dummy(self, rnd) -> dict:
+        h = self.cfg.hidden_size
+        return {"gate_up": self.make_gate_up(rnd(self.inter, h), rnd(self.inter, h)),
+                "down": self.make_linear(rnd(h, self.inter))}
+
     def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
         """Random-init weights of the configured shapes (TP-local shards)."""
         cfg, dev, dt = self.cfg, self.device, self.dtype
@@ -67,11 +104,11 @@ class LlamaModel:
         g.manual_seed(seed * 7919 + self.ps.tp_rank)
 
         def rnd(*shape):
-            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std).to(dt)
+            return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std
 
         h = cfg.hidden_size
-        self.embed = rnd(self.vocab_local, h)
-        self.lm_head = self.embed if cfg.tie_embeddings else rnd(self.vocab_local, h)
+        self.embed = rnd(self.vocab_local, h).to(dt)
+        self.lm_head = self.embed if cfg.tie_embeddings else rnd(self.vocab_local, h).to(dt)
         self.final_norm = torch.ones(h, device=dev, dtype=dt)
         qkv_out = (self.hq + 2 * self.hkv) * self.d
         self.layers = []
@@ -79,11 +116,10 @@ class LlamaModel:
             L = {
                 "in_norm": torch.ones(h, device=dev, dtype=dt),
                 "post_norm": torch.ones(h, device=dev, dtype=dt),
-                "qkv": DenseLinear(rnd(qkv_out, h)),
-                "o": DenseLinear(rnd(h, self.hq * self.d)),
-                "gate_up": GateUpLinear(rnd(self.inter, h), rnd(self.inter, h)),
-                "down": DenseLinear(rnd(h, self.inter)),
+                "qkv": self.make_linear(rnd(qkv_out, h)),
+                "o": self.make_linear(rnd(h, self.hq * self.d)),
             }
+            L.update(self.init_mlp_dummy(rnd))
             if cfg.qk_norm:
                 L["q_norm"] = torch.ones(self.d, device=dev, dtype=dt)
                 L["k_norm"] = torch.ones(self.d, device=dev, dtype=dt)
@@ -188,10 +224,14 @@ class LlamaModel:
             o = L["o"].forward(attn_out.view(T, self.hq * self.d),
                                out=comm.row_parallel_out(T, H))
             x, residual = comm.all_reduce_add_rms_norm(o, residual, L["post_norm"], eps)
-            h = L["gate_up"].forward(x)
-            x = L["down"].forward(h, out=comm.row_parallel_out(T, H))
+            x = self.mlp(li, L, x, comm.row_parallel_out(T, H))
         x, residual = comm.all_reduce_add_rms_norm(x, residual, self.final_norm, eps)
         return x
+
+    def mlp(self, li: int, L: dict, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+        """Dense SwiGLU MLP (row-parallel output, reduced by the caller)."""
+        h = L["gate_up"].forward(x)
+        return L["down"].forward(h, out=out)
 
     def greedy(self, hidden: torch.Tensor) -> torch.Tensor:
         """Vocab-parallel greedy sampling: local LM-head GEMM + argmax, then a

@@ -1,0 +1,80 @@
+"""Qwen3-MoE (e.g. Qwen3-30B-A3B): the Llama-style attention block with q/k
+RMSNorm and a routed-expert MLP (softmax top-k, renormalised), block-FP8
+weights when the checkpoint is FP8.
+
+Parallelism: attention is tensor-parallel; experts are expert-parallel over
+the same group (rank r owns experts [r*E/W, (r+1)*E/W)). Every rank holds
+every token after the attention all-reduce, so the MoE block needs no
+all-to-all: each rank runs its local experts for all tokens and the partial
+sums ride the fused all-reduce + residual + RMSNorm that follows.
+
+Reference parity: the Flint MoE block (``sm70/vllm_sm70/models/flint_sm70/
+model.py:200-300``) with its fused router and MoE methods; Qwen3-MoE is one
+of the BASELINE model families.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops import moe as moe_ops
+from .llama import LlamaModel
+
+
+class Qwen3MoeModel(LlamaModel):
+    def __init__(self, cfg, device, dtype=torch.bfloat16, ps=None):
+        super().__init__(cfg, device, dtype, ps)
+        tp = self.ps.tp_size
+        assert cfg.num_experts % tp == 0, "experts must divide across the EP group"
+        self.E_local = cfg.num_experts // tp
+        self.e_base = self.ps.tp_rank * self.E_local
+        self.moe_ws = None
+
+    def init_mlp_dummy(self, rnd) -> dict:
+        cfg = self.cfg
+        h, I, E = cfg.hidden_size, cfg.moe_intermediate_size, self.E_local
+        fmt = cfg.quant if cfg.quant in ("fp8", "awq", "nvfp4") else "bf16"
+        w13 = rnd(E, 2 * I, h)
+        w2 = rnd(E, h, I)
+        L = {"router": rnd(cfg.num_experts, h).to(self.dtype),
+             "experts": moe_ops.ExpertWeights.from_dense(fmt, w13, w2)}
+        if cfg.shared_expert_intermediate_size:
+            Is = cfg.shared_expert_intermediate_size // self.ps.tp_size
+            L["shared_gate_up"] = self.make_gate_up(rnd(Is, h), rnd(Is, h))
+            L["shared_down"] = self.make_linear(rnd(h, Is))
+            L["shared_gate"] = rnd(1, h).to(self.dtype)
+        return L
+
+    def _ws(self, T: int):
+        cfg = self.cfg
+        if self.moe_ws is None or self.moe_ws.max_tokens < T:
+            n = max(T, 256)
+            self.moe_ws = moe_ops.MoEWorkspace(n, cfg.top_k, self.E_local, cfg.hidden_size,
+                                               cfg.moe_intermediate_size, self.device)
+        return self.moe_ws
+
+    def reserve_workspace(self, max_tokens: int) -> None:
+        self._ws(max_tokens)
+
+    def mlp(self, li, L, x, out):
+        from .. import ops
+
+        cfg = self.cfg
+        T = x.shape[0]
+        logits = ops.gemm(x, L["router"]) if x.is_cuda else (x.float() @ L["router"].float().t())
+        ws = self._ws(T) if x.is_cuda else None
+        w = ws.w[:T] if ws else None
+        ids = ws.ids[:T] if ws else None
+        w, ids = moe_ops.topk(logits, cfg.top_k, use_sigmoid=False, renorm=cfg.norm_topk_prob,
+                              w=w, ids=ids)
+        shared = None
+        if "shared_gate_up" in L:
+            sh = L["shared_down"].forward(L["shared_gate_up"].forward(x))
+            gate = torch.sigmoid((x.float() @ L["shared_gate"].float().t()))
+            shared = (sh.float() * gate).to(x.dtype)
+        return moe_ops.experts_forward(x, w, ids, L["experts"], ws, self.e_base, shared, out)
+
+    def weight_bytes(self) -> int:
+        n = self.embed.numel() * 2 + (0 if self.cfg.tie_embeddings else self.lm_head.numel() * 2)
+        for L in self.layers:
+            n += L["qkv"].weight_bytes() + L["o"].weight_bytes() + L["experts"].bytes()
+        return n

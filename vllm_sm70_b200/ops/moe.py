@@ -1,0 +1,194 @@
+"""Mixture-of-experts: router top-k, expert-sorted permutation, grouped
+tcgen05 expert GEMMs (bf16 or weight-only FP8 / AWQ / NVFP4 with the
+dequantisation fused in the producer), SiLU*up, weighted combine.
+
+Expert parallelism: a rank owns experts ``[e_base, e_base + E_local)``; every
+rank holds every token (attention is tensor-parallel), so the rank computes
+its local experts for all tokens and the partial outputs are summed by the
+row-parallel all-reduce that the model already fuses with the next residual
+add + RMSNorm. Nothing in the data path depends on host-side counts, so the
+whole block is CUDA-graph capturable.
+
+Reference parity: MoE methods and routing runtime
+(``sm70/vllm_sm70/fused_moe/method.py:56-416``), FP8 / NVFP4 MoE methods
+(``quant/fp8_moe.py``, ``quant/nvfp4_moe.py``), the fused router (K13,
+``router.py``) and the decode MoE kernels (K12). The reference refuses EP
+(``method.py:357-358``); here EP over the TP group is the default at TP > 1.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _ext
+from ..utils import launch_count
+from . import linear as _lin
+from . import quant as _q
+
+FMT = {"bf16": 0, "fp8": 1, "awq": 2, "nvfp4": 3}
+
+
+def topk_ref(logits: torch.Tensor, k: int, use_sigmoid: bool = False, renorm: bool = True):
+    x = logits.float().nan_to_num(nan=float("-inf"))
+    sc = torch.sigmoid(x) if use_sigmoid else torch.softmax(x, -1)
+    sc = sc.nan_to_num(nan=0.0)
+    # ties -> lower expert id: stable sort on (-score, id)
+    order = torch.sort(-sc, dim=-1, stable=True).indices[:, :k]
+    w = torch.gather(sc, 1, order)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True).clamp_min(1e-20)
+    return w, order.to(torch.int32)
+
+
+def topk(logits: torch.Tensor, k: int, use_sigmoid: bool = False, renorm: bool = True,
+         bias: torch.Tensor | None = None, w: torch.Tensor | None = None,
+         ids: torch.Tensor | None = None):
+    T = logits.shape[0]
+    if w is None:
+        w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    if ids is None:
+        ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    if logits.is_cuda:
+        _ext.require()
+        torch.ops._b200_C.moe_topk(w, ids, logits, k, use_sigmoid, renorm, bias)
+        launch_count.add(1)
+    else:
+        ww, ii = topk_ref(logits if bias is None else logits, k, use_sigmoid, renorm)
+        w.copy_(ww)
+        ids.copy_(ii)
+    return w, ids
+
+
+@dataclass
+class ExpertWeights:
+    """Stacked per-expert weights: w13 [E*2I, H] ([gate | up] rows per expert)
+    and w2 [E*H, I], bf16 or raw quantised bytes with stacked scales."""
+    fmt: str
+    E: int
+    H: int
+    I: int
+    w13: torch.Tensor
+    w2: torch.Tensor
+    s13: torch.Tensor | None = None
+    s2: torch.Tensor | None = None
+    g13: float = 1.0
+    g2: float = 1.0
+
+    @classmethod
+    def from_dense(cls, fmt: str, w13: torch.Tensor, w2: torch.Tensor):
+        """w13 [E, 2I, H], w2 [E, H, I] dense (fp32/bf16) -> stacked format."""
+        E, I2, H = w13.shape
+        I = I2 // 2
+        if fmt == "bf16":
+            return cls(fmt, E, H, I, w13.reshape(E * I2, H).to(torch.bfloat16).contiguous(),
+                       w2.reshape(E * H, I).to(torch.bfloat16).contiguous())
+        l13 = _q.make_linear(fmt, w13.reshape(E * I2, H))
+        l2 = _q.make_linear(fmt, w2.reshape(E * H, I))
+        return cls(fmt, E, H, I, l13.raw, l2.raw, l13.scales, l2.scales, l13.out_scale,
+                   l2.out_scale)
+
+    def dense_ref(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp32 [E, 2I, H], [E, H, I] of what the kernels compute with."""
+        if self.fmt == "bf16":
+            return (self.w13.float().view(self.E, 2 * self.I, self.H),
+                    self.w2.float().view(self.E, self.H, self.I))
+        a = _wrap(self.fmt, self.w13, self.s13, self.g13, self.E * 2 * self.I, self.H)
+        b = _wrap(self.fmt, self.w2, self.s2, self.g2, self.E * self.H, self.I)
+        return (a.reference_weight().view(self.E, 2 * self.I, self.H),
+                b.reference_weight().view(self.E, self.H, self.I))
+
+    def bytes(self) -> int:
+        n = self.w13.numel() * self.w13.element_size() + self.w2.numel() * self.w2.element_size()
+        for s in (self.s13, self.s2):
+            if s is not None:
+                n += s.numel() * s.element_size()
+        return n
+
+
+def _wrap(fmt, raw, scales, gscale, N, K):
+    obj = object.__new__({"fp8": _q.Fp8BlockLinear, "awq": _q.AwqLinear,
+                          "nvfp4": _q.Nvfp4Linear}[fmt])
+    obj.raw, obj.scales, obj.out_scale = raw, scales, gscale
+    obj.out_features, obj.in_features = N, K
+    return obj
+
+
+class MoEWorkspace:
+    """Persistent per-forward buffers sized for ``max_tokens`` (graph-safe)."""
+
+    def __init__(self, max_tokens: int, k: int, E_local: int, H: int, I: int, device):
+        P = max_tokens * k
+        i32 = dict(dtype=torch.int32, device=device)
+        self.max_tokens, self.k = max_tokens, k
+        self.w = torch.empty(max_tokens, k, dtype=torch.float32, device=device)
+        self.ids = torch.empty(max_tokens, k, **i32)
+        self.counts = torch.empty(E_local, **i32)
+        self.offsets = torch.empty(E_local + 1, **i32)
+        self.tile_off = torch.empty(E_local + 1, **i32)
+        self.rank = torch.empty(P, **i32)
+        self.pos = torch.empty(max_tokens, k, **i32)
+        self.src = torch.empty(P, **i32)
+        self.x_perm = torch.empty(P, H, dtype=torch.bfloat16, device=device)
+        self.h = torch.empty(P, 2 * I, dtype=torch.bfloat16, device=device)
+        self.act = torch.empty(P, I, dtype=torch.bfloat16, device=device)
+        self.y = torch.empty(P, H, dtype=torch.bfloat16, device=device)
+
+
+def experts_forward_ref(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: ExpertWeights,
+                        e_base: int = 0) -> torch.Tensor:
+    """fp32 oracle of the routed experts (local experts only)."""
+    w13, w2 = ew.dense_ref()
+    T, k = ids.shape
+    out = torch.zeros(T, ew.H, dtype=torch.float32, device=x.device)
+    xf = x.float()
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j]) - e_base
+            if e < 0 or e >= ew.E:
+                continue
+            h = w13[e] @ xf[t]
+            g, u = h[: ew.I], h[ew.I:]
+            a = (g * torch.sigmoid(g) * u).to(torch.bfloat16).float()
+            out[t] += float(w[t, j]) * (w2[e] @ a)
+    return out
+
+
+def experts_forward(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: ExpertWeights,
+                    ws: MoEWorkspace, e_base: int = 0, shared: torch.Tensor | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed experts for tokens ``x [T, H]`` with routing ``(w, ids) [T, k]``;
+    only experts ``[e_base, e_base + ew.E)`` are computed here. ``shared``
+    (same shape as the output) is added in the combine."""
+    T, k = ids.shape
+    if out is None:
+        out = torch.empty(T, ew.H, dtype=torch.bfloat16, device=x.device)
+    if not x.is_cuda:
+        r = experts_forward_ref(x, w, ids, ew, e_base)
+        if shared is not None:
+            r = r + shared.float()
+        out.copy_(r.to(out.dtype))
+        return out
+    _ext.require()
+    ops = torch.ops._b200_C
+    P = T * k
+    xp, h, act, y = ws.x_perm[:P], ws.h[:P], ws.act[:P], ws.y[:P]
+    pos = ws.pos[:T]
+    ops.moe_permute(ids, ew.E, e_base, x, xp, ws.counts, ws.offsets, ws.rank, pos, ws.src)
+    fmt = FMT[ew.fmt]
+    ops.gemm_grouped_out(h, xp, ew.w13, ew.E, 2 * ew.I, ws.offsets, ws.tile_off, fmt, ew.s13,
+                         ew.g13, 0)
+    ops.silu_mul(act, h)
+    ops.gemm_grouped_out(y, act, ew.w2, ew.E, ew.H, ws.offsets, ws.tile_off, fmt, ew.s2,
+                         ew.g2, 0)
+    ops.moe_combine(out, y, pos, w, shared, 1.0)
+    launch_count.add(8)  # count, offsets, scatter, 2x(tiles + GEMM), silu, combine
+    return out
+
+
+def make_route_for_runner(runner):
+    """U3 provider hook: this library routes only its own MoE layers; vLLM's
+    upstream ``MoERunner`` objects keep upstream routing."""
+    if getattr(runner, "b200_route", None) is not None:
+        return runner.b200_route
+    return None
