@@ -1,0 +1,79 @@
+"""Gated-DeltaNet kernels vs the fp32 torch oracle: causal conv1d with
+rolling state (prefill then decode continues exactly), the gated delta rule
+(varlen prefill; decode steps continuing the state; slot < 0 = no state),
+gated RMSNorm."""
+import pytest
+import torch
+
+from vllm_sm70_b200.ops import gdn
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6))
+
+
+def test_conv1d_prefill_then_decode(b200_ops):
+    torch.manual_seed(0)
+    C, W = 256, 4
+    lens = [5, 1, 17]
+    T = sum(lens)
+    x = torch.randn(T, C, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(C, W, device="cuda", dtype=torch.bfloat16) * 0.5
+    cu = torch.tensor([0, 5, 6, 23], device="cuda", dtype=torch.int32)
+    slots = torch.tensor([2, 0, 1], device="cuda", dtype=torch.int32)
+    st = torch.randn(4, C, W - 1, device="cuda")
+    st_ref = st.clone()
+    y = gdn.causal_conv1d(x, w, None, st, cu, slots)
+    yr = gdn.causal_conv1d_ref(x, w, None, st_ref, cu, slots)
+    assert _rel(y, yr) < 1e-2
+    assert torch.allclose(st, st_ref)
+    # one decode token per sequence continues the state
+    x2 = torch.randn(3, C, device="cuda", dtype=torch.bfloat16)
+    cu2 = torch.arange(4, device="cuda", dtype=torch.int32)
+    y2 = gdn.causal_conv1d(x2, w, None, st, cu2, slots)
+    y2r = gdn.causal_conv1d_ref(x2, w, None, st_ref, cu2, slots)
+    assert _rel(y2, y2r) < 1e-2
+
+
+@pytest.mark.parametrize("HK,HV,D", [(2, 4, 128), (1, 1, 64)])
+def test_gdn_recurrent_prefill_and_decode(b200_ops, HK, HV, D):
+    torch.manual_seed(1)
+    lens = [7, 30, 1]
+    T = sum(lens)
+    cu = torch.tensor([0, 7, 37, 38], device="cuda", dtype=torch.int32)
+    slots = torch.tensor([1, -1, 0], device="cuda", dtype=torch.int32)
+
+    def inputs(T):
+        return (torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16),
+                torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16),
+                torch.randn(T, HV * D, device="cuda", dtype=torch.bfloat16),
+                torch.randn(T, HV, device="cuda", dtype=torch.bfloat16),
+                torch.randn(T, HV, device="cuda", dtype=torch.bfloat16))
+
+    A_log = torch.randn(HV, device="cuda") * 0.5
+    dt = torch.randn(HV, device="cuda") * 0.5
+    st = torch.randn(2, HV, D, D, device="cuda") * 0.1
+    st_ref = st.clone()
+    q, k, v, a, b = inputs(T)
+    o = gdn.gdn_recurrent(q, k, v, a, b, A_log, dt, st, cu, slots, HK, HV)
+    orf = gdn.gdn_recurrent_ref(q, k, v, a, b, A_log, dt, st_ref, cu, slots, HK, HV)
+    assert _rel(o, orf) < 2e-2
+    assert torch.allclose(st, st_ref, atol=1e-3, rtol=1e-3)
+    for _ in range(3):  # decode continues from the stored states
+        cu1 = torch.arange(4, device="cuda", dtype=torch.int32)
+        q, k, v, a, b = inputs(3)
+        o = gdn.gdn_recurrent(q, k, v, a, b, A_log, dt, st, cu1, slots, HK, HV)
+        orf = gdn.gdn_recurrent_ref(q, k, v, a, b, A_log, dt, st_ref, cu1, slots, HK, HV)
+        assert _rel(o, orf) < 2e-2
+
+
+def test_gated_rmsnorm(b200_ops):
+    torch.manual_seed(2)
+    o = torch.randn(9, 4 * 128, device="cuda", dtype=torch.bfloat16)
+    z = torch.randn(9, 4 * 128, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(128, device="cuda", dtype=torch.bfloat16)
+    ref = gdn.gated_rmsnorm_ref(o, z, w, 4, 1e-6)
+    gdn.gated_rmsnorm(o, z, w, 4, 1e-6)
+    assert _rel(o, ref) < 2e-2

@@ -11,6 +11,8 @@
 #include "ops_api.h"
 #include "comm/comm_api.h"
 #include "moe/moe_api.h"
+#include "sampler/sampler_api.h"
+#include "gdn/gdn_api.h"
 
 namespace b200 {
 namespace {
@@ -239,6 +241,102 @@ void gemm_grouped_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w_
                       device_status_ptr(x.get_device()), cur_stream());
 }
 
+void gumbel_argmax(at::Tensor& ids, at::Tensor& vals, const at::Tensor& logits,
+                   const at::Tensor& temperature, const at::Tensor& seeds, int64_t offset,
+                   int64_t id_offset) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "gumbel_argmax: 2-D logits");
+  const bool bf = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf || logits.scalar_type() == at::kFloat, "gumbel_argmax: bf16/fp32 logits");
+  TORCH_CHECK(temperature.scalar_type() == at::kFloat && seeds.scalar_type() == at::kLong,
+              "gumbel_argmax: fp32 temperature, int64 seeds");
+  c10::cuda::CUDAGuard g(logits.device());
+  gumbel_argmax_launch(logits.data_ptr(), bf, (int)logits.size(0), (int)logits.size(1),
+                       (int)logits.stride(0), temperature.data_ptr<float>(),
+                       seeds.data_ptr<int64_t>(), (uint64_t)offset, (int)id_offset,
+                       ids.data_ptr<int>(), vals.data_ptr<float>(), cur_stream());
+}
+
+void topk_candidates(at::Tensor& vals, at::Tensor& ids, const at::Tensor& logits, int64_t K,
+                     int64_t id_offset) {
+  CHECK_CUDA(logits);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "topk_candidates: 2-D logits");
+  const bool bf = logits.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf || logits.scalar_type() == at::kFloat, "topk_candidates: bf16/fp32 logits");
+  TORCH_CHECK(vals.numel() >= logits.size(0) * K && ids.numel() >= logits.size(0) * K,
+              "topk_candidates: outputs");
+  c10::cuda::CUDAGuard g(logits.device());
+  topk_candidates_launch(logits.data_ptr(), bf, (int)logits.size(0), (int)logits.size(1),
+                         (int)logits.stride(0), (int)K, (int)id_offset, vals.data_ptr<float>(),
+                         ids.data_ptr<int>(), cur_stream());
+}
+
+void sample_candidates(at::Tensor& out, const at::Tensor& cand_v, const at::Tensor& cand_i,
+                       const at::Tensor& temperature, const at::Tensor& top_k,
+                       const at::Tensor& top_p, const at::Tensor& seeds, int64_t offset) {
+  CHECK_CUDA(cand_v);
+  TORCH_CHECK(cand_v.dim() == 2 && cand_v.is_contiguous() && cand_i.is_contiguous(),
+              "sample_candidates: [rows, C]");
+  c10::cuda::CUDAGuard g(cand_v.device());
+  sample_candidates_launch(cand_v.data_ptr<float>(), cand_i.data_ptr<int>(), (int)cand_v.size(0),
+                           (int)cand_v.size(1), temperature.data_ptr<float>(),
+                           top_k.data_ptr<int>(), top_p.data_ptr<float>(),
+                           seeds.data_ptr<int64_t>(), (uint64_t)offset, out.data_ptr<int>(),
+                           cur_stream());
+}
+
+void causal_conv1d(at::Tensor& y, const at::Tensor& x, const at::Tensor& w,
+                   const c10::optional<at::Tensor>& bias, at::Tensor& state, const at::Tensor& cu,
+                   const at::Tensor& slots, bool silu) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(y); CHECK_BF16(w);
+  TORCH_CHECK(x.stride(1) == 1 && y.stride(1) == 1 && w.is_contiguous() && w.dim() == 2,
+              "causal_conv1d: layouts");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 3 &&
+                  state.size(1) == x.size(1) && state.size(2) == w.size(1) - 1,
+              "causal_conv1d: state [slots, C, W-1] fp32");
+  TORCH_CHECK(cu.scalar_type() == at::kInt && slots.scalar_type() == at::kInt, "int32 metadata");
+  c10::cuda::CUDAGuard g(x.device());
+  causal_conv1d_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr(),
+                       bias ? bias->data_ptr() : nullptr, y.data_ptr(), (int)y.stride(0),
+                       state.data_ptr<float>(), cu.data_ptr<int>(), slots.data_ptr<int>(),
+                       (int)slots.numel(), (int)x.size(1), (int)w.size(1), silu, cur_stream());
+}
+
+void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                   const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
+                   const at::Tensor& dt_bias, at::Tensor& state, const at::Tensor& cu,
+                   const at::Tensor& slots, int64_t HK, int64_t HV, bool reset_state) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(a); CHECK_BF16(b);
+  CHECK_BF16(o);
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
+              "gdn: fp32 A_log / dt_bias");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4,
+              "gdn: state [slots, HV, DV, DK] fp32");
+  const int DK = (int)(q.size(1) / HK), DV = (int)(v.size(1) / HV);
+  TORCH_CHECK(state.size(1) == HV && state.size(2) == DV && state.size(3) == DK, "gdn: state dims");
+  TORCH_CHECK(a.stride(0) == b.stride(0) && a.stride(1) == 1 && b.stride(1) == 1, "gdn: a/b layout");
+  GdnParams p{};
+  p.q = (const __nv_bfloat16*)q.data_ptr(); p.k = (const __nv_bfloat16*)k.data_ptr();
+  p.v = (const __nv_bfloat16*)v.data_ptr(); p.a = (const __nv_bfloat16*)a.data_ptr();
+  p.b = (const __nv_bfloat16*)b.data_ptr(); p.A_log = A_log.data_ptr<float>();
+  p.dt_bias = dt_bias.data_ptr<float>(); p.o = (__nv_bfloat16*)o.data_ptr();
+  p.state = state.data_ptr<float>(); p.cu = cu.data_ptr<int>(); p.slots = slots.data_ptr<int>();
+  p.ldq = (int)q.stride(0); p.ldk = (int)k.stride(0); p.ldv = (int)v.stride(0);
+  p.ldab = (int)a.stride(0); p.ldo = (int)o.stride(0);
+  p.HK = (int)HK; p.HV = (int)HV; p.reset_state = reset_state ? 1 : 0;
+  c10::cuda::CUDAGuard g(q.device());
+  gdn_recurrent_launch(p, (int)slots.numel(), DK, DV, cur_stream());
+}
+
+void gated_rmsnorm(at::Tensor& o, const at::Tensor& z, const at::Tensor& w, int64_t H, double eps) {
+  CHECK_CUDA(o); CHECK_BF16(o); CHECK_BF16(z); CHECK_BF16(w);
+  const int D = (int)w.numel();
+  TORCH_CHECK(o.size(1) == H * D && o.stride(1) == 1 && z.stride(1) == 1, "gated_rmsnorm: layout");
+  c10::cuda::CUDAGuard g(o.device());
+  gated_rmsnorm_launch(o.data_ptr(), (int)o.stride(0), z.data_ptr(), (int)z.stride(0),
+                       w.data_ptr(), (int)o.size(0), (int)H, D, (float)eps, cur_stream());
+}
+
 void rms_norm(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, double eps) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(out);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "rms_norm: 2-D rows");
@@ -464,6 +562,17 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("moe_combine(Tensor(a!) out, Tensor y, Tensor pos, Tensor w, Tensor? shared, float shared_scale) -> ()");
   m.def("gemm_grouped_out(Tensor(a!) out, Tensor x, Tensor w_stk, int E, int N, Tensor row_off, "
         "Tensor(b!) tile_off, int fmt, Tensor? scales, float out_scale, int bn=0) -> ()");
+  m.def("gumbel_argmax(Tensor(a!) ids, Tensor(b!) vals, Tensor logits, Tensor temperature, "
+        "Tensor seeds, int offset, int id_offset) -> ()");
+  m.def("topk_candidates(Tensor(a!) vals, Tensor(b!) ids, Tensor logits, int K, int id_offset) -> ()");
+  m.def("sample_candidates(Tensor(a!) out, Tensor cand_v, Tensor cand_i, Tensor temperature, "
+        "Tensor top_k, Tensor top_p, Tensor seeds, int offset) -> ()");
+  m.def("causal_conv1d(Tensor(a!) y, Tensor x, Tensor w, Tensor? bias, Tensor(b!) state, "
+        "Tensor cu, Tensor slots, bool silu) -> ()");
+  m.def("gdn_recurrent(Tensor(a!) o, Tensor q, Tensor k, Tensor v, Tensor a, Tensor b, "
+        "Tensor A_log, Tensor dt_bias, Tensor(b!) state, Tensor cu, Tensor slots, int HK, int HV, "
+        "bool reset_state) -> ()");
+  m.def("gated_rmsnorm(Tensor(a!) o, Tensor z, Tensor w, int H, float eps) -> ()");
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
   m.def("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()");
   m.def(
@@ -487,6 +596,12 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("gemm_bf16_out", &b200::gemm_bf16_out);
   m.impl("gemm_bf16_silu_mul_out", &b200::gemm_bf16_silu_mul_out);
   m.impl("rms_norm", &b200::rms_norm);
+  m.impl("causal_conv1d", &b200::causal_conv1d);
+  m.impl("gdn_recurrent", &b200::gdn_recurrent);
+  m.impl("gated_rmsnorm", &b200::gated_rmsnorm);
+  m.impl("gumbel_argmax", &b200::gumbel_argmax);
+  m.impl("topk_candidates", &b200::topk_candidates);
+  m.impl("sample_candidates", &b200::sample_candidates);
   m.impl("moe_topk", &b200::moe_topk);
   m.impl("moe_permute", &b200::moe_permute);
   m.impl("moe_combine", &b200::moe_combine);

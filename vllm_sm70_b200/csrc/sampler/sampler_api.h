@@ -1,0 +1,18 @@
+// Host API of the sampling kernels (sample.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace b200 {
+
+void gumbel_argmax_launch(const void* logits, bool bf16, int rows, int V, int ld,
+                          const float* temperature, const int64_t* seeds, uint64_t offset,
+                          int id_offset, int* ids, float* vals, cudaStream_t stream);
+void topk_candidates_launch(const void* logits, bool bf16, int rows, int V, int ld, int K,
+                            int id_offset, float* out_v, int* out_i, cudaStream_t stream);
+void sample_candidates_launch(const float* cand_v, const int* cand_i, int rows, int C,
+                              const float* temperature, const int* top_k, const float* top_p,
+                              const int64_t* seeds, uint64_t offset, int* out,
+                              cudaStream_t stream);
+
+}  // namespace b200

@@ -60,3 +60,46 @@ def merge_rank_top1(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
     cand = torch.where((vm == mx[None]) & ~nan, ids.to(torch.int64), torch.iinfo(torch.int64).max)
     pick = cand.min(0).values
     return torch.where(any_nan, nan_pick, pick).to(torch.int32)
+
+
+# ------------------------------------------------------------------ random sampling
+def gumbel_sample(logits: torch.Tensor, temperature: torch.Tensor, seeds: torch.Tensor,
+                  offset: int, id_offset: int = 0):
+    """Exact sample from softmax(logits / T) per row (Gumbel-max with Philox
+    noise keyed by (seed, global token id)); T <= 0 rows are greedy. Returns
+    (ids int32, perturbed max value) so vocab shards merge with
+    :func:`merge_rank_top1`."""
+    rows = logits.shape[0]
+    ids = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    vals = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    _ext.require()
+    torch.ops._b200_C.gumbel_argmax(ids, vals, logits, temperature, seeds, offset, id_offset)
+    launch_count.add(1)
+    return ids, vals
+
+
+def topk_candidates(logits: torch.Tensor, K: int, id_offset: int = 0):
+    """Per-row top-K (value desc, id asc) of a logit shard: (vals fp32, ids int32)."""
+    rows = logits.shape[0]
+    if not logits.is_cuda:
+        x = logits.float().nan_to_num(nan=float("-inf"))
+        order = torch.sort(-x, dim=-1, stable=True).indices[:, :K]
+        return torch.gather(x, 1, order), (order + id_offset).to(torch.int32)
+    vals = torch.empty(rows, K, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(rows, K, dtype=torch.int32, device=logits.device)
+    _ext.require()
+    torch.ops._b200_C.topk_candidates(vals, ids, logits, K, id_offset)
+    launch_count.add(1)
+    return vals, ids
+
+
+def sample_candidates(cand_v: torch.Tensor, cand_i: torch.Tensor, temperature: torch.Tensor,
+                      top_k: torch.Tensor, top_p: torch.Tensor, seeds: torch.Tensor,
+                      offset: int) -> torch.Tensor:
+    """Temperature / top-k / top-p sampling over merged candidate sets."""
+    out = torch.empty(cand_v.shape[0], dtype=torch.int32, device=cand_v.device)
+    _ext.require()
+    torch.ops._b200_C.sample_candidates(out, cand_v.contiguous(), cand_i.contiguous(),
+                                        temperature, top_k, top_p, seeds, offset)
+    launch_count.add(1)
+    return out
