@@ -68,3 +68,23 @@ def test_qwen3_moe_tiny_generates_and_is_batch_invariant():
     both = llm.generate(prompts, SamplingParams(max_tokens=5))
     solo = [llm.generate([p], SamplingParams(max_tokens=5))[0] for p in prompts]
     assert [o.output_token_ids for o in both] == [o.output_token_ids for o in solo]
+
+
+def test_qwen3_next_tiny_hybrid_generates_batch_invariant():
+    from vllm_sm70_b200.models.config import ModelConfig
+
+    cfg = ModelConfig(arch="qwen3_next", hidden_size=128, num_layers=4, num_heads=4,
+                      num_kv_heads=2, head_dim=64, intermediate_size=256, vocab_size=512,
+                      rope_theta=10000.0, rms_eps=1e-6, max_position=512, qk_norm=True,
+                      num_experts=8, top_k=2, moe_intermediate_size=64,
+                      shared_expert_intermediate_size=64,
+                      layer_types=("linear_attention",) * 3 + ("attention",),
+                      linear_num_k_heads=2, linear_num_v_heads=4, linear_k_head_dim=64,
+                      linear_v_head_dim=64, attn_output_gate=True, partial_rotary_factor=0.25)
+    llm = LLM(cfg, max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=24)
+    g = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (9, 30)]
+    both = llm.generate(prompts, SamplingParams(max_tokens=4))
+    solo = [llm.generate([p], SamplingParams(max_tokens=4))[0] for p in prompts]
+    assert [o.output_token_ids for o in both] == [o.output_token_ids for o in solo]

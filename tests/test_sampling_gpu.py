@@ -73,3 +73,44 @@ def test_sample_candidates_topk_topp_greedy(b200_ops):
     t.fill_(0.0)
     out = sampling.sample_candidates(v, i, t, k, p, seeds, 2)
     assert int(out.max()) == 0
+
+
+def test_rejection_sampler_preserves_target_distribution(b200_ops):
+    """With drafts sampled from q, the emitted first token must follow p
+    exactly (the defining property of speculative sampling)."""
+    V, rows, k = 6, 30000, 1
+    torch.manual_seed(4)
+    tl = torch.tensor([1.0, 0.2, -0.5, 2.0, 0.0, -1.0])
+    dl = torch.tensor([0.0, 1.5, 0.3, -0.2, 1.0, 0.5])
+    T = 0.8
+    p = torch.softmax(tl / T, -1)
+    q = torch.softmax(dl / T, -1)
+    drafts = torch.multinomial(q, rows, replacement=True).view(rows, 1).to(torch.int32).cuda()
+    tgt = tl.to(torch.bfloat16).expand(rows, k + 1, V).contiguous().cuda()
+    drf = dl.to(torch.bfloat16).expand(rows, k, V).contiguous().cuda()
+    temp = torch.full((rows,), T, device="cuda")
+    seeds = torch.arange(rows, device="cuda", dtype=torch.int64) * 7 + 1
+    out, n = sampling.rejection_sample(tgt, drf, drafts, temp, seeds, 0)
+    first = out[:, 0].long().cpu()
+    assert int(first.min()) >= 0
+    pb = torch.softmax(tl.to(torch.bfloat16).float() / T, -1)
+    counts = torch.bincount(first, minlength=V).float()
+    chi2 = float(((counts - rows * pb) ** 2 / (rows * pb)).sum())
+    assert chi2 < 30.0, (chi2, counts / rows, pb)
+    acc = (n.cpu() == 2).float().mean()
+    expect = float(torch.minimum(p, q).sum())  # acceptance rate of one draft
+    assert abs(float(acc) - expect) < 0.02
+
+
+def test_rejection_greedy(b200_ops):
+    V, k = 50, 3
+    tgt = torch.randn(4, k + 1, V, device="cuda").to(torch.bfloat16)
+    am = tgt.float().argmax(-1).to(torch.int32)
+    drafts = am[:, :k].clone()
+    drafts[1, 1] = (drafts[1, 1] + 1) % V  # row 1 rejects at position 1
+    temp = torch.zeros(4, device="cuda")
+    seeds = torch.zeros(4, device="cuda", dtype=torch.int64)
+    out, n = sampling.rejection_sample(tgt, tgt[:, :k].contiguous(), drafts, temp, seeds, 0)
+    assert n.tolist() == [4, 2, 4, 4]
+    assert out[0].tolist() == am[0].tolist()
+    assert out[1, :2].tolist() == am[1, :2].tolist() and out[1, 2:].tolist() == [-1, -1]

@@ -337,6 +337,24 @@ void gated_rmsnorm(at::Tensor& o, const at::Tensor& z, const at::Tensor& w, int6
                        w.data_ptr(), (int)o.size(0), (int)H, D, (float)eps, cur_stream());
 }
 
+void rejection_sample(at::Tensor& out_tokens, at::Tensor& num_out, const at::Tensor& target_logits,
+                      const at::Tensor& draft_logits, const at::Tensor& draft_ids,
+                      const at::Tensor& temperature, const at::Tensor& seeds, int64_t offset) {
+  CHECK_CUDA(target_logits); CHECK_BF16(target_logits); CHECK_BF16(draft_logits);
+  TORCH_CHECK(target_logits.dim() == 3 && draft_logits.dim() == 3 && target_logits.is_contiguous() &&
+                  draft_logits.is_contiguous(), "rejection_sample: [rows, k(+1), V] contiguous");
+  const int rows = (int)draft_ids.size(0), k = (int)draft_ids.size(1);
+  const int V = (int)target_logits.size(2);
+  TORCH_CHECK(target_logits.size(1) == k + 1 && draft_logits.size(1) == k &&
+                  draft_logits.size(2) == V, "rejection_sample: shapes");
+  TORCH_CHECK(draft_ids.scalar_type() == at::kInt && draft_ids.is_contiguous(), "draft ids int32");
+  c10::cuda::CUDAGuard g(target_logits.device());
+  rejection_sample_launch(target_logits.data_ptr(), draft_logits.data_ptr(),
+                          draft_ids.data_ptr<int>(), rows, k, V, temperature.data_ptr<float>(),
+                          seeds.data_ptr<int64_t>(), (uint64_t)offset, out_tokens.data_ptr<int>(),
+                          num_out.data_ptr<int>(), cur_stream());
+}
+
 void rms_norm(at::Tensor& out, const at::Tensor& x, const at::Tensor& w, double eps) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(w); CHECK_BF16(out);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "rms_norm: 2-D rows");
@@ -573,6 +591,8 @@ TORCH_LIBRARY(_b200_C, m) {
         "Tensor A_log, Tensor dt_bias, Tensor(b!) state, Tensor cu, Tensor slots, int HK, int HV, "
         "bool reset_state) -> ()");
   m.def("gated_rmsnorm(Tensor(a!) o, Tensor z, Tensor w, int H, float eps) -> ()");
+  m.def("rejection_sample(Tensor(a!) out_tokens, Tensor(b!) num_out, Tensor target_logits, "
+        "Tensor draft_logits, Tensor draft_ids, Tensor temperature, Tensor seeds, int offset) -> ()");
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor w, float eps) -> ()");
   m.def("fused_add_rms_norm(Tensor(a!) x, Tensor(b!) residual, Tensor w, float eps) -> ()");
   m.def(
@@ -596,6 +616,7 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("gemm_bf16_out", &b200::gemm_bf16_out);
   m.impl("gemm_bf16_silu_mul_out", &b200::gemm_bf16_silu_mul_out);
   m.impl("rms_norm", &b200::rms_norm);
+  m.impl("rejection_sample", &b200::rejection_sample);
   m.impl("causal_conv1d", &b200::causal_conv1d);
   m.impl("gdn_recurrent", &b200::gdn_recurrent);
   m.impl("gated_rmsnorm", &b200::gated_rmsnorm);

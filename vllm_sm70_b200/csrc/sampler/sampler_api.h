@@ -15,4 +15,12 @@ void sample_candidates_launch(const float* cand_v, const int* cand_i, int rows, 
                               const int64_t* seeds, uint64_t offset, int* out,
                               cudaStream_t stream);
 
+// Speculative-decoding verification: target logits [rows, k+1, V], draft
+// logits [rows, k, V] (bf16), draft ids [rows, k] -> out_tokens [rows, k+1],
+// num_out [rows].
+void rejection_sample_launch(const void* target_logits, const void* draft_logits,
+                             const int* draft_ids, int rows, int k, int V, const float* temperature,
+                             const int64_t* seeds, uint64_t offset, int* out_tokens, int* num_out,
+                             cudaStream_t stream);
+
 }  // namespace b200

@@ -63,6 +63,11 @@ class ModelRunner:
         self.row_base = torch.arange(B, dtype=torch.int64, device=dev) * self.out_cap
         self.bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32).pin_memory() \
             if dev.type == "cuda" else torch.zeros(B, self.max_blocks, dtype=torch.int32)
+        self.slot_ids = torch.arange(B, dtype=torch.int32, device=dev)
+        if hasattr(model, "allocate_states"):
+            model.allocate_states(B)
+        if hasattr(model, "reserve_workspace"):
+            model.reserve_workspace(B)
         self.use_graphs = use_graphs and dev.type == "cuda" and envs.get("VLLM_B200_CUDA_GRAPHS")
         self.capture_sizes = default_capture_sizes(B)
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
@@ -103,7 +108,7 @@ class ModelRunner:
         ns, po, pml = self._split_buffers(b)
         meta = AttnMeta(positions=pos, slot_mapping=slots, block_table=bt, seq_lens=sl,
                         cu_q=self.cu_q[: b + 1], max_q_len=1, decode=True, num_splits=ns,
-                        part_o=po, part_ml=pml)
+                        part_o=po, part_ml=pml, state_slots=self.slot_ids[:b])
         h = self.model.forward(self.ids[:b], meta, self.kv)
         nxt = self.model.greedy(h)
         self.ids[:b].copy_(nxt)
@@ -181,9 +186,13 @@ class ModelRunner:
             return (t.pin_memory() if pin else t).to(dev, non_blocking=True)
 
         ids_d = h2d(toks)
+        state_slots = h2d(torch.tensor(slots_idx, dtype=torch.int32))
+        fresh = [p[0] for p in pieces if p[2] == 0]
+        if fresh and hasattr(self.model, "reset_slots"):
+            self.model.reset_slots(h2d(torch.tensor(fresh, dtype=torch.int64)))
         meta = AttnMeta(positions=h2d(pos), slot_mapping=h2d(slot_map),
                         block_table=h2d(bt_rows), seq_lens=h2d(seq_lens), cu_q=h2d(cu),
-                        max_q_len=int(q_len.max()), decode=False)
+                        max_q_len=int(q_len.max()), decode=False, state_slots=state_slots)
         h = self.model.forward(ids_d, meta, self.kv)
         last = [i for i, p in enumerate(pieces) if p[3]]
         if not last:

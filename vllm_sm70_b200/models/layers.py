@@ -66,6 +66,7 @@ class AttnMeta:
     part_o: torch.Tensor | None = None
     part_ml: torch.Tensor | None = None
     last_token_idx: torch.Tensor | None = None  # [S] int64 rows whose logits are needed
+    state_slots: torch.Tensor | None = None     # [S] int32 recurrent-state slot per sequence
 
 
 @dataclass

@@ -1,0 +1,177 @@
+"""Qwen3-Next hybrid: 3:1 gated-DeltaNet linear-attention : gated full-
+attention layers, a 512-expert top-10 MoE with a gated shared expert, zero-
+centred RMSNorms, and a 1-layer MTP head for speculative decoding.
+
+Full-attention layer: ``q_proj`` emits [q | gate] per head (D each); q/k
+RMSNorm; partial RoPE (``partial_rotary_factor`` of the head dim); paged
+attention; ``out = attn * sigmoid(gate)``; ``o_proj``.
+Linear-attention layer (gated DeltaNet): ``in_proj_qkvz`` -> q, k (HK x DK),
+v, z (HV x DV); ``in_proj_ba`` -> b, a (HV); causal conv1d + SiLU over
+[q | k | v]; the gated delta rule with a per-sequence fp32 state; gated
+RMSNorm with z; ``out_proj``.
+
+Parallelism: attention heads, GDN heads and the shared expert are tensor-
+parallel; routed experts are expert-parallel over the same group (see
+``models/qwen3_moe.py``). KV cache exists only for the full-attention layers;
+the GDN conv / recurrent states live in per-batch-slot buffers.
+
+Reference parity: the Qwen GDN layer and hybrid model served by the
+reference (``sm70/vllm_sm70/gdn/layer.py:42-164``, upstream Qwen3-Next), and
+its DFlash2 draft for speculative decoding (replaced by the MTP head,
+``models/mtp.py``).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+from ..ops import gdn as gdn_ops
+from ..parallel import comm, state as pstate
+from ..utils import launch_count
+from .layers import AttnMeta, KVCache
+from .qwen3_moe import Qwen3MoeModel
+
+
+class Qwen3NextModel(Qwen3MoeModel):
+    def __init__(self, cfg, device, dtype=torch.bfloat16, ps=None):
+        super().__init__(cfg, device, dtype, ps)
+        tp = self.ps.tp_size
+        self.layer_types = list(cfg.layer_types) or [
+            "attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(cfg.num_layers)]
+        self.attn_layer_ids = [i for i, t in enumerate(self.layer_types) if t == "attention"]
+        self.HK = cfg.linear_num_k_heads // tp
+        self.HV = cfg.linear_num_v_heads // tp
+        self.DK = cfg.linear_k_head_dim
+        self.DV = cfg.linear_v_head_dim
+        self.conv_dim = 2 * self.HK * self.DK + self.HV * self.DV
+        self.conv_w = cfg.linear_conv_kernel
+        self.rot = int(self.d * cfg.partial_rotary_factor)
+        self.gdn_state = None
+        self.conv_state = None
+        self.max_slots = 0
+
+    # ------------------------------------------------------------------ state
+    def allocate_states(self, max_slots: int) -> None:
+        """Per-batch-slot GDN states: recurrent [L, slots, HV, DV, DK] fp32,
+        conv [L, slots, conv_dim, W-1] fp32."""
+        n_lin = sum(1 for t in self.layer_types if t == "linear_attention")
+        self.max_slots = max_slots
+        self.gdn_state = torch.zeros(n_lin, max_slots, self.HV, self.DV, self.DK,
+                                     dtype=torch.float32, device=self.device)
+        self.conv_state = torch.zeros(n_lin, max_slots, self.conv_dim, self.conv_w - 1,
+                                      dtype=torch.float32, device=self.device)
+
+    def reset_slots(self, slots: torch.Tensor) -> None:
+        if self.gdn_state is not None and slots.numel():
+            self.gdn_state.index_fill_(1, slots, 0.0)
+            self.conv_state.index_fill_(1, slots, 0.0)
+
+    # ------------------------------------------------------------------ weights
+    def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
+        cfg, dev, dt = self.cfg, self.device, self.dtype
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 7919 + self.ps.tp_rank)
+
+        def rnd(*shape):
+            return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std
+
+        h = cfg.hidden_size
+        self.embed = rnd(self.vocab_local, h).to(dt)
+        self.lm_head = self.embed if cfg.tie_embeddings else rnd(self.vocab_local, h).to(dt)
+        # zero-centred norms: effective weight = 1 + w (w = 0 at init)
+        self.final_norm = torch.ones(h, device=dev, dtype=dt)
+        self.layers = []
+        for li, kind in enumerate(self.layer_types):
+            L = {"kind": kind, "in_norm": torch.ones(h, device=dev, dtype=dt),
+                 "post_norm": torch.ones(h, device=dev, dtype=dt)}
+            if kind == "attention":
+                qkv_out = (2 * self.hq + 2 * self.hkv) * self.d  # [q | gate] per head, k, v
+                L["qkv"] = self.make_linear(rnd(qkv_out, h))
+                L["o"] = self.make_linear(rnd(h, self.hq * self.d))
+                L["q_norm"] = torch.ones(self.d, device=dev, dtype=dt)
+                L["k_norm"] = torch.ones(self.d, device=dev, dtype=dt)
+            else:
+                qkvz = 2 * self.HK * self.DK + 2 * self.HV * self.DV
+                L["qkvz"] = self.make_linear(rnd(qkvz, h))
+                L["ba_w"] = rnd(2 * self.HV, h).to(dt)  # tiny: kept bf16
+                L["conv_w"] = (rnd(self.conv_dim, self.conv_w) * 10).to(dt)
+                L["A_log"] = torch.log(torch.rand(self.HV, generator=g, device=dev) * 15 + 1)
+                L["dt_bias"] = torch.ones(self.HV, device=dev)
+                L["gnorm"] = torch.ones(self.DV, device=dev, dtype=dt)
+                L["out"] = self.make_linear(rnd(h, self.HV * self.DV))
+            L.update(self.init_mlp_dummy(rnd))
+            self.layers.append(L)
+        self._init_rope()
+
+    def _init_rope(self) -> None:
+        self.cos_sin = ops.attention.rope_cos_sin(self.rot, self.cfg.max_position,
+                                                  self.cfg.rope_theta, self.cfg.rope_scaling,
+                                                  device=self.device)
+
+    # ------------------------------------------------------------------ forward
+    def _attention(self, li, L, x, meta: AttnMeta, kv: KVCache, T):
+        d, hq, hkv = self.d, self.hq, self.hkv
+        qkvg = L["qkv"].forward(x)                          # [T, (2hq + 2hkv) d]
+        qg = qkvg[:, : 2 * hq * d].view(T, hq, 2, d)
+        gate = qg[:, :, 1]
+        # contiguous [q | k | v] for the fused RoPE + KV writer
+        qkv = torch.cat([qg[:, :, 0].reshape(T, hq * d), qkvg[:, 2 * hq * d:]], 1).contiguous()
+        ops.rope_kv_write(qkv, meta.positions, self.cos_sin, kv.k[li], kv.v[li],
+                          meta.slot_mapping, hq, hkv, L["q_norm"], L["k_norm"], self.cfg.rms_eps)
+        q = qkv.view(T, hq + 2 * hkv, d)[:, :hq]
+        attn = torch.empty(T, hq, d, device=x.device, dtype=self.dtype)
+        ops.paged_attention(attn, q, kv.k[li], kv.v[li], meta.block_table, meta.seq_lens,
+                            meta.cu_q, meta.max_q_len, self.scale, 0, None, meta.decode,
+                            meta.num_splits, meta.part_o, meta.part_ml)
+        attn = (attn.float() * torch.sigmoid(gate.float())).to(self.dtype)
+        return L["o"].forward(attn.view(T, hq * d), out=comm.row_parallel_out(T, x.shape[1]))
+
+    def _linear_attention(self, li, L, x, meta: AttnMeta, T):
+        HK, HV, DK, DV = self.HK, self.HV, self.DK, self.DV
+        lin_idx = sum(1 for t in self.layer_types[:li] if t == "linear_attention")
+        qkvz = L["qkvz"].forward(x)                         # [T, 2HK DK + 2HV DV]
+        mixed = qkvz[:, : self.conv_dim]
+        z = qkvz[:, self.conv_dim:]
+        ba = ops.gemm(x, L["ba_w"]) if x.is_cuda else (x.float() @ L["ba_w"].float().t()).to(x.dtype)
+        b, a = ba[:, :HV], ba[:, HV:]
+        conv_out = torch.empty(T, self.conv_dim, device=x.device, dtype=self.dtype)
+        slots = meta.state_slots
+        gdn_ops.causal_conv1d(mixed, L["conv_w"], None, self.conv_state[lin_idx], meta.cu_q,
+                              slots, True, out=conv_out)
+        q = conv_out[:, : HK * DK]
+        k = conv_out[:, HK * DK: 2 * HK * DK]
+        v = conv_out[:, 2 * HK * DK:]
+        o = gdn_ops.gdn_recurrent(q, k, v, a, b, L["A_log"], L["dt_bias"],
+                                  self.gdn_state[lin_idx], meta.cu_q, slots, HK, HV)
+        gdn_ops.gated_rmsnorm(o, z, L["gnorm"], HV, self.cfg.rms_eps)
+        return L["out"].forward(o, out=comm.row_parallel_out(T, x.shape[1]))
+
+    def forward(self, ids: torch.Tensor, meta: AttnMeta, kv: KVCache) -> torch.Tensor:
+        eps = self.cfg.rms_eps
+        T = ids.shape[0]
+        H = self.cfg.hidden_size
+        residual = comm.adopt_residual(self.embed_tokens(ids))
+        x = ops.rms_norm(residual, self.layers[0]["in_norm"], eps)
+        for li, L in enumerate(self.layers):
+            if li > 0:
+                x, residual = comm.all_reduce_add_rms_norm(x, residual, L["in_norm"], eps)
+            if L["kind"] == "attention":
+                o = self._attention(li, L, x, meta, kv, T)
+            else:
+                o = self._linear_attention(li, L, x, meta, T)
+            x, residual = comm.all_reduce_add_rms_norm(o, residual, L["post_norm"], eps)
+            x = self.mlp(li, L, x, comm.row_parallel_out(T, H))
+        x, residual = comm.all_reduce_add_rms_norm(x, residual, self.final_norm, eps)
+        self.last_hidden = x
+        return x
+
+    def weight_bytes(self) -> int:
+        n = self.embed.numel() * 2 + (0 if self.cfg.tie_embeddings else self.lm_head.numel() * 2)
+        for L in self.layers:
+            for key in ("qkv", "o", "qkvz", "out"):
+                if key in L and L[key] is not None:
+                    n += L[key].weight_bytes()
+            n += L["experts"].bytes()
+        return n

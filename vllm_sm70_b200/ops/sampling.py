@@ -103,3 +103,20 @@ def sample_candidates(cand_v: torch.Tensor, cand_i: torch.Tensor, temperature: t
                                         temperature, top_k, top_p, seeds, offset)
     launch_count.add(1)
     return out
+
+
+def rejection_sample(target_logits: torch.Tensor, draft_logits: torch.Tensor,
+                     draft_ids: torch.Tensor, temperature: torch.Tensor, seeds: torch.Tensor,
+                     offset: int):
+    """Verify ``k`` draft tokens per row. Returns (out_tokens [rows, k+1] with
+    -1 padding, num_out [rows]) -- accepted drafts plus one corrected / bonus
+    token."""
+    rows, k = draft_ids.shape
+    out = torch.empty(rows, k + 1, dtype=torch.int32, device=draft_ids.device)
+    n = torch.empty(rows, dtype=torch.int32, device=draft_ids.device)
+    _ext.require()
+    torch.ops._b200_C.rejection_sample(out, n, target_logits.contiguous(),
+                                       draft_logits.contiguous(), draft_ids.contiguous(),
+                                       temperature, seeds, offset)
+    launch_count.add(1)
+    return out, n
