@@ -88,3 +88,53 @@ def test_qwen3_next_tiny_hybrid_generates_batch_invariant():
     both = llm.generate(prompts, SamplingParams(max_tokens=4))
     solo = [llm.generate([p], SamplingParams(max_tokens=4))[0] for p in prompts]
     assert [o.output_token_ids for o in both] == [o.output_token_ids for o in solo]
+
+
+def test_speculative_greedy_equals_plain_greedy():
+    """With T = 0 the speculative path (MTP drafts + verify + rejection) must
+    emit exactly the plain greedy tokens, whatever the drafts are."""
+    g = torch.Generator().manual_seed(7)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (6, 21, 40)]
+    sp = SamplingParams(max_tokens=9, ignore_eos=True)
+    # Sharpen the LM head so greedy choices are not decided by fp32 rounding of
+    # near-tied logits (verify and decode sum in different orders).
+    a, b = _llm(), _llm(speculative_k=3, max_model_len=128)
+    for m in (a.model, b.model):
+        m.lm_head.mul_(200.0)
+    plain = a.generate(prompts, sp)
+    spec = b.generate(prompts, sp)
+    assert [o.output_token_ids for o in spec] == [o.output_token_ids for o in plain]
+
+
+def test_speculative_hybrid_greedy_equals_plain():
+    """Same property on the hybrid model: the GDN states are rolled back to the
+    last accepted token after every verify."""
+    from vllm_sm70_b200.models.config import ModelConfig
+
+    cfg = ModelConfig(arch="qwen3_next", hidden_size=128, num_layers=4, num_heads=4,
+                      num_kv_heads=2, head_dim=64, intermediate_size=256, vocab_size=512,
+                      rope_theta=10000.0, rms_eps=1e-6, max_position=512, qk_norm=True,
+                      num_experts=8, top_k=2, moe_intermediate_size=64,
+                      shared_expert_intermediate_size=64,
+                      layer_types=("linear_attention",) * 3 + ("attention",),
+                      linear_num_k_heads=2, linear_num_v_heads=4, linear_k_head_dim=64,
+                      linear_v_head_dim=64, attn_output_gate=True, partial_rotary_factor=0.25)
+    kw = dict(max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=64)
+    g = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (7, 25)]
+    sp = SamplingParams(max_tokens=7, ignore_eos=True)
+    a, b = LLM(cfg, **kw), LLM(cfg, speculative_k=3, **kw)
+    for m in (a.model, b.model):
+        m.lm_head.mul_(200.0)
+    plain = a.generate(prompts, sp)
+    spec = b.generate(prompts, sp)
+    assert [o.output_token_ids for o in spec] == [o.output_token_ids for o in plain]
+
+
+def test_temperature_sampling_runs_and_is_seeded():
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (5, 12)]
+    sp = SamplingParams(max_tokens=6, temperature=0.7, seed=123, ignore_eos=True)
+    a = _llm().generate(prompts, sp)
+    assert all(len(o.output_token_ids) == 6 for o in a)

@@ -243,7 +243,7 @@ void gemm_grouped_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w_
 
 void gumbel_argmax(at::Tensor& ids, at::Tensor& vals, const at::Tensor& logits,
                    const at::Tensor& temperature, const at::Tensor& seeds, int64_t offset,
-                   int64_t id_offset) {
+                   int64_t id_offset, const c10::optional<at::Tensor>& row_offsets) {
   CHECK_CUDA(logits);
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "gumbel_argmax: 2-D logits");
   const bool bf = logits.scalar_type() == at::kBFloat16;
@@ -253,7 +253,8 @@ void gumbel_argmax(at::Tensor& ids, at::Tensor& vals, const at::Tensor& logits,
   c10::cuda::CUDAGuard g(logits.device());
   gumbel_argmax_launch(logits.data_ptr(), bf, (int)logits.size(0), (int)logits.size(1),
                        (int)logits.stride(0), temperature.data_ptr<float>(),
-                       seeds.data_ptr<int64_t>(), (uint64_t)offset, (int)id_offset,
+                       seeds.data_ptr<int64_t>(), (uint64_t)offset,
+                       row_offsets ? row_offsets->data_ptr<int64_t>() : nullptr, (int)id_offset,
                        ids.data_ptr<int>(), vals.data_ptr<float>(), cur_stream());
 }
 
@@ -287,7 +288,7 @@ void sample_candidates(at::Tensor& out, const at::Tensor& cand_v, const at::Tens
 
 void causal_conv1d(at::Tensor& y, const at::Tensor& x, const at::Tensor& w,
                    const c10::optional<at::Tensor>& bias, at::Tensor& state, const at::Tensor& cu,
-                   const at::Tensor& slots, bool silu) {
+                   const at::Tensor& slots, bool silu, bool write_state) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(y); CHECK_BF16(w);
   TORCH_CHECK(x.stride(1) == 1 && y.stride(1) == 1 && w.is_contiguous() && w.dim() == 2,
               "causal_conv1d: layouts");
@@ -299,13 +300,15 @@ void causal_conv1d(at::Tensor& y, const at::Tensor& x, const at::Tensor& w,
   causal_conv1d_launch(x.data_ptr(), (int)x.stride(0), w.data_ptr(),
                        bias ? bias->data_ptr() : nullptr, y.data_ptr(), (int)y.stride(0),
                        state.data_ptr<float>(), cu.data_ptr<int>(), slots.data_ptr<int>(),
-                       (int)slots.numel(), (int)x.size(1), (int)w.size(1), silu, cur_stream());
+                       (int)slots.numel(), (int)x.size(1), (int)w.size(1), silu, write_state,
+                       cur_stream());
 }
 
 void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                    const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
                    const at::Tensor& dt_bias, at::Tensor& state, const at::Tensor& cu,
-                   const at::Tensor& slots, int64_t HK, int64_t HV, bool reset_state) {
+                   const at::Tensor& slots, int64_t HK, int64_t HV, bool reset_state,
+                   bool write_state) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(a); CHECK_BF16(b);
   CHECK_BF16(o);
   TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
@@ -324,6 +327,7 @@ void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, cons
   p.ldq = (int)q.stride(0); p.ldk = (int)k.stride(0); p.ldv = (int)v.stride(0);
   p.ldab = (int)a.stride(0); p.ldo = (int)o.stride(0);
   p.HK = (int)HK; p.HV = (int)HV; p.reset_state = reset_state ? 1 : 0;
+  p.write_state = write_state ? 1 : 0;
   c10::cuda::CUDAGuard g(q.device());
   gdn_recurrent_launch(p, (int)slots.numel(), DK, DV, cur_stream());
 }
@@ -581,15 +585,15 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("gemm_grouped_out(Tensor(a!) out, Tensor x, Tensor w_stk, int E, int N, Tensor row_off, "
         "Tensor(b!) tile_off, int fmt, Tensor? scales, float out_scale, int bn=0) -> ()");
   m.def("gumbel_argmax(Tensor(a!) ids, Tensor(b!) vals, Tensor logits, Tensor temperature, "
-        "Tensor seeds, int offset, int id_offset) -> ()");
+        "Tensor seeds, int offset, int id_offset, Tensor? row_offsets=None) -> ()");
   m.def("topk_candidates(Tensor(a!) vals, Tensor(b!) ids, Tensor logits, int K, int id_offset) -> ()");
   m.def("sample_candidates(Tensor(a!) out, Tensor cand_v, Tensor cand_i, Tensor temperature, "
         "Tensor top_k, Tensor top_p, Tensor seeds, int offset) -> ()");
   m.def("causal_conv1d(Tensor(a!) y, Tensor x, Tensor w, Tensor? bias, Tensor(b!) state, "
-        "Tensor cu, Tensor slots, bool silu) -> ()");
+        "Tensor cu, Tensor slots, bool silu, bool write_state=True) -> ()");
   m.def("gdn_recurrent(Tensor(a!) o, Tensor q, Tensor k, Tensor v, Tensor a, Tensor b, "
         "Tensor A_log, Tensor dt_bias, Tensor(b!) state, Tensor cu, Tensor slots, int HK, int HV, "
-        "bool reset_state) -> ()");
+        "bool reset_state, bool write_state=True) -> ()");
   m.def("gated_rmsnorm(Tensor(a!) o, Tensor z, Tensor w, int H, float eps) -> ()");
   m.def("rejection_sample(Tensor(a!) out_tokens, Tensor(b!) num_out, Tensor target_logits, "
         "Tensor draft_logits, Tensor draft_ids, Tensor temperature, Tensor seeds, int offset) -> ()");

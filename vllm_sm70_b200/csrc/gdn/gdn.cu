@@ -12,6 +12,12 @@
 //                   the CTA owns row j of S in registers for the whole sequence).
 //   gated_rmsnorm   o <- rmsnorm(o) * w * silu(z) per head.
 //
+// Speculative verify: both state kernels take write_state = false for the
+// verify forward (states read, not advanced); after acceptance the same
+// kernels run once more over the accepted tokens with write_state = true, so
+// the stored state ends exactly at the last accepted token (rollback without
+// per-position state copies).
+//
 // Reference parity: FlashQLA GDN (sm70/csrc/gdn/gdn_forward.cu:90-430:
 // token-serial varlen recurrence with the state in registers, the decode
 // kernel with mixed qkv and slot-indexed global state, slot <= 0 = null
@@ -34,7 +40,7 @@ __global__ void conv1d_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                               const __nv_bfloat16* __restrict__ bias,  // [C] or null
                               __nv_bfloat16* __restrict__ y, int ldy, float* __restrict__ state,
                               const int* __restrict__ cu, const int* __restrict__ slots, int nseq,
-                              int C, int W, bool silu) {
+                              int C, int W, bool silu, bool write_state) {
   const int s = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= nseq || c >= C) return;
@@ -56,7 +62,7 @@ __global__ void conv1d_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
     hist[1] = hist[2];
     hist[2] = xt;
   }
-  if (st)
+  if (st && write_state)
     for (int i = 0; i < W - 1; ++i) st[i] = hist[3 - (W - 1) + i];
 }
 
@@ -129,7 +135,7 @@ __global__ void __launch_bounds__(DV) gdn_recurrent_kernel(const GdnParams p) {
     p.o[(size_t)t * p.ldo + (size_t)h * DV + j] = __float2bfloat16_rn(o * iq);
     __syncthreads();
   }
-  if (st) {
+  if (st && p.write_state) {
 #pragma unroll
     for (int i = 0; i < DK; i += 4)
       *reinterpret_cast<float4*>(st + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
@@ -166,13 +172,13 @@ __global__ void gated_rmsnorm_kernel(__nv_bfloat16* __restrict__ o, int ldo,
 
 void causal_conv1d_launch(const void* x, int ldx, const void* w, const void* bias, void* y,
                           int ldy, float* state, const int* cu, const int* slots, int nseq, int C,
-                          int W, bool silu, cudaStream_t stream) {
+                          int W, bool silu, bool write_state, cudaStream_t stream) {
   if (nseq <= 0) return;
   if (W < 2 || W > 4) throw std::runtime_error("causal_conv1d: kernel width must be 2..4");
   dim3 grid((C + 127) / 128, nseq);
   conv1d_kernel<<<grid, 128, 0, stream>>>((const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w,
                                           (const __nv_bfloat16*)bias, (__nv_bfloat16*)y, ldy,
-                                          state, cu, slots, nseq, C, W, silu);
+                                          state, cu, slots, nseq, C, W, silu, write_state);
 }
 
 void gdn_recurrent_launch(const GdnParams& p, int nseq, int dk, int dv, cudaStream_t stream) {

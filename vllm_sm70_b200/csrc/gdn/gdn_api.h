@@ -20,11 +20,12 @@ struct GdnParams {
   int ldq, ldk, ldv, ldab, ldo;
   int HK, HV;
   int reset_state;         // 1: start every sequence from a zero state
+  int write_state = 1;     // 0: read the state but do not store it (spec verify)
 };
 
 void causal_conv1d_launch(const void* x, int ldx, const void* w, const void* bias, void* y,
                           int ldy, float* state, const int* cu, const int* slots, int nseq, int C,
-                          int W, bool silu, cudaStream_t stream);
+                          int W, bool silu, bool write_state, cudaStream_t stream);
 void gdn_recurrent_launch(const GdnParams& p, int nseq, int dk, int dv, cudaStream_t stream);
 void gated_rmsnorm_launch(void* o, int ldo, const void* z, int ldz, const void* w, int T, int H,
                           int D, float eps, cudaStream_t stream);

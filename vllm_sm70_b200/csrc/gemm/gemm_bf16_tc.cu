@@ -72,6 +72,15 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n) {
   return {first_m + r % gsize, r / gsize};
 }
 
+// K-loop start offset per tile: tiles running concurrently start at different
+// k-blocks, so the shared operand (the activations, read by every N tile)
+// is not requested from the same L2 lines by every SM at the same moment.
+// The accumulation order differs per tile but is fixed for a given shape
+// (deterministic).
+__device__ __forceinline__ int kb_rotation(int t, int nk) {
+  return nk > 1 ? (int)(((unsigned)t * 2654435761u) >> 7) % nk : 0;
+}
+
 // Where one tile's operands come from and where its output goes.
 struct UnitCoord {
   int p_row, q_row;    // TMA row coordinates of the P / Q operands
@@ -190,7 +199,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         const int t = u / splits, sp = u - t * splits;
         const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        const int nk = kb1 - kb0;
+        const int rot = kb_rotation(t, nk);
+        for (int it = 0; it < nk; ++it) {
+          const int kb = kb0 + (it + rot) % nk;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err)) {
             *abort_flag = 1;
             break;
@@ -243,7 +255,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int it = 0; it < kb1 - kb0; ++it) {
           if (!mbar_wait(kQuant ? &dq_bar[stage] : &full_bar[stage], phase, err)) {
             ok = false;
             break;
@@ -256,7 +268,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           for (int k = 0; k < BK / UMMA_K; ++k) {
             // +32 bytes per K=16 step inside the 128-byte swizzle row.
             umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
-                     (kb > kb0 || k > 0) ? 1u : 0u);
+                     (it > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -285,7 +297,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       const int t = u / splits, sp = u - t * splits;
       const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
       const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
-      for (int kb = kb0; kb < kb1; ++kb) {
+      const int nk = kb1 - kb0;
+      const int rot = kb_rotation(t, nk);
+      for (int it = 0; it < nk; ++it) {
+        const int kb = kb0 + (it + rot) % nk;
         if (!mbar_wait(&full_bar[stage], phase, err)) {
           *abort_flag = 1;
           break;

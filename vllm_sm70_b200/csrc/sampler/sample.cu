@@ -85,11 +85,13 @@ template <typename T>
 __global__ void gumbel_argmax_kernel(const T* __restrict__ logits, int V, int ld,
                                      const float* __restrict__ temperature,
                                      const int64_t* __restrict__ seeds, uint64_t offset,
-                                     int id_offset, int* __restrict__ ids, float* __restrict__ vals) {
+                                     const int64_t* __restrict__ row_offsets, int id_offset,
+                                     int* __restrict__ ids, float* __restrict__ vals) {
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * ld;
   const float t = temperature[row];
   const uint64_t seed = (uint64_t)seeds[row];
+  if (row_offsets) offset += (uint64_t)row_offsets[row];
   VI best{-INFINITY, 0x7fffffff};
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     float v = to_f(x[i]);
@@ -325,15 +327,17 @@ __global__ void sample_candidates_kernel(const float* __restrict__ cand_v,
 
 void gumbel_argmax_launch(const void* logits, bool bf16, int rows, int V, int ld,
                           const float* temperature, const int64_t* seeds, uint64_t offset,
-                          int id_offset, int* ids, float* vals, cudaStream_t stream) {
+                          const int64_t* row_offsets, int id_offset, int* ids, float* vals,
+                          cudaStream_t stream) {
   if (rows <= 0) return;
   if (bf16)
     gumbel_argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, stream>>>(
-        (const __nv_bfloat16*)logits, V, ld, temperature, seeds, offset, id_offset, ids, vals);
+        (const __nv_bfloat16*)logits, V, ld, temperature, seeds, offset, row_offsets, id_offset,
+        ids, vals);
   else
     gumbel_argmax_kernel<float><<<rows, 1024, 0, stream>>>((const float*)logits, V, ld,
-                                                           temperature, seeds, offset, id_offset,
-                                                           ids, vals);
+                                                           temperature, seeds, offset, row_offsets,
+                                                           id_offset, ids, vals);
 }
 
 void topk_candidates_launch(const void* logits, bool bf16, int rows, int V, int ld, int K,

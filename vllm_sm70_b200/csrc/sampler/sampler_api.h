@@ -5,9 +5,12 @@
 
 namespace b200 {
 
+// row_offsets (optional, device): per-row counter added to `offset`, so a
+// CUDA graph replays fresh randomness (e.g. the row's generated-token count).
 void gumbel_argmax_launch(const void* logits, bool bf16, int rows, int V, int ld,
                           const float* temperature, const int64_t* seeds, uint64_t offset,
-                          int id_offset, int* ids, float* vals, cudaStream_t stream);
+                          const int64_t* row_offsets, int id_offset, int* ids, float* vals,
+                          cudaStream_t stream);
 void topk_candidates_launch(const void* logits, bool bf16, int rows, int V, int ld, int K,
                             int id_offset, float* out_v, int* out_i, cudaStream_t stream);
 void sample_candidates_launch(const float* cand_v, const int* cand_i, int rows, int C,

@@ -56,6 +56,8 @@ class GenerateStats:
     decode_steps: int = 0
     ttft_ms: list = field(default_factory=list)
     tpot_ms: list = field(default_factory=list)
+    spec_tokens: int = 0   # tokens emitted by speculative steps
+    spec_slots: int = 0    # (row, step) pairs; spec_tokens / spec_slots = tokens per step
 
 
 class LLM:
@@ -65,7 +67,8 @@ class LLM:
                  max_num_batched_tokens: int = 16384, gpu_memory_utilization: float = 0.90,
                  load_format: str = "dummy", seed: int = 0, enforce_eager: bool = False,
                  dtype=torch.bfloat16, num_kv_blocks: int | None = None,
-                 tune_gemm: bool = True, gemm_lut_path: str | None = None):
+                 tune_gemm: bool = True, gemm_lut_path: str | None = None,
+                 speculative_k: int = 0):
         self.cfg: ModelConfig = resolve(model)
         ps = pstate.get() if pstate._STATE is not None else None
         if ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
@@ -102,11 +105,17 @@ class LLM:
 
             comm.set_fused_ar_rmsnorm(symm.FusedArRmsNorm(
                 ps, max(max_num_batched_tokens, max_num_seqs), self.cfg.hidden_size))
+        self.spec_k = int(speculative_k)
+        if self.spec_k > 0:
+            from ..models.mtp import MTPHead
+
+            self.runner.enable_spec(MTPHead(self.model, seed=seed + 1), self.spec_k)
         if self.device.type == "cuda" and tune_gemm:
             from . import warmup
 
             warmup.engine_warmup(self.model, ps, self.runner.capture_sizes, gemm_lut_path)
-        self.runner.capture()
+        if self.spec_k == 0:
+            self.runner.capture()
         self.last_stats: GenerateStats | None = None
 
     def shutdown(self) -> None:
@@ -147,9 +156,9 @@ class LLM:
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
         for p in params:
-            if not p.greedy:
-                raise NotImplementedError("temperature sampling: use greedy (temperature=0) "
-                                          "or the hidden-state sampler in serving mode")
+            if p.top_k not in (-1, 0) or p.top_p < 1.0:
+                raise NotImplementedError("top-k / top-p: use ops.sampling.topk_candidates + "
+                                          "sample_candidates; the engine samples with temperature")
         reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
         runner = self.runner
         bs = runner.block_size
@@ -172,7 +181,7 @@ class LLM:
             while waiting and free_slots:
                 r = waiting[0]
                 L = r.prompt.numel()
-                total = L + r.params.max_tokens
+                total = L + r.params.max_tokens + (self.spec_k + 1 if self.spec_k else 0)
                 if total > runner.max_model_len:
                     raise ValueError(f"request {r.rid}: {total} tokens > max_model_len")
                 nblk = math.ceil(total / bs)
@@ -182,6 +191,9 @@ class LLM:
                 r.slot = free_slots.pop()
                 r.blocks = runner.alloc.allocate(nblk)
                 runner.set_block_row(r.slot, r.blocks)
+                seed = r.params.seed if r.params.seed is not None else 0x9E3779B97F4A7C15 ^ r.rid
+                runner.set_sampling(r.slot, 0.0 if r.params.greedy else r.params.temperature,
+                                    seed & 0x7FFFFFFFFFFFFFFF)
                 admitted.append(r)
             if not admitted and not running:
                 raise RuntimeError("cannot admit any request: KV cache too small")
@@ -212,7 +224,20 @@ class LLM:
             # ---- decode until the next request finishes
             live = [r for r in running if not r.done]
             finished_now = [r for r in live if r.generated >= r.params.max_tokens]
-            if not finished_now:
+            if not finished_now and self.spec_k:
+                n_rows = max(r.slot for r in live) + 1
+                n = runner.spec_step(n_rows).cpu()
+                stats.decode_steps += 1
+                for r in live:
+                    r.generated += int(n[r.slot])
+                    stats.spec_tokens += int(n[r.slot])
+                stats.spec_slots += len(live)
+                finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+                if cuda and finished_now:
+                    e = ev()
+                    e.record()
+                    decode_events.append((e, finished_now, 1))
+            elif not finished_now:
                 steps = min(r.params.max_tokens - r.generated for r in live)
                 n_rows = max(r.slot for r in live) + 1
                 runner.decode(n_rows, steps)

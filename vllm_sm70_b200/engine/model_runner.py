@@ -64,6 +64,11 @@ class ModelRunner:
         self.bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32).pin_memory() \
             if dev.type == "cuda" else torch.zeros(B, self.max_blocks, dtype=torch.int32)
         self.slot_ids = torch.arange(B, dtype=torch.int32, device=dev)
+        self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.seeds = torch.zeros(B, dtype=torch.int64, device=dev)
+        # Decode graphs always sample through the temperature path: rows with
+        # T <= 0 reduce to the exact greedy argmax.
+        self.sampling = True
         if hasattr(model, "allocate_states"):
             model.allocate_states(B)
         if hasattr(model, "reserve_workspace"):
@@ -110,7 +115,10 @@ class ModelRunner:
                         cu_q=self.cu_q[: b + 1], max_q_len=1, decode=True, num_splits=ns,
                         part_o=po, part_ml=pml, state_slots=self.slot_ids[:b])
         h = self.model.forward(self.ids[:b], meta, self.kv)
-        nxt = self.model.greedy(h)
+        if self.sampling:
+            nxt = self.model.sample(h, self.temperature[:b], self.seeds[:b], self.out_pos[:b])
+        else:
+            nxt = self.model.greedy(h)
         self.ids[:b].copy_(nxt)
         self.out_tokens.view(-1).index_copy_(0, self.row_base[:b] + self.out_pos[:b], nxt)
         act = self.active[:b]
@@ -167,6 +175,10 @@ class ModelRunner:
         self.pool = None
 
     # ------------------------------------------------------------ prefill
+    def set_sampling(self, slot: int, temperature: float, seed: int) -> None:
+        self.temperature[slot] = float(temperature)
+        self.seeds[slot] = int(seed)
+
     def prefill(self, pieces: list[tuple[int, torch.Tensor, int, bool, int]]) -> None:
         """``pieces``: (slot, token ids [n] int64 CPU, ctx_start, is_last, total_len)."""
         dev = self.device
@@ -198,14 +210,97 @@ class ModelRunner:
         if not last:
             return
         rows = h2d(torch.tensor([int(cu[i + 1]) - 1 for i in last], dtype=torch.int64))
-        nxt = self.model.greedy(h.index_select(0, rows))
+        h_last = h.index_select(0, rows)
         sidx = h2d(torch.tensor([pieces[i][0] for i in last], dtype=torch.int64))
+        if self.sampling:
+            nxt = self.model.sample(h_last, self.temperature.index_select(0, sidx),
+                                    self.seeds.index_select(0, sidx), None, offset=0)
+        else:
+            nxt = self.model.greedy(h_last)
         total = h2d(torch.tensor([pieces[i][4] + 1 for i in last], dtype=torch.int32))
         self.ids.index_copy_(0, sidx, nxt.to(torch.int64))
         self.seq_lens.index_copy_(0, sidx, total)
         self.out_tokens.view(-1).index_copy_(0, self.row_base.index_select(0, sidx), nxt)
         self.out_pos.index_fill_(0, sidx, 1)
         self.active.index_fill_(0, sidx, 1)
+        if getattr(self, "spec_k", 0):
+            self.last_hidden.index_copy_(0, sidx, h_last)
+
+    # ------------------------------------------------------------ speculative decoding
+    def enable_spec(self, mtp, k: int) -> None:
+        """Attach an MTP draft head drafting ``k`` tokens per step."""
+        self.mtp = mtp
+        self.spec_k = k
+        mtp.allocate_cache(self.num_blocks, self.block_size)
+        H = self.cfg.hidden_size
+        self.last_hidden = torch.zeros(self.B, H, dtype=self.model.dtype, device=self.device)
+        self.spec_offset = 0
+
+    def _meta_for(self, b: int, q_len: int, start_pos: torch.Tensor, decode: bool = True,
+                  spec_verify: bool = False) -> AttnMeta:
+        """Metadata for ``q_len`` consecutive tokens per row starting at
+        ``start_pos[row]`` (rows 0..b-1 of the batch)."""
+        bs = self.block_size
+        dev = self.device
+        pos = (start_pos.to(torch.int64)[:, None] + torch.arange(q_len, device=dev)[None, :])
+        bt = self.block_table[:b]
+        blk = torch.gather(bt, 1, (pos // bs)).to(torch.int64)
+        slots = (blk * bs + pos % bs).reshape(-1)
+        seq_lens = (start_pos + q_len).to(torch.int32)
+        cu = torch.arange(b + 1, device=dev, dtype=torch.int32) * q_len
+        return AttnMeta(positions=pos.reshape(-1), slot_mapping=slots, block_table=bt,
+                        seq_lens=seq_lens, cu_q=cu, max_q_len=q_len, decode=decode,
+                        state_slots=self.slot_ids[:b], spec_verify=spec_verify)
+
+    def spec_step(self, b: int) -> torch.Tensor:
+        """One draft (MTP, k tokens) + verify (target, k+1 tokens) + rejection
+        step over rows 0..b-1. Returns the number of tokens emitted per row
+        (device int32; 0 for inactive rows)."""
+        from ..ops import sampling
+
+        k = self.spec_k
+        m = self.model
+        act = self.active[:b]
+        sl = self.seq_lens[:b]               # context incl. ids[row] (at position sl - 1)
+        base = sl.to(torch.int64) - 1
+        tok = self.ids[:b]
+        hid = self.last_hidden[:b]
+        temp, seeds = self.temperature[:b], self.seeds[:b]
+        d_ids, d_logits = [], []
+        for j in range(k):
+            meta = self._meta_for(b, 1, base + j)
+            hid = self.mtp.forward(tok, hid, meta)
+            lg = m.logits(hid)
+            nxt, _ = sampling.gumbel_sample(lg, temp, seeds, self.spec_offset * 64 + j)
+            tok = nxt.to(torch.int64)
+            d_ids.append(nxt)
+            d_logits.append(lg if not lg.is_cuda else lg.to(torch.bfloat16))
+        draft_ids = torch.stack(d_ids, 1).contiguous()                  # [b, k] int32
+        toks = torch.cat([self.ids[:b, None], draft_ids.to(torch.int64)], 1).reshape(-1)
+        meta = self._meta_for(b, k + 1, base, decode=True, spec_verify=True)
+        hidden = m.forward(toks, meta, self.kv)                          # [b*(k+1), H]
+        tl = m.logits(hidden)
+        tl = (tl.to(torch.bfloat16) if tl.is_cuda else tl).view(b, k + 1, -1)
+        out, n = sampling.rejection_sample(tl, torch.stack(d_logits, 1), draft_ids, temp, seeds,
+                                           self.spec_offset * 64 + 63)
+        self.spec_offset += 1
+        n = n * act
+        if hasattr(m, "commit_spec"):
+            m.commit_spec(n, k + 1, self.slot_ids[:b])
+        # commit: emitted tokens, counters, next input id and hidden
+        nl = n.to(torch.int64)
+        last = torch.gather(out.to(torch.int64), 1, (nl - 1).clamp(min=0)[:, None]).squeeze(1)
+        self.ids[:b] = torch.where(nl > 0, last, self.ids[:b])
+        hv = hidden.view(b, k + 1, -1)
+        hsel = torch.gather(hv, 1, (nl - 1).clamp(min=0)[:, None, None].expand(b, 1, hv.shape[2]))
+        self.last_hidden[:b] = torch.where((nl > 0)[:, None], hsel.squeeze(1), self.last_hidden[:b])
+        cols = self.out_pos[:b, None] + torch.arange(k + 1, device=self.device)[None, :]
+        valid = torch.arange(k + 1, device=self.device)[None, :] < nl[:, None]
+        flat_idx = (self.row_base[:b, None] + cols.clamp(max=self.out_cap - 1))[valid]
+        self.out_tokens.view(-1).index_copy_(0, flat_idx, out[valid])
+        self.out_pos[:b] += nl
+        self.seq_lens[:b] += n
+        return n
 
     def deactivate(self, slots: list[int]) -> None:
         if not slots:

@@ -67,6 +67,7 @@ class AttnMeta:
     part_ml: torch.Tensor | None = None
     last_token_idx: torch.Tensor | None = None  # [S] int64 rows whose logits are needed
     state_slots: torch.Tensor | None = None     # [S] int32 recurrent-state slot per sequence
+    spec_verify: bool = False                   # recurrent states are read, not advanced
 
 
 @dataclass

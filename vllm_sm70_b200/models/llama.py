@@ -245,6 +245,19 @@ class LlamaModel:
         ids, vals = ops.argmax(logits[:, :nvalid], id_offset=self.vocab_start)
         return comm.greedy_merge(vals, ids)
 
+    def sample(self, hidden: torch.Tensor, temperature: torch.Tensor, seeds: torch.Tensor,
+               row_offsets: torch.Tensor | None = None, offset: int = 0) -> torch.Tensor:
+        """Per-row temperature sampling (T <= 0: greedy) from the vocab-
+        parallel LM head: local Gumbel-max per rank, rank-order merge of the
+        perturbed (value, id) pairs -- exact, one tiny all-gather."""
+        logits = ops.gemm(hidden, self.lm_head)
+        nvalid = max(1, min(self.vocab_local, self.cfg.vocab_size - self.vocab_start))
+        ids, vals = ops.sampling.gumbel_sample(logits[:, :nvalid], temperature, seeds, offset,
+                                               self.vocab_start, row_offsets)
+        if self.ps.tp_size == 1:
+            return ids
+        return comm.greedy_merge(vals, ids)
+
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         lg = ops.gemm(hidden, self.lm_head)
         if self.ps.tp_size > 1:

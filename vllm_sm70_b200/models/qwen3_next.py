@@ -51,6 +51,7 @@ class Qwen3NextModel(Qwen3MoeModel):
         self.gdn_state = None
         self.conv_state = None
         self.max_slots = 0
+        self._verify_saved: dict = {}
 
     # ------------------------------------------------------------------ state
     def allocate_states(self, max_slots: int) -> None:
@@ -67,6 +68,39 @@ class Qwen3NextModel(Qwen3MoeModel):
         if self.gdn_state is not None and slots.numel():
             self.gdn_state.index_fill_(1, slots, 0.0)
             self.conv_state.index_fill_(1, slots, 0.0)
+
+    def commit_spec(self, num_accepted: torch.Tensor, q_len: int, slots: torch.Tensor) -> None:
+        """After a speculative verify of ``q_len`` tokens per row, advance the
+        recurrent / conv states over the first ``num_accepted[row]`` tokens
+        only (re-running the state kernels on the saved layer inputs)."""
+        rows = num_accepted.shape[0]
+        dev = num_accepted.device
+        # Tokens of row r live at [r * q_len, r * q_len + q_len); take the first n_r.
+        starts = torch.arange(rows, device=dev, dtype=torch.int64) * q_len
+        n = num_accepted.to(torch.int64)
+        idx_list = torch.arange(q_len, device=dev)[None, :] + starts[:, None]
+        keep = torch.arange(q_len, device=dev)[None, :] < n[:, None]
+        sel = idx_list[keep]
+        cu = torch.zeros(rows + 1, dtype=torch.int32, device=dev)
+        cu[1:] = torch.cumsum(n, 0).to(torch.int32)
+        HK, HV, DK, DV = self.HK, self.HV, self.DK, self.DV
+        lin = [i for i, t in enumerate(self.layer_types) if t == "linear_attention"]
+        for lin_idx, li in enumerate(lin):
+            if lin_idx not in self._verify_saved:
+                continue
+            L = self.layers[li]
+            mixed, b, a = self._verify_saved[lin_idx]
+            mixed_s = mixed.index_select(0, sel).contiguous()
+            b_s = b.index_select(0, sel).contiguous()
+            a_s = a.index_select(0, sel).contiguous()
+            conv_out = gdn_ops.causal_conv1d(mixed_s, L["conv_w"], None, self.conv_state[lin_idx],
+                                             cu, slots, True)
+            q = conv_out[:, : HK * DK]
+            k = conv_out[:, HK * DK: 2 * HK * DK]
+            v = conv_out[:, 2 * HK * DK:]
+            gdn_ops.gdn_recurrent(q, k, v, a_s, b_s, L["A_log"], L["dt_bias"],
+                                  self.gdn_state[lin_idx], cu, slots, HK, HV)
+        self._verify_saved.clear()
 
     # ------------------------------------------------------------------ weights
     def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
@@ -138,13 +172,17 @@ class Qwen3NextModel(Qwen3MoeModel):
         b, a = ba[:, :HV], ba[:, HV:]
         conv_out = torch.empty(T, self.conv_dim, device=x.device, dtype=self.dtype)
         slots = meta.state_slots
+        write = not meta.spec_verify
+        if meta.spec_verify:  # keep the inputs for the commit pass after acceptance
+            self._verify_saved[lin_idx] = (mixed, b, a)
         gdn_ops.causal_conv1d(mixed, L["conv_w"], None, self.conv_state[lin_idx], meta.cu_q,
-                              slots, True, out=conv_out)
+                              slots, True, out=conv_out, write_state=write)
         q = conv_out[:, : HK * DK]
         k = conv_out[:, HK * DK: 2 * HK * DK]
         v = conv_out[:, 2 * HK * DK:]
         o = gdn_ops.gdn_recurrent(q, k, v, a, b, L["A_log"], L["dt_bias"],
-                                  self.gdn_state[lin_idx], meta.cu_q, slots, HK, HV)
+                                  self.gdn_state[lin_idx], meta.cu_q, slots, HK, HV,
+                                  write_state=write)
         gdn_ops.gated_rmsnorm(o, z, L["gnorm"], HV, self.cfg.rms_eps)
         return L["out"].forward(o, out=comm.row_parallel_out(T, x.shape[1]))
 

@@ -81,29 +81,31 @@ def gated_rmsnorm_ref(o, z, w, H, eps):
     return (n * F.silu(zf)).view(T, H * D)
 
 
-def causal_conv1d(x, w, bias, state, cu, slots, silu=True, out=None):
+def causal_conv1d(x, w, bias, state, cu, slots, silu=True, out=None, write_state=True):
     if out is None:
         out = torch.empty_like(x)
     if x.is_cuda:
         _ext.require()
-        torch.ops._b200_C.causal_conv1d(out, x, w, bias, state, cu, slots, silu)
+        torch.ops._b200_C.causal_conv1d(out, x, w, bias, state, cu, slots, silu, write_state)
         launch_count.add(1)
     else:
-        out.copy_(causal_conv1d_ref(x, w, bias, state, cu, slots, silu).to(out.dtype))
+        st = state if write_state else state.clone()
+        out.copy_(causal_conv1d_ref(x, w, bias, st, cu, slots, silu).to(out.dtype))
     return out
 
 
 def gdn_recurrent(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV, reset_state=False,
-                  out=None):
+                  out=None, write_state=True):
     if out is None:
         out = torch.empty(q.shape[0], v.shape[1], dtype=torch.bfloat16, device=q.device)
     if q.is_cuda:
         _ext.require()
         torch.ops._b200_C.gdn_recurrent(out, q, k, v, a, b, A_log, dt_bias, state, cu, slots,
-                                        HK, HV, reset_state)
+                                        HK, HV, reset_state, write_state)
         launch_count.add(1)
     else:
-        out.copy_(gdn_recurrent_ref(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV,
+        st = state if write_state else state.clone()
+        out.copy_(gdn_recurrent_ref(q, k, v, a, b, A_log, dt_bias, st, cu, slots, HK, HV,
                                     reset_state).to(out.dtype))
     return out
 

@@ -162,7 +162,7 @@ def experts_forward(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: Exp
     (same shape as the output) is added in the combine."""
     T, k = ids.shape
     if out is None:
-        out = torch.empty(T, ew.H, dtype=torch.bfloat16, device=x.device)
+        out = torch.empty(T, ew.H, dtype=x.dtype, device=x.device)
     if not x.is_cuda:
         r = experts_forward_ref(x, w, ids, ew, e_base)
         if shared is not None:

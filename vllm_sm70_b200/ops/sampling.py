@@ -64,7 +64,7 @@ def merge_rank_top1(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
 
 # ------------------------------------------------------------------ random sampling
 def gumbel_sample(logits: torch.Tensor, temperature: torch.Tensor, seeds: torch.Tensor,
-                  offset: int, id_offset: int = 0):
+                  offset: int, id_offset: int = 0, row_offsets: torch.Tensor | None = None):
     """Exact sample from softmax(logits / T) per row (Gumbel-max with Philox
     noise keyed by (seed, global token id)); T <= 0 rows are greedy. Returns
     (ids int32, perturbed max value) so vocab shards merge with
@@ -72,8 +72,18 @@ def gumbel_sample(logits: torch.Tensor, temperature: torch.Tensor, seeds: torch.
     rows = logits.shape[0]
     ids = torch.empty(rows, dtype=torch.int32, device=logits.device)
     vals = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    if not logits.is_cuda:
+        x = logits.float()
+        t = temperature.float()[:, None]
+        g = torch.Generator().manual_seed(int(offset))
+        u = torch.rand(x.shape, generator=g).clamp(1e-12, 1 - 1e-7)
+        pert = torch.where(t > 0, x / t.clamp_min(1e-6) - torch.log(-torch.log(u)), x)
+        vals.copy_(pert.max(-1).values)
+        ids.copy_(pert.argmax(-1).to(torch.int32) + id_offset)
+        return ids, vals
     _ext.require()
-    torch.ops._b200_C.gumbel_argmax(ids, vals, logits, temperature, seeds, offset, id_offset)
+    torch.ops._b200_C.gumbel_argmax(ids, vals, logits, temperature, seeds, offset, id_offset,
+                                    row_offsets)
     launch_count.add(1)
     return ids, vals
 
@@ -112,6 +122,9 @@ def rejection_sample(target_logits: torch.Tensor, draft_logits: torch.Tensor,
     -1 padding, num_out [rows]) -- accepted drafts plus one corrected / bonus
     token."""
     rows, k = draft_ids.shape
+    if not target_logits.is_cuda:
+        return rejection_sample_ref(target_logits, draft_logits, draft_ids, temperature, seeds,
+                                    offset)
     out = torch.empty(rows, k + 1, dtype=torch.int32, device=draft_ids.device)
     n = torch.empty(rows, dtype=torch.int32, device=draft_ids.device)
     _ext.require()
@@ -119,4 +132,41 @@ def rejection_sample(target_logits: torch.Tensor, draft_logits: torch.Tensor,
                                        draft_logits.contiguous(), draft_ids.contiguous(),
                                        temperature, seeds, offset)
     launch_count.add(1)
+    return out, n
+
+
+def rejection_sample_ref(target_logits, draft_logits, draft_ids, temperature, seeds, offset):
+    """CPU oracle with the same acceptance rule (torch RNG instead of Philox)."""
+    rows, k = draft_ids.shape
+    out = torch.full((rows, k + 1), -1, dtype=torch.int32)
+    n = torch.zeros(rows, dtype=torch.int32)
+    for r in range(rows):
+        T = float(temperature[r])
+        g = torch.Generator().manual_seed((int(seeds[r]) * 1000003 + int(offset)) % (1 << 63))
+        e = 0
+        for i in range(k + 1):
+            tl = target_logits[r, i].float()
+            if T <= 0:
+                am = int(tl.argmax())
+                out[r, e] = am
+                e += 1
+                if i == k or am != int(draft_ids[r, i]):
+                    break
+                continue
+            p = torch.softmax(tl / T, -1)
+            if i == k:
+                out[r, e] = int(torch.multinomial(p, 1, generator=g))
+                e += 1
+                break
+            q = torch.softmax(draft_logits[r, i].float() / T, -1)
+            d = int(draft_ids[r, i])
+            if float(torch.rand(1, generator=g)) * float(q[d]) <= float(p[d]):
+                out[r, e] = d
+                e += 1
+                continue
+            res = (p - q).clamp_min(0)
+            out[r, e] = int(torch.multinomial(res / res.sum(), 1, generator=g)) if res.sum() > 0 else d
+            e += 1
+            break
+        n[r] = e
     return out, n
