@@ -155,12 +155,15 @@ def run_ours(args) -> dict:
     w0 = time.perf_counter()
     ev0.record()
     ttft, tpot = [], []
+    pre_ms = dec_ms = 0.0
     outs = None
     for i in range(args.steps):
         outs = llm.generate(timed[i], sp)
         st = llm.last_stats
         ttft += st.ttft_ms
         tpot += st.tpot_ms
+        pre_ms += st.prefill_ms
+        dec_ms += st.decode_ms
     ev1.record()
     torch.cuda.synchronize()
     _barrier()
@@ -185,6 +188,8 @@ def run_ours(args) -> dict:
                    "block_size": args.block_size, "prefill_chunk_tokens": args.chunk},
         "p50_ttft_ms": round(statistics.median(ttft), 1) if ttft else None,
         "p50_tpot_ms": round(statistics.median(tpot), 3) if tpot else None,
+        "phase_ms_per_step": {"prefill": round(pre_ms / args.steps, 1),
+                              "decode": round(dec_ms / args.steps, 1)},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": int(prompts.numel() * prompts.element_size()),
                 "d2h_bytes_per_step": int(N_REQ * OUT * 4)},

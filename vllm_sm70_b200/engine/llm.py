@@ -174,6 +174,7 @@ class LLM:
         wall0 = time.perf_counter()
         pending_first: list[tuple[object, list[_Req]]] = []
         decode_events: list[tuple[object, list[_Req], int]] = []
+        prefill_spans: list[tuple[object, object]] = []
 
         while waiting or running:
             # ---- admission
@@ -213,7 +214,14 @@ class LLM:
                     if last:
                         queue.popleft()
                         finishing.append(r)
+                if cuda:
+                    e_pre = ev()
+                    e_pre.record()
                 runner.prefill(pieces)
+                if cuda:
+                    e_post = ev()
+                    e_post.record()
+                    prefill_spans.append((e_pre, e_post))
                 for r in finishing:
                     r.generated = 1
                 if cuda and finishing:
@@ -274,6 +282,8 @@ class LLM:
                 for r in rs:
                     r.t_last = ms
             stats.total_ms = t0.elapsed_time(t_end)
+            stats.prefill_ms = sum(a.elapsed_time(b) for a, b in prefill_spans)
+            stats.decode_ms = stats.total_ms - stats.prefill_ms
         else:
             stats.total_ms = (time.perf_counter() - wall0) * 1e3
         outs = []
