@@ -102,6 +102,10 @@ void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K
 
 int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm);
 
+// Tile width (N side of the accumulator) and swap-AB flag of a config (0 / false if unknown).
+int gemm_cfg_tile_n(int cfg);
+bool gemm_cfg_is_swap(int cfg);
+
 // Explicit-workspace variant: splits > 1 needs ws >= tiles*splits*128*BN*4
 // bytes and counters[tiles] zeroed (they are re-armed by the kernel).
 void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,

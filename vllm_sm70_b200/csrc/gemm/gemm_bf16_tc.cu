@@ -600,6 +600,9 @@ std::unordered_map<PlanKey, GemmPlan, PlanKeyHash> g_plans;
 
 }  // namespace
 
+int gemm_cfg_tile_n(int cfg) { return cfg_bn(cfg); }
+bool gemm_cfg_is_swap(int cfg) { return cfg_swap(cfg); }
+
 GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
   {
     std::lock_guard<std::mutex> g(g_plan_mu);
