@@ -7,7 +7,8 @@ from vllm_sm70_b200.ops import linear
 pytestmark = pytest.mark.gpu
 
 CFGS = {"n256": 0, "n128": 1, "swap16": 2, "swap32": 3, "swap64": 4, "n192": 5, "n96": 6,
-        "n64": 7, "swap128": 8}
+        "n64": 7, "swap128": 8, "m2n256": 9, "m2n224": 10, "m2n128": 11, "m2n112": 12,
+        "m2n64": 13}
 
 
 def _ref(a, w):
@@ -54,6 +55,22 @@ def test_gemm_silu_mul(b200_ops, M, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("cfg", [0, 1, 9, 11])
+@pytest.mark.parametrize("M", [200, 256, 777])
+def test_gemm_silu_mul_configs(b200_ops, cfg, M, rel_err):
+    torch.manual_seed(6)
+    K, N = 1024, 640
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wg = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    wu = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    wi = linear.interleave_gate_up(wg, wu)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    torch.ops._b200_C.gemm_bf16_silu_mul_out(out, a, wi, cfg)
+    g = a.float() @ wg.float().t()
+    u = a.float() @ wu.float().t()
+    assert rel_err(out, g * torch.sigmoid(g) * u) < 2e-2
+
+
 def test_gemm_deterministic(b200_ops):
     torch.manual_seed(3)
     a = torch.randn(512, 1024, device="cuda", dtype=torch.bfloat16)
@@ -63,12 +80,14 @@ def test_gemm_deterministic(b200_ops):
     assert torch.equal(o1, o2)
 
 
-@pytest.mark.parametrize("cfg", ["n256", "n128", "swap16", "swap64", "n192", "n96", "swap128"])
+@pytest.mark.parametrize("cfg", ["n256", "n128", "swap16", "swap64", "n192", "n96", "swap128",
+                                 "m2n256", "m2n224", "m2n128", "m2n112", "m2n64"])
 @pytest.mark.parametrize("splits", [2, 3, 5, 8])
 def test_gemm_split_k(b200_ops, cfg, splits, rel_err):
     torch.manual_seed(4)
     M = {"n256": 256, "n128": 200, "swap16": 9, "swap64": 50, "n192": 256, "n96": 130,
-         "swap128": 100}[cfg]
+         "swap128": 100, "m2n256": 256, "m2n224": 300, "m2n128": 200, "m2n112": 512,
+         "m2n64": 256}[cfg]
     N, K = 1536, 4096 + 64
     a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05

@@ -24,7 +24,12 @@ enum GemmConfig : int {
   kCfgN96 = 6,     // 128 x 96
   kCfgN64 = 7,     // 128 x 64
   kCfgSwap128 = 8, // swap-AB: 128 weight rows x 128 tokens
-  kCfgCount = 9,
+  kCfgM2N256 = 9,  // tall tile: 256 x 256 (two M=128 accumulators), 3 stages
+  kCfgM2N224 = 10, // 256 x 224
+  kCfgM2N128 = 11, // 256 x 128
+  kCfgM2N112 = 12, // 256 x 112
+  kCfgM2N64 = 13,  // 256 x 64
+  kCfgCount = 14,
 };
 
 constexpr int kMaxSplits = 8;
@@ -104,6 +109,7 @@ int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm);
 
 // Tile width (N side of the accumulator) and swap-AB flag of a config (0 / false if unknown).
 int gemm_cfg_tile_n(int cfg);
+int gemm_cfg_tile_m(int cfg);  // 128 or 256 (tall tiles)
 bool gemm_cfg_is_swap(int cfg);
 
 // Explicit-workspace variant: splits > 1 needs ws >= tiles*splits*128*BN*4

@@ -17,6 +17,13 @@
 //               fused SiLU(gate)*up, store bf16 to global. Runs concurrently
 //               with the next tile's main loop (accumulator double buffer).
 //
+// Tall tiles (MH = 2, normal mode only): one CTA owns 256 P rows x BN, as two
+// M=128 MMAs per K step that share the Q (weight) tile and write two TMEM
+// accumulators. At decode batch sizes (M <= 256) every weight byte then
+// enters shared memory once instead of once per 128-row M tile, which cuts
+// the L2-to-SM operand traffic by up to a third; the accumulator is double
+// buffered while 2 * MH * BN fits the 512 TMEM columns, single buffered above.
+//
 // Reference parity: replaces the TurboMind sm70 GEMM family
 // (sm70/csrc/turbomind/lmdeploy/src/turbomind/kernels/gemm/gemm.h:14-50,
 // kernel/sm70_884_*.cu) and its gated-SiLU epilogue (types.h:141); the
@@ -72,13 +79,14 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int num_m, int num_n) {
   return {first_m + r % gsize, r / gsize};
 }
 
-// K-loop start offset per tile: tiles running concurrently start at different
-// k-blocks, so the shared operand (the activations, read by every N tile)
-// is not requested from the same L2 lines by every SM at the same moment.
-// The accumulation order differs per tile but is fixed for a given shape
-// (deterministic).
-__device__ __forceinline__ int kb_rotation(int t, int nk) {
-  return nk > 1 ? (int)(((unsigned)t * 2654435761u) >> 7) % nk : 0;
+// K-loop start offset per tile when there is a single M tile (decode-sized
+// M): tiles running concurrently start at different k-blocks, so the shared
+// activation tile is not requested from the same L2 lines by every SM at the
+// same moment. With several M tiles the tiles of a wave must walk K in step
+// instead (their operands then share L2 lines), so the offset is 0. The
+// accumulation order differs per tile but is fixed for a given shape.
+__device__ __forceinline__ int kb_rotation(int t, int nk, int num_m) {
+  return (nk > 1 && num_m == 1) ? (int)(((unsigned)t * 2654435761u) >> 7) % nk : 0;
 }
 
 // Where one tile's operands come from and where its output goes.
@@ -88,7 +96,7 @@ struct UnitCoord {
   int p_lim, q_lim;    // exclusive bounds for out_i0 + i / out_j0 + j
 };
 
-template <int BN>
+template <int BN, int BMT = BM>
 __device__ __forceinline__ UnitCoord unit_coord(int t, int num_m, int num_n, const GroupInfo& g,
                                                 int p_rows, int q_rows) {
   if (g.E > 0) {
@@ -114,12 +122,13 @@ __device__ __forceinline__ UnitCoord unit_coord(int t, int num_m, int num_n, con
     return u;
   }
   const TileCoord tc = tile_coord(t, num_m, num_n);
-  return UnitCoord{tc.mb * BM, tc.nb * BN, tc.mb * BM, tc.nb * BN, p_rows, q_rows};
+  return UnitCoord{tc.mb * BMT, tc.nb * BN, tc.mb * BMT, tc.nb * BN, p_rows, q_rows};
 }
 
-template <int BN, int STAGES, int WF = kWBf16>
+template <int BN, int STAGES, int WF = kWBf16, int MH = 1>
 struct Smem {
-  static constexpr int kPBytes = BM * BK * 2;
+  static constexpr int kHalfBytes = BM * BK * 2;  // one 128-row P sub-tile
+  static constexpr int kPBytes = MH * kHalfBytes;
   static constexpr int kQBytes = BN * BK * 2;
   static constexpr int kRawBytes = BM * raw_row_bytes(WF);  // weight = P side (swap)
   static constexpr int kStageBytes = kPBytes + kQBytes + kRawBytes;
@@ -128,7 +137,7 @@ struct Smem {
   static constexpr int kTotal = kTileBytes + kBarBytes + 1024;  // +1024 for manual alignment
 };
 
-template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16>
+template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1>
 __global__ void __launch_bounds__(WF == kWBf16 ? kThreads : kThreadsQ, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     const __grid_constant__ CUtensorMap tmap_q, __nv_bfloat16* __restrict__ C,
@@ -136,8 +145,15 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     int* __restrict__ counters, unsigned int* err, const WQParams wq,
                     const GroupInfo grp) {
   static_assert(WF == kWBf16 || SWAP, "quantised weights use the swap-AB (weight = P) form");
+  static_assert(MH == 1 || (!SWAP && WF == kWBf16), "tall tiles: normal-mode bf16 only");
   constexpr bool kQuant = WF != kWBf16;
-  using S = Smem<BN, STAGES, WF>;
+  constexpr int BMT = BM * MH;  // P rows per tile
+  // TMEM columns: the MH accumulators of one tile sit kHalfCols apart; two
+  // tiles' accumulators alternate when they fit.
+  constexpr int kHalfCols = MH == 1 ? BN : (BN + 31) / 32 * 32;
+  constexpr int kAccCols = MH == 1 ? BN : MH * kHalfCols;
+  constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
+  using S = Smem<BN, STAGES, WF, MH>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -153,14 +169,16 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int num_m = (p_rows + BM - 1) / BM;
+  const int num_m = (p_rows + BMT - 1) / BMT;
   const int num_n = (q_rows + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
   const int kb_per = (num_kb + splits - 1) / splits;
   const int num_units = grp.E > 0 ? __ldg(grp.tile_off + grp.E) * splits : num_tiles * splits;
-  constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
-                                 : (2 * BN <= 256) ? 256 : 512;
+  constexpr int kUsedCols = kNumAcc * kAccCols;
+  constexpr uint32_t kTmemCols = (kUsedCols <= 32) ? 32 : (kUsedCols <= 64) ? 64
+                                 : (kUsedCols <= 128) ? 128 : (kUsedCols <= 256) ? 256 : 512;
+  static_assert(kUsedCols <= 512, "accumulators exceed TMEM");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -197,10 +215,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       long issued = 0;
       for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
         const int t = u / splits, sp = u - t * splits;
-        const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
+        const UnitCoord uc = unit_coord<BN, BMT>(t, num_m, num_n, grp, p_rows, q_rows);
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int nk = kb1 - kb0;
-        const int rot = kb_rotation(t, nk);
+        const int rot = kb_rotation(t, nk, num_m);
         for (int it = 0; it < nk; ++it) {
           const int kb = kb0 + (it + rot) % nk;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err)) {
@@ -217,7 +235,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                         kb * raw_row_bytes(WF), uc.p_row);
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-            tma_load_2d(spp, &tmap_p, &full_bar[stage], kb * BK, uc.p_row);
+#pragma unroll
+            for (int h = 0; h < MH; ++h)
+              tma_load_2d(spp + h * S::kHalfBytes, &tmap_p, &full_bar[stage], kb * BK,
+                          uc.p_row + h * BM);
             tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, uc.q_row);
           }
           ++issued;
@@ -246,14 +267,14 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         const int t = u / splits, sp = u - t * splits;
         (void)t;
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        const int acc = kNumAcc == 2 ? (local & 1) : 0;
+        const uint32_t acc_phase = kNumAcc == 2 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, err)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * kAccCols;
         bool ok = true;
         for (int it = 0; it < kb1 - kb0; ++it) {
           if (!mbar_wait(kQuant ? &dq_bar[stage] : &full_bar[stage], phase, err)) {
@@ -262,13 +283,16 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           }
           tc_fence_after();
           const uint32_t spa = smem_u32(smem + stage * S::kStageBytes);
-          const uint64_t adesc = umma_desc_sw128(spa);
           const uint64_t bdesc = umma_desc_sw128(spa + S::kPBytes);
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             // +32 bytes per K=16 step inside the 128-byte swizzle row.
-            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
-                     (it > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {
+              const uint64_t adesc = umma_desc_sw128(spa + h * S::kHalfBytes);
+              umma_f16(d_tmem + h * kHalfCols, adesc + (uint64_t)(2 * k),
+                       bdesc + (uint64_t)(2 * k), idesc, (it > 0 || k > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -298,7 +322,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
       const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
       const int nk = kb1 - kb0;
-      const int rot = kb_rotation(t, nk);
+      const int rot = kb_rotation(t, nk, num_m);
       for (int it = 0; it < nk; ++it) {
         const int kb = kb0 + (it + rot) % nk;
         if (!mbar_wait(&full_bar[stage], phase, err)) {
@@ -330,43 +354,48 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
     const int etid = threadIdx.x - 64;  // 0..127
-    constexpr int CW = BN >= 32 ? 32 : 16;  // columns per tcgen05.ld
+    constexpr int CW = BN % 32 == 0 ? 32 : 16;  // columns per tcgen05.ld
+    static_assert(BN % CW == 0, "tile width must be a multiple of 16");
     const float out_scale = wq.out_scale;
     int local = 0;
     for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x, ++local) {
       const int t = u / splits, sp = u - t * splits;
-      const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const UnitCoord uc = unit_coord<BN, BMT>(t, num_m, num_n, grp, p_rows, q_rows);
+      const int acc = kNumAcc == 2 ? (local & 1) : 0;
+      const uint32_t acc_phase = kNumAcc == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      const int i = uc.out_i0 + row_in_tile;  // output index along P
+      const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols;
       const bool split = splits > 1;
-      // Tile-local fp32 partials of this unit: ws[(t * splits + s)][row][col].
-      float* ws_tile = split ? ws + (size_t)t * splits * (BM * BN) : nullptr;
+      // Tile-local fp32 partials of this unit: ws[(t * splits + s)][h][col][row].
+      float* ws_tile = split ? ws + (size_t)t * splits * (BMT * BN) : nullptr;
 
       if (split) {
-        // Column-group-major layout [BN/4][BM] of float4: the 32 lanes of a
-        // warp (consecutive rows) write 512 contiguous bytes per store.
-        float4* mine = reinterpret_cast<float4*>(ws_tile + (size_t)sp * (BM * BN)) + row_in_tile;
+        // Column-group-major layout [BN/4][BM] of float4 per M half: the 32
+        // lanes of a warp (consecutive rows) write 512 contiguous bytes per store.
 #pragma unroll 1
-        for (int ch = 0; ch < BN / CW; ++ch) {
-          uint32_t r[32];
-          if constexpr (CW == 32) {
-            tmem_ld_32x32b_x32(t_row + ch * CW, r);
-          } else {
-            tmem_ld_32x32b_x16(t_row + ch * CW, *reinterpret_cast<uint32_t(*)[16]>(r));
-          }
-          tmem_wait_ld();
+        for (int h = 0; h < MH; ++h) {
+          float4* mine = reinterpret_cast<float4*>(ws_tile + (size_t)sp * (BMT * BN) +
+                                                   (size_t)h * (BM * BN)) + row_in_tile;
+          const uint32_t t_row = t_acc + h * kHalfCols;
+#pragma unroll 1
+          for (int ch = 0; ch < BN / CW; ++ch) {
+            uint32_t r[32];
+            if constexpr (CW == 32) {
+              tmem_ld_32x32b_x32(t_row + ch * CW, r);
+            } else {
+              tmem_ld_32x32b_x16(t_row + ch * CW, *reinterpret_cast<uint32_t(*)[16]>(r));
+            }
+            tmem_wait_ld();
 #pragma unroll
-          for (int v = 0; v < CW / 4; ++v)
-            __stcg(mine + (size_t)(ch * (CW / 4) + v) * BM,
-                   make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+            for (int v = 0; v < CW / 4; ++v)
+              __stcg(mine + (size_t)(ch * (CW / 4) + v) * BM,
+                     make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+          }
         }
         // The accumulator is in global memory now: release TMEM early.
         tc_fence_before();
@@ -387,6 +416,11 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         __threadfence();
       }
 
+#pragma unroll 1
+      for (int h = 0; h < MH; ++h) {
+      const uint32_t t_row = t_acc + h * kHalfCols;
+      const int i = uc.out_i0 + h * BM + row_in_tile;  // output index along P
+      const float* ws_half = split ? ws_tile + (size_t)h * (BM * BN) : nullptr;
       // Fetch 32 (or 16) tile columns of this thread's row: from TMEM, or the
       // fixed-order (split 0, 1, ...) sum of the partials.
       auto fetch = [&](int col0, float (&v)[32]) {
@@ -413,7 +447,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             for (int j = 0; j < RG; ++j) {
               if (s0 + j < splits) {
                 const float4* src =
-                    reinterpret_cast<const float4*>(ws_tile + (size_t)(s0 + j) * (BM * BN)) +
+                    reinterpret_cast<const float4*>(ws_half + (size_t)(s0 + j) * (BMT * BN)) +
                     (size_t)(col0 / 4) * BM + row_in_tile;
 #pragma unroll
                 for (int c4 = 0; c4 < CW / 4; ++c4) x[j][c4] = __ldcg(src + (size_t)c4 * BM);
@@ -502,6 +536,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           }
         }
       }
+      }  // M halves
       if (!split) {
         tc_fence_before();
         __syncwarp();
@@ -528,13 +563,14 @@ struct SplitWorkspace {
 };
 SplitWorkspace g_split_ws[64];
 
-template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16>
+template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1>
 void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, int K, int ldp,
                 int ldq, int ldc, int splits, float* ws, int* counters, unsigned int* err,
                 cudaStream_t stream, const WQParams& wq = WQParams{},
                 const GroupInfo& grp = GroupInfo{}, int grid_units = 0) {
-  using S = Smem<BN, STAGES, WF>;
-  auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI, WF>;
+  using S = Smem<BN, STAGES, WF, MH>;
+  static_assert(S::kTotal <= 232448, "shared memory budget");
+  auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI, WF, MH>;
   static bool attr_set = false;  // per instantiation; idempotent if raced
   if (!attr_set) {
     cudaError_t e =
@@ -558,7 +594,8 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   int dev = 0;
   cudaGetDevice(&dev);
   const long units = grid_units > 0 ? grid_units
-                                    : (long)((p_rows + BM - 1) / BM) * ((q_rows + BN - 1) / BN) * splits;
+                                    : (long)((p_rows + BM * MH - 1) / (BM * MH)) *
+                                          ((q_rows + BN - 1) / BN) * splits;
   const int grid = units < num_sms(dev) ? (int)units : num_sms(dev);
   WQParams q = wq;
   if (WF == kWBf16) q.out_scale = 1.f;
@@ -573,14 +610,20 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
 struct CfgInfo {
   int bn;
   bool swap;
+  int mh;  // 128-row M halves per tile (2 = 256-row tall tile)
 };
 constexpr CfgInfo kCfgInfo[kCfgCount] = {
-    {256, false}, {128, false}, {16, true}, {32, true}, {64, true},
-    {192, false}, {96, false},  {64, false}, {128, true},
+    {256, false, 1}, {128, false, 1}, {16, true, 1},  {32, true, 1},   {64, true, 1},
+    {192, false, 1}, {96, false, 1},  {64, false, 1}, {128, true, 1},  {256, false, 2},
+    {224, false, 2}, {128, false, 2}, {112, false, 2}, {64, false, 2},
 };
 
 int cfg_bn(int cfg) { return (cfg >= 0 && cfg < kCfgCount) ? kCfgInfo[cfg].bn : 0; }
 bool cfg_swap(int cfg) { return cfg >= 0 && cfg < kCfgCount && kCfgInfo[cfg].swap; }
+int cfg_mh(int cfg) { return (cfg >= 0 && cfg < kCfgCount) ? kCfgInfo[cfg].mh : 1; }
+bool cfg_silu_ok(int cfg) {
+  return cfg == kCfgN256 || cfg == kCfgN128 || cfg == kCfgM2N256 || cfg == kCfgM2N128;
+}
 
 // Tuned dispatch table: (M, N, K, epi) -> plan, filled by the warm-up tuner
 // or imported from a LUT file; consulted before the cost model.
@@ -601,6 +644,7 @@ std::unordered_map<PlanKey, GemmPlan, PlanKeyHash> g_plans;
 }  // namespace
 
 int gemm_cfg_tile_n(int cfg) { return cfg_bn(cfg); }
+int gemm_cfg_tile_m(int cfg) { return 128 * cfg_mh(cfg); }
 bool gemm_cfg_is_swap(int cfg) { return cfg_swap(cfg); }
 
 GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
@@ -610,18 +654,28 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
     if (it != g_plans.end()) return it->second;
   }
   // Candidate tile shapes: swap-AB (weights on the 128-row side) for small M.
-  int cands[8];
+  int cands[12];
   int nc = 0;
   if (epi == kEpiNone && M <= 64) {
     cands[nc++] = M <= 16 ? kCfgSwap16 : (M <= 32 ? kCfgSwap32 : kCfgSwap64);
   } else if (epi == kEpiSiluMul) {
     cands[nc++] = kCfgN256;
     cands[nc++] = kCfgN128;
+    if (M > 128) {
+      cands[nc++] = kCfgM2N256;
+      cands[nc++] = kCfgM2N128;
+    }
   } else {
     cands[nc++] = kCfgN256;
     cands[nc++] = kCfgN192;
     cands[nc++] = kCfgN128;
     cands[nc++] = kCfgN96;
+    if (M > 128) {
+      cands[nc++] = kCfgM2N256;
+      cands[nc++] = kCfgM2N224;
+      cands[nc++] = kCfgM2N128;
+      cands[nc++] = kCfgM2N112;
+    }
   }
   const int num_kb = (K + 63) / 64;
   GemmPlan best{cands[0], 1};
@@ -630,19 +684,23 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
     const int cfg = cands[ci];
     const int bn = cfg_bn(cfg);
     const bool swap = cfg_swap(cfg);
+    const int mh = cfg_mh(cfg);
     const long p = swap ? N : M, qq = swap ? M : N;
-    const long tiles = ((p + 127) / 128) * ((qq + bn - 1) / bn);
+    const long tiles = ((p + 128 * mh - 1) / (128 * mh)) * ((qq + bn - 1) / bn);
     for (int s = 1; s <= kMaxSplits; ++s) {
       const int kb_per = (num_kb + s - 1) / s;
       if (s > 1 && kb_per < 4) break;
       const long units = tiles * s;
       const long waves = (units + num_sm - 1) / num_sm;
-      // Relative cost model: MMA time per k-block grows with BN, plus a fixed
-      // per-k-block latency share (operand traffic), per-unit prologue /
+      // Relative cost model: a k-block costs the larger of its MMA time
+      // (grows with the tile area) and its operand load time (grows with the
+      // rows loaded), plus a fixed latency share, per-unit prologue /
       // epilogue, and the split partial-sum round trips.
-      const double per_kb = bn / 256.0 + 0.35;
-      double t_unit = kb_per * per_kb + 3.0;
-      if (s > 1) t_unit += 4.0 + ((s + 3) / 4) * (bn / 256.0) * 2.0;
+      const double mma = mh * bn / 256.0;
+      const double load = (128.0 * mh + bn) / 384.0 * 0.8;
+      const double per_kb = (mma > load ? mma : load) + 0.25;
+      double t_unit = kb_per * per_kb + 3.0 * mh;
+      if (s > 1) t_unit += 4.0 + ((s + 3) / 4) * (mh * bn / 256.0) * 2.0;
       const double cost = waves * t_unit;
       if (cost < best_cost * 0.97) {
         best_cost = cost;
@@ -722,16 +780,17 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
   }
   if (splits <= 0) splits = 1;
   if (splits > kMaxSplits) splits = kMaxSplits;
-  if (epi == kEpiSiluMul && cfg != kCfgN256 && cfg != kCfgN128) cfg = kCfgN128;
+  if (epi == kEpiSiluMul && !cfg_silu_ok(cfg)) cfg = kCfgN128;
   const int bn = cfg_bn(cfg);
   if (bn == 0) throw std::runtime_error("gemm_bf16: unknown config " + std::to_string(cfg));
   const bool swap = cfg_swap(cfg);
+  const int bmt = 128 * cfg_mh(cfg);
   const long p = swap ? N : M, qq = swap ? M : N;
-  const long tiles = ((p + 127) / 128) * ((qq + bn - 1) / bn);
+  const long tiles = ((p + bmt - 1) / bmt) * ((qq + bn - 1) / bn);
   const int num_kb = (K + 63) / 64;
   if (splits > num_kb) splits = num_kb;
   if (splits > 1) {
-    const size_t need = (size_t)tiles * splits * 128 * bn * sizeof(float);
+    const size_t need = (size_t)tiles * splits * bmt * bn * sizeof(float);
     if (ws == nullptr || need > ws_bytes || tiles > n_counters) splits = 1;  // no room: no split
   }
   float* wsp = splits > 1 ? ws : nullptr;
@@ -741,12 +800,21 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
     if (cfg == kCfgN256)
       return launch_cfg<256, 4, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp,
                                                     cnt, err, stream);
+    if (cfg == kCfgM2N256)
+      return launch_cfg<256, 3, false, kEpiSiluMul, kWBf16, 2>(A, W, C, M, N, K, lda, ldw, ldc,
+                                                               splits, wsp, cnt, err, stream);
+    if (cfg == kCfgM2N128)
+      return launch_cfg<128, 4, false, kEpiSiluMul, kWBf16, 2>(A, W, C, M, N, K, lda, ldw, ldc,
+                                                               splits, wsp, cnt, err, stream);
     return launch_cfg<128, 6, false, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp,
                                                   cnt, err, stream);
   }
 #define B200_NORMAL(BN_, ST_) \
   return launch_cfg<BN_, ST_, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, \
                                                err, stream)
+#define B200_TALL(BN_, ST_) \
+  return launch_cfg<BN_, ST_, false, kEpiNone, kWBf16, 2>(A, W, C, M, N, K, lda, ldw, ldc, splits, \
+                                                          wsp, cnt, err, stream)
 #define B200_SWAP(BN_, ST_) \
   return launch_cfg<BN_, ST_, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt, \
                                               err, stream)
@@ -760,7 +828,13 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
     case kCfgSwap32: B200_SWAP(32, 8);
     case kCfgSwap64: B200_SWAP(64, 8);
     case kCfgSwap128: B200_SWAP(128, 6);
+    case kCfgM2N256: B200_TALL(256, 3);
+    case kCfgM2N224: B200_TALL(224, 3);
+    case kCfgM2N128: B200_TALL(128, 4);
+    case kCfgM2N112: B200_TALL(112, 4);
+    case kCfgM2N64: B200_TALL(64, 5);
   }
+#undef B200_TALL
 #undef B200_NORMAL
 #undef B200_SWAP
 }

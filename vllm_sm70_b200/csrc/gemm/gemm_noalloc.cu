@@ -97,8 +97,9 @@ extern "C" int b200_gemm_bf16_noalloc(const void* A, int lda, const void* W, int
     if (splits > 1) {
       const bool swap = b200::gemm_cfg_is_swap(cfg);
       const long p = swap ? N : M, q = swap ? M : N;
-      const long tiles = ((p + 127) / 128) * ((q + bn - 1) / bn);
-      const size_t need = (size_t)tiles * splits * 128 * bn * sizeof(float);
+      const int bm = b200::gemm_cfg_tile_m(cfg);
+      const long tiles = ((p + bm - 1) / bm) * ((q + bn - 1) / bn);
+      const size_t need = (size_t)tiles * splits * bm * bn * sizeof(float);
       if (need > B200_NOALLOC_WS_BYTES || tiles > B200_NOALLOC_MAX_TILES) {
         std::snprintf(g_last_error, sizeof(g_last_error),
                       "split-K scratch too small: need %zu bytes / %ld tiles, static limit %u bytes "

@@ -32,21 +32,26 @@ from .. import _ext, envs
 logger = logging.getLogger("vllm.b200.warmup")
 
 EPI_NONE, EPI_SILU = 0, 1
-# (cfg id, BN, swap)
-CFGS = {0: (256, False), 1: (128, False), 2: (16, True), 3: (32, True), 4: (64, True),
-        5: (192, False), 6: (96, False), 7: (64, False), 8: (128, True)}
+# cfg id -> (BN, swap, BM); BM 256 = tall tile (two M=128 accumulators)
+CFGS = {0: (256, False, 128), 1: (128, False, 128), 2: (16, True, 128), 3: (32, True, 128),
+        4: (64, True, 128), 5: (192, False, 128), 6: (96, False, 128), 7: (64, False, 128),
+        8: (128, True, 128), 9: (256, False, 256), 10: (224, False, 256), 11: (128, False, 256),
+        12: (112, False, 256), 13: (64, False, 256)}
+SILU_CFGS = (0, 1, 9, 11)
 SPLITS = (1, 2, 3, 4, 6, 8)
 
 
 def candidates(M: int, N: int, K: int, epi: int) -> list[tuple[int, int]]:
     out = []
     nkb = (K + 63) // 64
-    for cfg, (bn, swap) in CFGS.items():
-        if epi == EPI_SILU and cfg not in (0, 1):
+    for cfg, (bn, swap, bm) in CFGS.items():
+        if epi == EPI_SILU and cfg not in SILU_CFGS:
             continue
         if swap and (M > 128 or bn < min(M, 128) or (bn > 16 and bn // 2 >= M)):
             continue
         if not swap and M <= 16:
+            continue
+        if bm == 256 and M <= 128:
             continue
         for s in SPLITS:
             if s > 1 and (nkb + s - 1) // s < 4:

@@ -81,23 +81,30 @@ def _setup():
     linear.configure_workspace(dev)
 
 
-def bench_gemm(M, N, K, cfg=-1, splits=0, iters=20, flush=False, cublas=True):
+def bench_gemm(M, N, K, cfg=-1, splits=0, iters=20, flush=False, cublas=True, epi=0):
+    """epi 1: fused SiLU(gate)*up epilogue (N interleaved gate/up rows, N/2 outputs)."""
     from ..ops import linear
 
     a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
-    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    ms = time_fn(lambda: linear.gemm(a, w, out=out, cfg=cfg, splits=splits), iters, flush=flush)
+    out = torch.empty(M, N // 2 if epi else N, device="cuda", dtype=torch.bfloat16)
+    if epi:
+        fn = lambda: torch.ops._b200_C.gemm_bf16_silu_mul_out(out, a, w, cfg)  # noqa: E731
+    else:
+        fn = lambda: linear.gemm(a, w, out=out, cfg=cfg, splits=splits)  # noqa: E731
+    ms = time_fn(fn, iters, flush=flush)
     pk = peaks()
     flops = 2.0 * M * N * K
     byts = 2.0 * (M * K + N * K + M * N)
-    res = {"kernel": "gemm_bf16", "M": M, "N": N, "K": K, "plan": linear.plan(M, N, K),
+    res = {"kernel": "gemm_bf16_silu" if epi else "gemm_bf16", "M": M, "N": N, "K": K,
+           "plan": linear.plan(M, N, K, epi),
            "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1),
            "gbs": round(byts / ms / 1e6, 1),
            "frac_tensor": round(flops / ms / 1e9 / pk["bf16_tflops"], 3),
            "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}
     if cublas:
-        ms2 = time_fn(lambda: torch.matmul(a, w.t(), out=out), iters, flush=flush)
+        full = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ms2 = time_fn(lambda: torch.matmul(a, w.t(), out=full), iters, flush=flush)
         res["cublas_ms"] = round(ms2, 5)
         res["vs_cublas"] = round(ms2 / ms, 3)
     return res
@@ -149,7 +156,8 @@ def bench_prefill_attn(seqs=16, length=1024, hq=32, hkv=8, d=128, bs=16, iters=1
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "decode-attn", "prefill-attn", "all"])
+    ap.add_argument("case", choices=["gemm", "gemm-cublas", "decode-attn", "prefill-attn",
+                                     "all"])
     ap.add_argument("--M", type=int, default=256)
     ap.add_argument("--N", type=int, default=6144)
     ap.add_argument("--K", type=int, default=4096)
@@ -163,20 +171,32 @@ def main(argv=None):
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="gemm: time every (cfg, splits)")
+    ap.add_argument("--epi", type=int, default=0, help="gemm: 1 = fused SiLU*up epilogue")
     args = ap.parse_args(argv)
     _setup()
     out = []
     if args.case == "gemm" and args.sweep:
         from ..engine import warmup
 
-        for cfg, sp in warmup.candidates(args.M, args.N, args.K, 0):
-            r = bench_gemm(args.M, args.N, args.K, cfg, sp, args.iters, args.flush, False)
+        for cfg, sp in warmup.candidates(args.M, args.N, args.K, args.epi):
+            if args.epi and sp > 1:
+                continue  # the silu op takes no split override
+            r = bench_gemm(args.M, args.N, args.K, cfg, sp, args.iters, args.flush, False,
+                           args.epi)
             r["cfg"], r["splits"] = cfg, sp
             out.append(r)
-        out.append(bench_gemm(args.M, args.N, args.K, -1, 0, args.iters, args.flush, True))
+        out.append(bench_gemm(args.M, args.N, args.K, -1, 0, args.iters, args.flush, True,
+                              args.epi))
     elif args.case == "gemm":
         out.append(bench_gemm(args.M, args.N, args.K, args.cfg, args.splits, args.iters,
-                              args.flush, not args.no_cublas))
+                              args.flush, not args.no_cublas, args.epi))
+    elif args.case == "gemm-cublas":
+        a = torch.randn(args.M, args.K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(args.N, args.K, device="cuda", dtype=torch.bfloat16)
+        o = torch.empty(args.M, args.N, device="cuda", dtype=torch.bfloat16)
+        ms = time_fn(lambda: torch.matmul(a, w.t(), out=o), args.iters, flush=args.flush)
+        out.append({"kernel": "cublas_bf16", "M": args.M, "N": args.N, "K": args.K,
+                    "ms": round(ms, 5), "tflops": round(2.0 * args.M * args.N * args.K / ms / 1e9, 1)})
     elif args.case == "decode-attn":
         out.append(bench_decode_attn(args.batch, args.ctx, splits=max(1, args.splits),
                                      iters=args.iters))
