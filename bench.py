@@ -306,7 +306,11 @@ def main(argv=None):
     ap.add_argument("--requests", type=int, default=None, help="profiling only")
     ap.add_argument("--prompt-len", type=int, default=None, help="profiling only")
     ap.add_argument("--output-len", type=int, default=None, help="profiling only")
+    ap.add_argument("--verbose", action="store_true", help="log engine set-up (GEMM plans)")
     args = ap.parse_args(argv)
+    if args.verbose:
+        import logging
+        logging.basicConfig(level=logging.INFO, stream=sys.stderr)
     global N_REQ, PROMPT, OUT
     if args.requests or args.prompt_len or args.output_len:
         N_REQ = args.requests or N_REQ

@@ -8,7 +8,11 @@ pytestmark = pytest.mark.gpu
 
 CFGS = {"n256": 0, "n128": 1, "swap16": 2, "swap32": 3, "swap64": 4, "n192": 5, "n96": 6,
         "n64": 7, "swap128": 8, "m2n256": 9, "m2n224": 10, "m2n128": 11, "m2n112": 12,
-        "m2n64": 13}
+        "m2n64": 13, "cl_n256": 14, "cl_n128": 15, "cl_m2n128": 16, "cl_m2n112": 17,
+        "cl_m2n64": 18, "p2n256": 19, "p2n128": 20, "p2n192": 21, "p2n64": 22}
+# cluster split-K config -> the plain tile of the same shape (same summation order)
+CL_PLAIN = {"cl_n256": "n256", "cl_n128": "n128", "cl_m2n128": "m2n128", "cl_m2n112": "m2n112",
+            "cl_m2n64": "m2n64"}
 
 
 def _ref(a, w):
@@ -55,7 +59,7 @@ def test_gemm_silu_mul(b200_ops, M, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
-@pytest.mark.parametrize("cfg", [0, 1, 9, 11])
+@pytest.mark.parametrize("cfg", [0, 1, 9, 11, 19, 20])
 @pytest.mark.parametrize("M", [200, 256, 777])
 def test_gemm_silu_mul_configs(b200_ops, cfg, M, rel_err):
     torch.manual_seed(6)
@@ -97,6 +101,68 @@ def test_gemm_split_k(b200_ops, cfg, splits, rel_err):
     assert rel_err(outs[0], ref) < 1e-2
     # Fixed-order reduction: bitwise identical across calls (counters re-arm).
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+@pytest.mark.parametrize("cfg", ["p2n256", "p2n128", "p2n192", "p2n64"])
+@pytest.mark.parametrize("M,N,K", [(256, 1024, 4096), (300, 640, 520), (1024, 2048, 1024),
+                                   (128, 256, 64), (777, 1536, 2048)])
+def test_gemm_cta_pair(b200_ops, cfg, M, N, K, rel_err):
+    torch.manual_seed(9)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    out = linear.gemm(a, w, cfg=CFGS[cfg], splits=1)
+    torch.cuda.synchronize()
+    assert rel_err(out, _ref(a, w)) < 1e-2, (cfg, M, N, K)
+
+
+@pytest.mark.parametrize("cfg", ["p2n256", "p2n128"])
+@pytest.mark.parametrize("splits", [2, 3, 8])
+def test_gemm_cta_pair_split_k(b200_ops, cfg, splits, rel_err):
+    torch.manual_seed(10)
+    M, N, K = 256, 1536, 4096 + 64
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    outs = [linear.gemm(a, w, cfg=CFGS[cfg], splits=splits) for _ in range(2)]
+    torch.cuda.synchronize()
+    assert rel_err(outs[0], _ref(a, w)) < 1e-2
+    assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("cfg", list(CL_PLAIN))
+@pytest.mark.parametrize("splits", [2, 3, 5, 8])
+@pytest.mark.parametrize("M", [256, 200, 64])
+def test_gemm_cluster_split_matches_workspace_split(b200_ops, cfg, splits, M, rel_err):
+    torch.manual_seed(7)
+    N, K = 1024 + 128, 4096 + 64
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    outs = [linear.gemm(a, w, cfg=CFGS[cfg], splits=splits) for _ in range(2)]
+    plain = linear.gemm(a, w, cfg=CFGS[CL_PLAIN[cfg]], splits=splits)
+    torch.cuda.synchronize()
+    assert rel_err(outs[0], _ref(a, w)) < 1e-2
+    # DSMEM reduction sums the splits in the same fixed order as the workspace path.
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0], plain)
+
+
+@pytest.mark.parametrize("cfg", [14, 16])
+@pytest.mark.parametrize("splits", [2, 4])
+def test_gemm_silu_cluster_split(b200_ops, cfg, splits, rel_err):
+    torch.manual_seed(8)
+    M, K, N = 256, 4096, 640
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wg = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    wu = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    wi = linear.interleave_gate_up(wg, wu)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    torch.ops._b200_C.gemm_set_plan(M, 2 * N, K, 1, cfg, splits)
+    try:
+        torch.ops._b200_C.gemm_bf16_silu_mul_out(out, a, wi, -1)
+    finally:
+        torch.ops._b200_C.gemm_set_plan(M, 2 * N, K, 1, -1, 0)
+    g = a.float() @ wg.float().t()
+    u = a.float() @ wu.float().t()
+    assert rel_err(out, g * torch.sigmoid(g) * u) < 2e-2
 
 
 def test_gemm_silu_split(b200_ops, rel_err):

@@ -83,6 +83,15 @@ void gemm_set_plan_op(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t cfg,
   gemm_set_plan((int)M, (int)N, (int)K, (int)epi, (int)cfg, (int)splits);
 }
 void gemm_clear_plans_op() { gemm_clear_plans(); }
+void gemm_set_timeline_op(const std::optional<at::Tensor>& buf) {
+  if (buf.has_value()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong, "timeline: int64 CUDA tensor");
+    c10::cuda::CUDAGuard g(buf->device());
+    gemm_set_timeline(reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>()));
+  } else {
+    gemm_set_timeline(nullptr);
+  }
+}
 std::vector<int64_t> gemm_export_plans_op() {
   auto v = gemm_export_plans();
   return std::vector<int64_t>(v.begin(), v.end());
@@ -571,6 +580,7 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("gemm_set_plan(int M, int N, int K, int epi, int cfg, int splits) -> ()",
         &b200::gemm_set_plan_op);
   m.def("gemm_clear_plans() -> ()", &b200::gemm_clear_plans_op);
+  m.def("gemm_set_timeline(Tensor? buf) -> ()", &b200::gemm_set_timeline_op);
   m.def("gemm_export_plans() -> int[]", &b200::gemm_export_plans_op);
   m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
   m.def("gemm_bf16_config(int M, int N, int K, int epi) -> int", &b200::gemm_bf16_config);

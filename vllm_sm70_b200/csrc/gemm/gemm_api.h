@@ -29,7 +29,20 @@ enum GemmConfig : int {
   kCfgM2N128 = 11, // 256 x 128
   kCfgM2N112 = 12, // 256 x 112
   kCfgM2N64 = 13,  // 256 x 64
-  kCfgCount = 14,
+  // Cluster split-K (the K slices of a tile form one cluster, reduced through
+  // distributed shared memory; needs splits >= 2, else runs as the plain tile):
+  kCfgClN256 = 14,   // 128 x 256
+  kCfgClN128 = 15,   // 128 x 128
+  kCfgClM2N128 = 16, // 256 x 128
+  kCfgClM2N112 = 17, // 256 x 112
+  kCfgClM2N64 = 18,  // 256 x 64
+  // CTA pairs (tcgen05 cta_group::2): one 256-row tile over two SMs, each
+  // holding 128 rows of A, half of B's rows and its half of the accumulator.
+  kCfgP2N256 = 19,   // 256 x 256, 6 stages
+  kCfgP2N128 = 20,   // 256 x 128, 8 stages
+  kCfgP2N192 = 21,   // 256 x 192, 7 stages
+  kCfgP2N64 = 22,    // 256 x 64, 10 stages
+  kCfgCount = 23,
 };
 
 constexpr int kMaxSplits = 8;
@@ -107,9 +120,27 @@ void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K
 
 int gemm_bf16_pick_config(int M, int N, int K, int epi, int num_sm);
 
+// Profiling aid: install (or with nullptr remove) a device buffer of
+// 16 x grid uint64 that the next GEMM launches fill with per-CTA %globaltimer
+// stamps (entry, set-up, first TMA, first stage ready, last MMA, first
+// accumulator, epilogue done, exit, then split-K epilogue phases).
+void gemm_set_timeline(unsigned long long* buf);
+
 // Tile width (N side of the accumulator) and swap-AB flag of a config (0 / false if unknown).
 int gemm_cfg_tile_n(int cfg);
 int gemm_cfg_tile_m(int cfg);  // 128 or 256 (tall tiles)
+
+// Tile geometry the launcher uses for (M, N, K, cfg, splits): rows per P
+// tile (swap-AB tiles are fitted to the SM count), tile count, and the fp32
+// split-K workspace it needs.
+struct SplitGeometry {
+  int tile_rows = 128;
+  long tiles = 0;
+  size_t ws_bytes = 0;
+  long counters = 0;  // arrival counters the split needs
+};
+SplitGeometry gemm_split_geometry(int M, int N, int K, int cfg, int splits, int num_sm);
+bool gemm_cfg_is_cluster(int cfg);  // split-K reduced in a cluster (no workspace)
 bool gemm_cfg_is_swap(int cfg);
 
 // Explicit-workspace variant: splits > 1 needs ws >= tiles*splits*128*BN*4

@@ -45,6 +45,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -96,9 +97,9 @@ struct UnitCoord {
   int p_lim, q_lim;    // exclusive bounds for out_i0 + i / out_j0 + j
 };
 
-template <int BN, int BMT = BM>
+template <int BN>
 __device__ __forceinline__ UnitCoord unit_coord(int t, int num_m, int num_n, const GroupInfo& g,
-                                                int p_rows, int q_rows) {
+                                                int p_rows, int q_rows, int p_stride = BM) {
   if (g.E > 0) {
     // Grouped (swap-AB): tiles are ordered expert by expert; within an expert,
     // weight-row blocks vary fastest.
@@ -122,8 +123,15 @@ __device__ __forceinline__ UnitCoord unit_coord(int t, int num_m, int num_n, con
     return u;
   }
   const TileCoord tc = tile_coord(t, num_m, num_n);
-  return UnitCoord{tc.mb * BMT, tc.nb * BN, tc.mb * BMT, tc.nb * BN, p_rows, q_rows};
+  return UnitCoord{tc.mb * p_stride, tc.nb * BN, tc.mb * p_stride, tc.nb * BN, p_rows, q_rows};
 }
+
+// Optional per-CTA timeline (profiling aid, off unless a buffer is installed
+// with gemm_set_timeline): 16 %globaltimer slots per CTA -- entry, set-up
+// done, first TMA issued, first operand stage ready, last MMA issued, first
+// accumulator ready, epilogue done, exit, then the split-K epilogue phases
+// (partial written, fenced).
+__device__ unsigned long long* g_gemm_timeline = nullptr;
 
 template <int BN, int STAGES, int WF = kWBf16, int MH = 1>
 struct Smem {
@@ -137,23 +145,35 @@ struct Smem {
   static constexpr int kTotal = kTileBytes + kBarBytes + 1024;  // +1024 for manual alignment
 };
 
-template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1>
+template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1, bool CL = false,
+          bool PAIR = false>
 __global__ void __launch_bounds__(WF == kWBf16 ? kThreads : kThreadsQ, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     const __grid_constant__ CUtensorMap tmap_q, __nv_bfloat16* __restrict__ C,
                     int ldc, int p_rows, int q_rows, int K, int splits, float* __restrict__ ws,
                     int* __restrict__ counters, unsigned int* err, const WQParams wq,
-                    const GroupInfo grp) {
+                    const GroupInfo grp, const int pm, const int pbox, const int qbox) {
+  unsigned long long* const tl = g_gemm_timeline;
+#define B200_TL(i) \
+  do { if (tl) tl[(size_t)blockIdx.x * 16 + (i)] = globaltimer(); } while (0)
+  if (threadIdx.x == 0) B200_TL(0);
   static_assert(WF == kWBf16 || SWAP, "quantised weights use the swap-AB (weight = P) form");
   static_assert(MH == 1 || (!SWAP && WF == kWBf16), "tall tiles: normal-mode bf16 only");
+  static_assert(!CL || (!SWAP && WF == kWBf16), "cluster split-K: normal-mode bf16 only");
+  static_assert(!PAIR || (!SWAP && WF == kWBf16 && MH == 1 && !CL), "CTA pair: plain bf16 tiles");
   constexpr bool kQuant = WF != kWBf16;
-  constexpr int BMT = BM * MH;  // P rows per tile
+  constexpr int BMT = BM * MH;  // P rows per tile (per CTA)
+  // CTA pair: the tile is 256 P rows x BN; this CTA loads P rows
+  // [rank * 128, +128) and Q rows [rank * BN/2, +BN/2) and holds its 128
+  // accumulator rows x BN in its own TMEM.
+  constexpr int QR = PAIR ? BN / 2 : BN;       // Q rows loaded by this CTA
+  constexpr int UT = PAIR ? 2 * BM : BMT;      // P rows per unit tile
   // TMEM columns: the MH accumulators of one tile sit kHalfCols apart; two
   // tiles' accumulators alternate when they fit.
   constexpr int kHalfCols = MH == 1 ? BN : (BN + 31) / 32 * 32;
   constexpr int kAccCols = MH == 1 ? BN : MH * kHalfCols;
   constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
-  using S = Smem<BN, STAGES, WF, MH>;
+  using S = Smem<QR, STAGES, WF, MH>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -169,7 +189,16 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int num_m = (p_rows + BMT - 1) / BMT;
+  const uint32_t prank = PAIR ? (cluster_ctarank() & 1u) : 0u;  // rank within the pair
+  const bool leader = prank == 0;
+  const int unit0 = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+  const int ustride = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+  // P rows per tile: BMT, or fewer (pm, a multiple of 8) for single-half bf16
+  // tiles so that the tile count fits the SM count; the MMA still runs
+  // M = 128 and the rows past pm (stale shared memory) are never stored.
+  const int p_rows_tile = (MH == 1 && !kQuant && grp.E == 0 && pm > 0 && pm < BM) ? pm : BM;
+  const int p_tile = PAIR ? UT : (MH == 1 ? p_rows_tile : BMT);  // P-row stride between tiles
+  const int num_m = (p_rows + p_tile - 1) / p_tile;
   const int num_n = (q_rows + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
@@ -188,7 +217,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], PAIR ? 8 : 4);  // pair: both CTAs' epilogue warps
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -199,13 +228,23 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     tma_prefetch_desc(&tmap_q);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // Pair: the peer's TMA completions and barrier arrivals target this CTA's
+  // barriers, so both CTAs' initialisation must be visible first.
+  if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) B200_TL(1);
+  bool cl_ok = false;  // cluster split: this epilogue thread's accumulator is ready
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -213,9 +252,9 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
-      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+      for (int u = unit0; u < num_units && !*abort_flag; u += ustride) {
         const int t = u / splits, sp = u - t * splits;
-        const UnitCoord uc = unit_coord<BN, BMT>(t, num_m, num_n, grp, p_rows, q_rows);
+        const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int nk = kb1 - kb0;
         const int rot = kb_rotation(t, nk, num_m);
@@ -234,13 +273,35 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             tma_load_2d(spp + S::kPBytes + S::kQBytes, &tmap_p, &full_bar[stage],
                         kb * raw_row_bytes(WF), uc.p_row);
           } else {
-            mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+            // Operand tiles go in pbox- / qbox-row TMA boxes (8-row multiples
+            // keep the 1024-byte swizzle atoms aligned).
+            if constexpr (PAIR) {
+              // Both CTAs' halves complete on the leader's barrier, which
+              // expects the bytes of the whole pair.
+              if (leader)
+                mbar_arrive_expect_tx(&full_bar[stage],
+                                      (uint32_t)(2 * (BM * BK * 2 + S::kQBytes)));
+              const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0u);
+              for (int r = 0; r < BM; r += pbox)
+                tma_load_2d_pair(spp + r * (BK * 2), &tmap_p, fb, kb * BK,
+                                 uc.p_row + (int)prank * BM + r);
+              for (int r = 0; r < QR; r += qbox)
+                tma_load_2d_pair(spp + S::kPBytes + r * (BK * 2), &tmap_q, fb, kb * BK,
+                                 uc.q_row + (int)prank * QR + r);
+            } else {
+              mbar_arrive_expect_tx(&full_bar[stage],
+                                    (uint32_t)(MH * p_rows_tile * BK * 2 + S::kQBytes));
 #pragma unroll
-            for (int h = 0; h < MH; ++h)
-              tma_load_2d(spp + h * S::kHalfBytes, &tmap_p, &full_bar[stage], kb * BK,
-                          uc.p_row + h * BM);
-            tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, uc.q_row);
+              for (int h = 0; h < MH; ++h)
+                for (int r = 0; r < p_rows_tile; r += pbox)
+                  tma_load_2d(spp + h * S::kHalfBytes + r * (BK * 2), &tmap_p, &full_bar[stage],
+                              kb * BK, uc.p_row + h * BM + r);
+              for (int r = 0; r < BN; r += qbox)
+                tma_load_2d(spp + S::kPBytes + r * (BK * 2), &tmap_q, &full_bar[stage], kb * BK,
+                            uc.q_row + r);
+            }
           }
+          if (issued == 0) B200_TL(2);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -249,7 +310,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         }
       }
       // Drain: wait for the copies this thread issued into each slot (bounded).
-      const long n_drain = issued < STAGES ? issued : STAGES;
+      // A pair's second CTA counts its copies on the leader's barriers; its
+      // operands are consumed (and so landed) before the leader's final
+      // commit, which this CTA waits for before tearing down.
+      const long n_drain = (PAIR && !leader) ? 0 : (issued < STAGES ? issued : STAGES);
       for (long j = 0; j < n_drain; ++j) {
         const long it = issued - 1 - j;
         mbar_wait(&full_bar[it % STAGES], (uint32_t)((it / STAGES) & 1), err);
@@ -258,12 +322,15 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(BM, BN, true);
+    if (lane == 0 && PAIR && !leader) {
+      // The leader issues the pair's MMAs; its final commit lands here too.
+      mbar_wait(done_bar, 0, err);
+    } else if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(PAIR ? 2 * BM : BM, BN, true);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x, ++local) {
+      for (int u = unit0; u < num_units && !*abort_flag; u += ustride, ++local) {
         const int t = u / splits, sp = u - t * splits;
         (void)t;
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
@@ -281,6 +348,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             ok = false;
             break;
           }
+          if (local == 0 && it == 0) B200_TL(3);
           tc_fence_after();
           const uint32_t spa = smem_u32(smem + stage * S::kStageBytes);
           const uint64_t bdesc = umma_desc_sw128(spa + S::kPBytes);
@@ -290,24 +358,33 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 #pragma unroll
             for (int h = 0; h < MH; ++h) {
               const uint64_t adesc = umma_desc_sw128(spa + h * S::kHalfBytes);
-              umma_f16(d_tmem + h * kHalfCols, adesc + (uint64_t)(2 * k),
-                       bdesc + (uint64_t)(2 * k), idesc, (it > 0 || k > 0) ? 1u : 0u);
+              if constexpr (PAIR) {
+                umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                              (it > 0 || k > 0) ? 1u : 0u);
+              } else {
+                umma_f16(d_tmem + h * kHalfCols, adesc + (uint64_t)(2 * k),
+                         bdesc + (uint64_t)(2 * k), idesc, (it > 0 || k > 0) ? 1u : 0u);
+              }
             }
           }
-          umma_commit(&empty_bar[stage]);
+          if constexpr (PAIR) umma_commit_pair(&empty_bar[stage], 0x3);
+          else umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        umma_commit(&tfull_bar[acc]);
+        if constexpr (PAIR) umma_commit_pair(&tfull_bar[acc], 0x3);
+        else umma_commit(&tfull_bar[acc]);
         if (!ok) {
           *abort_flag = 1;
           break;
         }
       }
+      B200_TL(4);
       // Make sure no MMA is still writing TMEM before it is freed.
-      umma_commit(done_bar);
+      if constexpr (PAIR) umma_commit_pair(done_bar, 0x3);
+      else umma_commit(done_bar);
       mbar_wait(done_bar, 0, err);
     }
     __syncwarp();
@@ -317,7 +394,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     const int c = dt & 7;              // 16-byte chunk (8 k) of the row
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+    for (int u = unit0; u < num_units && !*abort_flag; u += ustride) {
       const int t = u / splits, sp = u - t * splits;
       const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows);
       const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
@@ -349,6 +426,16 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         }
       }
     }
+  } else if constexpr (CL) {
+    // ------------------------------------------------------------ epilogue (cluster split)
+    // One unit per CTA: wait for the accumulator; the exchange and the
+    // reduction run after the role branches, where every thread of the
+    // cluster can join the cluster barriers.
+    if ((int)blockIdx.x < num_units && !*abort_flag) {
+      cl_ok = mbar_wait(&tfull_bar[0], 0, err);
+      if (!cl_ok) *abort_flag = 1;
+      else tc_fence_after();
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -358,28 +445,41 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     static_assert(BN % CW == 0, "tile width must be a multiple of 16");
     const float out_scale = wq.out_scale;
     int local = 0;
-    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x, ++local) {
+    for (int u = unit0; u < num_units && !*abort_flag; u += ustride, ++local) {
       const int t = u / splits, sp = u - t * splits;
-      const UnitCoord uc = unit_coord<BN, BMT>(t, num_m, num_n, grp, p_rows, q_rows);
+      const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
       const int acc = kNumAcc == 2 ? (local & 1) : 0;
       const uint32_t acc_phase = kNumAcc == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, err)) {
         *abort_flag = 1;
         break;
       }
+      if (local == 0 && threadIdx.x == 64) B200_TL(5);
       tc_fence_after();
       const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols;
       const bool split = splits > 1;
-      // Tile-local fp32 partials of this unit: ws[(t * splits + s)][h][col][row].
-      float* ws_tile = split ? ws + (size_t)t * splits * (BMT * BN) : nullptr;
+      // Tile-local fp32 partials of this unit: ws[(t * splits + s)][h][col][row]
+      // (a pair's CTAs own halves h = 0 / 1 and count arrivals separately).
+      float* ws_tile = split ? ws + (size_t)t * splits * (UT * BN) : nullptr;
+      const int hbase = PAIR ? (int)prank : 0;
+      // Release this accumulator buffer: a pair's MMA issuer sits in the leader.
+      auto release_acc = [&]() {
+        if constexpr (PAIR) {
+          if (leader) mbar_arrive(&tempty_bar[acc]);
+          else mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0u));
+        } else {
+          mbar_arrive(&tempty_bar[acc]);
+        }
+      };
 
       if (split) {
         // Column-group-major layout [BN/4][BM] of float4 per M half: the 32
         // lanes of a warp (consecutive rows) write 512 contiguous bytes per store.
 #pragma unroll 1
         for (int h = 0; h < MH; ++h) {
-          float4* mine = reinterpret_cast<float4*>(ws_tile + (size_t)sp * (BMT * BN) +
-                                                   (size_t)h * (BM * BN)) + row_in_tile;
+          float4* mine = reinterpret_cast<float4*>(ws_tile + (size_t)sp * (UT * BN) +
+                                                   (size_t)(hbase + h) * (BM * BN)) +
+                         row_in_tile;
           const uint32_t t_row = t_acc + h * kHalfCols;
 #pragma unroll 1
           for (int ch = 0; ch < BN / CW; ++ch) {
@@ -398,15 +498,18 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           }
         }
         // The accumulator is in global memory now: release TMEM early.
+        if (etid == 0) B200_TL(8);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (lane == 0) release_acc();
         __threadfence();
+        if (etid == 0) B200_TL(9);
         named_barrier_sync(1, 128);
         if (etid == 0) {
-          const int old = atomicAdd(&counters[t], 1);
+          const int ci = PAIR ? 2 * t + (int)prank : t;
+          const int old = atomicAdd(&counters[ci], 1);
           const int last = old == splits - 1;
-          if (last) counters[t] = 0;  // re-arm for the next launch
+          if (last) counters[ci] = 0;  // re-arm for the next launch
           *last_flag = last;
         }
         named_barrier_sync(1, 128);
@@ -419,8 +522,9 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 #pragma unroll 1
       for (int h = 0; h < MH; ++h) {
       const uint32_t t_row = t_acc + h * kHalfCols;
-      const int i = uc.out_i0 + h * BM + row_in_tile;  // output index along P
-      const float* ws_half = split ? ws_tile + (size_t)h * (BM * BN) : nullptr;
+      const int i = uc.out_i0 + (hbase + h) * BM + row_in_tile;  // output index along P
+      const bool row_ok = row_in_tile < p_rows_tile;
+      const float* ws_half = split ? ws_tile + (size_t)(hbase + h) * (BM * BN) : nullptr;
       // Fetch 32 (or 16) tile columns of this thread's row: from TMEM, or the
       // fixed-order (split 0, 1, ...) sum of the partials.
       auto fetch = [&](int col0, float (&v)[32]) {
@@ -447,7 +551,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             for (int j = 0; j < RG; ++j) {
               if (s0 + j < splits) {
                 const float4* src =
-                    reinterpret_cast<const float4*>(ws_half + (size_t)(s0 + j) * (BMT * BN)) +
+                    reinterpret_cast<const float4*>(ws_half + (size_t)(s0 + j) * (UT * BN)) +
                     (size_t)(col0 / 4) * BM + row_in_tile;
 #pragma unroll
                 for (int c4 = 0; c4 < CW / 4; ++c4) x[j][c4] = __ldcg(src + (size_t)c4 * BM);
@@ -481,7 +585,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             fetch(blk * 128 + half * 32, g);
             fetch(blk * 128 + 64 + half * 32, uu);
             const int j0 = (uc.q_row / BN) * (BN / 2) + blk * 64 + half * 32;
-            if (i < uc.p_lim) {
+            if (row_ok && i < uc.p_lim) {
               uint32_t packed[16];
 #pragma unroll
               for (int c = 0; c < 16; ++c) {
@@ -509,7 +613,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           fetch(ch * CW, r);
           const int j0 = uc.out_j0 + ch * CW;
           if constexpr (!SWAP) {
-            if (i < uc.p_lim) {
+            if (row_ok && i < uc.p_lim) {
               __nv_bfloat16* dst = C + (size_t)i * ldc + j0;
 #pragma unroll
               for (int v = 0; v < CW / 8; ++v) {
@@ -526,7 +630,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           } else {
             // Transposed store: lane i holds P row i (an output column);
             // consecutive lanes write consecutive bf16 of one output row.
-            if (i < uc.p_lim) {
+            if (row_ok && i < uc.p_lim) {
 #pragma unroll
               for (int c = 0; c < CW; ++c) {
                 const int j = j0 + c;
@@ -540,17 +644,138 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       if (!split) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (lane == 0) release_acc();
       }
     }
   }
 
+  if constexpr (CL) {
+    // -------------------------------------------------- cluster reduction
+    // Rows of the tile are dealt out to the cluster's CTAs (CTA d owns rows
+    // [d * R, (d + 1) * R)). Barrier 1: every CTA's MMAs are complete, so the
+    // operand rings (reused as receive buffers) are idle. Each epilogue thread
+    // then pushes its accumulator row straight from TMEM into the owner's
+    // receive slot [split][row] with remote shared-memory stores (posted: no
+    // round trip is exposed). Barrier 2: all rows have landed; each CTA sums
+    // its rows over the splits in split order (the workspace path's fixed
+    // order), applies the epilogue and stores bf16. No CTA touches another's
+    // shared memory after barrier 2, so exiting is safe.
+    constexpr int CW = BN % 32 == 0 ? 32 : 16;
+    constexpr int LDP = BN + 4;  // padded row (floats): conflict-free 16-byte accesses
+    static_assert((BMT + kMaxSplits) * LDP * 4 <= S::kTileBytes, "receive buffer exceeds the ring");
+    static_assert(EPI != kEpiSiluMul || BN % 128 == 0, "SiLU tiles hold whole gate/up blocks");
+    cluster_sync_all();
+    if (cl_ok && warp >= 2) {
+      const int q = warp & 3;
+      const int row_in_tile = q * 32 + lane;
+      const int nsplit = splits;
+      const int R = (BMT + nsplit - 1) / nsplit;
+      const uint32_t rank = cluster_ctarank();
+      const uint32_t recv = smem_u32(smem);
+#pragma unroll 1
+      for (int h = 0; h < MH; ++h) {
+        const int row = h * BM + row_in_tile;
+        const int dst_cta = row / R;
+        const uint32_t slot = (uint32_t)(((int)rank * R + (row - dst_cta * R)) * LDP);
+        const uint32_t dst = mapa_shared(recv + slot * 4u, (uint32_t)dst_cta);
+        const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + h * kHalfCols;
+#pragma unroll 1
+        for (int ch = 0; ch < BN / CW; ++ch) {
+          uint32_t r[32];
+          if constexpr (CW == 32) {
+            tmem_ld_32x32b_x32(t_row + ch * CW, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + ch * CW, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int v = 0; v < CW / 4; ++v)
+            st_dsmem_f4(dst + (uint32_t)((ch * CW + 4 * v) * 4),
+                        make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                    __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+        }
+      }
+    }
+    cluster_sync_all();
+    if (!*abort_flag && (int)blockIdx.x < num_units) {
+      constexpr int LDP = BN + 4;
+      const int nsplit = splits;
+      const int rank = (int)cluster_ctarank();
+      const int t = (int)blockIdx.x / nsplit;
+      const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
+      const int R = (BMT + nsplit - 1) / nsplit;
+      const int r0 = rank * R, r1 = min(BMT, r0 + R);
+      // Receive slots: split s's copy of owned row r sits at (s * R + r - r0).
+      const float* recv = reinterpret_cast<const float*>(smem);
+      if constexpr (EPI == kEpiSiluMul) {
+        // Columns hold [gate 64 | up 64] blocks: 16 output float4 groups per block.
+        constexpr int G4 = BN / 8;
+        const int out_j0 = (uc.q_row / BN) * (BN / 2);
+        const int out_cols = q_rows / 2;
+        for (int idx = threadIdx.x; idx < (r1 - r0) * G4; idx += blockDim.x) {
+          const int r = r0 + idx / G4;
+          const int o4 = idx % G4;
+          const int gcol = (o4 / 16) * 128 + (o4 % 16) * 4;
+          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), uu = g;
+#pragma unroll
+          for (int sidx = 0; sidx < kMaxSplits; ++sidx) {
+            if (sidx < nsplit) {
+              const float* rowp = recv + (size_t)(sidx * R + r - r0) * LDP;
+              const float4 a = *reinterpret_cast<const float4*>(rowp + gcol);
+              const float4 b = *reinterpret_cast<const float4*>(rowp + gcol + 64);
+              g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+              uu.x += b.x; uu.y += b.y; uu.z += b.z; uu.w += b.w;
+            }
+          }
+          const int i = uc.out_i0 + r;
+          const int j = out_j0 + (o4 / 16) * 64 + (o4 % 16) * 4;
+          if ((MH == 2 || r < p_rows_tile) && i < p_rows && j < out_cols) {
+            uint2 pk;
+            pk.x = pack_bf16x2(g.x / (1.0f + __expf(-g.x)) * uu.x, g.y / (1.0f + __expf(-g.y)) * uu.y);
+            pk.y = pack_bf16x2(g.z / (1.0f + __expf(-g.z)) * uu.z, g.w / (1.0f + __expf(-g.w)) * uu.w);
+            *reinterpret_cast<uint2*>(C + (size_t)i * ldc + j) = pk;
+          }
+        }
+      } else {
+        constexpr int G4 = BN / 4;
+        for (int idx = threadIdx.x; idx < (r1 - r0) * G4; idx += blockDim.x) {
+          const int r = r0 + idx / G4;
+          const int c4 = idx % G4;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int sidx = 0; sidx < kMaxSplits; ++sidx) {
+            if (sidx < nsplit) {
+              const float4 a = *reinterpret_cast<const float4*>(
+                  recv + (size_t)(sidx * R + r - r0) * LDP + c4 * 4);
+              acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+            }
+          }
+          const int i = uc.out_i0 + r;
+          const int j = uc.out_j0 + c4 * 4;
+          if ((MH == 2 || r < p_rows_tile) && i < p_rows && j < q_rows) {
+            uint2 pk;
+            pk.x = pack_bf16x2(acc.x, acc.y);
+            pk.y = pack_bf16x2(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(C + (size_t)i * ldc + j) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  if (threadIdx.x == 64) B200_TL(6);
   tc_fence_before();
   __syncthreads();
+  // Pair: no CTA may leave while its peer can still signal its barriers or
+  // read its shared memory; the TMEM release is collective over the pair.
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0) B200_TL(7);
+#undef B200_TL
 }
 
 // Process-wide split-K workspace per device (fp32 partial tiles + arrival
@@ -563,12 +788,29 @@ struct SplitWorkspace {
 };
 SplitWorkspace g_split_ws[64];
 
+// Rows per TMA box for the bf16 operands (VLLM_B200_GEMM_TMA_BOX; 0 = whole tile).
+int tma_box_rows() {
+  static const int v = [] {
+    const char* e = std::getenv("VLLM_B200_GEMM_TMA_BOX");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1>
 void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, int K, int ldp,
                 int ldq, int ldc, int splits, float* ws, int* counters, unsigned int* err,
                 cudaStream_t stream, const WQParams& wq = WQParams{},
-                const GroupInfo& grp = GroupInfo{}, int grid_units = 0) {
+                const GroupInfo& grp = GroupInfo{}, int grid_units = 0, int pm = BM) {
   using S = Smem<BN, STAGES, WF, MH>;
+  if (MH != 1 || WF != kWBf16 || grp.E > 0 || pm <= 0 || pm > BM) pm = BM;
+  // TMA box rows per operand (bf16 operands only; 0 = one box per tile).
+  int pbox = pm, qbox = BN;
+  if (WF == kWBf16) {
+    const int want = tma_box_rows();
+    if (want > 0 && pm % want == 0) pbox = want;
+    if (want > 0 && BN % want == 0) qbox = want;
+  }
   static_assert(S::kTotal <= 232448, "shared memory budget");
   auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI, WF, MH>;
   static bool attr_set = false;  // per instantiation; idempotent if raced
@@ -581,7 +823,7 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   }
   CUtensorMap tp;
   if constexpr (WF == kWBf16) {
-    tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, K, (uint64_t)ldp * 2, BM,
+    tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, K, (uint64_t)ldp * 2, pbox,
                       BK);
   } else {
     // Raw quantised rows: K * bytes-per-element bytes, box = 128 rows x one k-block.
@@ -590,39 +832,167 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
                       (uint64_t)ldp, BM, rb, CU_TENSOR_MAP_SWIZZLE_NONE);
   }
   CUtensorMap tq = make_tmap_2d(Q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, K,
-                                (uint64_t)ldq * 2, BN, BK);
+                                (uint64_t)ldq * 2, qbox, BK);
   int dev = 0;
   cudaGetDevice(&dev);
+  const int p_stride = MH == 1 ? pm : BM * MH;
   const long units = grid_units > 0 ? grid_units
-                                    : (long)((p_rows + BM * MH - 1) / (BM * MH)) *
+                                    : (long)((p_rows + p_stride - 1) / p_stride) *
                                           ((q_rows + BN - 1) / BN) * splits;
   const int grid = units < num_sms(dev) ? (int)units : num_sms(dev);
   WQParams q = wq;
   if (WF == kWBf16) q.out_scale = 1.f;
   kernel<<<grid, WF == kWBf16 ? kThreads : kThreadsQ, S::kTotal, stream>>>(
       tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits, ws, counters,
-      err, q, grp);
+      err, q, grp, pm, pbox, qbox);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc launch: ") + cudaGetErrorString(e));
 }
 
+// Cluster split-K: the `splits` K-slices of a tile run as one thread-block
+// cluster (one tile-split per CTA, grid = tiles * splits) and reduce through
+// distributed shared memory; no workspace or counters.
+template <int BN, int STAGES, int EPI, int MH>
+void launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
+               int ldc, int splits, unsigned int* err, cudaStream_t stream) {
+  using S = Smem<BN, STAGES, kWBf16, MH>;
+  static_assert(S::kTotal <= 232448, "shared memory budget");
+  auto kernel = gemm_bf16_tc_kernel<BN, STAGES, false, EPI, kWBf16, MH, true>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    attr_set = true;
+  }
+  CUtensorMap tp = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, (uint64_t)lda * 2,
+                                BM, BK);
+  CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
+                                BN, BK);
+  const long tiles = (long)((M + BM * MH - 1) / (BM * MH)) * ((N + BN - 1) / BN);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)(tiles * splits), 1, 1);
+  lc.blockDim = dim3(kThreads, 1, 1);
+  lc.dynamicSmemBytes = S::kTotal;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
+                                     M, N, K, splits, (float*)nullptr, (int*)nullptr, err,
+                                     WQParams{}, GroupInfo{}, (int)BM, (int)BM, BN);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("gemm_bf16_tc cluster launch: ") + cudaGetErrorString(e));
+}
+
+// CTA pairs: cluster of 2, grid = 2 x min(units, SMs / 2), each pair
+// persistent over (256 x BN tile, split) units; split-K through the workspace
+// with one arrival counter per tile half (needs 2 x tiles counters).
+template <int BN, int STAGES, int EPI>
+void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
+                 int ldc, int splits, float* ws, int* counters, unsigned int* err,
+                 cudaStream_t stream) {
+  using S = Smem<BN / 2, STAGES, kWBf16, 1>;
+  static_assert(S::kTotal <= 232448, "shared memory budget");
+  auto kernel = gemm_bf16_tc_kernel<BN, STAGES, false, EPI, kWBf16, 1, false, true>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    attr_set = true;
+  }
+  CUtensorMap tp = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, (uint64_t)lda * 2,
+                                BM, BK);
+  CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
+                                BN / 2, BK);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long units = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * splits;
+  cudaLaunchConfig_t lc = {};
+  lc.blockDim = dim3(kThreads, 1, 1);
+  lc.dynamicSmemBytes = S::kTotal;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  // Pairs that can be resident at once (the GPC layout can leave SMs
+  // unpairable); the persistent grid never exceeds it, so every pair runs
+  // concurrently (the co-resident split-K reduction relies on it).
+  static int max_pairs[64] = {0};
+  if (max_pairs[dev] == 0) {
+    lc.gridDim = dim3((unsigned)(2 * (num_sms(dev) / 2)), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)kernel, &lc) != cudaSuccess || n <= 0)
+      n = num_sms(dev) / 2;
+    cudaGetLastError();
+    max_pairs[dev] = n < num_sms(dev) / 2 ? n : num_sms(dev) / 2;
+  }
+  const long pairs = units < max_pairs[dev] ? units : max_pairs[dev];
+  lc.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
+                                     M, N, K, splits, ws, counters, err, WQParams{}, GroupInfo{},
+                                     (int)BM, (int)BM, BN / 2);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("gemm_bf16_tc pair launch: ") + cudaGetErrorString(e));
+}
+
 struct CfgInfo {
   int bn;
   bool swap;
-  int mh;  // 128-row M halves per tile (2 = 256-row tall tile)
+  int mh;     // 128-row M halves per tile (2 = 256-row tall tile)
+  bool cl;    // split-K as a cluster with a distributed-shared-memory reduction
+  bool pair;  // CTA pair (cta_group::2): 256 x bn tile over two SMs
 };
 constexpr CfgInfo kCfgInfo[kCfgCount] = {
-    {256, false, 1}, {128, false, 1}, {16, true, 1},  {32, true, 1},   {64, true, 1},
-    {192, false, 1}, {96, false, 1},  {64, false, 1}, {128, true, 1},  {256, false, 2},
-    {224, false, 2}, {128, false, 2}, {112, false, 2}, {64, false, 2},
+    {256, false, 1, false, false}, {128, false, 1, false, false}, {16, true, 1, false, false},
+    {32, true, 1, false, false},   {64, true, 1, false, false},   {192, false, 1, false, false},
+    {96, false, 1, false, false},  {64, false, 1, false, false},  {128, true, 1, false, false},
+    {256, false, 2, false, false}, {224, false, 2, false, false}, {128, false, 2, false, false},
+    {112, false, 2, false, false}, {64, false, 2, false, false},  {256, false, 1, true, false},
+    {128, false, 1, true, false},  {128, false, 2, true, false},  {112, false, 2, true, false},
+    {64, false, 2, true, false},   {256, false, 1, false, true},  {128, false, 1, false, true},
+    {192, false, 1, false, true},  {64, false, 1, false, true},
 };
 
 int cfg_bn(int cfg) { return (cfg >= 0 && cfg < kCfgCount) ? kCfgInfo[cfg].bn : 0; }
+
+// Weight rows per swap-AB tile: the multiple of 8 in [32, 128] that minimises
+// waves x (rows + token tile) -- fewer rows per tile spread the weights over
+// more SMs when 128-row tiles would leave SMs idle or spill into a partial
+// wave (e.g. 4096 rows x 4 token tiles: 112 rows -> 148 tiles, one full wave).
+int swap_tile_rows(long p_rows, long q_tiles, int splits, int num_sm, int bn) {
+  int best = 128;
+  double best_cost = 1e30;
+  for (int pm = 128; pm >= 32; pm -= 8) {
+    const long units = ((p_rows + pm - 1) / pm) * q_tiles * splits;
+    const long waves = (units + num_sm - 1) / num_sm;
+    const double cost = (double)waves * (pm + bn);
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = pm;
+    }
+  }
+  return best;
+}
 bool cfg_swap(int cfg) { return cfg >= 0 && cfg < kCfgCount && kCfgInfo[cfg].swap; }
 int cfg_mh(int cfg) { return (cfg >= 0 && cfg < kCfgCount) ? kCfgInfo[cfg].mh : 1; }
+bool cfg_cl(int cfg) { return cfg >= 0 && cfg < kCfgCount && kCfgInfo[cfg].cl; }
+bool cfg_pair(int cfg) { return cfg >= 0 && cfg < kCfgCount && kCfgInfo[cfg].pair; }
 bool cfg_silu_ok(int cfg) {
-  return cfg == kCfgN256 || cfg == kCfgN128 || cfg == kCfgM2N256 || cfg == kCfgM2N128;
+  return cfg == kCfgN256 || cfg == kCfgN128 || cfg == kCfgM2N256 || cfg == kCfgM2N128 ||
+         cfg == kCfgClN256 || cfg == kCfgClM2N128 || cfg == kCfgP2N256 || cfg == kCfgP2N128;
 }
 
 // Tuned dispatch table: (M, N, K, epi) -> plan, filled by the warm-up tuner
@@ -644,7 +1014,31 @@ std::unordered_map<PlanKey, GemmPlan, PlanKeyHash> g_plans;
 }  // namespace
 
 int gemm_cfg_tile_n(int cfg) { return cfg_bn(cfg); }
-int gemm_cfg_tile_m(int cfg) { return 128 * cfg_mh(cfg); }
+
+void gemm_set_timeline(unsigned long long* buf) {
+  cudaError_t e = cudaMemcpyToSymbol(g_gemm_timeline, &buf, sizeof(buf));
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("gemm_set_timeline: ") + cudaGetErrorString(e));
+}
+int gemm_cfg_tile_m(int cfg) { return cfg_pair(cfg) ? 256 : 128 * cfg_mh(cfg); }
+
+SplitGeometry gemm_split_geometry(int M, int N, int K, int cfg, int splits, int num_sm) {
+  SplitGeometry g;
+  const int bn = cfg_bn(cfg);
+  const bool swap = cfg_swap(cfg);
+  const long p = swap ? N : M, qq = swap ? M : N;
+  const long q_tiles = bn > 0 ? (qq + bn - 1) / bn : 0;
+  g.tile_rows = gemm_cfg_tile_m(cfg);
+  if (swap && bn > 0) g.tile_rows = swap_tile_rows(p, q_tiles, splits, num_sm, bn);
+  g.tiles = ((p + g.tile_rows - 1) / g.tile_rows) * q_tiles;
+  // fp32 partials are stored for whole 128-row (or 256-row) MMA tiles; a CTA
+  // pair counts arrivals per tile half.
+  g.ws_bytes = (size_t)g.tiles * splits * gemm_cfg_tile_m(cfg) * bn * sizeof(float);
+  g.counters = cfg_pair(cfg) ? 2 * g.tiles : g.tiles;
+  (void)K;
+  return g;
+}
+bool gemm_cfg_is_cluster(int cfg) { return cfg_cl(cfg); }
 bool gemm_cfg_is_swap(int cfg) { return cfg_swap(cfg); }
 
 GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
@@ -654,7 +1048,7 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
     if (it != g_plans.end()) return it->second;
   }
   // Candidate tile shapes: swap-AB (weights on the 128-row side) for small M.
-  int cands[12];
+  int cands[24];
   int nc = 0;
   if (epi == kEpiNone && M <= 64) {
     cands[nc++] = M <= 16 ? kCfgSwap16 : (M <= 32 ? kCfgSwap32 : kCfgSwap64);
@@ -664,6 +1058,10 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
     if (M > 128) {
       cands[nc++] = kCfgM2N256;
       cands[nc++] = kCfgM2N128;
+    }
+    if (M > 128) {
+      cands[nc++] = kCfgP2N256;
+      cands[nc++] = kCfgP2N128;
     }
   } else {
     cands[nc++] = kCfgN256;
@@ -676,6 +1074,15 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
       cands[nc++] = kCfgM2N128;
       cands[nc++] = kCfgM2N112;
     }
+    if (M <= 256) {
+      cands[nc++] = kCfgSwap64;
+      cands[nc++] = kCfgSwap128;
+    }
+    if (M > 128) {
+      cands[nc++] = kCfgP2N256;
+      cands[nc++] = kCfgP2N192;
+      cands[nc++] = kCfgP2N128;
+    }
   }
   const int num_kb = (K + 63) / 64;
   GemmPlan best{cands[0], 1};
@@ -683,24 +1090,27 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
   for (int ci = 0; ci < nc; ++ci) {
     const int cfg = cands[ci];
     const int bn = cfg_bn(cfg);
-    const bool swap = cfg_swap(cfg);
     const int mh = cfg_mh(cfg);
-    const long p = swap ? N : M, qq = swap ? M : N;
-    const long tiles = ((p + 128 * mh - 1) / (128 * mh)) * ((qq + bn - 1) / bn);
-    for (int s = 1; s <= kMaxSplits; ++s) {
+    const bool cl = cfg_cl(cfg);
+    for (int s = cl ? 2 : 1; s <= kMaxSplits; ++s) {
       const int kb_per = (num_kb + s - 1) / s;
       if (s > 1 && kb_per < 4) break;
-      const long units = tiles * s;
-      const long waves = (units + num_sm - 1) / num_sm;
+      const SplitGeometry geo = gemm_split_geometry(M, N, K, cfg, s, num_sm);
+      const long units = geo.tiles * s;
+      const bool pair = cfg_pair(cfg);
+      const int slots = pair ? num_sm / 2 : num_sm;  // a pair unit occupies two SMs
+      const long waves = (units + slots - 1) / slots;
       // Relative cost model: a k-block costs the larger of its MMA time
       // (grows with the tile area) and its operand load time (grows with the
       // rows loaded), plus a fixed latency share, per-unit prologue /
       // epilogue, and the split partial-sum round trips.
-      const double mma = mh * bn / 256.0;
-      const double load = (128.0 * mh + bn) / 384.0 * 0.8;
+      const double mma = mh * bn / 256.0;  // per SM
+      const double load = pair ? (128.0 + bn / 2.0) / 384.0 * 0.8
+                               : ((double)geo.tile_rows + bn) / 384.0 * 0.8;
       const double per_kb = (mma > load ? mma : load) + 0.25;
       double t_unit = kb_per * per_kb + 3.0 * mh;
-      if (s > 1) t_unit += 4.0 + ((s + 3) / 4) * (mh * bn / 256.0) * 2.0;
+      if (cl) t_unit += 1.5 + (mh * bn / 256.0);  // parallel reduction over the cluster
+      else if (s > 1) t_unit += 4.0 + ((s + 3) / 4) * (mh * bn / 256.0) * 2.0;
       const double cost = waves * t_unit;
       if (cost < best_cost * 0.97) {
         best_cost = cost;
@@ -783,18 +1193,69 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
   if (epi == kEpiSiluMul && !cfg_silu_ok(cfg)) cfg = kCfgN128;
   const int bn = cfg_bn(cfg);
   if (bn == 0) throw std::runtime_error("gemm_bf16: unknown config " + std::to_string(cfg));
-  const bool swap = cfg_swap(cfg);
-  const int bmt = 128 * cfg_mh(cfg);
-  const long p = swap ? N : M, qq = swap ? M : N;
-  const long tiles = ((p + bmt - 1) / bmt) * ((qq + bn - 1) / bn);
   const int num_kb = (K + 63) / 64;
   if (splits > num_kb) splits = num_kb;
-  if (splits > 1) {
-    const size_t need = (size_t)tiles * splits * bmt * bn * sizeof(float);
-    if (ws == nullptr || need > ws_bytes || tiles > n_counters) splits = 1;  // no room: no split
+  if (cfg_cl(cfg)) {
+    if (epi == kEpiSiluMul && N % 128 != 0)
+      throw std::runtime_error("gemm_bf16 silu_mul: N must be a multiple of 128");
+    if (splits > 1) {
+      if (epi == kEpiSiluMul) {
+        if (cfg == kCfgClN256)
+          return launch_cl<256, 4, kEpiSiluMul, 1>(A, W, C, M, N, K, lda, ldw, ldc, splits, err,
+                                                   stream);
+        return launch_cl<128, 4, kEpiSiluMul, 2>(A, W, C, M, N, K, lda, ldw, ldc, splits, err,
+                                                 stream);
+      }
+      switch (cfg) {
+        case kCfgClN256:
+          return launch_cl<256, 4, kEpiNone, 1>(A, W, C, M, N, K, lda, ldw, ldc, splits, err, stream);
+        case kCfgClN128:
+          return launch_cl<128, 6, kEpiNone, 1>(A, W, C, M, N, K, lda, ldw, ldc, splits, err, stream);
+        case kCfgClM2N128:
+          return launch_cl<128, 4, kEpiNone, 2>(A, W, C, M, N, K, lda, ldw, ldc, splits, err, stream);
+        case kCfgClM2N112:
+          return launch_cl<112, 4, kEpiNone, 2>(A, W, C, M, N, K, lda, ldw, ldc, splits, err, stream);
+        case kCfgClM2N64:
+          return launch_cl<64, 5, kEpiNone, 2>(A, W, C, M, N, K, lda, ldw, ldc, splits, err, stream);
+      }
+    }
+    // One K slice: the plain persistent tile of the same shape.
+    cfg = cfg == kCfgClN256 ? kCfgN256 : cfg == kCfgClN128 ? kCfgN128
+        : cfg == kCfgClM2N128 ? kCfgM2N128 : cfg == kCfgClM2N112 ? kCfgM2N112 : kCfgM2N64;
+    splits = 1;
   }
+  SplitGeometry geo = gemm_split_geometry(M, N, K, cfg, splits, num_sms(dev));
+  if (splits > 1 && (ws == nullptr || geo.ws_bytes > ws_bytes || geo.counters > n_counters)) {
+    splits = 1;  // no room: no split
+    geo = gemm_split_geometry(M, N, K, cfg, splits, num_sms(dev));
+  }
+  const int pm = geo.tile_rows;
   float* wsp = splits > 1 ? ws : nullptr;
   int* cnt = splits > 1 ? counters : nullptr;
+  if (cfg_pair(cfg) && epi == kEpiSiluMul) {
+    if (N % 128 != 0) throw std::runtime_error("gemm_bf16 silu_mul: N must be a multiple of 128");
+    if (cfg == kCfgP2N256)
+      return launch_pair<256, 6, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt,
+                                              err, stream);
+    return launch_pair<128, 8, kEpiSiluMul>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
+                                            stream);
+  }
+  if (cfg_pair(cfg)) {
+    switch (cfg) {
+      case kCfgP2N256:
+        return launch_pair<256, 6, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
+                                             stream);
+      case kCfgP2N192:
+        return launch_pair<192, 7, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
+                                             stream);
+      case kCfgP2N128:
+        return launch_pair<128, 8, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
+                                             stream);
+      default:
+        return launch_pair<64, 10, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
+                                             stream);
+    }
+  }
   if (epi == kEpiSiluMul) {
     if (N % 128 != 0) throw std::runtime_error("gemm_bf16 silu_mul: N must be a multiple of 128");
     if (cfg == kCfgN256)
@@ -817,7 +1278,7 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
                                                           wsp, cnt, err, stream)
 #define B200_SWAP(BN_, ST_) \
   return launch_cfg<BN_, ST_, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt, \
-                                              err, stream)
+                                              err, stream, WQParams{}, GroupInfo{}, 0, pm)
   switch (cfg) {
     case kCfgN256: B200_NORMAL(256, 4);
     case kCfgN192: B200_NORMAL(192, 5);

@@ -94,13 +94,12 @@ extern "C" int b200_gemm_bf16_noalloc(const void* A, int lda, const void* W, int
     if (splits > b200::kMaxSplits) splits = b200::kMaxSplits;
     const int num_kb = (K + 63) / 64;
     if (splits > num_kb) splits = num_kb;
-    if (splits > 1) {
-      const bool swap = b200::gemm_cfg_is_swap(cfg);
-      const long p = swap ? N : M, q = swap ? M : N;
-      const int bm = b200::gemm_cfg_tile_m(cfg);
-      const long tiles = ((p + bm - 1) / bm) * ((q + bn - 1) / bn);
-      const size_t need = (size_t)tiles * splits * bm * bn * sizeof(float);
-      if (need > B200_NOALLOC_WS_BYTES || tiles > B200_NOALLOC_MAX_TILES) {
+    if (splits > 1 && !b200::gemm_cfg_is_cluster(cfg)) {
+      const b200::SplitGeometry geo =
+          b200::gemm_split_geometry(M, N, K, cfg, splits, b200::num_sms(dev));
+      const long tiles = geo.tiles;
+      const size_t need = geo.ws_bytes;
+      if (need > B200_NOALLOC_WS_BYTES || geo.counters > B200_NOALLOC_MAX_TILES) {
         std::snprintf(g_last_error, sizeof(g_last_error),
                       "split-K scratch too small: need %zu bytes / %ld tiles, static limit %u bytes "
                       "/ %d tiles (use fewer splits)",

@@ -36,8 +36,13 @@ EPI_NONE, EPI_SILU = 0, 1
 CFGS = {0: (256, False, 128), 1: (128, False, 128), 2: (16, True, 128), 3: (32, True, 128),
         4: (64, True, 128), 5: (192, False, 128), 6: (96, False, 128), 7: (64, False, 128),
         8: (128, True, 128), 9: (256, False, 256), 10: (224, False, 256), 11: (128, False, 256),
-        12: (112, False, 256), 13: (64, False, 256)}
-SILU_CFGS = (0, 1, 9, 11)
+        12: (112, False, 256), 13: (64, False, 256),
+        # CTA pairs (cta_group::2): 256-row tiles over two SMs
+        19: (256, False, 256), 20: (128, False, 256), 21: (192, False, 256), 22: (64, False, 256)}
+# cluster split-K configs (the K slices of a tile reduce through distributed
+# shared memory): cfg id -> (BN, BM); only tried with splits >= 2
+CLUSTER_CFGS = {14: (256, 128), 15: (128, 128), 16: (128, 256), 17: (112, 256), 18: (64, 256)}
+SILU_CFGS = (0, 1, 9, 11, 14, 16, 19, 20)
 SPLITS = (1, 2, 3, 4, 6, 8)
 
 
@@ -47,7 +52,7 @@ def candidates(M: int, N: int, K: int, epi: int) -> list[tuple[int, int]]:
     for cfg, (bn, swap, bm) in CFGS.items():
         if epi == EPI_SILU and cfg not in SILU_CFGS:
             continue
-        if swap and (M > 128 or bn < min(M, 128) or (bn > 16 and bn // 2 >= M)):
+        if swap and (M > 256 or bn < min(M, 128) // 2 or (bn > 16 and bn // 2 >= M)):
             continue
         if not swap and M <= 16:
             continue
@@ -57,6 +62,15 @@ def candidates(M: int, N: int, K: int, epi: int) -> list[tuple[int, int]]:
             if s > 1 and (nkb + s - 1) // s < 4:
                 continue
             out.append((cfg, s))
+    if M <= 512:
+        for cfg, (bn, bm) in CLUSTER_CFGS.items():
+            if epi == EPI_SILU and cfg not in SILU_CFGS:
+                continue
+            if M <= 16 or (bm == 256 and M <= 128):
+                continue
+            for s in SPLITS:
+                if s > 1 and (nkb + s - 1) // s >= 4:
+                    out.append((cfg, s))
     return out
 
 

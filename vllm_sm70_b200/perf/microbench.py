@@ -46,11 +46,25 @@ def flush_l2():
     _FLUSH.sum()
 
 
+GRAPH = False  # --graph: time CUDA-graph replays (no host launch work in the timed region)
+
+
 def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = False) -> float:
     """Mean device ms per call (CUDA events on the current stream)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if GRAPH:
+        s0 = torch.cuda.Stream()
+        s0.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s0):
+            fn()  # warm on the capture stream
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s0):
+                fn()
+        torch.cuda.synchronize()
+        fn = g.replay
     if not flush:
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
@@ -89,6 +103,9 @@ def bench_gemm(M, N, K, cfg=-1, splits=0, iters=20, flush=False, cublas=True, ep
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
     out = torch.empty(M, N // 2 if epi else N, device="cuda", dtype=torch.bfloat16)
     if epi:
+        if cfg >= 0 and splits > 0:  # the SiLU op takes its split from the plan table
+            torch.ops._b200_C.gemm_set_plan(M, N, K, 1, cfg, splits)
+            cfg = -1
         fn = lambda: torch.ops._b200_C.gemm_bf16_silu_mul_out(out, a, w, cfg)  # noqa: E731
     else:
         fn = lambda: linear.gemm(a, w, out=out, cfg=cfg, splits=splits)  # noqa: E731
@@ -172,19 +189,21 @@ def main(argv=None):
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="gemm: time every (cfg, splits)")
     ap.add_argument("--epi", type=int, default=0, help="gemm: 1 = fused SiLU*up epilogue")
+    ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays")
     args = ap.parse_args(argv)
+    global GRAPH
+    GRAPH = args.graph
     _setup()
     out = []
     if args.case == "gemm" and args.sweep:
         from ..engine import warmup
 
         for cfg, sp in warmup.candidates(args.M, args.N, args.K, args.epi):
-            if args.epi and sp > 1:
-                continue  # the silu op takes no split override
             r = bench_gemm(args.M, args.N, args.K, cfg, sp, args.iters, args.flush, False,
                            args.epi)
             r["cfg"], r["splits"] = cfg, sp
             out.append(r)
+        torch.ops._b200_C.gemm_clear_plans()
         out.append(bench_gemm(args.M, args.N, args.K, -1, 0, args.iters, args.flush, True,
                               args.epi))
     elif args.case == "gemm":
