@@ -190,11 +190,60 @@ def test_tuner_installs_plans(b200_ops):
     from vllm_sm70_b200.engine import warmup
 
     torch.ops._b200_C.gemm_clear_plans()
+    linear.clear_library()
     plans = warmup.tune_shapes([(256, 1536, 1024, 0), (64, 1024, 512, 0), (128, 1024, 512, 1)],
-                               iters=2)
+                               iters=2, library=False)
     assert len(plans) == 3
     exported = warmup.export_plans()
     assert sorted(map(tuple, exported)) == sorted(map(tuple, plans))
     for M, N, K, epi, cfg, sp in plans:
         assert tuple(torch.ops._b200_C.gemm_bf16_plan(M, N, K, epi, 148)) == (cfg, sp)
     torch.ops._b200_C.gemm_clear_plans()
+
+
+def test_tuner_library_route(b200_ops, rel_err):
+    """A shape the tuner routes to the vendor library still computes the GEMM,
+    and the route survives an export / import round trip."""
+    from vllm_sm70_b200.engine import warmup
+
+    torch.ops._b200_C.gemm_clear_plans()
+    linear.clear_library()
+    try:
+        M, N, K = 256, 2048, 1024
+        plans = warmup.tune_shapes([(M, N, K, 0)], iters=2, library=True)
+        exported = warmup.export_plans()
+        assert sorted(map(tuple, exported)) == sorted(map(tuple, plans))
+        linear.set_library(M, N, K)  # force the library route for the check
+        a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+        assert rel_err(linear.gemm(a, w), _ref(a, w)) < 1e-2
+        linear.clear_library()
+        warmup.install_plans([[M, N, K, 0, linear.LIBRARY_CFG, 0]])
+        assert (M, N, K) in linear.library_shapes()
+    finally:
+        torch.ops._b200_C.gemm_clear_plans()
+        linear.clear_library()
+
+
+def test_silu_mul_interleaved_and_library_route(b200_ops, rel_err):
+    torch.manual_seed(11)
+    M, K, N = 200, 512, 640
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    wg = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    wu = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    wi = linear.interleave_gate_up(wg, wu)
+    g = a.float() @ wg.float().t()
+    u = a.float() @ wu.float().t()
+    ref = g * torch.sigmoid(g) * u
+    # interleaved SiLU kernel on a precomputed [M, 2N] interleaved product
+    gu = (a.float() @ wi.float().t()).to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    torch.ops._b200_C.silu_mul(out, gu, linear.GATE_UP_BLOCK)
+    assert rel_err(out, ref) < 2e-2
+    # the tuner's library route for gate_up
+    linear.clear_library()
+    try:
+        linear.set_library(M, 2 * N, K, True, 1)
+        assert rel_err(linear.gemm_silu_mul(a, wi), ref) < 2e-2
+    finally:
+        linear.clear_library()

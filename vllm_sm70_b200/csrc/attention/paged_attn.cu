@@ -31,6 +31,7 @@
 #include <string>
 
 #include "attention/attn_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
@@ -113,6 +114,8 @@ constexpr int kBtCache = 512;  // block ids cached in smem per window
 template <int D, int KT, int NW, int STAGES, bool DECODE>
 __global__ void __launch_bounds__(NW * 32)
 paged_attn_kernel(const Params p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int ROWS = DECODE ? 16 : 16 * NW;
   constexpr int KW = DECODE ? KT / NW : KT;  // keys per warp per tile
   static_assert(KW % 16 == 0, "keys per warp must be a multiple of 16");
@@ -456,6 +459,8 @@ paged_attn_kernel(const Params p) {
 // Merge split-KV partials in split order (deterministic).
 template <int D>
 __global__ void combine_splits_kernel(const Params p, int T) {
+  pdl_wait();
+  pdl_trigger();
   const int tok = blockIdx.x;
   const int head = blockIdx.y;
   const int d = threadIdx.x;
@@ -498,7 +503,7 @@ void launch_attn(const Params& p, cudaStream_t stream) {
   }
   const int row_tiles = (p.rows_per_seq_max + ROWS - 1) / ROWS;
   dim3 grid(row_tiles, p.num_seqs, p.Hkv * (DECODE ? p.num_splits : 1));
-  kernel<<<grid, NW * 32, smem, stream>>>(p);
+  launch_pdl(kernel, grid, dim3(NW * 32), smem, stream, nullptr, p);
 }
 
 }  // namespace
@@ -554,9 +559,12 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   }
   if (p.num_splits > 1) {
     dim3 grid(a.num_tokens, a.Hq);
-    if (a.head_dim == 128) combine_splits_kernel<128><<<grid, 128, 0, stream>>>(p, a.num_tokens);
-    else if (a.head_dim == 256) combine_splits_kernel<256><<<grid, 128, 0, stream>>>(p, a.num_tokens);
-    else combine_splits_kernel<64><<<grid, 64, 0, stream>>>(p, a.num_tokens);
+    if (a.head_dim == 128)
+      launch_pdl(combine_splits_kernel<128>, grid, dim3(128), 0, stream, nullptr, p, a.num_tokens);
+    else if (a.head_dim == 256)
+      launch_pdl(combine_splits_kernel<256>, grid, dim3(128), 0, stream, nullptr, p, a.num_tokens);
+    else
+      launch_pdl(combine_splits_kernel<64>, grid, dim3(64), 0, stream, nullptr, p, a.num_tokens);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)

@@ -17,6 +17,7 @@
 #include <stdexcept>
 
 #include "ops_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
@@ -28,6 +29,8 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, const int64_t* _
                                const __nv_bfloat16* __restrict__ q_norm,
                                const __nv_bfloat16* __restrict__ k_norm, int T, int Hq, int Hkv,
                                int BS, float eps, int rot_dim, long long blk_stride) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int P = D / 64;  // pairs per lane (first-half index i, second-half i + D/2)
   const int warps_per_block = blockDim.x / 32;
   const int gw = blockIdx.x * warps_per_block + threadIdx.x / 32;
@@ -122,6 +125,8 @@ __global__ void kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_
                                 long long ldk, long long ldv, __nv_bfloat16* __restrict__ kc,
                                 __nv_bfloat16* __restrict__ vc, const int64_t* __restrict__ slots,
                                 int T, int Hkv, int D, int BS, long long blk_stride) {
+  pdl_wait();
+  pdl_trigger();
   const long long chunks_per_tok = (long long)Hkv * (D / 8);
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long total = (long long)T * chunks_per_tok * 2;
@@ -147,9 +152,9 @@ void kv_cache_write_launch(const void* k, const void* v, long long ldk, long lon
   if (T <= 0) return;
   const long long total = (long long)T * Hkv * (D / 8) * 2;
   const int thr = 256;
-  kv_write_kernel<<<(unsigned)((total + thr - 1) / thr), thr, 0, stream>>>(
-      (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, ldk, ldv, (__nv_bfloat16*)k_cache,
-      (__nv_bfloat16*)v_cache, slots, T, Hkv, D, BS, blk_stride);
+  launch_pdl(kv_write_kernel, dim3((unsigned)((total + thr - 1) / thr)), dim3(thr), 0, stream,
+             nullptr, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, ldk, ldv,
+             (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slots, T, Hkv, D, BS, blk_stride);
 }
 
 void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, void* k_cache,
@@ -162,10 +167,10 @@ void rope_kv_write_launch(void* qkv, const int64_t* pos, const float* cos_sin, v
   const int wpb = 8;
   const long blocks = (warps + wpb - 1) / wpb;
 #define B200_ROPE(DD)                                                                           \
-  rope_kv_kernel<DD><<<blocks, wpb * 32, 0, stream>>>(                                          \
-      (__nv_bfloat16*)qkv, pos, cos_sin, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slots, \
-      (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, T, Hq, Hkv, BS, eps, rot_dim, \
-      blk_stride)
+  launch_pdl(rope_kv_kernel<DD>, dim3((unsigned)blocks), dim3(wpb * 32), 0, stream, nullptr,    \
+             (__nv_bfloat16*)qkv, pos, cos_sin, (__nv_bfloat16*)k_cache,                      \
+             (__nv_bfloat16*)v_cache, slots, (const __nv_bfloat16*)q_norm,                     \
+             (const __nv_bfloat16*)k_norm, T, Hq, Hkv, BS, eps, rot_dim, blk_stride)
   if (D == 128) B200_ROPE(128);
   else if (D == 256) B200_ROPE(256);
   else if (D == 64) B200_ROPE(64);

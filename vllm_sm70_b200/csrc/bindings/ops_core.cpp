@@ -546,12 +546,12 @@ void argmax(at::Tensor& ids, const c10::optional<at::Tensor>& vals, const at::Te
                 vals ? vals->data_ptr<float>() : nullptr, (int)id_offset, cur_stream());
 }
 
-void silu_mul(at::Tensor& out, const at::Tensor& x) {
+void silu_mul(at::Tensor& out, const at::Tensor& x, int64_t block) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "silu_mul: 2-D rows");
   c10::cuda::CUDAGuard g(x.device());
   silu_mul_launch(out.data_ptr(), x.data_ptr(), (int)x.size(0), (int)(x.size(1) / 2),
-                  (int)x.stride(0), (int)out.stride(0), cur_stream());
+                  (int)x.stride(0), (int)out.stride(0), cur_stream(), (int)block);
 }
 
 void embedding(at::Tensor& out, const at::Tensor& ids, const at::Tensor& table,
@@ -621,7 +621,7 @@ TORCH_LIBRARY(_b200_C, m) {
         "int T, int H, Tensor w, float eps, int timeout_ms, int grid) -> ()");
   m.def("kv_cache_write(Tensor k, Tensor v, Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor slots) -> ()");
   m.def("argmax(Tensor(a!) ids, Tensor(b!)? vals, Tensor logits, int id_offset) -> ()");
-  m.def("silu_mul(Tensor(a!) out, Tensor x) -> ()");
+  m.def("silu_mul(Tensor(a!) out, Tensor x, int block=0) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor ids, Tensor table, int vocab_start) -> ()");
 }
 

@@ -41,6 +41,7 @@
 
 #include "common/ptx.cuh"
 #include "comm/comm_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
@@ -93,6 +94,8 @@ constexpr int kMaxVec = 4;  // 16-byte vectors per thread kept in registers (H <
 
 template <int W>
 __global__ void __launch_bounds__(512) ar_rmsnorm_kernel(ArRmsNormParams p) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ int s_ok;
   const int tid = threadIdx.x;
@@ -210,9 +213,9 @@ void ar_rmsnorm_launch(const ArRmsNormParams& p, int grid, cudaStream_t stream) 
   if (threads < 64) threads = 64;
   if (threads > 512) throw std::runtime_error("ar_rmsnorm: H too large");
   switch (p.world) {
-    case 2: ar_rmsnorm_kernel<2><<<grid, threads, 0, stream>>>(p); break;
-    case 4: ar_rmsnorm_kernel<4><<<grid, threads, 0, stream>>>(p); break;
-    case 8: ar_rmsnorm_kernel<8><<<grid, threads, 0, stream>>>(p); break;
+    case 2: launch_pdl(ar_rmsnorm_kernel<2>, dim3(grid), dim3(threads), 0, stream, nullptr, p); break;
+    case 4: launch_pdl(ar_rmsnorm_kernel<4>, dim3(grid), dim3(threads), 0, stream, nullptr, p); break;
+    case 8: launch_pdl(ar_rmsnorm_kernel<8>, dim3(grid), dim3(threads), 0, stream, nullptr, p); break;
     default: throw std::runtime_error("ar_rmsnorm: world size must be 2, 4 or 8");
   }
   cudaError_t e = cudaGetLastError();

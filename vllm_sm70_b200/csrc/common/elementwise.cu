@@ -10,18 +10,24 @@
 #include <stdexcept>
 
 #include "ops_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
 
-// x [T, 2I] = [gate | up]; out [T, I]
+// x [T, 2I] = [gate | up] (block = 0), or gate/up interleaved in blocks of
+// `block` columns ([g0..g_b-1, u0..u_b-1, g_b.., ...], the layout of the
+// fused-epilogue gate_up weights); out [T, I]
 __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
-                                int I, int ld_x, int ld_o) {
+                                int I, int ld_x, int ld_o, int block) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int i8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (i8 >= I) return;
-  const __nv_bfloat16* g = x + (size_t)t * ld_x + i8;
-  const __nv_bfloat16* u = g + I;
+  const __nv_bfloat16* g =
+      x + (size_t)t * ld_x + (block > 0 ? (i8 / block) * 2 * block + i8 % block : i8);
+  const __nv_bfloat16* u = g + (block > 0 ? block : I);
   const uint4 gv = *reinterpret_cast<const uint4*>(g);
   const uint4 uv = *reinterpret_cast<const uint4*>(u);
   const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
@@ -42,6 +48,8 @@ __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
 __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int64_t* __restrict__ ids,
                                  const __nv_bfloat16* __restrict__ table, int H, int64_t vocab_start,
                                  int64_t vocab_end) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int64_t id = ids[t];
   uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
@@ -53,20 +61,22 @@ __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int64_t*
 }  // namespace
 
 void silu_mul_launch(void* out, const void* x, int T, int I, int ld_x, int ld_o,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int block) {
   if (T <= 0) return;
   if (I % 8) throw std::runtime_error("silu_mul: I % 8 != 0");
+  if (block < 0 || block % 8 || (block > 0 && I % block))
+    throw std::runtime_error("silu_mul: interleave block must be a multiple of 8 dividing I");
   dim3 grid((I / 8 + 127) / 128, T);
-  silu_mul_kernel<<<grid, 128, 0, stream>>>((__nv_bfloat16*)out, (const __nv_bfloat16*)x, I, ld_x,
-                                            ld_o);
+  launch_pdl(silu_mul_kernel, grid, dim3(128), 0, stream, nullptr, (__nv_bfloat16*)out,
+             (const __nv_bfloat16*)x, I, ld_x, ld_o, block);
 }
 
 void embedding_launch(void* out, const int64_t* ids, const void* table, int T, int H,
                       int64_t vocab_start, int64_t vocab_end, cudaStream_t stream) {
   if (T <= 0) return;
   if (H % 8) throw std::runtime_error("embedding: H % 8 != 0");
-  embedding_kernel<<<T, 256, 0, stream>>>((__nv_bfloat16*)out, ids, (const __nv_bfloat16*)table, H,
-                                          vocab_start, vocab_end);
+  launch_pdl(embedding_kernel, dim3(T), dim3(256), 0, stream, nullptr, (__nv_bfloat16*)out, ids,
+             (const __nv_bfloat16*)table, H, vocab_start, vocab_end);
 }
 
 }  // namespace b200

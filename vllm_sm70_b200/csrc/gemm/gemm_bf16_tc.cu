@@ -52,6 +52,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "common/launch.h"
 #include "common/ptx.cuh"
 #include "common/tmap.h"
 #include "gemm/gemm_api.h"
@@ -157,6 +158,12 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 #define B200_TL(i) \
   do { if (tl) tl[(size_t)blockIdx.x * 16 + (i)] = globaltimer(); } while (0)
   if (threadIdx.x == 0) B200_TL(0);
+  // Programmatic dependent launch: grouped tile lists and quantised
+  // operands are read by every role, so those launches wait up front; plain
+  // bf16 launches wait in the producer only, after warming L2 with the first
+  // weight tiles (weights are never written by an earlier kernel).
+  const bool early_wait = grp.E > 0 || WF != kWBf16;
+  if (early_wait) pdl_wait();
   static_assert(WF == kWBf16 || SWAP, "quantised weights use the swap-AB (weight = P) form");
   static_assert(MH == 1 || (!SWAP && WF == kWBf16), "tall tiles: normal-mode bf16 only");
   static_assert(!CL || (!SWAP && WF == kWBf16), "cluster split-K: normal-mode bf16 only");
@@ -243,7 +250,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   if constexpr (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (threadIdx.x == 0) B200_TL(1);
+  if (threadIdx.x == 0) {
+    B200_TL(1);
+    pdl_trigger();
+  }
   bool cl_ok = false;  // cluster split: this epilogue thread's accumulator is ready
 
   if (warp == 0) {
@@ -252,6 +262,29 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
+      if (!early_wait) {
+        // Before waiting for the previous kernel: pull the weight tiles of
+        // this CTA's first 2 x STAGES k-blocks into L2.
+        if (unit0 < num_units) {
+          const int t = unit0 / splits, sp = unit0 - t * splits;
+          const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
+          const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+          const int nk = kb1 - kb0;
+          const int rot = kb_rotation(t, nk, num_m);
+          const int npf = min(nk, 2 * STAGES);
+          for (int it = 0; it < npf; ++it) {
+            const int kb = kb0 + (it + rot) % nk;
+            if constexpr (SWAP) {
+              for (int r = 0; r < p_rows_tile; r += pbox)
+                tma_prefetch_l2_2d(&tmap_p, kb * BK, uc.p_row + r);
+            } else {
+              for (int r = 0; r < QR; r += qbox)
+                tma_prefetch_l2_2d(&tmap_q, kb * BK, uc.q_row + (int)prank * QR + r);
+            }
+          }
+        }
+        pdl_wait();
+      }
       for (int u = unit0; u < num_units && !*abort_flag; u += ustride) {
         const int t = u / splits, sp = u - t * splits;
         const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
@@ -842,12 +875,9 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   const int grid = units < num_sms(dev) ? (int)units : num_sms(dev);
   WQParams q = wq;
   if (WF == kWBf16) q.out_scale = 1.f;
-  kernel<<<grid, WF == kWBf16 ? kThreads : kThreadsQ, S::kTotal, stream>>>(
-      tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits, ws, counters,
-      err, q, grp, pm, pbox, qbox);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess)
-    throw std::runtime_error(std::string("gemm_bf16_tc launch: ") + cudaGetErrorString(e));
+  launch_pdl(kernel, dim3(grid), dim3(WF == kWBf16 ? kThreads : kThreadsQ), S::kTotal, stream,
+             nullptr, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits,
+             ws, counters, err, q, grp, pm, pbox, qbox);
 }
 
 // Cluster split-K: the `splits` K-slices of a tile run as one thread-block
@@ -877,13 +907,15 @@ void launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int l
   lc.blockDim = dim3(kThreads, 1, 1);
   lc.dynamicSmemBytes = S::kTotal;
   lc.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = 1;
+  lc.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
                                      M, N, K, splits, (float*)nullptr, (int*)nullptr, err,
                                      WQParams{}, GroupInfo{}, (int)BM, (int)BM, BN);
@@ -920,13 +952,15 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
   lc.blockDim = dim3(kThreads, 1, 1);
   lc.dynamicSmemBytes = S::kTotal;
   lc.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = 1;
+  lc.numAttrs = 1;  // occupancy query: cluster shape only
   // Pairs that can be resident at once (the GPC layout can leave SMs
   // unpairable); the persistent grid never exceeds it, so every pair runs
   // concurrently (the co-resident split-K reduction relies on it).
@@ -941,6 +975,7 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
   }
   const long pairs = units < max_pairs[dev] ? units : max_pairs[dev];
   lc.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  lc.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
                                      M, N, K, splits, ws, counters, err, WQParams{}, GroupInfo{},
                                      (int)BM, (int)BM, BN / 2);

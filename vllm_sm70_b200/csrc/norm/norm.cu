@@ -16,6 +16,7 @@
 #include <string>
 
 #include "ops_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
@@ -59,6 +60,8 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, int ld_out,
                                 __nv_bfloat16* __restrict__ x, int ld_x,
                                 __nv_bfloat16* __restrict__ residual, int ld_r,
                                 const __nv_bfloat16* __restrict__ w, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -122,18 +125,18 @@ void rms_norm_launch(void* out, int ld_out, const void* x, int ld_x, const void*
                      int H, float eps, cudaStream_t stream) {
   if (H % 8) throw std::runtime_error("rms_norm: H % 8 != 0");
   if (rows <= 0) return;
-  rms_norm_kernel<false><<<rows, norm_threads(H), 0, stream>>>(
-      (__nv_bfloat16*)out, ld_out, (__nv_bfloat16*)x, ld_x, nullptr, 0, (const __nv_bfloat16*)w,
-      H, eps);
+  launch_pdl(rms_norm_kernel<false>, dim3(rows), dim3(norm_threads(H)), 0, stream, nullptr,
+             (__nv_bfloat16*)out, ld_out, (__nv_bfloat16*)x, ld_x, (__nv_bfloat16*)nullptr, 0,
+             (const __nv_bfloat16*)w, H, eps);
 }
 
 void fused_add_rms_norm_launch(void* x, int ld_x, void* residual, int ld_r, const void* w,
                                int rows, int H, float eps, cudaStream_t stream) {
   if (H % 8) throw std::runtime_error("fused_add_rms_norm: H % 8 != 0");
   if (rows <= 0) return;
-  rms_norm_kernel<true><<<rows, norm_threads(H), 0, stream>>>(
-      (__nv_bfloat16*)x, ld_x, (__nv_bfloat16*)x, ld_x, (__nv_bfloat16*)residual, ld_r,
-      (const __nv_bfloat16*)w, H, eps);
+  launch_pdl(rms_norm_kernel<true>, dim3(rows), dim3(norm_threads(H)), 0, stream, nullptr,
+             (__nv_bfloat16*)x, ld_x, (__nv_bfloat16*)x, ld_x, (__nv_bfloat16*)residual, ld_r,
+             (const __nv_bfloat16*)w, H, eps);
 }
 
 }  // namespace b200

@@ -28,8 +28,10 @@ void kv_cache_write_launch(const void* k, const void* v, long long ldk, long lon
                            int D, int BS, long long blk_stride, cudaStream_t stream);
 void argmax_launch(const void* logits, bool is_bf16, int rows, int V, int ld, int* ids, float* vals,
                    int id_offset, cudaStream_t stream);
+// block = 0: x = [gate | up]; block > 0: gate / up interleaved in blocks of
+// `block` columns.
 void silu_mul_launch(void* out, const void* x, int T, int I, int ld_x, int ld_o,
-                     cudaStream_t stream);
+                     cudaStream_t stream, int block = 0);
 void embedding_launch(void* out, const int64_t* ids, const void* table, int T, int H,
                       int64_t vocab_start, int64_t vocab_end, cudaStream_t stream);
 

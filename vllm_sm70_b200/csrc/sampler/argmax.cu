@@ -10,6 +10,7 @@
 #include <stdexcept>
 
 #include "ops_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
@@ -37,6 +38,8 @@ __device__ __forceinline__ float to_f<float>(float x) { return x; }
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ logits, int V, int ld, int* __restrict__ ids,
                               float* __restrict__ vals, int id_offset) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * ld;
   VI best{-INFINITY, 0x7fffffff};
@@ -68,11 +71,11 @@ void argmax_launch(const void* logits, bool is_bf16, int rows, int V, int ld, in
                    float* vals, int id_offset, cudaStream_t stream) {
   if (rows <= 0) return;
   if (is_bf16)
-    argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, stream>>>((const __nv_bfloat16*)logits, V, ld,
-                                                            ids, vals, id_offset);
+    launch_pdl(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(1024), 0, stream, nullptr,
+               (const __nv_bfloat16*)logits, V, ld, ids, vals, id_offset);
   else
-    argmax_kernel<float><<<rows, 1024, 0, stream>>>((const float*)logits, V, ld, ids, vals,
-                                                    id_offset);
+    launch_pdl(argmax_kernel<float>, dim3(rows), dim3(1024), 0, stream, nullptr,
+               (const float*)logits, V, ld, ids, vals, id_offset);
 }
 
 }  // namespace b200

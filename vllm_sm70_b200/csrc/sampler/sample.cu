@@ -26,6 +26,7 @@
 #include <stdexcept>
 
 #include "sampler/sampler_api.h"
+#include "common/launch.h"
 
 namespace b200 {
 namespace {
@@ -87,6 +88,8 @@ __global__ void gumbel_argmax_kernel(const T* __restrict__ logits, int V, int ld
                                      const int64_t* __restrict__ seeds, uint64_t offset,
                                      const int64_t* __restrict__ row_offsets, int id_offset,
                                      int* __restrict__ ids, float* __restrict__ vals) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * ld;
   const float t = temperature[row];
@@ -134,6 +137,8 @@ template <typename T>
 __global__ void topk_candidates_kernel(const T* __restrict__ logits, int V, int ld, int K,
                                        int id_offset, float* __restrict__ out_v,
                                        int* __restrict__ out_i) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int hist[256];
   __shared__ uint32_t s_prefix, s_mask;
   __shared__ int s_need;
@@ -228,6 +233,8 @@ __global__ void sample_candidates_kernel(const float* __restrict__ cand_v,
                                          const float* __restrict__ top_p,
                                          const int64_t* __restrict__ seeds, uint64_t offset,
                                          int* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int CMAX = 512;
   __shared__ float sv[CMAX];
   __shared__ int si[CMAX];
@@ -331,13 +338,13 @@ void gumbel_argmax_launch(const void* logits, bool bf16, int rows, int V, int ld
                           cudaStream_t stream) {
   if (rows <= 0) return;
   if (bf16)
-    gumbel_argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, stream>>>(
-        (const __nv_bfloat16*)logits, V, ld, temperature, seeds, offset, row_offsets, id_offset,
-        ids, vals);
+    launch_pdl(gumbel_argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(1024), 0, stream, nullptr,
+               (const __nv_bfloat16*)logits, V, ld, temperature, seeds, offset, row_offsets,
+               id_offset, ids, vals);
   else
-    gumbel_argmax_kernel<float><<<rows, 1024, 0, stream>>>((const float*)logits, V, ld,
-                                                           temperature, seeds, offset, row_offsets,
-                                                           id_offset, ids, vals);
+    launch_pdl(gumbel_argmax_kernel<float>, dim3(rows), dim3(1024), 0, stream, nullptr,
+               (const float*)logits, V, ld, temperature, seeds, offset, row_offsets, id_offset,
+               ids, vals);
 }
 
 void topk_candidates_launch(const void* logits, bool bf16, int rows, int V, int ld, int K,
@@ -345,11 +352,11 @@ void topk_candidates_launch(const void* logits, bool bf16, int rows, int V, int 
   if (rows <= 0) return;
   if (K < 1 || K > 64) throw std::runtime_error("topk_candidates: K must be in [1, 64]");
   if (bf16)
-    topk_candidates_kernel<__nv_bfloat16><<<rows, 512, 0, stream>>>(
-        (const __nv_bfloat16*)logits, V, ld, K, id_offset, out_v, out_i);
+    launch_pdl(topk_candidates_kernel<__nv_bfloat16>, dim3(rows), dim3(512), 0, stream, nullptr,
+               (const __nv_bfloat16*)logits, V, ld, K, id_offset, out_v, out_i);
   else
-    topk_candidates_kernel<float><<<rows, 512, 0, stream>>>((const float*)logits, V, ld, K,
-                                                            id_offset, out_v, out_i);
+    launch_pdl(topk_candidates_kernel<float>, dim3(rows), dim3(512), 0, stream, nullptr,
+               (const float*)logits, V, ld, K, id_offset, out_v, out_i);
 }
 
 void sample_candidates_launch(const float* cand_v, const int* cand_i, int rows, int C,
@@ -358,8 +365,8 @@ void sample_candidates_launch(const float* cand_v, const int* cand_i, int rows, 
                               cudaStream_t stream) {
   if (rows <= 0) return;
   if (C > 512) throw std::runtime_error("sample_candidates: at most 512 candidates");
-  sample_candidates_kernel<<<rows, 256, 0, stream>>>(cand_v, cand_i, C, temperature, top_k,
-                                                     top_p, seeds, offset, out);
+  launch_pdl(sample_candidates_kernel, dim3(rows), dim3(256), 0, stream, nullptr, cand_v, cand_i,
+             C, temperature, top_k, top_p, seeds, offset, out);
 }
 
 }  // namespace b200

@@ -113,7 +113,9 @@ class LLM:
         if self.device.type == "cuda" and tune_gemm:
             from . import warmup
 
-            warmup.engine_warmup(self.model, ps, self.runner.capture_sizes, gemm_lut_path)
+            # decode batch sizes plus the full prefill chunk
+            tune_ms = sorted(set(self.runner.capture_sizes) | {self.max_num_batched_tokens})
+            warmup.engine_warmup(self.model, ps, tune_ms, gemm_lut_path)
         if self.spec_k == 0:
             self.runner.capture()
         self.last_stats: GenerateStats | None = None

@@ -28,6 +28,7 @@ from pathlib import Path
 import torch
 
 from .. import _ext, envs
+from ..ops import linear as _lin
 
 logger = logging.getLogger("vllm.b200.warmup")
 
@@ -90,8 +91,12 @@ def _time(fn, iters: int, flush_buf: torch.Tensor) -> float:
 
 
 def tune_shapes(shapes: list[tuple[int, int, int, int]], iters: int = 5,
-                device: torch.device | None = None) -> list[list[int]]:
-    """Time candidates for each (M, N, K, epi); install and return the winners."""
+                device: torch.device | None = None, library: bool | None = None) -> list[list[int]]:
+    """Time candidates for each (M, N, K, epi); install and return the winners.
+    ``library``: also time cuBLAS for plain GEMMs (cfg -2 in the returned plans
+    marks a shape routed to it); default VLLM_B200_GEMM_LIBRARY."""
+    if library is None:
+        library = envs.get("VLLM_B200_GEMM_LIBRARY")
     _ext.require()
     ops = torch.ops._b200_C
     dev = device or torch.device("cuda", torch.cuda.current_device())
@@ -119,8 +124,28 @@ def tune_shapes(shapes: list[tuple[int, int, int, int]], iters: int = 5,
                 continue
             if best is None or ms < best[0]:
                 best = (ms, cfg, sp)
+        if best is not None and library:
+            # The vendor library is a candidate too (kept only when it beats the
+            # best tcgen05 plan by more than noise): the plain GEMM, or for
+            # gate_up the GEMM on the interleaved weights + the SiLU*up kernel.
+            if epi == EPI_NONE:
+                fn = lambda: torch.mm(a, w.t(), out=out)  # noqa: E731
+            else:
+                gu = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+
+                def fn():
+                    torch.mm(a, w.t(), out=gu)
+                    ops.silu_mul(out, gu, _lin.GATE_UP_BLOCK)
+            ms = _time(fn, iters, flush)
+            if ms < best[0] * 0.97:
+                best = (ms, _lin.LIBRARY_CFG, 0)
         if best is not None:
-            ops.gemm_set_plan(M, N, K, epi, best[1], best[2])
+            if best[1] == _lin.LIBRARY_CFG:
+                _lin.set_library(M, N, K, True, epi)
+                ops.gemm_set_plan(M, N, K, epi, -1, 0)
+            else:
+                _lin.set_library(M, N, K, False, epi)
+                ops.gemm_set_plan(M, N, K, epi, best[1], best[2])
             plans.append([M, N, K, epi, best[1], best[2]])
             cache[key] = best
             logger.info("gemm plan M=%d N=%d K=%d epi=%d -> cfg=%d splits=%d (%.1f us)",
@@ -132,13 +157,21 @@ def tune_shapes(shapes: list[tuple[int, int, int, int]], iters: int = 5,
 def install_plans(plans) -> None:
     _ext.require()
     for p in plans:
-        torch.ops._b200_C.gemm_set_plan(*[int(x) for x in p])
+        M, N, K, epi, cfg, sp = [int(x) for x in p]
+        if cfg == _lin.LIBRARY_CFG:
+            _lin.set_library(M, N, K, True, epi)
+            torch.ops._b200_C.gemm_set_plan(M, N, K, epi, -1, 0)
+        else:
+            _lin.set_library(M, N, K, False, epi)
+            torch.ops._b200_C.gemm_set_plan(M, N, K, epi, cfg, sp)
 
 
 def export_plans() -> list[list[int]]:
     _ext.require()
     flat = list(torch.ops._b200_C.gemm_export_plans())
-    return [flat[i:i + 6] for i in range(0, len(flat), 6)]
+    plans = [flat[i:i + 6] for i in range(0, len(flat), 6)]
+    return (plans + [[M, N, K, EPI_NONE, _lin.LIBRARY_CFG, 0] for (M, N, K) in _lin.library_shapes()]
+            + [[M, N, K, EPI_SILU, _lin.LIBRARY_CFG, 0] for (M, N, K) in _lin.library_shapes(1)])
 
 
 def manifest() -> dict:

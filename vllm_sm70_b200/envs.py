@@ -84,6 +84,12 @@ _reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
 _reg("VLLM_B200_CUDA_GRAPHS", "kill", True, "runtime", "Capture decode steps in CUDA graphs.")
 _reg("VLLM_B200_GRAPH_MAX_BS", "int", 512, "runtime", "Largest captured decode batch.")
 _reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tuning.")
+_reg("VLLM_B200_GEMM_LIBRARY", "kill", True, "runtime",
+     "Let the warm-up tuner route a plain bf16 GEMM shape to cuBLAS when it measures faster "
+     "than every tcgen05 plan (fused / quantised / grouped GEMMs never are).")
+_reg("VLLM_B200_PDL", "kill", True, "runtime",
+     "Launch the decode-path kernels with programmatic dependent launch (read by the native "
+     "library at load).")
 _reg("VLLM_B200_GEMM_LUT_PATH", "path", None, "runtime", "Tuned GEMM config table to import.")
 _reg("VLLM_B200_GEMM_LUT_EXPORT_PATH", "path", None, "runtime", "Where to export the table.")
 _reg("VLLM_B200_GEMM_LUT_STRICT", "optin", False, "runtime",

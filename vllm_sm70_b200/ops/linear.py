@@ -50,11 +50,37 @@ def plan(M: int, N: int, K: int, epi: int = 0, num_sm: int = 148) -> tuple[int, 
     return int(c), int(s)
 
 
+# Plain bf16 GEMM shapes (M, N, K) for which the warm-up tuner measured the
+# vendor library (cuBLAS through torch.mm) faster than every tcgen05 plan;
+# fused, quantised and grouped GEMMs always run the tcgen05 kernels.
+LIBRARY_CFG = -2
+_LIBRARY: set = set()
+_LIBRARY_SILU: set = set()  # gate_up shapes: library GEMM + interleaved SiLU kernel
+
+
+def set_library(M: int, N: int, K: int, on: bool = True, epi: int = 0) -> None:
+    target = _LIBRARY_SILU if epi else _LIBRARY
+    (target.add if on else target.discard)((int(M), int(N), int(K)))
+
+
+def clear_library() -> None:
+    _LIBRARY.clear()
+    _LIBRARY_SILU.clear()
+
+
+def library_shapes(epi: int = 0) -> list[tuple[int, int, int]]:
+    return sorted(_LIBRARY_SILU if epi else _LIBRARY)
+
+
 def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
          cfg: int = -1, splits: int = 0) -> torch.Tensor:
     """``x[M, K] @ w[N, K].T`` in bf16 with fp32 accumulation."""
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    if (cfg < 0 and splits <= 0 and _LIBRARY and x.is_cuda
+            and (x.shape[0], w.shape[0], x.shape[1]) in _LIBRARY):
+        torch.mm(x, w.t(), out=out)
+        return out
     if _use_native(x):
         torch.ops._b200_C.gemm_bf16_out(out, x, w, cfg, splits)
         launch_count.add(1)
@@ -90,6 +116,15 @@ def gemm_silu_mul(x: torch.Tensor, w_interleaved: torch.Tensor,
     n = w_interleaved.shape[0] // 2
     if out is None:
         out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
+    M, K = x.shape
+    if (cfg < 0 and _LIBRARY_SILU and x.is_cuda
+            and (M, w_interleaved.shape[0], K) in _LIBRARY_SILU):
+        # Tuner's choice for this shape: vendor GEMM on the interleaved weights,
+        # then the interleaved SiLU*up kernel.
+        gu = torch.mm(x, w_interleaved.t())
+        torch.ops._b200_C.silu_mul(out, gu, GATE_UP_BLOCK)
+        launch_count.add(1)
+        return out
     if _use_native(x) and envs.get("VLLM_B200_GEMM_SILU_EPILOGUE"):
         torch.ops._b200_C.gemm_bf16_silu_mul_out(out, x, w_interleaved, cfg)
         launch_count.add(1)
