@@ -76,6 +76,27 @@ def test_sinks_and_window(b200_ops, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
+def test_decode_sinks_window(b200_ops, rel_err):
+    q, kc, vc, bt, sl, cu = _case([1, 1, 1], [600, 40, 1300], 32, 8, 128, 16, seed=6)
+    sinks = torch.randn(32, device="cuda")
+    out = torch.empty_like(q)
+    A.paged_attention(out, q, kc, vc, bt, sl, cu, 1, 0.1, window=256, sinks=sinks, decode=True)
+    ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 0.1, window=256, sinks=sinks)
+    assert rel_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("bs", [16, 64])
+def test_decode_interleaved_cache(b200_ops, bs, rel_err):
+    """K and V of a block interleaved in one allocation ([blocks, 2, Hkv, BS, D],
+    the vLLM backend layout): strided cache blocks through the decode path."""
+    q, kc, vc, bt, sl, cu = _case([1] * 4, [5, 333, 1024, 77], 32, 8, 128, bs, seed=7)
+    both = torch.stack([kc, vc], dim=1).contiguous()
+    out = torch.empty_like(q)
+    A.paged_attention(out, q, both[:, 0], both[:, 1], bt, sl, cu, 1, 0.09, decode=True)
+    ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 0.09)
+    assert rel_err(out, ref) < 2e-2
+
+
 def test_rope_kv_write(b200_ops, rel_err):
     torch.manual_seed(5)
     T, hq, hkv, d, bs = 37, 8, 2, 128, 16

@@ -1,0 +1,99 @@
+"""HF-layout safetensors checkpoints through ``LLM(path, load_format=...)``:
+export -> load round trips (Llama, Qwen3-MoE), block-FP8 checkpoints kept in
+FP8 with their scales, and an explicit error where loading is not built."""
+import json
+
+import pytest
+import torch
+
+from vllm_sm70_b200.engine import LLM, SamplingParams
+from vllm_sm70_b200.models.config import ModelConfig
+from vllm_sm70_b200.ops import quant
+
+KW = dict(max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+          enforce_eager=True, max_num_batched_tokens=64)
+
+
+def _hf_config(cfg: ModelConfig, **extra) -> dict:
+    d = {"model_type": "qwen3_moe" if cfg.arch == "qwen3_moe" else "llama",
+         "hidden_size": cfg.hidden_size, "num_hidden_layers": cfg.num_layers,
+         "num_attention_heads": cfg.num_heads, "num_key_value_heads": cfg.num_kv_heads,
+         "head_dim": cfg.head_dim, "intermediate_size": cfg.intermediate_size,
+         "vocab_size": cfg.vocab_size, "rope_theta": cfg.rope_theta, "rms_norm_eps": cfg.rms_eps,
+         "max_position_embeddings": cfg.max_position, "tie_word_embeddings": False}
+    if cfg.arch == "qwen3_moe":
+        d.update(num_experts=cfg.num_experts, num_experts_per_tok=cfg.top_k,
+                 moe_intermediate_size=cfg.moe_intermediate_size, norm_topk_prob=True)
+    d.update(extra)
+    return d
+
+
+def _write(tmp_path, cfg_json: dict, sd: dict):
+    from safetensors.torch import save_file
+
+    (tmp_path / "config.json").write_text(json.dumps(cfg_json))
+    save_file(sd, str(tmp_path / "model.safetensors"))
+    return str(tmp_path)
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(3)
+    return [torch.randint(0, 512, (n,), generator=g) for n in (9, 30, 4)]
+
+
+def _tokens(llm):
+    return [o.output_token_ids for o in llm.generate(_prompts(), SamplingParams(max_tokens=5))]
+
+
+TINY = ModelConfig(arch="llama", hidden_size=128, num_layers=2, num_heads=4, num_kv_heads=4,
+                   head_dim=32, intermediate_size=256, vocab_size=512, rope_theta=10000.0,
+                   rms_eps=1e-5, max_position=512)
+
+
+def test_llama_roundtrip(tmp_path):
+    a = LLM(TINY, **KW)
+    path = _write(tmp_path, _hf_config(TINY), a.model.hf_state_dict())
+    b = LLM(path, load_format="safetensors", **KW)
+    assert _tokens(a) == _tokens(b)
+    for La, Lb in zip(a.model.layers, b.model.layers):
+        assert torch.equal(La["qkv"].w, Lb["qkv"].w) and torch.equal(La["gate_up"].w, Lb["gate_up"].w)
+
+
+def test_fp8_checkpoint_stays_fp8(tmp_path):
+    a = LLM(TINY, **KW)
+    sd = a.model.hf_state_dict()
+    dense = dict(sd)
+    for name in list(sd):
+        if name.endswith("_proj.weight"):
+            wq, s = quant.quantize_fp8_block(sd[name].float())
+            sd[name] = wq
+            sd[name.replace(".weight", ".weight_scale_inv")] = s
+            dense[name] = quant.Fp8BlockLinear(wq, s).dequant_ref().float()
+    cfg = _hf_config(TINY, quantization_config={"quant_method": "fp8",
+                                                "weight_block_size": [128, 128]})
+    b = LLM(_write(tmp_path, cfg, sd), load_format="safetensors", **KW)
+    L0 = b.model.layers[0]
+    assert isinstance(L0["qkv"], quant.Fp8BlockLinear) and isinstance(L0["o"], quant.Fp8BlockLinear)
+    q = dense["model.layers.0.self_attn.q_proj.weight"]
+    k = dense["model.layers.0.self_attn.k_proj.weight"]
+    v = dense["model.layers.0.self_attn.v_proj.weight"]
+    ref = torch.cat([q, k, v])
+    assert torch.allclose(L0["qkv"].reference_weight(), ref, atol=1e-6)
+    assert all(len(t) == 5 for t in _tokens(b))
+
+
+def test_qwen3_moe_roundtrip(tmp_path):
+    cfg = ModelConfig(arch="qwen3_moe", hidden_size=128, num_layers=2, num_heads=4,
+                      num_kv_heads=2, head_dim=32, intermediate_size=256, vocab_size=512,
+                      rope_theta=10000.0, rms_eps=1e-6, max_position=512, qk_norm=True,
+                      num_experts=8, top_k=2, moe_intermediate_size=64)
+    a = LLM(cfg, **KW)
+    path = _write(tmp_path, _hf_config(cfg), a.model.hf_state_dict())
+    b = LLM(path, load_format="safetensors", **KW)
+    assert _tokens(a) == _tokens(b)
+
+
+def test_missing_checkpoint_is_a_clear_error(tmp_path):
+    (tmp_path / "config.json").write_text(json.dumps(_hf_config(TINY)))
+    with pytest.raises(FileNotFoundError):
+        LLM(str(tmp_path), load_format="safetensors", **KW)

@@ -126,14 +126,49 @@ class LlamaModel:
             self.layers.append(L)
         self._init_rope()
 
-    def load_hf_state(self, get_tensor) -> None:
-        """Load from an HF Llama checkpoint; ``get_tensor(name)`` returns the
-        full (unsharded) tensor. Shards for this TP rank are cut here."""
+    def load_hf_state(self, get_tensor, has=None) -> None:
+        """Load from an HF Llama / Qwen3-dense checkpoint: bf16 / fp16 weights,
+        or block-FP8 (``weight`` e4m3 + ``weight_scale_inv`` per 128x128
+        block, the HF "fp8" quantization_config layout). ``get_tensor(name)``
+        returns the full (unsharded) tensor; this rank's shards are cut here
+        (FP8 shards stay aligned to the 128-row / -column scale blocks)."""
         cfg, dev, dt = self.cfg, self.device, self.dtype
         tp, r = self.ps.tp_size, self.ps.tp_rank
+        has = has or (lambda name: True)
 
         def t(name):
             return get_tensor(name).to(device=dev, dtype=dt)
+
+        def fp8(prefix):
+            return cfg.quant == "fp8" and has(prefix + ".weight_scale_inv")
+
+        def blocks(sl: slice) -> slice:
+            assert sl.start % 128 == 0 and sl.stop % 128 == 0, "FP8 shard not block aligned"
+            return slice(sl.start // 128, sl.stop // 128)
+
+        def linear(parts, cols=None):
+            """Concatenate the row slices ``parts = [(prefix, rows)]`` (rows of
+            each projection), optionally cutting input columns ``cols``."""
+            if all(fp8(pre) for pre, _ in parts):
+                ws, ss = [], []
+                for pre, rows in parts:
+                    w = get_tensor(pre + ".weight")
+                    s = get_tensor(pre + ".weight_scale_inv").float()
+                    rows = rows or slice(0, w.shape[0])
+                    w, s = w[rows], s[blocks(rows)]
+                    if cols is not None:
+                        w, s = w[:, cols], s[:, blocks(cols)]
+                    ws.append(w)
+                    ss.append(s)
+                from ..ops import quant
+
+                return quant.Fp8BlockLinear(torch.cat(ws).to(dev), torch.cat(ss).to(dev))
+            ws = []
+            for pre, rows in parts:
+                w = t(pre + ".weight")
+                w = w[rows] if rows is not None else w
+                ws.append(w[:, cols] if cols is not None else w)
+            return DenseLinear(torch.cat(ws, 0))
 
         vs = slice(r * self.vocab_local, (r + 1) * self.vocab_local)
         emb = t("model.embed_tokens.weight")
@@ -155,27 +190,65 @@ class LlamaModel:
             ks = slice(kvh * self.d, (kvh + 1) * self.d)
         else:
             ks = _shard(cfg.num_kv_heads * self.d, tp, r)
-        is_ = _shard(cfg.intermediate_size, tp, r)
         self.layers = []
         for i in range(cfg.num_layers):
             p = f"model.layers.{i}."
-            q = t(p + "self_attn.q_proj.weight")[qs]
-            k = t(p + "self_attn.k_proj.weight")[ks]
-            v = t(p + "self_attn.v_proj.weight")[ks]
+            a, m = p + "self_attn.", p + "mlp."
             L = {
                 "in_norm": t(p + "input_layernorm.weight"),
                 "post_norm": t(p + "post_attention_layernorm.weight"),
-                "qkv": DenseLinear(torch.cat([q, k, v], 0)),
-                "o": DenseLinear(t(p + "self_attn.o_proj.weight")[:, qs]),
-                "gate_up": GateUpLinear(t(p + "mlp.gate_proj.weight")[is_],
-                                        t(p + "mlp.up_proj.weight")[is_]),
-                "down": DenseLinear(t(p + "mlp.down_proj.weight")[:, is_]),
+                "qkv": linear([(a + "q_proj", qs), (a + "k_proj", ks), (a + "v_proj", ks)]),
+                "o": linear([(a + "o_proj", None)], cols=qs),
             }
+            L.update(self._load_mlp(m, get_tensor, has, t, fp8, linear))
             if cfg.qk_norm:
-                L["q_norm"] = t(p + "self_attn.q_norm.weight")
-                L["k_norm"] = t(p + "self_attn.k_norm.weight")
+                L["q_norm"] = t(a + "q_norm.weight")
+                L["k_norm"] = t(a + "k_norm.weight")
             self.layers.append(L)
         self._init_rope()
+
+    def hf_state_dict(self) -> dict:
+        """This (TP = 1, bf16) model's weights under HF checkpoint names: the
+        inverse of ``load_hf_state`` (used to write converted checkpoints)."""
+        assert self.ps.tp_size == 1, "export from a single-rank model"
+        cfg, hq, hkv, d = self.cfg, self.hq, self.hkv, self.d
+        sd = {"model.embed_tokens.weight": self.embed[: cfg.vocab_size],
+              "model.norm.weight": self.final_norm}
+        if not cfg.tie_embeddings:
+            sd["lm_head.weight"] = self.lm_head[: cfg.vocab_size]
+        for i, L in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            a = p + "self_attn."
+            q, k, v = torch.split(L["qkv"].w, [hq * d, hkv * d, hkv * d])
+            sd.update({p + "input_layernorm.weight": L["in_norm"],
+                       p + "post_attention_layernorm.weight": L["post_norm"],
+                       a + "q_proj.weight": q, a + "k_proj.weight": k, a + "v_proj.weight": v,
+                       a + "o_proj.weight": L["o"].w})
+            if cfg.qk_norm:
+                sd[a + "q_norm.weight"] = L["q_norm"]
+                sd[a + "k_norm.weight"] = L["k_norm"]
+            sd.update(self._mlp_state(p + "mlp.", L))
+        return {k: v.detach().contiguous().cpu() for k, v in sd.items()}
+
+    def _mlp_state(self, m: str, L: dict) -> dict:
+        g, u = ops.linear.deinterleave_gate_up(L["gate_up"].w)
+        return {m + "gate_proj.weight": g, m + "up_proj.weight": u,
+                m + "down_proj.weight": L["down"].w}
+
+    def _load_mlp(self, m: str, get_tensor, has, t, fp8, linear) -> dict:
+        """Dense SwiGLU MLP at checkpoint prefix ``m`` (``...mlp.``)."""
+        is_ = _shard(self.cfg.intermediate_size, self.ps.tp_size, self.ps.tp_rank)
+        return self._load_swiglu(m, is_, t, fp8, linear)
+
+    @staticmethod
+    def _load_swiglu(m: str, rows: slice, t, fp8, linear) -> dict:
+        out = {"down": linear([(m + "down_proj", None)], cols=rows)}
+        if fp8(m + "gate_proj") and fp8(m + "up_proj"):
+            out["gate_up"] = _QuantGateUp(linear([(m + "gate_proj", rows), (m + "up_proj", rows)]))
+        else:
+            out["gate_up"] = GateUpLinear(t(m + "gate_proj.weight")[rows],
+                                          t(m + "up_proj.weight")[rows])
+        return out
 
     def _init_rope(self) -> None:
         rot = int(self.d * self.cfg.partial_rotary_factor)

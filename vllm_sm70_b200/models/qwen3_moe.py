@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import torch
 
+from ..ops import linear as linear_ops
 from ..ops import moe as moe_ops
 from .llama import LlamaModel
 
@@ -43,6 +44,62 @@ class Qwen3MoeModel(LlamaModel):
             L["shared_down"] = self.make_linear(rnd(h, Is))
             L["shared_gate"] = rnd(1, h).to(self.dtype)
         return L
+
+    def _load_mlp(self, m: str, get_tensor, has, t, fp8, linear) -> dict:
+        """Router ``mlp.gate``, this rank's experts ``mlp.experts.{e}.*`` (bf16
+        or block-FP8, stacked as loaded) and the optional shared expert."""
+        cfg = self.cfg
+        E, e0 = self.E_local, self.e_base
+        L = {"router": t(m + "gate.weight")}
+        ex = [f"{m}experts.{e0 + j}." for j in range(E)]
+        if all(fp8(x + "gate_proj") for x in ex):
+            def cat(names, scale):
+                suffix = ".weight_scale_inv" if scale else ".weight"
+                v = [get_tensor(n + suffix) for n in names]
+                return torch.cat([x.float() if scale else x for x in v]).to(self.device)
+
+            w13 = cat([x + pr for x in ex for pr in ("gate_proj", "up_proj")], False)
+            s13 = cat([x + pr for x in ex for pr in ("gate_proj", "up_proj")], True)
+            w2 = cat([x + "down_proj" for x in ex], False)
+            s2 = cat([x + "down_proj" for x in ex], True)
+            L["experts"] = moe_ops.ExpertWeights(
+                "fp8", E, cfg.hidden_size, cfg.moe_intermediate_size,
+                w13.contiguous().view(torch.uint8), w2.contiguous().view(torch.uint8),
+                s13.contiguous(), s2.contiguous())
+        else:
+            w13 = torch.stack([torch.cat([t(x + "gate_proj.weight"), t(x + "up_proj.weight")])
+                               for x in ex])
+            w2 = torch.stack([t(x + "down_proj.weight") for x in ex])
+            L["experts"] = moe_ops.ExpertWeights.from_dense("bf16", w13, w2)
+        if cfg.shared_expert_intermediate_size:
+            from .llama import _shard
+
+            rows = _shard(cfg.shared_expert_intermediate_size, self.ps.tp_size, self.ps.tp_rank)
+            sh = self._load_swiglu(m + "shared_expert.", rows, t, fp8, linear)
+            L["shared_gate_up"], L["shared_down"] = sh["gate_up"], sh["down"]
+            L["shared_gate"] = t(m + "shared_expert_gate.weight")
+        return L
+
+    def _mlp_state(self, m: str, L: dict) -> dict:
+        cfg = self.cfg
+        ew = L["experts"]
+        assert ew.fmt == "bf16", "export of quantised experts is not supported"
+        I, H = cfg.moe_intermediate_size, cfg.hidden_size
+        w13 = ew.w13.view(ew.E, 2 * I, H)
+        w2 = ew.w2.view(ew.E, H, I)
+        sd = {m + "gate.weight": L["router"]}
+        for e in range(ew.E):
+            x = f"{m}experts.{e}."
+            sd[x + "gate_proj.weight"] = w13[e, :I]
+            sd[x + "up_proj.weight"] = w13[e, I:]
+            sd[x + "down_proj.weight"] = w2[e]
+        if "shared_gate_up" in L:
+            g, u = linear_ops.deinterleave_gate_up(L["shared_gate_up"].w)
+            sd.update({m + "shared_expert.gate_proj.weight": g,
+                       m + "shared_expert.up_proj.weight": u,
+                       m + "shared_expert.down_proj.weight": L["shared_down"].w,
+                       m + "shared_expert_gate.weight": L["shared_gate"]})
+        return sd
 
     def _ws(self, T: int):
         cfg = self.cfg
