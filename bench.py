@@ -1,6 +1,6 @@
 """Headline benchmark: output tokens/s of the Llama-3.1-8B-shaped workload.
 
-Workload (BASELINE config 2): Llama-3.1-8B shapes, random-init bf16 weights
+Workload: Llama-3.1-8B shapes, random-init bf16 weights
 (std 0.02), 256 requests with uniform-random prompt ids of length 1024, 256
 greedy output tokens each (ignore EOS), tensor-parallel over N GPUs of one
 node. One bench "step" is the whole workload: prefill of all 256 prompts and
@@ -32,9 +32,9 @@ import torch
 ROOT = Path(__file__).resolve().parent
 METRIC = "output tok/s (box, max over ranks) at 1/2/4/8 B200; p50 TTFT/TPOT"
 MODEL = "Llama-3.1-8B-shaped (32L, h4096, 32q/8kv, d128, ffn14336, vocab128256)"
-N_REQ, PROMPT, OUT = 256, 1024, 256  # the BASELINE workload; --requests/--prompt-len/
+N_REQ, PROMPT, OUT = 256, 1024, 256  # the headline workload; --requests/--prompt-len/
 # --output-len exist only for profiling runs and mark the JSON line "profiling"
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this config
+BASELINE_VALUE = None  # no published number exists for this config
 
 
 def _env_int(name, default):

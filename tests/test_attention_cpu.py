@@ -1,6 +1,6 @@
 """CPU correctness of paged decode attention vs a dense torch SDPA reference.
 
-This is the first BASELINE configuration: batch 8, 32 query heads, 8 KV
+This is the reference's CPU configuration: batch 8, 32 query heads, 8 KV
 heads, head_dim 128, KV block size 16, per-sequence context lengths uniform in
 [1, 2048], q/k/v fp32 N(0, 1), KV scattered into a random block table, fixed
 seed. Unused cache slots hold NaN so any out-of-context read poisons the

@@ -7,7 +7,7 @@
 // of a 16K-token prefill chunk is built here in one pass instead of in Python.
 //
 // Reference parity: the reference relies on upstream vLLM's KV-cache manager
-// (SURVEY L7); this runtime owns its scheduler, so the block manager is native.
+// (Python); this runtime owns its scheduler, so the block manager is native.
 #include <torch/custom_class.h>
 #include <torch/library.h>
 #include <torch/torch.h>

@@ -14,7 +14,7 @@
 // argmax_j r_j / E_j, E_j ~ Exp(1), which needs no normalisation.
 //
 // Reference parity: upstream vLLM's RejectionSampler used by the reference's
-// spec-decode path (SURVEY 3.5), and the sparse rejection of the fork bundle
+// spec-decode path, and the sparse rejection of the fork bundle
 // (sm70/reference/fork-cf9492a/qwen-dflash2/sparse_rejection.py), here as one
 // CUDA kernel per verify step.
 #include <cuda_runtime.h>

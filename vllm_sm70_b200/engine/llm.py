@@ -13,7 +13,7 @@ are admitted. Under ``torchrun`` every rank constructs the same ``LLM`` and
 runs the same schedule (decisions depend only on rank-uniform inputs).
 
 Reference parity: the reference serves through upstream vLLM ``LLM`` /
-``vllm serve`` (SURVEY L7); this in-repo runner is the engine the B200
+``vllm serve``; this in-repo runner is the engine the B200
 kernels and fused collectives run under (also exposed to vLLM through the
 platform plugin, ``vllm_sm70_b200.integration``).
 """

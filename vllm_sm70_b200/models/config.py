@@ -138,14 +138,14 @@ LLAMA31_ROPE_SCALING = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor":
 
 
 def llama31_8b() -> ModelConfig:
-    """Llama-3.1-8B shapes."""
+    """Llama-3.1-8B shapes (the headline benchmark model)."""
     return ModelConfig(arch="llama", hidden_size=4096, num_layers=32, num_heads=32,
                        num_kv_heads=8, head_dim=128, intermediate_size=14336, vocab_size=128256,
                        rope_theta=500000.0, rope_scaling=dict(LLAMA31_ROPE_SCALING), rms_eps=1e-5)
 
 
 def llama31_70b_awq() -> ModelConfig:
-    """Llama-3.1-70B shapes, AWQ int4 g128 (BASELINE config 4)."""
+    """Llama-3.1-70B shapes, AWQ int4 g128."""
     return ModelConfig(arch="llama", hidden_size=8192, num_layers=80, num_heads=64,
                        num_kv_heads=8, head_dim=128, intermediate_size=28672, vocab_size=128256,
                        rope_theta=500000.0, rope_scaling=dict(LLAMA31_ROPE_SCALING), rms_eps=1e-5,
@@ -153,7 +153,7 @@ def llama31_70b_awq() -> ModelConfig:
 
 
 def qwen3_30b_a3b_fp8() -> ModelConfig:
-    """Qwen3-30B-A3B shapes, block-FP8 128x128 (BASELINE config 3)."""
+    """Qwen3-30B-A3B shapes, block-FP8 128x128."""
     return ModelConfig(arch="qwen3_moe", hidden_size=2048, num_layers=48, num_heads=32,
                        num_kv_heads=4, head_dim=128, intermediate_size=6144, vocab_size=151936,
                        rope_theta=1000000.0, rms_eps=1e-6, qk_norm=True, num_experts=128, top_k=8,
@@ -161,7 +161,7 @@ def qwen3_30b_a3b_fp8() -> ModelConfig:
 
 
 def qwen3_next_80b_nvfp4() -> ModelConfig:
-    """Qwen3-Next-80B-A3B shapes, NVFP4 (BASELINE config 5)."""
+    """Qwen3-Next-80B-A3B shapes, NVFP4."""
     n = 48
     lt = tuple("attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(n))
     return ModelConfig(arch="qwen3_next", hidden_size=2048, num_layers=n, num_heads=16,

@@ -14,7 +14,7 @@ indexed by the same block table as the target.
 
 Reference parity: the reference's DFlash2 draft (``sm70/vllm_sm70/models/
 qwen/dflash_sm70.py``) serves the same role for Qwen3.8; Qwen3-Next ships an
-MTP layer (``num_nextn_predict_layers``), which BASELINE config 5 uses (k=3).
+MTP layer (``num_nextn_predict_layers``), used with k=3 draft tokens.
 """
 from __future__ import annotations
 

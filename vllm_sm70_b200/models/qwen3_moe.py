@@ -10,7 +10,7 @@ sums ride the fused all-reduce + residual + RMSNorm that follows.
 
 Reference parity: the Flint MoE block (``sm70/vllm_sm70/models/flint_sm70/
 model.py:200-300``) with its fused router and MoE methods; Qwen3-MoE is one
-of the BASELINE model families.
+of the supported model families.
 """
 from __future__ import annotations
 
