@@ -2,6 +2,10 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cstdint>
+
+#include <cstdint>
+
 namespace b200 {
 
 struct AttnArgs {
@@ -23,8 +27,21 @@ struct AttnArgs {
   bool decode;     // use the decode (1-warp, split-KV) variant
   int num_splits;  // decode split-KV factor (1 = none)
   long long kv_block_stride = 0;  // elements between cache blocks (0 = Hkv*BS*D, packed)
+  int num_blocks = 0;             // cache blocks (the tensor-core prefill path needs it)
 };
 
 void paged_attention_launch(const AttnArgs& a, cudaStream_t stream);
+
+// tcgen05 prefill attention (attention/fa_tc.cu): used by paged_attention_launch
+// for the shapes fa_tc_supported accepts (VLLM_B200_ATTN_PREFILL_TC=0 disables).
+bool fa_tc_enabled();
+bool fa_tc_supported(const AttnArgs& a);
+void fa_tc_launch(const AttnArgs& a, cudaStream_t stream);
+// Bring-up aid: override the V operand descriptor strides (0, 0 = defaults).
+void fa_tc_set_v_strides(uint32_t lbo, uint32_t sbo);
+// Profiling aid: 8 x grid uint64 %globaltimer stamps per launch (nullptr = off):
+// entry, set-up done, Q landed, first S ready, softmax loop done, last PV
+// done, epilogue stored, exit.
+void fa_tc_set_timeline(unsigned long long* buf);
 
 }  // namespace b200

@@ -1,0 +1,551 @@
+// Prefill / chunked-prefill paged attention on the 5th-generation tensor
+// cores (head_dim 128, bf16, causal with optional sliding window and sinks).
+//
+// One CTA owns 128 query rows of one (sequence, KV head): GQA-packed rows
+// r -> token t0 + r / G, head kvh * G + r % G, so every K/V tile is read once
+// for the whole group. Six warps:
+//   warp 0     producer: the Q tile once (3-D tensor map over q [T][Hq][D],
+//              box 64 x G x 128/G, 128-byte swizzle), then each 128-key K and
+//              V tile from the paged cache (3-D maps over [block][head*BS +
+//              key][d], one box per (cache block, 64-column half)) into a
+//              2-stage mbarrier ring.
+//   warp 1     TMEM owner + MMA issuer: S_j = Q K_j^T (M=N=K=128) into one of
+//              two TMEM S buffers, then O += P_{j-1} V_{j-1} (V as an MN-major
+//              B operand) into the TMEM O accumulator; S of the next tile is
+//              issued before the PV of the previous one so the tensor core
+//              works while the softmax warps do.
+//   warps 2-5  softmax, one query row per thread: tcgen05.ld of its S row,
+//              mask, running max, exp2, row sum, P (bf16) into a swizzled
+//              shared tile (the A operand of PV). O is rescaled in TMEM
+//              (tcgen05.ld / st) only when a row's running max grows by more
+//              than 2^8 over the max its exponentials use, so most tiles skip
+//              the correction; at the end each thread normalises its O row and
+//              stores it.
+// Rows of a partly filled last cache block hold stale data: their scores are
+// masked by selection, and the softmax warps zero the matching V rows before
+// the last PV (a zero P times a stale NaN would not be zero).
+//
+// Reference parity: the Flash-V100 prefill / chunked-prefill kernel
+// (sm70/csrc/flash_v100/fused_mha_forward_paged.cu:357) with its paged block
+// table, GQA and causal rules; the reference computes it with WMMA on sm_70.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <cstdlib>
+#include <stdexcept>
+#include <string>
+
+#include "attention/attn_api.h"
+#include "common/launch.h"
+#include "common/ptx.cuh"
+#include "common/tmap.h"
+#include "ops_api.h"
+
+namespace b200 {
+namespace {
+
+constexpr int FD = 128;                // head dim
+constexpr int FM = 128;                // query rows per CTA
+constexpr int FN = 128;                // keys per tile
+constexpr int FNS = 2;                 // K/V ring stages
+constexpr int kHalf = 128 * 128;       // 128 rows x 64 bf16
+constexpr int kQBytes = 2 * kHalf;     // Q: two 64-column halves
+constexpr int kKVBytes = 4 * kHalf;    // K halves, then V halves
+constexpr int kPBytes = 2 * kHalf;     // P: two 64-key halves
+constexpr int kBarBytes = 256;
+constexpr int kFaSmem = kQBytes + FNS * kKVBytes + kPBytes + kBarBytes + 1024;
+constexpr int kFaThreads = 192;
+constexpr uint32_t kTmemColsFa = 512;  // S0 | S1 | O | (unused)
+
+struct FaParams {
+  const int* block_table;
+  const int* seq_lens;
+  const int* cu_q;
+  const float* sinks;
+  __nv_bfloat16* out;
+  int num_seqs, Hq, Hkv, G, block_size, block_shift, max_blocks, window, o_stride_t;
+  float scale_log2;
+  unsigned int* err;
+  uint32_t v_lbo, v_sbo;  // V (MN-major B operand) descriptor strides, bytes
+};
+
+// Optional per-CTA timeline (profiling aid, off unless a buffer is installed
+// with fa_tc_set_timeline): %globaltimer stamps, 8 slots per CTA.
+__device__ unsigned long long* g_fa_timeline = nullptr;
+
+// 2^x on the multi-function unit (P values lie in [0, 2^8]).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+             const __grid_constant__ CUtensorMap tmv, const FaParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kQBytes;
+  uint8_t* sP = sKV + FNS * kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;            // [FNS]
+  uint64_t* k_empty = k_full + FNS;       // [FNS]
+  uint64_t* v_full = k_empty + FNS;       // [FNS]
+  uint64_t* v_empty = v_full + FNS;       // [FNS]
+  uint64_t* s_full = v_empty + FNS;       // [2]
+  uint64_t* s_free = s_full + 2;          // [2]
+  uint64_t* p_full = s_free + 2;
+  uint64_t* p_free = p_full + 1;
+  uint64_t* o_done = p_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  unsigned long long* const tl = g_fa_timeline;
+  const size_t tl_cta =
+      ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+#define FA_TL(i) \
+  do { if (tl) tl[tl_cta * 64 + (i)] = globaltimer(); } while (0)
+  // per-tile detail (first 8 tiles): slot 8 + 7 * j + k
+#define FA_TLJ(j, k) \
+  do { if (tl && (j) < 8) tl[tl_cta * 64 + 8 + 7 * (j) + (k)] = globaltimer(); } while (0)
+  if (threadIdx.x == 0) FA_TL(0);
+  pdl_wait();
+  const int seq = blockIdx.y;
+  const int kvh = blockIdx.z;
+  const int G = p.G;
+  const int q0 = p.cu_q[seq];
+  const int q_len = p.cu_q[seq + 1] - q0;
+  const int seq_len = p.seq_lens[seq];
+  const int n_qt = (q_len * G + FM - 1) / FM;
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest causal rows first
+  if (qt >= n_qt) return;
+  const int tpt = FM / G;  // tokens per tile
+  const int t0 = qt * tpt;
+  const int pos_first = seq_len - q_len + t0;
+  const int pos_last = seq_len - q_len + min(q_len, t0 + tpt) - 1;
+  int k_lo = p.window > 0 ? max(0, pos_first - p.window + 1) : 0;
+  k_lo = (k_lo / FN) * FN;
+  const int k_hi = pos_last + 1;
+  const int n_tiles = (k_hi - k_lo + FN - 1) / FN;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < FNS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 4);
+    }
+    mbar_init(p_full, 4);  // one arrival per softmax warp, after its P / V writes
+    mbar_init(p_free, 1);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmq);
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemColsFa);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    pdl_trigger();
+    FA_TL(1);
+  }
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tS = tmem_base, tO = tmem_base + 256;
+  const int BS = p.block_size;
+  const int blk_last = (seq_len - 1) >> p.block_shift;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const int* bt = p.block_table + (size_t)seq * p.max_blocks;
+    const int nb = FN / BS;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, (uint32_t)kQBytes);
+      tma_load_3d(sQ, &tmq, q_full, 0, kvh * G, q0 + t0);
+      tma_load_3d(sQ + kHalf, &tmq, q_full, 64, kvh * G, q0 + t0);
+    }
+    // K runs one tile ahead of V: K_j's slot frees right after S_j, V_j's
+    // only after PV_j, so K_{j+1} never queues behind V_j's slot.
+    auto issue = [&](int j, bool is_v) -> bool {
+      const int b0 = (k_lo + j * FN) >> p.block_shift;
+      int my = 0;
+      if (lane < nb) my = __ldg(bt + min(b0 + lane, blk_last));
+      const int st = j % FNS;
+      const uint32_t ph = (uint32_t)((j / FNS) & 1);
+      uint64_t* fullb = is_v ? &v_full[st] : &k_full[st];
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ph ^ 1u, p.err) ? 1 : 0;
+        if (!is_v) FA_TLJ(j, 0);
+        if (ok) mbar_arrive_expect_tx(fullb, (uint32_t)(2 * kHalf));
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
+      uint8_t* dst = sKV + st * kKVBytes + (is_v ? 2 * kHalf : 0);
+      const CUtensorMap* tm = is_v ? &tmv : &tmk;
+      for (int i = 0; i < nb; ++i) {
+        const int blk = __shfl_sync(0xffffffffu, my, i);
+        if (lane == 0) {
+          tma_load_3d(dst + i * BS * 128, tm, fullb, 0, kvh * BS, blk);
+          tma_load_3d(dst + kHalf + i * BS * 128, tm, fullb, 64, kvh * BS, blk);
+        }
+      }
+      return true;
+    };
+    bool ok = n_tiles == 0 || issue(0, false);
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (j + 1 < n_tiles) ok = issue(j + 1, false);
+      if (ok) ok = issue(j, true);
+    }
+    if (!ok) *abort_flag = 1;
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_f16(FM, FN, true);
+      constexpr uint32_t idesc_pv = umma_idesc_f16(FM, FD, true) | (1u << 16);  // B MN-major
+      bool ok = mbar_wait(q_full, 0, p.err);
+      FA_TL(2);
+      auto pv = [&](int i) -> bool {
+        const int st = i % FNS;
+        if (!mbar_wait(p_full, (uint32_t)(i & 1), p.err) ||
+            !mbar_wait(&v_full[st], (uint32_t)((i / FNS) & 1), p.err))
+          return false;
+        FA_TLJ(i, 3);
+        tc_fence_after();
+        const uint32_t sv = smem_u32(sKV + st * kKVBytes + 2 * kHalf);
+        const uint32_t sp = smem_u32(sP);
+#pragma unroll
+        for (int s = 0; s < FN / 16; ++s) {
+          const uint64_t ap = umma_desc_sw128(sp + (s >> 2) * kHalf) + (uint64_t)(2 * (s & 3));
+          const uint64_t bv = umma_desc_sw128_mn(sv + s * 16 * 128, p.v_lbo, p.v_sbo);
+          umma_f16(tO, ap, bv, idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
+        }
+        umma_commit(p_free);
+        umma_commit(&v_empty[st]);
+        return true;
+      };
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int sb = j & 1;
+        if (!mbar_wait(&s_free[sb], (uint32_t)(((j >> 1) & 1) ^ 1), p.err) ||
+            !mbar_wait(&k_full[stage], phase, p.err)) {
+          ok = false;
+          break;
+        }
+        FA_TLJ(j, 2);
+        tc_fence_after();
+        const uint32_t sq = smem_u32(sQ);
+        const uint32_t sk = smem_u32(sKV + stage * kKVBytes);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint64_t aq = umma_desc_sw128(sq + kb * kHalf);
+          const uint64_t bk = umma_desc_sw128(sk + kb * kHalf);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tS + sb * FN, aq + (uint64_t)(2 * k), bk + (uint64_t)(2 * k), idesc_s,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[stage]);
+        if (j > 0 && !pv(j - 1)) {
+          ok = false;
+          break;
+        }
+        if (++stage == FNS) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok && n_tiles > 0) ok = pv(n_tiles - 1);
+      if (!ok) *abort_flag = 1;
+      umma_commit(o_done);
+      mbar_wait(o_done, 0, p.err);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int stid = threadIdx.x - 64;  // 0..127
+    const int t = row / G;
+    const int head = kvh * G + row % G;
+    const bool valid_row = t0 + t < q_len;
+    const int row_pos = seq_len - q_len + t0 + t;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int sb = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)((j >> 1) & 1), p.err));
+      if (!ok) break;
+      if (stid == 0 && j == 0) FA_TL(3);
+      if (stid == 0) FA_TLJ(j, 4);
+      tc_fence_after();
+      const int kbase = k_lo + j * FN;
+      const bool mask = !valid_row || kbase + FN - 1 > row_pos || kbase + FN > seq_len ||
+                        (p.window > 0 && kbase <= row_pos - p.window);
+      const int win = p.window;
+      // Score of key kbase + col in log2 units, -inf where masked.
+      auto score = [&](uint32_t bits, int col) -> float {
+        const float v = __uint_as_float(bits) * p.scale_log2;
+        if (!mask) return v;
+        const int key = kbase + col;
+        bool in = valid_row && key <= row_pos && key < seq_len;
+        if (win > 0) in = in && key > row_pos - win;
+        return in ? v : -INFINITY;
+      };
+      const uint32_t s_row = tS + lane_base + sb * FN;
+      // One sweep over the row's 128 scores, two 32-column TMEM loads in
+      // flight per wait. With write: P = exp2(S - mu) as bf16 into the
+      // swizzled A tile of PV (keys c*32 .. c*32+31 are half c/2, 16-byte
+      // chunks (c%2)*4 .. +3); returns the row max, adds the row sum to *rs.
+      auto sweep = [&](float mu, bool write, float* rs) -> float {
+        float mx2[2] = {-INFINITY, -INFINITY};
+        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+        const bool live = mu != -INFINITY;
+#pragma unroll 1
+        for (int c2 = 0; c2 < 4; c2 += 2) {
+          uint32_t r[2][32];
+          tmem_ld_32x32b_x32(s_row + c2 * 32, r[0]);
+          tmem_ld_32x32b_x32(s_row + c2 * 32 + 32, r[1]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c = c2 + h;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int col = 8 * u + 2 * e;
+                const float va = score(r[h][col], c * 32 + col);
+                const float vb = score(r[h][col + 1], c * 32 + col + 1);
+                mx2[0] = fmaxf(mx2[0], va);
+                mx2[1] = fmaxf(mx2[1], vb);
+                if (write) {
+                  const float a = live ? fast_exp2(va - mu) : 0.f;
+                  const float b = live ? fast_exp2(vb - mu) : 0.f;
+                  rs4[e] += a + b;
+                  w[e] = pack_bf16x2(a, b);
+                }
+              }
+              if (write)
+                *reinterpret_cast<uint4*>(sP + (c >> 1) * kHalf + sw_off(row, (c & 1) * 4 + u)) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        if (write) *rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+        return fmaxf(mx2[0], mx2[1]);
+      };
+      // PV_{j-1} must be done with the P tile (and O) before they change.
+      if (j > 0) ok = mbar_wait(p_free, (uint32_t)((j - 1) & 1), p.err);
+      if (stid == 0) FA_TLJ(j, 5);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // Rows without a finite running max yet (first tile) take this tile's
+      // max first; otherwise the exponentials reuse the running max and the
+      // tile is redone only when its max exceeds it by more than 2^8.
+      if (__any_sync(0xffffffffu, m_used == -INFINITY)) {
+        const float mx = sweep(0.f, false, nullptr);
+        if (m_used == -INFINITY) m_used = mx;
+      }
+      float rs = 0.f;
+      float mx = sweep(m_used, true, &rs);
+      const bool resc = mx > m_used + 8.f;
+      if (__any_sync(0xffffffffu, resc)) {
+        const float alpha = resc ? exp2f(m_used - mx) : 1.f;
+        if (resc) {
+          l *= alpha;
+          m_used = mx;
+        }
+        if (j > 0) {
+          // O (final after PV_{j-1}) *= alpha for this row.
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x32(tO + lane_base + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+        mx = sweep(m_used, true, &rs);  // redo P with the new max
+      }
+      l += rs;
+      // S buffer fully read: the MMA may overwrite it.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      if (j == n_tiles - 1 && kbase + FN > seq_len &&
+          __all_sync(0xffffffffu, mbar_wait(&v_full[j % FNS], (uint32_t)((j / FNS) & 1), p.err))) {
+        // Zero the V rows past the sequence end (stale cache-block contents).
+        uint8_t* sv = sKV + (j % FNS) * kKVBytes + 2 * kHalf;
+        const int first_bad = max(0, seq_len - kbase);
+        for (int idx = stid; idx < (FN - first_bad) * 16; idx += 128) {
+          const int key = first_bad + idx / 16, c16 = idx % 16;
+          *reinterpret_cast<uint4*>(sv + (c16 >> 3) * kHalf + sw_off(key, c16 & 7)) =
+              make_uint4(0, 0, 0, 0);
+        }
+      }
+      // Generic-proxy writes -> visible to the tensor core, then one arrival
+      // per warp.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (stid == 0) FA_TLJ(j, 6);
+    }
+    if (stid == 0) FA_TL(4);
+    if (!ok) *abort_flag = 1;
+    if (ok && n_tiles > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(o_done, 0, p.err));
+      if (stid == 0) FA_TL(5);
+      if (ok) {
+        tc_fence_after();
+        float denom = l;
+        if (p.sinks != nullptr) {
+          if (m_used == -INFINITY) denom = 1.f;
+          else denom += exp2f(p.sinks[head] * 1.4426950408889634f - m_used);
+        }
+        const float inv = denom > 0.f ? 1.f / denom : 0.f;
+        __nv_bfloat16* dst = p.out + (size_t)(q0 + t0 + t) * p.o_stride_t + (size_t)head * FD;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);  // warp-collective: every lane
+          tmem_wait_ld();
+          if (valid_row) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[8 * v]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+            }
+          }
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 64) FA_TL(6);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemColsFa);
+  }
+  if (threadIdx.x == 0) FA_TL(7);
+#undef FA_TL
+#undef FA_TLJ
+}
+
+}  // namespace
+
+void fa_tc_set_timeline(unsigned long long* buf) {
+  cudaError_t e = cudaMemcpyToSymbol(g_fa_timeline, &buf, sizeof(buf));
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("fa_tc_set_timeline: ") + cudaGetErrorString(e));
+}
+
+bool fa_tc_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLLM_B200_ATTN_PREFILL_TC");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+uint32_t g_fa_v_lbo = 0, g_fa_v_sbo = 0;  // 0 = defaults (bring-up override)
+
+void fa_tc_set_v_strides(uint32_t lbo, uint32_t sbo) {
+  g_fa_v_lbo = lbo;
+  g_fa_v_sbo = sbo;
+}
+
+bool fa_tc_supported(const AttnArgs& a) {
+  const int G = a.Hkv > 0 ? a.Hq / a.Hkv : 0;
+  return !a.decode && a.head_dim == FD && a.num_blocks > 0 && G > 0 && FM % G == 0 &&
+         a.block_size >= 16 && a.block_size <= FN && (FN % a.block_size) == 0 &&
+         a.q_stride_t % 8 == 0;
+}
+
+void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
+  auto kernel = fa_tc_kernel;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFaSmem);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("fa_tc attribute: ") + cudaGetErrorString(e));
+    attr = true;
+  }
+  const int G = a.Hq / a.Hkv;
+  const int BS = a.block_size;
+  const long long blk_stride = a.kv_block_stride > 0 ? a.kv_block_stride
+                                                     : (long long)a.Hkv * BS * FD;
+  // q [T][Hq][D] with token stride q_stride_t: box 64 d x G heads x 128/G tokens.
+  CUtensorMap tq = make_tmap_3d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)a.num_tokens,
+                                (uint64_t)a.Hq, FD, (uint64_t)FD * 2, (uint64_t)a.q_stride_t * 2,
+                                (uint32_t)(FM / G), (uint32_t)G, 64);
+  const uint64_t rows = (uint64_t)a.Hkv * BS;
+  CUtensorMap tk = make_tmap_3d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                (uint64_t)a.num_blocks, rows, FD, (uint64_t)FD * 2,
+                                (uint64_t)blk_stride * 2, 1, (uint32_t)BS, 64);
+  CUtensorMap tv = make_tmap_3d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                (uint64_t)a.num_blocks, rows, FD, (uint64_t)FD * 2,
+                                (uint64_t)blk_stride * 2, 1, (uint32_t)BS, 64);
+  FaParams p{};
+  p.block_table = a.block_table;
+  p.seq_lens = a.seq_lens;
+  p.cu_q = a.cu_q;
+  p.sinks = a.sinks;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.num_seqs = a.num_seqs;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.G = G;
+  p.block_size = BS;
+  p.block_shift = __builtin_ctz(BS);
+  p.max_blocks = a.max_blocks;
+  p.window = a.window;
+  p.o_stride_t = a.o_stride_t;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  p.err = device_status_ptr(dev);
+  p.v_lbo = g_fa_v_lbo ? g_fa_v_lbo : (uint32_t)kHalf;  // next 64-d block of V
+  p.v_sbo = g_fa_v_sbo ? g_fa_v_sbo : 1024u;            // next 8-key group
+  const int max_qt = (a.max_q_len * G + FM - 1) / FM;
+  if (max_qt <= 0 || a.num_seqs <= 0) return;
+  launch_pdl(kernel, dim3(max_qt, a.num_seqs, a.Hkv), dim3(kFaThreads), kFaSmem, stream, nullptr,
+             tq, tk, tv, p);
+}
+
+}  // namespace b200

@@ -539,7 +539,9 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   p.rows_per_seq_max = a.max_q_len * (a.Hq / a.Hkv);
   if (p.num_splits > 1 && (a.part_o == nullptr || a.part_ml == nullptr))
     throw std::runtime_error("paged_attention: split-KV needs partial buffers");
-  if (a.head_dim == 128) {
+  if (!a.decode && fa_tc_enabled() && fa_tc_supported(a)) {
+    fa_tc_launch(a, stream);
+  } else if (a.head_dim == 128) {
     if (a.decode)
       launch_attn<128, 64, 4, 3, true>(p, stream);
     else

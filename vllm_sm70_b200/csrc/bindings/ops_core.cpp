@@ -83,6 +83,16 @@ void gemm_set_plan_op(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t cfg,
   gemm_set_plan((int)M, (int)N, (int)K, (int)epi, (int)cfg, (int)splits);
 }
 void gemm_clear_plans_op() { gemm_clear_plans(); }
+void attn_fa_set_timeline_op(const std::optional<at::Tensor>& buf) {
+  fa_tc_set_timeline(buf.has_value()
+                         ? reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>())
+                         : nullptr);
+}
+
+void attn_fa_set_v_strides_op(int64_t lbo, int64_t sbo) {
+  fa_tc_set_v_strides((uint32_t)lbo, (uint32_t)sbo);
+}
+
 void gemm_set_timeline_op(const std::optional<at::Tensor>& buf) {
   if (buf.has_value()) {
     TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong, "timeline: int64 CUDA tensor");
@@ -479,6 +489,7 @@ void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_c
   a.head_dim = (int)q.size(2);
   a.block_size = (int)k_cache.size(2);
   a.max_blocks = (int)block_table.size(1);
+  a.num_blocks = (int)k_cache.size(0);
   a.max_q_len = (int)max_q_len;
   a.window = (int)window;
   a.q_stride_t = (int)q.stride(0);
@@ -581,6 +592,8 @@ TORCH_LIBRARY(_b200_C, m) {
         &b200::gemm_set_plan_op);
   m.def("gemm_clear_plans() -> ()", &b200::gemm_clear_plans_op);
   m.def("gemm_set_timeline(Tensor? buf) -> ()", &b200::gemm_set_timeline_op);
+  m.def("attn_fa_set_v_strides(int lbo, int sbo) -> ()", &b200::attn_fa_set_v_strides_op);
+  m.def("attn_fa_set_timeline(Tensor? buf) -> ()", &b200::attn_fa_set_timeline_op);
   m.def("gemm_export_plans() -> int[]", &b200::gemm_export_plans_op);
   m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");
   m.def("gemm_bf16_config(int M, int N, int K, int epi) -> int", &b200::gemm_bf16_config);

@@ -167,7 +167,7 @@ def bench_prefill_attn(seqs=16, length=1024, hq=32, hkv=8, d=128, bs=16, iters=1
     flops = seqs * hq * length * length * d * 2.0  # causal: 2 GEMMs x L^2/2 x 2 flop
     pk = peaks()
     return {"kernel": "paged_attention_prefill", "seqs": seqs, "len": length, "hq": hq, "hkv": hkv,
-            "d": d, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1),
+            "d": d, "block": bs, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 1),
             "frac_tensor": round(flops / ms / 1e9 / pk["bf16_tflops"], 3), "peaks": pk["src"]}
 
 
@@ -190,6 +190,7 @@ def main(argv=None):
     ap.add_argument("--sweep", action="store_true", help="gemm: time every (cfg, splits)")
     ap.add_argument("--epi", type=int, default=0, help="gemm: 1 = fused SiLU*up epilogue")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays")
+    ap.add_argument("--block", type=int, default=16, help="attention: KV-cache block size")
     args = ap.parse_args(argv)
     global GRAPH
     GRAPH = args.graph
@@ -217,10 +218,10 @@ def main(argv=None):
         out.append({"kernel": "cublas_bf16", "M": args.M, "N": args.N, "K": args.K,
                     "ms": round(ms, 5), "tflops": round(2.0 * args.M * args.N * args.K / ms / 1e9, 1)})
     elif args.case == "decode-attn":
-        out.append(bench_decode_attn(args.batch, args.ctx, splits=max(1, args.splits),
-                                     iters=args.iters))
+        out.append(bench_decode_attn(args.batch, args.ctx, bs=args.block,
+                                     splits=max(1, args.splits), iters=args.iters))
     elif args.case == "prefill-attn":
-        out.append(bench_prefill_attn(args.seqs, args.len, iters=args.iters))
+        out.append(bench_prefill_attn(args.seqs, args.len, bs=args.block, iters=args.iters))
     else:
         for (M, N, K) in [(16384, 6144, 4096), (16384, 4096, 4096), (16384, 28672, 4096),
                           (16384, 4096, 14336), (256, 6144, 4096), (256, 4096, 4096),
