@@ -7,20 +7,22 @@
 //   warp 0     producer: the Q tile once (3-D tensor map over q [T][Hq][D],
 //              box 64 x G x 128/G, 128-byte swizzle), then each 128-key K and
 //              V tile from the paged cache (3-D maps over [block][head*BS +
-//              key][d], one box per (cache block, 64-column half)) into a
-//              2-stage mbarrier ring.
+//              key][d], one box per (cache block, 64-column half)) into
+//              separate 3-stage K and V rings, K one tile ahead of V.
 //   warp 1     TMEM owner + MMA issuer: S_j = Q K_j^T (M=N=K=128) into one of
-//              two TMEM S buffers, then O += P_{j-1} V_{j-1} (V as an MN-major
-//              B operand) into the TMEM O accumulator; S of the next tile is
-//              issued before the PV of the previous one so the tensor core
-//              works while the softmax warps do.
-//   warps 2-5  softmax, one query row per thread: tcgen05.ld of its S row,
-//              mask, running max, exp2, row sum, P (bf16) into a swizzled
-//              shared tile (the A operand of PV). O is rescaled in TMEM
-//              (tcgen05.ld / st) only when a row's running max grows by more
-//              than 2^8 over the max its exponentials use, so most tiles skip
-//              the correction; at the end each thread normalises its O row and
-//              stores it.
+//              two TMEM S buffers, then O += P_{j-1} V_{j-1} with P read from
+//              TMEM as the A operand and V as an MN-major B operand; S of the
+//              next tile is issued before the PV of the previous one so the
+//              tensor core works while the softmax warps do.
+//   warps 2-5  softmax, one query row per thread: tcgen05.ld of its S row
+//              (64 scores per wait), running max, exp2 via packed fp32 pairs,
+//              row sum, P as bf16 pairs tcgen05.st into one of two TMEM P
+//              buffers. Tiles that need no causal / window / padding mask run
+//              a mask-free sweep. O is rescaled in TMEM only when a row's
+//              running max grows by more than 2^8 over the max its
+//              exponentials use, so most tiles skip the correction; at the end
+//              each thread normalises its O row and stores it.
+// TMEM: S0 | S1 | O | P0 | P1 = 128 + 128 + 128 + 64 + 64 columns.
 // Rows of a partly filled last cache block hold stale data: their scores are
 // masked by selection, and the softmax warps zero the matching V rows before
 // the last PV (a zero P times a stale NaN would not be zero).
@@ -35,6 +37,7 @@
 #include <cstdlib>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 
 #include "attention/attn_api.h"
 #include "common/launch.h"
@@ -48,15 +51,14 @@ namespace {
 constexpr int FD = 128;                // head dim
 constexpr int FM = 128;                // query rows per CTA
 constexpr int FN = 128;                // keys per tile
-constexpr int FNS = 2;                 // K/V ring stages
+constexpr int FNS = 3;                 // K/V ring stages
 constexpr int kHalf = 128 * 128;       // 128 rows x 64 bf16
 constexpr int kQBytes = 2 * kHalf;     // Q: two 64-column halves
 constexpr int kKVBytes = 4 * kHalf;    // K halves, then V halves
-constexpr int kPBytes = 2 * kHalf;     // P: two 64-key halves
 constexpr int kBarBytes = 256;
-constexpr int kFaSmem = kQBytes + FNS * kKVBytes + kPBytes + kBarBytes + 1024;
+constexpr int kFaSmem = kQBytes + FNS * kKVBytes + kBarBytes + 1024;
 constexpr int kFaThreads = 192;
-constexpr uint32_t kTmemColsFa = 512;  // S0 | S1 | O | (unused)
+constexpr uint32_t kTmemColsFa = 512;  // S0 | S1 | O | P0 | P1 (P: 64 columns each)
 
 struct FaParams {
   const int* block_table;
@@ -93,8 +95,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + kQBytes;
-  uint8_t* sP = sKV + FNS * kKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + FNS * kKVBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;            // [FNS]
   uint64_t* k_empty = k_full + FNS;       // [FNS]
@@ -102,9 +103,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
   uint64_t* v_empty = v_full + FNS;       // [FNS]
   uint64_t* s_full = v_empty + FNS;       // [2]
   uint64_t* s_free = s_full + 2;          // [2]
-  uint64_t* p_full = s_free + 2;
-  uint64_t* p_free = p_full + 1;
-  uint64_t* o_done = p_free + 1;
+  uint64_t* p_full = s_free + 2;          // [2]
+  uint64_t* p_free = p_full + 2;          // [2]
+  uint64_t* o_done = p_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -149,8 +150,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], 4);
     }
-    mbar_init(p_full, 4);  // one arrival per softmax warp, after its P / V writes
-    mbar_init(p_free, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 4);  // one arrival per softmax warp, after its P / V writes
+      mbar_init(&p_free[b], 1);
+    }
     mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -172,7 +175,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     FA_TL(1);
   }
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tS = tmem_base, tO = tmem_base + 256;
+  const uint32_t tS = tmem_base, tO = tmem_base + 256, tP = tmem_base + 384;
   const int BS = p.block_size;
   const int blk_last = (seq_len - 1) >> p.block_shift;
 
@@ -185,19 +188,33 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       tma_load_3d(sQ, &tmq, q_full, 0, kvh * G, q0 + t0);
       tma_load_3d(sQ + kHalf, &tmq, q_full, 64, kvh * G, q0 + t0);
     }
+    // Cache-block ids are fetched ahead: one warp-wide load covers `per`
+    // tiles (lane L: tile L / nb, block L % nb), and the next group's load is
+    // in flight while the current group is issued.
+    const int per = 32 / nb;
+    auto load_ids = [&](int g) -> int {
+      const int tile = g * per + lane / nb;
+      if (tile >= n_tiles) return 0;
+      const int b = ((k_lo + tile * FN) >> p.block_shift) + lane % nb;
+      return __ldg(bt + min(b, blk_last));
+    };
+    int ids_cur = load_ids(0), ids_next = load_ids(1), g_cur = 0;
     // K runs one tile ahead of V: K_j's slot frees right after S_j, V_j's
     // only after PV_j, so K_{j+1} never queues behind V_j's slot.
     auto issue = [&](int j, bool is_v) -> bool {
-      const int b0 = (k_lo + j * FN) >> p.block_shift;
-      int my = 0;
-      if (lane < nb) my = __ldg(bt + min(b0 + lane, blk_last));
+      const int g = j / per;
+      if (is_v && g > g_cur) {
+        ids_cur = ids_next;
+        ids_next = load_ids(++g_cur + 1);
+      }
+      const int ids = g == g_cur ? ids_cur : ids_next;
       const int st = j % FNS;
       const uint32_t ph = (uint32_t)((j / FNS) & 1);
       uint64_t* fullb = is_v ? &v_full[st] : &k_full[st];
       int ok = 1;
       if (lane == 0) {
         ok = mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ph ^ 1u, p.err) ? 1 : 0;
-        if (!is_v) FA_TLJ(j, 0);
+        FA_TLJ(j, is_v ? 1 : 0);
         if (ok) mbar_arrive_expect_tx(fullb, (uint32_t)(2 * kHalf));
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -205,7 +222,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       uint8_t* dst = sKV + st * kKVBytes + (is_v ? 2 * kHalf : 0);
       const CUtensorMap* tm = is_v ? &tmv : &tmk;
       for (int i = 0; i < nb; ++i) {
-        const int blk = __shfl_sync(0xffffffffu, my, i);
+        const int blk = __shfl_sync(0xffffffffu, ids, (j % per) * nb + i);
         if (lane == 0) {
           tma_load_3d(dst + i * BS * 128, tm, fullb, 0, kvh * BS, blk);
           tma_load_3d(dst + kHalf + i * BS * 128, tm, fullb, 64, kvh * BS, blk);
@@ -227,21 +244,19 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       bool ok = mbar_wait(q_full, 0, p.err);
       FA_TL(2);
       auto pv = [&](int i) -> bool {
-        const int st = i % FNS;
-        if (!mbar_wait(p_full, (uint32_t)(i & 1), p.err) ||
+        const int st = i % FNS, pb = i & 1;
+        if (!mbar_wait(&p_full[pb], (uint32_t)((i >> 1) & 1), p.err) ||
             !mbar_wait(&v_full[st], (uint32_t)((i / FNS) & 1), p.err))
           return false;
         FA_TLJ(i, 3);
         tc_fence_after();
         const uint32_t sv = smem_u32(sKV + st * kKVBytes + 2 * kHalf);
-        const uint32_t sp = smem_u32(sP);
 #pragma unroll
         for (int s = 0; s < FN / 16; ++s) {
-          const uint64_t ap = umma_desc_sw128(sp + (s >> 2) * kHalf) + (uint64_t)(2 * (s & 3));
           const uint64_t bv = umma_desc_sw128_mn(sv + s * 16 * 128, p.v_lbo, p.v_sbo);
-          umma_f16(tO, ap, bv, idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tP + pb * 64 + s * 8, bv, idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
         }
-        umma_commit(p_free);
+        umma_commit(&p_free[pb]);
         umma_commit(&v_empty[st]);
         return true;
       };
@@ -294,87 +309,92 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     const bool valid_row = t0 + t < q_len;
     const int row_pos = seq_len - q_len + t0 + t;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;
+    // Keys this row may attend to: [key_lo, key_hi] (empty for padding rows).
+    const int key_hi = valid_row ? min(row_pos, seq_len - 1) : -1;
+    const int key_lo = p.window > 0 ? row_pos - p.window + 1 : 0;
+    const float sc = p.scale_log2;
+    const uint64_t sc2 = f32x2_pack(sc, sc);
+    float m_used = -INFINITY, l = 0.f;  // running max (log2 units) and row sum
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
+      const int sb = j & 1, pb = j & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (uint32_t)((j >> 1) & 1), p.err));
       if (!ok) break;
       if (stid == 0 && j == 0) FA_TL(3);
       if (stid == 0) FA_TLJ(j, 4);
       tc_fence_after();
       const int kbase = k_lo + j * FN;
-      const bool mask = !valid_row || kbase + FN - 1 > row_pos || kbase + FN > seq_len ||
-                        (p.window > 0 && kbase <= row_pos - p.window);
-      const int win = p.window;
-      // Score of key kbase + col in log2 units, -inf where masked.
-      auto score = [&](uint32_t bits, int col) -> float {
-        const float v = __uint_as_float(bits) * p.scale_log2;
-        if (!mask) return v;
-        const int key = kbase + col;
-        bool in = valid_row && key <= row_pos && key < seq_len;
-        if (win > 0) in = in && key > row_pos - win;
-        return in ? v : -INFINITY;
-      };
+      const int lo = key_lo - kbase, hi = key_hi - kbase;  // in-tile bounds
+      const bool masked = __any_sync(0xffffffffu, lo > 0 || hi < FN - 1);
       const uint32_t s_row = tS + lane_base + sb * FN;
-      // One sweep over the row's 128 scores, two 32-column TMEM loads in
-      // flight per wait. With write: P = exp2(S - mu) as bf16 into the
-      // swizzled A tile of PV (keys c*32 .. c*32+31 are half c/2, 16-byte
-      // chunks (c%2)*4 .. +3); returns the row max, adds the row sum to *rs.
-      auto sweep = [&](float mu, bool write, float* rs) -> float {
-        float mx2[2] = {-INFINITY, -INFINITY};
-        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-        const bool live = mu != -INFINITY;
+      const uint32_t p_row = tP + lane_base + pb * 64;
+      // One sweep over the row's 128 raw scores, 64 per TMEM wait. With
+      // WRITE: P = exp2(S * scale - mu) packed as bf16 pairs into this row's
+      // lane of the P buffer (key 2c, 2c+1 -> column c), row sum into *rs.
+      // Returns the row max in log2 units.
+      auto sweep = [&](auto masked_c, auto write_c, float mu, float* rs) -> float {
+        constexpr bool kMasked = decltype(masked_c)::value;
+        constexpr bool kWrite = decltype(write_c)::value;
+        float mxa = -INFINITY, mxb = -INFINITY;
+        uint64_t acc = f32x2_pack(0.f, 0.f);
+        const float mu_eff = mu == -INFINITY ? 0.f : mu;
+        const uint64_t nmu2 = f32x2_pack(-mu_eff, -mu_eff);
 #pragma unroll 1
-        for (int c2 = 0; c2 < 4; c2 += 2) {
+        for (int h = 0; h < 2; ++h) {
           uint32_t r[2][32];
-          tmem_ld_32x32b_x32(s_row + c2 * 32, r[0]);
-          tmem_ld_32x32b_x32(s_row + c2 * 32 + 32, r[1]);
+          tmem_ld_32x32b_x32(s_row + h * 64, r[0]);
+          tmem_ld_32x32b_x32(s_row + h * 64 + 32, r[1]);
           tmem_wait_ld();
+          uint32_t w[32];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = c2 + h;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint32_t w[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int col = 8 * u + 2 * e;
-                const float va = score(r[h][col], c * 32 + col);
-                const float vb = score(r[h][col + 1], c * 32 + col + 1);
-                mx2[0] = fmaxf(mx2[0], va);
-                mx2[1] = fmaxf(mx2[1], vb);
-                if (write) {
-                  const float a = live ? fast_exp2(va - mu) : 0.f;
-                  const float b = live ? fast_exp2(vb - mu) : 0.f;
-                  rs4[e] += a + b;
-                  w[e] = pack_bf16x2(a, b);
-                }
-              }
-              if (write)
-                *reinterpret_cast<uint4*>(sP + (c >> 1) * kHalf + sw_off(row, (c & 1) * 4 + u)) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
+          for (int i = 0; i < 32; ++i) {
+            float va = __uint_as_float(r[i >> 4][(2 * i) & 31]);
+            float vb = __uint_as_float(r[i >> 4][(2 * i + 1) & 31]);
+            if constexpr (kMasked) {
+              const int k = h * 64 + 2 * i;
+              if (k < lo || k > hi) va = -INFINITY;
+              if (k + 1 < lo || k + 1 > hi) vb = -INFINITY;
+            }
+            mxa = fmaxf(mxa, va);
+            mxb = fmaxf(mxb, vb);
+            if constexpr (kWrite) {
+              float ea, eb;
+              f32x2_unpack(f32x2_fma(f32x2_pack(va, vb), sc2, nmu2), ea, eb);
+              ea = fast_exp2(ea);
+              eb = fast_exp2(eb);
+              const uint64_t e2 = f32x2_pack(ea, eb);
+              acc = f32x2_add(acc, e2);
+              w[i] = pack_bf16x2(ea, eb);
             }
           }
+          if constexpr (kWrite) tmem_st_32x32b_x32(p_row + h * 32, w);
         }
-        if (write) *rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-        return fmaxf(mx2[0], mx2[1]);
+        if constexpr (kWrite) {
+          float a0, a1;
+          f32x2_unpack(acc, a0, a1);
+          *rs = a0 + a1;
+        }
+        return fmaxf(mxa, mxb) * sc;
       };
-      // PV_{j-1} must be done with the P tile (and O) before they change.
-      if (j > 0) ok = mbar_wait(p_free, (uint32_t)((j - 1) & 1), p.err);
+      using T_ = std::true_type;
+      using F_ = std::false_type;
+      auto sweep_w = [&](float mu, float* rs) -> float {
+        return masked ? sweep(T_{}, T_{}, mu, rs) : sweep(F_{}, T_{}, mu, rs);
+      };
+      // Rows without a finite running max yet (first tile) take this tile's
+      // max first; afterwards exponentials reuse the running max and a tile
+      // is redone only when its max exceeds it by more than 2^8.
+      if (__any_sync(0xffffffffu, m_used == -INFINITY)) {
+        const float mx = masked ? sweep(T_{}, F_{}, 0.f, nullptr) : sweep(F_{}, F_{}, 0.f, nullptr);
+        if (m_used == -INFINITY) m_used = mx;
+      }
+      // P buffer pb is free once PV_{j-2} has completed.
+      if (j >= 2) ok = mbar_wait(&p_free[pb], (uint32_t)(((j - 2) >> 1) & 1), p.err);
       if (stid == 0) FA_TLJ(j, 5);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      tc_fence_after();
-      // Rows without a finite running max yet (first tile) take this tile's
-      // max first; otherwise the exponentials reuse the running max and the
-      // tile is redone only when its max exceeds it by more than 2^8.
-      if (__any_sync(0xffffffffu, m_used == -INFINITY)) {
-        const float mx = sweep(0.f, false, nullptr);
-        if (m_used == -INFINITY) m_used = mx;
-      }
       float rs = 0.f;
-      float mx = sweep(m_used, true, &rs);
+      float mx = sweep_w(m_used, &rs);
       const bool resc = mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, resc)) {
         const float alpha = resc ? exp2f(m_used - mx) : 1.f;
@@ -383,7 +403,11 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
           m_used = mx;
         }
         if (j > 0) {
-          // O (final after PV_{j-1}) *= alpha for this row.
+          // O (final once PV_{j-1} completes) *= alpha for this row.
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&p_free[pb ^ 1], (uint32_t)(((j - 1) >> 1) & 1), p.err));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -393,12 +417,13 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
             tmem_st_32x32b_x32(tO + lane_base + c * 32, o);
           }
-          tmem_wait_st();
         }
-        mx = sweep(m_used, true, &rs);  // redo P with the new max
+        tmem_wait_st();
+        mx = sweep_w(m_used, &rs);  // redo P with the new max
       }
       l += rs;
-      // S buffer fully read: the MMA may overwrite it.
+      tmem_wait_st();
+      // S buffer fully read, P and any O correction written.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
@@ -412,12 +437,11 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
           *reinterpret_cast<uint4*>(sv + (c16 >> 3) * kHalf + sw_off(key, c16 & 7)) =
               make_uint4(0, 0, 0, 0);
         }
+        // Generic-proxy writes -> visible to the tensor core.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
       }
-      // Generic-proxy writes -> visible to the tensor core, then one arrival
-      // per warp.
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[pb]);
       if (stid == 0) FA_TLJ(j, 6);
     }
     if (stid == 0) FA_TL(4);
