@@ -22,7 +22,7 @@ def _case(lens_q, lens_ctx, hq, hkv, d, bs, seed=0):
 
 
 @pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (128, 8, 1), (256, 16, 2), (64, 8, 8)])
-@pytest.mark.parametrize("bs", [16, 32])
+@pytest.mark.parametrize("bs", [16, 32, 128])
 def test_decode(b200_ops, d, hq, hkv, bs, rel_err):
     lens = [1, 17, 300, 1029, 64]
     q, kc, vc, bt, sl, cu = _case([1] * len(lens), lens, hq, hkv, d, bs)
@@ -94,6 +94,26 @@ def test_decode_interleaved_cache(b200_ops, bs, rel_err):
     out = torch.empty_like(q)
     A.paged_attention(out, q, both[:, 0], both[:, 1], bt, sl, cu, 1, 0.09, decode=True)
     ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 0.09)
+    assert rel_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("bs", [16, 128])
+@pytest.mark.parametrize("decode", [True, False])
+def test_stale_cache_rows_nan(b200_ops, bs, decode, rel_err):
+    """Cache rows past each sequence end hold NaN (stale contents of a
+    recycled block): masking and V-row zeroing keep them out of the output."""
+    lens = [1, 17, 300, 129]
+    lens_q = [1] * 4 if decode else [1, 17, 44, 129]
+    q, kc, vc, bt, sl, cu = _case(lens_q, lens, 32, 8, 128, bs, seed=8)
+    for i, L in enumerate(lens):
+        if L % bs:
+            blk = int(bt[i, (L - 1) // bs])
+            kc[blk, :, L % bs:] = float("nan")
+            vc[blk, :, L % bs:] = float("nan")
+    out = torch.empty_like(q)
+    A.paged_attention(out, q, kc, vc, bt, sl, cu, max(lens_q), 0.09, decode=decode)
+    ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 0.09)
+    assert torch.isfinite(out.float()).all()
     assert rel_err(out, ref) < 2e-2
 
 

@@ -57,7 +57,7 @@ constexpr int kQBytes = 2 * kHalf;     // Q: two 64-column halves
 constexpr int kKVBytes = 4 * kHalf;    // K halves, then V halves
 constexpr int kBarBytes = 256;
 constexpr int kFaSmem = kQBytes + FNS * kKVBytes + kBarBytes + 1024;
-constexpr int kFaThreads = 192;
+constexpr int kFaThreads = 224;
 constexpr uint32_t kTmemColsFa = 512;  // S0 | S1 | O | P0 | P1 (P: 64 columns each)
 
 struct FaParams {
@@ -179,11 +179,12 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
   const int BS = p.block_size;
   const int blk_last = (seq_len - 1) >> p.block_shift;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------- producers (K: 0, V: 6)
+    const bool is_v = warp == 6;
     const int* bt = p.block_table + (size_t)seq * p.max_blocks;
     const int nb = FN / BS;
-    if (lane == 0) {
+    if (!is_v && lane == 0) {
       mbar_arrive_expect_tx(q_full, (uint32_t)kQBytes);
       tma_load_3d(sQ, &tmq, q_full, 0, kvh * G, q0 + t0);
       tma_load_3d(sQ + kHalf, &tmq, q_full, 64, kvh * G, q0 + t0);
@@ -199,11 +200,11 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       return __ldg(bt + min(b, blk_last));
     };
     int ids_cur = load_ids(0), ids_next = load_ids(1), g_cur = 0;
-    // K runs one tile ahead of V: K_j's slot frees right after S_j, V_j's
-    // only after PV_j, so K_{j+1} never queues behind V_j's slot.
-    auto issue = [&](int j, bool is_v) -> bool {
+    // K and V stream from separate warps: K_j's slot frees right after S_j,
+    // V_j's only after PV_j, so K never queues behind V.
+    auto issue = [&](int j) -> bool {
       const int g = j / per;
-      if (is_v && g > g_cur) {
+      if (g > g_cur) {
         ids_cur = ids_next;
         ids_next = load_ids(++g_cur + 1);
       }
@@ -221,20 +222,19 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       if (!ok) return false;
       uint8_t* dst = sKV + st * kKVBytes + (is_v ? 2 * kHalf : 0);
       const CUtensorMap* tm = is_v ? &tmv : &tmk;
-      for (int i = 0; i < nb; ++i) {
-        const int blk = __shfl_sync(0xffffffffu, ids, (j % per) * nb + i);
-        if (lane == 0) {
-          tma_load_3d(dst + i * BS * 128, tm, fullb, 0, kvh * BS, blk);
-          tma_load_3d(dst + kHalf + i * BS * 128, tm, fullb, 64, kvh * BS, blk);
-        }
+      // One (cache block, column half) per lane: a bulk-tensor instruction
+      // costs the issuing warp a few hundred ns plus a little per active
+      // lane, so the tile's 2 * nb boxes go out as one warp-wide instruction.
+      const int bi = lane % nb;
+      const int blk = __shfl_sync(0xffffffffu, ids, (j % per) * nb + bi);
+      if (lane < 2 * nb) {
+        const int h = lane / nb;
+        tma_load_3d(dst + h * kHalf + bi * BS * 128, tm, fullb, h * 64, kvh * BS, blk);
       }
       return true;
     };
-    bool ok = n_tiles == 0 || issue(0, false);
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      if (j + 1 < n_tiles) ok = issue(j + 1, false);
-      if (ok) ok = issue(j, true);
-    }
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) ok = issue(j);
     if (!ok) *abort_flag = 1;
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer

@@ -27,11 +27,15 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
 #include "attention/attn_api.h"
 #include "common/launch.h"
+#include "common/ptx.cuh"
+#include "common/tmap.h"
+#include "ops_api.h"
 
 namespace b200 {
 namespace {
@@ -489,6 +493,376 @@ __global__ void combine_splits_kernel(const Params p, int T) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode / spec-verify on TMA. Four consumer warps do the math of the decode
+// variant above (16 GQA-packed rows, each warp a quarter of every K/V tile,
+// warp-order merge); a fifth warp streams the K/V tiles with 3-D tensor
+// copies (box 64 columns x min(BS, KT) keys of one cache block, 128-byte
+// swizzle) into a STAGES-deep mbarrier ring. The copies of one tile go out as
+// one warp-wide instruction, a cache block (and column half, K or V) per
+// lane: a bulk-tensor instruction costs its warp a few hundred ns however many
+// lanes it carries, so per-block serial issue would cap the stream far below
+// HBM rate. The consumers issue no load instructions at all, so their issue
+// slots go to the MMAs and the softmax; tiles that need no mask skip the
+// masking code, and O is rescaled only when a row's max grows by more than
+// 2^8 over the max its exponentials use.
+// Rows of a cache block past the sequence end hold stale data: their scores
+// are masked by selection and each warp zeroes its V rows there before PV.
+//
+// Shared layout of a K (or V) tile: D/64 column halves of KT rows x 128 B,
+// 16-byte chunk c of row r at (c ^ (r & 7)) within the row.
+__device__ __forceinline__ uint32_t tma_tile_off(int r, int ch, int rows) {
+  return (uint32_t)((ch >> 3) * rows * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+
+constexpr int kDecThreads = 160;
+
+template <int D, int KT, int STAGES>
+constexpr int decode_tma_smem() {
+  return STAGES * 4 * KT * D + 16 * D * 2 + 2 * STAGES * 8 + 1024;
+}
+
+template <int D, int KT, int STAGES>
+__global__ void __launch_bounds__(kDecThreads)
+decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                  const Params p, unsigned int* err) {
+  constexpr int NW = 4, ROWS = 16, KW = KT / NW, CH = D / 8, H = D / 64;
+  constexpr int kTile = KT * D * 2;
+  constexpr int kStage = 2 * kTile;
+  static_assert(KW % 16 == 0, "keys per warp must be a multiple of 16");
+  static_assert(STAGES * kStage >= (NW * 16 * D + NW * 32) * 4, "merge buffer must fit the ring");
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* ring = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sQ = ring + STAGES * kStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sQ + ROWS * D * 2);
+  uint64_t* empty = full + STAGES;
+
+  pdl_wait();
+  pdl_trigger();
+  const int seq = blockIdx.y;
+  const int kvh = blockIdx.z % p.Hkv;
+  const int split = blockIdx.z / p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int q0 = p.cu_q[seq];
+  const int q_len = p.cu_q[seq + 1] - q0;
+  const int seq_len = p.seq_lens[seq];
+  const int rows_total = q_len * G;
+  const int rt = blockIdx.x;
+  if (rt * ROWS >= rows_total || q_len == 0) return;
+  const int row0 = rt * ROWS;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+
+  const int first_pos = seq_len - q_len + row0 / G;
+  const int last_row = min(row0 + ROWS, rows_total) - 1;
+  const int last_pos = seq_len - q_len + last_row / G;
+  int k_begin = p.window > 0 ? max(0, first_pos - p.window + 1) : 0;
+  int k_end = last_pos + 1;
+  if (p.num_splits > 1) {
+    const int span = k_end - k_begin;
+    const int per = ((span + p.num_splits - 1) / p.num_splits + KT - 1) / KT * KT;
+    const int b = k_begin + split * per;
+    k_end = min(k_end, b + per);
+    k_begin = b;
+  }
+  k_begin = (k_begin / KT) * KT;
+  const int n_tiles = k_end > k_begin ? (k_end - k_begin + KT - 1) / KT : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    fence_barrier_init();
+  }
+  // Q rows (row r -> token r / G, head r % G); padding rows are zero.
+  for (int c = tid; c < ROWS * CH; c += kDecThreads) {
+    const int r = c / CH, ch = c % CH;
+    const int gr = row0 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (gr < rows_total) {
+      const int tok = gr / G, h = kvh * G + gr % G;
+      v = *reinterpret_cast<const uint4*>(p.q + (size_t)(q0 + tok) * p.q_stride_t + (size_t)h * D +
+                                          ch * 8);
+    }
+    *reinterpret_cast<uint4*>(sQ + swz<D>(r, ch)) = v;
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    // ------------------------------------------------------------ producer
+    const int BS = p.block_size;
+    const int nb = BS >= KT ? 1 : KT / BS;
+    const int rows_box = BS >= KT ? KT : BS;
+    const int nlanes = 2 * H * nb;
+    const int* bt = p.block_table + (size_t)seq * p.max_blocks;
+    const int blk_last = k_end > 0 ? (k_end - 1) >> p.block_shift : 0;
+    auto blk_of = [&](int t) -> int {
+      const int b = ((k_begin + t * KT) >> p.block_shift) + lane % nb;
+      return __ldg(bt + min(b, blk_last));
+    };
+    int cur = n_tiles > 0 ? blk_of(0) : 0;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int nxt = t + 1 < n_tiles ? blk_of(t + 1) : 0;  // ids one tile ahead
+      const int st = t % STAGES;
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait(&empty[st], (uint32_t)(((t / STAGES) & 1) ^ 1), err) ? 1 : 0;
+        if (ok) mbar_arrive_expect_tx(&full[st], (uint32_t)kStage);
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int kbase = k_begin + t * KT;
+      const int y = kvh * BS + (BS > KT ? (kbase & (BS - 1)) : 0);
+      uint8_t* stage = ring + st * kStage;
+      for (int idx = lane; idx < nlanes; idx += 32) {
+        const int kv = idx / (H * nb), h = (idx / nb) % H, i = idx % nb;
+        tma_load_3d(stage + kv * kTile + h * KT * 128 + i * rows_box * 128, kv ? &tmv : &tmk,
+                    &full[st], h * 64, y, cur);
+      }
+      cur = nxt;
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int key_off = warp * KW;
+  uint32_t qf[D / 16][4];
+  {
+    const int r = (lane % 8) + ((lane / 8) % 2) * 8;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int ch = kk * 2 + lane / 16;
+      ldmatrix_x4(smem_addr(sQ) + swz<D>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    }
+  }
+  const int g = lane / 4, t4 = lane % 4;
+  int row_pos[2];
+  bool row_valid[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int gr = row0 + g + h * 8;
+    row_valid[h] = gr < rows_total;
+    row_pos[h] = seq_len - q_len + (row_valid[h] ? gr / G : 0);
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};  // max the exponentials use
+  float l_run[2] = {0.f, 0.f};
+
+  bool ok = true;
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int st = tile % STAGES;
+    ok = mbar_wait(&full[st], (uint32_t)((tile / STAGES) & 1), err);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const uint32_t sK = smem_addr(ring + st * kStage);
+    const uint32_t sV = sK + kTile;
+    const int kbase = k_begin + tile * KT + key_off;
+    if (kbase + KW > k_end) {
+      // This warp's rows past the range end: zero V (stale cache rows).
+      uint8_t* v = ring + st * kStage + kTile;
+      for (int c = lane; c < KW * CH; c += 32) {
+        const int r = key_off + c / CH;
+        if (k_begin + tile * KT + r >= k_end)
+          *reinterpret_cast<uint4*>(v + tma_tile_off(r, c % CH, KT)) = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
+
+    float s[KW / 8][4];
+#pragma unroll
+    for (int n = 0; n < KW / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int n2 = 0; n2 < KW / 16; ++n2) {
+        const int key = key_off + n2 * 16 + (lane % 8) + (lane / 16) * 8;
+        const int ch = kk * 2 + (lane / 8) % 2;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(sK + tma_tile_off(key, ch, KT), b0, b1, b2, b3);
+        mma_bf16(s[2 * n2], qf[kk], b0, b1);
+        mma_bf16(s[2 * n2 + 1], qf[kk], b2, b3);
+      }
+    }
+
+    // Every key of this warp's slice visible to every row?
+    const bool need_mask = kbase + KW - 1 > first_pos || kbase + KW > k_end ||
+                           (p.window > 0 && kbase <= last_pos - p.window);
+    float mx[2] = {-INFINITY, -INFINITY};
+    if (need_mask) {
+#pragma unroll
+      for (int n = 0; n < KW / 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e / 2;
+          const int key = kbase + n * 8 + t4 * 2 + (e & 1);
+          bool in = row_valid[h] && key <= row_pos[h] && key < k_end;
+          if (p.window > 0) in = in && key > row_pos[h] - p.window;
+          s[n][e] = in ? s[n][e] * p.scale_log2 : -INFINITY;
+          mx[h] = fmaxf(mx[h], s[n][e]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < KW / 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s[n][e] *= p.scale_log2;
+          mx[e / 2] = fmaxf(mx[e / 2], s[n][e]);
+        }
+      }
+    }
+    bool resc = false;
+    float corr[2] = {1.f, 1.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2));
+      if (mx[h] > m_run[h] + 8.f) {  // also the first finite max (m_run = -inf)
+        corr[h] = exp2f(m_run[h] - mx[h]);
+        m_run[h] = mx[h];
+        l_run[h] *= corr[h];
+        resc = true;
+      }
+    }
+    if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= corr[0];
+        o[i][1] *= corr[0];
+        o[i][2] *= corr[1];
+        o[i][3] *= corr[1];
+      }
+    }
+    const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
+    const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
+    uint32_t pf[KW / 16][4];
+#pragma unroll
+    for (int n = 0; n < KW / 8; ++n) {
+      const float e0 = exp2f(s[n][0] - mu0), e1 = exp2f(s[n][1] - mu0);
+      const float e2 = exp2f(s[n][2] - mu1), e3 = exp2f(s[n][3] - mu1);
+      l_run[0] += e0 + e1;
+      l_run[1] += e2 + e3;
+      const int kk = n / 2, hi = n % 2;
+      pf[kk][hi * 2 + 0] = pack2(e0, e1);
+      pf[kk][hi * 2 + 1] = pack2(e2, e3);
+    }
+#pragma unroll
+    for (int kk = 0; kk < KW / 16; ++kk) {
+#pragma unroll
+      for (int d2 = 0; d2 < D / 16; ++d2) {
+        const int key = key_off + kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+        const int ch = d2 * 2 + lane / 16;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(sV + tma_tile_off(key, ch, KT), b0, b1, b2, b3);
+        mma_bf16(o[2 * d2], pf[kk], b0, b1);
+        mma_bf16(o[2 * d2 + 1], pf[kk], b2, b3);
+      }
+    }
+    // Generic-proxy reads (and any zeroing) done before the TMA refills.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffff, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffff, l_run[h], 2);
+  }
+  // Warp-order merge through the (now idle) ring; consumer warps only.
+  named_barrier_sync(1, NW * 32);
+  float* sO = reinterpret_cast<float*>(ring);  // [NW][16][D]
+  float* sM = sO + NW * 16 * D;                 // [NW][16]
+  float* sL = sM + NW * 16;                     // [NW][16]
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = g + h * 8;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const int d = i * 8 + t4 * 2;
+      *reinterpret_cast<float2*>(&sO[(warp * 16 + r) * D + d]) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
+    }
+    if (t4 == 0) {
+      sM[warp * 16 + r] = m_run[h];
+      sL[warp * 16 + r] = l_run[h];
+    }
+  }
+  named_barrier_sync(1, NW * 32);
+  for (int idx = tid; idx < 16 * D; idx += NW * 32) {
+    const int r = idx / D, d = idx % D;
+    const int gr = row0 + r;
+    if (gr >= rows_total) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sM[w * 16 + r]);
+    float L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = sM[w * 16 + r];
+      const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      L += sL[w * 16 + r] * sc;
+      acc += sO[(w * 16 + r) * D + d] * sc;
+    }
+    const int tok = gr / G;
+    const int head = kvh * G + gr % G;
+    if (p.num_splits > 1) {
+      const size_t T = (size_t)p.cu_q[p.num_seqs];
+      const size_t base = ((size_t)split * T + (q0 + tok)) * p.Hq + head;
+      p.part_o[base * D + d] = L > 0.f ? acc / L : 0.f;
+      if (d == 0) {
+        p.part_ml[base * 2 + 0] = L > 0.f ? M : -INFINITY;
+        p.part_ml[base * 2 + 1] = L;
+      }
+    } else {
+      float denom = L;
+      if (p.sinks != nullptr) {
+        if (M == -INFINITY || L == 0.f) denom = 1.f;
+        else denom += exp2f(p.sinks[head] * 1.4426950408889634f - M);
+      }
+      const float inv = denom > 0.f ? 1.f / denom : 0.f;
+      p.out[(size_t)(q0 + tok) * p.o_stride_t + (size_t)head * D + d] = __float2bfloat16_rn(acc * inv);
+    }
+  }
+}
+
+template <int D, int KT, int STAGES>
+void launch_decode_tma(const Params& p, const AttnArgs& a, cudaStream_t stream) {
+  constexpr int smem = decode_tma_smem<D, KT, STAGES>();
+  auto kernel = decode_tma_kernel<D, KT, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("decode_tma attribute: ") + cudaGetErrorString(e));
+    attr = true;
+  }
+  const int BS = a.block_size;
+  const uint32_t rows_box = (uint32_t)(BS >= KT ? KT : BS);
+  const uint64_t rows = (uint64_t)a.Hkv * BS;
+  const uint64_t bstride = (uint64_t)p.kv_block_stride * 2;
+  CUtensorMap tk = make_tmap_3d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                (uint64_t)a.num_blocks, rows, D, (uint64_t)D * 2, bstride, 1,
+                                rows_box, 64);
+  CUtensorMap tv = make_tmap_3d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                (uint64_t)a.num_blocks, rows, D, (uint64_t)D * 2, bstride, 1,
+                                rows_box, 64);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int row_tiles = (p.rows_per_seq_max + 15) / 16;
+  dim3 grid(row_tiles, p.num_seqs, p.Hkv * p.num_splits);
+  launch_pdl(kernel, grid, dim3(kDecThreads), smem, stream, nullptr, tk, tv, p,
+             device_status_ptr(dev));
+}
+
+bool decode_tma_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLLM_B200_ATTN_DECODE_TMA");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int D, int KT, int NW, int STAGES, bool DECODE>
 void launch_attn(const Params& p, cudaStream_t stream) {
   constexpr int ROWS = DECODE ? 16 : 16 * NW;
@@ -539,8 +913,18 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   p.rows_per_seq_max = a.max_q_len * (a.Hq / a.Hkv);
   if (p.num_splits > 1 && (a.part_o == nullptr || a.part_ml == nullptr))
     throw std::runtime_error("paged_attention: split-KV needs partial buffers");
+  const bool tma_ok = a.num_blocks > 0 && a.block_size >= 8 && a.q_stride_t % 8 == 0 &&
+                      p.kv_block_stride % 8 == 0 &&
+                      (reinterpret_cast<uintptr_t>(a.k_cache) & 15u) == 0 &&
+                      (reinterpret_cast<uintptr_t>(a.v_cache) & 15u) == 0;
   if (!a.decode && fa_tc_enabled() && fa_tc_supported(a)) {
     fa_tc_launch(a, stream);
+  } else if (a.decode && tma_ok && decode_tma_enabled() &&
+             (a.head_dim == 128 || a.head_dim == 64)) {
+    if (a.head_dim == 128)
+      launch_decode_tma<128, 64, 3>(p, a, stream);
+    else
+      launch_decode_tma<64, 64, 4>(p, a, stream);
   } else if (a.head_dim == 128) {
     if (a.decode)
       launch_attn<128, 64, 4, 3, true>(p, stream);
