@@ -522,8 +522,15 @@ constexpr int decode_tma_smem() {
   return STAGES * 4 * KT * D + 16 * D * 2 + 2 * STAGES * 8 + 1024;
 }
 
+// CTAs per SM the shared-memory footprint allows (228 KB per SM, 1 KB
+// reserved per CTA); the register budget is capped to match.
 template <int D, int KT, int STAGES>
-__global__ void __launch_bounds__(kDecThreads)
+constexpr int decode_tma_ctas() {
+  return (decode_tma_smem<D, KT, STAGES>() + 1024) * 3 <= 228 * 1024 ? 3 : 2;
+}
+
+template <int D, int KT, int STAGES>
+__global__ void __launch_bounds__(kDecThreads, (decode_tma_ctas<D, KT, STAGES>()))
 decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const Params p, unsigned int* err) {
   constexpr int NW = 4, ROWS = 16, KW = KT / NW, CH = D / 8, H = D / 64;
@@ -921,8 +928,11 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
     fa_tc_launch(a, stream);
   } else if (a.decode && tma_ok && decode_tma_enabled() &&
              (a.head_dim == 128 || a.head_dim == 64)) {
+    // Two 64-key stages per CTA and three CTAs per SM measured faster than
+    // three stages at two CTAs per SM (more consumer warps per SM keep the
+    // same bytes in flight).
     if (a.head_dim == 128)
-      launch_decode_tma<128, 64, 3>(p, a, stream);
+      launch_decode_tma<128, 64, 2>(p, a, stream);
     else
       launch_decode_tma<64, 64, 4>(p, a, stream);
   } else if (a.head_dim == 128) {

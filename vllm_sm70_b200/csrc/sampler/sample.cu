@@ -96,15 +96,30 @@ __global__ void gumbel_argmax_kernel(const T* __restrict__ logits, int V, int ld
   const uint64_t seed = (uint64_t)seeds[row];
   if (row_offsets) offset += (uint64_t)row_offsets[row];
   VI best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float v = to_f(x[i]);
+  auto visit = [&](float v, int i) {
     if (t > 0.f && v == v) {
       const float u = rand_u01(seed, 0, offset, (uint32_t)(i + id_offset));
       v = v / t - __logf(-__logf(u));
     }
     const VI c{v, i};
     if (better(c, best)) best = c;
+  };
+  // 16-byte vector loads when the row allows them (the row is read once, so
+  // the load width sets the rate).
+  constexpr int E = 16 / sizeof(T);
+  int done = 0;
+  if (ld % E == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0) {
+    const int nv = V / E;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (int j = threadIdx.x; j < nv; j += blockDim.x) {
+      const uint4 raw = __ldg(xv + j);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int k = 0; k < E; ++k) visit(to_f(e[k]), j * E + k);
+    }
+    done = nv * E;
   }
+  for (int i = done + threadIdx.x; i < V; i += blockDim.x) visit(to_f(x[i]), i);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     VI other{__shfl_xor_sync(0xffffffff, best.v, o), __shfl_xor_sync(0xffffffff, best.i, o)};

@@ -127,13 +127,15 @@ def bench_gemm(M, N, K, cfg=-1, splits=0, iters=20, flush=False, cublas=True, ep
     return res
 
 
-def bench_decode_attn(batch=256, ctx=1152, hq=32, hkv=8, d=128, bs=16, splits=1, iters=20):
+def bench_decode_attn(batch=256, ctx=1152, hq=32, hkv=8, d=128, bs=16, splits=1, iters=20,
+                      seq_blocks=False):
     from ..ops import attention as A
 
     nb = batch * math.ceil(ctx / bs)
     kc = torch.randn(nb, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
     vc = torch.randn_like(kc)
-    bt = torch.randperm(nb, device="cuda", dtype=torch.int32).view(batch, -1)
+    bt = (torch.arange(nb, device="cuda", dtype=torch.int32) if seq_blocks
+          else torch.randperm(nb, device="cuda", dtype=torch.int32)).view(batch, -1)
     sl = torch.full((batch,), ctx, device="cuda", dtype=torch.int32)
     cu = torch.arange(batch + 1, device="cuda", dtype=torch.int32)
     q = torch.randn(batch, hq, d, device="cuda", dtype=torch.bfloat16)
@@ -147,7 +149,8 @@ def bench_decode_attn(batch=256, ctx=1152, hq=32, hkv=8, d=128, bs=16, splits=1,
     byts = batch * ctx * hkv * d * 2 * 2
     pk = peaks()
     return {"kernel": "paged_attention_decode", "batch": batch, "ctx": ctx, "hq": hq, "hkv": hkv,
-            "d": d, "block": bs, "splits": splits, "ms": round(ms, 5),
+            "d": d, "block": bs, "splits": splits, "blocks": "sequential" if seq_blocks else "random",
+            "ms": round(ms, 5),
             "gbs": round(byts / ms / 1e6, 1), "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3),
             "peaks": pk["src"]}
 
@@ -191,6 +194,8 @@ def main(argv=None):
     ap.add_argument("--epi", type=int, default=0, help="gemm: 1 = fused SiLU*up epilogue")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays")
     ap.add_argument("--block", type=int, default=16, help="attention: KV-cache block size")
+    ap.add_argument("--seq-blocks", action="store_true",
+                    help="decode-attn: sequential block table (default: random permutation)")
     args = ap.parse_args(argv)
     global GRAPH
     GRAPH = args.graph
@@ -219,7 +224,8 @@ def main(argv=None):
                     "ms": round(ms, 5), "tflops": round(2.0 * args.M * args.N * args.K / ms / 1e9, 1)})
     elif args.case == "decode-attn":
         out.append(bench_decode_attn(args.batch, args.ctx, bs=args.block,
-                                     splits=max(1, args.splits), iters=args.iters))
+                                     splits=max(1, args.splits), iters=args.iters,
+                                     seq_blocks=args.seq_blocks))
     elif args.case == "prefill-attn":
         out.append(bench_prefill_attn(args.seqs, args.len, bs=args.block, iters=args.iters))
     else:
