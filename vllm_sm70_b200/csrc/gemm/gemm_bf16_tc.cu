@@ -258,82 +258,96 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      long issued = 0;
+    // A bulk-tensor instruction costs its warp a few hundred ns, so the L2
+    // warm-up and the initial pipeline fill go out lane-parallel (one k-block
+    // per lane); the steady-state loop issues from lane 0.
+    auto load_stage = [&](const UnitCoord& uc, int kb, int stage) {
+      uint8_t* spp = smem + stage * S::kStageBytes;
+      if constexpr (kQuant) {
+        // Activations (Q side, bf16) + the raw weight tile; the P operand is
+        // written by the dequant warps.
+        mbar_arrive_expect_tx(&full_bar[stage], S::kQBytes + S::kRawBytes);
+        tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, uc.q_row);
+        tma_load_2d(spp + S::kPBytes + S::kQBytes, &tmap_p, &full_bar[stage],
+                    kb * raw_row_bytes(WF), uc.p_row);
+      } else {
+        // Operand tiles go in pbox- / qbox-row TMA boxes (8-row multiples
+        // keep the 1024-byte swizzle atoms aligned).
+        if constexpr (PAIR) {
+          // Both CTAs' halves complete on the leader's barrier, which
+          // expects the bytes of the whole pair.
+          if (leader)
+            mbar_arrive_expect_tx(&full_bar[stage],
+                                  (uint32_t)(2 * (BM * BK * 2 + S::kQBytes)));
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0u);
+          for (int r = 0; r < BM; r += pbox)
+            tma_load_2d_pair(spp + r * (BK * 2), &tmap_p, fb, kb * BK,
+                             uc.p_row + (int)prank * BM + r);
+          for (int r = 0; r < QR; r += qbox)
+            tma_load_2d_pair(spp + S::kPBytes + r * (BK * 2), &tmap_q, fb, kb * BK,
+                             uc.q_row + (int)prank * QR + r);
+        } else {
+          mbar_arrive_expect_tx(&full_bar[stage],
+                                (uint32_t)(MH * p_rows_tile * BK * 2 + S::kQBytes));
+#pragma unroll
+          for (int h = 0; h < MH; ++h)
+            for (int r = 0; r < p_rows_tile; r += pbox)
+              tma_load_2d(spp + h * S::kHalfBytes + r * (BK * 2), &tmap_p, &full_bar[stage],
+                          kb * BK, uc.p_row + h * BM + r);
+          for (int r = 0; r < BN; r += qbox)
+            tma_load_2d(spp + S::kPBytes + r * (BK * 2), &tmap_q, &full_bar[stage], kb * BK,
+                        uc.q_row + r);
+        }
+      }
+    };
+    int pre = 0;  // k-blocks of the first unit issued lane-parallel
+    if (unit0 < num_units) {
+      const int t = unit0 / splits, sp = unit0 - t * splits;
+      const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
+      const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+      const int nk = kb1 - kb0;
+      const int rot = kb_rotation(t, nk, num_m);
       if (!early_wait) {
         // Before waiting for the previous kernel: pull the weight tiles of
         // this CTA's first 2 x STAGES k-blocks into L2.
-        if (unit0 < num_units) {
-          const int t = unit0 / splits, sp = unit0 - t * splits;
-          const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
-          const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
-          const int nk = kb1 - kb0;
-          const int rot = kb_rotation(t, nk, num_m);
-          const int npf = min(nk, 2 * STAGES);
-          for (int it = 0; it < npf; ++it) {
-            const int kb = kb0 + (it + rot) % nk;
-            if constexpr (SWAP) {
-              for (int r = 0; r < p_rows_tile; r += pbox)
-                tma_prefetch_l2_2d(&tmap_p, kb * BK, uc.p_row + r);
-            } else {
-              for (int r = 0; r < QR; r += qbox)
-                tma_prefetch_l2_2d(&tmap_q, kb * BK, uc.q_row + (int)prank * QR + r);
-            }
+        const int npf = min(nk, 2 * STAGES);
+        for (int it = lane; it < npf; it += 32) {
+          const int kb = kb0 + (it + rot) % nk;
+          if constexpr (SWAP) {
+            for (int r = 0; r < p_rows_tile; r += pbox)
+              tma_prefetch_l2_2d(&tmap_p, kb * BK, uc.p_row + r);
+          } else {
+            for (int r = 0; r < QR; r += qbox)
+              tma_prefetch_l2_2d(&tmap_q, kb * BK, uc.q_row + (int)prank * QR + r);
           }
         }
         pdl_wait();
       }
+      if constexpr (!kQuant) {
+        pre = max(0, min(nk, STAGES));
+        if (lane < pre) load_stage(uc, kb0 + (lane + rot) % nk, lane);
+        if (lane == 0 && pre > 0) B200_TL(2);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      int stage = pre % STAGES;
+      uint32_t phase = pre == STAGES ? 1u : 0u;
+      long issued = pre;
+      bool first = true;
       for (int u = unit0; u < num_units && !*abort_flag; u += ustride) {
         const int t = u / splits, sp = u - t * splits;
         const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int nk = kb1 - kb0;
         const int rot = kb_rotation(t, nk, num_m);
-        for (int it = 0; it < nk; ++it) {
+        for (int it = first ? pre : 0; it < nk; ++it) {
           const int kb = kb0 + (it + rot) % nk;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err)) {
             *abort_flag = 1;
             break;
           }
-          uint8_t* spp = smem + stage * S::kStageBytes;
-          if constexpr (kQuant) {
-            // Activations (Q side, bf16) + the raw weight tile; the P operand is
-            // written by the dequant warps.
-            mbar_arrive_expect_tx(&full_bar[stage], S::kQBytes + S::kRawBytes);
-            tma_load_2d(spp + S::kPBytes, &tmap_q, &full_bar[stage], kb * BK, uc.q_row);
-            tma_load_2d(spp + S::kPBytes + S::kQBytes, &tmap_p, &full_bar[stage],
-                        kb * raw_row_bytes(WF), uc.p_row);
-          } else {
-            // Operand tiles go in pbox- / qbox-row TMA boxes (8-row multiples
-            // keep the 1024-byte swizzle atoms aligned).
-            if constexpr (PAIR) {
-              // Both CTAs' halves complete on the leader's barrier, which
-              // expects the bytes of the whole pair.
-              if (leader)
-                mbar_arrive_expect_tx(&full_bar[stage],
-                                      (uint32_t)(2 * (BM * BK * 2 + S::kQBytes)));
-              const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0u);
-              for (int r = 0; r < BM; r += pbox)
-                tma_load_2d_pair(spp + r * (BK * 2), &tmap_p, fb, kb * BK,
-                                 uc.p_row + (int)prank * BM + r);
-              for (int r = 0; r < QR; r += qbox)
-                tma_load_2d_pair(spp + S::kPBytes + r * (BK * 2), &tmap_q, fb, kb * BK,
-                                 uc.q_row + (int)prank * QR + r);
-            } else {
-              mbar_arrive_expect_tx(&full_bar[stage],
-                                    (uint32_t)(MH * p_rows_tile * BK * 2 + S::kQBytes));
-#pragma unroll
-              for (int h = 0; h < MH; ++h)
-                for (int r = 0; r < p_rows_tile; r += pbox)
-                  tma_load_2d(spp + h * S::kHalfBytes + r * (BK * 2), &tmap_p, &full_bar[stage],
-                              kb * BK, uc.p_row + h * BM + r);
-              for (int r = 0; r < BN; r += qbox)
-                tma_load_2d(spp + S::kPBytes + r * (BK * 2), &tmap_q, &full_bar[stage], kb * BK,
-                            uc.q_row + r);
-            }
-          }
+          load_stage(uc, kb, stage);
           if (issued == 0) B200_TL(2);
           ++issued;
           if (++stage == STAGES) {
@@ -341,8 +355,9 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             phase ^= 1u;
           }
         }
+        first = false;
       }
-      // Drain: wait for the copies this thread issued into each slot (bounded).
+      // Drain: wait for the copies this warp issued into each slot (bounded).
       // A pair's second CTA counts its copies on the leader's barriers; its
       // operands are consumed (and so landed) before the leader's final
       // commit, which this CTA waits for before tearing down.

@@ -84,6 +84,9 @@ def _time(fn, iters: int, flush_buf: torch.Tensor) -> float:
     ts = []
     for _ in range(iters):
         flush_buf.sum()  # read-based L2 eviction (no dirty lines left behind)
+        # Keep the GPU busy while the host enqueues the timed launch, so host
+        # launch overhead never shows up as device time.
+        torch.cuda._sleep(100_000)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()

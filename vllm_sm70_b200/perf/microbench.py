@@ -76,6 +76,7 @@ def time_fn(fn, iters: int = 20, warmup: int = 3, flush: bool = False) -> float:
     tot = 0.0
     for _ in range(iters):
         flush_l2()
+        torch.cuda._sleep(100_000)  # GPU busy while the host enqueues the timed launch
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         fn()
