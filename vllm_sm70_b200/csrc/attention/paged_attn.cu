@@ -537,7 +537,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
   constexpr int kTile = KT * D * 2;
   constexpr int kStage = 2 * kTile;
   static_assert(KW % 16 == 0, "keys per warp must be a multiple of 16");
-  static_assert(STAGES * kStage >= (NW * 16 * D + NW * 32) * 4, "merge buffer must fit the ring");
+  constexpr int DS = D + 8;  // merge row stride (floats): 8 rows of a warp hit distinct banks
+  static_assert(STAGES * kStage >= (NW * 16 * DS + NW * 32) * 4, "merge buffer must fit the ring");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* ring = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -779,8 +780,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
   }
   // Warp-order merge through the (now idle) ring; consumer warps only.
   named_barrier_sync(1, NW * 32);
-  float* sO = reinterpret_cast<float*>(ring);  // [NW][16][D]
-  float* sM = sO + NW * 16 * D;                 // [NW][16]
+  float* sO = reinterpret_cast<float*>(ring);  // [NW][16][DS]
+  float* sM = sO + NW * 16 * DS;                // [NW][16]
   float* sL = sM + NW * 16;                     // [NW][16]
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -788,7 +789,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) {
       const int d = i * 8 + t4 * 2;
-      *reinterpret_cast<float2*>(&sO[(warp * 16 + r) * D + d]) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
+      *reinterpret_cast<float2*>(&sO[(warp * 16 + r) * DS + d]) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
     }
     if (t4 == 0) {
       sM[warp * 16 + r] = m_run[h];
@@ -809,7 +810,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
       const float mw = sM[w * 16 + r];
       const float sc = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
       L += sL[w * 16 + r] * sc;
-      acc += sO[(w * 16 + r) * D + d] * sc;
+      acc += sO[(w * 16 + r) * DS + d] * sc;
     }
     const int tok = gr / G;
     const int head = kvh * G + gr % G;

@@ -14,3 +14,6 @@ def register() -> None:
     from . import hooks
 
     hooks.install()
+    # The <think> / <tool_call> reasoning parser registers itself on import
+    # ("glm47_b200").
+    from . import reasoning  # noqa: F401
