@@ -37,8 +37,8 @@ __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
   for (int k = 0; k < 4; ++k) {
     const float g0 = __uint_as_float(gw[k] << 16), g1 = __uint_as_float(gw[k] & 0xffff0000u);
     const float u0 = __uint_as_float(uw[k] << 16), u1 = __uint_as_float(uw[k] & 0xffff0000u);
-    const float o0 = g0 / (1.f + __expf(-g0)) * u0;
-    const float o1 = g1 / (1.f + __expf(-g1)) * u1;
+    const float o0 = __fdividef(g0, 1.f + __expf(-g0)) * u0;
+    const float o1 = __fdividef(g1, 1.f + __expf(-g1)) * u1;
     __nv_bfloat162 h = __floats2bfloat162_rn(o0, o1);
     ow[k] = *reinterpret_cast<uint32_t*>(&h);
   }

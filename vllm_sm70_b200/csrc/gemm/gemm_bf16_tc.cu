@@ -638,8 +638,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 #pragma unroll
               for (int c = 0; c < 16; ++c) {
                 const float g0 = g[2 * c], g1 = g[2 * c + 1];
-                const float o0 = g0 / (1.0f + __expf(-g0)) * uu[2 * c];
-                const float o1 = g1 / (1.0f + __expf(-g1)) * uu[2 * c + 1];
+                const float o0 = __fdividef(g0, 1.0f + __expf(-g0)) * uu[2 * c];
+                const float o1 = __fdividef(g1, 1.0f + __expf(-g1)) * uu[2 * c + 1];
                 packed[c] = pack_bf16x2(o0, o1);
               }
               __nv_bfloat16* dst = C + (size_t)i * ldc + j0;
@@ -779,8 +779,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           const int j = out_j0 + (o4 / 16) * 64 + (o4 % 16) * 4;
           if ((MH == 2 || r < p_rows_tile) && i < p_rows && j < out_cols) {
             uint2 pk;
-            pk.x = pack_bf16x2(g.x / (1.0f + __expf(-g.x)) * uu.x, g.y / (1.0f + __expf(-g.y)) * uu.y);
-            pk.y = pack_bf16x2(g.z / (1.0f + __expf(-g.z)) * uu.z, g.w / (1.0f + __expf(-g.w)) * uu.w);
+            pk.x = pack_bf16x2(__fdividef(g.x, 1.0f + __expf(-g.x)) * uu.x,
+                               __fdividef(g.y, 1.0f + __expf(-g.y)) * uu.y);
+            pk.y = pack_bf16x2(__fdividef(g.z, 1.0f + __expf(-g.z)) * uu.z,
+                               __fdividef(g.w, 1.0f + __expf(-g.w)) * uu.w);
             *reinterpret_cast<uint2*>(C + (size_t)i * ldc + j) = pk;
           }
         }
