@@ -115,7 +115,8 @@ class LLM:
 
             # decode batch sizes plus the full prefill chunk
             tune_ms = sorted(set(self.runner.capture_sizes) | {self.max_num_batched_tokens})
-            warmup.engine_warmup(self.model, ps, tune_ms, gemm_lut_path)
+            warmup.engine_warmup(self.model, ps, tune_ms, gemm_lut_path,
+                                 lm_ms=list(self.runner.capture_sizes))
         if self.spec_k == 0:
             self.runner.capture()
         self.last_stats: GenerateStats | None = None

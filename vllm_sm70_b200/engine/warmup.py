@@ -231,8 +231,11 @@ def agree(plans: list | None, ps) -> list:
     return box[0]
 
 
-def model_gemm_shapes(model, Ms: list[int]) -> list[tuple[int, int, int, int]]:
-    """(M, N, K, epi) of every distinct GEMM the model runs at each M."""
+def model_gemm_shapes(model, Ms: list[int],
+                      lm_ms: list[int] | None = None) -> list[tuple[int, int, int, int]]:
+    """(M, N, K, epi) of every distinct GEMM the model runs at each M; the LM
+    head only at ``lm_ms`` (it sees one sampled row per sequence, so the
+    prefill chunk size never reaches it). ``lm_ms`` None: every M."""
     shapes = []
     seen = set()
     for L in model.layers:
@@ -248,15 +251,18 @@ def model_gemm_shapes(model, Ms: list[int]) -> list[tuple[int, int, int, int]]:
                 continue
             seen.add(nk)
     lm = getattr(model, "lm_head", None)
-    if lm is not None:
-        seen.add((lm.shape[0], lm.shape[1], EPI_NONE))
+    lm_nk = (lm.shape[0], lm.shape[1], EPI_NONE) if lm is not None else None
+    lm_set = set(Ms if lm_ms is None else lm_ms)
     for M in Ms:
         for (N, K, epi) in sorted(seen):
             shapes.append((M, N, K, epi))
+        if lm_nk is not None and lm_nk not in seen and M in lm_set:
+            shapes.append((M,) + lm_nk)
     return shapes
 
 
-def engine_warmup(model, ps, Ms: list[int], lut_path: str | None = None) -> None:
+def engine_warmup(model, ps, Ms: list[int], lut_path: str | None = None,
+                  lm_ms: list[int] | None = None) -> None:
     """Tune (or import) the plans for the decode batch sizes before capture."""
     if not envs.get("VLLM_B200_WARMUP"):
         return
@@ -268,7 +274,7 @@ def engine_warmup(model, ps, Ms: list[int], lut_path: str | None = None) -> None
     plans = None
     if ps is None or ps.rank == 0:
         try:
-            plans = tune_shapes(model_gemm_shapes(model, Ms))
+            plans = tune_shapes(model_gemm_shapes(model, Ms, lm_ms))
         except Exception as e:  # noqa: BLE001 - shared with the other ranks by agree()
             logger.error("GEMM tuning failed: %s", e)
             plans = None
