@@ -133,3 +133,113 @@ def test_fused_ar_rmsnorm_peer_timeout(b200_ops):
     if world < 2:
         pytest.skip("needs 2+ GPUs")
     _mp.run(_timeout_body, 2, timeout=300)
+
+
+def _fused_gemm_body(rank, world):
+    """Row-parallel GEMM + all-reduce + residual + RMSNorm in ONE kernel must
+    equal, bit for bit, the same tcgen05 GEMM into the stage followed by the
+    collective kernel -- for several tiles / splits, repeated calls and
+    CUDA-graph replays."""
+    import torch.distributed as dist
+
+    from vllm_sm70_b200.parallel import symm, state
+
+    ps = _setup(rank, world)
+    from vllm_sm70_b200.ops import linear
+
+    linear.configure_workspace(ps.device.index)
+    H, K = 4096, 1536
+    f = symm.FusedArRmsNorm(ps, 512, H)
+    dev = ps.device
+    w = (torch.randn(H, device=dev) * 0.5 + 1).to(torch.bfloat16)
+    dist.broadcast(w, 0)
+    ops = torch.ops._b200_C
+    # (T, cfg, splits): cfgs that the fused launcher keeps as they are
+    cases = [(256, 1, 1), (256, 0, 2), (7, 7, 1), (512, 9, 1), (128, 11, 3), (256, 1, 4)]
+    for it, (T, cfg, sp) in enumerate(cases):
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + it)
+        x = (torch.randn(T, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        lw = (torch.randn(H, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        gs = torch.Generator(device=dev).manual_seed(77 + it)  # shared residual
+        res = torch.randn(T, H, device=dev, generator=gs).to(torch.bfloat16)
+        st = f.stage_view(T)
+        ops.gemm_bf16_out(st, x, lw, cfg, sp)
+        xr, rr = f(st, res.clone(), w, 1e-5)
+        x_ref, r_ref = xr.clone(), rr.clone()
+        got = f.gemm(x, lw, res.clone(), w, 1e-5, cfg, sp)
+        assert got is not None, f"fused path refused T={T} cfg={cfg}"
+        xf, rf = got
+        torch.cuda.synchronize()
+        assert torch.equal(rf, r_ref), f"residual mismatch T={T} cfg={cfg} splits={sp}"
+        assert torch.equal(xf, x_ref), (
+            f"output mismatch T={T} cfg={cfg} splits={sp}: {(xf.float() - x_ref.float()).abs().max()}")
+        assert int(ops.read_status(dev.index, True)) == 0
+    # auto plan, against an fp32 reference of the whole chain
+    T = 96
+    g = torch.Generator(device=dev).manual_seed(4242 + rank)
+    x = (torch.randn(T, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    lw = (torch.randn(H, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    res = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
+        torch.bfloat16)
+    part = (x.float() @ lw.float().t())
+    allp = [torch.empty_like(part) for _ in range(world)]
+    dist.all_gather(allp, part)
+    tot = sum(allp).to(torch.bfloat16).float() + res.float()
+    r_exp = tot.to(torch.bfloat16).float()
+    x_exp = r_exp * torch.rsqrt(r_exp.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    xf, rf = f.gemm(x, lw, res.clone(), w, 1e-5)
+    torch.cuda.synchronize()
+    assert (rf.float() - r_exp).abs().max() < 0.05 * r_exp.abs().max()
+    assert (xf.float() - x_exp).abs().max() < 0.05 * x_exp.abs().max()
+    # CUDA-graph capture + replays (arrival counter and epoch flags survive replays)
+    T, cfg, sp = 256, 1, 2
+    xs = torch.empty(T, K, device=dev, dtype=torch.bfloat16)
+    lw = (torch.randn(H, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    resv = f.res_view(T)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        f.gemm(xs.normal_(), lw, resv, w, 1e-5, cfg, sp)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        outg, _ = f.gemm(xs, lw, resv, w, 1e-5, cfg, sp)
+    for it in range(8):
+        gi = torch.Generator(device=dev).manual_seed(900 + 10 * it + rank)
+        xs.copy_((torch.randn(T, K, device=dev, generator=gi) * 0.5).to(torch.bfloat16))
+        res = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(
+            300 + it)).to(torch.bfloat16)
+        st = f.stage_view(T)
+        ops.gemm_bf16_out(st, xs, lw, cfg, sp)
+        xr, rr = f(st, res.clone(), w, 1e-5)
+        x_ref, r_ref = xr.clone(), rr.clone()
+        resv.copy_(res)
+        graph.replay()
+        torch.cuda.synchronize()
+        stat = int(ops.read_status(dev.index, True))
+        if not torch.equal(outg, x_ref):
+            bad = (outg != x_ref).any(-1).nonzero().flatten()[:4].tolist()
+            for r in bad:
+                v = resv[r].float()
+                inv = torch.rsqrt(v.pow(2).sum() / H + 1e-5)
+                o = (v * inv).to(torch.bfloat16).float() * w.float()
+                print(f"rank {rank} replay {it} row {r}: |fused-py| "
+                      f"{(outg[r].float() - o).abs().max().item():.3e} |ref-py| "
+                      f"{(x_ref[r].float() - o).abs().max().item():.3e}", flush=True)
+        assert torch.equal(outg, x_ref) and torch.equal(resv, r_ref), (
+            f"graph replay {it}: status {stat}, out diff rows "
+            f"{(outg != x_ref).any(-1).nonzero().flatten()[:8].tolist()}, res diff rows "
+            f"{(resv != r_ref).any(-1).nonzero().flatten()[:8].tolist()}")
+    del graph
+    assert int(ops.read_status(dev.index, True)) == 0
+    torch.cuda.synchronize()
+    dist.barrier()
+    state.shutdown()
+
+
+def test_fused_gemm_ar_rmsnorm_bitwise(b200_ops):
+    world = _world()
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    _mp.run(_fused_gemm_body, world, timeout=600)

@@ -544,6 +544,49 @@ void ar_rmsnorm(const std::vector<int64_t>& stage_ptrs, const std::vector<int64_
   ar_rmsnorm_launch(p, (int)grid, cur_stream());
 }
 
+// Row-parallel GEMM x @ lin_w^T into this rank's stage, fused in one kernel
+// with the all-reduce + residual add + RMSNorm. Returns false when the
+// shape / tile is not taken (nothing launched; the caller runs the unfused pair).
+bool gemm_ar_rmsnorm(const at::Tensor& x, const at::Tensor& lin_w,
+                     const std::vector<int64_t>& stage_ptrs, const std::vector<int64_t>& res_ptrs,
+                     const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& flag_ptrs,
+                     int64_t rank, const at::Tensor& w, double eps, int64_t timeout_ms,
+                     int64_t cfg, int64_t splits) {
+  const int W = (int)stage_ptrs.size();
+  TORCH_CHECK(W == 2 || W == 4 || W == 8, "gemm_ar_rmsnorm: world size must be 2, 4 or 8");
+  TORCH_CHECK((int)res_ptrs.size() == W && (int)out_ptrs.size() == W && (int)flag_ptrs.size() == W,
+              "gemm_ar_rmsnorm: pointer lists must have one entry per rank");
+  TORCH_CHECK(rank >= 0 && rank < W, "gemm_ar_rmsnorm: bad rank");
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(lin_w); CHECK_BF16(w);
+  TORCH_CHECK(x.dim() == 2 && lin_w.dim() == 2 && x.stride(1) == 1 && lin_w.stride(1) == 1 &&
+              x.size(1) == lin_w.size(1), "gemm_ar_rmsnorm: x [T, K], lin_w [H, K]");
+  const int64_t T = x.size(0), H = lin_w.size(0), K = x.size(1);
+  TORCH_CHECK(w.numel() == H && H % 8 == 0, "gemm_ar_rmsnorm: norm weight size / H % 8");
+  ArRmsNormParams p{};
+  for (int q = 0; q < W; ++q) {
+    p.stage_peer[q] = reinterpret_cast<const __nv_bfloat16*>(stage_ptrs[q]);
+    p.res_peer[q] = reinterpret_cast<__nv_bfloat16*>(res_ptrs[q]);
+    p.out_peer[q] = reinterpret_cast<__nv_bfloat16*>(out_ptrs[q]);
+    p.flags_peer[q] = reinterpret_cast<uint32_t*>(flag_ptrs[q]);
+    TORCH_CHECK((stage_ptrs[q] | res_ptrs[q] | out_ptrs[q]) % 16 == 0,
+                "gemm_ar_rmsnorm: 16B alignment");
+  }
+  p.flags_local = p.flags_peer[rank];
+  p.res_local = p.res_peer[rank];
+  p.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  p.rank = (int)rank;
+  p.world = W;
+  p.T = (int)T;
+  p.H = (int)H;
+  p.eps = (float)eps;
+  p.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  p.err = device_status_ptr(x.get_device());
+  c10::cuda::CUDAGuard g(x.device());
+  return gemm_ar_rmsnorm_launch(x.data_ptr(), lin_w.data_ptr(), (int)T, (int)H, (int)K,
+                                (int)x.stride(0), (int)lin_w.stride(0), (int)cfg, (int)splits, p,
+                                p.err, cur_stream());
+}
+
 void argmax(at::Tensor& ids, const c10::optional<at::Tensor>& vals, const at::Tensor& logits,
             int64_t id_offset) {
   CHECK_CUDA(logits);
@@ -632,6 +675,9 @@ TORCH_LIBRARY(_b200_C, m) {
       "Tensor? sinks, bool decode, int num_splits, Tensor? part_o, Tensor? part_ml) -> ()");
   m.def("ar_rmsnorm(int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, int[] flag_ptrs, int rank, "
         "int T, int H, Tensor w, float eps, int timeout_ms, int grid) -> ()");
+  m.def("gemm_ar_rmsnorm(Tensor x, Tensor lin_w, int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, "
+        "int[] flag_ptrs, int rank, Tensor w, float eps, int timeout_ms, int cfg, int splits) "
+        "-> bool");
   m.def("kv_cache_write(Tensor k, Tensor v, Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor slots) -> ()");
   m.def("argmax(Tensor(a!) ids, Tensor(b!)? vals, Tensor logits, int id_offset) -> ()");
   m.def("silu_mul(Tensor(a!) out, Tensor x, int block=0) -> ()");
@@ -662,6 +708,7 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("argmax", &b200::argmax);
   m.impl("kv_cache_write", &b200::kv_cache_write);
   m.impl("ar_rmsnorm", &b200::ar_rmsnorm);
+  m.impl("gemm_ar_rmsnorm", &b200::gemm_ar_rmsnorm);
   m.impl("silu_mul", &b200::silu_mul);
   m.impl("embedding", &b200::embedding);
 }

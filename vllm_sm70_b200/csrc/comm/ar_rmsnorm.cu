@@ -39,185 +39,32 @@
 #include <stdexcept>
 #include <string>
 
-#include "common/ptx.cuh"
+#include "comm/ar_rmsnorm_dev.cuh"
 #include "comm/comm_api.h"
 #include "common/launch.h"
 
 namespace b200 {
 namespace {
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded acquire-spin until *p >= target (wrap-safe compare).
-__device__ __forceinline__ bool wait_geq(const uint32_t* p, uint32_t target, unsigned int* err,
-                                         unsigned long long timeout_ns) {
-  const unsigned long long t0 = globaltimer();
-  uint32_t n = 0;
-  while ((int32_t)(ld_acquire_sys(p) - target) < 0) {
-    if ((++n & 255u) == 0) {
-      if (globaltimer() - t0 > timeout_ns) {
-        atomicCAS(err, kErrNone, kErrPeerTimeout);
-        return false;
-      }
-      if (*(volatile unsigned int*)err != kErrNone) return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(f[2 * i], f[2 * i + 1]);
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-constexpr int kMaxVec = 4;  // 16-byte vectors per thread kept in registers (H <= 8*4*threads)
-
-template <int W>
 __global__ void __launch_bounds__(512) ar_rmsnorm_kernel(ArRmsNormParams p) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[32];
+  __shared__ float part[ardev::kMaxVec * 512];
+  __shared__ float bcast;
   __shared__ int s_ok;
-  const int tid = threadIdx.x;
-  uint32_t* ready = p.flags_local;          // [W]
-  uint32_t* done = p.flags_local + W;       // [W]
-  uint32_t* epoch_p = p.flags_local + 2 * W;
-  uint32_t* target_p = p.flags_local + 2 * W + 1;  // cumulative CTAs per peer
-  const uint32_t epoch = *(volatile uint32_t*)epoch_p + 1;
-
-  // ---- start barrier: every peer's stage is complete
-  if (tid == 0) {
-    if (blockIdx.x == 0) {
-      __threadfence_system();
-#pragma unroll
-      for (int q = 0; q < W; ++q) st_release_sys(p.flags_peer[q] + p.rank, epoch);
-    }
-    int ok = 1;
-#pragma unroll
-    for (int q = 0; q < W; ++q) ok &= wait_geq(ready + q, epoch, p.err, p.timeout_ns);
-    s_ok = ok;
-  }
-  __syncthreads();
-  if (!s_ok) return;
-
-  const int H = p.H;
-  const int nvec = H / 8;
-  const int rows_per_rank = (p.T + W - 1) / W;
-  const int r0 = p.rank * rows_per_rank;
-  const int r1 = min(p.T, r0 + rows_per_rank);
-  for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
-    float v[kMaxVec][8];
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < kMaxVec; ++k) {
-      const int i = tid + k * blockDim.x;
-      if (i < nvec) {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        uint4 parts[W];
-#pragma unroll
-        for (int q = 0; q < W; ++q)
-          parts[q] = __ldcv(reinterpret_cast<const uint4*>(p.stage_peer[q] + (size_t)row * H) + i);
-#pragma unroll
-        for (int q = 0; q < W; ++q) {  // rank order
-          float f[8];
-          unpack8(parts[q], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += f[e];
-        }
-        float res[8];
-        unpack8(*(reinterpret_cast<const uint4*>(p.res_local + (size_t)row * H) + i), res);
-        // bf16(allreduce) + residual, rounded: matches fused_add_rms_norm(x, res).
-        const uint4 xs = pack8(acc);
-        unpack8(xs, acc);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += res[e];
-        const uint4 rs = pack8(acc);
-        unpack8(rs, v[k]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
-#pragma unroll
-        for (int q = 0; q < W; ++q)
-          *(reinterpret_cast<uint4*>(p.res_peer[q] + (size_t)row * H) + i) = rs;
-      }
-    }
-    // block reduction (fixed order)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
-    __syncthreads();
-    const float inv = rsqrtf(tot / (float)H + p.eps);
-#pragma unroll
-    for (int k = 0; k < kMaxVec; ++k) {
-      const int i = tid + k * blockDim.x;
-      if (i < nvec) {
-        float wf[8], o[8];
-        unpack8(*(reinterpret_cast<const uint4*>(p.w) + i), wf);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          o[e] = __bfloat162float(__float2bfloat16_rn(v[k][e] * inv)) * wf[e];
-        const uint4 ov = pack8(o);
-#pragma unroll
-        for (int q = 0; q < W; ++q)
-          *(reinterpret_cast<uint4*>(p.out_peer[q] + (size_t)row * H) + i) = ov;
-      }
-    }
-  }
-
-  // ---- end barrier: all peers finished with our stage / wrote our rows
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence_system();
-#pragma unroll
-    for (int q = 0; q < W; ++q) red_release_sys_add(p.flags_peer[q] + W + p.rank, 1u);
-    if (blockIdx.x == 0) {
-      const uint32_t target = *(volatile uint32_t*)target_p + gridDim.x;
-      bool ok = true;
-#pragma unroll
-      for (int q = 0; q < W; ++q) ok &= wait_geq(done + q, target, p.err, p.timeout_ns);
-      (void)ok;
-      *(volatile uint32_t*)target_p = target;
-      *(volatile uint32_t*)epoch_p = epoch;
-      __threadfence();
-    }
-  }
+  ardev::run_any(p, /*gated=*/false, part, &bcast, &s_ok);
 }
 
 }  // namespace
 
 void ar_rmsnorm_launch(const ArRmsNormParams& p, int grid, cudaStream_t stream) {
   if (p.H % 8 != 0) throw std::runtime_error("ar_rmsnorm: H % 8 != 0");
-  int threads = ((p.H / 8 + kMaxVec - 1) / kMaxVec + 31) / 32 * 32;
+  int threads = ((p.H / 8 + ardev::kMaxVec - 1) / ardev::kMaxVec + 31) / 32 * 32;
   if (threads < 64) threads = 64;
   if (threads > 512) throw std::runtime_error("ar_rmsnorm: H too large");
-  switch (p.world) {
-    case 2: launch_pdl(ar_rmsnorm_kernel<2>, dim3(grid), dim3(threads), 0, stream, nullptr, p); break;
-    case 4: launch_pdl(ar_rmsnorm_kernel<4>, dim3(grid), dim3(threads), 0, stream, nullptr, p); break;
-    case 8: launch_pdl(ar_rmsnorm_kernel<8>, dim3(grid), dim3(threads), 0, stream, nullptr, p); break;
-    default: throw std::runtime_error("ar_rmsnorm: world size must be 2, 4 or 8");
-  }
+  if (p.world != 2 && p.world != 4 && p.world != 8)
+    throw std::runtime_error("ar_rmsnorm: world size must be 2, 4 or 8");
+  launch_pdl(ar_rmsnorm_kernel, dim3(grid), dim3(threads), 0, stream, nullptr, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("ar_rmsnorm: ") + cudaGetErrorString(e));
 }

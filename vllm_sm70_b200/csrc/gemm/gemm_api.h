@@ -6,11 +6,15 @@
 
 #include <vector>
 
+#include "comm/comm_api.h"
+
 namespace b200 {
 
 enum GemmEpilogue : int {
   kEpiNone = 0,     // C = A W^T (bf16)
   kEpiSiluMul = 1,  // W rows interleaved in [gate 64 | up 64] blocks; C = silu(g) * u, N/2 cols
+  kEpiArNorm = 2,   // C = this rank's stage of a TP all-reduce; the kernel then runs the fused
+                    // all-reduce + residual add + RMSNorm over NVLink peer memory (WQParams::ar)
 };
 
 enum GemmConfig : int {
@@ -66,6 +70,7 @@ struct WQParams {
   const uint8_t* scales_u8 = nullptr;               // kWNvfp4
   int scale_ld = 0;                                 // elements per scale row
   float out_scale = 1.f;                            // kWNvfp4 global scale
+  ArRmsNormParams ar{};                             // kEpiArNorm: the collective after the GEMM
 };
 
 // Grouped (MoE) GEMM: per-expert tiles read from device arrays.
@@ -148,6 +153,14 @@ bool gemm_cfg_is_swap(int cfg);
 void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,
                             int ldw, int ldc, int epi, int cfg, int splits, float* ws,
                             size_t ws_bytes, int* counters, int n_counters, unsigned int* err,
+                            cudaStream_t stream);
+
+// Row-parallel GEMM fused with the TP all-reduce + residual add + RMSNorm in one
+// kernel: C = A W^T goes into this rank's symmetric stage (ar.stage_peer[rank]),
+// then the same CTAs run the collective over NVLink peer memory. N == ar.H,
+// M == ar.T. Returns false (nothing launched) for shapes it does not take.
+bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, int lda, int ldw,
+                            int cfg, int splits, const ArRmsNormParams& ar, unsigned int* err,
                             cudaStream_t stream);
 
 }  // namespace b200

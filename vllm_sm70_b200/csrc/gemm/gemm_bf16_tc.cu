@@ -54,6 +54,7 @@
 
 #include "common/launch.h"
 #include "common/ptx.cuh"
+#include "comm/ar_rmsnorm_dev.cuh"
 #include "common/tmap.h"
 #include "gemm/gemm_api.h"
 #include "gemm/dequant.cuh"
@@ -825,6 +826,15 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     else tmem_dealloc(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0) B200_TL(7);
+  if constexpr (EPI == kEpiArNorm) {
+    // Fused TP collective: every tile of this rank's stage is stored once all
+    // CTAs have arrived; the same CTAs then all-reduce, add the residual and
+    // RMS-normalise the rows this rank owns (peer loads / stores over NVLink).
+    __shared__ float ar_part[ardev::kMaxVec * kThreads];
+    __shared__ float ar_bcast;
+    __shared__ int ar_ok;
+    if (!*abort_flag) ardev::run_any(wq.ar, /*gated=*/true, ar_part, &ar_bcast, &ar_ok);
+  }
 #undef B200_TL
 }
 
@@ -1350,6 +1360,62 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
 #undef B200_TALL
 #undef B200_NORMAL
 #undef B200_SWAP
+}
+
+bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, int lda, int ldw,
+                            int cfg, int splits, const ArRmsNormParams& ar, unsigned int* err,
+                            cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return true;
+  if (M != ar.T || N != ar.H || K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0 || N % 8 != 0)
+    return false;
+  if ((ar.world != 2 && ar.world != 4 && ar.world != 8) ||
+      N / 8 > ardev::kMaxVec * kThreads)
+    return false;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cfg < 0) {
+    GemmPlan pl = gemm_bf16_plan(M, N, K, kEpiNone, num_sms(dev));
+    cfg = pl.cfg;
+    if (splits <= 0) splits = pl.splits;
+  }
+  if (splits <= 0) splits = 1;
+  if (splits > kMaxSplits) splits = kMaxSplits;
+  // Normal (non-swap, single-CTA) tiles only: the collective phase needs the
+  // whole grid resident (grid <= SMs) and the stage in row-major order.
+  switch (cfg) {
+    case kCfgN192: case kCfgN96: case kCfgSwap128: case kCfgP2N128: case kCfgP2N192:
+    case kCfgClN128: cfg = kCfgN128; break;
+    case kCfgSwap16: case kCfgSwap32: case kCfgSwap64: case kCfgP2N64: cfg = kCfgN64; break;
+    case kCfgM2N224: case kCfgM2N112: case kCfgClM2N128: case kCfgClM2N112: cfg = kCfgM2N128;
+      break;
+    case kCfgM2N64: case kCfgClM2N64: cfg = kCfgN64; break;
+    case kCfgP2N256: cfg = kCfgM2N256; break;
+    case kCfgClN256: cfg = kCfgN256; break;
+    default: break;
+  }
+  const int num_kb = (K + 63) / 64;
+  if (splits > num_kb) splits = num_kb;
+  SplitWorkspace& sw = g_split_ws[dev];
+  SplitGeometry geo = gemm_split_geometry(M, N, K, cfg, splits, num_sms(dev));
+  if (splits > 1 && (sw.ws == nullptr || geo.ws_bytes > sw.ws_bytes || geo.counters > sw.n_counters))
+    splits = 1;
+  float* wsp = splits > 1 ? sw.ws : nullptr;
+  int* cnt = splits > 1 ? sw.counters : nullptr;
+  void* C = const_cast<__nv_bfloat16*>(ar.stage_peer[ar.rank]);
+  WQParams wq{};
+  wq.ar = ar;
+#define B200_AR(BN_, ST_, MH_)                                                                \
+  launch_cfg<BN_, ST_, false, kEpiArNorm, kWBf16, MH_>(A, W, C, M, N, K, lda, ldw, N, splits, \
+                                                       wsp, cnt, err, stream, wq);            \
+  return true
+  switch (cfg) {
+    case kCfgN256: B200_AR(256, 4, 1);
+    case kCfgN64: B200_AR(64, 8, 1);
+    case kCfgM2N256: B200_AR(256, 3, 2);
+    case kCfgM2N128: B200_AR(128, 4, 2);
+    default: B200_AR(128, 6, 1);
+  }
+#undef B200_AR
 }
 
 void gemm_wq_launch(const void* A, const void* Wraw, void* C, int M, int N, int K, int lda,

@@ -2,9 +2,10 @@
 //
 // fused_add_rms_norm: s = bf16(x + residual) ; residual <- s ;
 //                     x <- bf16(s * rsqrt(mean(s^2) + eps) * w)
-// The variance is taken from the rounded bf16 sum, so the fused collective
-// variant (comm/ar_rmsnorm.cu) that performs the same rounding matches this
-// kernel bit for bit.
+// The variance is taken from the rounded bf16 sum, reduced in a block-size-
+// independent order (common/rowsum.cuh), so the fused collective variants
+// (comm/ar_rmsnorm.cu, and the GEMM that runs it as its last phase) that
+// perform the same rounding match this kernel bit for bit.
 //
 // Reference parity: upstream vLLM fused_add_rms_norm as pinned by the reference
 // (sm70/vllm_sm70/_cuda_platform.py:276-302) and the TP2 AR+RMSNorm kernel's
@@ -17,23 +18,10 @@
 
 #include "ops_api.h"
 #include "common/launch.h"
+#include "common/rowsum.cuh"
 
 namespace b200 {
 namespace {
-
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  const int nw = blockDim.x / 32;
-  float t = 0.f;
-  // Fixed summation order: every thread adds the warp partials in index order.
-  for (int i = 0; i < nw; ++i) t += red[i];
-  __syncthreads();
-  return t;
-}
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -62,7 +50,8 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, int ld_out,
                                 const __nv_bfloat16* __restrict__ w, int H, float eps) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[32];
+  __shared__ float part[kMaxVec * 1024];  // one partial per 8-element vector
+  __shared__ float bcast;
   const int row = blockIdx.x;
   const int nvec = H / 8;
   uint4* xr = reinterpret_cast<uint4*>(x + (size_t)row * ld_x);
@@ -70,7 +59,6 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, int ld_out,
   uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * ld_out);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   float v[kMaxVec][8];
-  float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
@@ -85,11 +73,13 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, int ld_out,
         rr[i] = s;
         unpack8(s, v[k]);  // continue with the rounded sum
       }
+      float ss = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
+      part[i] = ss;
     }
   }
-  const float tot = block_sum(ss, red);
+  const float tot = canonical_block_sum(part, nvec, &bcast);
   const float inv = rsqrtf(tot / (float)H + eps);
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {

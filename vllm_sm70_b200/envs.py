@@ -87,6 +87,10 @@ _reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tu
 _reg("VLLM_B200_GEMM_LIBRARY", "kill", True, "runtime",
      "Let the warm-up tuner route a plain bf16 GEMM shape to cuBLAS when it measures faster "
      "than every tcgen05 plan (fused / quantised / grouped GEMMs never are).")
+_reg("VLLM_B200_FUSED_GEMM_AR", "optin", False, "comm",
+     "TP > 1: run each row-parallel GEMM (o_proj, down_proj) and the following all-reduce + "
+     "residual + RMSNorm as one kernel (tcgen05 tiles, then the collective over NVLink peer "
+     "memory) instead of a GEMM followed by the collective kernel.")
 _reg("VLLM_B200_PDL", "kill", True, "runtime",
      "Launch the decode-path kernels with programmatic dependent launch (read by the native "
      "library at load).")

@@ -283,9 +283,8 @@ class LlamaModel:
         residual = comm.adopt_residual(self.embed_tokens(ids))
         x = ops.rms_norm(residual, self.layers[0]["in_norm"], eps)
         attn_out = torch.empty(T, self.hq, self.d, device=ids.device, dtype=self.dtype)
+        n_layers = len(self.layers)
         for li, L in enumerate(self.layers):
-            if li > 0:
-                x, residual = comm.all_reduce_add_rms_norm(x, residual, L["in_norm"], eps)
             qkv = L["qkv"].forward(x)
             ops.rope_kv_write(qkv, meta.positions, self.cos_sin, kv.k[li], kv.v[li],
                               meta.slot_mapping, self.hq, self.hkv, L.get("q_norm"),
@@ -294,12 +293,23 @@ class LlamaModel:
             ops.paged_attention(attn_out, q, kv.k[li], kv.v[li], meta.block_table,
                                 meta.seq_lens, meta.cu_q, meta.max_q_len, self.scale, 0, None,
                                 meta.decode, meta.num_splits, meta.part_o, meta.part_ml)
-            o = L["o"].forward(attn_out.view(T, self.hq * self.d),
-                               out=comm.row_parallel_out(T, H))
-            x, residual = comm.all_reduce_add_rms_norm(o, residual, L["post_norm"], eps)
-            x = self.mlp(li, L, x, comm.row_parallel_out(T, H))
-        x, residual = comm.all_reduce_add_rms_norm(x, residual, self.final_norm, eps)
+            x, residual = comm.linear_all_reduce_add_rms_norm(
+                L["o"], attn_out.view(T, self.hq * self.d), residual, L["post_norm"], eps)
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < n_layers else self.final_norm
+            x, residual = self.mlp_ar(li, L, x, residual, nxt, eps)
         return x
+
+    def mlp_ar(self, li: int, L: dict, x: torch.Tensor, residual: torch.Tensor,
+               norm_w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+        """MLP, then the TP all-reduce + residual add + RMSNorm with ``norm_w``
+        (the next layer's input norm, or the final norm). The dense SwiGLU's
+        down projection can run fused with the collective in one kernel."""
+        T, H = x.shape[0], self.cfg.hidden_size
+        if type(self).mlp is LlamaModel.mlp:
+            h = L["gate_up"].forward(x)
+            return comm.linear_all_reduce_add_rms_norm(L["down"], h, residual, norm_w, eps)
+        out = self.mlp(li, L, x, comm.row_parallel_out(T, H))
+        return comm.all_reduce_add_rms_norm(out, residual, norm_w, eps)
 
     def mlp(self, li: int, L: dict, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
         """Dense SwiGLU MLP (row-parallel output, reduced by the caller)."""

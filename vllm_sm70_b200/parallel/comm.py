@@ -75,6 +75,26 @@ def all_reduce_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Te
     return x, residual
 
 
+def linear_all_reduce_add_rms_norm(lin, x: torch.Tensor, residual: torch.Tensor,
+                                   w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Row-parallel linear followed by :func:`all_reduce_add_rms_norm`. With
+    TP > 1, a bf16 dense weight and the fused workspace up, the GEMM and the
+    collective run as ONE kernel (``VLLM_B200_FUSED_GEMM_AR``); otherwise the
+    GEMM writes the stage and the collective follows."""
+    st = pstate.get()
+    T, H = x.shape[0], getattr(lin, "out_features", None)
+    if st.tp_size > 1 and envs.get("VLLM_B200_FUSED_GEMM_AR"):
+        impl = fused_ar_rmsnorm()
+        lw = getattr(lin, "w", None)
+        if (impl is not None and type(lin).__name__ == "DenseLinear" and lw is not None
+                and lw.dtype == torch.bfloat16 and x.is_cuda and x.stride(1) == 1):
+            r = impl.gemm(x, lw, residual, w, eps)
+            if r is not None:
+                return r
+    out = lin.forward(x, out=row_parallel_out(T, H) if H is not None else None)
+    return all_reduce_add_rms_norm(out, residual, w, eps)
+
+
 def greedy_merge(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
     """Gather per-rank (max value, id) pairs and pick the global top-1 in rank
     order with the shared tie rule. Reference parity: F12 greedy

@@ -25,7 +25,7 @@ from ..utils import launch_count
 
 logger = logging.getLogger("vllm.b200.symm")
 
-SIGNAL_WORDS = 64  # uint32 words per rank: ready[W], done[W], epoch, done_target
+SIGNAL_WORDS = 64  # uint32 words per rank: ready[W], done[W], epoch, done_target, arrive
 
 
 class FusedArRmsNorm:
@@ -93,6 +93,27 @@ class FusedArRmsNorm:
         torch.ops._b200_C.ar_rmsnorm(self.stage_ptrs, self.res_ptrs, self.out_ptrs,
                                      self.flag_ptrs, self.ps.tp_rank, T, self.H, w, eps,
                                      self.timeout_ms, self.grid(T))
+        launch_count.add(1)
+        self.calls += 1
+        return self.out_view(T), rv
+
+    def gemm(self, x: torch.Tensor, lin_w: torch.Tensor, residual: torch.Tensor,
+             w: torch.Tensor, eps: float, cfg: int = -1, splits: int = 0):
+        """Row-parallel ``x @ lin_w^T`` fused with the all-reduce + residual
+        add + RMSNorm in ONE kernel (the tcgen05 GEMM writes this rank's stage,
+        then its CTAs run the collective over NVLink). Returns (normalised x,
+        residual) as views of the symmetric buffers, or None when not taken."""
+        T = x.shape[0]
+        if not self.admits(T) or lin_w.shape[0] != self.H:
+            return None
+        rv = self.res_view(T)
+        if residual.data_ptr() != rv.data_ptr():
+            rv.copy_(residual)
+        ok = torch.ops._b200_C.gemm_ar_rmsnorm(x, lin_w, self.stage_ptrs, self.res_ptrs,
+                                               self.out_ptrs, self.flag_ptrs, self.ps.tp_rank,
+                                               w, eps, self.timeout_ms, cfg, splits)
+        if not ok:
+            return None
         launch_count.add(1)
         self.calls += 1
         return self.out_view(T), rv
