@@ -87,10 +87,15 @@ _reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tu
 _reg("VLLM_B200_GEMM_LIBRARY", "kill", True, "runtime",
      "Let the warm-up tuner route a plain bf16 GEMM shape to cuBLAS when it measures faster "
      "than every tcgen05 plan (fused / quantised / grouped GEMMs never are).")
-_reg("VLLM_B200_FUSED_GEMM_AR", "optin", False, "comm",
+_reg("VLLM_B200_FUSED_GEMM_AR", "kill", True, "comm",
      "TP > 1: run each row-parallel GEMM (o_proj, down_proj) and the following all-reduce + "
      "residual + RMSNorm as one kernel (tcgen05 tiles, then the collective over NVLink peer "
-     "memory) instead of a GEMM followed by the collective kernel.")
+     "memory) instead of a GEMM followed by the collective kernel, for token counts of at "
+     "least VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS.")
+_reg("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS", "int", 1024, "comm",
+     "Smallest token count that takes the fused GEMM + all-reduce kernel (measured at TP2 on "
+     "Llama-3.1-8B shapes: faster for 16384-token prefill chunks, slower than the vendor GEMM + "
+     "collective kernel at 256-row decode steps).")
 _reg("VLLM_B200_PDL", "kill", True, "runtime",
      "Launch the decode-path kernels with programmatic dependent launch (read by the native "
      "library at load).")

@@ -79,11 +79,13 @@ def linear_all_reduce_add_rms_norm(lin, x: torch.Tensor, residual: torch.Tensor,
                                    w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
     """Row-parallel linear followed by :func:`all_reduce_add_rms_norm`. With
     TP > 1, a bf16 dense weight and the fused workspace up, the GEMM and the
-    collective run as ONE kernel (``VLLM_B200_FUSED_GEMM_AR``); otherwise the
-    GEMM writes the stage and the collective follows."""
+    collective run as ONE kernel (``VLLM_B200_FUSED_GEMM_AR``, from
+    ``VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS`` tokens up -- a rank-uniform choice);
+    otherwise the GEMM writes the stage and the collective follows."""
     st = pstate.get()
     T, H = x.shape[0], getattr(lin, "out_features", None)
-    if st.tp_size > 1 and envs.get("VLLM_B200_FUSED_GEMM_AR"):
+    if (st.tp_size > 1 and envs.get("VLLM_B200_FUSED_GEMM_AR")
+            and T >= envs.get("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS")):
         impl = fused_ar_rmsnorm()
         lw = getattr(lin, "w", None)
         if (impl is not None and type(lin).__name__ == "DenseLinear" and lw is not None
