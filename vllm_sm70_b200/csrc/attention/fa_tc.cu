@@ -67,6 +67,7 @@ struct FaParams {
   const float* sinks;
   __nv_bfloat16* out;
   int num_seqs, Hq, Hkv, G, block_size, block_shift, max_blocks, window, o_stride_t;
+  int num_blocks;  // cache blocks (debug-build bounds checks)
   float scale_log2;
   unsigned int* err;
   uint32_t v_lbo, v_sbo;  // V (MN-major B operand) descriptor strides, bytes
@@ -197,7 +198,8 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       const int tile = g * per + lane / nb;
       if (tile >= n_tiles) return 0;
       const int b = ((k_lo + tile * FN) >> p.block_shift) + lane % nb;
-      return __ldg(bt + min(b, blk_last));
+      const int id = __ldg(bt + min(b, blk_last));
+      return in_bounds(id >= 0 && id < p.num_blocks, p.err) ? id : 0;
     };
     int ids_cur = load_ids(0), ids_next = load_ids(1), g_cur = 0;
     // K and V stream from separate warps: K_j's slot frees right after S_j,
@@ -558,6 +560,7 @@ void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
   p.block_size = BS;
   p.block_shift = __builtin_ctz(BS);
   p.max_blocks = a.max_blocks;
+  p.num_blocks = a.num_blocks;
   p.window = a.window;
   p.o_stride_t = a.o_stride_t;
   p.scale_log2 = a.scale * 1.4426950408889634f;

@@ -106,6 +106,7 @@ struct Params {
   float scale_log2;            // softmax scale * log2(e)
   int num_splits;              // decode split-KV
   int rows_per_seq_max;        // max over seqs of q_len*G (grid sizing)
+  int num_blocks;              // cache blocks (debug-build bounds checks)
 };
 
 constexpr int kBtCache = 512;  // block ids cached in smem per window
@@ -607,7 +608,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     const int blk_last = k_end > 0 ? (k_end - 1) >> p.block_shift : 0;
     auto blk_of = [&](int t) -> int {
       const int b = ((k_begin + t * KT) >> p.block_shift) + lane % nb;
-      return __ldg(bt + min(b, blk_last));
+      const int id = __ldg(bt + min(b, blk_last));
+      return in_bounds(id >= 0 && id < p.num_blocks, err) ? id : 0;
     };
     int cur = n_tiles > 0 ? blk_of(0) : 0;
     for (int t = 0; t < n_tiles; ++t) {
@@ -919,6 +921,7 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.num_splits = a.decode ? (a.num_splits > 0 ? a.num_splits : 1) : 1;
   p.rows_per_seq_max = a.max_q_len * (a.Hq / a.Hkv);
+  p.num_blocks = a.num_blocks;
   if (p.num_splits > 1 && (a.part_o == nullptr || a.part_ml == nullptr))
     throw std::runtime_error("paged_attention: split-KV needs partial buffers");
   const bool tma_ok = a.num_blocks > 0 && a.block_size >= 8 && a.q_stride_t % 8 == 0 &&

@@ -27,7 +27,22 @@ enum : unsigned int {
   kErrPeerTimeout = 2,
   kErrBadArg = 3,
   kErrOverflow = 4,
+  kErrBounds = 5,  // debug build: a data-dependent index was out of range (access skipped)
 };
+
+// Bounds check of the debug build (build_ext --debug-bounds defines
+// B200_DEBUG_BOUNDS): a failed check records kErrBounds in the status word and
+// returns false so the caller skips the access -- it never traps. Release
+// builds compile the check away (returns true).
+__device__ __forceinline__ bool in_bounds(bool ok, unsigned int* err) {
+#if defined(B200_DEBUG_BOUNDS)
+  if (!ok && err) atomicCAS(err, 0u, 5u);
+  return ok;
+#else
+  (void)err;
+  return true;
+#endif
+}
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;

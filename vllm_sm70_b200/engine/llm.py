@@ -26,9 +26,12 @@ from dataclasses import dataclass, field
 
 import torch
 
+from .. import envs
 from ..models import build_model
 from ..models.config import ModelConfig, resolve
 from ..parallel import state as pstate
+from ..utils import tracing
+from ..utils.watchdog import StreamWatchdog
 from .model_runner import ModelRunner
 from .sampling_params import RequestOutput, SamplingParams
 
@@ -120,6 +123,8 @@ class LLM:
         if self.spec_k == 0:
             self.runner.capture()
         self.last_stats: GenerateStats | None = None
+        wd = int(envs.get("VLLM_B200_WATCHDOG_S"))
+        self.watchdog = (StreamWatchdog(wd) if wd > 0 and self.device.type == "cuda" else None)
 
     def shutdown(self) -> None:
         """Release CUDA graphs (they may hold NCCL work) before the process
@@ -130,6 +135,9 @@ class LLM:
         from ..parallel import comm
 
         comm.set_fused_ar_rmsnorm(None)
+        if getattr(self, "watchdog", None) is not None:
+            self.watchdog.close()
+            self.watchdog = None
 
     def _size_kv(self, max_num_seqs, max_model_len, block_size, util) -> int:
         m = self.model
@@ -217,14 +225,20 @@ class LLM:
                     if last:
                         queue.popleft()
                         finishing.append(r)
+                if self.watchdog is not None:
+                    self.watchdog.check()
                 if cuda:
                     e_pre = ev()
                     e_pre.record()
+                tracing.push("prefill")
                 runner.prefill(pieces)
+                tracing.pop()
                 if cuda:
                     e_post = ev()
                     e_post.record()
                     prefill_spans.append((e_pre, e_post))
+                    if self.watchdog is not None:
+                        self.watchdog.arm(e_post, "prefill chunk")
                 for r in finishing:
                     r.generated = 1
                 if cuda and finishing:
@@ -251,7 +265,11 @@ class LLM:
             elif not finished_now:
                 steps = min(r.params.max_tokens - r.generated for r in live)
                 n_rows = max(r.slot for r in live) + 1
+                if self.watchdog is not None:
+                    self.watchdog.check()
+                tracing.push("decode")
                 runner.decode(n_rows, steps)
+                tracing.pop()
                 stats.decode_steps += steps
                 for r in live:
                     r.generated += steps
@@ -260,6 +278,8 @@ class LLM:
                     e = ev()
                     e.record()
                     decode_events.append((e, finished_now, steps))
+                    if self.watchdog is not None:
+                        self.watchdog.arm(e, f"decode burst of {steps} steps")
             # ---- retire
             if finished_now:
                 slots = [r.slot for r in finished_now]

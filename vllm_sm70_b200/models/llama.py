@@ -24,7 +24,7 @@ import torch
 
 from .. import ops
 from ..parallel import comm, state as pstate
-from ..utils import launch_count
+from ..utils import launch_count, tracing
 from .config import ModelConfig
 from .layers import AttnMeta, DenseLinear, GateUpLinear, KVCache
 
@@ -285,6 +285,7 @@ class LlamaModel:
         attn_out = torch.empty(T, self.hq, self.d, device=ids.device, dtype=self.dtype)
         n_layers = len(self.layers)
         for li, L in enumerate(self.layers):
+            tracing.push(f"layer{li}")
             qkv = L["qkv"].forward(x)
             ops.rope_kv_write(qkv, meta.positions, self.cos_sin, kv.k[li], kv.v[li],
                               meta.slot_mapping, self.hq, self.hkv, L.get("q_norm"),
@@ -297,6 +298,7 @@ class LlamaModel:
                 L["o"], attn_out.view(T, self.hq * self.d), residual, L["post_norm"], eps)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < n_layers else self.final_norm
             x, residual = self.mlp_ar(li, L, x, residual, nxt, eps)
+            tracing.pop()
         return x
 
     def mlp_ar(self, li: int, L: dict, x: torch.Tensor, residual: torch.Tensor,
