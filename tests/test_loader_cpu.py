@@ -97,3 +97,53 @@ def test_missing_checkpoint_is_a_clear_error(tmp_path):
     (tmp_path / "config.json").write_text(json.dumps(_hf_config(TINY)))
     with pytest.raises(FileNotFoundError):
         LLM(str(tmp_path), load_format="safetensors", **KW)
+
+
+def test_qwen3_next_roundtrip(tmp_path):
+    """Hybrid gated-DeltaNet / gated-attention model: HF layouts (per key-head
+    group qkvz / ba rows, zero-centred norms) round-trip exactly."""
+    cfg = ModelConfig.from_hf({
+        "model_type": "qwen3_next", "hidden_size": 128, "num_hidden_layers": 4,
+        "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 32,
+        "intermediate_size": 256, "vocab_size": 512, "rope_theta": 10000.0,
+        "rms_norm_eps": 1e-6, "max_position_embeddings": 512, "tie_word_embeddings": False,
+        "num_experts": 8, "num_experts_per_tok": 2, "moe_intermediate_size": 64,
+        "shared_expert_intermediate_size": 64, "norm_topk_prob": True,
+        "linear_num_key_heads": 2, "linear_num_value_heads": 4, "linear_key_head_dim": 32,
+        "linear_value_head_dim": 32, "linear_conv_kernel_dim": 4, "full_attention_interval": 2,
+        "partial_rotary_factor": 0.25, "num_nextn_predict_layers": 1})
+    a = LLM(cfg, **KW)
+    g = torch.Generator().manual_seed(11)
+    m = a.model
+    # non-trivial norms and GDN parameters so every conversion is exercised
+    m.final_norm += torch.randn(m.final_norm.shape, generator=g) * 0.1
+    for L in m.layers:
+        for k in ("in_norm", "post_norm", "q_norm", "k_norm", "gnorm"):
+            if k in L:
+                L[k] += torch.randn(L[k].shape, generator=g) * 0.1
+    hf_json = {"model_type": "qwen3_next", "hidden_size": 128, "num_hidden_layers": 4,
+               "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 32,
+               "intermediate_size": 256, "vocab_size": 512, "rope_theta": 10000.0,
+               "rms_norm_eps": 1e-6, "max_position_embeddings": 512,
+               "tie_word_embeddings": False, "num_experts": 8, "num_experts_per_tok": 2,
+               "moe_intermediate_size": 64, "shared_expert_intermediate_size": 64,
+               "norm_topk_prob": True, "linear_num_key_heads": 2, "linear_num_value_heads": 4,
+               "linear_key_head_dim": 32, "linear_value_head_dim": 32,
+               "linear_conv_kernel_dim": 4, "full_attention_interval": 2,
+               "partial_rotary_factor": 0.25, "num_nextn_predict_layers": 1}
+    sd = m.hf_state_dict()
+    # HF stores the gated-DeltaNet projection per key-head group: group 1's q
+    # rows follow group 0's [q | k | v | z] block.
+    w = sd["model.layers.0.linear_attn.in_proj_qkvz.weight"]
+    S = 2 * 32 + 2 * 32 * 2
+    assert torch.equal(w[S:S + 32], m.layers[0]["qkvz"].w[32:64])
+    path = _write(tmp_path, hf_json, sd)
+    b = LLM(path, load_format="safetensors", **KW)
+    for La, Lb in zip(a.model.layers, b.model.layers):
+        for k, va in La.items():
+            vb = Lb[k]
+            if isinstance(va, torch.Tensor):
+                assert torch.allclose(va.float(), vb.float(), atol=1e-6), k
+            elif hasattr(va, "w") and isinstance(va.w, torch.Tensor):
+                assert torch.equal(va.w, vb.w), k
+    assert _tokens(a) == _tokens(b)

@@ -126,15 +126,13 @@ class LlamaModel:
             self.layers.append(L)
         self._init_rope()
 
-    def load_hf_state(self, get_tensor, has=None) -> None:
-        """Load from an HF Llama / Qwen3-dense checkpoint: bf16 / fp16 weights,
-        or block-FP8 (``weight`` e4m3 + ``weight_scale_inv`` per 128x128
-        block, the HF "fp8" quantization_config layout). ``get_tensor(name)``
-        returns the full (unsharded) tensor; this rank's shards are cut here
-        (FP8 shards stay aligned to the 128-row / -column scale blocks)."""
+    def _loader_helpers(self, get_tensor, has):
+        """(t, fp8, linear) closures over a checkpoint: ``t(name)`` a tensor on
+        this device in the compute dtype; ``fp8(prefix)`` whether that
+        projection is stored block-FP8; ``linear(parts, cols)`` a linear layer
+        from row slices of one or more projections (FP8 shards stay aligned to
+        the 128-row / -column scale blocks)."""
         cfg, dev, dt = self.cfg, self.device, self.dtype
-        tp, r = self.ps.tp_size, self.ps.tp_rank
-        has = has or (lambda name: True)
 
         def t(name):
             return get_tensor(name).to(device=dev, dtype=dt)
@@ -170,6 +168,18 @@ class LlamaModel:
                 ws.append(w[:, cols] if cols is not None else w)
             return DenseLinear(torch.cat(ws, 0))
 
+        return t, fp8, linear
+
+    def load_hf_state(self, get_tensor, has=None) -> None:
+        """Load from an HF Llama / Qwen3-dense checkpoint: bf16 / fp16 weights,
+        or block-FP8 (``weight`` e4m3 + ``weight_scale_inv`` per 128x128
+        block, the HF "fp8" quantization_config layout). ``get_tensor(name)``
+        returns the full (unsharded) tensor; this rank's shards are cut here
+        (FP8 shards stay aligned to the 128-row / -column scale blocks)."""
+        cfg = self.cfg
+        tp, r = self.ps.tp_size, self.ps.tp_rank
+        has = has or (lambda name: True)
+        t, fp8, linear = self._loader_helpers(get_tensor, has)
         vs = slice(r * self.vocab_local, (r + 1) * self.vocab_local)
         emb = t("model.embed_tokens.weight")
         pad = self.vocab_local * tp - emb.shape[0]

@@ -104,12 +104,140 @@ class Qwen3NextModel(Qwen3MoeModel):
 
     # ------------------------------------------------------------------ weights
     def load_hf_state(self, get_tensor, has=None) -> None:
-        raise NotImplementedError(
-            "Qwen3-Next checkpoint loading (linear-attention / gated-attention layers) is not "
-            "implemented yet; use load_format='dummy'")
+        """Load an HF Qwen3-Next checkpoint (bf16, or block-FP8 projections).
+
+        Layouts converted here: the zero-centred RMSNorm weights (input /
+        post-attention / final / q / k norms store ``w`` with effective weight
+        ``1 + w``) become effective weights; the gated-DeltaNet ``in_proj_qkvz``
+        rows, stored per key-head group as [q | k | v | z] (the group's value
+        heads together), become [q (all local key heads) | k | v | z], and
+        ``in_proj_ba`` ([b | a] per group) becomes [b | a]; ``conv1d.weight``
+        [C, 1, W] channels are already [q | k | v]. This rank keeps its key-head
+        groups (with their value heads), attention heads and MLP shards.
+        Quantised GDN projections are dequantised, reordered and re-quantised
+        per ``cfg.quant``.
+        """
+        cfg, dev, dt = self.cfg, self.device, self.dtype
+        tp, r = self.ps.tp_size, self.ps.tp_rank
+        has = has or (lambda name: True)
+        t, fp8, linear = self._loader_helpers(get_tensor, has)
+
+        def zc(name):  # zero-centred norm -> effective weight
+            return (1.0 + get_tensor(name).float()).to(device=dev, dtype=dt)
+
+        def dense(prefix):  # full-precision weight of a projection (dequantised if FP8)
+            w = get_tensor(prefix + ".weight")
+            if fp8(prefix):
+                s = get_tensor(prefix + ".weight_scale_inv").float()
+                s = s.repeat_interleave(128, 0)[: w.shape[0]].repeat_interleave(128, 1)[:, : w.shape[1]]
+                w = w.float() * s
+            return w.float()
+
+        h, d = cfg.hidden_size, self.d
+        vs = slice(r * self.vocab_local, (r + 1) * self.vocab_local)
+        emb = t("model.embed_tokens.weight")
+        pad = self.vocab_local * tp - emb.shape[0]
+        if pad:
+            emb = torch.cat([emb, emb.new_zeros(pad, emb.shape[1])])
+        self.embed = emb[vs].contiguous()
+        if cfg.tie_embeddings:
+            self.lm_head = self.embed
+        else:
+            lm = t("lm_head.weight")
+            if pad:
+                lm = torch.cat([lm, lm.new_zeros(pad, lm.shape[1])])
+            self.lm_head = lm[vs].contiguous()
+        self.final_norm = zc("model.norm.weight")
+        # attention: q_proj rows are [q | gate] per head (2d rows per head)
+        qg_rows = slice(r * self.hq * 2 * d, (r + 1) * self.hq * 2 * d)
+        o_cols = slice(r * self.hq * d, (r + 1) * self.hq * d)
+        if self.kv_replicated:
+            kvh = r * cfg.num_kv_heads // tp
+            ks = slice(kvh * d, (kvh + 1) * d)
+        else:
+            ks = slice(r * self.hkv * d, (r + 1) * self.hkv * d)
+        # gated DeltaNet: key-head groups [g0, g1) and their value heads
+        HKa, HVa = cfg.linear_num_k_heads, cfg.linear_num_v_heads
+        rat = HVa // HKa
+        DK, DV = self.DK, self.DV
+        S = 2 * DK + 2 * DV * rat
+        g0, g1 = r * self.HK, (r + 1) * self.HK
+        kd = HKa * DK
+        self.layers = []
+        for i, kind in enumerate(self.layer_types):
+            p = f"model.layers.{i}."
+            L = {"kind": kind, "in_norm": zc(p + "input_layernorm.weight"),
+                 "post_norm": zc(p + "post_attention_layernorm.weight")}
+            if kind == "attention":
+                a = p + "self_attn."
+                L["qkv"] = linear([(a + "q_proj", qg_rows), (a + "k_proj", ks), (a + "v_proj", ks)])
+                L["o"] = linear([(a + "o_proj", None)], cols=o_cols)
+                L["q_norm"] = zc(a + "q_norm.weight")
+                L["k_norm"] = zc(a + "k_norm.weight")
+            else:
+                la = p + "linear_attn."
+                W = dense(la + "in_proj_qkvz").view(HKa, S, h)[g0:g1]
+                qkvz = torch.cat([W[:, :DK].reshape(-1, h), W[:, DK:2 * DK].reshape(-1, h),
+                                  W[:, 2 * DK:2 * DK + DV * rat].reshape(-1, h),
+                                  W[:, 2 * DK + DV * rat:].reshape(-1, h)])
+                L["qkvz"] = self.make_linear(qkvz.to(dev))
+                BA = dense(la + "in_proj_ba").view(HKa, 2 * rat, h)[g0:g1]
+                L["ba_w"] = torch.cat([BA[:, :rat].reshape(-1, h),
+                                       BA[:, rat:].reshape(-1, h)]).to(device=dev, dtype=dt)
+                conv = get_tensor(la + "conv1d.weight").reshape(-1, get_tensor(
+                    la + "conv1d.weight").shape[-1])
+                L["conv_w"] = torch.cat([conv[g0 * DK:g1 * DK], conv[kd + g0 * DK:kd + g1 * DK],
+                                         conv[2 * kd + g0 * rat * DV:2 * kd + g1 * rat * DV]]
+                                        ).to(device=dev, dtype=dt)
+                vh = slice(g0 * rat, g1 * rat)
+                L["A_log"] = get_tensor(la + "A_log").float()[vh].to(dev)
+                L["dt_bias"] = get_tensor(la + "dt_bias").float()[vh].to(dev)
+                L["gnorm"] = t(la + "norm.weight")
+                L["out"] = linear([(la + "out_proj", None)],
+                                  cols=slice(g0 * rat * DV, g1 * rat * DV))
+            L.update(self._load_mlp(p + "mlp.", get_tensor, has, t, fp8, linear))
+            self.layers.append(L)
+        self._init_rope()
 
     def hf_state_dict(self) -> dict:
-        raise NotImplementedError("Qwen3-Next checkpoint export is not implemented")
+        """This (TP = 1, bf16) model's weights under HF Qwen3-Next names and
+        layouts: the inverse of ``load_hf_state``."""
+        assert self.ps.tp_size == 1, "export from a single-rank model"
+        cfg, d, h = self.cfg, self.d, self.cfg.hidden_size
+        hq, hkv = self.hq, self.hkv
+        HK, HV, DK, DV = self.HK, self.HV, self.DK, self.DV
+        rat = HV // HK
+
+        def unzc(w):
+            return (w.float() - 1.0).to(w.dtype)
+
+        sd = {"model.embed_tokens.weight": self.embed[: cfg.vocab_size],
+              "model.norm.weight": unzc(self.final_norm)}
+        if not cfg.tie_embeddings:
+            sd["lm_head.weight"] = self.lm_head[: cfg.vocab_size]
+        for i, L in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            sd[p + "input_layernorm.weight"] = unzc(L["in_norm"])
+            sd[p + "post_attention_layernorm.weight"] = unzc(L["post_norm"])
+            if L["kind"] == "attention":
+                a = p + "self_attn."
+                qg, k, v = torch.split(L["qkv"].w, [2 * hq * d, hkv * d, hkv * d])
+                sd.update({a + "q_proj.weight": qg, a + "k_proj.weight": k, a + "v_proj.weight": v,
+                           a + "o_proj.weight": L["o"].w, a + "q_norm.weight": unzc(L["q_norm"]),
+                           a + "k_norm.weight": unzc(L["k_norm"])})
+            else:
+                la = p + "linear_attn."
+                q, k, v, z = torch.split(L["qkvz"].w, [HK * DK, HK * DK, HV * DV, HV * DV])
+                W = torch.cat([q.view(HK, DK, h), k.view(HK, DK, h), v.view(HK, rat * DV, h),
+                               z.view(HK, rat * DV, h)], 1).reshape(-1, h)
+                b, a_ = torch.split(L["ba_w"], [HV, HV])
+                BA = torch.cat([b.view(HK, rat, h), a_.view(HK, rat, h)], 1).reshape(-1, h)
+                sd.update({la + "in_proj_qkvz.weight": W, la + "in_proj_ba.weight": BA,
+                           la + "conv1d.weight": L["conv_w"].unsqueeze(1),
+                           la + "A_log": L["A_log"], la + "dt_bias": L["dt_bias"],
+                           la + "norm.weight": L["gnorm"], la + "out_proj.weight": L["out"].w})
+            sd.update(self._mlp_state(p + "mlp.", L))
+        return {k: v.detach().contiguous().cpu() for k, v in sd.items()}
 
     def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
         cfg, dev, dt = self.cfg, self.device, self.dtype
