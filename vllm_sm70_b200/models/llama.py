@@ -72,7 +72,8 @@ class LlamaModel:
         self.layers: list[dict] = []
         self.scale = 1.0 / math.sqrt(self.d)
         self.cos_sin = None
-        self.embed = None
+        self.embed = None        # this rank's vocab shard (LM-head tie)
+        self.embed_full = None   # the whole table, replicated: no collective on lookup
         self.lm_head = None
         self.final_norm = None
 
@@ -107,7 +108,7 @@ class LlamaModel:
             return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std
 
         h = cfg.hidden_size
-        self.embed = rnd(self.vocab_local, h).to(dt)
+        self._set_embedding(self._dummy_embedding(seed, std))
         self.lm_head = self.embed if cfg.tie_embeddings else rnd(self.vocab_local, h).to(dt)
         self.final_norm = torch.ones(h, device=dev, dtype=dt)
         qkv_out = (self.hq + 2 * self.hkv) * self.d
@@ -185,7 +186,7 @@ class LlamaModel:
         pad = self.vocab_local * tp - emb.shape[0]
         if pad:
             emb = torch.cat([emb, emb.new_zeros(pad, emb.shape[1])])
-        self.embed = emb[vs].contiguous()
+        self._set_embedding(emb)
         if cfg.tie_embeddings:
             self.lm_head = self.embed
         else:
@@ -272,16 +273,34 @@ class LlamaModel:
         return n
 
     # ------------------------------------------------------------------ forward
+    def _dummy_embedding(self, seed: int, std: float) -> torch.Tensor:
+        """Random full (padded) embedding table, identical on every rank."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 7919 + 104723)
+        n = self.vocab_local * self.ps.tp_size
+        return (torch.randn(n, self.cfg.hidden_size, generator=g, device=self.device,
+                            dtype=torch.float32) * std).to(self.dtype)
+
+    def _set_embedding(self, full: torch.Tensor) -> None:
+        """Keep the whole (padded) table on every rank -- one lookup, no
+        all-reduce per step -- and this rank's vocab shard as a view of it
+        (the LM head's rows when the embeddings are tied)."""
+        r = self.ps.tp_rank
+        self.embed_full = full.contiguous()
+        self.embed = self.embed_full[r * self.vocab_local:(r + 1) * self.vocab_local]
+
     def embed_tokens(self, ids: torch.Tensor) -> torch.Tensor:
         out = torch.empty(ids.shape[0], self.cfg.hidden_size, device=ids.device, dtype=self.dtype)
+        full = self.embed_full is not None
+        table, start = (self.embed_full, 0) if full else (self.embed, self.vocab_start)
         if ids.is_cuda:
-            torch.ops._b200_C.embedding(out, ids, self.embed, self.vocab_start)
+            torch.ops._b200_C.embedding(out, ids, table, start)
             launch_count.add(1)
         else:
-            loc = ids - self.vocab_start
-            ok = (loc >= 0) & (loc < self.embed.shape[0])
-            out.copy_(self.embed[loc.clamp(0, self.embed.shape[0] - 1)] * ok[:, None])
-        if self.ps.tp_size > 1:
+            loc = ids - start
+            ok = (loc >= 0) & (loc < table.shape[0])
+            out.copy_(table[loc.clamp(0, table.shape[0] - 1)] * ok[:, None])
+        if self.ps.tp_size > 1 and not full:
             pstate.tp_all_reduce(out)
         return out
 

@@ -139,7 +139,7 @@ class Qwen3NextModel(Qwen3MoeModel):
         pad = self.vocab_local * tp - emb.shape[0]
         if pad:
             emb = torch.cat([emb, emb.new_zeros(pad, emb.shape[1])])
-        self.embed = emb[vs].contiguous()
+        self._set_embedding(emb)
         if cfg.tie_embeddings:
             self.lm_head = self.embed
         else:
@@ -248,7 +248,7 @@ class Qwen3NextModel(Qwen3MoeModel):
             return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std
 
         h = cfg.hidden_size
-        self.embed = rnd(self.vocab_local, h).to(dt)
+        self._set_embedding(self._dummy_embedding(seed, std))
         self.lm_head = self.embed if cfg.tie_embeddings else rnd(self.vocab_local, h).to(dt)
         # zero-centred norms: effective weight = 1 + w (w = 0 at init)
         self.final_norm = torch.ones(h, device=dev, dtype=dt)
