@@ -138,3 +138,40 @@ def test_temperature_sampling_runs_and_is_seeded():
     sp = SamplingParams(max_tokens=6, temperature=0.7, seed=123, ignore_eos=True)
     a = _llm().generate(prompts, sp)
     assert all(len(o.output_token_ids) == 6 for o in a)
+
+
+def test_prefix_caching_reuses_blocks_and_matches():
+    """Requests sharing a prompt prefix reuse its KV blocks (fewer prefilled
+    tokens) and generate exactly what a cache-free engine generates; blocks
+    held only by the cache are evicted when allocation runs short."""
+    g = torch.Generator().manual_seed(5)
+    prefix = torch.randint(0, 512, (50,), generator=g)
+    prompts = [torch.cat([prefix, torch.randint(0, 512, (n,), generator=g)]) for n in (5, 9, 17)]
+    sp = SamplingParams(max_tokens=5, ignore_eos=True)
+    ref = _llm()
+    want = [ref.generate([p], sp)[0].output_token_ids for p in prompts]
+    llm = _llm(enable_prefix_caching=True)
+    got = [llm.generate([p], sp)[0].output_token_ids for p in prompts]
+    assert got == want
+    pc = llm.prefix_cache
+    assert pc.hits >= 2 * 3  # 3 full blocks of the 50-token prefix, reused twice
+    # the cache's blocks stay allocated between generate calls
+    assert all(llm.runner.alloc.block_refcount(b) == 1 for b in pc.entries.values())
+    # whole prompt cached: the last token is still prefilled
+    again = llm.generate([prompts[0]], sp)[0].output_token_ids
+    assert again == want[0]
+    # scarcity: a tiny KV pool forces eviction of cache-only blocks
+    small = _llm(enable_prefix_caching=True, num_kv_blocks=9)
+    outs = [small.generate([p], sp)[0].output_token_ids for p in prompts]
+    assert outs == want
+
+
+def test_prefix_cache_keys_chain():
+    from vllm_sm70_b200.engine.prefix_cache import block_keys
+
+    a = torch.arange(64)
+    b = torch.cat([torch.arange(16, 32), torch.arange(16), torch.arange(32, 64)])
+    ka, kb = block_keys(a, 16, 4), block_keys(b, 16, 4)
+    # same tokens in block 2 and 3 but after a different prefix: different keys
+    assert ka[0] != kb[0] and ka[2] != kb[2] and ka[3] != kb[3]
+    assert block_keys(a, 16, 2) == ka[:2]

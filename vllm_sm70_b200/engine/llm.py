@@ -33,6 +33,7 @@ from ..parallel import state as pstate
 from ..utils import tracing
 from ..utils.watchdog import StreamWatchdog
 from .model_runner import ModelRunner
+from .prefix_cache import PrefixCache
 from .sampling_params import RequestOutput, SamplingParams
 
 
@@ -71,7 +72,7 @@ class LLM:
                  load_format: str = "dummy", seed: int = 0, enforce_eager: bool = False,
                  dtype=torch.bfloat16, num_kv_blocks: int | None = None,
                  tune_gemm: bool = True, gemm_lut_path: str | None = None,
-                 speculative_k: int = 0):
+                 speculative_k: int = 0, enable_prefix_caching: bool | None = None):
         self.cfg: ModelConfig = resolve(model)
         ps = pstate.get() if pstate._STATE is not None else None
         if ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
@@ -123,6 +124,14 @@ class LLM:
         if self.spec_k == 0:
             self.runner.capture()
         self.last_stats: GenerateStats | None = None
+        # Prefix caching: content-addressed reuse of full prompt KV blocks. Not
+        # for models with recurrent state or with a speculative draft head
+        # (neither state is cached with the blocks).
+        if enable_prefix_caching is None:
+            enable_prefix_caching = bool(envs.get("VLLM_B200_PREFIX_CACHING"))
+        hybrid = hasattr(self.model, "reset_slots")
+        self.prefix_cache = (PrefixCache(self.runner.alloc, self.runner.block_size)
+                             if enable_prefix_caching and not hybrid and self.spec_k == 0 else None)
         wd = int(envs.get("VLLM_B200_WATCHDOG_S"))
         self.watchdog = (StreamWatchdog(wd) if wd > 0 and self.device.type == "cuda" else None)
 
@@ -197,11 +206,20 @@ class LLM:
                 if total > runner.max_model_len:
                     raise ValueError(f"request {r.rid}: {total} tokens > max_model_len")
                 nblk = math.ceil(total / bs)
-                if runner.alloc.num_free() < nblk:
+                pc = self.prefix_cache
+                hit = pc.lookup(r.prompt)[1] if pc is not None else []
+                need = nblk - len(hit)
+                if pc is not None and runner.alloc.num_free() < need:
+                    pc.evict(need)
+                if runner.alloc.num_free() < need:
+                    if hit:  # give the prefix references back
+                        runner.alloc.free(torch.tensor(hit, dtype=torch.int32))
                     break
                 waiting.popleft()
                 r.slot = free_slots.pop()
-                r.blocks = runner.alloc.allocate(nblk)
+                r.blocks = torch.cat([torch.tensor(hit, dtype=torch.int32),
+                                      runner.alloc.allocate(need)])
+                r.prefilled = len(hit) * bs  # cached KV: prefill starts after it
                 runner.set_block_row(r.slot, r.blocks)
                 seed = r.params.seed if r.params.seed is not None else 0x9E3779B97F4A7C15 ^ r.rid
                 runner.set_sampling(r.slot, 0.0 if r.params.greedy else r.params.temperature,
@@ -241,6 +259,8 @@ class LLM:
                         self.watchdog.arm(e_post, "prefill chunk")
                 for r in finishing:
                     r.generated = 1
+                    if self.prefix_cache is not None:
+                        self.prefix_cache.insert(r.prompt, r.blocks)
                 if cuda and finishing:
                     e = ev()
                     e.record()

@@ -96,6 +96,9 @@ _reg("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS", "int", 1024, "comm",
      "Smallest token count that takes the fused GEMM + all-reduce kernel (measured at TP2 on "
      "Llama-3.1-8B shapes: faster for 16384-token prefill chunks, slower than the vendor GEMM + "
      "collective kernel at 256-row decode steps).")
+_reg("VLLM_B200_PREFIX_CACHING", "optin", False, "runtime",
+     "Reuse the KV of full prompt blocks across requests with the same token prefix "
+     "(LLM(enable_prefix_caching=...) overrides).")
 _reg("VLLM_B200_NVTX", "optin", False, "runtime",
      "Emit NVTX ranges per layer and engine phase for profiler timelines.")
 _reg("VLLM_B200_WATCHDOG_S", "int", 0, "runtime",
