@@ -1,0 +1,119 @@
+"""OpenAI-compatible server over the engine (CPU engine, tiny model, a fake
+tokenizer): completions from token ids and text, batching of concurrent
+requests, stop tokens / strings, chat with the reasoning split, and the
+400s for what is not served."""
+import threading
+
+import pytest
+import torch
+
+from vllm_sm70_b200.engine import LLM, SamplingParams
+from vllm_sm70_b200.entrypoints.openai_server import build_app
+from vllm_sm70_b200.models.config import ModelConfig
+
+TINY = ModelConfig(arch="llama", hidden_size=128, num_layers=2, num_heads=4, num_kv_heads=2,
+                   head_dim=32, intermediate_size=256, vocab_size=512, rope_theta=10000.0,
+                   rms_eps=1e-5, max_position=512)
+
+
+class Tok:
+    """Characters <-> ids 1..255; a few special tokens above."""
+    eos_token_id = 300
+    eos_token = "</s>"
+    chat_template = "{% if add_generation_prompt %}<|assistant|><think>{% endif %}"
+    special = {301: "<think>", 302: "</think>", 300: "</s>"}
+
+    def encode(self, text):
+        return [min(255, max(1, ord(c))) for c in text]
+
+    def decode(self, ids, skip_special_tokens=True):
+        out = []
+        for i in ids:
+            if i in self.special:
+                if not skip_special_tokens:
+                    out.append(self.special[i])
+            elif 0 < i < 256:
+                out.append(chr(i))
+            else:
+                out.append("?")
+        return "".join(out)
+
+    def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=True, **kw):
+        text = "".join(f"<{m['role']}>{m['content']}" for m in messages)
+        return self.encode(text) + [301]
+
+
+@pytest.fixture(scope="module")
+def client():
+    from fastapi.testclient import TestClient
+
+    llm = LLM(TINY, max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=64)
+    app = build_app(llm, Tok(), "tiny", reasoning_parser="glm47_b200", max_batch=4)
+    with TestClient(app) as c:
+        c.llm = llm
+        c.app_ = app
+        yield c
+
+
+def test_models_and_health(client):
+    assert client.get("/health").json()["status"] == "ok"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+
+
+def test_completion_token_ids_match_engine(client):
+    ids = list(range(10, 30))
+    r = client.post("/v1/completions", json={"prompt": ids, "max_tokens": 6,
+                                              "temperature": 0.0, "ignore_eos": True}).json()
+    want = client.llm.generate([torch.tensor(ids)], SamplingParams(max_tokens=6))[0]
+    assert r["choices"][0]["token_ids"] == want.output_token_ids
+    assert r["usage"] == {"prompt_tokens": 20, "completion_tokens": 6, "total_tokens": 26}
+    assert r["choices"][0]["finish_reason"] == "length"
+
+
+def test_text_prompt_batch_and_concurrency(client):
+    r = client.post("/v1/completions", json={"prompt": ["hello", "world!!"], "max_tokens": 4,
+                                              "temperature": 0.0, "ignore_eos": True}).json()
+    assert [c["index"] for c in r["choices"]] == [0, 1]
+    assert all(len(c["token_ids"]) == 4 and isinstance(c["text"], str) for c in r["choices"])
+    # concurrent requests are served (batched by the worker)
+    res = []
+
+    def go(i):
+        res.append(client.post("/v1/completions", json={
+            "prompt": list(range(5 + i, 25 + i)), "max_tokens": 3, "temperature": 0.0,
+            "ignore_eos": True}).status_code)
+
+    th = [threading.Thread(target=go, args=(i,)) for i in range(6)]
+    [t.start() for t in th]
+    [t.join() for t in th]
+    assert res == [200] * 6
+
+
+def test_stop_string_and_unsupported(client):
+    r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8, "temperature": 0.0,
+                                              "ignore_eos": True, "stop": ["\\u0000"]})
+    assert r.status_code == 200
+    for bad in ({"n": 2}, {"stream": True}, {"logprobs": 1}):
+        body = {"prompt": [1, 2, 3], "max_tokens": 2, **bad}
+        assert client.post("/v1/completions", json=body).status_code == 400
+
+
+def test_chat_reasoning_split(client):
+    r = client.post("/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": "hi"}], "max_tokens": 5, "temperature": 0.0,
+        "ignore_eos": True}).json()
+    msg = r["choices"][0]["message"]
+    assert msg["role"] == "assistant" and "content" in msg
+    # the template opens <think>: everything before </think> is reasoning
+    assert "reasoning_content" in msg
+
+
+def test_stop_token_truncates_engine_output():
+    from vllm_sm70_b200.engine.llm import _truncate_at_stop
+
+    sp = SamplingParams(max_tokens=8, stop_token_ids=[7])
+    assert _truncate_at_stop([1, 2, 7, 9, 7], sp) == [1, 2, 7]
+    assert _truncate_at_stop([1, 2, 3], sp) == [1, 2, 3]
+    sp2 = SamplingParams(max_tokens=8, stop_token_ids=[7], ignore_eos=True)
+    assert _truncate_at_stop([1, 7, 3], sp2) == [1, 7, 3]

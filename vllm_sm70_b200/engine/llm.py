@@ -64,6 +64,19 @@ class GenerateStats:
     spec_slots: int = 0    # (row, step) pairs; spec_tokens / spec_slots = tokens per step
 
 
+def _truncate_at_stop(tokens: list[int], p: SamplingParams) -> list[int]:
+    """Cut the output after the first stop token (kept, like vLLM's token ids)
+    unless the request ignores EOS. Decode runs whole bursts on the device, so
+    tokens past a stop are computed and dropped here."""
+    if p.ignore_eos or not p.stop_token_ids:
+        return tokens
+    stops = set(p.stop_token_ids)
+    for i, t in enumerate(tokens):
+        if t in stops:
+            return tokens[: i + 1]
+    return tokens
+
+
 class LLM:
     def __init__(self, model: str | ModelConfig | dict = "llama-3.1-8b",
                  tensor_parallel_size: int | None = None, max_num_seqs: int = 256,
@@ -307,7 +320,7 @@ class LLM:
                 outs = runner.out_tokens[torch.tensor(slots, device=self.device)]
                 outs_h = outs.to("cpu", non_blocking=False)
                 for r, row in zip(finished_now, outs_h):
-                    r.out = row[: r.params.max_tokens].tolist()
+                    r.out = _truncate_at_stop(row[: r.params.max_tokens].tolist(), r.params)
                     r.done = True
                     runner.alloc.free(r.blocks)
                     free_slots.append(r.slot)

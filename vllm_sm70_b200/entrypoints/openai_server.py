@@ -1,0 +1,286 @@
+"""OpenAI-compatible HTTP server over the engine (``LLM``).
+
+    python -m vllm_sm70_b200.entrypoints.openai_server --model /path/to/hf-checkpoint \\
+        --port 8000 [--max-num-seqs 256] [--max-model-len 4096]
+    (TP: one process per GPU under torchrun; rank 0 serves HTTP, every rank runs the engine)
+
+Endpoints: ``GET /health``, ``GET /v1/models``, ``POST /v1/completions``,
+``POST /v1/chat/completions``. Requests are batched: a worker thread takes
+every request queued when it becomes free and runs them as one
+``LLM.generate`` call (chunked prefill + CUDA-graph decode across the batch);
+each handler awaits its own result. With a tokenizer, text prompts and chat
+messages (through the checkpoint's chat template) are accepted and the
+``<think>`` / ``<tool_call>`` reasoning split is applied to chat replies
+(``--reasoning-parser glm47_b200``). Token-id prompts work without one.
+
+Scope: n = 1, no streaming, no log-probabilities (requests asking for them
+get HTTP 400); sampling is greedy or temperature (Gumbel-max, seeded).
+
+Reference parity: the reference is served through ``vllm serve`` with its
+plugin; this is the same OpenAI surface for the standalone runtime.
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import concurrent.futures
+import queue
+import threading
+import time
+import uuid
+
+from ..engine.sampling_params import SamplingParams
+
+
+class Batcher:
+    """Collects requests from handler threads / coroutines and runs them in
+    batches on one worker thread (the engine is not re-entrant)."""
+
+    def __init__(self, llm, max_batch: int = 256, group=None):
+        self.llm = llm
+        self.max_batch = max_batch
+        self.group = group  # TP: the CPU group whose other ranks run follower_loop
+        self.q: queue.Queue = queue.Queue()
+        self._stop = False
+        self.batches = 0
+        self.thread = threading.Thread(target=self._run, name="b200-batcher", daemon=True)
+        self.thread.start()
+
+    def submit(self, prompt_ids: list[int], params: SamplingParams) -> concurrent.futures.Future:
+        fut: concurrent.futures.Future = concurrent.futures.Future()
+        self.q.put((prompt_ids, params, fut))
+        return fut
+
+    def _run(self) -> None:
+        import torch
+
+        while not self._stop:
+            try:
+                first = self.q.get(timeout=0.1)
+            except queue.Empty:
+                continue
+            items = [first]
+            while len(items) < self.max_batch:
+                try:
+                    items.append(self.q.get_nowait())
+                except queue.Empty:
+                    break
+            try:
+                batch = ([p for p, _, _ in items], [sp for _, sp, _ in items])
+                if self.group is not None:  # every rank runs the same generate call
+                    import torch.distributed as dist
+
+                    dist.broadcast_object_list([batch], src=0, group=self.group)
+                outs = self.llm.generate([torch.tensor(p, dtype=torch.int64) for p in batch[0]],
+                                         batch[1])
+                self.batches += 1
+                for (_, _, fut), o in zip(items, outs):
+                    fut.set_result(o)
+            except Exception as e:  # noqa: BLE001 - reported to every waiting request
+                for _, _, fut in items:
+                    if not fut.done():
+                        fut.set_exception(e)
+
+    def close(self) -> None:
+        self._stop = True
+        self.thread.join(timeout=2.0)
+        if self.group is not None:  # release the followers
+            import torch.distributed as dist
+
+            dist.broadcast_object_list([None], src=0, group=self.group)
+
+
+def follower_loop(llm, group) -> None:
+    """Ranks > 0 under TP: run every batch rank 0 broadcasts, until it sends
+    None (rank-uniform: the same generate calls in the same order)."""
+    import torch
+    import torch.distributed as dist
+
+    while True:
+        obj = [None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        if obj[0] is None:
+            return
+        prompts, params = obj[0]
+        llm.generate([torch.tensor(p, dtype=torch.int64) for p in prompts], params)
+
+
+def _params(body: dict, tokenizer) -> SamplingParams:
+    if int(body.get("n", 1)) != 1:
+        raise ValueError("only n = 1 is served")
+    if body.get("logprobs") or body.get("stream"):
+        raise ValueError("streaming and log-probabilities are not served")
+    stop_ids = list(body.get("stop_token_ids") or [])
+    ignore_eos = bool(body.get("ignore_eos", False))
+    eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
+    if eos is not None and not ignore_eos:
+        stop_ids.append(int(eos))
+    return SamplingParams(max_tokens=int(body.get("max_tokens") or 16),
+                          temperature=float(body.get("temperature", 1.0)),
+                          seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids)
+
+
+def _apply_stop_strings(text: str, stop) -> tuple[str, bool]:
+    if not stop:
+        return text, False
+    stops = [stop] if isinstance(stop, str) else list(stop)
+    cut = min((text.find(s) for s in stops if s and text.find(s) >= 0), default=-1)
+    return (text[:cut], True) if cut >= 0 else (text, False)
+
+
+def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: str | None = None,
+              max_batch: int = 256, group=None):
+    from fastapi import FastAPI, HTTPException
+
+    from ..integration import reasoning as rp
+
+    import contextlib
+
+    batcher = Batcher(llm, max_batch, group)
+
+    @contextlib.asynccontextmanager
+    async def lifespan(_app):
+        yield
+        batcher.close()
+
+    app = FastAPI(title="vllm-b200", lifespan=lifespan)
+    app.state.batcher = batcher
+    created = int(time.time())
+
+    def encode(prompt):
+        if isinstance(prompt, list) and all(isinstance(t, int) for t in prompt):
+            return list(prompt)
+        if isinstance(prompt, str):
+            if tokenizer is None:
+                raise HTTPException(400, "text prompts need a tokenizer; send token ids")
+            return list(tokenizer.encode(prompt))
+        raise HTTPException(400, "prompt must be a string or a list of token ids")
+
+    def decode(ids):
+        return tokenizer.decode(ids, skip_special_tokens=True) if tokenizer is not None else None
+
+    async def run(prompt_ids, sp):
+        fut = batcher.submit(prompt_ids, sp)
+        return await asyncio.wrap_future(fut)
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model",
+                                            "created": created, "owned_by": "vllm-b200"}]}
+
+    @app.post("/v1/completions")
+    async def completions(body: dict):
+        try:
+            sp = _params(body, tokenizer)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        prompts = body.get("prompt")
+        batch = (prompts if isinstance(prompts, list) and prompts
+                 and not all(isinstance(t, int) for t in prompts) else [prompts])
+        ids = [encode(p) for p in batch]
+        outs = await asyncio.gather(*[run(p, sp) for p in ids])
+        choices, n_out = [], 0
+        for i, o in enumerate(outs):
+            text = decode(o.output_token_ids)
+            last = o.output_token_ids[-1] if o.output_token_ids else None
+            stopped = last is not None and last in sp.stop_token_ids
+            if text is not None:
+                text, hit = _apply_stop_strings(text, body.get("stop"))
+                stopped = stopped or hit
+            n_out += len(o.output_token_ids)
+            choices.append({"index": i, "text": text, "token_ids": o.output_token_ids,
+                            "finish_reason": "stop" if stopped else "length"})
+        return {"id": f"cmpl-{uuid.uuid4().hex}", "object": "text_completion", "created":
+                int(time.time()), "model": model_name, "choices": choices,
+                "usage": {"prompt_tokens": sum(len(p) for p in ids), "completion_tokens": n_out,
+                          "total_tokens": sum(len(p) for p in ids) + n_out}}
+
+    @app.post("/v1/chat/completions")
+    async def chat(body: dict):
+        if tokenizer is None or not hasattr(tokenizer, "apply_chat_template"):
+            raise HTTPException(400, "chat needs a tokenizer with a chat template")
+        try:
+            sp = _params(body, tokenizer)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        kwargs = body.get("chat_template_kwargs") or {}
+        ids = list(tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True,
+                                                 tokenize=True, **kwargs))
+        o = await run(ids, sp)
+        raw = tokenizer.decode(o.output_token_ids, skip_special_tokens=False)
+        last = o.output_token_ids[-1] if o.output_token_ids else None
+        stopped = last is not None and last in sp.stop_token_ids
+        msg = {"role": "assistant"}
+        if reasoning_parser == "glm47_b200":
+            enabled, inside = rp.thinking_policy(getattr(tokenizer, "chat_template", None), kwargs)
+            if enabled:
+                r, c = rp.ThinkSplitter(inside).feed(raw)
+                msg["reasoning_content"] = r.rstrip() or None
+                raw = c
+        content = raw
+        eos_text = getattr(tokenizer, "eos_token", None)
+        if eos_text and content.endswith(eos_text):
+            content = content[: -len(eos_text)]
+        content, hit = _apply_stop_strings(content, body.get("stop"))
+        msg["content"] = content
+        return {"id": f"chatcmpl-{uuid.uuid4().hex}", "object": "chat.completion",
+                "created": int(time.time()), "model": model_name,
+                "choices": [{"index": 0, "message": msg,
+                             "finish_reason": "stop" if (stopped or hit) else "length"}],
+                "usage": {"prompt_tokens": len(ids),
+                          "completion_tokens": len(o.output_token_ids),
+                          "total_tokens": len(ids) + len(o.output_token_ids)}}
+
+    return app
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", required=True, help="HF checkpoint directory or preset name")
+    ap.add_argument("--load-format", default="safetensors", choices=["safetensors", "dummy"])
+    ap.add_argument("--served-model-name", default=None)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--tensor-parallel-size", type=int, default=1)
+    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--max-model-len", type=int, default=4096)
+    ap.add_argument("--max-num-batched-tokens", type=int, default=16384)
+    ap.add_argument("--block-size", type=int, default=16)
+    ap.add_argument("--enable-prefix-caching", action="store_true")
+    ap.add_argument("--reasoning-parser", default=None, choices=[None, "glm47_b200"])
+    args = ap.parse_args(argv)
+
+    from ..engine import LLM
+    from ..parallel import state as pstate
+
+    llm = LLM(args.model, tensor_parallel_size=args.tensor_parallel_size,
+              max_num_seqs=args.max_num_seqs, max_model_len=args.max_model_len,
+              max_num_batched_tokens=args.max_num_batched_tokens, block_size=args.block_size,
+              load_format=args.load_format, enable_prefix_caching=args.enable_prefix_caching)
+    tok = None
+    if args.load_format == "safetensors":
+        try:
+            from transformers import AutoTokenizer
+
+            tok = AutoTokenizer.from_pretrained(args.model)
+        except Exception:  # noqa: BLE001 - token-id prompts still work
+            tok = None
+    ps = pstate.get()
+    group = ps.cpu_group if ps.tp_size > 1 else None
+    if ps.tp_size > 1 and ps.tp_rank != 0:
+        follower_loop(llm, group)
+        return
+    import uvicorn
+
+    app = build_app(llm, tok, args.served_model_name or args.model,
+                    reasoning_parser=args.reasoning_parser, max_batch=args.max_num_seqs,
+                    group=group)
+    uvicorn.run(app, host=args.host, port=args.port)
+
+
+if __name__ == "__main__":
+    main()
