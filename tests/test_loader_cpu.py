@@ -147,3 +147,34 @@ def test_qwen3_next_roundtrip(tmp_path):
             elif hasattr(va, "w") and isinstance(va.w, torch.Tensor):
                 assert torch.equal(va.w, vb.w), k
     assert _tokens(a) == _tokens(b)
+
+
+def test_qwen3_next_mtp_roundtrip(tmp_path):
+    """The MTP draft layer (``mtp.*``, gated attention + MoE, zero-centred
+    norms) loads from the checkpoint; speculative greedy decoding then equals
+    plain greedy decoding of the same weights."""
+    hf_json = {"model_type": "qwen3_next", "hidden_size": 128, "num_hidden_layers": 4,
+               "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 32,
+               "intermediate_size": 256, "vocab_size": 512, "rope_theta": 10000.0,
+               "rms_norm_eps": 1e-6, "max_position_embeddings": 512,
+               "tie_word_embeddings": False, "num_experts": 8, "num_experts_per_tok": 2,
+               "moe_intermediate_size": 64, "shared_expert_intermediate_size": 64,
+               "norm_topk_prob": True, "linear_num_key_heads": 2, "linear_num_value_heads": 4,
+               "linear_key_head_dim": 32, "linear_value_head_dim": 32,
+               "linear_conv_kernel_dim": 4, "full_attention_interval": 2,
+               "partial_rotary_factor": 0.25, "num_nextn_predict_layers": 1}
+    cfg = ModelConfig.from_hf(hf_json)
+    a = LLM(cfg, speculative_k=2, **KW)
+    head = a.runner.mtp
+    g = torch.Generator().manual_seed(12)
+    for k in ("norm_e", "norm_h", "final_norm"):
+        getattr(head, k).add_(torch.randn(getattr(head, k).shape, generator=g) * 0.1)
+    sd = dict(a.model.hf_state_dict())
+    sd.update(head.hf_state_dict())
+    path = _write(tmp_path, hf_json, sd)
+    b = LLM(path, load_format="safetensors", speculative_k=2, **KW)
+    hb = b.runner.mtp
+    assert torch.allclose(hb.norm_e.float(), head.norm_e.float(), atol=1e-6)
+    assert torch.equal(hb.fc.w, head.fc.w) and torch.equal(hb.layer["qkv"].w, head.layer["qkv"].w)
+    plain = LLM(path, load_format="safetensors", **KW)
+    assert _tokens(b) == _tokens(plain)

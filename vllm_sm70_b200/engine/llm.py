@@ -126,7 +126,14 @@ class LLM:
         if self.spec_k > 0:
             from ..models.mtp import MTPHead
 
-            self.runner.enable_spec(MTPHead(self.model, seed=seed + 1), self.spec_k)
+            head = MTPHead(self.model, seed=seed + 1)
+            if load_format != "dummy" and head.gated:
+                from ..models.loader import SafetensorsIndex
+
+                index = SafetensorsIndex(model)
+                if "mtp.fc.weight" in index:  # the checkpoint ships its MTP layer
+                    head.load_hf_state(index.get, has=index.__contains__)
+            self.runner.enable_spec(head, self.spec_k)
         if self.device.type == "cuda" and tune_gemm:
             from . import warmup
 

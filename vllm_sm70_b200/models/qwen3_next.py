@@ -148,14 +148,7 @@ class Qwen3NextModel(Qwen3MoeModel):
                 lm = torch.cat([lm, lm.new_zeros(pad, lm.shape[1])])
             self.lm_head = lm[vs].contiguous()
         self.final_norm = zc("model.norm.weight")
-        # attention: q_proj rows are [q | gate] per head (2d rows per head)
-        qg_rows = slice(r * self.hq * 2 * d, (r + 1) * self.hq * 2 * d)
-        o_cols = slice(r * self.hq * d, (r + 1) * self.hq * d)
-        if self.kv_replicated:
-            kvh = r * cfg.num_kv_heads // tp
-            ks = slice(kvh * d, (kvh + 1) * d)
-        else:
-            ks = slice(r * self.hkv * d, (r + 1) * self.hkv * d)
+        qg_rows, ks, o_cols = self.attn_shards()
         # gated DeltaNet: key-head groups [g0, g1) and their value heads
         HKa, HVa = cfg.linear_num_k_heads, cfg.linear_num_v_heads
         rat = HVa // HKa
@@ -198,6 +191,20 @@ class Qwen3NextModel(Qwen3MoeModel):
             L.update(self._load_mlp(p + "mlp.", get_tensor, has, t, fp8, linear))
             self.layers.append(L)
         self._init_rope()
+
+    def attn_shards(self) -> tuple[slice, slice, slice]:
+        """This rank's rows of a gated-attention q_proj ([q | gate] per head,
+        2d rows each) and of k_proj / v_proj, and its columns of o_proj."""
+        cfg, d = self.cfg, self.d
+        tp, r = self.ps.tp_size, self.ps.tp_rank
+        qg_rows = slice(r * self.hq * 2 * d, (r + 1) * self.hq * 2 * d)
+        o_cols = slice(r * self.hq * d, (r + 1) * self.hq * d)
+        if self.kv_replicated:
+            kvh = r * cfg.num_kv_heads // tp
+            ks = slice(kvh * d, (kvh + 1) * d)
+        else:
+            ks = slice(r * self.hkv * d, (r + 1) * self.hkv * d)
+        return qg_rows, ks, o_cols
 
     def hf_state_dict(self) -> dict:
         """This (TP = 1, bf16) model's weights under HF Qwen3-Next names and
