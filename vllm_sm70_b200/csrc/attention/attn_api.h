@@ -38,7 +38,6 @@ bool fa_tc_enabled();
 bool fa_tc_supported(const AttnArgs& a);
 void fa_tc_launch(const AttnArgs& a, cudaStream_t stream);
 // Bring-up aid: override the V operand descriptor strides (0, 0 = defaults).
-void fa_tc_set_v_strides(uint32_t lbo, uint32_t sbo);
 // Profiling aid: 8 x grid uint64 %globaltimer stamps per launch (nullptr = off):
 // entry, set-up done, Q landed, first S ready, softmax loop done, last PV
 // done, epilogue stored, exit.

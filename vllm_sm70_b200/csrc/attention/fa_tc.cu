@@ -508,12 +508,6 @@ bool fa_tc_enabled() {
   return on;
 }
 
-uint32_t g_fa_v_lbo = 0, g_fa_v_sbo = 0;  // 0 = defaults (bring-up override)
-
-void fa_tc_set_v_strides(uint32_t lbo, uint32_t sbo) {
-  g_fa_v_lbo = lbo;
-  g_fa_v_sbo = sbo;
-}
 
 bool fa_tc_supported(const AttnArgs& a) {
   const int G = a.Hkv > 0 ? a.Hq / a.Hkv : 0;
@@ -567,8 +561,10 @@ void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   p.err = device_status_ptr(dev);
-  p.v_lbo = g_fa_v_lbo ? g_fa_v_lbo : (uint32_t)kHalf;  // next 64-d block of V
-  p.v_sbo = g_fa_v_sbo ? g_fa_v_sbo : 1024u;            // next 8-key group
+  // V as an MN-major B operand: the next 64-column block of V is a whole
+  // 128-row half (16 KB) away, the next group of 8 keys one 1024-byte atom.
+  p.v_lbo = (uint32_t)kHalf;
+  p.v_sbo = 1024u;
   const int max_qt = (a.max_q_len * G + FM - 1) / FM;
   if (max_qt <= 0 || a.num_seqs <= 0) return;
   launch_pdl(kernel, dim3(max_qt, a.num_seqs, a.Hkv), dim3(kFaThreads), kFaSmem, stream, nullptr,

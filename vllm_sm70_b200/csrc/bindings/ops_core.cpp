@@ -89,10 +89,6 @@ void attn_fa_set_timeline_op(const std::optional<at::Tensor>& buf) {
                          : nullptr);
 }
 
-void attn_fa_set_v_strides_op(int64_t lbo, int64_t sbo) {
-  fa_tc_set_v_strides((uint32_t)lbo, (uint32_t)sbo);
-}
-
 void gemm_set_timeline_op(const std::optional<at::Tensor>& buf) {
   if (buf.has_value()) {
     TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong, "timeline: int64 CUDA tensor");
@@ -635,7 +631,6 @@ TORCH_LIBRARY(_b200_C, m) {
         &b200::gemm_set_plan_op);
   m.def("gemm_clear_plans() -> ()", &b200::gemm_clear_plans_op);
   m.def("gemm_set_timeline(Tensor? buf) -> ()", &b200::gemm_set_timeline_op);
-  m.def("attn_fa_set_v_strides(int lbo, int sbo) -> ()", &b200::attn_fa_set_v_strides_op);
   m.def("attn_fa_set_timeline(Tensor? buf) -> ()", &b200::attn_fa_set_timeline_op);
   m.def("gemm_export_plans() -> int[]", &b200::gemm_export_plans_op);
   m.def("gemm_bf16_silu_mul_out(Tensor(a!) out, Tensor a, Tensor w, int cfg=-1) -> ()");

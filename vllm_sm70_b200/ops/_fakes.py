@@ -31,7 +31,6 @@ NO_FAKE = {
     "gemm_bf16_config": "plan query (host)",
     "gemm_set_timeline": "profiling hook",
     "attn_fa_set_timeline": "profiling hook",
-    "attn_fa_set_v_strides": "bring-up hook",
     "build_prefill_meta": "host-side metadata builder (CPU tensors, data-dependent sizes)",
     "ar_rmsnorm": "NVLink collective over peer pointers (eager / CUDA-graph only)",
     "gemm_ar_rmsnorm": "GEMM + NVLink collective over peer pointers (eager / CUDA-graph only)",
