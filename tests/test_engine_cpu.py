@@ -175,3 +175,26 @@ def test_prefix_cache_keys_chain():
     # same tokens in block 2 and 3 but after a different prefix: different keys
     assert ka[0] != kb[0] and ka[2] != kb[2] and ka[3] != kb[3]
     assert block_keys(a, 16, 2) == ka[:2]
+
+
+def test_prefix_cache_host_tier_restores_evicted_blocks():
+    """A tiny device pool forces the shared prefix out; the host tier keeps a
+    copy and a later request restores it (no re-prefill) with identical output."""
+    from vllm_sm70_b200.engine.prefix_cache import HostKVTier, PrefixCache
+
+    g = torch.Generator().manual_seed(9)
+    prefix = torch.randint(0, 512, (48,), generator=g)
+    a = torch.cat([prefix, torch.randint(0, 512, (6,), generator=g)])
+    others = [torch.randint(0, 512, (60,), generator=g) for _ in range(3)]
+    b = torch.cat([prefix, torch.randint(0, 512, (7,), generator=g)])
+    sp = SamplingParams(max_tokens=4, ignore_eos=True)
+    ref = _llm()
+    want_b = ref.generate([b], sp)[0].output_token_ids
+    llm = _llm(enable_prefix_caching=True, num_kv_blocks=7)
+    host = HostKVTier(llm.runner.kv, 32)
+    llm.prefix_cache = PrefixCache(llm.runner.alloc, llm.runner.block_size, host)
+    for p in [a] + others:
+        llm.generate([p], sp)
+    assert host.saved > 0  # the prefix blocks were pushed out to the host tier
+    got_b = llm.generate([b], sp)[0].output_token_ids
+    assert host.restored >= 2 and got_b == want_b

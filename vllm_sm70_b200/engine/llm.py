@@ -33,7 +33,7 @@ from ..parallel import state as pstate
 from ..utils import tracing
 from ..utils.watchdog import StreamWatchdog
 from .model_runner import ModelRunner
-from .prefix_cache import PrefixCache
+from .prefix_cache import HostKVTier, PrefixCache
 from .sampling_params import RequestOutput, SamplingParams
 
 
@@ -150,8 +150,11 @@ class LLM:
         if enable_prefix_caching is None:
             enable_prefix_caching = bool(envs.get("VLLM_B200_PREFIX_CACHING"))
         hybrid = hasattr(self.model, "reset_slots")
-        self.prefix_cache = (PrefixCache(self.runner.alloc, self.runner.block_size)
-                             if enable_prefix_caching and not hybrid and self.spec_k == 0 else None)
+        self.prefix_cache = None
+        if enable_prefix_caching and not hybrid and self.spec_k == 0:
+            host_blocks = int(envs.get("VLLM_B200_PREFIX_HOST_BLOCKS"))
+            host = HostKVTier(self.runner.kv, host_blocks) if host_blocks > 0 else None
+            self.prefix_cache = PrefixCache(self.runner.alloc, self.runner.block_size, host)
         wd = int(envs.get("VLLM_B200_WATCHDOG_S"))
         self.watchdog = (StreamWatchdog(wd) if wd > 0 and self.device.type == "cuda" else None)
 

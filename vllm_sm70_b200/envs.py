@@ -99,6 +99,9 @@ _reg("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS", "int", 1024, "comm",
 _reg("VLLM_B200_PREFIX_CACHING", "optin", False, "runtime",
      "Reuse the KV of full prompt blocks across requests with the same token prefix "
      "(LLM(enable_prefix_caching=...) overrides).")
+_reg("VLLM_B200_PREFIX_HOST_BLOCKS", "int", 0, "runtime",
+     "Prefix caching: KV blocks kept in pinned host memory after eviction from the device "
+     "(0 = no host tier).")
 _reg("VLLM_B200_NVTX", "optin", False, "runtime",
      "Emit NVTX ranges per layer and engine phase for profiler timelines.")
 _reg("VLLM_B200_WATCHDOG_S", "int", 0, "runtime",
