@@ -1,0 +1,46 @@
+"""Tensor parallelism end to end on CPU (two gloo ranks, fp32): the same
+safetensors checkpoint at TP = 2 and TP = 1 gives the same greedy tokens.
+Exercises the host-side TP plumbing -- shard cutting, the replicated
+embedding, the row-parallel linear + all-reduce + RMSNorm fallback path and
+the vocab-parallel greedy merge -- without a GPU."""
+import json
+
+import torch
+
+from . import _mp
+from .test_engine_tp_gpu import HF, _checkpoint, _prompts
+
+KW = dict(max_num_seqs=8, max_model_len=256, block_size=16, max_num_batched_tokens=64,
+          num_kv_blocks=128, dtype=torch.float32, enforce_eager=True)
+
+
+def _generate(path, tp):
+    from vllm_sm70_b200.engine import LLM, SamplingParams
+
+    llm = LLM(str(path), tensor_parallel_size=tp, load_format="safetensors", **KW)
+    outs = llm.generate(_prompts(), SamplingParams(max_tokens=6, ignore_eos=True))
+    toks = [o.output_token_ids for o in outs]
+    llm.shutdown()
+    return toks
+
+
+def _tp_body(rank, world, path, out_file):
+    from pathlib import Path
+
+    from vllm_sm70_b200.parallel import state
+
+    state.init(tp_size=world, backend="gloo", timeout_s=120)
+    toks = _generate(Path(path), world)
+    if rank == 0:
+        Path(out_file).write_text(json.dumps(toks))
+    state.shutdown()
+
+
+def test_tp2_equals_tp1_cpu(tmp_path):
+    _checkpoint(tmp_path)
+    out_file = tmp_path / "tp2.json"
+    _mp.run(_tp_body, 2, args=(str(tmp_path), str(out_file)), timeout=300)
+    tp2 = json.loads(out_file.read_text())
+    tp1 = _generate(tmp_path, 1)
+    assert tp1 == tp2
+    assert HF["num_key_value_heads"] % 2 == 0
