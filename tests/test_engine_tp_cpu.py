@@ -1,10 +1,13 @@
-"""Tensor parallelism end to end on CPU (two gloo ranks, fp32): the same
-safetensors checkpoint at TP = 2 and TP = 1 gives the same greedy tokens.
-Exercises the host-side TP plumbing -- shard cutting, the replicated
+"""Tensor parallelism end to end on CPU (gloo ranks, fp32): the same
+safetensors checkpoint at TP = 2 and TP = 4 gives the same greedy tokens as at
+TP = 1. Exercises the host-side TP plumbing -- shard cutting, the replicated
 embedding, the row-parallel linear + all-reduce + RMSNorm fallback path and
-the vocab-parallel greedy merge -- without a GPU."""
+the vocab-parallel greedy merge -- without a GPU. The checkpoint has two KV
+heads, so TP = 4 also covers KV-head replication (each rank keeps the one KV
+head its query heads read)."""
 import json
 
+import pytest
 import torch
 
 from . import _mp
@@ -36,11 +39,11 @@ def _tp_body(rank, world, path, out_file):
     state.shutdown()
 
 
-def test_tp2_equals_tp1_cpu(tmp_path):
+@pytest.mark.parametrize("tp", [2, 4])
+def test_tp_equals_tp1_cpu(tmp_path, tp):
     _checkpoint(tmp_path)
-    out_file = tmp_path / "tp2.json"
-    _mp.run(_tp_body, 2, args=(str(tmp_path), str(out_file)), timeout=300)
-    tp2 = json.loads(out_file.read_text())
+    out_file = tmp_path / f"tp{tp}.json"
+    _mp.run(_tp_body, tp, args=(str(tmp_path), str(out_file)), timeout=300)
+    got = json.loads(out_file.read_text())
     tp1 = _generate(tmp_path, 1)
-    assert tp1 == tp2
-    assert HF["num_key_value_heads"] % 2 == 0
+    assert tp1 == got
