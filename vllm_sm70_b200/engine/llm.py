@@ -12,6 +12,15 @@ finishes; finished requests release their slot and blocks and waiting ones
 are admitted. Under ``torchrun`` every rank constructs the same ``LLM`` and
 runs the same schedule (decisions depend only on rank-uniform inputs).
 
+Data parallelism (``data_parallel_size = world size``, TP 1 per replica):
+every rank holds a whole replica and ``generate`` serves that rank's own
+prompts. With ``enable_expert_parallel`` an MoE model splits its experts over
+the ranks and exchanges tokens in every MoE block (``parallel/ep.py``); each
+forward is then preceded by a vote over the ranks, and a rank that runs out
+of work keeps serving idle passes until every rank is done, so all ranks take
+the same collective steps. That mode runs eager (the all-to-all split sizes
+are host values).
+
 Reference parity: the reference serves through upstream vLLM ``LLM`` /
 ``vllm serve``; this in-repo runner is the engine the B200
 kernels and fused collectives run under (also exposed to vLLM through the
@@ -85,10 +94,20 @@ class LLM:
                  load_format: str = "dummy", seed: int = 0, enforce_eager: bool = False,
                  dtype=torch.bfloat16, num_kv_blocks: int | None = None,
                  tune_gemm: bool = True, gemm_lut_path: str | None = None,
-                 speculative_k: int = 0, enable_prefix_caching: bool | None = None):
+                 speculative_k: int = 0, enable_prefix_caching: bool | None = None,
+                 data_parallel_size: int = 1, enable_expert_parallel: bool = False):
         self.cfg: ModelConfig = resolve(model)
         ps = pstate.get() if pstate._STATE is not None else None
-        if ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
+        dp = int(data_parallel_size)
+        if dp > 1:
+            if (tensor_parallel_size or 1) != 1:
+                raise NotImplementedError("data parallelism runs TP 1 inside each replica")
+            ep = dp if enable_expert_parallel else 1
+            if ps is None or ps.tp_size != 1 or ps.world_size != dp or ps.ep_size != ep:
+                ps = pstate.init(tp_size=1, ep_size=ep)
+            if ps.world_size != dp:
+                raise ValueError(f"data_parallel_size {dp} != world size {ps.world_size}")
+        elif ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
             ps = pstate.init(tp_size=tensor_parallel_size)
         self.ps = ps
         self.device = ps.device
@@ -114,8 +133,10 @@ class LLM:
                                           gpu_memory_utilization)
         num_sms = (torch.cuda.get_device_properties(self.device).multi_processor_count
                    if self.device.type == "cuda" else 148)
+        self.ep = getattr(self.model, "ep_a2a", None)  # DP attention + all-to-all MoE
         self.runner = ModelRunner(self.model, max_num_seqs, max_model_len, block_size,
-                                  num_kv_blocks, self.device, use_graphs=not enforce_eager,
+                                  num_kv_blocks, self.device,
+                                  use_graphs=not enforce_eager and self.ep is None,
                                   num_sms=num_sms)
         if self.device.type == "cuda" and ps.tp_size > 1:
             from ..parallel import comm, symm
@@ -123,6 +144,8 @@ class LLM:
             comm.set_fused_ar_rmsnorm(symm.FusedArRmsNorm(
                 ps, max(max_num_batched_tokens, max_num_seqs), self.cfg.hidden_size))
         self.spec_k = int(speculative_k)
+        if self.spec_k > 0 and self.ep is not None:
+            raise NotImplementedError("speculative decoding with the all-to-all EP layout")
         if self.spec_k > 0:
             from ..models.mtp import MTPHead
 
@@ -335,6 +358,8 @@ class LLM:
                     runner.alloc.free(r.blocks)
                     free_slots.append(r.slot)
                 running = [r for r in running if not r.done]
+        if self.ep is not None:  # serve the other ranks' MoE traffic until all are done
+            self.model.ep_drain()
         if cuda:
             t_end = ev()
             t_end.record()

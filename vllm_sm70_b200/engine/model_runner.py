@@ -79,6 +79,8 @@ class ModelRunner:
         self.graph_launches: dict[int, int] = {}
         self.split_bufs: dict[int, tuple] = {}
         self.pool = None
+        # DP attention + all-to-all MoE: every forward starts with the ranks' vote
+        self.ep = getattr(model, "ep_a2a", None)
 
     # ------------------------------------------------------------ block tables
     def set_block_row(self, slot: int, blocks: torch.Tensor) -> None:
@@ -114,6 +116,8 @@ class ModelRunner:
         meta = AttnMeta(positions=pos, slot_mapping=slots, block_table=bt, seq_lens=sl,
                         cu_q=self.cu_q[: b + 1], max_q_len=1, decode=True, num_splits=ns,
                         part_o=po, part_ml=pml, state_slots=self.slot_ids[:b])
+        if self.ep is not None:
+            self.ep.step(True)
         h = self.model.forward(self.ids[:b], meta, self.kv)
         if self.sampling:
             nxt = self.model.sample(h, self.temperature[:b], self.seeds[:b], self.out_pos[:b])
@@ -205,6 +209,8 @@ class ModelRunner:
         meta = AttnMeta(positions=h2d(pos), slot_mapping=h2d(slot_map),
                         block_table=h2d(bt_rows), seq_lens=h2d(seq_lens), cu_q=h2d(cu),
                         max_q_len=int(q_len.max()), decode=False, state_slots=state_slots)
+        if self.ep is not None:
+            self.ep.step(True)
         h = self.model.forward(ids_d, meta, self.kv)
         last = [i for i, p in enumerate(pieces) if p[3]]
         if not last:

@@ -2,11 +2,19 @@
 RMSNorm and a routed-expert MLP (softmax top-k, renormalised), block-FP8
 weights when the checkpoint is FP8.
 
-Parallelism: attention is tensor-parallel; experts are expert-parallel over
-the same group (rank r owns experts [r*E/W, (r+1)*E/W)). Every rank holds
-every token after the attention all-reduce, so the MoE block needs no
-all-to-all: each rank runs its local experts for all tokens and the partial
-sums ride the fused all-reduce + residual + RMSNorm that follows.
+Parallelism, two layouts:
+
+* TP (the default at TP > 1): attention is tensor-parallel; experts are
+  expert-parallel over the same group (rank r owns experts
+  [r*E/W, (r+1)*E/W)). Every rank holds every token after the attention
+  all-reduce, so the MoE block needs no all-to-all: each rank runs its local
+  experts for all tokens and the partial sums ride the fused all-reduce +
+  residual + RMSNorm that follows.
+* DP attention + EP (``LLM(data_parallel_size=W, enable_expert_parallel=
+  True)``): every rank holds the whole attention / dense part and serves its
+  own requests; the experts are split over the EP group and the MoE block
+  dispatches tokens to the ranks that own their experts and combines the
+  results (``parallel/ep.py``).
 
 Reference parity: the Flint MoE block (``sm70/vllm_sm70/models/flint_sm70/
 model.py:200-300``) with its fused router and MoE methods; Qwen3-MoE is one
@@ -24,10 +32,18 @@ from .llama import LlamaModel
 class Qwen3MoeModel(LlamaModel):
     def __init__(self, cfg, device, dtype=torch.bfloat16, ps=None):
         super().__init__(cfg, device, dtype, ps)
-        tp = self.ps.tp_size
-        assert cfg.num_experts % tp == 0, "experts must divide across the EP group"
-        self.E_local = cfg.num_experts // tp
-        self.e_base = self.ps.tp_rank * self.E_local
+        ps = self.ps
+        self.ep_a2a = None
+        if ps.tp_size == 1 and ps.ep_size > 1:  # data-parallel attention, all-to-all MoE
+            from ..parallel.ep import EPAllToAll
+
+            self.ep_a2a = EPAllToAll(ps, cfg.num_experts, cfg.top_k)
+            n, r = ps.ep_size, ps.ep_rank
+        else:
+            n, r = ps.tp_size, ps.tp_rank
+        assert cfg.num_experts % n == 0, "experts must divide across the EP group"
+        self.E_local = cfg.num_experts // n
+        self.e_base = r * self.E_local
         self.moe_ws = None
 
     def init_mlp_dummy(self, rnd) -> dict:
@@ -128,7 +144,42 @@ class Qwen3MoeModel(LlamaModel):
             sh = L["shared_down"].forward(L["shared_gate_up"].forward(x))
             gate = torch.sigmoid((x.float() @ L["shared_gate"].float().t()))
             shared = (sh.float() * gate).to(x.dtype)
+        if self.ep_a2a is not None:
+            return self._ep_moe(L, x, w, ids, shared, out)
         return moe_ops.experts_forward(x, w, ids, L["experts"], ws, self.e_base, shared, out)
+
+    # ------------------------------------------------------------------ DP + EP
+    def _ep_moe(self, L, x, w, ids, shared, out):
+        """Dispatch -> local experts -> combine (data-parallel attention). Rows
+        travel in the model dtype on every rank (the idle pass's too), so the
+        byte counts of the exchange agree whatever dtype a layer hands in."""
+        ep = self.ep_a2a
+        dt = x.dtype
+        xr, wr, idr, plan = ep.dispatch(x.to(self.dtype), w, ids)
+        yr = xr.new_empty(xr.shape[0], self.cfg.hidden_size)
+        if xr.shape[0]:
+            ws = self._ws(xr.shape[0]) if xr.is_cuda else None
+            moe_ops.experts_forward(xr, wr, idr, L["experts"], ws, self.e_base, None, yr)
+        res = ep.combine(yr, plan, shared, out)
+        return res if res.dtype == dt else res.to(dt)
+
+    def ep_idle_pass(self) -> None:
+        """A forward without local tokens: every MoE block still serves the
+        rows the other ranks dispatch to this rank's experts."""
+        H, k = self.cfg.hidden_size, self.cfg.top_k
+        x = torch.empty(0, H, device=self.device, dtype=self.dtype)
+        w = torch.empty(0, k, device=self.device, dtype=torch.float32)
+        ids = torch.empty(0, k, device=self.device, dtype=torch.int32)
+        for L in self.layers:
+            if "experts" in L:
+                self._ep_moe(L, x, w, ids, None, None)
+
+    def ep_drain(self) -> None:
+        """Keep serving idle passes until no rank of the group has work."""
+        if self.ep_a2a is None:
+            return
+        while self.ep_a2a.step(False) > 0:
+            self.ep_idle_pass()
 
     def weight_bytes(self) -> int:
         n = self.embed.numel() * 2 + (0 if self.cfg.tie_embeddings else self.lm_head.numel() * 2)
