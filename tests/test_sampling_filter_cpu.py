@@ -1,0 +1,76 @@
+"""Top-k / top-p sampling on CPU: the candidate sampler's oracle follows the
+kernel's rules (ordering, top-k cut, nucleus prefix, greedy at T <= 0, a
+distribution proportional to softmax over the kept set), and the engine
+routes requests with top-k / top-p through it: top_k = 1 and a vanishing
+top_p reduce to greedy decoding, a fixed seed is reproducible, and greedy
+requests batched with filtered ones are unchanged."""
+import torch
+
+from vllm_sm70_b200.engine import SamplingParams
+from vllm_sm70_b200.ops import sampling
+
+from .test_engine_cpu import _llm
+
+
+def _cands(rows, C):
+    v = torch.linspace(3, -3, C).expand(rows, C).contiguous()
+    i = torch.arange(C, dtype=torch.int32).expand(rows, C).contiguous()
+    perm = torch.randperm(C, generator=torch.Generator().manual_seed(0))
+    return v[:, perm].contiguous(), i[:, perm].contiguous()   # unsorted input
+
+
+def test_oracle_rules():
+    rows, C = 200, 16
+    v, i = _cands(rows, C)
+    t = torch.ones(rows)
+    seeds = torch.arange(rows, dtype=torch.int64)
+    k = torch.full((rows,), 3, dtype=torch.int32)
+    p = torch.ones(rows)
+    out = sampling.sample_candidates(v, i, t, k, p, seeds, 0)
+    assert int(out.max()) < 3 and int(out.min()) >= 0 and len(set(out.tolist())) == 3
+    k.fill_(-1)
+    p.fill_(0.5)
+    out = sampling.sample_candidates(v, i, t, k, p, seeds, 1)
+    probs = torch.softmax(torch.linspace(3, -3, C), 0)
+    keep = int((torch.cumsum(probs, 0) < 0.5).sum()) + 1
+    assert int(out.max()) < keep
+    t.fill_(0.0)
+    assert sampling.sample_candidates(v, i, t, k, p, seeds, 2).tolist() == [0] * rows
+    # absent candidates (id < 0) are never picked; none at all -> -1
+    i2 = i.clone()
+    i2[:, :] = -1
+    assert sampling.sample_candidates(v, i2, torch.ones(rows), k, torch.ones(rows), seeds,
+                                      3).tolist() == [-1] * rows
+
+
+def test_oracle_distribution():
+    rows, C = 6000, 4
+    v = torch.tensor([1.0, 0.5, 0.0, -4.0]).expand(rows, C).contiguous()
+    i = torch.arange(C, dtype=torch.int32).expand(rows, C).contiguous()
+    out = sampling.sample_candidates(v, i, torch.ones(rows), torch.full((rows,), 3, dtype=torch.int32),
+                                     torch.ones(rows), torch.arange(rows, dtype=torch.int64), 7)
+    freq = torch.bincount(out.to(torch.int64), minlength=C).float() / rows
+    want = torch.softmax(torch.tensor([1.0, 0.5, 0.0]), 0)
+    assert freq[3] == 0
+    assert torch.allclose(freq[:3], want, atol=0.03), (freq, want)
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(4)
+    return [torch.randint(0, 512, (n,), generator=g) for n in (7, 21, 12)]
+
+
+def test_engine_filtered_requests():
+    llm = _llm()
+    greedy = [o.output_token_ids for o in llm.generate(_prompts(), SamplingParams(max_tokens=5))]
+    k1 = llm.generate(_prompts(), SamplingParams(max_tokens=5, temperature=1.0, top_k=1))
+    assert [o.output_token_ids for o in k1] == greedy
+    p0 = llm.generate(_prompts(), SamplingParams(max_tokens=5, temperature=1.0, top_p=1e-9, seed=2))
+    assert [o.output_token_ids for o in p0] == greedy
+    sp = SamplingParams(max_tokens=5, temperature=1.5, top_k=20, top_p=0.9, seed=11)
+    a = [o.output_token_ids for o in llm.generate(_prompts(), sp)]
+    b = [o.output_token_ids for o in llm.generate(_prompts(), sp)]
+    assert a == b and all(len(t) == 5 for t in a)
+    mixed = llm.generate(_prompts(), [SamplingParams(max_tokens=5), sp, SamplingParams(max_tokens=5)])
+    assert mixed[0].output_token_ids == greedy[0] and mixed[2].output_token_ids == greedy[2]
+    assert not llm.runner.filtering  # reset after the call

@@ -221,11 +221,18 @@ class LLM:
             prompts = [torch.as_tensor(p, dtype=torch.int64) for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
-        for p in params:
-            if p.top_k not in (-1, 0) or p.top_p < 1.0:
-                raise NotImplementedError("top-k / top-p: use ops.sampling.topk_candidates + "
-                                          "sample_candidates; the engine samples with temperature")
+        filtering = any(p.top_k not in (-1, 0) or p.top_p < 1.0 for p in params)
+        if filtering and self.spec_k:
+            raise NotImplementedError("top-k / top-p with speculative decoding")
         reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
+        runner = self.runner
+        runner.filtering = filtering
+        try:
+            return self._generate(reqs)
+        finally:
+            runner.filtering = False
+
+    def _generate(self, reqs: list[_Req]) -> list[RequestOutput]:
         runner = self.runner
         bs = runner.block_size
         waiting = deque(reqs)
@@ -269,7 +276,7 @@ class LLM:
                 runner.set_block_row(r.slot, r.blocks)
                 seed = r.params.seed if r.params.seed is not None else 0x9E3779B97F4A7C15 ^ r.rid
                 runner.set_sampling(r.slot, 0.0 if r.params.greedy else r.params.temperature,
-                                    seed & 0x7FFFFFFFFFFFFFFF)
+                                    seed & 0x7FFFFFFFFFFFFFFF, r.params.top_k, r.params.top_p)
                 admitted.append(r)
             if not admitted and not running:
                 raise RuntimeError("cannot admit any request: KV cache too small")

@@ -66,9 +66,14 @@ class ModelRunner:
         self.slot_ids = torch.arange(B, dtype=torch.int32, device=dev)
         self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
         self.seeds = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.top_k = torch.full((B,), -1, dtype=torch.int32, device=dev)
+        self.top_p = torch.ones(B, dtype=torch.float32, device=dev)
         # Decode graphs always sample through the temperature path: rows with
         # T <= 0 reduce to the exact greedy argmax.
         self.sampling = True
+        # Top-k / top-p requests in flight: candidate sampling, eager decode
+        # (the captured graphs hold the temperature path).
+        self.filtering = False
         if hasattr(model, "allocate_states"):
             model.allocate_states(B)
         if hasattr(model, "reserve_workspace"):
@@ -119,7 +124,11 @@ class ModelRunner:
         if self.ep is not None:
             self.ep.step(True)
         h = self.model.forward(self.ids[:b], meta, self.kv)
-        if self.sampling:
+        if self.filtering:
+            nxt = self.model.sample_filtered(h, self.temperature[:b], self.top_k[:b],
+                                             self.top_p[:b], self._step_seeds(self.seeds[:b],
+                                                                              self.out_pos[:b]))
+        elif self.sampling:
             nxt = self.model.sample(h, self.temperature[:b], self.seeds[:b], self.out_pos[:b])
         else:
             nxt = self.model.greedy(h)
@@ -128,6 +137,12 @@ class ModelRunner:
         act = self.active[:b]
         self.out_pos[:b] += act
         self.seq_lens[:b] += act
+
+    @staticmethod
+    def _step_seeds(seeds: torch.Tensor, out_pos: torch.Tensor) -> torch.Tensor:
+        """Per-row sampling key of the token at ``out_pos`` (fresh noise every
+        step without a host-side counter)."""
+        return seeds ^ (out_pos * 0x100000001)
 
     def bucket(self, n_rows: int) -> int:
         for s in self.capture_sizes:
@@ -165,7 +180,7 @@ class ModelRunner:
 
     def decode(self, n_rows: int, steps: int) -> None:
         b = self.bucket(n_rows)
-        g = self.graphs.get(b)
+        g = None if self.filtering else self.graphs.get(b)
         for _ in range(steps):
             if g is not None:
                 g.replay()
@@ -179,9 +194,12 @@ class ModelRunner:
         self.pool = None
 
     # ------------------------------------------------------------ prefill
-    def set_sampling(self, slot: int, temperature: float, seed: int) -> None:
+    def set_sampling(self, slot: int, temperature: float, seed: int, top_k: int = -1,
+                     top_p: float = 1.0) -> None:
         self.temperature[slot] = float(temperature)
         self.seeds[slot] = int(seed)
+        self.top_k[slot] = int(top_k) if top_k > 0 else -1
+        self.top_p[slot] = float(top_p)
 
     def prefill(self, pieces: list[tuple[int, torch.Tensor, int, bool, int]]) -> None:
         """``pieces``: (slot, token ids [n] int64 CPU, ctx_start, is_last, total_len)."""
@@ -218,7 +236,12 @@ class ModelRunner:
         rows = h2d(torch.tensor([int(cu[i + 1]) - 1 for i in last], dtype=torch.int64))
         h_last = h.index_select(0, rows)
         sidx = h2d(torch.tensor([pieces[i][0] for i in last], dtype=torch.int64))
-        if self.sampling:
+        if self.filtering:  # first output token: out_pos 0
+            nxt = self.model.sample_filtered(h_last, self.temperature.index_select(0, sidx),
+                                             self.top_k.index_select(0, sidx),
+                                             self.top_p.index_select(0, sidx),
+                                             self.seeds.index_select(0, sidx))
+        elif self.sampling:
             nxt = self.model.sample(h_last, self.temperature.index_select(0, sidx),
                                     self.seeds.index_select(0, sidx), None, offset=0)
         else:

@@ -14,7 +14,9 @@ messages (through the checkpoint's chat template) are accepted and the
 (``--reasoning-parser glm47_b200``). Token-id prompts work without one.
 
 Scope: n = 1, no streaming, no log-probabilities (requests asking for them
-get HTTP 400); sampling is greedy or temperature (Gumbel-max, seeded).
+get HTTP 400); sampling is greedy, temperature (Gumbel-max, seeded) or
+temperature with top-k / top-p (over the top-64 candidates of each vocab
+shard).
 
 Reference parity: the reference is served through ``vllm serve`` with its
 plugin; this is the same OpenAI surface for the standalone runtime.
@@ -115,8 +117,11 @@ def _params(body: dict, tokenizer) -> SamplingParams:
     eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
     if eos is not None and not ignore_eos:
         stop_ids.append(int(eos))
+    top_k = body.get("top_k")
     return SamplingParams(max_tokens=int(body.get("max_tokens") or 16),
                           temperature=float(body.get("temperature", 1.0)),
+                          top_k=int(top_k) if top_k is not None else -1,
+                          top_p=float(body.get("top_p", 1.0)),
                           seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids)
 
 

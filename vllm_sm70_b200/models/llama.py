@@ -46,6 +46,9 @@ class _QuantGateUp:
         return self.lin.weight_bytes()
 
 
+CANDIDATES = 64  # per-shard candidate set of top-k / top-p sampling (kernel limit)
+
+
 def _shard(n: int, tp: int, rank: int) -> slice:
     assert n % tp == 0, (n, tp)
     k = n // tp
@@ -371,6 +374,23 @@ class LlamaModel:
         if self.ps.tp_size == 1:
             return ids
         return comm.greedy_merge(vals, ids)
+
+    def sample_filtered(self, hidden: torch.Tensor, temperature: torch.Tensor,
+                        top_k: torch.Tensor, top_p: torch.Tensor,
+                        seeds: torch.Tensor) -> torch.Tensor:
+        """Per-row temperature + top-k + top-p sampling: the local top-64
+        candidates of each vocab shard, all-gathered over TP, then one
+        sampling kernel over the merged set (top-k is bounded by the
+        candidate count and top-p is taken over the candidates). ``seeds``
+        must already differ per step."""
+        logits = ops.gemm(hidden, self.lm_head)
+        nvalid = max(1, min(self.vocab_local, self.cfg.vocab_size - self.vocab_start))
+        C = min(CANDIDATES, nvalid)
+        v, i = ops.sampling.topk_candidates(logits[:, :nvalid], C, self.vocab_start)
+        if self.ps.tp_size > 1:
+            v = pstate.tp_all_gather(v, dim=1)
+            i = pstate.tp_all_gather(i, dim=1)
+        return ops.sampling.sample_candidates(v, i, temperature, top_k, top_p, seeds, 0)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         lg = ops.gemm(hidden, self.lm_head)

@@ -107,12 +107,49 @@ def sample_candidates(cand_v: torch.Tensor, cand_i: torch.Tensor, temperature: t
                       top_k: torch.Tensor, top_p: torch.Tensor, seeds: torch.Tensor,
                       offset: int) -> torch.Tensor:
     """Temperature / top-k / top-p sampling over merged candidate sets."""
+    if not cand_v.is_cuda:
+        return sample_candidates_ref(cand_v, cand_i, temperature, top_k, top_p, seeds, offset)
     out = torch.empty(cand_v.shape[0], dtype=torch.int32, device=cand_v.device)
     _ext.require()
     torch.ops._b200_C.sample_candidates(out, cand_v.contiguous(), cand_i.contiguous(),
                                         temperature, top_k, top_p, seeds, offset)
     launch_count.add(1)
     return out
+
+
+def sample_candidates_ref(cand_v, cand_i, temperature, top_k, top_p, seeds, offset):
+    """CPU oracle of :func:`sample_candidates` with the kernel's rules:
+    candidates with id < 0 are absent; order by (value desc, id asc);
+    T <= 0 -> the first candidate; keep the first ``top_k`` (> 0), then the
+    shortest prefix whose softmax(v / T) mass reaches ``top_p``; pick
+    argmax p_j / E_j with E_j ~ Exp(1) (torch RNG keyed by (seed, offset)
+    instead of Philox)."""
+    rows = cand_v.shape[0]
+    out = torch.empty(rows, dtype=torch.int32)
+    for r in range(rows):
+        v = cand_v[r].float()
+        ids = cand_i[r].to(torch.int64)
+        ok = ids >= 0
+        v, ids = v[ok], ids[ok]
+        if ids.numel() == 0:
+            out[r] = -1
+            continue
+        order = sorted(range(ids.numel()), key=lambda j: (-float(v[j]), int(ids[j])))
+        v, ids = v[order], ids[order]
+        t = float(temperature[r])
+        if t <= 0:
+            out[r] = int(ids[0])
+            continue
+        k = int(top_k[r])
+        kk = min(k, ids.numel()) if k > 0 else ids.numel()
+        p = torch.exp((v[:kk] - v[0]) / t)
+        csum = torch.cumsum(p, 0)
+        hit = (csum >= float(top_p[r]) * float(csum[-1])).nonzero()
+        keep = int(hit[0]) + 1 if hit.numel() else kk
+        g = torch.Generator().manual_seed((int(seeds[r]) * 1000003 + int(offset)) & 0x7FFFFFFFFFFFFFFF)
+        e = torch.empty(keep).exponential_(generator=g)
+        out[r] = int(ids[int(torch.argmax(p[:keep] / e))])
+    return out.to(cand_v.device)
 
 
 def rejection_sample(target_logits: torch.Tensor, draft_logits: torch.Tensor,
