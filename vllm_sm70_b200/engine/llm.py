@@ -211,6 +211,53 @@ class LLM:
         return int(max(2, min(need, budget // per_block)))
 
     # ------------------------------------------------------------------ API
+    def score(self, prompt_token_ids, logits_rows: int = 1024) -> list[torch.Tensor]:
+        """Teacher-forced log-probabilities (vLLM's ``prompt_logprobs``): for
+        each prompt ``x`` of length L, ``lp[i] = log p(x[i+1] | x[:i+1])``
+        for i < L - 1 (fp32, on the host). The prompt is prefilled in chunks
+        of ``max_num_batched_tokens`` into a scratch slot; the LM head and
+        log-softmax run on at most ``logits_rows`` rows at a time (the full
+        vocabulary row of every token is not held at once). Call between
+        ``generate`` calls (it uses batch slot 0)."""
+        if isinstance(prompt_token_ids, torch.Tensor):
+            prompts = [row for row in prompt_token_ids.to(torch.int64)]
+        else:
+            prompts = [torch.as_tensor(p, dtype=torch.int64) for p in prompt_token_ids]
+        runner = self.runner
+        slot, out = 0, []
+        for p in prompts:
+            L = p.numel()
+            if L > runner.max_model_len:
+                raise ValueError(f"prompt of {L} tokens > max_model_len")
+            nblk = math.ceil(L / runner.block_size)
+            if runner.alloc.num_free() < nblk and self.prefix_cache is not None:
+                self.prefix_cache.evict(nblk)
+            if runner.alloc.num_free() < nblk:
+                raise RuntimeError("KV cache too small to score the prompt")
+            blocks = runner.alloc.allocate(nblk)
+            runner.set_block_row(slot, blocks)
+            lp = torch.empty(max(L - 1, 0), dtype=torch.float32)
+            try:
+                pos = 0
+                while pos < L:
+                    n = min(self.max_num_batched_tokens, L - pos)
+                    h = runner.prefill_hidden([(slot, p[pos:pos + n], pos, False, L)])
+                    m = min(n, L - 1 - pos)  # rows that predict a prompt token
+                    for a in range(0, m, logits_rows):
+                        e = min(m, a + logits_rows)
+                        lg = self.model.logits(h[a:e]).float()
+                        tgt = p[pos + a + 1:pos + e + 1].to(lg.device)
+                        got = lg.gather(1, tgt[:, None]).squeeze(1) - torch.logsumexp(lg, 1)
+                        lp[pos + a:pos + e] = got.cpu()
+                    pos += n
+            finally:
+                runner.alloc.free(blocks)
+                runner.deactivate([slot])
+            out.append(lp)
+        if self.ep is not None:
+            self.model.ep_drain()
+        return out
+
     def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
                  collect_stats: bool = True) -> list[RequestOutput]:
         if sampling_params is None:

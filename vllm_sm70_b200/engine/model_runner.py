@@ -203,6 +203,15 @@ class ModelRunner:
 
     def prefill(self, pieces: list[tuple[int, torch.Tensor, int, bool, int]]) -> None:
         """``pieces``: (slot, token ids [n] int64 CPU, ctx_start, is_last, total_len)."""
+        h, cu, h2d = self._prefill_forward(pieces)
+        self._sample_last(pieces, h, cu, h2d)
+
+    def prefill_hidden(self, pieces) -> torch.Tensor:
+        """The forward of :meth:`prefill` without sampling: the final hidden
+        states of every token of the chunk (``[sum n, H]``)."""
+        return self._prefill_forward(pieces)[0]
+
+    def _prefill_forward(self, pieces):
         dev = self.device
         S = len(pieces)
         toks = torch.cat([p[1] for p in pieces])
@@ -229,7 +238,10 @@ class ModelRunner:
                         max_q_len=int(q_len.max()), decode=False, state_slots=state_slots)
         if self.ep is not None:
             self.ep.step(True)
-        h = self.model.forward(ids_d, meta, self.kv)
+        return self.model.forward(ids_d, meta, self.kv), cu, h2d
+
+    def _sample_last(self, pieces, h, cu, h2d) -> None:
+        """First output token of every piece that completes its prompt."""
         last = [i for i, p in enumerate(pieces) if p[3]]
         if not last:
             return
