@@ -1,7 +1,9 @@
 """OpenAI-compatible server over the engine (CPU engine, tiny model, a fake
 tokenizer): completions from token ids and text, batching of concurrent
-requests, stop tokens / strings, chat with the reasoning split, and the
-400s for what is not served."""
+requests, stop tokens / strings, chat with the reasoning split, streamed
+(server-sent events) completions and chat equal to the unstreamed replies,
+and the 400s for what is not served."""
+import json
 import threading
 
 import pytest
@@ -94,7 +96,7 @@ def test_stop_string_and_unsupported(client):
     r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8, "temperature": 0.0,
                                               "ignore_eos": True, "stop": ["\\u0000"]})
     assert r.status_code == 200
-    for bad in ({"n": 2}, {"stream": True}, {"logprobs": 1}):
+    for bad in ({"n": 2}, {"logprobs": 1}, {"stream": True, "prompt": ["a", "b"]}):
         body = {"prompt": [1, 2, 3], "max_tokens": 2, **bad}
         assert client.post("/v1/completions", json=body).status_code == 400
 
@@ -117,3 +119,43 @@ def test_stop_token_truncates_engine_output():
     assert _truncate_at_stop([1, 2, 3], sp) == [1, 2, 3]
     sp2 = SamplingParams(max_tokens=8, stop_token_ids=[7], ignore_eos=True)
     assert _truncate_at_stop([1, 7, 3], sp2) == [1, 7, 3]
+
+
+def _events(client, url, body):
+    """The JSON payloads of a server-sent event stream (``[DONE]`` last)."""
+    out = []
+    with client.stream("POST", url, json=body) as r:
+        assert r.status_code == 200
+        assert r.headers["content-type"].startswith("text/event-stream")
+        for line in r.iter_lines():
+            if line.startswith("data: "):
+                data = line[len("data: "):]
+                out.append(data if data == "[DONE]" else json.loads(data))
+    assert out and out[-1] == "[DONE]"
+    return out[:-1]
+
+
+def test_stream_completion_equals_unstreamed(client):
+    body = {"prompt": "streaming!", "max_tokens": 19, "temperature": 0.0, "ignore_eos": True}
+    whole = client.post("/v1/completions", json=body).json()["choices"][0]
+    ev = _events(client, "/v1/completions", {**body, "stream": True})
+    assert len(ev) >= 3  # several bursts of at most STREAM_INTERVAL tokens
+    ids = [t for e in ev for t in e["choices"][0]["token_ids"]]
+    text = "".join(e["choices"][0]["text"] for e in ev)
+    assert ids == whole["token_ids"] and text == whole["text"]
+    assert [e["choices"][0]["finish_reason"] for e in ev][-1] == "length"
+    assert all(e["choices"][0]["finish_reason"] is None for e in ev[:-1])
+
+
+def test_stream_chat_equals_unstreamed(client):
+    body = {"messages": [{"role": "user", "content": "hey"}], "max_tokens": 12,
+            "temperature": 0.0, "ignore_eos": True}
+    whole = client.post("/v1/chat/completions", json=body).json()["choices"][0]["message"]
+    ev = _events(client, "/v1/chat/completions", {**body, "stream": True})
+    assert ev[0]["choices"][0]["delta"] == {"role": "assistant"}
+    deltas = [e["choices"][0]["delta"] for e in ev[1:]]
+    reasoning = "".join(d.get("reasoning_content", "") for d in deltas)
+    content = "".join(d.get("content", "") for d in deltas)
+    assert (reasoning.rstrip() or None) == whole["reasoning_content"]
+    assert content == whole["content"]
+    assert ev[-1]["choices"][0]["finish_reason"] == "length"

@@ -59,6 +59,8 @@ class _Req:
     out: list = field(default_factory=list)
     t_first: float | None = None
     t_last: float | None = None
+    streamed: int = 0              # output tokens already handed to the stream callback
+    stream_stopped: bool = False   # a stop token was streamed: nothing more is
 
 
 @dataclass
@@ -259,7 +261,16 @@ class LLM:
         return out
 
     def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
-                 collect_stats: bool = True) -> list[RequestOutput]:
+                 collect_stats: bool = True, on_tokens=None,
+                 stream_interval: int = 0) -> list[RequestOutput]:
+        """Serve the prompts to completion; returns one output per prompt.
+
+        Streaming: ``on_tokens(request_index, new_token_ids, finished)`` is
+        called with each request's new tokens after its prefill and after
+        every decode burst (at most ``stream_interval`` steps per burst when
+        > 0), and once with ``finished=True``; tokens after a stop token are
+        not streamed. Under TP every rank must pass the same
+        ``stream_interval`` (it sets the burst boundaries)."""
         if sampling_params is None:
             sampling_params = SamplingParams()
         if isinstance(prompt_token_ids, torch.Tensor):
@@ -275,12 +286,34 @@ class LLM:
         runner = self.runner
         runner.filtering = filtering
         try:
-            return self._generate(reqs)
+            return self._generate(reqs, on_tokens, int(stream_interval))
         finally:
             runner.filtering = False
 
-    def _generate(self, reqs: list[_Req]) -> list[RequestOutput]:
+    def _generate(self, reqs: list[_Req], on_tokens=None,
+                  stream_interval: int = 0) -> list[RequestOutput]:
         runner = self.runner
+
+        def emit(rs, rows_h=None, final=False):
+            """Hand each request's not-yet-streamed tokens to ``on_tokens``."""
+            if on_tokens is None or not rs:
+                return
+            if rows_h is None:
+                idx = torch.tensor([r.slot for r in rs], device=self.device)
+                rows_h = runner.out_tokens.index_select(0, idx).cpu()
+            for r, row in zip(rs, rows_h):
+                upto = min(r.generated, r.params.max_tokens)
+                new = [] if r.stream_stopped else row[r.streamed:upto].tolist()
+                if new and not r.params.ignore_eos and r.params.stop_token_ids:
+                    stops = set(r.params.stop_token_ids)
+                    for j, t in enumerate(new):
+                        if t in stops:
+                            new, r.stream_stopped = new[: j + 1], True
+                            break
+                r.streamed = upto
+                if new or final:
+                    on_tokens(r.rid, new, final)
+
         bs = runner.block_size
         waiting = deque(reqs)
         running: list[_Req] = []
@@ -365,6 +398,7 @@ class LLM:
                     e = ev()
                     e.record()
                     pending_first.append((e, finishing))
+                emit([r for r in finishing if r.params.max_tokens > 1])
                 running.extend(finishing)
             # ---- decode until the next request finishes
             live = [r for r in running if not r.done]
@@ -384,6 +418,8 @@ class LLM:
                     decode_events.append((e, finished_now, 1))
             elif not finished_now:
                 steps = min(r.params.max_tokens - r.generated for r in live)
+                if stream_interval > 0:
+                    steps = min(steps, stream_interval)
                 n_rows = max(r.slot for r in live) + 1
                 if self.watchdog is not None:
                     self.watchdog.check()
@@ -400,12 +436,14 @@ class LLM:
                     decode_events.append((e, finished_now, steps))
                     if self.watchdog is not None:
                         self.watchdog.arm(e, f"decode burst of {steps} steps")
+            emit([r for r in live if r.generated < r.params.max_tokens])
             # ---- retire
             if finished_now:
                 slots = [r.slot for r in finished_now]
                 runner.deactivate(slots)
                 outs = runner.out_tokens[torch.tensor(slots, device=self.device)]
                 outs_h = outs.to("cpu", non_blocking=False)
+                emit(finished_now, outs_h, final=True)
                 for r, row in zip(finished_now, outs_h):
                     r.out = _truncate_at_stop(row[: r.params.max_tokens].tolist(), r.params)
                     r.done = True

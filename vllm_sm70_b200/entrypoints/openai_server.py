@@ -13,10 +13,13 @@ messages (through the checkpoint's chat template) are accepted and the
 ``<think>`` / ``<tool_call>`` reasoning split is applied to chat replies
 (``--reasoning-parser glm47_b200``). Token-id prompts work without one.
 
-Scope: n = 1, no streaming, no log-probabilities (requests asking for them
-get HTTP 400); sampling is greedy, temperature (Gumbel-max, seeded) or
-temperature with top-k / top-p (over the top-64 candidates of each vocab
-shard).
+Streaming (``"stream": true``): server-sent events, one chunk per decode
+burst of at most ``STREAM_INTERVAL`` steps (text deltas from the cumulative
+decode, so multi-token characters are not split), then ``data: [DONE]``.
+
+Scope: n = 1, no log-probabilities (requests asking for them get HTTP 400);
+sampling is greedy, temperature (Gumbel-max, seeded) or temperature with
+top-k / top-p (over the top-64 candidates of each vocab shard).
 
 Reference parity: the reference is served through ``vllm serve`` with its
 plugin; this is the same OpenAI surface for the standalone runtime.
@@ -26,12 +29,15 @@ from __future__ import annotations
 import argparse
 import asyncio
 import concurrent.futures
+import json
 import queue
 import threading
 import time
 import uuid
 
 from ..engine.sampling_params import SamplingParams
+
+STREAM_INTERVAL = 8  # decode steps per streamed chunk
 
 
 class Batcher:
@@ -48,9 +54,13 @@ class Batcher:
         self.thread = threading.Thread(target=self._run, name="b200-batcher", daemon=True)
         self.thread.start()
 
-    def submit(self, prompt_ids: list[int], params: SamplingParams) -> concurrent.futures.Future:
+    def submit(self, prompt_ids: list[int], params: SamplingParams,
+               stream=None) -> concurrent.futures.Future:
+        """Queue one request. ``stream(new_ids, finished)`` (optional) is called
+        from the worker thread as tokens are produced; ``new_ids`` is None if
+        the batch failed."""
         fut: concurrent.futures.Future = concurrent.futures.Future()
-        self.q.put((prompt_ids, params, fut))
+        self.q.put((prompt_ids, params, fut, stream))
         return fut
 
     def _run(self) -> None:
@@ -67,21 +77,30 @@ class Batcher:
                     items.append(self.q.get_nowait())
                 except queue.Empty:
                     break
+            streams = [it[3] for it in items]
+            interval = STREAM_INTERVAL if any(streams) else 0
             try:
-                batch = ([p for p, _, _ in items], [sp for _, sp, _ in items])
+                batch = ([it[0] for it in items], [it[1] for it in items], interval)
                 if self.group is not None:  # every rank runs the same generate call
                     import torch.distributed as dist
 
                     dist.broadcast_object_list([batch], src=0, group=self.group)
+
+                def on_tokens(i, ids, fin):
+                    if streams[i] is not None:
+                        streams[i](ids, fin)
                 outs = self.llm.generate([torch.tensor(p, dtype=torch.int64) for p in batch[0]],
-                                         batch[1])
+                                         batch[1], on_tokens=on_tokens if interval else None,
+                                         stream_interval=interval)
                 self.batches += 1
-                for (_, _, fut), o in zip(items, outs):
-                    fut.set_result(o)
+                for it, o in zip(items, outs):
+                    it[2].set_result(o)
             except Exception as e:  # noqa: BLE001 - reported to every waiting request
-                for _, _, fut in items:
+                for _, _, fut, cb in items:
                     if not fut.done():
                         fut.set_exception(e)
+                    if cb is not None:
+                        cb(None, True)
 
     def close(self) -> None:
         self._stop = True
@@ -103,15 +122,16 @@ def follower_loop(llm, group) -> None:
         dist.broadcast_object_list(obj, src=0, group=group)
         if obj[0] is None:
             return
-        prompts, params = obj[0]
-        llm.generate([torch.tensor(p, dtype=torch.int64) for p in prompts], params)
+        prompts, params, interval = obj[0]
+        llm.generate([torch.tensor(p, dtype=torch.int64) for p in prompts], params,
+                     stream_interval=interval)
 
 
 def _params(body: dict, tokenizer) -> SamplingParams:
     if int(body.get("n", 1)) != 1:
         raise ValueError("only n = 1 is served")
-    if body.get("logprobs") or body.get("stream"):
-        raise ValueError("streaming and log-probabilities are not served")
+    if body.get("logprobs"):
+        raise ValueError("log-probabilities are not served")
     stop_ids = list(body.get("stop_token_ids") or [])
     ignore_eos = bool(body.get("ignore_eos", False))
     eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
@@ -133,9 +153,32 @@ def _apply_stop_strings(text: str, stop) -> tuple[str, bool]:
     return (text[:cut], True) if cut >= 0 else (text, False)
 
 
+class _TextStream:
+    """Token ids -> text deltas by decoding the cumulative ids (a trailing
+    incomplete character is held back until the next piece completes it)."""
+
+    def __init__(self, decode):
+        self.decode = decode
+        self.ids: list[int] = []
+        self.sent = ""
+
+    def push(self, ids: list[int], final: bool) -> str:
+        self.ids += ids
+        full = self.decode(self.ids)
+        if (not final and full.endswith("\ufffd")) or not full.startswith(self.sent):
+            return ""
+        delta, self.sent = full[len(self.sent):], full
+        return delta
+
+
+def _sse(obj) -> str:
+    return f"data: {json.dumps(obj)}\n\n"
+
+
 def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: str | None = None,
               max_batch: int = 256, group=None):
     from fastapi import FastAPI, HTTPException
+    from fastapi.responses import StreamingResponse
 
     from ..integration import reasoning as rp
 
@@ -168,6 +211,47 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         fut = batcher.submit(prompt_ids, sp)
         return await asyncio.wrap_future(fut)
 
+    def start_stream(prompt_ids, sp) -> asyncio.Queue:
+        """Submit a streamed request; its (new ids, finished) pieces arrive on
+        the returned queue."""
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        batcher.submit(prompt_ids, sp,
+                       lambda ids, fin: loop.call_soon_threadsafe(q.put_nowait, (ids, fin)))
+        return q
+
+    def stream_completion(prompt_ids, sp, stop):
+        q = start_stream(prompt_ids, sp)
+        rid, made = f"cmpl-{uuid.uuid4().hex}", int(time.time())
+
+        async def events():
+            ts = _TextStream(decode) if tokenizer is not None else None
+            hit = stopped = False
+            while True:
+                ids, fin = await q.get()
+                if ids is None:
+                    yield _sse({"error": {"message": "generation failed"}})
+                    break
+                if ids and ids[-1] in sp.stop_token_ids:
+                    stopped = True
+                text = None
+                if ts is not None:
+                    text = "" if hit else ts.push(ids, fin)
+                    if not hit and stop:
+                        cut, hit = _apply_stop_strings(ts.sent, stop)
+                        if hit:  # drop what follows the stop string
+                            text = text[: max(0, len(text) - (len(ts.sent) - len(cut)))]
+                choice = {"index": 0, "text": text, "token_ids": ids,
+                          "finish_reason": ("stop" if (stopped or hit) else "length") if fin
+                          else None}
+                yield _sse({"id": rid, "object": "text_completion", "created": made,
+                            "model": model_name, "choices": [choice]})
+                if fin:
+                    break
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(events(), media_type="text/event-stream")
+
     @app.get("/health")
     async def health():
         return {"status": "ok"}
@@ -187,6 +271,10 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         batch = (prompts if isinstance(prompts, list) and prompts
                  and not all(isinstance(t, int) for t in prompts) else [prompts])
         ids = [encode(p) for p in batch]
+        if body.get("stream"):
+            if len(ids) != 1:
+                raise HTTPException(400, "streaming serves one prompt per request")
+            return stream_completion(ids[0], sp, body.get("stop"))
         outs = await asyncio.gather(*[run(p, sp) for p in ids])
         choices, n_out = [], 0
         for i, o in enumerate(outs):
@@ -204,6 +292,55 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 "usage": {"prompt_tokens": sum(len(p) for p in ids), "completion_tokens": n_out,
                           "total_tokens": sum(len(p) for p in ids) + n_out}}
 
+    def stream_chat(prompt_ids, sp, kwargs, stop):
+        q = start_stream(prompt_ids, sp)
+        rid, made = f"chatcmpl-{uuid.uuid4().hex}", int(time.time())
+        splitter = None
+        if reasoning_parser == "glm47_b200":
+            enabled, inside = rp.thinking_policy(getattr(tokenizer, "chat_template", None), kwargs)
+            splitter = rp.ThinkSplitter(inside) if enabled else None
+        stops = set(sp.stop_token_ids)
+        # special tokens are kept (the reasoning markers); stop tokens are not text
+        ts = _TextStream(lambda ids: tokenizer.decode([t for t in ids if t not in stops],
+                                                      skip_special_tokens=False))
+
+        def chunk(delta, finish=None):
+            return _sse({"id": rid, "object": "chat.completion.chunk", "created": made,
+                         "model": model_name,
+                         "choices": [{"index": 0, "delta": delta, "finish_reason": finish}]})
+
+        async def events():
+            yield chunk({"role": "assistant"})
+            stopped = hit = False
+            content_sent = ""
+            while True:
+                ids, fin = await q.get()
+                if ids is None:
+                    yield _sse({"error": {"message": "generation failed"}})
+                    break
+                if ids and ids[-1] in stops:
+                    stopped = True
+                text = ts.push(ids, fin)
+                delta = {}
+                if text and not hit:
+                    r, c = splitter.feed(text) if splitter is not None else ("", text)
+                    if r:
+                        delta["reasoning_content"] = r
+                    if c and stop:
+                        cut, hit = _apply_stop_strings(content_sent + c, stop)
+                        c = cut[len(content_sent):] if hit else c
+                    if c:
+                        delta["content"] = c
+                        content_sent += c
+                if delta:
+                    yield chunk(delta)
+                if fin:
+                    yield chunk({}, "stop" if (stopped or hit) else "length")
+                    break
+            yield "data: [DONE]\n\n"
+
+        return StreamingResponse(events(), media_type="text/event-stream")
+
     @app.post("/v1/chat/completions")
     async def chat(body: dict):
         if tokenizer is None or not hasattr(tokenizer, "apply_chat_template"):
@@ -215,6 +352,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         kwargs = body.get("chat_template_kwargs") or {}
         ids = list(tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True,
                                                  tokenize=True, **kwargs))
+        if body.get("stream"):
+            return stream_chat(ids, sp, kwargs, body.get("stop"))
         o = await run(ids, sp)
         raw = tokenizer.decode(o.output_token_ids, skip_special_tokens=False)
         last = o.output_token_ids[-1] if o.output_token_ids else None
