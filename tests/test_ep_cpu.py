@@ -94,6 +94,10 @@ def _model(arch):
 
     if arch == "qwen3_next":  # hybrid: gated DeltaNet + gated attention, shared expert
         return ModelConfig.from_hf(NEXT_HF), NEXT_HF
+    if arch == "flint":  # sliding / full attention with sinks, dense + sigmoid MoE layers
+        from .test_flint_cpu import HF as FLINT_HF
+
+        return ModelConfig.from_hf(FLINT_HF), FLINT_HF
     cfg = ModelConfig(arch="qwen3_moe", hidden_size=128, num_layers=2, num_heads=4,
                       num_kv_heads=2, head_dim=32, intermediate_size=256, vocab_size=512,
                       rope_theta=10000.0, rms_eps=1e-5, max_position=512, qk_norm=True,
@@ -137,7 +141,8 @@ def _dp_body(rank, world, path, out_file):
     state.shutdown()
 
 
-@pytest.mark.parametrize("arch,world", [("qwen3_moe", 2), ("qwen3_moe", 4), ("qwen3_next", 2)])
+@pytest.mark.parametrize("arch,world", [("qwen3_moe", 2), ("qwen3_moe", 4), ("qwen3_next", 2),
+                                        ("flint", 2)])
 def test_dp_ep_engine_equals_single_process(tmp_path, arch, world):
     from vllm_sm70_b200.engine import LLM
 

@@ -1,4 +1,5 @@
-"""Model families: Llama-style dense decoders, Qwen3-MoE, Qwen3-Next hybrid."""
+"""Model families: Llama-style dense decoders, Qwen3-MoE, Qwen3-Next hybrid,
+Flint (sliding / full attention with sinks, sigmoid MoE)."""
 from __future__ import annotations
 
 import torch
@@ -19,4 +20,8 @@ def build_model(cfg: ModelConfig, device: torch.device, dtype=torch.bfloat16, ps
         from .qwen3_next import Qwen3NextModel
 
         return Qwen3NextModel(cfg, device, dtype, ps)
+    if cfg.arch == "flint":
+        from .flint import FlintModel
+
+        return FlintModel(cfg, device, dtype, ps)
     raise ValueError(f"unknown architecture {cfg.arch}")

@@ -10,7 +10,7 @@ from pathlib import Path
 
 @dataclass(frozen=True)
 class ModelConfig:
-    arch: str = "llama"               # llama | qwen3_moe | qwen3_next
+    arch: str = "llama"               # llama | qwen3_moe | qwen3_next | flint
     hidden_size: int = 4096
     num_layers: int = 32
     num_heads: int = 32
@@ -128,6 +128,28 @@ class ModelConfig:
                         attn_output_gate=True,
                         partial_rotary_factor=float(cfg.get("partial_rotary_factor", 0.25)),
                         num_mtp_layers=int(cfg.get("num_nextn_predict_layers", 1)))
+        elif mt == "flint" or any("Flint" in a for a in cfg.get("architectures") or []):
+            if cfg.get("attention_bias"):
+                raise NotImplementedError("Flint with attention biases")
+            if cfg.get("router_score_function", "sigmoid") != "sigmoid":
+                raise ValueError("Flint routes with sigmoid scores")
+            n = base["num_layers"]
+            rp = cfg.get("rope_parameters") or {}
+            by_type = {}
+            if rp and all(isinstance(v, dict) for v in rp.values()):  # per layer type
+                by_type = {k: float(v.get("rope_theta", base["rope_theta"])) for k, v in rp.items()}
+            elif "rope_theta" in rp:
+                base["rope_theta"] = float(rp["rope_theta"])
+            base.update(arch="flint", qk_norm=True, num_experts=cfg["num_experts"],
+                        top_k=cfg["num_experts_per_tok"],
+                        moe_intermediate_size=cfg["moe_intermediate_size"],
+                        shared_expert_intermediate_size=cfg.get("shared_expert_intermediate_size", 0),
+                        norm_topk_prob=bool(cfg.get("norm_topk_prob", True)),
+                        layer_types=tuple(cfg.get("layer_types") or ["full_attention"] * n),
+                        extra={"sliding_window": int(cfg.get("sliding_window") or 0),
+                               "no_rope_layers": list(cfg.get("no_rope_layer_indices") or []),
+                               "mlp_only_layers": list(cfg.get("mlp_only_layers") or []),
+                               "rope_theta_by_type": by_type})
         elif mt in ("qwen3", "qwen2"):
             base.update(arch="llama", qk_norm=(mt == "qwen3"))
         return cls(**base)

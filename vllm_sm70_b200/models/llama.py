@@ -101,6 +101,10 @@ class LlamaModel:
         return {"gate_up": self.make_gate_up(rnd(self.inter, h), rnd(self.inter, h)),
                 "down": self.make_linear(rnd(h, self.inter))}
 
+    def init_layer_mlp_dummy(self, rnd, li: int) -> dict:
+        """The MLP weights of layer ``li`` (every layer alike here)."""
+        return self.init_mlp_dummy(rnd)
+
     def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
         """Random-init weights of the configured shapes (TP-local shards)."""
         cfg, dev, dt = self.cfg, self.device, self.dtype
@@ -123,7 +127,7 @@ class LlamaModel:
                 "qkv": self.make_linear(rnd(qkv_out, h)),
                 "o": self.make_linear(rnd(h, self.hq * self.d)),
             }
-            L.update(self.init_mlp_dummy(rnd))
+            L.update(self.init_layer_mlp_dummy(rnd, len(self.layers)))
             if cfg.qk_norm:
                 L["q_norm"] = torch.ones(self.d, device=dev, dtype=dt)
                 L["k_norm"] = torch.ones(self.d, device=dev, dtype=dt)
@@ -214,10 +218,11 @@ class LlamaModel:
                 "qkv": linear([(a + "q_proj", qs), (a + "k_proj", ks), (a + "v_proj", ks)]),
                 "o": linear([(a + "o_proj", None)], cols=qs),
             }
-            L.update(self._load_mlp(m, get_tensor, has, t, fp8, linear))
+            L.update(self._load_layer_mlp(i, m, get_tensor, has, t, fp8, linear))
             if cfg.qk_norm:
                 L["q_norm"] = t(a + "q_norm.weight")
                 L["k_norm"] = t(a + "k_norm.weight")
+            L.update(self._load_layer_extra(i, a, get_tensor, has, t))
             self.layers.append(L)
         self._init_rope()
 
@@ -248,6 +253,14 @@ class LlamaModel:
         g, u = ops.linear.deinterleave_gate_up(L["gate_up"].w)
         return {m + "gate_proj.weight": g, m + "up_proj.weight": u,
                 m + "down_proj.weight": L["down"].w}
+
+    def _load_layer_mlp(self, li: int, m: str, get_tensor, has, t, fp8, linear) -> dict:
+        """The MLP of layer ``li`` (every layer alike here)."""
+        return self._load_mlp(m, get_tensor, has, t, fp8, linear)
+
+    def _load_layer_extra(self, li: int, a: str, get_tensor, has, t) -> dict:
+        """Further attention tensors of layer ``li`` (none here)."""
+        return {}
 
     def _load_mlp(self, m: str, get_tensor, has, t, fp8, linear) -> dict:
         """Dense SwiGLU MLP at checkpoint prefix ``m`` (``...mlp.``)."""
@@ -318,20 +331,26 @@ class LlamaModel:
         n_layers = len(self.layers)
         for li, L in enumerate(self.layers):
             tracing.push(f"layer{li}")
+            cos_sin, window, sinks = self.attn_params(li, L)
             qkv = L["qkv"].forward(x)
-            ops.rope_kv_write(qkv, meta.positions, self.cos_sin, kv.k[li], kv.v[li],
+            ops.rope_kv_write(qkv, meta.positions, cos_sin, kv.k[li], kv.v[li],
                               meta.slot_mapping, self.hq, self.hkv, L.get("q_norm"),
                               L.get("k_norm"), eps)
             q = qkv.view(T, self.hq + 2 * self.hkv, self.d)[:, : self.hq]
             ops.paged_attention(attn_out, q, kv.k[li], kv.v[li], meta.block_table,
-                                meta.seq_lens, meta.cu_q, meta.max_q_len, self.scale, 0, None,
-                                meta.decode, meta.num_splits, meta.part_o, meta.part_ml)
+                                meta.seq_lens, meta.cu_q, meta.max_q_len, self.scale, window,
+                                sinks, meta.decode, meta.num_splits, meta.part_o, meta.part_ml)
             x, residual = comm.linear_all_reduce_add_rms_norm(
                 L["o"], attn_out.view(T, self.hq * self.d), residual, L["post_norm"], eps)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < n_layers else self.final_norm
             x, residual = self.mlp_ar(li, L, x, residual, nxt, eps)
             tracing.pop()
         return x
+
+    def attn_params(self, li: int, L: dict):
+        """(RoPE cos/sin table, sliding window (0 = none), sink logits or
+        None) of attention layer ``li``."""
+        return self.cos_sin, 0, None
 
     def mlp_ar(self, li: int, L: dict, x: torch.Tensor, residual: torch.Tensor,
                norm_w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:

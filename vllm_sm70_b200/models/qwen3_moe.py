@@ -45,6 +45,7 @@ class Qwen3MoeModel(LlamaModel):
         self.E_local = cfg.num_experts // n
         self.e_base = r * self.E_local
         self.moe_ws = None
+        self.router_sigmoid = False  # softmax top-k scores (sigmoid: Flint)
 
     def init_mlp_dummy(self, rnd) -> dict:
         cfg = self.cfg
@@ -93,7 +94,8 @@ class Qwen3MoeModel(LlamaModel):
             rows = _shard(cfg.shared_expert_intermediate_size, self.ps.tp_size, self.ps.tp_rank)
             sh = self._load_swiglu(m + "shared_expert.", rows, t, fp8, linear)
             L["shared_gate_up"], L["shared_down"] = sh["gate_up"], sh["down"]
-            L["shared_gate"] = t(m + "shared_expert_gate.weight")
+            if has(m + "shared_expert_gate.weight"):
+                L["shared_gate"] = t(m + "shared_expert_gate.weight")
         return L
 
     def _mlp_state(self, m: str, L: dict) -> dict:
@@ -113,8 +115,9 @@ class Qwen3MoeModel(LlamaModel):
             g, u = linear_ops.deinterleave_gate_up(L["shared_gate_up"].w)
             sd.update({m + "shared_expert.gate_proj.weight": g,
                        m + "shared_expert.up_proj.weight": u,
-                       m + "shared_expert.down_proj.weight": L["shared_down"].w,
-                       m + "shared_expert_gate.weight": L["shared_gate"]})
+                       m + "shared_expert.down_proj.weight": L["shared_down"].w})
+            if "shared_gate" in L:
+                sd[m + "shared_expert_gate.weight"] = L["shared_gate"]
         return sd
 
     def _ws(self, T: int):
@@ -137,13 +140,16 @@ class Qwen3MoeModel(LlamaModel):
         ws = self._ws(T) if x.is_cuda else None
         w = ws.w[:T] if ws else None
         ids = ws.ids[:T] if ws else None
-        w, ids = moe_ops.topk(logits, cfg.top_k, use_sigmoid=False, renorm=cfg.norm_topk_prob,
-                              w=w, ids=ids)
+        w, ids = moe_ops.topk(logits, cfg.top_k, use_sigmoid=self.router_sigmoid,
+                              renorm=cfg.norm_topk_prob, w=w, ids=ids)
         shared = None
         if "shared_gate_up" in L:
             sh = L["shared_down"].forward(L["shared_gate_up"].forward(x))
-            gate = torch.sigmoid((x.float() @ L["shared_gate"].float().t()))
-            shared = (sh.float() * gate).to(x.dtype)
+            if "shared_gate" in L:  # sigmoid-gated shared expert (Qwen3-Next)
+                gate = torch.sigmoid((x.float() @ L["shared_gate"].float().t()))
+                shared = (sh.float() * gate).to(x.dtype)
+            else:
+                shared = sh
         if self.ep_a2a is not None:
             return self._ep_moe(L, x, w, ids, shared, out)
         return moe_ops.experts_forward(x, w, ids, L["experts"], ws, self.e_base, shared, out)
