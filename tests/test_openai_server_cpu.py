@@ -159,3 +159,26 @@ def test_stream_chat_equals_unstreamed(client):
     assert (reasoning.rstrip() or None) == whole["reasoning_content"]
     assert content == whole["content"]
     assert ev[-1]["choices"][0]["finish_reason"] == "length"
+
+
+def test_tokenize_detokenize_and_metrics(client):
+    t = client.post("/tokenize", json={"prompt": "hey"}).json()
+    assert t["tokens"] == [ord("h"), ord("e"), ord("y")] and t["count"] == 3
+    c = client.post("/tokenize", json={"messages": [{"role": "user", "content": "x"}]}).json()
+    assert c["tokens"][-1] == 301  # the template opens <think>
+    assert client.post("/detokenize", json={"tokens": t["tokens"]}).json()["prompt"] == "hey"
+    before = client.get("/metrics").text
+    client.post("/v1/completions", json={"prompt": list(range(10, 17)), "max_tokens": 4,
+                                         "temperature": 0.0, "ignore_eos": True})
+    text = client.get("/metrics").text
+
+    def value(body, name):
+        for line in body.splitlines():
+            if line.startswith(name + "{") or line.startswith(name + " "):
+                return float(line.rsplit(" ", 1)[1])
+        return 0.0
+    assert value(text, "vllm:prompt_tokens_total") - value(before, "vllm:prompt_tokens_total") == 7
+    assert (value(text, "vllm:generation_tokens_total")
+            - value(before, "vllm:generation_tokens_total")) == 4
+    assert "vllm:time_to_first_token_seconds_bucket" in text
+    assert 'finished_reason="length"' in text

@@ -5,7 +5,8 @@
     (TP: one process per GPU under torchrun; rank 0 serves HTTP, every rank runs the engine)
 
 Endpoints: ``GET /health``, ``GET /v1/models``, ``POST /v1/completions``,
-``POST /v1/chat/completions``. Requests are batched: a worker thread takes
+``POST /v1/chat/completions``, ``POST /tokenize``, ``POST /detokenize`` and
+``GET /metrics`` (Prometheus, vLLM's metric names: ``entrypoints/metrics.py``). Requests are batched: a worker thread takes
 every request queued when it becomes free and runs them as one
 ``LLM.generate`` call (chunked prefill + CUDA-graph decode across the batch);
 each handler awaits its own result. With a tokenizer, text prompts and chat
@@ -44,10 +45,11 @@ class Batcher:
     """Collects requests from handler threads / coroutines and runs them in
     batches on one worker thread (the engine is not re-entrant)."""
 
-    def __init__(self, llm, max_batch: int = 256, group=None):
+    def __init__(self, llm, max_batch: int = 256, group=None, metrics=None):
         self.llm = llm
         self.max_batch = max_batch
         self.group = group  # TP: the CPU group whose other ranks run follower_loop
+        self.metrics = metrics
         self.q: queue.Queue = queue.Queue()
         self._stop = False
         self.batches = 0
@@ -89,10 +91,14 @@ class Batcher:
                 def on_tokens(i, ids, fin):
                     if streams[i] is not None:
                         streams[i](ids, fin)
+                if self.metrics is not None:
+                    self.metrics.batch_started(len(items), self.q.qsize())
                 outs = self.llm.generate([torch.tensor(p, dtype=torch.int64) for p in batch[0]],
                                          batch[1], on_tokens=on_tokens if interval else None,
                                          stream_interval=interval)
                 self.batches += 1
+                if self.metrics is not None:
+                    self.metrics.batch_finished(self.llm, batch[0], batch[1], outs)
                 for it, o in zip(items, outs):
                     it[2].set_result(o)
             except Exception as e:  # noqa: BLE001 - reported to every waiting request
@@ -184,7 +190,10 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
 
     import contextlib
 
-    batcher = Batcher(llm, max_batch, group)
+    from .metrics import ServerMetrics
+
+    metrics = ServerMetrics(model_name)
+    batcher = Batcher(llm, max_batch, group, metrics)
 
     @contextlib.asynccontextmanager
     async def lifespan(_app):
@@ -255,6 +264,32 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
     @app.get("/health")
     async def health():
         return {"status": "ok"}
+
+    @app.get("/metrics")
+    async def prometheus():
+        from fastapi.responses import Response
+        from prometheus_client import CONTENT_TYPE_LATEST
+
+        return Response(metrics.exposition(), media_type=CONTENT_TYPE_LATEST)
+
+    @app.post("/tokenize")
+    async def tokenize(body: dict):
+        if "messages" in body:
+            if tokenizer is None or not hasattr(tokenizer, "apply_chat_template"):
+                raise HTTPException(400, "chat needs a tokenizer with a chat template")
+            ids = list(tokenizer.apply_chat_template(
+                body["messages"], add_generation_prompt=bool(body.get("add_generation_prompt",
+                                                                      True)),
+                tokenize=True, **(body.get("chat_template_kwargs") or {})))
+        else:
+            ids = encode(body.get("prompt"))
+        return {"tokens": ids, "count": len(ids), "max_model_len": llm.runner.max_model_len}
+
+    @app.post("/detokenize")
+    async def detokenize(body: dict):
+        if tokenizer is None:
+            raise HTTPException(400, "detokenize needs a tokenizer")
+        return {"prompt": decode(list(body.get("tokens") or []))}
 
     @app.get("/v1/models")
     async def models():
