@@ -1,6 +1,8 @@
 """HF-layout safetensors checkpoints through ``LLM(path, load_format=...)``:
-export -> load round trips (Llama, Qwen3-MoE), block-FP8 checkpoints kept in
-FP8 with their scales, and an explicit error where loading is not built."""
+export -> load round trips (Llama, Qwen3-MoE), block-FP8, AutoAWQ int4 and
+ModelOpt NVFP4 checkpoints kept in their formats (dense projections, fused
+q/k/v and gate/up, MoE experts), and an explicit error where loading is not
+built."""
 import json
 
 import pytest
@@ -178,3 +180,104 @@ def test_qwen3_next_mtp_roundtrip(tmp_path):
     assert torch.equal(hb.fc.w, head.fc.w) and torch.equal(hb.layer["qkv"].w, head.layer["qkv"].w)
     plain = LLM(path, load_format="safetensors", **KW)
     assert _tokens(b) == _tokens(plain)
+
+
+def _quantize_sd(sd, fmt):
+    """Quantise every ``*_proj`` weight of an HF state dict the way AutoAWQ /
+    ModelOpt store it. NVFP4: q/k/v and gate/up are quantised jointly (one
+    global scale per fused group, as ModelOpt exports them). Returns the
+    quantised dict and, per projection prefix, the dense weight it encodes."""
+    out, want = {}, {}
+    groups = {}
+    for k in sd:
+        if k.endswith("_proj.weight"):
+            pre = k[: -len(".weight")]
+            base, proj = pre.rsplit(".", 1)
+            key = {"q_proj": "qkv", "k_proj": "qkv", "v_proj": "qkv", "gate_proj": "gu",
+                   "up_proj": "gu"}.get(proj, proj)
+            groups.setdefault((base, key), []).append(pre)
+        else:
+            out[k] = sd[k]
+    for (_, _), pres in groups.items():
+        ws = [sd[p + ".weight"].float() for p in pres]
+        if fmt == "awq":
+            for p, w in zip(pres, ws):
+                qw, qz, sc = quant.quantize_awq(w)
+                out[p + ".qweight"], out[p + ".qzeros"], out[p + ".scales"] = qw, qz, sc
+                want[p] = quant.AwqLinear(qw, qz, sc).reference_weight()
+            continue
+        packed, bs, g = quant.quantize_nvfp4(torch.cat(ws))
+        r0 = 0
+        for p, w in zip(pres, ws):
+            n = w.shape[0]
+            out[p + ".weight"] = packed[r0:r0 + n].contiguous()
+            out[p + ".weight_scale"] = bs[r0:r0 + n].contiguous()
+            out[p + ".weight_scale_2"] = torch.tensor(g, dtype=torch.float32)
+            out[p + ".input_scale"] = torch.tensor(1.0, dtype=torch.float32)
+            want[p] = quant.Nvfp4Linear(packed[r0:r0 + n], bs[r0:r0 + n], g).reference_weight()
+            r0 += n
+    return out, want
+
+
+QCFG = {"awq": {"quant_method": "awq", "bits": 4, "group_size": 128, "version": "gemm"},
+        "nvfp4": {"quant_method": "modelopt", "quant_algo": "NVFP4"}}
+
+
+@pytest.mark.parametrize("fmt", ["awq", "nvfp4"])
+def test_quantized_dense_checkpoint(tmp_path, fmt):
+    a = LLM(TINY, **KW)
+    sd, want = _quantize_sd(a.model.hf_state_dict(), fmt)
+    b = LLM(_write(tmp_path, _hf_config(TINY, quantization_config=QCFG[fmt]), sd),
+            load_format="safetensors", **KW)
+    assert b.cfg.quant == fmt
+    cls = {"awq": quant.AwqLinear, "nvfp4": quant.Nvfp4Linear}[fmt]
+    for i, L in enumerate(b.model.layers):
+        p = f"model.layers.{i}."
+        assert isinstance(L["qkv"], cls) and isinstance(L["down"], cls)
+        qkv = torch.cat([want[p + f"self_attn.{x}_proj"] for x in "qkv"])
+        assert torch.equal(L["qkv"].reference_weight(), qkv)
+        assert torch.equal(L["o"].reference_weight(), want[p + "self_attn.o_proj"])
+        gu = torch.cat([want[p + "mlp.gate_proj"], want[p + "mlp.up_proj"]])
+        assert torch.equal(L["gate_up"].lin.reference_weight(), gu)
+        assert torch.equal(L["down"].reference_weight(), want[p + "mlp.down_proj"])
+    assert all(len(t) == 5 for t in _tokens(b))
+
+
+@pytest.mark.parametrize("fmt", ["awq", "nvfp4"])
+def test_quantized_moe_checkpoint(tmp_path, fmt):
+    cfg = ModelConfig(arch="qwen3_moe", hidden_size=128, num_layers=2, num_heads=4,
+                      num_kv_heads=4, head_dim=32, intermediate_size=256, vocab_size=512,
+                      rope_theta=10000.0, rms_eps=1e-5, max_position=512, qk_norm=True,
+                      num_experts=4, top_k=2, moe_intermediate_size=128)
+    a = LLM(cfg, **KW)
+    sd, want = _quantize_sd(a.model.hf_state_dict(), fmt)
+    b = LLM(_write(tmp_path, _hf_config(cfg, quantization_config=QCFG[fmt]), sd),
+            load_format="safetensors", **KW)
+    ew = b.model.layers[1]["experts"]
+    assert ew.fmt == fmt and ew.E == 4
+    w13, w2 = ew.dense_ref()
+    p = "model.layers.1.mlp.experts."
+    for e in range(4):
+        ref13 = torch.cat([want[f"{p}{e}.gate_proj"], want[f"{p}{e}.up_proj"]])
+        if fmt == "nvfp4":  # per-expert globals are folded into the block scales
+            rel = ((w13[e] - ref13).abs() / ref13.abs().clamp_min(1e-3)).max().item()
+            assert rel < 0.07, rel
+        else:
+            assert torch.equal(w13[e], ref13)
+            assert torch.equal(w2[e], want[f"{p}{e}.down_proj"])
+    assert all(len(t) == 5 for t in _tokens(b))
+
+
+def test_merge_nvfp4_parts_rescales_block_scales():
+    g = torch.Generator().manual_seed(2)
+    w1, w2 = torch.randn(16, 64, generator=g), 4 * torch.randn(16, 64, generator=g)
+    p1, p2 = quant.quantize_nvfp4(w1), quant.quantize_nvfp4(w2)
+    assert p1[2] != p2[2]
+    w, s, gm = quant.merge_nvfp4_parts([p1[0], p2[0]], [p1[1], p2[1]], [p1[2], p2[2]])
+    assert gm == max(p1[2], p2[2])
+    merged = quant.Nvfp4Linear(w, s, gm).reference_weight()
+    ref = torch.cat([quant.Nvfp4Linear(*p1).reference_weight(),
+                     quant.Nvfp4Linear(*p2).reference_weight()])
+    assert torch.equal(merged[16:], ref[16:])  # the part that owns the largest global
+    rel = ((merged - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
+    assert rel < 0.07, rel

@@ -89,10 +89,10 @@ class FlintModel(Qwen3MoeModel):
             full = torch.randn(self.cfg.num_heads, generator=g, device=self.device)
             L["sinks"] = full[heads].contiguous()
 
-    def _load_layer_mlp(self, li, m, get_tensor, has, t, fp8, linear) -> dict:
+    def _load_layer_mlp(self, li, m, get_tensor, has, t, qfmt, linear) -> dict:
         if li in self.mlp_only:
-            return LlamaModel._load_mlp(self, m, get_tensor, has, t, fp8, linear)
-        return self._load_mlp(m, get_tensor, has, t, fp8, linear)
+            return LlamaModel._load_mlp(self, m, get_tensor, has, t, qfmt, linear)
+        return self._load_mlp(m, get_tensor, has, t, qfmt, linear)
 
     def _mlp_state(self, m: str, L: dict) -> dict:
         if "experts" not in L:

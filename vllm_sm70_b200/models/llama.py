@@ -135,48 +135,108 @@ class LlamaModel:
         self._init_rope()
 
     def _loader_helpers(self, get_tensor, has):
-        """(t, fp8, linear) closures over a checkpoint: ``t(name)`` a tensor on
-        this device in the compute dtype; ``fp8(prefix)`` whether that
-        projection is stored block-FP8; ``linear(parts, cols)`` a linear layer
-        from row slices of one or more projections (FP8 shards stay aligned to
-        the 128-row / -column scale blocks)."""
+        """(t, qfmt, linear) closures over a checkpoint: ``t(name)`` a tensor
+        on this device in the compute dtype; ``qfmt(prefix)`` the storage
+        format of that projection (``"fp8"`` block-FP8, ``"awq"`` AutoAWQ
+        int4, ``"nvfp4"`` ModelOpt NVFP4, None for plain floats);
+        ``linear(parts, cols)`` a linear layer from row slices of one or more
+        projections in their format (shards stay aligned to the scale blocks:
+        128 rows / columns for FP8, 8 output columns / 128 input rows for
+        AWQ, 16 input columns for NVFP4)."""
         cfg, dev, dt = self.cfg, self.device, self.dtype
+        from ..ops import quant
 
         def t(name):
             return get_tensor(name).to(device=dev, dtype=dt)
 
-        def fp8(prefix):
-            return cfg.quant == "fp8" and has(prefix + ".weight_scale_inv")
+        def qfmt(prefix):
+            if cfg.quant == "fp8" and has(prefix + ".weight_scale_inv"):
+                return "fp8"
+            if has(prefix + ".qweight"):
+                return "awq"
+            if has(prefix + ".weight_scale") and has(prefix + ".weight_scale_2"):
+                return "nvfp4"
+            return None
 
-        def blocks(sl: slice) -> slice:
-            assert sl.start % 128 == 0 and sl.stop % 128 == 0, "FP8 shard not block aligned"
-            return slice(sl.start // 128, sl.stop // 128)
+        def div(sl: slice, n: int, what: str) -> slice:
+            assert sl.start % n == 0 and sl.stop % n == 0, f"{what} shard not aligned to {n}"
+            return slice(sl.start // n, sl.stop // n)
+
+        def fp8_part(pre, rows, cols):
+            w = get_tensor(pre + ".weight")
+            s = get_tensor(pre + ".weight_scale_inv").float()
+            rows = rows or slice(0, w.shape[0])
+            w, s = w[rows], s[div(rows, 128, "FP8")]
+            if cols is not None:
+                w, s = w[:, cols], s[:, div(cols, 128, "FP8")]
+            return w, s
+
+        def awq_part(pre, rows, cols):
+            q, z, sc = (get_tensor(pre + n) for n in (".qweight", ".qzeros", ".scales"))
+            rows = rows or slice(0, q.shape[1] * 8)
+            q, z, sc = q[:, div(rows, 8, "AWQ")], z[:, div(rows, 8, "AWQ")], sc[:, rows]
+            if cols is not None:
+                g = div(cols, 128, "AWQ")
+                q, z, sc = q[cols], z[g], sc[g]
+            return q, z, sc
+
+        def nvfp4_part(pre, rows, cols):
+            w = get_tensor(pre + ".weight").view(torch.uint8)
+            s = get_tensor(pre + ".weight_scale").view(torch.float8_e4m3fn)
+            g = float(get_tensor(pre + ".weight_scale_2").float().max())
+            rows = rows or slice(0, w.shape[0])
+            w, s = w[rows], s[rows]
+            if cols is not None:
+                w, s = w[:, div(cols, 2, "NVFP4")], s[:, div(cols, 16, "NVFP4")]
+            return w, s, g
 
         def linear(parts, cols=None):
             """Concatenate the row slices ``parts = [(prefix, rows)]`` (rows of
             each projection), optionally cutting input columns ``cols``."""
-            if all(fp8(pre) for pre, _ in parts):
-                ws, ss = [], []
-                for pre, rows in parts:
-                    w = get_tensor(pre + ".weight")
-                    s = get_tensor(pre + ".weight_scale_inv").float()
-                    rows = rows or slice(0, w.shape[0])
-                    w, s = w[rows], s[blocks(rows)]
-                    if cols is not None:
-                        w, s = w[:, cols], s[:, blocks(cols)]
-                    ws.append(w)
-                    ss.append(s)
-                from ..ops import quant
-
+            fmts = {qfmt(pre) for pre, _ in parts}
+            if fmts == {"fp8"}:
+                ws, ss = zip(*(fp8_part(pre, rows, cols) for pre, rows in parts))
                 return quant.Fp8BlockLinear(torch.cat(ws).to(dev), torch.cat(ss).to(dev))
+            if fmts == {"awq"}:
+                qs, zs, scs = zip(*(awq_part(pre, rows, cols) for pre, rows in parts))
+                return quant.AwqLinear(torch.cat(qs, 1).to(dev), torch.cat(zs, 1).to(dev),
+                                       torch.cat(scs, 1).to(dev), cfg.quant_group)
+            if fmts == {"nvfp4"}:
+                ws, ss, gs = zip(*(nvfp4_part(pre, rows, cols) for pre, rows in parts))
+                w, s, g = quant.merge_nvfp4_parts(list(ws), list(ss), list(gs))
+                return quant.Nvfp4Linear(w.to(dev), s.to(dev), g)
             ws = []
             for pre, rows in parts:
-                w = t(pre + ".weight")
+                w = (self._dense_weight(get_tensor, qfmt, pre).to(device=dev, dtype=dt)
+                     if qfmt(pre) else t(pre + ".weight"))
                 w = w[rows] if rows is not None else w
                 ws.append(w[:, cols] if cols is not None else w)
             return DenseLinear(torch.cat(ws, 0))
 
-        return t, fp8, linear
+        return t, qfmt, linear
+
+    @staticmethod
+    def _dense_weight(get_tensor, qfmt, prefix: str) -> torch.Tensor:
+        """The full-precision (fp32, CPU) weight ``[N, K]`` of a projection in
+        any stored format (quantised ones dequantised)."""
+        from ..ops import quant
+
+        fmt = qfmt(prefix)
+        if fmt is None:
+            return get_tensor(prefix + ".weight").float()
+        if fmt == "fp8":
+            w = get_tensor(prefix + ".weight")
+            s = get_tensor(prefix + ".weight_scale_inv").float()
+            s = s.repeat_interleave(128, 0)[: w.shape[0]].repeat_interleave(128, 1)[:, : w.shape[1]]
+            return w.float() * s
+        if fmt == "awq":
+            lin = quant.AwqLinear(get_tensor(prefix + ".qweight"), get_tensor(prefix + ".qzeros"),
+                                  get_tensor(prefix + ".scales"))
+        else:
+            lin = quant.Nvfp4Linear(get_tensor(prefix + ".weight").view(torch.uint8),
+                                    get_tensor(prefix + ".weight_scale"),
+                                    float(get_tensor(prefix + ".weight_scale_2").float().max()))
+        return lin.reference_weight()
 
     def load_hf_state(self, get_tensor, has=None) -> None:
         """Load from an HF Llama / Qwen3-dense checkpoint: bf16 / fp16 weights,
@@ -187,7 +247,7 @@ class LlamaModel:
         cfg = self.cfg
         tp, r = self.ps.tp_size, self.ps.tp_rank
         has = has or (lambda name: True)
-        t, fp8, linear = self._loader_helpers(get_tensor, has)
+        t, qfmt, linear = self._loader_helpers(get_tensor, has)
         vs = slice(r * self.vocab_local, (r + 1) * self.vocab_local)
         emb = t("model.embed_tokens.weight")
         pad = self.vocab_local * tp - emb.shape[0]
@@ -218,7 +278,7 @@ class LlamaModel:
                 "qkv": linear([(a + "q_proj", qs), (a + "k_proj", ks), (a + "v_proj", ks)]),
                 "o": linear([(a + "o_proj", None)], cols=qs),
             }
-            L.update(self._load_layer_mlp(i, m, get_tensor, has, t, fp8, linear))
+            L.update(self._load_layer_mlp(i, m, get_tensor, has, t, qfmt, linear))
             if cfg.qk_norm:
                 L["q_norm"] = t(a + "q_norm.weight")
                 L["k_norm"] = t(a + "k_norm.weight")
@@ -254,23 +314,24 @@ class LlamaModel:
         return {m + "gate_proj.weight": g, m + "up_proj.weight": u,
                 m + "down_proj.weight": L["down"].w}
 
-    def _load_layer_mlp(self, li: int, m: str, get_tensor, has, t, fp8, linear) -> dict:
+    def _load_layer_mlp(self, li: int, m: str, get_tensor, has, t, qfmt, linear) -> dict:
         """The MLP of layer ``li`` (every layer alike here)."""
-        return self._load_mlp(m, get_tensor, has, t, fp8, linear)
+        return self._load_mlp(m, get_tensor, has, t, qfmt, linear)
 
     def _load_layer_extra(self, li: int, a: str, get_tensor, has, t) -> dict:
         """Further attention tensors of layer ``li`` (none here)."""
         return {}
 
-    def _load_mlp(self, m: str, get_tensor, has, t, fp8, linear) -> dict:
+    def _load_mlp(self, m: str, get_tensor, has, t, qfmt, linear) -> dict:
         """Dense SwiGLU MLP at checkpoint prefix ``m`` (``...mlp.``)."""
         is_ = _shard(self.cfg.intermediate_size, self.ps.tp_size, self.ps.tp_rank)
-        return self._load_swiglu(m, is_, t, fp8, linear)
+        return self._load_swiglu(m, is_, t, qfmt, linear)
 
     @staticmethod
-    def _load_swiglu(m: str, rows: slice, t, fp8, linear) -> dict:
+    def _load_swiglu(m: str, rows: slice, t, qfmt, linear) -> dict:
         out = {"down": linear([(m + "down_proj", None)], cols=rows)}
-        if fp8(m + "gate_proj") and fp8(m + "up_proj"):
+        gf = qfmt(m + "gate_proj")
+        if gf is not None and gf == qfmt(m + "up_proj"):  # quantised [gate | up]
             out["gate_up"] = _QuantGateUp(linear([(m + "gate_proj", rows), (m + "up_proj", rows)]))
         else:
             out["gate_up"] = GateUpLinear(t(m + "gate_proj.weight")[rows],

@@ -104,7 +104,7 @@ class MTPHead:
         t = self.t
         assert self.gated, "checkpoint MTP weights are the Qwen3-Next (gated attention) layout"
         has = has or (lambda name: True)
-        tt, fp8, linear = t._loader_helpers(get_tensor, has)
+        tt, qfmt, linear = t._loader_helpers(get_tensor, has)
 
         def zc(name):
             return (1.0 + get_tensor(name).float()).to(device=t.device, dtype=t.dtype)
@@ -121,7 +121,7 @@ class MTPHead:
              "qkv": linear([(a + "q_proj", qg_rows), (a + "k_proj", ks), (a + "v_proj", ks)]),
              "o": linear([(a + "o_proj", None)], cols=o_cols),
              "q_norm": zc(a + "q_norm.weight"), "k_norm": zc(a + "k_norm.weight")}
-        L.update(t._load_mlp(p + "mlp.", get_tensor, has, tt, fp8, linear))
+        L.update(t._load_mlp(p + "mlp.", get_tensor, has, tt, qfmt, linear))
         self.layer = L
 
     def hf_state_dict(self, prefix: str = "mtp.") -> dict:

@@ -62,14 +62,17 @@ class Qwen3MoeModel(LlamaModel):
             L["shared_gate"] = rnd(1, h).to(self.dtype)
         return L
 
-    def _load_mlp(self, m: str, get_tensor, has, t, fp8, linear) -> dict:
-        """Router ``mlp.gate``, this rank's experts ``mlp.experts.{e}.*`` (bf16
-        or block-FP8, stacked as loaded) and the optional shared expert."""
+    def _load_mlp(self, m: str, get_tensor, has, t, qfmt, linear) -> dict:
+        """Router ``mlp.gate``, this rank's experts ``mlp.experts.{e}.*`` (bf16,
+        block-FP8, AWQ int4 or ModelOpt NVFP4, stacked as loaded) and the
+        optional shared expert."""
         cfg = self.cfg
         E, e0 = self.E_local, self.e_base
         L = {"router": t(m + "gate.weight")}
         ex = [f"{m}experts.{e0 + j}." for j in range(E)]
-        if all(fp8(x + "gate_proj") for x in ex):
+        fmts = {qfmt(x + pr) for x in ex for pr in ("gate_proj", "up_proj", "down_proj")}
+        H, I = cfg.hidden_size, cfg.moe_intermediate_size
+        if fmts == {"fp8"}:
             def cat(names, scale):
                 suffix = ".weight_scale_inv" if scale else ".weight"
                 v = [get_tensor(n + suffix) for n in names]
@@ -80,9 +83,28 @@ class Qwen3MoeModel(LlamaModel):
             w2 = cat([x + "down_proj" for x in ex], False)
             s2 = cat([x + "down_proj" for x in ex], True)
             L["experts"] = moe_ops.ExpertWeights(
-                "fp8", E, cfg.hidden_size, cfg.moe_intermediate_size,
-                w13.contiguous().view(torch.uint8), w2.contiguous().view(torch.uint8),
-                s13.contiguous(), s2.contiguous())
+                "fp8", E, H, I, w13.contiguous().view(torch.uint8),
+                w2.contiguous().view(torch.uint8), s13.contiguous(), s2.contiguous())
+        elif fmts in ({"awq"}, {"nvfp4"}):
+            # per expert: [gate | up] and down as quantised linears, then stacked by rows
+            l13 = [linear([(x + "gate_proj", None), (x + "up_proj", None)]) for x in ex]
+            l2 = [linear([(x + "down_proj", None)]) for x in ex]
+            fmt = fmts.pop()
+            if fmt == "awq":
+                L["experts"] = moe_ops.ExpertWeights(
+                    "awq", E, H, I, torch.cat([a.raw for a in l13]), torch.cat([a.raw for a in l2]),
+                    torch.cat([a.scales for a in l13]), torch.cat([a.scales for a in l2]))
+            else:
+                from ..ops import quant
+
+                w13, s13, g13 = quant.merge_nvfp4_parts([a.raw for a in l13],
+                                                        [a.scales for a in l13],
+                                                        [a.out_scale for a in l13])
+                w2, s2, g2 = quant.merge_nvfp4_parts([a.raw for a in l2], [a.scales for a in l2],
+                                                     [a.out_scale for a in l2])
+                L["experts"] = moe_ops.ExpertWeights("nvfp4", E, H, I, w13, w2,
+                                                     s13.view(torch.uint8), s2.view(torch.uint8),
+                                                     g13, g2)
         else:
             w13 = torch.stack([torch.cat([t(x + "gate_proj.weight"), t(x + "up_proj.weight")])
                                for x in ex])
@@ -92,7 +114,7 @@ class Qwen3MoeModel(LlamaModel):
             from .llama import _shard
 
             rows = _shard(cfg.shared_expert_intermediate_size, self.ps.tp_size, self.ps.tp_rank)
-            sh = self._load_swiglu(m + "shared_expert.", rows, t, fp8, linear)
+            sh = self._load_swiglu(m + "shared_expert.", rows, t, qfmt, linear)
             L["shared_gate_up"], L["shared_down"] = sh["gate_up"], sh["down"]
             if has(m + "shared_expert_gate.weight"):
                 L["shared_gate"] = t(m + "shared_expert_gate.weight")

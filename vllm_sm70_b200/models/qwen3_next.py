@@ -120,18 +120,13 @@ class Qwen3NextModel(Qwen3MoeModel):
         cfg, dev, dt = self.cfg, self.device, self.dtype
         tp, r = self.ps.tp_size, self.ps.tp_rank
         has = has or (lambda name: True)
-        t, fp8, linear = self._loader_helpers(get_tensor, has)
+        t, qfmt, linear = self._loader_helpers(get_tensor, has)
 
         def zc(name):  # zero-centred norm -> effective weight
             return (1.0 + get_tensor(name).float()).to(device=dev, dtype=dt)
 
-        def dense(prefix):  # full-precision weight of a projection (dequantised if FP8)
-            w = get_tensor(prefix + ".weight")
-            if fp8(prefix):
-                s = get_tensor(prefix + ".weight_scale_inv").float()
-                s = s.repeat_interleave(128, 0)[: w.shape[0]].repeat_interleave(128, 1)[:, : w.shape[1]]
-                w = w.float() * s
-            return w.float()
+        def dense(prefix):  # full-precision weight of a projection (dequantised if stored so)
+            return self._dense_weight(get_tensor, qfmt, prefix)
 
         h, d = cfg.hidden_size, self.d
         vs = slice(r * self.vocab_local, (r + 1) * self.vocab_local)
@@ -188,7 +183,7 @@ class Qwen3NextModel(Qwen3MoeModel):
                 L["gnorm"] = t(la + "norm.weight")
                 L["out"] = linear([(la + "out_proj", None)],
                                   cols=slice(g0 * rat * DV, g1 * rat * DV))
-            L.update(self._load_mlp(p + "mlp.", get_tensor, has, t, fp8, linear))
+            L.update(self._load_mlp(p + "mlp.", get_tensor, has, t, qfmt, linear))
             self.layers.append(L)
         self._init_rope()
 

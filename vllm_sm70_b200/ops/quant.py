@@ -212,6 +212,23 @@ class Nvfp4Linear(_WQLinear):
         return w
 
 
+def merge_nvfp4_parts(ws, ss, gs):
+    """Row-concatenate NVFP4 parts (``weight`` uint8 ``[n_i, K/2]``, block
+    scales e4m3 ``[n_i, K/16]``, global scale ``g_i``) under ONE global scale,
+    the largest: each part's block scales are multiplied by ``g_i / g`` and
+    rounded to e4m3 -- exact when the globals agree (ModelOpt exports fused
+    projections and MoE experts that way), a rounding of the block scales
+    otherwise."""
+    g = max(gs)
+    out = []
+    for s, gi in zip(ss, gs):
+        s = s.view(torch.float8_e4m3fn)
+        if gi != g:
+            s = (s.float() * (gi / g)).to(torch.float8_e4m3fn)
+        out.append(s)
+    return torch.cat(list(ws)), torch.cat(out), float(g)
+
+
 def make_linear(fmt: str, w: torch.Tensor) -> _WQLinear:
     """Quantise a dense weight ``[N, K]`` into the given format (tests and
     random-init models)."""
