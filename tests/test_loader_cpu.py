@@ -281,3 +281,47 @@ def test_merge_nvfp4_parts_rescales_block_scales():
     assert torch.equal(merged[16:], ref[16:])  # the part that owns the largest global
     rel = ((merged - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
     assert rel < 0.07, rel
+
+
+TP_CFG = ModelConfig(arch="llama", hidden_size=256, num_layers=1, num_heads=4, num_kv_heads=2,
+                     head_dim=64, intermediate_size=512, vocab_size=512, rope_theta=10000.0,
+                     rms_eps=1e-5, max_position=512)
+
+
+def _tp_shard_body(rank, world, path, out):
+    from vllm_sm70_b200.parallel import state
+
+    state.init(tp_size=world, backend="gloo", timeout_s=120)
+    llm = LLM(path, tensor_parallel_size=world, load_format="safetensors", **KW)
+    L = llm.model.layers[0]
+    torch.save({"qkv": L["qkv"].reference_weight(), "o": L["o"].reference_weight(),
+                "gate_up": L["gate_up"].lin.reference_weight(),
+                "down": L["down"].reference_weight()}, f"{out}.{rank}")
+    llm.shutdown()
+    state.shutdown()
+
+
+@pytest.mark.parametrize("fmt", ["awq", "nvfp4"])
+def test_quantized_tp2_shards(tmp_path, fmt):
+    """TP2 shards of a quantised checkpoint (rows of q/k/v and gate/up, input
+    columns of o / down, cut on the scale-block boundaries) are the matching
+    slices of the TP1 weights."""
+    from . import _mp
+
+    a = LLM(TP_CFG, **KW)
+    sd, want = _quantize_sd(a.model.hf_state_dict(), fmt)
+    path = _write(tmp_path, _hf_config(TP_CFG, quantization_config=QCFG[fmt]), sd)
+    _mp.run(_tp_shard_body, 2, args=(path, str(tmp_path / "w")), timeout=300)
+    p = "model.layers.0."
+    hd, I = 64, 512
+    for r in range(2):
+        got = torch.load(tmp_path / f"w.{r}")
+        q = want[p + "self_attn.q_proj"][r * 2 * hd:(r + 1) * 2 * hd]
+        k = want[p + "self_attn.k_proj"][r * hd:(r + 1) * hd]
+        v = want[p + "self_attn.v_proj"][r * hd:(r + 1) * hd]
+        assert torch.equal(got["qkv"], torch.cat([q, k, v]))
+        assert torch.equal(got["o"], want[p + "self_attn.o_proj"][:, r * 2 * hd:(r + 1) * 2 * hd])
+        rows = slice(r * I // 2, (r + 1) * I // 2)
+        assert torch.equal(got["gate_up"], torch.cat([want[p + "mlp.gate_proj"][rows],
+                                                      want[p + "mlp.up_proj"][rows]]))
+        assert torch.equal(got["down"], want[p + "mlp.down_proj"][:, rows])
