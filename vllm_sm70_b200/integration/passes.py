@@ -69,5 +69,7 @@ def install_composite_pass(vllm_config) -> bool:
 
 
 def register() -> None:
-    """Plugin area hook (patterns register themselves on import)."""
-    return None
+    """Plugin area hook: register the built-in patterns."""
+    from . import ar_norm_fusion
+
+    register_pattern(ar_norm_fusion.fuse_all_reduce_add_rms_norm)
