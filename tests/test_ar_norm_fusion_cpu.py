@@ -97,3 +97,13 @@ def test_composite_pass_carries_pattern():
 
     passes.register()
     assert f.fuse_all_reduce_add_rms_norm in passes.CompositePass().patterns
+
+
+def test_worker_install_declines_without_tp():
+    """Outside a vLLM TP group (here: no distributed state) nothing is
+    allocated or installed."""
+    from vllm_sm70_b200.integration import ar_norm_fusion as f
+
+    before = f._route["fn"]
+    assert f.install_for_worker(object()) is False
+    assert f._route["fn"] is before

@@ -289,8 +289,10 @@ def engine_warmup(model, ps, Ms: list[int], lut_path: str | None = None,
 def platform_warmup(worker) -> None:
     """vLLM ``kernel_warmup`` hook (U1): router and sampler preparation and
     GEMM planning for vLLM-owned linears go through the same tables."""
+    from ..integration import ar_norm_fusion
     from ..models import router
     from . import hidden_state_sampler
 
     router.prepare_worker(worker)
     hidden_state_sampler.prepare_worker(worker)
+    ar_norm_fusion.install_for_worker(worker)

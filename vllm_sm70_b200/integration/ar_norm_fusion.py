@@ -40,6 +40,57 @@ def install_fused_route(fn) -> None:
     _route["fn"] = fn
 
 
+def install_for_worker(worker) -> bool:
+    """Inside a vLLM worker (``kernel_warmup``, before graph capture):
+    allocate the symmetric workspace over vLLM's TP group and install the
+    fused route. Every rank decides from rank-uniform facts and the ranks
+    agree over the CPU group before the collective allocation, so either all
+    of them install it or none does. Returns whether it was installed."""
+    from types import SimpleNamespace
+
+    import torch.distributed as dist
+
+    from .. import envs
+
+    try:
+        from vllm.distributed import get_tp_group
+
+        g = get_tp_group()
+    except Exception:  # noqa: BLE001 - no vLLM distributed state: nothing to fuse
+        return False
+    ok = (bool(envs.get("VLLM_B200_FUSED_AR_RMSNORM")) and torch.cuda.is_available()
+          and g.world_size in (2, 4, 8))
+    cfg = getattr(worker, "vllm_config", None)
+    if ok and cfg is not None:
+        H = int(cfg.model_config.get_hidden_size())
+        T = int(cfg.scheduler_config.max_num_batched_tokens)
+        ok = cfg.model_config.dtype == torch.bfloat16 and H % 8 == 0
+    else:
+        ok = False
+    if g.world_size > 1:
+        flags = [None] * g.world_size
+        dist.all_gather_object(flags, ok, group=g.cpu_group)
+        ok = all(flags)
+    if not ok:
+        return False
+    from ..parallel.symm import FusedArRmsNorm
+
+    ps = SimpleNamespace(tp_size=g.world_size, tp_rank=g.rank_in_group,
+                         device=torch.device("cuda", torch.cuda.current_device()),
+                         tp_group=g.device_group, cpu_group=g.cpu_group)
+    impl = FusedArRmsNorm(ps, T, H)
+
+    def route(x, residual, weight, eps):
+        if (x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous()
+                or residual.shape != x.shape or weight.dtype != torch.bfloat16):
+            return None
+        return impl(x, residual, weight, eps)
+
+    install_fused_route(route)
+    logger.info("fused all-reduce + RMSNorm route installed (TP %d, %d tokens)", g.world_size, T)
+    return True
+
+
 def _unfused(x, residual, weight, eps, group_name):
     ar = torch.ops.vllm.all_reduce(x, group_name)
     return torch.ops.vllm_ir.fused_add_rms_norm(ar, residual, weight, eps)
