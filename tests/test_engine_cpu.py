@@ -198,3 +198,39 @@ def test_prefix_cache_host_tier_restores_evicted_blocks():
     assert host.saved > 0  # the prefix blocks were pushed out to the host tier
     got_b = llm.generate([b], sp)[0].output_token_ids
     assert host.restored >= 2 and got_b == want_b
+
+
+def test_prefix_cache_disk_tier_survives_the_engine(tmp_path):
+    """A second engine (same model, same cache directory) starts with the
+    first one's prompt blocks: it restores them from disk instead of
+    prefilling and generates exactly what a cache-free engine does. An engine
+    of another model (other seed) lives in another namespace and finds
+    nothing; damaged files are refused, not read."""
+    g = torch.Generator().manual_seed(21)
+    prefix = torch.randint(0, 512, (48,), generator=g)
+    a = torch.cat([prefix, torch.randint(0, 512, (5,), generator=g)])
+    b = torch.cat([prefix, torch.randint(0, 512, (9,), generator=g)])
+    sp = SamplingParams(max_tokens=4, ignore_eos=True)
+    want_b = _llm().generate([b], sp)[0].output_token_ids
+    first = _llm(enable_prefix_caching=True, prefix_cache_dir=str(tmp_path))
+    first.generate([a], sp)
+    disk = first.prefix_cache.disk
+    assert disk.saved == 3 and len(list(disk.dir.glob("*.kv"))) == 3
+    second = _llm(enable_prefix_caching=True, prefix_cache_dir=str(tmp_path))
+    assert second.prefix_cache.disk.dir == disk.dir
+    assert second.generate([b], sp)[0].output_token_ids == want_b
+    assert second.prefix_cache.disk.restored == 3 and second.prefix_cache.hits == 3
+    other = _llm(enable_prefix_caching=True, prefix_cache_dir=str(tmp_path), seed=7)
+    assert other.prefix_cache.disk.dir != disk.dir
+    other.generate([b], sp)
+    assert other.prefix_cache.disk.restored == 0
+    # a truncated file is refused and the block is prefilled instead
+    for f in disk.dir.glob("*.kv"):
+        f.write_bytes(f.read_bytes()[:100])
+    third = _llm(enable_prefix_caching=True, prefix_cache_dir=str(tmp_path))
+    assert third.generate([b], sp)[0].output_token_ids == want_b
+    assert third.prefix_cache.disk.restored == 0
+    # ... and replaced by a good copy when the block is cached again
+    fourth = _llm(enable_prefix_caching=True, prefix_cache_dir=str(tmp_path))
+    assert fourth.generate([b], sp)[0].output_token_ids == want_b
+    assert fourth.prefix_cache.disk.restored == 3

@@ -42,7 +42,7 @@ from ..parallel import state as pstate
 from ..utils import tracing
 from ..utils.watchdog import StreamWatchdog
 from .model_runner import ModelRunner
-from .prefix_cache import HostKVTier, PrefixCache
+from .prefix_cache import DiskKVTier, HostKVTier, PrefixCache
 from .sampling_params import RequestOutput, SamplingParams
 
 
@@ -97,7 +97,8 @@ class LLM:
                  dtype=torch.bfloat16, num_kv_blocks: int | None = None,
                  tune_gemm: bool = True, gemm_lut_path: str | None = None,
                  speculative_k: int = 0, enable_prefix_caching: bool | None = None,
-                 data_parallel_size: int = 1, enable_expert_parallel: bool = False):
+                 data_parallel_size: int = 1, enable_expert_parallel: bool = False,
+                 prefix_cache_dir: str | None = None):
         self.cfg: ModelConfig = resolve(model)
         ps = pstate.get() if pstate._STATE is not None else None
         dp = int(data_parallel_size)
@@ -179,9 +180,34 @@ class LLM:
         if enable_prefix_caching and not hybrid and self.spec_k == 0:
             host_blocks = int(envs.get("VLLM_B200_PREFIX_HOST_BLOCKS"))
             host = HostKVTier(self.runner.kv, host_blocks) if host_blocks > 0 else None
-            self.prefix_cache = PrefixCache(self.runner.alloc, self.runner.block_size, host)
+            disk = None
+            disk_dir = prefix_cache_dir or envs.get("VLLM_B200_PREFIX_DISK_DIR")
+            if disk_dir:
+                disk = DiskKVTier(self.runner.kv, disk_dir,
+                                  self._kv_namespace(model, load_format, seed, dtype),
+                                  int(envs.get("VLLM_B200_PREFIX_DISK_BLOCKS")))
+            self.prefix_cache = PrefixCache(self.runner.alloc, self.runner.block_size, host, disk)
         wd = int(envs.get("VLLM_B200_WATCHDOG_S"))
         self.watchdog = (StreamWatchdog(wd) if wd > 0 and self.device.type == "cuda" else None)
+
+    def _kv_namespace(self, model, load_format: str, seed: int, dtype) -> str:
+        """Name of this engine's KV bytes: model shapes, weight source, dtype,
+        cache layout and TP position (the disk tier's directory)."""
+        import hashlib
+        import json
+        from pathlib import Path
+
+        src = model if isinstance(model, str) else None
+        if src is not None and Path(src).exists():
+            files = sorted(Path(src).glob("*.safetensors")) if Path(src).is_dir() else [Path(src)]
+            src = [str(Path(src).resolve())] + [(f.name, f.stat().st_size, int(f.stat().st_mtime))
+                                               for f in files]
+        ident = {"cfg": self.cfg.to_dict(), "src": src, "format": load_format,
+                 "seed": seed if load_format == "dummy" else None, "dtype": str(dtype),
+                 "block": self.runner.block_size, "hkv": self.model.hkv, "d": self.model.d,
+                 "tp": [self.ps.tp_size, self.ps.tp_rank]}
+        blob = json.dumps(ident, sort_keys=True, default=str).encode()
+        return hashlib.sha256(blob).hexdigest()[:20]
 
     def shutdown(self) -> None:
         """Release CUDA graphs (they may hold NCCL work) before the process

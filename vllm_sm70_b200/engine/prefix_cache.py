@@ -11,6 +11,11 @@ only the cache still references are evicted least-recently-used first -- into
 an optional host-memory tier (``HostKVTier``) from which a later hit copies
 them back.
 
+A third, persistent tier (``DiskKVTier``) writes every indexed block
+through to files named by its key, so a later engine process with the same
+model, layout and rank -- after a restart, or another replica on the same
+host -- starts with those prefixes cached.
+
 Hybrid models with recurrent state (gated DeltaNet) cannot skip prefill on a
 KV hit -- the state is not cached -- so the engine does not enable this for
 them.
@@ -20,7 +25,10 @@ deployment keeps on (``sm70/nix/module.nix:241``).
 """
 from __future__ import annotations
 
+import io
+import os
 from collections import OrderedDict
+from pathlib import Path
 
 import torch
 
@@ -84,11 +92,92 @@ class HostKVTier:
         return True
 
 
+class DiskKVTier:
+    """Persistent tier: one file per block under ``root/namespace``, named by
+    the block's chained key (keys are deterministic across processes: they
+    hash token ids only). ``namespace`` must identify everything that makes
+    KV bytes differ -- model, weights, dtype, block size, TP rank -- so
+    tiers of different engines never mix. Files are written atomically
+    (temporary name + rename); the least recently used ones beyond
+    ``capacity_blocks`` are deleted. Reads check the tensor shapes."""
+
+    def __init__(self, kv, root: str | Path, namespace: str, capacity_blocks: int):
+        self.kv = kv
+        self.layers = [i for i, t in enumerate(kv.k) if t is not None]
+        self.dir = Path(root) / namespace
+        self.dir.mkdir(parents=True, exist_ok=True)
+        self.capacity = int(capacity_blocks)
+        self.saved = 0
+        self.restored = 0
+        self._size: int | None = None  # bytes of one block file (a shorter file is damaged)
+
+    def _path(self, key: int) -> Path:
+        return self.dir / f"{key:016x}.kv"
+
+    def has(self, key: int) -> bool:
+        return self._path(key).exists()
+
+    def save(self, key: int, block: int) -> None:
+        p = self._path(key)
+        if self._size is not None and p.exists() and p.stat().st_size == self._size:
+            os.utime(p)  # already there (and whole): refresh its LRU time
+            return
+        k = torch.stack([self.kv.k[i][block] for i in self.layers]).cpu()
+        v = torch.stack([self.kv.v[i][block] for i in self.layers]).cpu()
+        buf = io.BytesIO()
+        torch.save({"k": k, "v": v}, buf)
+        blob = buf.getvalue()
+        self._size = len(blob)  # every block of a namespace serialises to this size
+        if p.exists() and p.stat().st_size == self._size:
+            os.utime(p)
+            return
+        tmp = p.with_name(f"{p.name}.{os.getpid()}.tmp")
+        tmp.write_bytes(blob)
+        os.replace(tmp, p)
+        self.saved += 1
+        self._trim()
+
+    def restore(self, key: int, block: int) -> bool:
+        p = self._path(key)
+        try:
+            d = torch.load(p, map_location="cpu", weights_only=True)
+        except FileNotFoundError:
+            return False
+        except Exception:  # noqa: BLE001 - damaged file: drop it, the block is prefilled
+            p.unlink(missing_ok=True)
+            return False
+        ref = self.kv.k[self.layers[0]][block]
+        if (not isinstance(d, dict) or "k" not in d or "v" not in d
+                or d["k"].shape != (len(self.layers),) + tuple(ref.shape)
+                or d["k"].dtype != ref.dtype or d["v"].shape != d["k"].shape):
+            p.unlink(missing_ok=True)
+            return False
+        for j, i in enumerate(self.layers):
+            self.kv.k[i][block].copy_(d["k"][j])
+            self.kv.v[i][block].copy_(d["v"][j])
+        os.utime(p)
+        self.restored += 1
+        return True
+
+    def _trim(self) -> None:
+        files = list(self.dir.glob("*.kv"))
+        if len(files) <= self.capacity:
+            return
+        files.sort(key=lambda f: f.stat().st_mtime)
+        for f in files[: len(files) - self.capacity]:
+            try:
+                f.unlink()
+            except FileNotFoundError:
+                pass
+
+
 class PrefixCache:
-    def __init__(self, alloc, block_size: int, host: HostKVTier | None = None):
+    def __init__(self, alloc, block_size: int, host: HostKVTier | None = None,
+                 disk: DiskKVTier | None = None):
         self.alloc = alloc
         self.bs = block_size
         self.host = host
+        self.disk = disk
         self.entries: OrderedDict[int, int] = OrderedDict()  # key -> block id (LRU order)
         self.hits = 0      # blocks served from the cache (either tier)
         self.queries = 0   # full blocks looked up
@@ -110,16 +199,19 @@ class PrefixCache:
                 self.alloc.incref(torch.tensor([b], dtype=torch.int32))
                 blocks.append(b)
                 continue
-            # host tier: back into a fresh device block (the cache keeps a reference),
-            # making room by pushing other cache-only blocks to the host first
-            if self.host is None or k not in self.host.slots:
+            # host or disk tier: back into a fresh device block (the cache keeps a
+            # reference), making room by pushing other cache-only blocks out first
+            in_host = self.host is not None and k in self.host.slots
+            if not in_host and (self.disk is None or not self.disk.has(k)):
                 break
             if self.alloc.num_free() < 1:
                 self.evict(1)
             if self.alloc.num_free() < 1:
                 break
             b = int(self.alloc.allocate(1)[0])
-            self.host.restore(k, b)
+            if not (self.host.restore(k, b) if in_host else self.disk.restore(k, b)):
+                self.alloc.free(torch.tensor([b], dtype=torch.int32))
+                break
             self.entries[k] = b
             self.alloc.incref(torch.tensor([b], dtype=torch.int32))
             blocks.append(b)
@@ -140,6 +232,8 @@ class PrefixCache:
                 continue
             self.entries[k] = b
             new.append(b)
+            if self.disk is not None:  # write through: persists past this process
+                self.disk.save(k, b)
         if new:
             self.alloc.incref(torch.tensor(new, dtype=torch.int32))
 

@@ -102,6 +102,12 @@ _reg("VLLM_B200_PREFIX_CACHING", "optin", False, "runtime",
 _reg("VLLM_B200_PREFIX_HOST_BLOCKS", "int", 0, "runtime",
      "Prefix caching: KV blocks kept in pinned host memory after eviction from the device "
      "(0 = no host tier).")
+_reg("VLLM_B200_PREFIX_DISK_DIR", "path", None, "runtime",
+     "Prefix caching: directory of a persistent KV tier (every cached prompt block is also "
+     "written there, one file per block, and found again by later engine processes of the "
+     "same model / layout / rank). Unset = no disk tier.")
+_reg("VLLM_B200_PREFIX_DISK_BLOCKS", "int", 65536, "runtime",
+     "Prefix caching: blocks kept in the disk tier (least recently used files deleted).")
 _reg("VLLM_B200_NVTX", "optin", False, "runtime",
      "Emit NVTX ranges per layer and engine phase for profiler timelines.")
 _reg("VLLM_B200_WATCHDOG_S", "int", 0, "runtime",
