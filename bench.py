@@ -35,6 +35,25 @@ MODEL = "Llama-3.1-8B-shaped (32L, h4096, 32q/8kv, d128, ffn14336, vocab128256)"
 N_REQ, PROMPT, OUT = 256, 1024, 256  # the headline workload; --requests/--prompt-len/
 # --output-len exist only for profiling runs and mark the JSON line "profiling"
 BASELINE_VALUE = None  # no published number exists for this config
+PRESET, TEMPERATURE, SPEC_K = "llama-3.1-8b", 0.0, 0
+
+# The other BASELINE configurations (--config): preset, workload, sampling.
+WORKLOADS = {
+    "llama-3.1-8b": dict(preset="llama-3.1-8b", model=MODEL, requests=256, prompt=1024,
+                         output=256, temperature=0.0, spec_k=0),
+    "qwen3-30b-a3b-fp8": dict(
+        preset="qwen3-30b-a3b-fp8", requests=512, prompt=2048, output=256, temperature=0.0,
+        spec_k=0, model="Qwen3-30B-A3B-shaped (48L, h2048, 32q/4kv, d128, 128 experts top-8, "
+                        "expert ffn 768, vocab151936), block-FP8 weights"),
+    "llama-3.1-70b-awq": dict(
+        preset="llama-3.1-70b-awq", requests=128, prompt=4096, output=512, temperature=0.0,
+        spec_k=0, model="Llama-3.1-70B-shaped (80L, h8192, 64q/8kv, d128, ffn28672), AWQ int4 g128"),
+    "qwen3-next-80b-a3b-nvfp4": dict(
+        preset="qwen3-next-80b-a3b-nvfp4", requests=256, prompt=8192, output=256,
+        temperature=0.7, spec_k=3,
+        model="Qwen3-Next-80B-A3B-shaped (48L hybrid 3:1 gated-DeltaNet / gated attention, "
+              "512 experts top-10 + shared, MTP k=3), NVFP4 weights"),
+}
 
 
 def _env_int(name, default):
@@ -112,6 +131,16 @@ def _max_over_ranks(x: float) -> float:
     return x
 
 
+def _sum_over_ranks(x: float) -> float:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        return float(t.item())
+    return x
+
+
 def _barrier():
     import torch.distributed as dist
 
@@ -134,14 +163,22 @@ def run_ours(args) -> dict:
     from vllm_sm70_b200.utils import launch_count
 
     world, rank = _dist_setup()
-    ps = pstate.init(tp_size=args.gpus if world > 1 else 1)
-    llm = LLM("llama-3.1-8b", tensor_parallel_size=ps.tp_size, max_num_seqs=N_REQ,
-              max_model_len=PROMPT + OUT, block_size=args.block_size,
-              max_num_batched_tokens=args.chunk, load_format="dummy", seed=0)
-    warm = [make_prompts(1000 + i).pin_memory() for i in range(args.warmup)]
-    timed = [make_prompts(2000 + i).pin_memory() for i in range(args.steps)]
+    dp = args.layout == "dp-ep" and world > 1  # each rank serves its share of the requests
+    if dp:
+        ps = pstate.init(tp_size=1, ep_size=world)
+    else:
+        ps = pstate.init(tp_size=args.gpus if world > 1 else 1)
+    share = (lambda p: p[rank::world].contiguous()) if dp else (lambda p: p)
+    llm = LLM(PRESET, tensor_parallel_size=ps.tp_size,
+              max_num_seqs=(N_REQ + world - 1) // world if dp else N_REQ,
+              max_model_len=PROMPT + OUT + (SPEC_K + 1 if SPEC_K else 0),
+              block_size=args.block_size, max_num_batched_tokens=args.chunk,
+              load_format="dummy", seed=0, speculative_k=SPEC_K,
+              data_parallel_size=world if dp else 1, enable_expert_parallel=dp)
+    warm = [share(make_prompts(1000 + i)).pin_memory() for i in range(args.warmup)]
+    timed = [share(make_prompts(2000 + i)).pin_memory() for i in range(args.steps)]
     prompts = timed[0]
-    sp = SamplingParams(max_tokens=OUT, temperature=0.0, ignore_eos=True)
+    sp = SamplingParams(max_tokens=OUT, temperature=TEMPERATURE, ignore_eos=True)
     for w in warm:
         llm.generate(w, sp)
     torch.cuda.synchronize()
@@ -174,6 +211,8 @@ def run_ours(args) -> dict:
     dev_ms = _max_over_ranks(dev_ms)
     wall = _max_over_ranks(wall)
     n_out = sum(len(o.output_token_ids) for o in outs) * args.steps
+    if dp:  # every rank served its own share: the job's tokens are the sum
+        n_out = int(_sum_over_ranks(float(n_out)))
     value = n_out / (dev_ms / 1e3)
     e2e = n_out / wall
     res = {
@@ -183,7 +222,9 @@ def run_ours(args) -> dict:
         "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 3),
         "dtype": "bf16", "data": "synthetic (uniform-random prompt ids, random-init weights std 0.02)",
         "config": {"model": MODEL, "global_batch": N_REQ, "seq_len": PROMPT,
-                   "output_len": OUT, "parallelism": f"tp{args.gpus}",
+                   "output_len": OUT,
+                   "parallelism": f"dp{args.gpus}-ep{args.gpus}" if dp else f"tp{args.gpus}",
+                   "temperature": TEMPERATURE, "speculative_k": SPEC_K,
                    "l2": "inputs larger than L2 (16 GB of weights streamed per step)",
                    "block_size": args.block_size, "prefill_chunk_tokens": args.chunk},
         "p50_ttft_ms": round(statistics.median(ttft), 1) if ttft else None,
@@ -307,11 +348,23 @@ def main(argv=None):
     ap.add_argument("--prompt-len", type=int, default=None, help="profiling only")
     ap.add_argument("--output-len", type=int, default=None, help="profiling only")
     ap.add_argument("--verbose", action="store_true", help="log engine set-up (GEMM plans)")
+    ap.add_argument("--config", choices=sorted(WORKLOADS), default="llama-3.1-8b",
+                    help="BASELINE configuration (default: the headline Llama-3.1-8B workload)")
+    ap.add_argument("--layout", choices=["tp", "dp-ep"], default="tp",
+                    help="N > 1: tensor parallel (MoE experts sliced over the TP group), or "
+                         "data-parallel attention with all-to-all expert parallelism")
     args = ap.parse_args(argv)
     if args.verbose:
         import logging
         logging.basicConfig(level=logging.INFO, stream=sys.stderr)
-    global N_REQ, PROMPT, OUT
+    global N_REQ, PROMPT, OUT, MODEL, PRESET, TEMPERATURE, SPEC_K
+    wl = WORKLOADS[args.config]
+    N_REQ, PROMPT, OUT, MODEL = wl["requests"], wl["prompt"], wl["output"], wl["model"]
+    PRESET, TEMPERATURE, SPEC_K = wl["preset"], wl["temperature"], wl["spec_k"]
+    if args.impl == "reference" and args.config != "llama-3.1-8b":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "the reference arm is wired for the headline Llama-3.1-8B config only"}))
+        return
     if args.requests or args.prompt_len or args.output_len:
         N_REQ = args.requests or N_REQ
         PROMPT = args.prompt_len or PROMPT
