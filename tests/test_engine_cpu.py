@@ -234,3 +234,33 @@ def test_prefix_cache_disk_tier_survives_the_engine(tmp_path):
     fourth = _llm(enable_prefix_caching=True, prefix_cache_dir=str(tmp_path))
     assert fourth.generate([b], sp)[0].output_token_ids == want_b
     assert fourth.prefix_cache.disk.restored == 3
+
+
+def test_continuous_batching_feed():
+    """Requests fed while others decode join the running batch and give the
+    same greedy tokens as a plain batch call; an unservable request (longer
+    than max_model_len) finishes with an error while the rest are served; a
+    closed feed ends the call once the running requests are done."""
+    g = torch.Generator().manual_seed(0)
+    P = [torch.randint(0, 512, (n,), generator=g) for n in (7, 33, 12, 20, 9)]
+    llm = _llm()
+    ref = [o.output_token_ids for o in llm.generate(P, SamplingParams(max_tokens=6))]
+    sp = SamplingParams(max_tokens=6)
+    plan = {0: [(0, P[0].tolist(), sp), (1, P[1].tolist(), sp)],
+            2: [(2, P[2].tolist(), sp), (99, list(range(200)), sp)],   # 99: too long
+            4: [(3, P[3].tolist(), sp), (4, P[4].tolist(), sp)]}
+    calls = []
+
+    def feed(block):
+        calls.append(block)
+        n = len(calls) - 1
+        if not plan:
+            return None  # closed: finish what runs
+        return plan.pop(n, [])
+
+    done = {}
+    out = llm.generate([], feed=feed, on_finish=lambda o: done.__setitem__(o.request_id, o))
+    assert out == []
+    assert [done[i].output_token_ids for i in range(5)] == ref
+    assert done[99].error and done[99].output_token_ids == []
+    assert all(done[i].error is None for i in range(5))

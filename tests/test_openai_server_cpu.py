@@ -182,3 +182,32 @@ def test_tokenize_detokenize_and_metrics(client):
             - value(before, "vllm:generation_tokens_total")) == 4
     assert "vllm:time_to_first_token_seconds_bucket" in text
     assert 'finished_reason="length"' in text
+
+
+def test_continuous_batching_late_short_request_overtakes():
+    """A short request submitted while a long one is decoding joins the
+    running batch and finishes first (it does not wait for the long one);
+    both equal their stand-alone results."""
+    import threading
+
+    from vllm_sm70_b200.entrypoints.openai_server import Batcher
+
+    llm = LLM(TINY, max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=64)
+    long_p, short_p = list(range(10, 30)), list(range(40, 50))
+    want_long = llm.generate([torch.tensor(long_p)], SamplingParams(max_tokens=60))[0]
+    want_short = llm.generate([torch.tensor(short_p)], SamplingParams(max_tokens=3))[0]
+    b = Batcher(llm, max_batch=4)
+    order = []
+    started = threading.Event()
+    f_long = b.submit(long_p, SamplingParams(max_tokens=60),
+                      stream=lambda ids, fin: started.set())
+    assert started.wait(30)  # the long request is decoding
+    f_short = b.submit(short_p, SamplingParams(max_tokens=3))
+    f_short.add_done_callback(lambda f: order.append("short"))
+    f_long.add_done_callback(lambda f: order.append("long"))
+    assert f_short.result(60).output_token_ids == want_short.output_token_ids
+    assert f_long.result(60).output_token_ids == want_long.output_token_ids
+    assert order == ["short", "long"] and b.batches >= 2
+    b.close()
+    assert not b.thread.is_alive()

@@ -75,6 +75,11 @@ class GenerateStats:
     spec_slots: int = 0    # (row, step) pairs; spec_tokens / spec_slots = tokens per step
 
 
+def _filters(p: SamplingParams) -> bool:
+    """Whether the request needs top-k / top-p candidate sampling."""
+    return p.top_k not in (-1, 0) or p.top_p < 1.0
+
+
 def _truncate_at_stop(tokens: list[int], p: SamplingParams) -> list[int]:
     """Cut the output after the first stop token (kept, like vLLM's token ids)
     unless the request ignores EOS. Decode runs whole bursts on the device, so
@@ -170,6 +175,7 @@ class LLM:
         if self.spec_k == 0:
             self.runner.capture()
         self.last_stats: GenerateStats | None = None
+        self.spec_hook = None  # spec_hook(rows, emitted tokens) after each speculative step
         # Prefix caching: content-addressed reuse of full prompt KV blocks. Not
         # for models with recurrent state or with a speculative draft head
         # (neither state is cached with the blocks).
@@ -288,7 +294,7 @@ class LLM:
 
     def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
                  collect_stats: bool = True, on_tokens=None,
-                 stream_interval: int = 0) -> list[RequestOutput]:
+                 stream_interval: int = 0, feed=None, on_finish=None) -> list[RequestOutput]:
         """Serve the prompts to completion; returns one output per prompt.
 
         Streaming: ``on_tokens(request_index, new_token_ids, finished)`` is
@@ -296,7 +302,19 @@ class LLM:
         every decode burst (at most ``stream_interval`` steps per burst when
         > 0), and once with ``finished=True``; tokens after a stop token are
         not streamed. Under TP every rank must pass the same
-        ``stream_interval`` (it sets the burst boundaries)."""
+        ``stream_interval`` (it sets the burst boundaries).
+
+        Continuous batching (``feed``): ``feed(block)`` is called once per
+        scheduler iteration and returns new requests ``[(request_id, prompt
+        ids, SamplingParams)]`` to admit alongside the running ones (waiting
+        for at least one when ``block`` is true: nothing runs), or None to
+        finish once the running requests are done. Finished requests go to
+        ``on_finish(RequestOutput)`` instead of the return value; a request
+        that cannot be served (longer than ``max_model_len``, larger than the
+        KV cache) finishes with ``error`` set while the others carry on.
+        Bursts are at most ``stream_interval`` (default 8) steps, so arrivals
+        join within a few steps. Under TP every rank's ``feed`` must return
+        the same requests in the same calls (rank 0 broadcasts them)."""
         if sampling_params is None:
             sampling_params = SamplingParams()
         if isinstance(prompt_token_ids, torch.Tensor):
@@ -305,20 +323,25 @@ class LLM:
             prompts = [torch.as_tensor(p, dtype=torch.int64) for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
-        filtering = any(p.top_k not in (-1, 0) or p.top_p < 1.0 for p in params)
+        filtering = any(_filters(p) for p in params)
         if filtering and self.spec_k:
             raise NotImplementedError("top-k / top-p with speculative decoding")
         reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
         runner = self.runner
         runner.filtering = filtering
         try:
-            return self._generate(reqs, on_tokens, int(stream_interval))
+            return self._generate(reqs, on_tokens, int(stream_interval), feed, on_finish)
         finally:
             runner.filtering = False
 
-    def _generate(self, reqs: list[_Req], on_tokens=None,
-                  stream_interval: int = 0) -> list[RequestOutput]:
+    def _generate(self, reqs: list[_Req], on_tokens=None, stream_interval: int = 0,
+                  feed=None, on_finish=None) -> list[RequestOutput]:
         runner = self.runner
+        online = feed is not None
+        if online and on_finish is None:
+            on_finish = lambda out: None  # noqa: E731 - e.g. TP followers
+        if online and stream_interval <= 0:
+            stream_interval = 8  # bounded bursts: arrivals join within a few steps
 
         def emit(rs, rows_h=None, final=False):
             """Hand each request's not-yet-streamed tokens to ``on_tokens``."""
@@ -355,7 +378,25 @@ class LLM:
         decode_events: list[tuple[object, list[_Req], int]] = []
         prefill_spans: list[tuple[object, object]] = []
 
-        while waiting or running:
+        def pull() -> bool:
+            """Queue the feed's new requests; False once it is closed."""
+            items = feed(not waiting and not running)
+            if items is None:
+                return False
+            for rid, ids, sp in items:
+                if _filters(sp):
+                    if self.spec_k:
+                        raise NotImplementedError("top-k / top-p with speculative decoding")
+                    runner.filtering = True
+                waiting.append(_Req(rid, torch.as_tensor(ids, dtype=torch.int64), sp))
+            return True
+
+        feed_open = online
+        while waiting or running or feed_open:
+            if feed_open:
+                feed_open = pull()
+                if not (waiting or running):
+                    continue
             # ---- admission
             admitted: list[_Req] = []
             while waiting and free_slots:
@@ -363,7 +404,12 @@ class LLM:
                 L = r.prompt.numel()
                 total = L + r.params.max_tokens + (self.spec_k + 1 if self.spec_k else 0)
                 if total > runner.max_model_len:
-                    raise ValueError(f"request {r.rid}: {total} tokens > max_model_len")
+                    msg = f"request {r.rid}: {total} tokens > max_model_len"
+                    if not online:
+                        raise ValueError(msg)
+                    waiting.popleft()  # fail this request, keep serving the others
+                    on_finish(RequestOutput(r.rid, r.prompt.tolist(), [], True, error=msg))
+                    continue
                 nblk = math.ceil(total / bs)
                 pc = self.prefix_cache
                 hit = pc.lookup(r.prompt)[1] if pc is not None else []
@@ -385,7 +431,14 @@ class LLM:
                                     seed & 0x7FFFFFFFFFFFFFFF, r.params.top_k, r.params.top_p)
                 admitted.append(r)
             if not admitted and not running:
-                raise RuntimeError("cannot admit any request: KV cache too small")
+                if not waiting:  # (online) every new request was refused above
+                    continue
+                if not online:
+                    raise RuntimeError("cannot admit any request: KV cache too small")
+                r = waiting.popleft()
+                on_finish(RequestOutput(r.rid, r.prompt.tolist(), [], True,
+                                        error="KV cache too small for this request"))
+                continue
             # ---- chunked prefill of the admitted prompts
             queue = deque(admitted)
             while queue:
@@ -437,6 +490,8 @@ class LLM:
                     r.generated += int(n[r.slot])
                     stats.spec_tokens += int(n[r.slot])
                 stats.spec_slots += len(live)
+                if self.spec_hook is not None:
+                    self.spec_hook(len(live), sum(int(n[r.slot]) for r in live))
                 finished_now = [r for r in live if r.generated >= r.params.max_tokens]
                 if cuda and finished_now:
                     e = ev()
@@ -475,7 +530,13 @@ class LLM:
                     r.done = True
                     runner.alloc.free(r.blocks)
                     free_slots.append(r.slot)
+                    if on_finish is not None:
+                        on_finish(RequestOutput(r.rid, r.prompt.tolist(), r.out, True))
                 running = [r for r in running if not r.done]
+                if online:  # a long-lived session keeps no per-request records
+                    pending_first.clear()
+                    decode_events.clear()
+                    prefill_spans.clear()
         if self.ep is not None:  # serve the other ranks' MoE traffic until all are done
             self.model.ep_drain()
         if cuda:

@@ -28,3 +28,4 @@ class RequestOutput:
     finished: bool = True
     ttft_s: float | None = None
     tpot_s: float | None = None
+    error: str | None = None       # set when the request could not be served

@@ -5,8 +5,8 @@ time-per-output-token histograms, running / waiting gauges, prefix-cache
 queries and hits, and speculative-decoding acceptance counters.
 
 Each server owns its own ``CollectorRegistry`` (several apps can live in one
-process, e.g. in tests). Times come from the engine's device-event
-statistics of each batch (``LLM.last_stats``).
+process, e.g. in tests). Request times are host clock from submission to the
+first / last token of the continuous-batching engine loop.
 
 Reference parity: serving metrics are read from upstream vLLM's Prometheus
 ``/metrics`` by the reference's checks (``scripts/check6-lmcache-reaper.py``
@@ -54,34 +54,24 @@ class ServerMetrics:
                                      "Draft tokens accepted (emitted minus one per step).")
         self.spec_emitted = counter("vllm:spec_decode_num_emitted_tokens",
                                     "Tokens emitted by speculative steps.")
-        self.batches = counter("vllm_b200:engine_batches", "Engine generate calls.")
         self._pc_seen = (0, 0)
 
-    def batch_started(self, n: int, queued: int) -> None:
-        self.running.set(n)
-        self.waiting.set(queued)
+    def gauges(self, running: int, waiting: int) -> None:
+        self.running.set(running)
+        self.waiting.set(waiting)
 
-    def batch_finished(self, llm, prompts, params, outs) -> None:
-        """Account one finished ``generate`` call."""
-        self.batches.inc()
-        self.running.set(0)
-        for p, sp, o in zip(prompts, params, outs):
-            toks = o.output_token_ids
-            self.prompt_tokens.inc(len(p))
-            self.generation_tokens.inc(len(toks))
-            stopped = bool(toks) and toks[-1] in set(sp.stop_token_ids) and not sp.ignore_eos
-            self.requests.labels(model_name=self.model_name,
-                                 finished_reason="stop" if stopped else "length").inc()
-        st = getattr(llm, "last_stats", None)
-        if st is not None:
-            for ms in st.ttft_ms:
-                self.ttft.observe(ms / 1e3)
-            for ms in st.tpot_ms:
-                self.tpot.observe(ms / 1e3)
-            if st.spec_slots:
-                self.spec_drafts.inc(st.spec_slots)
-                self.spec_emitted.inc(st.spec_tokens)
-                self.spec_accepted.inc(max(0, st.spec_tokens - st.spec_slots))
+    def request_finished(self, llm, n_prompt: int, out, sp, ttft_s, tpot_s) -> None:
+        """Account one finished request (times: host clock from submission)."""
+        toks = out.output_token_ids
+        self.prompt_tokens.inc(n_prompt)
+        self.generation_tokens.inc(len(toks))
+        stopped = bool(toks) and toks[-1] in set(sp.stop_token_ids) and not sp.ignore_eos
+        self.requests.labels(model_name=self.model_name,
+                             finished_reason="stop" if stopped else "length").inc()
+        if ttft_s is not None:
+            self.ttft.observe(ttft_s)
+        if tpot_s is not None:
+            self.tpot.observe(tpot_s)
         pc = getattr(llm, "prefix_cache", None)
         if pc is not None:  # the cache counts blocks; export tokens
             q, h = pc.queries * pc.bs, pc.hits * pc.bs
@@ -89,6 +79,12 @@ class ServerMetrics:
             self.prefix_queries.inc(max(0, q - q0))
             self.prefix_hits.inc(max(0, h - h0))
             self._pc_seen = (q, h)
+
+    def spec_step(self, rows: int, emitted: int) -> None:
+        """Speculative decoding: ``rows`` rows stepped, ``emitted`` tokens."""
+        self.spec_drafts.inc(rows)
+        self.spec_emitted.inc(emitted)
+        self.spec_accepted.inc(max(0, emitted - rows))
 
     def exposition(self) -> bytes:
         return generate_latest(self.registry)

@@ -6,10 +6,10 @@
 
 Endpoints: ``GET /health``, ``GET /v1/models``, ``POST /v1/completions``,
 ``POST /v1/chat/completions``, ``POST /tokenize``, ``POST /detokenize`` and
-``GET /metrics`` (Prometheus, vLLM's metric names: ``entrypoints/metrics.py``). Requests are batched: a worker thread takes
-every request queued when it becomes free and runs them as one
-``LLM.generate`` call (chunked prefill + CUDA-graph decode across the batch);
-each handler awaits its own result. With a tokenizer, text prompts and chat
+``GET /metrics`` (Prometheus, vLLM's metric names: ``entrypoints/metrics.py``).
+Requests are continuously batched: one engine thread runs a long-lived
+``LLM.generate`` that admits each request as it arrives, next to the running
+ones, after the current decode burst; each handler awaits its own result. With a tokenizer, text prompts and chat
 messages (through the checkpoint's chat template) are accepted and the
 ``<think>`` / ``<tool_call>`` reasoning split is applied to chat replies
 (``--reasoning-parser glm47_b200``). Token-id prompts work without one.
@@ -42,95 +42,147 @@ STREAM_INTERVAL = 8  # decode steps per streamed chunk
 
 
 class Batcher:
-    """Collects requests from handler threads / coroutines and runs them in
-    batches on one worker thread (the engine is not re-entrant)."""
+    """Continuous batching: one engine thread runs a single long-lived
+    ``LLM.generate`` whose ``feed`` hands it the requests queued since its
+    last scheduler iteration, so a request that arrives while others decode
+    joins them after the current burst (at most ``STREAM_INTERVAL`` steps)
+    instead of waiting for them to finish. Under TP, rank 0's feed broadcasts
+    each iteration's new requests over the CPU group and the other ranks'
+    ``follower_loop`` feeds the same ones to their engines."""
 
     def __init__(self, llm, max_batch: int = 256, group=None, metrics=None):
         self.llm = llm
         self.max_batch = max_batch
-        self.group = group  # TP: the CPU group whose other ranks run follower_loop
+        self.group = group
         self.metrics = metrics
         self.q: queue.Queue = queue.Queue()
         self._stop = False
-        self.batches = 0
-        self.thread = threading.Thread(target=self._run, name="b200-batcher", daemon=True)
+        self._dead: BaseException | None = None
+        self._lock = threading.Lock()
+        self._next = 0
+        self.inflight: dict[int, dict] = {}
+        self.batches = 0  # scheduler iterations that admitted new requests
+        if metrics is not None:
+            llm.spec_hook = metrics.spec_step
+        self.thread = threading.Thread(target=self._run, name="b200-engine", daemon=True)
         self.thread.start()
 
     def submit(self, prompt_ids: list[int], params: SamplingParams,
                stream=None) -> concurrent.futures.Future:
         """Queue one request. ``stream(new_ids, finished)`` (optional) is called
-        from the worker thread as tokens are produced; ``new_ids`` is None if
-        the batch failed."""
+        from the engine thread as tokens are produced; ``new_ids`` is None if
+        the request failed."""
         fut: concurrent.futures.Future = concurrent.futures.Future()
-        self.q.put((prompt_ids, params, fut, stream))
+        if self._dead is not None:
+            fut.set_exception(RuntimeError(f"engine stopped: {self._dead}"))
+            return fut
+        with self._lock:
+            rid = self._next
+            self._next += 1
+        self.q.put((rid, list(prompt_ids), params, fut, stream))
         return fut
 
-    def _run(self) -> None:
-        import torch
-
-        while not self._stop:
-            try:
-                first = self.q.get(timeout=0.1)
-            except queue.Empty:
-                continue
-            items = [first]
-            while len(items) < self.max_batch:
-                try:
-                    items.append(self.q.get_nowait())
-                except queue.Empty:
-                    break
-            streams = [it[3] for it in items]
-            interval = STREAM_INTERVAL if any(streams) else 0
-            try:
-                batch = ([it[0] for it in items], [it[1] for it in items], interval)
-                if self.group is not None:  # every rank runs the same generate call
-                    import torch.distributed as dist
-
-                    dist.broadcast_object_list([batch], src=0, group=self.group)
-
-                def on_tokens(i, ids, fin):
-                    if streams[i] is not None:
-                        streams[i](ids, fin)
-                if self.metrics is not None:
-                    self.metrics.batch_started(len(items), self.q.qsize())
-                outs = self.llm.generate([torch.tensor(p, dtype=torch.int64) for p in batch[0]],
-                                         batch[1], on_tokens=on_tokens if interval else None,
-                                         stream_interval=interval)
-                self.batches += 1
-                if self.metrics is not None:
-                    self.metrics.batch_finished(self.llm, batch[0], batch[1], outs)
-                for it, o in zip(items, outs):
-                    it[2].set_result(o)
-            except Exception as e:  # noqa: BLE001 - reported to every waiting request
-                for _, _, fut, cb in items:
-                    if not fut.done():
-                        fut.set_exception(e)
-                    if cb is not None:
-                        cb(None, True)
-
-    def close(self) -> None:
-        self._stop = True
-        self.thread.join(timeout=2.0)
-        if self.group is not None:  # release the followers
+    # -- engine-thread callbacks ---------------------------------------------
+    def _bcast(self, obj):
+        if self.group is not None:
             import torch.distributed as dist
 
-            dist.broadcast_object_list([None], src=0, group=self.group)
+            dist.broadcast_object_list([obj], src=0, group=self.group)
+        return obj
+
+    def _feed(self, block: bool):
+        items = []
+        try:
+            if block:
+                while not self._stop and not items:
+                    try:
+                        items.append(self.q.get(timeout=0.05))
+                    except queue.Empty:
+                        pass
+            while len(items) < self.max_batch:
+                items.append(self.q.get_nowait())
+        except queue.Empty:
+            pass
+        if self._stop and not items:
+            return self._bcast(None)
+        now = time.perf_counter()
+        for rid, ids, sp, fut, cb in items:
+            self.inflight[rid] = {"fut": fut, "stream": cb, "sp": sp, "n_prompt": len(ids),
+                                  "t0": now, "t_first": None, "t_last": None}
+        if items:
+            self.batches += 1
+        if self.metrics is not None:
+            self.metrics.gauges(len(self.inflight), self.q.qsize())
+        return self._bcast([(rid, ids, sp) for rid, ids, sp, _, _ in items])
+
+    def _on_tokens(self, rid, ids, fin):
+        e = self.inflight.get(rid)
+        if e is None:
+            return
+        if ids:
+            t = time.perf_counter()
+            e["t_first"] = e["t_first"] or t
+            e["t_last"] = t
+        if e["stream"] is not None:
+            e["stream"](ids, fin)
+
+    def _on_finish(self, out):
+        e = self.inflight.pop(out.request_id, None)
+        if e is None:
+            return
+        if out.error is not None:
+            if e["stream"] is not None:
+                e["stream"](None, True)
+            e["fut"].set_exception(ValueError(out.error))
+            return
+        if self.metrics is not None:
+            n = len(out.output_token_ids)
+            ttft = e["t_first"] - e["t0"] if e["t_first"] else None
+            tpot = ((e["t_last"] - e["t_first"]) / (n - 1)
+                    if e["t_first"] and e["t_last"] and n > 1 else None)
+            self.metrics.request_finished(self.llm, e["n_prompt"], out, e["sp"], ttft, tpot)
+            self.metrics.gauges(len(self.inflight), self.q.qsize())
+        e["fut"].set_result(out)
+
+    def _run(self) -> None:
+        try:
+            self.llm.generate([], feed=self._feed, on_tokens=self._on_tokens,
+                              on_finish=self._on_finish, stream_interval=STREAM_INTERVAL)
+        except BaseException as exc:  # noqa: BLE001 - reported to every waiting request
+            self._dead = exc
+            pending = list(self.inflight.values())
+            self.inflight.clear()
+            while True:
+                try:
+                    _, _, _, fut, cb = self.q.get_nowait()
+                except queue.Empty:
+                    break
+                pending.append({"fut": fut, "stream": cb})
+            for e in pending:
+                if e["stream"] is not None:
+                    e["stream"](None, True)
+                if not e["fut"].done():
+                    e["fut"].set_exception(exc)
+
+    def close(self) -> None:
+        """Finish the running requests, then end the engine loop (under TP
+        this also releases the followers)."""
+        self._stop = True
+        self.thread.join(timeout=60.0)
 
 
 def follower_loop(llm, group) -> None:
-    """Ranks > 0 under TP: run every batch rank 0 broadcasts, until it sends
-    None (rank-uniform: the same generate calls in the same order)."""
-    import torch
+    """Ranks > 0 under TP: run rank 0's engine loop in lock step -- every
+    scheduler iteration takes the requests rank 0 broadcasts -- until rank 0
+    closes it."""
     import torch.distributed as dist
 
-    while True:
+    def feed(_block):
         obj = [None]
         dist.broadcast_object_list(obj, src=0, group=group)
-        if obj[0] is None:
-            return
-        prompts, params, interval = obj[0]
-        llm.generate([torch.tensor(p, dtype=torch.int64) for p in prompts], params,
-                     stream_interval=interval)
+        return obj[0]
+
+    llm.generate([], feed=feed, stream_interval=STREAM_INTERVAL)
 
 
 def _params(body: dict, tokenizer) -> SamplingParams:
