@@ -96,7 +96,8 @@ def test_stop_string_and_unsupported(client):
     r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8, "temperature": 0.0,
                                               "ignore_eos": True, "stop": ["\\u0000"]})
     assert r.status_code == 200
-    for bad in ({"n": 2}, {"logprobs": 1}, {"stream": True, "prompt": ["a", "b"]}):
+    for bad in ({"n": 2}, {"logprobs": 21}, {"logprobs": 1, "stream": True},
+                {"stream": True, "prompt": ["a", "b"]}):
         body = {"prompt": [1, 2, 3], "max_tokens": 2, **bad}
         assert client.post("/v1/completions", json=body).status_code == 400
 
@@ -211,3 +212,36 @@ def test_continuous_batching_late_short_request_overtakes():
     assert order == ["short", "long"] and b.batches >= 2
     b.close()
     assert not b.thread.is_alive()
+
+
+def test_completion_logprobs_and_echo(client):
+    """``logprobs`` / ``echo`` follow OpenAI's legacy completions format and
+    equal the engine's teacher-forced scores; ``max_tokens: 0`` with ``echo``
+    scores the prompt alone (what loglikelihood evaluations send)."""
+    ids = list(range(60, 72))
+    r = client.post("/v1/completions", json={"prompt": ids, "max_tokens": 4, "temperature": 0.0,
+                                             "ignore_eos": True, "logprobs": 2}).json()
+    lp = r["choices"][0]["logprobs"]
+    out = r["choices"][0]["token_ids"]
+    assert len(lp["tokens"]) == 4 and len(lp["token_logprobs"]) == 4
+    assert all(len(t) >= 2 for t in lp["top_logprobs"])
+    seq = torch.tensor(ids + out)
+    ref = client.llm.score([seq])[0]
+    assert all(abs(a - float(b)) < 1e-4 for a, b in zip(lp["token_logprobs"], ref[len(ids) - 1:]))
+    e = client.post("/v1/completions", json={"prompt": ids, "max_tokens": 0, "echo": True,
+                                             "logprobs": 0}).json()["choices"][0]
+    assert e["token_ids"] == [] and e["logprobs"]["token_logprobs"][0] is None
+    ref_p = client.llm.score([torch.tensor(ids)])[0]
+    got = e["logprobs"]["token_logprobs"][1:]
+    assert len(got) == len(ids) - 1 and all(abs(a - float(b)) < 1e-4 for a, b in zip(got, ref_p))
+
+
+def test_chat_logprobs(client):
+    r = client.post("/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "temperature": 0.0,
+        "ignore_eos": True, "logprobs": True, "top_logprobs": 2}).json()
+    content = r["choices"][0]["logprobs"]["content"]
+    assert len(content) == 3
+    for c in content:
+        assert c["logprob"] <= 0 and 1 <= len(c["top_logprobs"]) <= 2
+        assert c["top_logprobs"][0]["logprob"] >= c["logprob"] - 1e-6  # greedy = top-1

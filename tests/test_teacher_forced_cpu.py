@@ -90,3 +90,36 @@ def test_gate_passes_legit_runs_and_catches_mutations(cfg, mutations, monkeypatc
             bad = _llm(cfg, 48).score(_prompts())
         res = tf.gate(ref, bad, env, floor=1e-4)
         assert not res.passed, (mutate.__name__, res)
+
+
+def test_generate_logprobs_match_dense_reference():
+    """``SamplingParams(logprobs=N, prompt_logprobs=M)``: each output token
+    carries its log-prob and the top-N of the model's distribution, each
+    prompt token (after the first) its log-prob and the top-M -- equal to the
+    log-softmax of an independent dense forward; greedy tokens are their
+    position's top-1; requests without them are unchanged."""
+    from vllm_sm70_b200.engine import SamplingParams
+
+    llm = _llm(TINY, 32)
+    p = _prompts()[0][:40]
+    sp = SamplingParams(max_tokens=5, logprobs=3, prompt_logprobs=2)
+    o = llm.generate([p], sp)[0]
+    plain = llm.generate([p], SamplingParams(max_tokens=5))[0]
+    assert o.output_token_ids == plain.output_token_ids and plain.logprobs is None
+    seq = torch.cat([p, torch.tensor(o.output_token_ids)])
+    ref = torch.log_softmax(llama_logits(llm.model, seq), -1)       # [L, V]
+    Lp = p.numel()
+    assert len(o.logprobs) == 5 and len(o.prompt_logprobs) == Lp and o.prompt_logprobs[0] is None
+    for k, tok in enumerate(o.output_token_ids):
+        d, row = o.logprobs[k], ref[Lp - 1 + k]
+        assert abs(d[tok] - float(row[tok])) < 1e-4
+        top = row.topk(3).indices.tolist()
+        assert top[0] == tok and set(top) <= set(d)
+        assert all(abs(d[t] - float(row[t])) < 1e-4 for t in top)
+    for i in range(1, Lp):
+        d, row = o.prompt_logprobs[i], ref[i - 1]
+        assert abs(d[int(p[i])] - float(row[int(p[i])])) < 1e-4
+        assert set(row.topk(2).indices.tolist()) <= set(d)
+    echo = llm.generate([p], SamplingParams(max_tokens=0, prompt_logprobs=0))[0]
+    assert echo.output_token_ids == [] and len(echo.prompt_logprobs) == Lp
+    assert all(len(d) == 1 for d in echo.prompt_logprobs[1:])

@@ -60,7 +60,9 @@ class _Req:
     t_first: float | None = None
     t_last: float | None = None
     streamed: int = 0              # output tokens already handed to the stream callback
-    stream_stopped: bool = False   # a stop token was streamed: nothing more is
+    logprobs: list | None = None
+    prompt_logprobs: list | None = None
+    stream_stopped: bool = False   # a stop token was streamed: nothing more follows
 
 
 @dataclass
@@ -249,7 +251,7 @@ class LLM:
         """Teacher-forced log-probabilities (vLLM's ``prompt_logprobs``): for
         each prompt ``x`` of length L, ``lp[i] = log p(x[i+1] | x[:i+1])``
         for i < L - 1 (fp32, on the host). The prompt is prefilled in chunks
-        of ``max_num_batched_tokens`` into a scratch slot; the LM head and
+        of ``max_num_batched_tokens`` into scratch blocks; the LM head and
         log-softmax run on at most ``logits_rows`` rows at a time (the full
         vocabulary row of every token is not held at once). Call between
         ``generate`` calls (it uses batch slot 0)."""
@@ -257,40 +259,84 @@ class LLM:
             prompts = [row for row in prompt_token_ids.to(torch.int64)]
         else:
             prompts = [torch.as_tensor(p, dtype=torch.int64) for p in prompt_token_ids]
-        runner = self.runner
-        slot, out = 0, []
+        out = []
         for p in prompts:
-            L = p.numel()
-            if L > runner.max_model_len:
-                raise ValueError(f"prompt of {L} tokens > max_model_len")
-            nblk = math.ceil(L / runner.block_size)
-            if runner.alloc.num_free() < nblk and self.prefix_cache is not None:
-                self.prefix_cache.evict(nblk)
-            if runner.alloc.num_free() < nblk:
-                raise RuntimeError("KV cache too small to score the prompt")
-            blocks = runner.alloc.allocate(nblk)
-            runner.set_block_row(slot, blocks)
-            lp = torch.empty(max(L - 1, 0), dtype=torch.float32)
-            try:
-                pos = 0
-                while pos < L:
-                    n = min(self.max_num_batched_tokens, L - pos)
-                    h = runner.prefill_hidden([(slot, p[pos:pos + n], pos, False, L)])
-                    m = min(n, L - 1 - pos)  # rows that predict a prompt token
-                    for a in range(0, m, logits_rows):
-                        e = min(m, a + logits_rows)
-                        lg = self.model.logits(h[a:e]).float()
-                        tgt = p[pos + a + 1:pos + e + 1].to(lg.device)
-                        got = lg.gather(1, tgt[:, None]).squeeze(1) - torch.logsumexp(lg, 1)
-                        lp[pos + a:pos + e] = got.cpu()
-                    pos += n
-            finally:
-                runner.alloc.free(blocks)
-                runner.deactivate([slot])
-            out.append(lp)
+            if p.numel() > self.runner.max_model_len:
+                raise ValueError(f"prompt of {p.numel()} tokens > max_model_len")
+            out.append(self._score_seq(0, p, 0, logits_rows)[0])
         if self.ep is not None:
             self.model.ep_drain()
         return out
+
+    def _score_seq(self, slot: int, seq: torch.Tensor, top_n: int = 0,
+                   logits_rows: int = 1024):
+        """Teacher-forced pass over ``seq`` through batch slot ``slot`` (which
+        must be idle) on freshly allocated blocks, so no block another request
+        or the prefix cache holds is rewritten. Returns (lp ``[L-1]``, top ids
+        ``[L-1, top_n]``, top log-probs) -- the last two None when top_n is
+        0 -- of the model's raw distribution (no temperature / top-k)."""
+        runner = self.runner
+        L = seq.numel()
+        nblk = math.ceil(L / runner.block_size)
+        if runner.alloc.num_free() < nblk and self.prefix_cache is not None:
+            self.prefix_cache.evict(nblk)
+        if runner.alloc.num_free() < nblk:
+            raise RuntimeError("KV cache too small to score the sequence")
+        blocks = runner.alloc.allocate(nblk)
+        runner.set_block_row(slot, blocks)
+        lp = torch.empty(max(L - 1, 0), dtype=torch.float32)
+        tids = torch.empty(max(L - 1, 0), top_n, dtype=torch.int64) if top_n else None
+        tlp = torch.empty(max(L - 1, 0), top_n, dtype=torch.float32) if top_n else None
+        try:
+            pos = 0
+            while pos < L:
+                n = min(self.max_num_batched_tokens, L - pos)
+                h = runner.prefill_hidden([(slot, seq[pos:pos + n], pos, False, L)])
+                m = min(n, L - 1 - pos)  # rows that predict a token of seq
+                for a in range(0, m, logits_rows):
+                    e = min(m, a + logits_rows)
+                    lg = self.model.logits(h[a:e]).float()
+                    lsm = lg - torch.logsumexp(lg, 1, keepdim=True)
+                    tgt = seq[pos + a + 1:pos + e + 1].to(lg.device)
+                    lp[pos + a:pos + e] = lsm.gather(1, tgt[:, None]).squeeze(1).cpu()
+                    if top_n:
+                        v, i = lsm.topk(top_n, dim=1)
+                        tids[pos + a:pos + e] = i.cpu()
+                        tlp[pos + a:pos + e] = v.cpu()
+                pos += n
+        finally:
+            runner.alloc.free(blocks)
+            runner.deactivate([slot])
+        return lp, tids, tlp
+
+    @staticmethod
+    def _output(r: "_Req") -> RequestOutput:
+        return RequestOutput(r.rid, r.prompt.tolist(), r.out, True, logprobs=r.logprobs,
+                             prompt_logprobs=r.prompt_logprobs)
+
+    def _logprobs_of(self, r: "_Req") -> tuple[list | None, list | None]:
+        """(output, prompt) log-prob lists of a finished request that asked
+        for them: one ``{token id: log-prob}`` per token with the chosen token
+        and the top-N."""
+        sp = r.params
+        top = max(sp.logprobs or 0, sp.prompt_logprobs or 0)
+        seq = torch.cat([r.prompt, torch.tensor(r.out, dtype=torch.int64)])
+        lp, tids, tlp = self._score_seq(r.slot, seq, top)
+        Lp = r.prompt.numel()
+
+        def entry(i: int, n: int) -> dict:  # token seq[i + 1]
+            d = {int(seq[i + 1]): float(lp[i])}
+            for j in range(n):
+                d.setdefault(int(tids[i, j]), float(tlp[i, j]))
+            return d
+
+        out = None
+        if sp.logprobs is not None:
+            out = [entry(Lp - 1 + k, sp.logprobs) for k in range(len(r.out))]
+        prompt = None
+        if sp.prompt_logprobs is not None:
+            prompt = [None] + [entry(i, sp.prompt_logprobs) for i in range(Lp - 1)]
+        return out, prompt
 
     def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
                  collect_stats: bool = True, on_tokens=None,
@@ -529,9 +575,11 @@ class LLM:
                     r.out = _truncate_at_stop(row[: r.params.max_tokens].tolist(), r.params)
                     r.done = True
                     runner.alloc.free(r.blocks)
+                    if r.params.logprobs is not None or r.params.prompt_logprobs is not None:
+                        r.logprobs, r.prompt_logprobs = self._logprobs_of(r)
                     free_slots.append(r.slot)
                     if on_finish is not None:
-                        on_finish(RequestOutput(r.rid, r.prompt.tolist(), r.out, True))
+                        on_finish(self._output(r))
                 running = [r for r in running if not r.done]
                 if online:  # a long-lived session keeps no per-request records
                     pending_first.clear()
@@ -562,8 +610,9 @@ class LLM:
                 stats.ttft_ms.append(r.t_first)
                 if r.t_last is not None and len(r.out) > 1:
                     stats.tpot_ms.append((r.t_last - r.t_first) / (len(r.out) - 1))
-            outs.append(RequestOutput(r.rid, r.prompt.tolist(), r.out, True,
-                                      None if r.t_first is None else r.t_first / 1e3,
-                                      None if not stats.tpot_ms else stats.tpot_ms[-1] / 1e3))
+            o = self._output(r)
+            o.ttft_s = None if r.t_first is None else r.t_first / 1e3
+            o.tpot_s = None if not stats.tpot_ms else stats.tpot_ms[-1] / 1e3
+            outs.append(o)
         self.last_stats = stats
         return outs

@@ -14,6 +14,8 @@ class SamplingParams:
     seed: int | None = None
     ignore_eos: bool = False
     stop_token_ids: list[int] = field(default_factory=list)
+    logprobs: int | None = None          # per output token: its log-prob + the top-N
+    prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 
     @property
     def greedy(self) -> bool:
@@ -29,3 +31,7 @@ class RequestOutput:
     ttft_s: float | None = None
     tpot_s: float | None = None
     error: str | None = None       # set when the request could not be served
+    # {token id: log-prob} per output / prompt token (the chosen token and the
+    # top-N of the model's raw distribution); None when not requested
+    logprobs: list | None = None
+    prompt_logprobs: list | None = None

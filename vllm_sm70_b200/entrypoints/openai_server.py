@@ -18,8 +18,12 @@ Streaming (``"stream": true``): server-sent events, one chunk per decode
 burst of at most ``STREAM_INTERVAL`` steps (text deltas from the cumulative
 decode, so multi-token characters are not split), then ``data: [DONE]``.
 
-Scope: n = 1, no log-probabilities (requests asking for them get HTTP 400);
-sampling is greedy, temperature (Gumbel-max, seeded) or temperature with
+Log-probabilities: completions ``logprobs`` (top-N, up to 20) and ``echo``
+(prompt log-probs too, also with ``max_tokens: 0`` for scoring); chat
+``logprobs`` / ``top_logprobs``. They are the model's raw distribution, from
+a teacher-forced pass when the request finishes, and are not streamed.
+
+Scope: n = 1; sampling is greedy, temperature (Gumbel-max, seeded) or temperature with
 top-k / top-p (over the top-64 candidates of each vocab shard).
 
 Reference parity: the reference is served through ``vllm serve`` with its
@@ -185,18 +189,35 @@ def follower_loop(llm, group) -> None:
     llm.generate([], feed=feed, stream_interval=STREAM_INTERVAL)
 
 
-def _params(body: dict, tokenizer) -> SamplingParams:
+MAX_LOGPROBS = 20
+
+
+def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
+    """SamplingParams of a request body. Log-probs: completions take
+    ``logprobs`` (top-N, OpenAI's legacy form) and ``echo`` (the prompt's
+    too); chat takes ``logprobs: true`` with ``top_logprobs``."""
     if int(body.get("n", 1)) != 1:
         raise ValueError("only n = 1 is served")
-    if body.get("logprobs"):
-        raise ValueError("log-probabilities are not served")
+    if chat:
+        n_lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
+        prompt_lp = None
+    else:
+        n_lp = body.get("logprobs")
+        n_lp = None if n_lp is None or n_lp is False else int(n_lp)
+        prompt_lp = (n_lp or 0) if body.get("echo") else None
+    if n_lp is not None and not 0 <= n_lp <= MAX_LOGPROBS:
+        raise ValueError(f"logprobs must be in [0, {MAX_LOGPROBS}]")
+    if (n_lp is not None or prompt_lp is not None) and body.get("stream"):
+        raise ValueError("log-probabilities are not streamed")
     stop_ids = list(body.get("stop_token_ids") or [])
     ignore_eos = bool(body.get("ignore_eos", False))
     eos = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
     if eos is not None and not ignore_eos:
         stop_ids.append(int(eos))
     top_k = body.get("top_k")
-    return SamplingParams(max_tokens=int(body.get("max_tokens") or 16),
+    mt = body.get("max_tokens")
+    return SamplingParams(max_tokens=16 if mt is None else int(mt),
+                          logprobs=n_lp, prompt_logprobs=prompt_lp,
                           temperature=float(body.get("temperature", 1.0)),
                           top_k=int(top_k) if top_k is not None else -1,
                           top_p=float(body.get("top_p", 1.0)),
@@ -267,6 +288,24 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
 
     def decode(ids):
         return tokenizer.decode(ids, skip_special_tokens=True) if tokenizer is not None else None
+
+    def tok_str(i: int) -> str:
+        return (tokenizer.decode([i], skip_special_tokens=False) if tokenizer is not None
+                else f"token_id:{i}")
+
+    def completion_logprobs(ids, entries, offset0: int) -> dict:
+        """OpenAI's legacy completions ``logprobs`` object for token ``ids``
+        with engine entries ``{id: log-prob}`` (None for a first prompt token)."""
+        toks, lps, tops, offs = [], [], [], []
+        off = offset0
+        for i, d in zip(ids, entries):
+            s_ = tok_str(i)
+            toks.append(s_)
+            offs.append(off)
+            off += len(s_)
+            lps.append(None if d is None else d[i])
+            tops.append(None if d is None else {tok_str(k): v for k, v in d.items()})
+        return {"tokens": toks, "token_logprobs": lps, "top_logprobs": tops, "text_offset": offs}
 
     async def run(prompt_ids, sp):
         fut = batcher.submit(prompt_ids, sp)
@@ -362,7 +401,11 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             if len(ids) != 1:
                 raise HTTPException(400, "streaming serves one prompt per request")
             return stream_completion(ids[0], sp, body.get("stop"))
-        outs = await asyncio.gather(*[run(p, sp) for p in ids])
+        try:
+            outs = await asyncio.gather(*[run(p, sp) for p in ids])
+        except ValueError as e:  # a request the engine could not serve
+            raise HTTPException(400, str(e)) from e
+        echo = bool(body.get("echo"))
         choices, n_out = [], 0
         for i, o in enumerate(outs):
             text = decode(o.output_token_ids)
@@ -372,8 +415,22 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 text, hit = _apply_stop_strings(text, body.get("stop"))
                 stopped = stopped or hit
             n_out += len(o.output_token_ids)
-            choices.append({"index": i, "text": text, "token_ids": o.output_token_ids,
-                            "finish_reason": "stop" if stopped else "length"})
+            ch = {"index": i, "text": text, "token_ids": o.output_token_ids,
+                  "finish_reason": "stop" if stopped else "length", "logprobs": None}
+            if echo:
+                ptext = decode(ids[i])
+                ch["text"] = (ptext or "") + (text or "") if tokenizer is not None else None
+                ch["prompt_token_ids"] = ids[i]
+            if sp.logprobs is not None or echo and sp.prompt_logprobs is not None:
+                lp_ids, lp_entries = [], []
+                if echo:
+                    lp_ids += ids[i]
+                    lp_entries += o.prompt_logprobs or [None] * len(ids[i])
+                if sp.logprobs is not None:
+                    lp_ids += o.output_token_ids
+                    lp_entries += o.logprobs or []
+                ch["logprobs"] = completion_logprobs(lp_ids, lp_entries, 0)
+            choices.append(ch)
         return {"id": f"cmpl-{uuid.uuid4().hex}", "object": "text_completion", "created":
                 int(time.time()), "model": model_name, "choices": choices,
                 "usage": {"prompt_tokens": sum(len(p) for p in ids), "completion_tokens": n_out,
@@ -433,7 +490,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         if tokenizer is None or not hasattr(tokenizer, "apply_chat_template"):
             raise HTTPException(400, "chat needs a tokenizer with a chat template")
         try:
-            sp = _params(body, tokenizer)
+            sp = _params(body, tokenizer, chat=True)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         kwargs = body.get("chat_template_kwargs") or {}
@@ -441,7 +498,10 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                                                  tokenize=True, **kwargs))
         if body.get("stream"):
             return stream_chat(ids, sp, kwargs, body.get("stop"))
-        o = await run(ids, sp)
+        try:
+            o = await run(ids, sp)
+        except ValueError as e:  # a request the engine could not serve
+            raise HTTPException(400, str(e)) from e
         raw = tokenizer.decode(o.output_token_ids, skip_special_tokens=False)
         last = o.output_token_ids[-1] if o.output_token_ids else None
         stopped = last is not None and last in sp.stop_token_ids
@@ -458,9 +518,18 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             content = content[: -len(eos_text)]
         content, hit = _apply_stop_strings(content, body.get("stop"))
         msg["content"] = content
+        logprobs = None
+        if sp.logprobs is not None:
+            def item(tok, lp):
+                s_ = tok_str(tok)
+                return {"token": s_, "logprob": lp, "bytes": list(s_.encode())}
+            logprobs = {"content": [
+                dict(item(t, d[t]), top_logprobs=[item(k, v) for k, v in sorted(
+                    d.items(), key=lambda kv: -kv[1])[: sp.logprobs]])
+                for t, d in zip(o.output_token_ids, o.logprobs or [])]}
         return {"id": f"chatcmpl-{uuid.uuid4().hex}", "object": "chat.completion",
                 "created": int(time.time()), "model": model_name,
-                "choices": [{"index": 0, "message": msg,
+                "choices": [{"index": 0, "message": msg, "logprobs": logprobs,
                              "finish_reason": "stop" if (stopped or hit) else "length"}],
                 "usage": {"prompt_tokens": len(ids),
                           "completion_tokens": len(o.output_token_ids),
