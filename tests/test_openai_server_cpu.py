@@ -96,7 +96,8 @@ def test_stop_string_and_unsupported(client):
     r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8, "temperature": 0.0,
                                               "ignore_eos": True, "stop": ["\\u0000"]})
     assert r.status_code == 200
-    for bad in ({"n": 2}, {"logprobs": 21}, {"logprobs": 1, "stream": True},
+    for bad in ({"n": 17}, {"n": 2, "stream": True}, {"logprobs": 21},
+                {"logprobs": 1, "stream": True},
                 {"stream": True, "prompt": ["a", "b"]}):
         body = {"prompt": [1, 2, 3], "max_tokens": 2, **bad}
         assert client.post("/v1/completions", json=body).status_code == 400
@@ -245,3 +246,21 @@ def test_chat_logprobs(client):
     for c in content:
         assert c["logprob"] <= 0 and 1 <= len(c["top_logprobs"]) <= 2
         assert c["top_logprobs"][0]["logprob"] >= c["logprob"] - 1e-6  # greedy = top-1
+
+
+def test_n_samples(client):
+    """``n`` samples per prompt: greedy ones agree, seeded temperature ones
+    differ from one another and repeat with the same seed."""
+    body = {"prompt": list(range(20, 30)), "max_tokens": 6, "ignore_eos": True, "n": 3}
+    g = client.post("/v1/completions", json={**body, "temperature": 0.0}).json()["choices"]
+    assert [c["index"] for c in g] == [0, 1, 2]
+    assert g[0]["token_ids"] == g[1]["token_ids"] == g[2]["token_ids"]
+    t = {**body, "temperature": 1.5, "seed": 7}
+    a = [c["token_ids"] for c in client.post("/v1/completions", json=t).json()["choices"]]
+    b = [c["token_ids"] for c in client.post("/v1/completions", json=t).json()["choices"]]
+    assert a == b and len({tuple(x) for x in a}) > 1
+    c = client.post("/v1/chat/completions", json={
+        "messages": [{"role": "user", "content": "yo"}], "max_tokens": 3, "temperature": 0.0,
+        "ignore_eos": True, "n": 2}).json()
+    assert [ch["index"] for ch in c["choices"]] == [0, 1]
+    assert c["usage"]["completion_tokens"] == 6

@@ -23,7 +23,7 @@ Log-probabilities: completions ``logprobs`` (top-N, up to 20) and ``echo``
 ``logprobs`` / ``top_logprobs``. They are the model's raw distribution, from
 a teacher-forced pass when the request finishes, and are not streamed.
 
-Scope: n = 1; sampling is greedy, temperature (Gumbel-max, seeded) or temperature with
+Scope: ``n`` samples per prompt (up to 16; one when streaming); sampling is greedy, temperature (Gumbel-max, seeded) or temperature with
 top-k / top-p (over the top-64 candidates of each vocab shard).
 
 Reference parity: the reference is served through ``vllm serve`` with its
@@ -190,14 +190,29 @@ def follower_loop(llm, group) -> None:
 
 
 MAX_LOGPROBS = 20
+MAX_N = 16
+
+
+def _samples(sp: SamplingParams, n: int) -> list[SamplingParams]:
+    """The ``n`` requests of one prompt: distinct sampling seeds (the given
+    seed + i, or the engine's per-request default)."""
+    import dataclasses
+
+    if n == 1:
+        return [sp]
+    return [dataclasses.replace(sp, seed=None if sp.seed is None else int(sp.seed) + i)
+            for i in range(n)]
 
 
 def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
     """SamplingParams of a request body. Log-probs: completions take
     ``logprobs`` (top-N, OpenAI's legacy form) and ``echo`` (the prompt's
     too); chat takes ``logprobs: true`` with ``top_logprobs``."""
-    if int(body.get("n", 1)) != 1:
-        raise ValueError("only n = 1 is served")
+    n = int(body.get("n", 1))
+    if not 1 <= n <= MAX_N:
+        raise ValueError(f"n must be in [1, {MAX_N}]")
+    if n > 1 and body.get("stream"):
+        raise ValueError("streaming serves n = 1")
     if chat:
         n_lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
         prompt_lp = None
@@ -401,13 +416,15 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             if len(ids) != 1:
                 raise HTTPException(400, "streaming serves one prompt per request")
             return stream_completion(ids[0], sp, body.get("stop"))
+        n = int(body.get("n", 1))
+        jobs = [(pi, spj) for pi in range(len(ids)) for spj in _samples(sp, n)]
         try:
-            outs = await asyncio.gather(*[run(p, sp) for p in ids])
+            outs = await asyncio.gather(*[run(ids[pi], spj) for pi, spj in jobs])
         except ValueError as e:  # a request the engine could not serve
             raise HTTPException(400, str(e)) from e
         echo = bool(body.get("echo"))
         choices, n_out = [], 0
-        for i, o in enumerate(outs):
+        for k, ((i, _), o) in enumerate(zip(jobs, outs)):
             text = decode(o.output_token_ids)
             last = o.output_token_ids[-1] if o.output_token_ids else None
             stopped = last is not None and last in sp.stop_token_ids
@@ -415,7 +432,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 text, hit = _apply_stop_strings(text, body.get("stop"))
                 stopped = stopped or hit
             n_out += len(o.output_token_ids)
-            ch = {"index": i, "text": text, "token_ids": o.output_token_ids,
+            ch = {"index": k, "text": text, "token_ids": o.output_token_ids,
                   "finish_reason": "stop" if stopped else "length", "logprobs": None}
             if echo:
                 ptext = decode(ids[i])
@@ -499,9 +516,18 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         if body.get("stream"):
             return stream_chat(ids, sp, kwargs, body.get("stop"))
         try:
-            o = await run(ids, sp)
+            outs = await asyncio.gather(*[run(ids, spj)
+                                          for spj in _samples(sp, int(body.get("n", 1)))])
         except ValueError as e:  # a request the engine could not serve
             raise HTTPException(400, str(e)) from e
+        choices = [chat_choice(k, o, sp, kwargs, body.get("stop")) for k, o in enumerate(outs)]
+        n_out = sum(len(o.output_token_ids) for o in outs)
+        return {"id": f"chatcmpl-{uuid.uuid4().hex}", "object": "chat.completion",
+                "created": int(time.time()), "model": model_name, "choices": choices,
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out,
+                          "total_tokens": len(ids) + n_out}}
+
+    def chat_choice(index, o, sp, kwargs, stop) -> dict:
         raw = tokenizer.decode(o.output_token_ids, skip_special_tokens=False)
         last = o.output_token_ids[-1] if o.output_token_ids else None
         stopped = last is not None and last in sp.stop_token_ids
@@ -516,7 +542,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         eos_text = getattr(tokenizer, "eos_token", None)
         if eos_text and content.endswith(eos_text):
             content = content[: -len(eos_text)]
-        content, hit = _apply_stop_strings(content, body.get("stop"))
+        content, hit = _apply_stop_strings(content, stop)
         msg["content"] = content
         logprobs = None
         if sp.logprobs is not None:
@@ -527,13 +553,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 dict(item(t, d[t]), top_logprobs=[item(k, v) for k, v in sorted(
                     d.items(), key=lambda kv: -kv[1])[: sp.logprobs]])
                 for t, d in zip(o.output_token_ids, o.logprobs or [])]}
-        return {"id": f"chatcmpl-{uuid.uuid4().hex}", "object": "chat.completion",
-                "created": int(time.time()), "model": model_name,
-                "choices": [{"index": 0, "message": msg, "logprobs": logprobs,
-                             "finish_reason": "stop" if (stopped or hit) else "length"}],
-                "usage": {"prompt_tokens": len(ids),
-                          "completion_tokens": len(o.output_token_ids),
-                          "total_tokens": len(ids) + len(o.output_token_ids)}}
+        return {"index": index, "message": msg, "logprobs": logprobs,
+                "finish_reason": "stop" if (stopped or hit) else "length"}
 
     return app
 

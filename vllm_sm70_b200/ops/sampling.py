@@ -73,10 +73,19 @@ def gumbel_sample(logits: torch.Tensor, temperature: torch.Tensor, seeds: torch.
     ids = torch.empty(rows, dtype=torch.int32, device=logits.device)
     vals = torch.empty(rows, dtype=torch.float32, device=logits.device)
     if not logits.is_cuda:
+        # noise keyed like the kernel's: per row by (seed, output position,
+        # offset), per column by the GLOBAL token id -- so a request's samples
+        # do not depend on its batch row, and vocab shards merge exactly
         x = logits.float()
         t = temperature.float()[:, None]
-        g = torch.Generator().manual_seed(int(offset))
-        u = torch.rand(x.shape, generator=g).clamp(1e-12, 1 - 1e-7)
+        V = x.shape[1]
+        u = torch.empty_like(x)
+        for r in range(rows):
+            pos = int(row_offsets[r]) if row_offsets is not None else 0
+            key = (int(seeds[r]) * 1000003 + pos * 7919 + int(offset)) & 0x7FFFFFFFFFFFFFFF
+            g = torch.Generator().manual_seed(key)
+            u[r] = torch.rand(id_offset + V, generator=g)[id_offset:]
+        u = u.clamp(1e-12, 1 - 1e-7)
         pert = torch.where(t > 0, x / t.clamp_min(1e-6) - torch.log(-torch.log(u)), x)
         vals.copy_(pert.max(-1).values)
         ids.copy_(pert.argmax(-1).to(torch.int32) + id_offset)
