@@ -12,7 +12,10 @@ Requests are continuously batched: one engine thread runs a long-lived
 ones, after the current decode burst; each handler awaits its own result. With a tokenizer, text prompts and chat
 messages (through the checkpoint's chat template) are accepted and the
 ``<think>`` / ``<tool_call>`` reasoning split is applied to chat replies
-(``--reasoning-parser glm47_b200``). Token-id prompts work without one.
+(``--reasoning-parser glm47_b200``); when a chat request offers ``tools``,
+they reach the chat template and ``<tool_call>`` blocks in the reply become
+OpenAI ``tool_calls`` (``integration/tool_calls.py``). Token-id prompts work
+without a tokenizer.
 
 Streaming (``"stream": true``): server-sent events, one chunk per decode
 burst of at most ``STREAM_INTERVAL`` steps (text deltas from the cumulative
@@ -511,8 +514,10 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         kwargs = body.get("chat_template_kwargs") or {}
+        tools = body.get("tools") if body.get("tool_choice", "auto") != "none" else None
+        tpl = dict(kwargs, tools=tools) if tools else kwargs
         ids = list(tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True,
-                                                 tokenize=True, **kwargs))
+                                                 tokenize=True, **tpl))
         if body.get("stream"):
             return stream_chat(ids, sp, kwargs, body.get("stop"))
         try:
@@ -520,14 +525,15 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                                           for spj in _samples(sp, int(body.get("n", 1)))])
         except ValueError as e:  # a request the engine could not serve
             raise HTTPException(400, str(e)) from e
-        choices = [chat_choice(k, o, sp, kwargs, body.get("stop")) for k, o in enumerate(outs)]
+        choices = [chat_choice(k, o, sp, kwargs, body.get("stop"), bool(tools))
+                   for k, o in enumerate(outs)]
         n_out = sum(len(o.output_token_ids) for o in outs)
         return {"id": f"chatcmpl-{uuid.uuid4().hex}", "object": "chat.completion",
                 "created": int(time.time()), "model": model_name, "choices": choices,
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out,
                           "total_tokens": len(ids) + n_out}}
 
-    def chat_choice(index, o, sp, kwargs, stop) -> dict:
+    def chat_choice(index, o, sp, kwargs, stop, tools=False) -> dict:
         raw = tokenizer.decode(o.output_token_ids, skip_special_tokens=False)
         last = o.output_token_ids[-1] if o.output_token_ids else None
         stopped = last is not None and last in sp.stop_token_ids
@@ -544,6 +550,14 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             content = content[: -len(eos_text)]
         content, hit = _apply_stop_strings(content, stop)
         msg["content"] = content
+        finish = "stop" if (stopped or hit) else "length"
+        if tools:  # the request offered tools: <tool_call> blocks become tool_calls
+            from ..integration.tool_calls import parse_tool_calls
+
+            rest, calls = parse_tool_calls(content)
+            if calls:
+                msg["content"], msg["tool_calls"] = rest, calls
+                finish = "tool_calls"
         logprobs = None
         if sp.logprobs is not None:
             def item(tok, lp):
@@ -553,8 +567,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 dict(item(t, d[t]), top_logprobs=[item(k, v) for k, v in sorted(
                     d.items(), key=lambda kv: -kv[1])[: sp.logprobs]])
                 for t, d in zip(o.output_token_ids, o.logprobs or [])]}
-        return {"index": index, "message": msg, "logprobs": logprobs,
-                "finish_reason": "stop" if (stopped or hit) else "length"}
+        return {"index": index, "message": msg, "logprobs": logprobs, "finish_reason": finish}
 
     return app
 
