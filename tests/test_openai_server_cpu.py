@@ -264,3 +264,34 @@ def test_n_samples(client):
         "ignore_eos": True, "n": 2}).json()
     assert [ch["index"] for ch in c["choices"]] == [0, 1]
     assert c["usage"]["completion_tokens"] == 6
+
+
+def test_cli_builds_engine_and_app(tmp_path, monkeypatch):
+    """``python -m vllm_sm70_b200.entrypoints.openai_server`` flags reach the
+    engine (here: dummy weights of a checkpoint config, prefix cache with a
+    disk tier, eager) and the app is handed to uvicorn."""
+    import json as _json
+
+    import uvicorn
+
+    from vllm_sm70_b200.entrypoints import openai_server as srv
+
+    from .test_loader_cpu import _hf_config
+
+    (tmp_path / "config.json").write_text(_json.dumps(_hf_config(TINY)))
+    seen = {}
+    monkeypatch.setattr(uvicorn, "run", lambda app, host, port: seen.update(app=app, port=port))
+    built = {}
+    real = srv.build_app
+
+    def spy(llm, *a, **k):
+        built["llm"] = llm
+        return real(llm, *a, **k)
+    monkeypatch.setattr(srv, "build_app", spy)
+    srv.main(["--model", str(tmp_path), "--load-format", "dummy", "--port", "8123",
+              "--max-num-seqs", "2", "--max-model-len", "64", "--enforce-eager",
+              "--prefix-cache-dir", str(tmp_path / "kv"), "--max-num-batched-tokens", "64"])
+    llm = built["llm"]
+    assert seen["port"] == 8123 and llm.prefix_cache is not None
+    assert llm.prefix_cache.disk is not None and not llm.runner.use_graphs
+    seen["app"].state.batcher.close()

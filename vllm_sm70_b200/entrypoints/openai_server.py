@@ -585,6 +585,15 @@ def main(argv=None) -> None:
     ap.add_argument("--max-num-batched-tokens", type=int, default=16384)
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--enable-prefix-caching", action="store_true")
+    ap.add_argument("--prefix-cache-dir", default=None,
+                    help="persistent KV tier of the prefix cache (implies prefix caching)")
+    ap.add_argument("--gpu-memory-utilization", type=float, default=0.90)
+    ap.add_argument("--enforce-eager", action="store_true", help="no CUDA-graph decode")
+    ap.add_argument("--speculative-k", type=int, default=0,
+                    help="draft tokens per step from the model's MTP head (0 = off)")
+    ap.add_argument("--seed", type=int, default=0, help="dummy-weight seed")
+    ap.add_argument("--gemm-lut", default=None, help="tuned GEMM plan table to import")
+    ap.add_argument("--tokenizer", default=None, help="tokenizer directory (default: --model)")
     ap.add_argument("--reasoning-parser", default=None, choices=[None, "glm47_b200"])
     args = ap.parse_args(argv)
 
@@ -594,13 +603,18 @@ def main(argv=None) -> None:
     llm = LLM(args.model, tensor_parallel_size=args.tensor_parallel_size,
               max_num_seqs=args.max_num_seqs, max_model_len=args.max_model_len,
               max_num_batched_tokens=args.max_num_batched_tokens, block_size=args.block_size,
-              load_format=args.load_format, enable_prefix_caching=args.enable_prefix_caching)
+              load_format=args.load_format,
+              enable_prefix_caching=args.enable_prefix_caching or bool(args.prefix_cache_dir),
+              prefix_cache_dir=args.prefix_cache_dir,
+              gpu_memory_utilization=args.gpu_memory_utilization,
+              enforce_eager=args.enforce_eager, speculative_k=args.speculative_k,
+              seed=args.seed, gemm_lut_path=args.gemm_lut)
     tok = None
-    if args.load_format == "safetensors":
+    if args.load_format == "safetensors" or args.tokenizer:
         try:
             from transformers import AutoTokenizer
 
-            tok = AutoTokenizer.from_pretrained(args.model)
+            tok = AutoTokenizer.from_pretrained(args.tokenizer or args.model)
         except Exception:  # noqa: BLE001 - token-id prompts still work
             tok = None
     ps = pstate.get()
