@@ -37,7 +37,7 @@ N_REQ, PROMPT, OUT = 256, 1024, 256  # the headline workload; --requests/--promp
 BASELINE_VALUE = None  # no published number exists for this config
 PRESET, TEMPERATURE, SPEC_K = "llama-3.1-8b", 0.0, 0
 
-# The other BASELINE configurations (--config): preset, workload, sampling.
+# The other benchmark configurations of this project (--config): preset, workload, sampling.
 WORKLOADS = {
     "llama-3.1-8b": dict(preset="llama-3.1-8b", model=MODEL, requests=256, prompt=1024,
                          output=256, temperature=0.0, spec_k=0),
@@ -349,7 +349,7 @@ def main(argv=None):
     ap.add_argument("--output-len", type=int, default=None, help="profiling only")
     ap.add_argument("--verbose", action="store_true", help="log engine set-up (GEMM plans)")
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="llama-3.1-8b",
-                    help="BASELINE configuration (default: the headline Llama-3.1-8B workload)")
+                    help="benchmark configuration (default: the headline Llama-3.1-8B workload)")
     ap.add_argument("--layout", choices=["tp", "dp-ep"], default="tp",
                     help="N > 1: tensor parallel (MoE experts sliced over the TP group), or "
                          "data-parallel attention with all-to-all expert parallelism")
