@@ -264,3 +264,32 @@ def test_continuous_batching_feed():
     assert [done[i].output_token_ids for i in range(5)] == ref
     assert done[99].error and done[99].output_token_ids == []
     assert all(done[i].error is None for i in range(5))
+
+
+def test_text_prompts_and_chat_with_tokenizer():
+    """With a tokenizer, ``generate`` takes text prompts and fills
+    ``RequestOutput.text``; ``chat`` applies the chat template; without one,
+    text prompts are refused with a clear error."""
+    import pytest
+
+    class Tok:
+        def encode(self, text):
+            return [ord(c) % 500 + 1 for c in text]
+
+        def decode(self, ids, skip_special_tokens=True):
+            return "".join(chr(65 + i % 26) for i in ids)
+
+        def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=True, **kw):
+            return self.encode("".join(m["content"] for m in messages) + "|a:")
+
+    sp = SamplingParams(max_tokens=4)
+    llm = _llm(tokenizer=Tok())
+    o = llm.generate(["hello there"], sp)[0]
+    ids_o = llm.generate([Tok().encode("hello there")], sp)[0]
+    assert o.output_token_ids == ids_o.output_token_ids and o.text == Tok().decode(o.output_token_ids)
+    c = llm.chat([{"role": "user", "content": "hi"}], sp)[0]
+    assert c.prompt_token_ids == Tok().encode("hi|a:") and len(c.text) == 4
+    two = llm.chat([[{"role": "user", "content": "a"}], [{"role": "user", "content": "b"}]], sp)
+    assert len(two) == 2
+    with pytest.raises(ValueError, match="tokenizer"):
+        _llm().generate(["text"], sp)

@@ -105,8 +105,21 @@ class LLM:
                  tune_gemm: bool = True, gemm_lut_path: str | None = None,
                  speculative_k: int = 0, enable_prefix_caching: bool | None = None,
                  data_parallel_size: int = 1, enable_expert_parallel: bool = False,
-                 prefix_cache_dir: str | None = None):
+                 prefix_cache_dir: str | None = None, tokenizer=None):
         self.cfg: ModelConfig = resolve(model)
+        # tokenizer: an object with encode / decode (/ apply_chat_template), a
+        # directory for transformers.AutoTokenizer, or None (then the checkpoint
+        # directory's tokenizer is tried on first use)
+        self._tokenizer = tokenizer
+        self._tokenizer_src = None  # a checkpoint directory that ships tokenizer files
+        if isinstance(model, str):
+            from pathlib import Path
+
+            d = Path(model)
+            if d.is_dir() and any((d / f).exists() for f in ("tokenizer.json",
+                                                              "tokenizer_config.json",
+                                                              "tokenizer.model")):
+                self._tokenizer_src = str(d)
         ps = pstate.get() if pstate._STATE is not None else None
         dp = int(data_parallel_size)
         if dp > 1:
@@ -247,6 +260,43 @@ class LLM:
         return int(max(2, min(need, budget // per_block)))
 
     # ------------------------------------------------------------------ API
+    # ------------------------------------------------------------------ text
+    @property
+    def tokenizer(self):
+        """The tokenizer (loaded on first use), or None when there is none."""
+        if isinstance(self._tokenizer, str) or (self._tokenizer is None and self._tokenizer_src):
+            src = self._tokenizer if isinstance(self._tokenizer, str) else self._tokenizer_src
+            self._tokenizer_src = None
+            try:
+                from transformers import AutoTokenizer
+
+                self._tokenizer = AutoTokenizer.from_pretrained(src)
+            except Exception:  # noqa: BLE001 - presets and bare configs have none
+                self._tokenizer = None
+        return self._tokenizer
+
+    def _encode(self, text: str) -> list[int]:
+        tok = self.tokenizer
+        if tok is None:
+            raise ValueError("text prompts need a tokenizer (LLM(..., tokenizer=...))")
+        return list(tok.encode(text))
+
+    def chat(self, messages, sampling_params: SamplingParams | None = None,
+             chat_template_kwargs: dict | None = None, tools=None) -> list[RequestOutput]:
+        """vLLM's ``LLM.chat``: one conversation (a list of ``{"role",
+        "content"}`` messages) or a list of them, through the tokenizer's
+        chat template with the generation prompt appended."""
+        tok = self.tokenizer
+        if tok is None or not hasattr(tok, "apply_chat_template"):
+            raise ValueError("chat needs a tokenizer with a chat template")
+        convs = [messages] if messages and isinstance(messages[0], dict) else list(messages)
+        kw = dict(chat_template_kwargs or {})
+        if tools:
+            kw["tools"] = tools
+        ids = [list(tok.apply_chat_template(c, add_generation_prompt=True, tokenize=True, **kw))
+               for c in convs]
+        return self.generate(ids, sampling_params)
+
     def score(self, prompt_token_ids, logits_rows: int = 1024) -> list[torch.Tensor]:
         """Teacher-forced log-probabilities (vLLM's ``prompt_logprobs``): for
         each prompt ``x`` of length L, ``lp[i] = log p(x[i+1] | x[:i+1])``
@@ -363,10 +413,13 @@ class LLM:
         the same requests in the same calls (rank 0 broadcasts them)."""
         if sampling_params is None:
             sampling_params = SamplingParams()
+        if isinstance(prompt_token_ids, str):
+            prompt_token_ids = [prompt_token_ids]
         if isinstance(prompt_token_ids, torch.Tensor):
             prompts = [row for row in prompt_token_ids.to(torch.int64)]
         else:
-            prompts = [torch.as_tensor(p, dtype=torch.int64) for p in prompt_token_ids]
+            prompts = [torch.as_tensor(self._encode(p) if isinstance(p, str) else p,
+                                       dtype=torch.int64) for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
         filtering = any(_filters(p) for p in params)
@@ -615,4 +668,8 @@ class LLM:
             o.tpot_s = None if not stats.tpot_ms else stats.tpot_ms[-1] / 1e3
             outs.append(o)
         self.last_stats = stats
+        tok = self.tokenizer if outs else None
+        if tok is not None:  # vLLM's RequestOutput.text
+            for o in outs:
+                o.text = tok.decode(o.output_token_ids, skip_special_tokens=True)
         return outs

@@ -35,3 +35,4 @@ class RequestOutput:
     # top-N of the model's raw distribution); None when not requested
     logprobs: list | None = None
     prompt_logprobs: list | None = None
+    text: str | None = None        # the decoded output, when the engine has a tokenizer
