@@ -293,3 +293,35 @@ def test_text_prompts_and_chat_with_tokenizer():
     assert len(two) == 2
     with pytest.raises(ValueError, match="tokenizer"):
         _llm().generate(["text"], sp)
+
+
+def test_online_prefill_interleaves_with_decode():
+    """Online (feed) mode: a long prompt that arrives while another request
+    decodes is prefilled one chunk per scheduler iteration, and the running
+    request keeps producing tokens between those chunks; both results equal
+    a plain batch call."""
+    g = torch.Generator().manual_seed(3)
+    short, long_ = torch.randint(0, 512, (8,), generator=g), torch.randint(0, 512, (100,), generator=g)
+    llm = _llm(max_num_batched_tokens=16)
+    want_s = llm.generate([short], SamplingParams(max_tokens=40))[0].output_token_ids
+    want_l = llm.generate([long_], SamplingParams(max_tokens=4))[0].output_token_ids
+    events, calls = [], []
+    plan = {0: [(0, short.tolist(), SamplingParams(max_tokens=40))],
+            3: [(1, long_.tolist(), SamplingParams(max_tokens=4))]}
+
+    def feed(block):
+        calls.append(1)
+        if not plan:
+            return None
+        return plan.pop(len(calls) - 1, [])
+
+    done = {}
+    llm.generate([], feed=feed, stream_interval=2,
+                 on_tokens=lambda rid, ids, fin: events.append((rid, len(ids))),
+                 on_finish=lambda o: done.__setitem__(o.request_id, o.output_token_ids))
+    assert done[0] == want_s and done[1] == want_l
+    first_long = next(i for i, (rid, n) in enumerate(events) if rid == 1 and n)
+    admitted_at = 3  # the long prompt arrived with the 4th feed call
+    short_between = sum(1 for rid, n in events[:first_long] if rid == 0 and n)
+    # 100 prompt tokens / 16 per chunk = 7 chunks; the short request decodes between them
+    assert short_between >= admitted_at + 5, events[:first_long + 1]

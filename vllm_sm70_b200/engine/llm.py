@@ -441,6 +441,14 @@ class LLM:
             on_finish = lambda out: None  # noqa: E731 - e.g. TP followers
         if online and stream_interval <= 0:
             stream_interval = 8  # bounded bursts: arrivals join within a few steps
+        # Online, models without recurrent state: one prefill chunk per scheduler
+        # iteration, so the running requests decode between a long prompt's
+        # chunks. The prompt's device block row is published only when its prefill
+        # completes; until then its decode rows are padding (scratch block 0).
+        # (Decode steps update every row's recurrent state, so hybrid models finish
+        # a prompt's prefill before decoding.)
+        interleave = online and not hasattr(self.model, "reset_slots")
+        prefilling: deque = deque()
 
         def emit(rs, rows_h=None, final=False):
             """Hand each request's not-yet-streamed tokens to ``on_tokens``."""
@@ -479,7 +487,7 @@ class LLM:
 
         def pull() -> bool:
             """Queue the feed's new requests; False once it is closed."""
-            items = feed(not waiting and not running)
+            items = feed(not waiting and not running and not prefilling)
             if items is None:
                 return False
             for rid, ids, sp in items:
@@ -491,10 +499,10 @@ class LLM:
             return True
 
         feed_open = online
-        while waiting or running or feed_open:
+        while waiting or running or prefilling or feed_open:
             if feed_open:
                 feed_open = pull()
-                if not (waiting or running):
+                if not (waiting or running or prefilling):
                     continue
             # ---- admission
             admitted: list[_Req] = []
@@ -524,12 +532,12 @@ class LLM:
                 r.blocks = torch.cat([torch.tensor(hit, dtype=torch.int32),
                                       runner.alloc.allocate(need)])
                 r.prefilled = len(hit) * bs  # cached KV: prefill starts after it
-                runner.set_block_row(r.slot, r.blocks)
+                runner.set_block_row(r.slot, r.blocks, device=not interleave)
                 seed = r.params.seed if r.params.seed is not None else 0x9E3779B97F4A7C15 ^ r.rid
                 runner.set_sampling(r.slot, 0.0 if r.params.greedy else r.params.temperature,
                                     seed & 0x7FFFFFFFFFFFFFFF, r.params.top_k, r.params.top_p)
                 admitted.append(r)
-            if not admitted and not running:
+            if not admitted and not running and not prefilling:
                 if not waiting:  # (online) every new request was refused above
                     continue
                 if not online:
@@ -539,7 +547,11 @@ class LLM:
                                         error="KV cache too small for this request"))
                 continue
             # ---- chunked prefill of the admitted prompts
-            queue = deque(admitted)
+            if interleave:
+                queue = prefilling
+                queue.extend(admitted)
+            else:
+                queue = deque(admitted)
             while queue:
                 budget = self.max_num_batched_tokens
                 pieces, finishing = [], []
@@ -576,11 +588,17 @@ class LLM:
                     e = ev()
                     e.record()
                     pending_first.append((e, finishing))
+                if interleave and finishing:
+                    runner.publish_rows([r.slot for r in finishing])
                 emit([r for r in finishing if r.params.max_tokens > 1])
                 running.extend(finishing)
+                if interleave:
+                    break  # one chunk, then a decode burst of the running requests
             # ---- decode until the next request finishes
             live = [r for r in running if not r.done]
             finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+            if not live:
+                continue  # (interleaved) only prompts mid-prefill
             if not finished_now and self.spec_k:
                 n_rows = max(r.slot for r in live) + 1
                 n = runner.spec_step(n_rows).cpu()

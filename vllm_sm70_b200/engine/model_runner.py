@@ -88,11 +88,22 @@ class ModelRunner:
         self.ep = getattr(model, "ep_a2a", None)
 
     # ------------------------------------------------------------ block tables
-    def set_block_row(self, slot: int, blocks: torch.Tensor) -> None:
+    def set_block_row(self, slot: int, blocks: torch.Tensor, device: bool = True) -> None:
+        """Host block-table row of ``slot`` (prefill metadata reads it) and,
+        unless ``device`` is False, the device row decode steps read. A slot
+        whose device row stays zero is decode padding: its decode rows read
+        and write only the reserved scratch block 0 (see :meth:`publish_rows`)."""
         n = blocks.numel()
         self.bt_host[slot].zero_()
         self.bt_host[slot, :n] = blocks
-        self.block_table[slot].copy_(self.bt_host[slot], non_blocking=True)
+        if device:
+            self.block_table[slot].copy_(self.bt_host[slot], non_blocking=True)
+
+    def publish_rows(self, slots: list[int]) -> None:
+        """Copy the host block-table rows of ``slots`` to the device (a request
+        whose prefill has completed joins the decode batch)."""
+        for s in slots:
+            self.block_table[s].copy_(self.bt_host[s], non_blocking=True)
 
     # ------------------------------------------------------------ decode
     def _splits_for(self, b: int) -> int:
