@@ -192,3 +192,19 @@ def test_ext_fingerprint_and_ops():
     if _ext.load():
         assert _ext.has_op("gemm_bf16_out") and _ext.has_op("paged_attention")
         assert not _ext.has_op("definitely_not_an_op")
+
+
+def test_top_level_cli_dispatch(monkeypatch, capsys):
+    import importlib
+
+    from vllm_sm70_b200 import __main__ as cli
+
+    seen = []
+    mod = importlib.import_module("vllm_sm70_b200.models.convert_gguf")
+    monkeypatch.setattr(mod, "main", lambda argv: seen.append(argv))
+    assert cli.main(["convert-gguf", "a.gguf", "out"]) == 0 and seen == [["a.gguf", "out"]]
+    assert cli.main([]) == 0 and "serve" in capsys.readouterr().out
+    assert cli.main(["nope"]) == 2
+    from vllm_sm70_b200.integration.models import ARCHS
+
+    assert ARCHS["B200FlintForCausalLM"].endswith(":FlintModel")

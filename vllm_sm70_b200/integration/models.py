@@ -7,6 +7,7 @@ ARCHS = {
     "B200LlamaForCausalLM": "vllm_sm70_b200.models.llama:LlamaModel",
     "B200Qwen3MoeForCausalLM": "vllm_sm70_b200.models.qwen3_moe:Qwen3MoeModel",
     "B200Qwen3NextForCausalLM": "vllm_sm70_b200.models.qwen3_next:Qwen3NextModel",
+    "B200FlintForCausalLM": "vllm_sm70_b200.models.flint:FlintModel",
 }
 
 
