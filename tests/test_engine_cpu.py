@@ -325,3 +325,15 @@ def test_online_prefill_interleaves_with_decode():
     short_between = sum(1 for rid, n in events[:first_long] if rid == 0 and n)
     # 100 prompt tokens / 16 per chunk = 7 chunks; the short request decodes between them
     assert short_between >= admitted_at + 5, events[:first_long + 1]
+
+
+def test_single_prompt_forms():
+    """One prompt may be passed as a flat list of ids, a 1-D tensor row or
+    inside a list; all give the same tokens."""
+    llm = _llm()
+    ids = list(range(30, 45))
+    sp = SamplingParams(max_tokens=3)
+    a = llm.generate(ids, sp)
+    b = llm.generate([ids], sp)
+    c = llm.generate(torch.tensor([ids]), sp)
+    assert len(a) == 1 and a[0].output_token_ids == b[0].output_token_ids == c[0].output_token_ids

@@ -413,8 +413,10 @@ class LLM:
         the same requests in the same calls (rank 0 broadcasts them)."""
         if sampling_params is None:
             sampling_params = SamplingParams()
-        if isinstance(prompt_token_ids, str):
-            prompt_token_ids = [prompt_token_ids]
+        if isinstance(prompt_token_ids, str) or (
+                isinstance(prompt_token_ids, (list, tuple)) and prompt_token_ids
+                and isinstance(prompt_token_ids[0], int)):
+            prompt_token_ids = [prompt_token_ids]  # one prompt (text or token ids)
         if isinstance(prompt_token_ids, torch.Tensor):
             prompts = [row for row in prompt_token_ids.to(torch.int64)]
         else:
