@@ -295,3 +295,30 @@ def test_cli_builds_engine_and_app(tmp_path, monkeypatch):
     assert seen["port"] == 8123 and llm.prefix_cache is not None
     assert llm.prefix_cache.disk is not None and not llm.runner.use_graphs
     seen["app"].state.batcher.close()
+
+
+def test_continuous_batching_with_speculative_decoding():
+    """The online engine loop with an MTP draft head (Qwen3-Next, k = 2):
+    requests submitted while others run give the plain greedy tokens."""
+    import threading
+
+    from vllm_sm70_b200.entrypoints.openai_server import Batcher
+    from vllm_sm70_b200.models.config import ModelConfig
+
+    from .test_ep_cpu import NEXT_HF
+
+    cfg = ModelConfig.from_hf({**NEXT_HF, "num_nextn_predict_layers": 1})
+    kw = dict(max_num_seqs=4, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=32)
+    plain = LLM(cfg, **kw)
+    spec = LLM(cfg, speculative_k=2, **kw)
+    g = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (9, 30, 5)]
+    want = [o.output_token_ids for o in plain.generate(prompts, SamplingParams(max_tokens=7))]
+    b = Batcher(spec, max_batch=4)
+    first = threading.Event()
+    futs = [b.submit(prompts[0], SamplingParams(max_tokens=7), stream=lambda i, f: first.set())]
+    assert first.wait(60)
+    futs += [b.submit(p, SamplingParams(max_tokens=7)) for p in prompts[1:]]
+    assert [f.result(120).output_token_ids for f in futs] == want
+    b.close()
