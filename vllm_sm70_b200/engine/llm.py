@@ -359,6 +359,12 @@ class LLM:
             runner.deactivate([slot])
         return lp, tids, tlp
 
+    def model_ep_drain(self) -> None:
+        """Serve the other ranks' expert traffic until every rank is idle (the
+        all-to-all EP layout); a no-op otherwise."""
+        if self.ep is not None:
+            self.model.ep_drain()
+
     @staticmethod
     def _output(r: "_Req") -> RequestOutput:
         return RequestOutput(r.rid, r.prompt.tolist(), r.out, True, logprobs=r.logprobs,

@@ -46,6 +46,7 @@ import uuid
 from ..engine.sampling_params import SamplingParams
 
 STREAM_INTERVAL = 8  # decode steps per streamed chunk
+HEARTBEAT_S = 1.0    # longest idle wait of rank 0 while other ranks wait on it
 
 
 class Batcher:
@@ -101,7 +102,10 @@ class Batcher:
         items = []
         try:
             if block:
-                while not self._stop and not items:
+                # idle: wait for a request, at most HEARTBEAT_S when other ranks wait on
+                # this one in a collective (they must not reach the group's timeout)
+                until = time.perf_counter() + (HEARTBEAT_S if self.group is not None else 1e9)
+                while not self._stop and not items and time.perf_counter() < until:
                     try:
                         items.append(self.q.get(timeout=0.05))
                     except queue.Empty:
@@ -176,6 +180,104 @@ class Batcher:
         this also releases the followers)."""
         self._stop = True
         self.thread.join(timeout=60.0)
+
+
+class DPBatcher(Batcher):
+    """Data-parallel serving (each rank a whole replica, optionally with
+    all-to-all expert parallelism): rank 0 takes the HTTP requests and hands
+    each to a rank; every rank runs its own engine loop. Each scheduler
+    iteration is a lock-step unit over the CPU group: (1) serve the other
+    ranks' expert traffic until every rank is idle (``ep_drain``), (2) gather
+    the followers' streamed tokens and finished outputs to rank 0, (3) rank 0
+    assigns the new requests (to the least-loaded rank) and broadcasts them.
+    The loop is closed only once no rank has work, so all ranks leave it
+    together."""
+
+    def __init__(self, llm, max_batch: int = 256, group=None, metrics=None):
+        import torch.distributed as dist
+
+        self.world = dist.get_world_size(group)
+        self.load = [0] * self.world          # requests in flight per rank
+        self.assigned = [0] * self.world      # requests handed to each rank so far
+        self.owner: dict[int, int] = {}
+        super().__init__(llm, max_batch, group, metrics)
+
+    def _feed(self, block: bool):
+        import torch.distributed as dist
+
+        self.llm.model_ep_drain()
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, (not block, []), group=self.group)
+        any_busy = any(b for b, _ in gathered)
+        for r in range(1, self.world):
+            for ev in gathered[r][1]:
+                self._event(ev)
+        items = []
+        try:
+            if not any_busy and not self.inflight:
+                until = time.perf_counter() + HEARTBEAT_S
+                while not self._stop and not items and time.perf_counter() < until:
+                    try:
+                        items.append(self.q.get(timeout=0.05))
+                    except queue.Empty:
+                        pass
+            while len(items) < self.max_batch:
+                items.append(self.q.get_nowait())
+        except queue.Empty:
+            pass
+        if self._stop and not items and not any_busy and not self.inflight:
+            dist.broadcast_object_list([None], src=0, group=self.group)
+            return None
+        now = time.perf_counter()
+        shares = [[] for _ in range(self.world)]
+        for rid, ids, sp, fut, cb in items:
+            rank = min(range(self.world), key=lambda r: self.load[r])
+            self.load[rank] += 1
+            self.assigned[rank] += 1
+            self.owner[rid] = rank
+            self.inflight[rid] = {"fut": fut, "stream": cb, "sp": sp, "n_prompt": len(ids),
+                                  "t0": now, "t_first": None, "t_last": None}
+            shares[rank].append((rid, ids, sp))
+        if items:
+            self.batches += 1
+        if self.metrics is not None:
+            self.metrics.gauges(len(self.inflight), self.q.qsize())
+        dist.broadcast_object_list([shares], src=0, group=self.group)
+        return shares[0]
+
+    def _event(self, ev) -> None:
+        if ev[0] == "tok":
+            self._on_tokens(ev[1], ev[2], ev[3])
+        else:
+            self._on_finish(ev[1])
+
+    def _on_finish(self, out):
+        r = self.owner.pop(out.request_id, None)
+        if r is not None:
+            self.load[r] -= 1
+        super()._on_finish(out)
+
+
+def dp_follower_loop(llm, group) -> None:
+    """Ranks > 0 of data-parallel serving: run this rank's engine loop on the
+    requests rank 0 assigns to it, in the lock step of :class:`DPBatcher`."""
+    import torch.distributed as dist
+
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    events: list = []
+
+    def feed(block):
+        llm.model_ep_drain()
+        dist.all_gather_object([None] * world, (not block, list(events)), group=group)
+        events.clear()
+        obj = [None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return None if obj[0] is None else obj[0][rank]
+
+    llm.generate([], feed=feed, stream_interval=STREAM_INTERVAL,
+                 on_tokens=lambda rid, ids, fin: events.append(("tok", rid, ids, fin)),
+                 on_finish=lambda out: events.append(("fin", out)))
 
 
 def follower_loop(llm, group) -> None:
@@ -284,7 +386,10 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
     from .metrics import ServerMetrics
 
     metrics = ServerMetrics(model_name)
-    batcher = Batcher(llm, max_batch, group, metrics)
+    ps = getattr(llm, "ps", None)
+    dp = ps is not None and ps.world_size > 1 and ps.tp_size == 1
+    batcher = (DPBatcher(llm, max_batch, ps.cpu_group, metrics) if dp
+               else Batcher(llm, max_batch, group, metrics))
 
     @contextlib.asynccontextmanager
     async def lifespan(_app):
@@ -580,6 +685,10 @@ def main(argv=None) -> None:
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--tensor-parallel-size", type=int, default=1)
+    ap.add_argument("--data-parallel-size", type=int, default=1,
+                    help="replicas (one per rank under torchrun); rank 0 serves HTTP")
+    ap.add_argument("--enable-expert-parallel", action="store_true",
+                    help="data-parallel MoE: experts split over the ranks, all-to-all tokens")
     ap.add_argument("--max-num-seqs", type=int, default=256)
     ap.add_argument("--max-model-len", type=int, default=4096)
     ap.add_argument("--max-num-batched-tokens", type=int, default=16384)
@@ -608,7 +717,9 @@ def main(argv=None) -> None:
               prefix_cache_dir=args.prefix_cache_dir,
               gpu_memory_utilization=args.gpu_memory_utilization,
               enforce_eager=args.enforce_eager, speculative_k=args.speculative_k,
-              seed=args.seed, gemm_lut_path=args.gemm_lut)
+              seed=args.seed, gemm_lut_path=args.gemm_lut,
+              data_parallel_size=args.data_parallel_size,
+              enable_expert_parallel=args.enable_expert_parallel)
     tok = None
     if args.load_format == "safetensors" or args.tokenizer:
         try:
@@ -621,6 +732,9 @@ def main(argv=None) -> None:
     group = ps.cpu_group if ps.tp_size > 1 else None
     if ps.tp_size > 1 and ps.tp_rank != 0:
         follower_loop(llm, group)
+        return
+    if ps.world_size > 1 and ps.tp_size == 1 and ps.rank != 0:  # data-parallel replicas
+        dp_follower_loop(llm, ps.cpu_group)
         return
     import uvicorn
 
