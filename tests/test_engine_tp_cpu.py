@@ -47,3 +47,32 @@ def test_tp_equals_tp1_cpu(tmp_path, tp):
     got = json.loads(out_file.read_text())
     tp1 = _generate(tmp_path, 1)
     assert tp1 == got
+
+
+def _pen_body(rank, world, path, out_file):
+    from pathlib import Path
+
+    from vllm_sm70_b200.engine import LLM, SamplingParams
+    from vllm_sm70_b200.parallel import state
+
+    state.init(tp_size=world, backend="gloo", timeout_s=120)
+    llm = LLM(str(path), tensor_parallel_size=world, load_format="safetensors", **KW)
+    sp = SamplingParams(max_tokens=6, repetition_penalty=1.7, frequency_penalty=0.5)
+    toks = [o.output_token_ids for o in llm.generate(_prompts(), sp)]
+    if rank == 0:
+        Path(out_file).write_text(json.dumps(toks))
+    llm.shutdown()
+    state.shutdown()
+
+
+def test_tp2_penalties_equal_tp1_cpu(tmp_path):
+    """Sampling penalties on vocab-parallel logit shards (each rank rewrites
+    its own slice) give the TP1 tokens."""
+    from vllm_sm70_b200.engine import LLM, SamplingParams
+
+    _checkpoint(tmp_path)
+    out_file = tmp_path / "pen.json"
+    _mp.run(_pen_body, 2, args=(str(tmp_path), str(out_file)), timeout=300)
+    one = LLM(str(tmp_path), tensor_parallel_size=1, load_format="safetensors", **KW)
+    sp = SamplingParams(max_tokens=6, repetition_penalty=1.7, frequency_penalty=0.5)
+    assert json.loads(out_file.read_text()) == [o.output_token_ids for o in one.generate(_prompts(), sp)]

@@ -74,3 +74,43 @@ def test_engine_filtered_requests():
     mixed = llm.generate(_prompts(), [SamplingParams(max_tokens=5), sp, SamplingParams(max_tokens=5)])
     assert mixed[0].output_token_ids == greedy[0] and mixed[2].output_token_ids == greedy[2]
     assert not llm.runner.filtering  # reset after the call
+
+
+def _penalized_greedy(model, prompt, n, rep=1.0, pres=0.0, freq=0.0):
+    """Greedy decoding with vLLM's penalty rules on a dense forward."""
+    from ._llama_ref import llama_logits
+
+    ids, out = prompt.clone(), []
+    for _ in range(n):
+        lg = llama_logits(model, ids)[-1].clone()
+        counts = torch.bincount(torch.tensor(out, dtype=torch.int64), minlength=lg.numel()).float() \
+            if out else torch.zeros_like(lg)
+        seen = counts > 0
+        pseen = torch.zeros_like(lg, dtype=torch.bool)
+        pseen[prompt] = True
+        m = seen | pseen
+        lg = torch.where(m, torch.where(lg > 0, lg / rep, lg * rep), lg)
+        lg = lg - freq * counts - pres * seen.float()
+        t = int(lg.argmax())
+        out.append(t)
+        ids = torch.cat([ids, torch.tensor([t])])
+    return out
+
+
+def test_penalties_match_dense_reference():
+    """repetition / presence / frequency penalties (greedy) equal a dense
+    reference applying vLLM's rules; a request without penalties in the same
+    batch is unchanged; penalties change the output of a repetitive prompt."""
+    llm = _llm()
+    p = torch.tensor([5, 9, 5, 9, 5, 9, 5, 9, 7, 7, 7, 7])
+    plain = llm.generate([p], SamplingParams(max_tokens=8))[0].output_token_ids
+    for kw in (dict(repetition_penalty=1.8), dict(presence_penalty=2.0),
+               dict(frequency_penalty=1.5), dict(repetition_penalty=1.3, frequency_penalty=0.7)):
+        sp = SamplingParams(max_tokens=8, **kw)
+        got = llm.generate([p, p], [sp, SamplingParams(max_tokens=8)])
+        want = _penalized_greedy(llm.model, p, 8, kw.get("repetition_penalty", 1.0),
+                                 kw.get("presence_penalty", 0.0), kw.get("frequency_penalty", 0.0))
+        assert got[0].output_token_ids == want, kw
+        assert got[1].output_token_ids == plain
+    strong = llm.generate([p], SamplingParams(max_tokens=8, frequency_penalty=50.0))[0]
+    assert len(set(strong.output_token_ids)) == 8  # every repeat is penalised away

@@ -77,9 +77,15 @@ class GenerateStats:
     spec_slots: int = 0    # (row, step) pairs; spec_tokens / spec_slots = tokens per step
 
 
+def _penalized(p: SamplingParams) -> bool:
+    return (p.repetition_penalty != 1.0 or p.presence_penalty != 0.0
+            or p.frequency_penalty != 0.0)
+
+
 def _filters(p: SamplingParams) -> bool:
-    """Whether the request needs top-k / top-p candidate sampling."""
-    return p.top_k not in (-1, 0) or p.top_p < 1.0
+    """Whether the request needs the candidate sampling path (top-k / top-p,
+    or sampling penalties)."""
+    return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p)
 
 
 def _truncate_at_stop(tokens: list[int], p: SamplingParams) -> list[int]:
@@ -436,10 +442,12 @@ class LLM:
         reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
         runner = self.runner
         runner.filtering = filtering
+        runner.penalties = any(_penalized(p) for p in params)
         try:
             return self._generate(reqs, on_tokens, int(stream_interval), feed, on_finish)
         finally:
             runner.filtering = False
+            runner.penalties = False
 
     def _generate(self, reqs: list[_Req], on_tokens=None, stream_interval: int = 0,
                   feed=None, on_finish=None) -> list[RequestOutput]:
@@ -503,6 +511,7 @@ class LLM:
                     if self.spec_k:
                         raise NotImplementedError("top-k / top-p with speculative decoding")
                     runner.filtering = True
+                    runner.penalties = runner.penalties or _penalized(sp)
                 waiting.append(_Req(rid, torch.as_tensor(ids, dtype=torch.int64), sp))
             return True
 
@@ -542,8 +551,12 @@ class LLM:
                 r.prefilled = len(hit) * bs  # cached KV: prefill starts after it
                 runner.set_block_row(r.slot, r.blocks, device=not interleave)
                 seed = r.params.seed if r.params.seed is not None else 0x9E3779B97F4A7C15 ^ r.rid
-                runner.set_sampling(r.slot, 0.0 if r.params.greedy else r.params.temperature,
-                                    seed & 0x7FFFFFFFFFFFFFFF, r.params.top_k, r.params.top_p)
+                sp = r.params
+                runner.set_sampling(r.slot, 0.0 if sp.greedy else sp.temperature,
+                                    seed & 0x7FFFFFFFFFFFFFFF, sp.top_k, sp.top_p,
+                                    sp.repetition_penalty, sp.presence_penalty,
+                                    sp.frequency_penalty,
+                                    r.prompt if runner.penalties else None)
                 admitted.append(r)
             if not admitted and not running and not prefilling:
                 if not waiting:  # (online) every new request was refused above

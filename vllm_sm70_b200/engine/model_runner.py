@@ -68,6 +68,12 @@ class ModelRunner:
         self.seeds = torch.zeros(B, dtype=torch.int64, device=dev)
         self.top_k = torch.full((B,), -1, dtype=torch.int32, device=dev)
         self.top_p = torch.ones(B, dtype=torch.float32, device=dev)
+        # sampling penalties (vLLM semantics), applied on the candidate path
+        self.rep_pen = torch.ones(B, dtype=torch.float32, device=dev)
+        self.pres_pen = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.freq_pen = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.prompt_ids: torch.Tensor | None = None  # [B, max_model_len], -1 padded
+        self.penalties = False
         # Decode graphs always sample through the temperature path: rows with
         # T <= 0 reduce to the exact greedy argmax.
         self.sampling = True
@@ -138,7 +144,8 @@ class ModelRunner:
         if self.filtering:
             nxt = self.model.sample_filtered(h, self.temperature[:b], self.top_k[:b],
                                              self.top_p[:b], self._step_seeds(self.seeds[:b],
-                                                                              self.out_pos[:b]))
+                                                                              self.out_pos[:b]),
+                                             self._penalizer(self.slot_ids[:b].long()))
         elif self.sampling:
             nxt = self.model.sample(h, self.temperature[:b], self.seeds[:b], self.out_pos[:b])
         else:
@@ -148,6 +155,35 @@ class ModelRunner:
         act = self.active[:b]
         self.out_pos[:b] += act
         self.seq_lens[:b] += act
+
+    def _penalizer(self, rows: torch.Tensor):
+        """Logit rewrite of the sampling penalties for batch slots ``rows``
+        (None when no request in flight uses them): repetition over prompt and
+        output tokens (divide positive logits, multiply negative ones),
+        presence and frequency over output tokens (subtract per occurrence)."""
+        if not self.penalties:
+            return None
+
+        def apply(lg: torch.Tensor, vs: int) -> torch.Tensor:
+            b, V = lg.shape
+            outs = self.out_tokens.index_select(0, rows).long()
+            pos = self.out_pos.index_select(0, rows)
+            ok = torch.arange(outs.shape[1], device=lg.device)[None, :] < pos[:, None]
+            loc = outs - vs
+            ok &= (loc >= 0) & (loc < V)
+            counts = torch.zeros(b, V, device=lg.device)
+            counts.scatter_add_(1, loc.clamp(0, V - 1), ok.float())
+            pr = self.prompt_ids.index_select(0, rows)
+            ploc = pr - vs
+            pok = (pr >= 0) & (ploc >= 0) & (ploc < V)
+            pseen = torch.zeros(b, V, device=lg.device)
+            pseen.scatter_add_(1, ploc.clamp(0, V - 1), pok.float())
+            seen = counts > 0
+            rp = self.rep_pen.index_select(0, rows)[:, None]
+            lg = torch.where(seen | (pseen > 0), torch.where(lg > 0, lg / rp, lg * rp), lg)
+            return (lg - self.freq_pen.index_select(0, rows)[:, None] * counts
+                    - self.pres_pen.index_select(0, rows)[:, None] * seen.float())
+        return apply
 
     @staticmethod
     def _step_seeds(seeds: torch.Tensor, out_pos: torch.Tensor) -> torch.Tensor:
@@ -206,11 +242,22 @@ class ModelRunner:
 
     # ------------------------------------------------------------ prefill
     def set_sampling(self, slot: int, temperature: float, seed: int, top_k: int = -1,
-                     top_p: float = 1.0) -> None:
+                     top_p: float = 1.0, repetition_penalty: float = 1.0,
+                     presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
+                     prompt: torch.Tensor | None = None) -> None:
         self.temperature[slot] = float(temperature)
         self.seeds[slot] = int(seed)
         self.top_k[slot] = int(top_k) if top_k > 0 else -1
         self.top_p[slot] = float(top_p)
+        self.rep_pen[slot] = float(repetition_penalty)
+        self.pres_pen[slot] = float(presence_penalty)
+        self.freq_pen[slot] = float(frequency_penalty)
+        if prompt is not None:  # the prompt's tokens count for the repetition penalty
+            if self.prompt_ids is None:
+                self.prompt_ids = torch.full((self.B, self.max_model_len), -1, dtype=torch.int64,
+                                             device=self.device)
+            self.prompt_ids[slot].fill_(-1)
+            self.prompt_ids[slot, : prompt.numel()] = prompt.to(self.device)
 
     def prefill(self, pieces: list[tuple[int, torch.Tensor, int, bool, int]]) -> None:
         """``pieces``: (slot, token ids [n] int64 CPU, ctx_start, is_last, total_len)."""
@@ -263,7 +310,8 @@ class ModelRunner:
             nxt = self.model.sample_filtered(h_last, self.temperature.index_select(0, sidx),
                                              self.top_k.index_select(0, sidx),
                                              self.top_p.index_select(0, sidx),
-                                             self.seeds.index_select(0, sidx))
+                                             self.seeds.index_select(0, sidx),
+                                             self._penalizer(sidx))
         elif self.sampling:
             nxt = self.model.sample(h_last, self.temperature.index_select(0, sidx),
                                     self.seeds.index_select(0, sidx), None, offset=0)

@@ -14,6 +14,9 @@ class SamplingParams:
     seed: int | None = None
     ignore_eos: bool = False
     stop_token_ids: list[int] = field(default_factory=list)
+    repetition_penalty: float = 1.0      # > 1 discourages prompt / output tokens
+    presence_penalty: float = 0.0        # subtracted once per token present in the output
+    frequency_penalty: float = 0.0       # subtracted per occurrence in the output
     logprobs: int | None = None          # per output token: its log-prob + the top-N
     prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 

@@ -457,16 +457,21 @@ class LlamaModel:
 
     def sample_filtered(self, hidden: torch.Tensor, temperature: torch.Tensor,
                         top_k: torch.Tensor, top_p: torch.Tensor,
-                        seeds: torch.Tensor) -> torch.Tensor:
+                        seeds: torch.Tensor, penalize=None) -> torch.Tensor:
         """Per-row temperature + top-k + top-p sampling: the local top-64
         candidates of each vocab shard, all-gathered over TP, then one
         sampling kernel over the merged set (top-k is bounded by the
         candidate count and top-p is taken over the candidates). ``seeds``
-        must already differ per step."""
+        must already differ per step. ``penalize(logits, vocab_start)``
+        (optional) rewrites this rank's fp32 logit shard first (sampling
+        penalties)."""
         logits = ops.gemm(hidden, self.lm_head)
         nvalid = max(1, min(self.vocab_local, self.cfg.vocab_size - self.vocab_start))
         C = min(CANDIDATES, nvalid)
-        v, i = ops.sampling.topk_candidates(logits[:, :nvalid], C, self.vocab_start)
+        lg = logits[:, :nvalid]
+        if penalize is not None:
+            lg = penalize(lg.float(), self.vocab_start).contiguous()
+        v, i = ops.sampling.topk_candidates(lg, C, self.vocab_start)
         if self.ps.tp_size > 1:
             v = pstate.tp_all_gather(v, dim=1)
             i = pstate.tp_all_gather(i, dim=1)
