@@ -337,3 +337,35 @@ def test_single_prompt_forms():
     b = llm.generate([ids], sp)
     c = llm.generate(torch.tensor([ids]), sp)
     assert len(a) == 1 and a[0].output_token_ids == b[0].output_token_ids == c[0].output_token_ids
+
+
+def test_stop_strings_and_min_tokens():
+    """``stop`` strings cut tokens and text (the stop string kept only with
+    ``include_stop_str_in_output``); ``min_tokens`` ignores stop tokens and
+    strings that end earlier."""
+    from vllm_sm70_b200.engine.llm import _cut_at_stop_string, _truncate_at_stop
+
+    dec = lambda ids: "".join(chr(97 + i % 26) for i in ids)  # noqa: E731 - one char per id
+    toks = [0, 1, 2, 3, 2, 3, 4]                             # "abcdcde"
+    sp = SamplingParams(stop=["cd"])
+    assert _cut_at_stop_string(toks, sp, dec) == ([0, 1, 2, 3], "ab")
+    sp = SamplingParams(stop=["cd"], include_stop_str_in_output=True)
+    assert _cut_at_stop_string(toks, sp, dec) == ([0, 1, 2, 3], "abcd")
+    sp = SamplingParams(stop=["cd"], min_tokens=5)  # the first "cd" ends at token 4
+    assert _cut_at_stop_string(toks, sp, dec) == ([0, 1, 2, 3, 2, 3], "abcd")
+    assert _truncate_at_stop([5, 7, 5, 7], SamplingParams(stop_token_ids=[7], min_tokens=3)) == [5, 7, 5, 7]
+    assert _truncate_at_stop([5, 7, 5, 7], SamplingParams(stop_token_ids=[7])) == [5, 7]
+
+    class Tok:
+        def encode(self, text):
+            return [ord(c) - 96 for c in text]
+
+        def decode(self, ids, skip_special_tokens=True):
+            return "".join(chr(97 + i % 26) for i in ids)
+
+    llm = _llm(tokenizer=Tok())
+    full = llm.generate(["hello"], SamplingParams(max_tokens=8))[0]
+    stop = full.text[2:4]
+    cut = llm.generate(["hello"], SamplingParams(max_tokens=8, stop=[stop]))[0]
+    assert cut.text == full.text[: full.text.find(stop)]
+    assert cut.output_token_ids == full.output_token_ids[: len(cut.text) + len(stop)]

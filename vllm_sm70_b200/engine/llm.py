@@ -96,9 +96,42 @@ def _truncate_at_stop(tokens: list[int], p: SamplingParams) -> list[int]:
         return tokens
     stops = set(p.stop_token_ids)
     for i, t in enumerate(tokens):
-        if t in stops:
+        if t in stops and i + 1 > p.min_tokens:
             return tokens[: i + 1]
     return tokens
+
+
+def _cut_at_stop_string(tokens: list[int], p: SamplingParams, decode) -> tuple[list[int], str]:
+    """(tokens, text) cut at the first stop string that ends after
+    ``min_tokens`` tokens: the tokens up to the one that completes it, the
+    text up to its start (or its end with ``include_stop_str_in_output``)."""
+    text = decode(tokens)
+    if not p.stop:
+        return tokens, text
+    best = None
+    for st in p.stop:
+        at = text.find(st) if st else -1
+        while at >= 0:
+            end = at + len(st)
+            # the first token count whose decoded prefix covers the stop string
+            # (decoded length grows with the count: bisect)
+            lo, hi = 1, len(tokens)
+            while lo < hi:
+                mid = (lo + hi) // 2
+                if len(decode(tokens[:mid])) >= end:
+                    hi = mid
+                else:
+                    lo = mid + 1
+            k = lo
+            if k > p.min_tokens:
+                if best is None or at < best[0]:
+                    best = (at, end, k)
+                break
+            at = text.find(st, at + 1)
+    if best is None:
+        return tokens, text
+    at, end, k = best
+    return tokens[:k], text[: end if p.include_stop_str_in_output else at]
 
 
 class LLM:
@@ -708,7 +741,11 @@ class LLM:
             outs.append(o)
         self.last_stats = stats
         tok = self.tokenizer if outs else None
-        if tok is not None:  # vLLM's RequestOutput.text
-            for o in outs:
-                o.text = tok.decode(o.output_token_ids, skip_special_tokens=True)
+        if tok is not None:  # vLLM's RequestOutput.text (and stop strings)
+            dec = lambda ids: tok.decode(ids, skip_special_tokens=True)  # noqa: E731
+            for o, r in zip(outs, reqs):
+                o.output_token_ids, o.text = _cut_at_stop_string(o.output_token_ids, r.params,
+                                                                 dec)
+        elif any(r.params.stop for r in reqs):
+            raise ValueError("stop strings need a tokenizer (LLM(..., tokenizer=...))")
         return outs

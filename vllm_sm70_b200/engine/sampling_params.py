@@ -14,6 +14,9 @@ class SamplingParams:
     seed: int | None = None
     ignore_eos: bool = False
     stop_token_ids: list[int] = field(default_factory=list)
+    stop: list[str] = field(default_factory=list)   # stop strings (needs a tokenizer)
+    include_stop_str_in_output: bool = False
+    min_tokens: int = 0                              # stop tokens / strings ignored before
     repetition_penalty: float = 1.0      # > 1 discourages prompt / output tokens
     presence_penalty: float = 0.0        # subtracted once per token present in the output
     frequency_penalty: float = 0.0       # subtracted per occurrence in the output
