@@ -322,3 +322,75 @@ def test_continuous_batching_with_speculative_decoding():
     futs += [b.submit(p, SamplingParams(max_tokens=7)) for p in prompts[1:]]
     assert [f.result(120).output_token_ids for f in futs] == want
     b.close()
+
+
+def test_abort_running_and_queued_requests():
+    """``Batcher.abort``: a decoding request leaves the batch at the next
+    iteration with the tokens it has (its future fails with "aborted"), a
+    request still queued never runs, and the others are unaffected."""
+    import threading
+
+    from vllm_sm70_b200.entrypoints.openai_server import Batcher
+
+    llm = LLM(TINY, max_num_seqs=2, max_model_len=128, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=64)
+    other = list(range(50, 60))
+    want = llm.generate([torch.tensor(other)], SamplingParams(max_tokens=5))[0]
+    b = Batcher(llm, max_batch=2)
+    started = threading.Event()
+    f_long = b.submit(list(range(10, 30)), SamplingParams(max_tokens=100),
+                      stream=lambda ids, fin: started.set())
+    assert started.wait(30)
+    b.abort(f_long.rid)
+    with pytest.raises(ValueError, match="aborted"):
+        f_long.result(30)
+    f_ok = b.submit(other, SamplingParams(max_tokens=5))
+    assert f_ok.result(30).output_token_ids == want.output_token_ids
+    b.close()
+
+
+def test_stream_client_disconnect_aborts(client, monkeypatch):
+    """A streaming client that goes away after the first chunk (an ASGI
+    ``http.disconnect``): its request is aborted instead of running to
+    max_tokens. Decode bursts are slowed so that the request cannot finish on
+    its own in the meantime."""
+    import asyncio
+    import json as _json
+    import time as _t
+
+    b = client.app_.state.batcher
+    runner = client.llm.runner
+    real = runner.decode
+    monkeypatch.setattr(runner, "decode", lambda *a, **k: (_t.sleep(0.2), real(*a, **k))[1])
+    before = b.aborted
+    body = _json.dumps({"prompt": list(range(5, 15)), "max_tokens": 100, "temperature": 0.0,
+                        "ignore_eos": True, "stream": True}).encode()
+
+    async def drive():
+        first = asyncio.Event()
+        sent_request = False
+
+        async def receive():
+            nonlocal sent_request
+            if not sent_request:
+                sent_request = True
+                return {"type": "http.request", "body": body, "more_body": False}
+            await first.wait()
+            return {"type": "http.disconnect"}
+
+        async def send(m):
+            if m["type"] == "http.response.body" and b"data: {" in m.get("body", b""):
+                first.set()
+
+        scope = {"type": "http", "asgi": {"version": "3.0"}, "http_version": "1.1",
+                 "method": "POST", "scheme": "http", "path": "/v1/completions", "raw_path":
+                 b"/v1/completions", "query_string": b"", "root_path": "",
+                 "headers": [(b"content-type", b"application/json")],
+                 "client": ("test", 1), "server": ("test", 80)}
+        await asyncio.wait_for(client.app_(scope, receive, send), 60)
+
+    asyncio.run(drive())
+    deadline = _t.time() + 30
+    while b.inflight and _t.time() < deadline:
+        _t.sleep(0.05)
+    assert not b.inflight and b.aborted == before + 1

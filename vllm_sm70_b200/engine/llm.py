@@ -63,6 +63,7 @@ class _Req:
     logprobs: list | None = None
     prompt_logprobs: list | None = None
     stream_stopped: bool = False   # a stop token was streamed: nothing more follows
+    aborted: bool = False          # cancelled by the caller (online mode)
 
 
 @dataclass
@@ -447,7 +448,7 @@ class LLM:
 
         Continuous batching (``feed``): ``feed(block)`` is called once per
         scheduler iteration and returns new requests ``[(request_id, prompt
-        ids, SamplingParams)]`` to admit alongside the running ones (waiting
+        ids, SamplingParams)]`` (or ``("abort", request_id)`` to cancel one) to admit alongside the running ones (waiting
         for at least one when ``block`` is true: nothing runs), or None to
         finish once the running requests are done. Finished requests go to
         ``on_finish(RequestOutput)`` instead of the return value; a request
@@ -534,12 +535,35 @@ class LLM:
         decode_events: list[tuple[object, list[_Req], int]] = []
         prefill_spans: list[tuple[object, object]] = []
 
+        def cancel(rid) -> None:
+            """Abort a request wherever it is: queued, mid-prefill or decoding
+            (a decoding one finishes at the end of the current burst with the
+            tokens it has)."""
+            for r in list(waiting):
+                if r.rid == rid:
+                    waiting.remove(r)
+                    on_finish(RequestOutput(r.rid, r.prompt.tolist(), [], True, error="aborted"))
+            for r in list(prefilling):
+                if r.rid == rid:
+                    prefilling.remove(r)
+                    runner.deactivate([r.slot])
+                    runner.alloc.free(r.blocks)
+                    free_slots.append(r.slot)
+                    on_finish(RequestOutput(r.rid, r.prompt.tolist(), [], True, error="aborted"))
+            for r in running:
+                if r.rid == rid and not r.done:
+                    r.aborted = True
+
         def pull() -> bool:
             """Queue the feed's new requests; False once it is closed."""
             items = feed(not waiting and not running and not prefilling)
             if items is None:
                 return False
-            for rid, ids, sp in items:
+            for item in items:
+                if item[0] == "abort":  # ("abort", request id)
+                    cancel(item[1])
+                    continue
+                rid, ids, sp = item
                 if _filters(sp):
                     if self.spec_k:
                         raise NotImplementedError("top-k / top-p with speculative decoding")
@@ -650,7 +674,7 @@ class LLM:
                     break  # one chunk, then a decode burst of the running requests
             # ---- decode until the next request finishes
             live = [r for r in running if not r.done]
-            finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+            finished_now = [r for r in live if r.generated >= r.params.max_tokens or r.aborted]
             if not live:
                 continue  # (interleaved) only prompts mid-prefill
             if not finished_now and self.spec_k:
@@ -663,7 +687,7 @@ class LLM:
                 stats.spec_slots += len(live)
                 if self.spec_hook is not None:
                     self.spec_hook(len(live), sum(int(n[r.slot]) for r in live))
-                finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+                finished_now = [r for r in live if r.generated >= r.params.max_tokens or r.aborted]
                 if cuda and finished_now:
                     e = ev()
                     e.record()
@@ -681,7 +705,7 @@ class LLM:
                 stats.decode_steps += steps
                 for r in live:
                     r.generated += steps
-                finished_now = [r for r in live if r.generated >= r.params.max_tokens]
+                finished_now = [r for r in live if r.generated >= r.params.max_tokens or r.aborted]
                 if cuda:
                     e = ev()
                     e.record()
@@ -697,14 +721,17 @@ class LLM:
                 outs_h = outs.to("cpu", non_blocking=False)
                 emit(finished_now, outs_h, final=True)
                 for r, row in zip(finished_now, outs_h):
-                    r.out = _truncate_at_stop(row[: r.params.max_tokens].tolist(), r.params)
+                    n_out = min(r.generated, r.params.max_tokens)
+                    r.out = _truncate_at_stop(row[:n_out].tolist(), r.params)
                     r.done = True
                     runner.alloc.free(r.blocks)
                     if r.params.logprobs is not None or r.params.prompt_logprobs is not None:
                         r.logprobs, r.prompt_logprobs = self._logprobs_of(r)
                     free_slots.append(r.slot)
                     if on_finish is not None:
-                        on_finish(self._output(r))
+                        o = self._output(r)
+                        o.error = "aborted" if r.aborted else None
+                        on_finish(o)
                 running = [r for r in running if not r.done]
                 if online:  # a long-lived session keeps no per-request records
                     pending_first.clear()

@@ -64,12 +64,14 @@ class Batcher:
         self.group = group
         self.metrics = metrics
         self.q: queue.Queue = queue.Queue()
+        self.aborts: queue.Queue = queue.Queue()
         self._stop = False
         self._dead: BaseException | None = None
         self._lock = threading.Lock()
         self._next = 0
         self.inflight: dict[int, dict] = {}
         self.batches = 0  # scheduler iterations that admitted new requests
+        self.aborted = 0  # requests that ended by abort
         if metrics is not None:
             llm.spec_hook = metrics.spec_step
         self.thread = threading.Thread(target=self._run, name="b200-engine", daemon=True)
@@ -87,8 +89,22 @@ class Batcher:
         with self._lock:
             rid = self._next
             self._next += 1
+        fut.rid = rid
         self.q.put((rid, list(prompt_ids), params, fut, stream))
         return fut
+
+    def abort(self, rid: int) -> None:
+        """Cancel a request (e.g. its client went away): it leaves the batch at
+        the next scheduler iteration; its future fails with "aborted"."""
+        self.aborts.put(rid)
+
+    def _take_aborts(self) -> list:
+        out = []
+        while True:
+            try:
+                out.append(("abort", self.aborts.get_nowait()))
+            except queue.Empty:
+                return out
 
     # -- engine-thread callbacks ---------------------------------------------
     def _bcast(self, obj):
@@ -124,7 +140,8 @@ class Batcher:
             self.batches += 1
         if self.metrics is not None:
             self.metrics.gauges(len(self.inflight), self.q.qsize())
-        return self._bcast([(rid, ids, sp) for rid, ids, sp, _, _ in items])
+        return self._bcast([(rid, ids, sp) for rid, ids, sp, _, _ in items]
+                           + self._take_aborts())
 
     def _on_tokens(self, rid, ids, fin):
         e = self.inflight.get(rid)
@@ -135,15 +152,23 @@ class Batcher:
             e["t_first"] = e["t_first"] or t
             e["t_last"] = t
         if e["stream"] is not None:
-            e["stream"](ids, fin)
+            try:
+                e["stream"](ids, fin)
+            except Exception:  # noqa: BLE001 - the consumer is gone: drop only this request
+                e["stream"] = None
+                self.abort(rid)
 
     def _on_finish(self, out):
         e = self.inflight.pop(out.request_id, None)
         if e is None:
             return
         if out.error is not None:
+            self.aborted += out.error == "aborted"
             if e["stream"] is not None:
-                e["stream"](None, True)
+                try:
+                    e["stream"](None, True)
+                except Exception:  # noqa: BLE001 - the consumer is gone
+                    pass
             e["fut"].set_exception(ValueError(out.error))
             return
         if self.metrics is not None:
@@ -171,7 +196,10 @@ class Batcher:
                 pending.append({"fut": fut, "stream": cb})
             for e in pending:
                 if e["stream"] is not None:
-                    e["stream"](None, True)
+                    try:
+                        e["stream"](None, True)
+                    except Exception:  # noqa: BLE001 - the consumer is gone
+                        pass
                 if not e["fut"].done():
                     e["fut"].set_exception(exc)
 
@@ -238,6 +266,9 @@ class DPBatcher(Batcher):
             self.inflight[rid] = {"fut": fut, "stream": cb, "sp": sp, "n_prompt": len(ids),
                                   "t0": now, "t_first": None, "t_last": None}
             shares[rank].append((rid, ids, sp))
+        for ab in self._take_aborts():
+            if ab[1] in self.owner:
+                shares[self.owner[ab[1]]].append(ab)
         if items:
             self.batches += 1
         if self.metrics is not None:
@@ -442,9 +473,22 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         the returned queue."""
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        batcher.submit(prompt_ids, sp,
-                       lambda ids, fin: loop.call_soon_threadsafe(q.put_nowait, (ids, fin)))
+        fut = batcher.submit(prompt_ids, sp,
+                             lambda ids, fin: loop.call_soon_threadsafe(q.put_nowait, (ids, fin)))
+        q.rid = getattr(fut, "rid", None)
         return q
+
+    async def guarded(gen, q):
+        """Pass the stream through; if the client goes away before it ends,
+        abort the request so it stops holding a batch slot."""
+        done = False
+        try:
+            async for item in gen:
+                yield item
+            done = True
+        finally:
+            if not done and q.rid is not None:
+                batcher.abort(q.rid)
 
     def stream_completion(prompt_ids, sp, stop):
         q = start_stream(prompt_ids, sp)
@@ -476,7 +520,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                     break
             yield "data: [DONE]\n\n"
 
-        return StreamingResponse(events(), media_type="text/event-stream")
+        return StreamingResponse(guarded(events(), q), media_type="text/event-stream")
 
     @app.get("/health")
     async def health():
@@ -611,7 +655,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                     break
             yield "data: [DONE]\n\n"
 
-        return StreamingResponse(events(), media_type="text/event-stream")
+        return StreamingResponse(guarded(events(), q), media_type="text/event-stream")
 
     @app.post("/v1/chat/completions")
     async def chat(body: dict):
