@@ -244,6 +244,75 @@ def run_ours(args) -> dict:
     return res
 
 
+def run_online(args) -> dict:
+    """Serving under load (one GPU): requests arrive as a Poisson process of
+    ``--arrival-rate`` per second (seeded) into the continuous-batching engine
+    loop; per-request TTFT / TPOT from host clocks (arrival to first token,
+    first to last token). Not the headline metric."""
+    import random
+
+    sys.path.insert(0, str(ROOT))
+    from vllm_sm70_b200.engine import LLM, SamplingParams
+
+    world, _ = _dist_setup()
+    if world > 1:
+        raise SystemExit("--arrival-rate runs on one GPU")
+    llm = LLM(PRESET, max_num_seqs=N_REQ, max_model_len=PROMPT + OUT + (SPEC_K + 1 if SPEC_K else 0),
+              block_size=args.block_size, max_num_batched_tokens=args.chunk,
+              load_format="dummy", seed=0, speculative_k=SPEC_K)
+    sp = SamplingParams(max_tokens=OUT, temperature=TEMPERATURE, ignore_eos=True)
+    for i in range(args.warmup):  # warm-up: a short plain batch
+        llm.generate(make_prompts(1000 + i)[:8], sp)
+    prompts = make_prompts(3000)
+    rng = random.Random(7)
+    arrivals, t = [], 0.0
+    for _ in range(N_REQ):
+        t += rng.expovariate(args.arrival_rate)
+        arrivals.append(t)
+    t0 = time.perf_counter()
+    nxt, first, last, done = 0, {}, {}, {}
+
+    def feed(block):
+        nonlocal nxt
+        if nxt >= N_REQ:
+            return None
+        now = time.perf_counter() - t0
+        if block and arrivals[nxt] > now:
+            time.sleep(arrivals[nxt] - now)
+            now = arrivals[nxt]
+        out = []
+        while nxt < N_REQ and arrivals[nxt] <= now:
+            out.append((nxt, prompts[nxt], sp))
+            nxt += 1
+        return out
+
+    def on_tokens(rid, ids, fin):
+        if ids:
+            tt = time.perf_counter() - t0
+            first.setdefault(rid, tt)
+            last[rid] = tt
+
+    llm.generate([], feed=feed, on_tokens=on_tokens,
+                 on_finish=lambda o: done.__setitem__(o.request_id, len(o.output_token_ids)))
+    wall = time.perf_counter() - t0
+    ttft = sorted(first[i] - arrivals[i] for i in done)
+    tpot = sorted((last[i] - first[i]) / (done[i] - 1) for i in done if done[i] > 1)
+
+    def pct(v, q):
+        return round(v[min(len(v) - 1, int(q * len(v)))] * 1e3, 2) if v else None
+
+    res = {"metric": "online serving: output tok/s and p50 / p90 TTFT, TPOT (host clock)",
+           "value": round(sum(done.values()) / wall, 1), "unit": "tok/s",
+           "arrival_rate_per_s": args.arrival_rate, "requests": N_REQ,
+           "p50_ttft_ms": pct(ttft, 0.5), "p90_ttft_ms": pct(ttft, 0.9),
+           "p50_tpot_ms": pct(tpot, 0.5), "p90_tpot_ms": pct(tpot, 0.9),
+           "config": {"model": MODEL, "seq_len": PROMPT, "output_len": OUT},
+           "profiling": True}
+    print(json.dumps(res), flush=True)
+    llm.shutdown()
+    return res
+
+
 # ----------------------------------------------------------------------------- reference
 def _write_hf_config(d: Path):
     cfg = {
@@ -350,6 +419,9 @@ def main(argv=None):
     ap.add_argument("--verbose", action="store_true", help="log engine set-up (GEMM plans)")
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="llama-3.1-8b",
                     help="benchmark configuration (default: the headline Llama-3.1-8B workload)")
+    ap.add_argument("--arrival-rate", type=float, default=None,
+                    help="serving under load instead of the headline batch: Poisson "
+                         "arrivals per second into the continuous-batching loop (1 GPU)")
     ap.add_argument("--layout", choices=["tp", "dp-ep"], default="tp",
                     help="N > 1: tensor parallel (MoE experts sliced over the TP group), or "
                          "data-parallel attention with all-to-all expert parallelism")
@@ -375,6 +447,8 @@ def main(argv=None):
         print("warning: --warmup < 3 does not meet the timing rules", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.arrival_rate:
+        run_online(args)
     else:
         run_ours(args)
 
