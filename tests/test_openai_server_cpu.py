@@ -394,3 +394,17 @@ def test_stream_client_disconnect_aborts(client, monkeypatch):
     while b.inflight and _t.time() < deadline:
         _t.sleep(0.05)
     assert not b.inflight and b.aborted == before + 1
+
+
+def test_embeddings(client):
+    """``/v1/embeddings`` and ``LLM.embed``: unit vectors of the last token's
+    final hidden state; the same input gives the same vector whether sent as
+    text or ids, and equals the engine's own call."""
+    r = client.post("/v1/embeddings", json={"input": ["hey", "there!"]}).json()
+    vs = [torch.tensor(d["embedding"]) for d in r["data"]]
+    assert len(vs) == 2 and all(abs(float(v.norm()) - 1) < 1e-5 for v in vs)
+    ids = [ord(c) for c in "hey"]
+    r2 = client.post("/v1/embeddings", json={"input": ids}).json()
+    assert torch.allclose(torch.tensor(r2["data"][0]["embedding"]), vs[0], atol=1e-6)
+    direct = client.llm.embed([ids])[0]
+    assert torch.allclose(direct, vs[0], atol=1e-6) and r["usage"]["prompt_tokens"] == 9

@@ -358,6 +358,41 @@ class LLM:
             self.model.ep_drain()
         return out
 
+    def embed(self, prompts, normalize: bool = True) -> list[torch.Tensor]:
+        """vLLM's ``LLM.embed`` for a decoder: the final (normed) hidden state
+        of each prompt's last token (last-token pooling), L2-normalised unless
+        ``normalize`` is False; fp32 on the host. Text prompts need a
+        tokenizer. Call between ``generate`` calls (it uses batch slot 0)."""
+        if isinstance(prompts, str) or (isinstance(prompts, (list, tuple)) and prompts
+                                        and isinstance(prompts[0], int)):
+            prompts = [prompts]
+        runner = self.runner
+        out = []
+        for p in prompts:
+            seq = torch.as_tensor(self._encode(p) if isinstance(p, str) else p, dtype=torch.int64)
+            L = seq.numel()
+            if L > runner.max_model_len:
+                raise ValueError(f"prompt of {L} tokens > max_model_len")
+            nblk = math.ceil(L / runner.block_size)
+            if runner.alloc.num_free() < nblk and self.prefix_cache is not None:
+                self.prefix_cache.evict(nblk)
+            blocks = runner.alloc.allocate(nblk)
+            runner.set_block_row(0, blocks)
+            try:
+                pos, h = 0, None
+                while pos < L:
+                    n = min(self.max_num_batched_tokens, L - pos)
+                    h = runner.prefill_hidden([(0, seq[pos:pos + n], pos, False, L)])
+                    pos += n
+                v = h[-1].float().cpu()
+            finally:
+                runner.alloc.free(blocks)
+                runner.deactivate([0])
+            out.append(torch.nn.functional.normalize(v, dim=0) if normalize else v)
+        if self.ep is not None:
+            self.model.ep_drain()
+        return out
+
     def _score_seq(self, slot: int, seq: torch.Tensor, top_n: int = 0,
                    logits_rows: int = 1024):
         """Teacher-forced pass over ``seq`` through batch slot ``slot`` (which

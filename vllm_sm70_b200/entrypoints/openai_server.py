@@ -65,6 +65,7 @@ class Batcher:
         self.metrics = metrics
         self.q: queue.Queue = queue.Queue()
         self.aborts: queue.Queue = queue.Queue()
+        self.calls: queue.Queue = queue.Queue()
         self._stop = False
         self._dead: BaseException | None = None
         self._lock = threading.Lock()
@@ -93,6 +94,28 @@ class Batcher:
         self.q.put((rid, list(prompt_ids), params, fut, stream))
         return fut
 
+    def call(self, fn) -> concurrent.futures.Future:
+        """Run ``fn()`` on the engine thread when the loop is idle -- no request
+        queued, prefilling or decoding, so every batch slot is free (engine
+        calls such as embeddings use slot 0); single-rank deployments only."""
+        fut: concurrent.futures.Future = concurrent.futures.Future()
+        if self.group is not None:
+            fut.set_exception(RuntimeError("engine calls are served on one rank only"))
+            return fut
+        self.calls.put((fn, fut))
+        return fut
+
+    def _run_calls(self) -> None:
+        while True:
+            try:
+                fn, fut = self.calls.get_nowait()
+            except queue.Empty:
+                return
+            try:
+                fut.set_result(fn())
+            except Exception as e:  # noqa: BLE001 - reported to the caller
+                fut.set_exception(e)
+
     def abort(self, rid: int) -> None:
         """Cancel a request (e.g. its client went away): it leaves the batch at
         the next scheduler iteration; its future fails with "aborted"."""
@@ -118,14 +141,16 @@ class Batcher:
         items = []
         try:
             if block:
-                # idle: wait for a request, at most HEARTBEAT_S when other ranks wait on
-                # this one in a collective (they must not reach the group's timeout)
+                # idle (every batch slot free): engine calls run now; then wait for a
+                # request, at most HEARTBEAT_S when other ranks wait on this one in a
+                # collective (they must not reach the group's timeout)
+                self._run_calls()
                 until = time.perf_counter() + (HEARTBEAT_S if self.group is not None else 1e9)
                 while not self._stop and not items and time.perf_counter() < until:
                     try:
                         items.append(self.q.get(timeout=0.05))
                     except queue.Empty:
-                        pass
+                        self._run_calls()
             while len(items) < self.max_batch:
                 items.append(self.q.get_nowait())
         except queue.Empty:
@@ -532,6 +557,21 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         from prometheus_client import CONTENT_TYPE_LATEST
 
         return Response(metrics.exposition(), media_type=CONTENT_TYPE_LATEST)
+
+    @app.post("/v1/embeddings")
+    async def embeddings(body: dict):
+        """Last-token embeddings of the inputs (run on the engine thread between
+        its scheduler iterations)."""
+        inp = body.get("input")
+        batch = inp if isinstance(inp, list) and inp and not isinstance(inp[0], int) else [inp]
+        ids = [encode(x) for x in batch]
+        fut = batcher.call(lambda: llm.embed(ids))
+        vecs = await asyncio.wrap_future(fut)
+        return {"object": "list", "model": model_name,
+                "data": [{"object": "embedding", "index": i, "embedding": v.tolist()}
+                         for i, v in enumerate(vecs)],
+                "usage": {"prompt_tokens": sum(len(x) for x in ids),
+                          "total_tokens": sum(len(x) for x in ids)}}
 
     @app.post("/tokenize")
     async def tokenize(body: dict):
