@@ -408,3 +408,16 @@ def test_embeddings(client):
     assert torch.allclose(torch.tensor(r2["data"][0]["embedding"]), vs[0], atol=1e-6)
     direct = client.llm.embed([ids])[0]
     assert torch.allclose(direct, vs[0], atol=1e-6) and r["usage"]["prompt_tokens"] == 9
+
+
+def test_stream_usage_and_max_completion_tokens(client):
+    ev = _events(client, "/v1/completions", {
+        "prompt": list(range(7, 17)), "max_tokens": 5, "temperature": 0.0, "ignore_eos": True,
+        "stream": True, "stream_options": {"include_usage": True}})
+    assert ev[-1]["choices"] == [] and ev[-1]["usage"] == {
+        "prompt_tokens": 10, "completion_tokens": 5, "total_tokens": 15}
+    ev = _events(client, "/v1/chat/completions", {
+        "messages": [{"role": "user", "content": "q"}], "max_completion_tokens": 3,
+        "temperature": 0.0, "ignore_eos": True, "stream": True,
+        "stream_options": {"include_usage": True}})
+    assert ev[-1]["usage"]["completion_tokens"] == 3

@@ -391,7 +391,7 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
     if eos is not None and not ignore_eos:
         stop_ids.append(int(eos))
     top_k = body.get("top_k")
-    mt = body.get("max_tokens")
+    mt = body.get("max_completion_tokens", body.get("max_tokens"))
     return SamplingParams(max_tokens=16 if mt is None else int(mt),
                           logprobs=n_lp, prompt_logprobs=prompt_lp,
                           temperature=float(body.get("temperature", 1.0)),
@@ -515,13 +515,14 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             if not done and q.rid is not None:
                 batcher.abort(q.rid)
 
-    def stream_completion(prompt_ids, sp, stop):
+    def stream_completion(prompt_ids, sp, stop, usage=False):
         q = start_stream(prompt_ids, sp)
         rid, made = f"cmpl-{uuid.uuid4().hex}", int(time.time())
 
         async def events():
             ts = _TextStream(decode) if tokenizer is not None else None
             hit = stopped = False
+            n_gen = 0
             while True:
                 ids, fin = await q.get()
                 if ids is None:
@@ -541,8 +542,14 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                           else None}
                 yield _sse({"id": rid, "object": "text_completion", "created": made,
                             "model": model_name, "choices": [choice]})
+                n_gen += len(ids)
                 if fin:
                     break
+            if usage:
+                yield _sse({"id": rid, "object": "text_completion", "created": made,
+                            "model": model_name, "choices": [],
+                            "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": n_gen,
+                                      "total_tokens": len(prompt_ids) + n_gen}})
             yield "data: [DONE]\n\n"
 
         return StreamingResponse(guarded(events(), q), media_type="text/event-stream")
@@ -610,7 +617,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         if body.get("stream"):
             if len(ids) != 1:
                 raise HTTPException(400, "streaming serves one prompt per request")
-            return stream_completion(ids[0], sp, body.get("stop"))
+            return stream_completion(ids[0], sp, body.get("stop"),
+                                     bool((body.get("stream_options") or {}).get("include_usage")))
         n = int(body.get("n", 1))
         jobs = [(pi, spj) for pi in range(len(ids)) for spj in _samples(sp, n)]
         try:
@@ -648,7 +656,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 "usage": {"prompt_tokens": sum(len(p) for p in ids), "completion_tokens": n_out,
                           "total_tokens": sum(len(p) for p in ids) + n_out}}
 
-    def stream_chat(prompt_ids, sp, kwargs, stop):
+    def stream_chat(prompt_ids, sp, kwargs, stop, usage=False):
         q = start_stream(prompt_ids, sp)
         rid, made = f"chatcmpl-{uuid.uuid4().hex}", int(time.time())
         splitter = None
@@ -668,6 +676,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         async def events():
             yield chunk({"role": "assistant"})
             stopped = hit = False
+            n_gen = 0
             content_sent = ""
             while True:
                 ids, fin = await q.get()
@@ -690,9 +699,15 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                         content_sent += c
                 if delta:
                     yield chunk(delta)
+                n_gen += len(ids)
                 if fin:
                     yield chunk({}, "stop" if (stopped or hit) else "length")
                     break
+            if usage:
+                yield _sse({"id": rid, "object": "chat.completion.chunk", "created": made,
+                            "model": model_name, "choices": [],
+                            "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": n_gen,
+                                      "total_tokens": len(prompt_ids) + n_gen}})
             yield "data: [DONE]\n\n"
 
         return StreamingResponse(guarded(events(), q), media_type="text/event-stream")
@@ -711,7 +726,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         ids = list(tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True,
                                                  tokenize=True, **tpl))
         if body.get("stream"):
-            return stream_chat(ids, sp, kwargs, body.get("stop"))
+            return stream_chat(ids, sp, kwargs, body.get("stop"),
+                               bool((body.get("stream_options") or {}).get("include_usage")))
         try:
             outs = await asyncio.gather(*[run(ids, spj)
                                           for spj in _samples(sp, int(body.get("n", 1)))])
