@@ -421,3 +421,22 @@ def test_stream_usage_and_max_completion_tokens(client):
         "temperature": 0.0, "ignore_eos": True, "stream": True,
         "stream_options": {"include_usage": True}})
     assert ev[-1]["usage"]["completion_tokens"] == 3
+
+
+def test_health_reports_a_dead_engine():
+    """/health turns 503 once the engine loop stopped on an error; pending and
+    new requests fail instead of hanging; ``LLM`` is a context manager."""
+    from fastapi.testclient import TestClient
+
+    with LLM(TINY, max_num_seqs=2, max_model_len=64, block_size=16, dtype=torch.float32,
+             enforce_eager=True, max_num_batched_tokens=32) as llm:
+        def boom(*a, **k):
+            raise RuntimeError("device lost")
+        llm.runner.prefill = boom
+        with TestClient(build_app(llm, None, "tiny"), raise_server_exceptions=False) as c:
+            assert c.get("/health").status_code == 200
+            assert c.get("/v1/models").json()["data"][0]["max_model_len"] == 64
+            r = c.post("/v1/completions", json={"prompt": [1, 2, 3], "max_tokens": 2})
+            assert r.status_code == 500
+            h = c.get("/health")
+            assert h.status_code == 503 and "device lost" in h.json()["error"]

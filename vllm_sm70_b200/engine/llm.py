@@ -270,6 +270,12 @@ class LLM:
         blob = json.dumps(ident, sort_keys=True, default=str).encode()
         return hashlib.sha256(blob).hexdigest()[:20]
 
+    def __enter__(self) -> "LLM":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.shutdown()
+
     def shutdown(self) -> None:
         """Release CUDA graphs (they may hold NCCL work) before the process
         group is destroyed."""

@@ -556,6 +556,13 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
 
     @app.get("/health")
     async def health():
+        """200 while the engine loop runs; 503 once it has stopped on an error
+        (an orchestrator should restart the server)."""
+        if batcher._dead is not None or not batcher.thread.is_alive():
+            from fastapi.responses import JSONResponse
+
+            return JSONResponse({"status": "engine stopped", "error": str(batcher._dead)},
+                                status_code=503)
         return {"status": "ok"}
 
     @app.get("/metrics")
@@ -602,7 +609,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
     @app.get("/v1/models")
     async def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model",
-                                            "created": created, "owned_by": "vllm-b200"}]}
+                                            "created": created, "owned_by": "vllm-b200",
+                                            "max_model_len": llm.runner.max_model_len}]}
 
     @app.post("/v1/completions")
     async def completions(body: dict):
