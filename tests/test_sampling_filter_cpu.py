@@ -114,3 +114,30 @@ def test_penalties_match_dense_reference():
         assert got[1].output_token_ids == plain
     strong = llm.generate([p], SamplingParams(max_tokens=8, frequency_penalty=50.0))[0]
     assert len(set(strong.output_token_ids)) == 8  # every repeat is penalised away
+
+
+def test_min_p_keeps_only_likely_tokens():
+    """Every token sampled with ``min_p`` is in its step's min_p set
+    (probability >= min_p x the top one, i.e. logit >= max + T log min_p),
+    checked against a dense teacher-forced forward; min_p = 1 is greedy."""
+    import math
+
+    from ._llama_ref import llama_logits
+
+    llm = _llm()
+    T, mp = 1.0, 0.5
+
+    def violations(sp):
+        n = 0
+        for p, o in zip(_prompts(), llm.generate(_prompts(), sp)):
+            seq = torch.cat([p, torch.tensor(o.output_token_ids)])
+            for k, tok in enumerate(o.output_token_ids):
+                lg = llama_logits(llm.model, seq[: p.numel() + k])[-1]
+                n += float(lg[tok]) < float(lg.max()) + T * math.log(mp) - 1e-4
+        return n
+
+    assert violations(SamplingParams(max_tokens=6, temperature=T, min_p=mp, seed=5)) == 0
+    assert violations(SamplingParams(max_tokens=6, temperature=T, seed=5)) > 0  # discriminates
+    greedy = [o.output_token_ids for o in llm.generate(_prompts(), SamplingParams(max_tokens=5))]
+    top = SamplingParams(max_tokens=5, temperature=2.0, min_p=1.0, seed=3)
+    assert [o.output_token_ids for o in llm.generate(_prompts(), top)] == greedy

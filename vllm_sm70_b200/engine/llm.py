@@ -80,7 +80,7 @@ class GenerateStats:
 
 def _penalized(p: SamplingParams) -> bool:
     return (p.repetition_penalty != 1.0 or p.presence_penalty != 0.0
-            or p.frequency_penalty != 0.0)
+            or p.frequency_penalty != 0.0 or p.min_p > 0.0)
 
 
 def _filters(p: SamplingParams) -> bool:
@@ -654,7 +654,7 @@ class LLM:
                                     seed & 0x7FFFFFFFFFFFFFFF, sp.top_k, sp.top_p,
                                     sp.repetition_penalty, sp.presence_penalty,
                                     sp.frequency_penalty,
-                                    r.prompt if runner.penalties else None)
+                                    r.prompt if runner.penalties else None, sp.min_p)
                 admitted.append(r)
             if not admitted and not running and not prefilling:
                 if not waiting:  # (online) every new request was refused above

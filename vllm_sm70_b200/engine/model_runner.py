@@ -72,6 +72,7 @@ class ModelRunner:
         self.rep_pen = torch.ones(B, dtype=torch.float32, device=dev)
         self.pres_pen = torch.zeros(B, dtype=torch.float32, device=dev)
         self.freq_pen = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.min_p = torch.zeros(B, dtype=torch.float32, device=dev)
         self.prompt_ids: torch.Tensor | None = None  # [B, max_model_len], -1 padded
         self.penalties = False
         # Decode graphs always sample through the temperature path: rows with
@@ -181,8 +182,24 @@ class ModelRunner:
             seen = counts > 0
             rp = self.rep_pen.index_select(0, rows)[:, None]
             lg = torch.where(seen | (pseen > 0), torch.where(lg > 0, lg / rp, lg * rp), lg)
-            return (lg - self.freq_pen.index_select(0, rows)[:, None] * counts
-                    - self.pres_pen.index_select(0, rows)[:, None] * seen.float())
+            lg = (lg - self.freq_pen.index_select(0, rows)[:, None] * counts
+                  - self.pres_pen.index_select(0, rows)[:, None] * seen.float())
+            mp = self.min_p.index_select(0, rows)
+            if bool((mp > 0).any()):
+                # p_i >= min_p * p_max  <=>  logit_i >= max logit + T * log(min_p),
+                # with the row maximum over every vocab shard
+                mx = lg.max(1).values
+                from ..parallel import state as pstate
+
+                if pstate.get().tp_size > 1:
+                    import torch.distributed as dist
+
+                    dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=pstate.get().tp_group)
+                t = self.temperature.index_select(0, rows).clamp_min(1e-6)
+                cut = mx + t * torch.log(mp.clamp_min(1e-30))
+                lg = torch.where((mp[:, None] > 0) & (lg < cut[:, None]),
+                                 torch.full_like(lg, float("-inf")), lg)
+            return lg
         return apply
 
     @staticmethod
@@ -244,7 +261,7 @@ class ModelRunner:
     def set_sampling(self, slot: int, temperature: float, seed: int, top_k: int = -1,
                      top_p: float = 1.0, repetition_penalty: float = 1.0,
                      presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
-                     prompt: torch.Tensor | None = None) -> None:
+                     prompt: torch.Tensor | None = None, min_p: float = 0.0) -> None:
         self.temperature[slot] = float(temperature)
         self.seeds[slot] = int(seed)
         self.top_k[slot] = int(top_k) if top_k > 0 else -1
@@ -252,6 +269,7 @@ class ModelRunner:
         self.rep_pen[slot] = float(repetition_penalty)
         self.pres_pen[slot] = float(presence_penalty)
         self.freq_pen[slot] = float(frequency_penalty)
+        self.min_p[slot] = float(min_p)
         if prompt is not None:  # the prompt's tokens count for the repetition penalty
             if self.prompt_ids is None:
                 self.prompt_ids = torch.full((self.B, self.max_model_len), -1, dtype=torch.int64,

@@ -17,6 +17,7 @@ class SamplingParams:
     stop: list[str] = field(default_factory=list)   # stop strings (needs a tokenizer)
     include_stop_str_in_output: bool = False
     min_tokens: int = 0                              # stop tokens / strings ignored before
+    min_p: float = 0.0                   # drop tokens below min_p x the top probability
     repetition_penalty: float = 1.0      # > 1 discourages prompt / output tokens
     presence_penalty: float = 0.0        # subtracted once per token present in the output
     frequency_penalty: float = 0.0       # subtracted per occurrence in the output

@@ -398,6 +398,7 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           top_k=int(top_k) if top_k is not None else -1,
                           top_p=float(body.get("top_p", 1.0)),
                           repetition_penalty=float(body.get("repetition_penalty", 1.0)),
+                          min_p=float(body.get("min_p", 0.0)),
                           presence_penalty=float(body.get("presence_penalty", 0.0)),
                           frequency_penalty=float(body.get("frequency_penalty", 0.0)),
                           seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids)
