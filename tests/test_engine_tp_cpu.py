@@ -49,6 +49,12 @@ def test_tp_equals_tp1_cpu(tmp_path, tp):
     assert tp1 == got
 
 
+def _minp():
+    from vllm_sm70_b200.engine import SamplingParams
+
+    return SamplingParams(max_tokens=6, temperature=1.0, min_p=0.5, seed=9)
+
+
 def _pen_body(rank, world, path, out_file):
     from pathlib import Path
 
@@ -59,6 +65,7 @@ def _pen_body(rank, world, path, out_file):
     llm = LLM(str(path), tensor_parallel_size=world, load_format="safetensors", **KW)
     sp = SamplingParams(max_tokens=6, repetition_penalty=1.7, frequency_penalty=0.5)
     toks = [o.output_token_ids for o in llm.generate(_prompts(), sp)]
+    toks += [o.output_token_ids for o in llm.generate(_prompts(), _minp())]
     if rank == 0:
         Path(out_file).write_text(json.dumps(toks))
     llm.shutdown()
@@ -66,8 +73,9 @@ def _pen_body(rank, world, path, out_file):
 
 
 def test_tp2_penalties_equal_tp1_cpu(tmp_path):
-    """Sampling penalties on vocab-parallel logit shards (each rank rewrites
-    its own slice) give the TP1 tokens."""
+    """Sampling penalties and min_p on vocab-parallel logit shards (each rank
+    rewrites its own slice; min_p's row maximum is reduced over the shards)
+    give the TP1 tokens."""
     from vllm_sm70_b200.engine import LLM, SamplingParams
 
     _checkpoint(tmp_path)
@@ -75,4 +83,6 @@ def test_tp2_penalties_equal_tp1_cpu(tmp_path):
     _mp.run(_pen_body, 2, args=(str(tmp_path), str(out_file)), timeout=300)
     one = LLM(str(tmp_path), tensor_parallel_size=1, load_format="safetensors", **KW)
     sp = SamplingParams(max_tokens=6, repetition_penalty=1.7, frequency_penalty=0.5)
-    assert json.loads(out_file.read_text()) == [o.output_token_ids for o in one.generate(_prompts(), sp)]
+    want = [o.output_token_ids for o in one.generate(_prompts(), sp)]
+    want += [o.output_token_ids for o in one.generate(_prompts(), _minp())]
+    assert json.loads(out_file.read_text()) == want
