@@ -369,3 +369,11 @@ def test_stop_strings_and_min_tokens():
     cut = llm.generate(["hello"], SamplingParams(max_tokens=8, stop=[stop]))[0]
     assert cut.text == full.text[: full.text.find(stop)]
     assert cut.output_token_ids == full.output_token_ids[: len(cut.text) + len(stop)]
+
+
+def test_vllm_style_outputs():
+    """vLLM-style call and result shape: ``use_tqdm`` is accepted and
+    ``outputs[0].token_ids`` mirrors ``output_token_ids``."""
+    llm = _llm()
+    o = llm.generate([list(range(20, 30))], SamplingParams(max_tokens=3), use_tqdm=False)[0]
+    assert o.outputs[0].token_ids == o.output_token_ids and o.outputs[0].index == 0

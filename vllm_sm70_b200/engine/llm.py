@@ -477,7 +477,8 @@ class LLM:
 
     def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
                  collect_stats: bool = True, on_tokens=None,
-                 stream_interval: int = 0, feed=None, on_finish=None) -> list[RequestOutput]:
+                 stream_interval: int = 0, feed=None, on_finish=None,
+                 use_tqdm: bool = False) -> list[RequestOutput]:
         """Serve the prompts to completion; returns one output per prompt.
 
         Streaming: ``on_tokens(request_index, new_token_ids, finished)`` is

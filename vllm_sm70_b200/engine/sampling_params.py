@@ -30,6 +30,16 @@ class SamplingParams:
 
 
 @dataclass
+class CompletionOutput:
+    """vLLM's per-sample view (``RequestOutput.outputs[i]``)."""
+    index: int
+    text: str | None
+    token_ids: list[int]
+    logprobs: list | None = None
+    finish_reason: str | None = None
+
+
+@dataclass
 class RequestOutput:
     request_id: int
     prompt_token_ids: list[int]
@@ -43,3 +53,9 @@ class RequestOutput:
     logprobs: list | None = None
     prompt_logprobs: list | None = None
     text: str | None = None        # the decoded output, when the engine has a tokenizer
+
+    @property
+    def outputs(self) -> list[CompletionOutput]:
+        """vLLM's shape: ``outputs[0].text`` / ``outputs[0].token_ids``."""
+        reason = "abort" if self.error == "aborted" else ("error" if self.error else None)
+        return [CompletionOutput(0, self.text, self.output_token_ids, self.logprobs, reason)]
