@@ -377,3 +377,17 @@ def test_vllm_style_outputs():
     llm = _llm()
     o = llm.generate([list(range(20, 30))], SamplingParams(max_tokens=3), use_tqdm=False)[0]
     assert o.outputs[0].token_ids == o.output_token_ids and o.outputs[0].index == 0
+
+
+def test_n_samples_offline():
+    """``SamplingParams(n=3)``: one RequestOutput per prompt whose
+    ``outputs`` holds the three samples (seeded: distinct, reproducible)."""
+    llm = _llm()
+    sp = SamplingParams(max_tokens=6, temperature=1.5, seed=11, n=3)
+    prompts = [list(range(20, 30)), list(range(40, 47))]
+    a = llm.generate(prompts, sp)
+    b = llm.generate(prompts, sp)
+    assert len(a) == 2 and [len(o.outputs) for o in a] == [3, 3]
+    assert [[c.token_ids for c in o.outputs] for o in a] == [[c.token_ids for c in o.outputs] for o in b]
+    assert len({tuple(c.token_ids) for c in a[0].outputs}) > 1
+    assert [c.index for c in a[1].outputs] == [0, 1, 2] and a[1].request_id == 1

@@ -512,6 +512,8 @@ class LLM:
                                        dtype=torch.int64) for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
+        if any(p.n > 1 for p in params) and feed is None:
+            return self._generate_n(prompts, params, collect_stats, on_tokens, stream_interval)
         filtering = any(_filters(p) for p in params)
         if filtering and self.spec_k:
             raise NotImplementedError("top-k / top-p with speculative decoding")
@@ -524,6 +526,29 @@ class LLM:
         finally:
             runner.filtering = False
             runner.penalties = False
+
+    def _generate_n(self, prompts, params, collect_stats, on_tokens, stream_interval):
+        """``n`` samples per prompt: each sample is its own request (distinct
+        seeds: the given one + i, or the per-request default), run in one
+        batch; sample i > 0 goes to the first sample's ``more``."""
+        import dataclasses
+
+        flat_p, flat_sp, owner = [], [], []
+        for i, (p, sp) in enumerate(zip(prompts, params)):
+            for j in range(max(1, sp.n)):
+                flat_p.append(p)
+                flat_sp.append(dataclasses.replace(
+                    sp, n=1, seed=None if sp.seed is None else int(sp.seed) + j))
+                owner.append(i)
+        outs = self.generate(flat_p, flat_sp, collect_stats, on_tokens, stream_interval)
+        merged: list[RequestOutput] = []
+        for i, o in zip(owner, outs):
+            if i == len(merged):
+                o.request_id = i
+                merged.append(o)
+            else:
+                merged[i].more = (merged[i].more or []) + [o]
+        return merged
 
     def _generate(self, reqs: list[_Req], on_tokens=None, stream_interval: int = 0,
                   feed=None, on_finish=None) -> list[RequestOutput]:

@@ -8,6 +8,7 @@ from dataclasses import dataclass, field
 @dataclass
 class SamplingParams:
     max_tokens: int = 16
+    n: int = 1                            # samples per prompt (LLM.generate)
     temperature: float = 0.0
     top_k: int = -1
     top_p: float = 1.0
@@ -53,9 +54,14 @@ class RequestOutput:
     logprobs: list | None = None
     prompt_logprobs: list | None = None
     text: str | None = None        # the decoded output, when the engine has a tokenizer
+    more: list | None = None       # samples 2..n (RequestOutput each) when n > 1
 
     @property
     def outputs(self) -> list[CompletionOutput]:
-        """vLLM's shape: ``outputs[0].text`` / ``outputs[0].token_ids``."""
-        reason = "abort" if self.error == "aborted" else ("error" if self.error else None)
-        return [CompletionOutput(0, self.text, self.output_token_ids, self.logprobs, reason)]
+        """vLLM's shape: ``outputs[i].text`` / ``outputs[i].token_ids``, one
+        entry per sample."""
+        out = []
+        for i, o in enumerate([self] + list(self.more or [])):
+            reason = "abort" if o.error == "aborted" else ("error" if o.error else None)
+            out.append(CompletionOutput(i, o.text, o.output_token_ids, o.logprobs, reason))
+        return out
