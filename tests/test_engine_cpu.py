@@ -391,3 +391,18 @@ def test_n_samples_offline():
     assert [[c.token_ids for c in o.outputs] for o in a] == [[c.token_ids for c in o.outputs] for o in b]
     assert len({tuple(c.token_ids) for c in a[0].outputs}) > 1
     assert [c.index for c in a[1].outputs] == [0, 1, 2] and a[1].request_id == 1
+
+
+def test_n_samples_ids_and_streaming_guard():
+    """n > 1: every sample reports its prompt's index; streaming callbacks
+    (which take one index per stream) are refused instead of receiving flat
+    sample indices."""
+    import pytest
+
+    llm = _llm()
+    sp = SamplingParams(max_tokens=3, temperature=1.0, seed=5, n=2)
+    outs = llm.generate([list(range(20, 30)), list(range(40, 47))], sp)
+    assert [o.request_id for o in outs] == [0, 1]
+    assert all(m.request_id == o.request_id for o in outs for m in (o.more or []))
+    with pytest.raises(ValueError, match="n = 1"):
+        llm.generate([list(range(20, 30))], sp, on_tokens=lambda *a: None)

@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 CFGS = {"n256": 0, "n128": 1, "swap16": 2, "swap32": 3, "swap64": 4, "n192": 5, "n96": 6,
         "n64": 7, "swap128": 8, "m2n256": 9, "m2n224": 10, "m2n128": 11, "m2n112": 12,
         "m2n64": 13, "cl_n256": 14, "cl_n128": 15, "cl_m2n128": 16, "cl_m2n112": 17,
-        "cl_m2n64": 18, "p2n256": 19, "p2n128": 20, "p2n192": 21, "p2n64": 22}
+        "cl_m2n64": 18, "p2n256": 19, "p2n128": 20, "p2n192": 21, "p2n64": 22, "p2n96": 23}
 # cluster split-K config -> the plain tile of the same shape (same summation order)
 CL_PLAIN = {"cl_n256": "n256", "cl_n128": "n128", "cl_m2n128": "m2n128", "cl_m2n112": "m2n112",
             "cl_m2n64": "m2n64"}
@@ -103,7 +103,7 @@ def test_gemm_split_k(b200_ops, cfg, splits, rel_err):
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
 
 
-@pytest.mark.parametrize("cfg", ["p2n256", "p2n128", "p2n192", "p2n64"])
+@pytest.mark.parametrize("cfg", ["p2n256", "p2n128", "p2n192", "p2n64", "p2n96"])
 @pytest.mark.parametrize("M,N,K", [(256, 1024, 4096), (300, 640, 520), (1024, 2048, 1024),
                                    (128, 256, 64), (777, 1536, 2048)])
 def test_gemm_cta_pair(b200_ops, cfg, M, N, K, rel_err):
@@ -115,7 +115,7 @@ def test_gemm_cta_pair(b200_ops, cfg, M, N, K, rel_err):
     assert rel_err(out, _ref(a, w)) < 1e-2, (cfg, M, N, K)
 
 
-@pytest.mark.parametrize("cfg", ["p2n256", "p2n128"])
+@pytest.mark.parametrize("cfg", ["p2n256", "p2n128", "p2n96"])
 @pytest.mark.parametrize("splits", [2, 3, 8])
 def test_gemm_cta_pair_split_k(b200_ops, cfg, splits, rel_err):
     torch.manual_seed(10)
@@ -247,3 +247,37 @@ def test_silu_mul_interleaved_and_library_route(b200_ops, rel_err):
         assert rel_err(linear.gemm_silu_mul(a, wi), ref) < 2e-2
     finally:
         linear.clear_library()
+
+
+@pytest.mark.parametrize("cfg,M", [("n128", 1024), ("p2n128", 2048), ("swap64", 200)])
+@pytest.mark.parametrize("splits", [2, 3])
+def test_gemm_split_k_multi_round(b200_ops, cfg, M, splits, rel_err):
+    """More split units than resident CTAs: the serial (last-arriving split)
+    reduction, not the distributed one-round reduction, runs; results are
+    correct and bitwise repeatable."""
+    torch.manual_seed(12)
+    N, K = 4096, 2048
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    outs = [linear.gemm(a, w, cfg=CFGS[cfg], splits=splits) for _ in range(2)]
+    torch.cuda.synchronize()
+    assert rel_err(outs[0], _ref(a, w)) < 1e-2
+    assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 6144, 4096), (256, 4096, 14336), (256, 4096, 4096)])
+def test_gemm_decode_shapes_all_plans(b200_ops, M, N, K, rel_err):
+    """Every tuner candidate (tile config x split) on the decode shapes of the
+    headline model: correct, and repeatable bit for bit."""
+    from vllm_sm70_b200.engine import warmup
+
+    torch.manual_seed(13)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    ref = _ref(a, w)
+    for cfg, sp in warmup.candidates(M, N, K, 0):
+        o1 = linear.gemm(a, w, cfg=cfg, splits=sp)
+        o2 = linear.gemm(a, w, cfg=cfg, splits=sp)
+        torch.cuda.synchronize()
+        assert rel_err(o1, ref) < 1e-2, (cfg, sp)
+        assert torch.equal(o1, o2), (cfg, sp)

@@ -205,6 +205,7 @@ def test_top_level_cli_dispatch(monkeypatch, capsys):
     assert cli.main(["convert-gguf", "a.gguf", "out"]) == 0 and seen == [["a.gguf", "out"]]
     assert cli.main([]) == 0 and "serve" in capsys.readouterr().out
     assert cli.main(["nope"]) == 2
-    from vllm_sm70_b200.integration.models import ARCHS
+    from vllm_sm70_b200.integration.models import ENGINE_ARCHS, VLLM_ARCHS
 
-    assert ARCHS["B200FlintForCausalLM"].endswith(":FlintModel")
+    assert ENGINE_ARCHS["flint"].endswith(":FlintModel")
+    assert VLLM_ARCHS["B200LlamaForCausalLM"].endswith(":B200LlamaForCausalLM")

@@ -73,3 +73,30 @@ def test_noalloc_rejects_oversized_split(b200_ops):
     assert rc == EINVAL
     torch.cuda.synchronize()
     assert bool((out == 7.0).all())  # nothing was launched
+
+
+def test_noalloc_on_two_devices(b200_ops):
+    """One process driving two GPUs: the entry point's per-device set-up (the
+    static scratch address and the kernel's shared-memory limit) must run on
+    each device, so the second device's calls succeed as well."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    lib = _lib()
+    M, N, K, cfg, splits = 64, 2048, 4096, 2, 4
+    prev = torch.cuda.current_device()
+    try:
+        for dev in (0, 1, 0, 1):
+            torch.cuda.set_device(dev)
+            g = torch.Generator(device="cuda").manual_seed(11 + dev)
+            a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+            w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+            out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+            rc = _call(lib, out, a, w, cfg, splits)
+            assert rc == OK, (dev, lib.b200_gemm_bf16_noalloc_last_error())
+            torch.cuda.synchronize()
+            torch.testing.assert_close(out.float(), a.float() @ w.float().t(), atol=5e-2, rtol=2e-2)
+            st = ctypes.c_uint(123)
+            assert lib.b200_gemm_bf16_noalloc_status(ctypes.byref(st)) == OK
+            assert st.value == 0
+    finally:
+        torch.cuda.set_device(prev)

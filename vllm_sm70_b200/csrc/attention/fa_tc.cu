@@ -518,14 +518,8 @@ bool fa_tc_supported(const AttnArgs& a) {
 
 void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
   auto kernel = fa_tc_kernel;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFaSmem);
-    if (e != cudaSuccess)
-      throw std::runtime_error(std::string("fa_tc attribute: ") + cudaGetErrorString(e));
-    attr = true;
-  }
+  static bool attr[kMaxDevices] = {};
+  set_smem_attr_once(kernel, kFaSmem, attr, "fa_tc");
   const int G = a.Hq / a.Hkv;
   const int BS = a.block_size;
   const long long blk_stride = a.kv_block_stride > 0 ? a.kv_block_stride

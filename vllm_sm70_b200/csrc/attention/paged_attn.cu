@@ -840,13 +840,8 @@ template <int D, int KT, int STAGES>
 void launch_decode_tma(const Params& p, const AttnArgs& a, cudaStream_t stream) {
   constexpr int smem = decode_tma_smem<D, KT, STAGES>();
   auto kernel = decode_tma_kernel<D, KT, STAGES>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess)
-      throw std::runtime_error(std::string("decode_tma attribute: ") + cudaGetErrorString(e));
-    attr = true;
-  }
+  static bool attr[kMaxDevices] = {};
+  set_smem_attr_once(kernel, smem, attr, "decode_tma");
   const int BS = a.block_size;
   const uint32_t rows_box = (uint32_t)(BS >= KT ? KT : BS);
   const uint64_t rows = (uint64_t)a.Hkv * BS;
@@ -880,11 +875,8 @@ void launch_attn(const Params& p, cudaStream_t stream) {
   static_assert(!DECODE || STAGES * 2 * KT * D * 2 >= (NW * 16 * D + NW * 32) * 4,
                 "decode merge buffer must fit in the K/V ring");
   auto kernel = paged_attn_kernel<D, KT, NW, STAGES, DECODE>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  static bool attr[kMaxDevices] = {};
+  set_smem_attr_once(kernel, smem, attr, "paged_attn");
   const int row_tiles = (p.rows_per_seq_max + ROWS - 1) / ROWS;
   dim3 grid(row_tiles, p.num_seqs, p.Hkv * (DECODE ? p.num_splits : 1));
   launch_pdl(kernel, grid, dim3(NW * 32), smem, stream, nullptr, p);

@@ -40,6 +40,25 @@ inline bool pdl_enabled() {
   return on;
 }
 
+// cudaFuncSetAttribute applies to the current device only: a process that
+// drives several GPUs sets the dynamic shared-memory limit once per device.
+// `done` is one flag array per kernel instantiation (a function-local static).
+constexpr int kMaxDevices = 64;
+template <typename Kernel>
+inline void set_smem_attr_once(Kernel kernel, int bytes, bool (&done)[kMaxDevices],
+                               const char* what) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices)
+    throw std::runtime_error(std::string(what) + ": device index out of range");
+  if (done[dev]) return;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string(what) + " attribute: " + cudaGetErrorString(e));
+  done[dev] = true;
+}
+
 // cudaLaunchKernelEx with the programmatic-serialization attribute (when
 // enabled) plus up to one extra attribute (e.g. a cluster shape).
 template <typename... KArgs, typename... Args>

@@ -113,6 +113,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// Bounded acquire-spin (GPU scope) until *p >= target. Used by CTAs of one
+// launch that are all resident at once (never across launches); returns false
+// and records kErrMbarTimeout on timeout or when another role already failed.
+__device__ __forceinline__ bool wait_geq_gpu(const int* p, int target, unsigned int* err) {
+  const unsigned long long t0 = globaltimer();
+  uint32_t spins = 0;
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    if ((++spins & 63u) == 0) {
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        if (err) atomicCAS(err, kErrNone, kErrMbarTimeout);
+        return false;
+      }
+      if (err && *(volatile unsigned int*)err != kErrNone) return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

@@ -46,7 +46,8 @@ enum GemmConfig : int {
   kCfgP2N128 = 20,   // 256 x 128, 8 stages
   kCfgP2N192 = 21,   // 256 x 192, 7 stages
   kCfgP2N64 = 22,    // 256 x 64, 10 stages
-  kCfgCount = 23,
+  kCfgP2N96 = 23,    // 256 x 96, 9 stages (decode: 64 pairs over N = 6144)
+  kCfgCount = 24,
 };
 
 constexpr int kMaxSplits = 8;

@@ -212,6 +212,12 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   const int num_kb = (K + BK - 1) / BK;
   const int kb_per = (num_kb + splits - 1) / splits;
   const int num_units = grp.E > 0 ? __ldg(grp.tile_off + grp.E) * splits : num_tiles * splits;
+  // Distributed split-K reduction: when every unit runs in the first (only)
+  // round, all splits of a tile are resident together, so each split reduces
+  // the column chunks it owns (its own partial straight from TMEM, the others'
+  // from the workspace) instead of the last-arriving split reducing the whole
+  // tile. Same summation order (split 0, 1, ...) as the serial path.
+  const bool dist = splits > 1 && grp.E == 0 && num_units <= ustride;
   constexpr int kUsedCols = kNumAcc * kAccCols;
   constexpr uint32_t kTmemCols = (kUsedCols <= 32) ? 32 : (kUsedCols <= 64) ? 64
                                  : (kUsedCols <= 128) ? 128 : (kUsedCols <= 256) ? 256 : 512;
@@ -521,7 +527,60 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         }
       };
 
-      if (split) {
+      // Ownership of column chunks in the distributed reduction: CW-wide
+      // chunks (whole 128-column gate/up blocks for the SiLU epilogue) are
+      // dealt round-robin to the splits.
+      auto owned = [&](int col0) -> bool {
+        if (!dist) return true;
+        const int unit = EPI == kEpiSiluMul ? col0 / 128 : col0 / CW;
+        return unit % splits == sp;
+      };
+      const int ci = PAIR ? 2 * t + (int)prank : t;  // arrival counter of this tile (half)
+      if (split && dist) {
+        // Publish the chunks the other splits own (same workspace layout as
+        // the serial path), then wait until every split of the tile has.
+#pragma unroll 1
+        for (int h = 0; h < MH; ++h) {
+          float4* mine = reinterpret_cast<float4*>(ws_tile + (size_t)sp * (UT * BN) +
+                                                   (size_t)(hbase + h) * (BM * BN)) +
+                         row_in_tile;
+          const uint32_t t_row = t_acc + h * kHalfCols;
+#pragma unroll 1
+          for (int ch = 0; ch < BN / CW; ++ch) {
+            if (owned(ch * CW)) continue;
+            uint32_t r[32];
+            if constexpr (CW == 32) {
+              tmem_ld_32x32b_x32(t_row + ch * CW, r);
+            } else {
+              tmem_ld_32x32b_x16(t_row + ch * CW, *reinterpret_cast<uint32_t(*)[16]>(r));
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int v = 0; v < CW / 4; ++v)
+              __stcg(mine + (size_t)(ch * (CW / 4) + v) * BM,
+                     make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+          }
+        }
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (etid == 0) {
+          atomicAdd(&counters[ci], 1);
+          *last_flag = wait_geq_gpu(&counters[ci], splits, err) ? 1 : 0;
+        }
+        named_barrier_sync(1, 128);
+        const int arrived = *last_flag;
+        named_barrier_sync(1, 128);  // last_flag is rewritten below
+        if (!arrived) {
+          *abort_flag = 1;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_acc();
+          break;
+        }
+        __threadfence();
+      }
+      if (split && !dist) {
         // Column-group-major layout [BN/4][BM] of float4 per M half: the 32
         // lanes of a warp (consecutive rows) write 512 contiguous bytes per store.
 #pragma unroll 1
@@ -555,7 +614,6 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         if (etid == 0) B200_TL(9);
         named_barrier_sync(1, 128);
         if (etid == 0) {
-          const int ci = PAIR ? 2 * t + (int)prank : t;
           const int old = atomicAdd(&counters[ci], 1);
           const int last = old == splits - 1;
           if (last) counters[ci] = 0;  // re-arm for the next launch
@@ -577,7 +635,39 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       // Fetch 32 (or 16) tile columns of this thread's row: from TMEM, or the
       // fixed-order (split 0, 1, ...) sum of the partials.
       auto fetch = [&](int col0, float (&v)[32]) {
-        if (!split) {
+        if (dist) {
+          uint32_t r[32];
+          if constexpr (CW == 32) {
+            tmem_ld_32x32b_x32(t_row + col0, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + col0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] = 0.f;
+          for (int s2 = 0; s2 < splits; ++s2) {
+            if (s2 == sp) {
+#pragma unroll
+              for (int c = 0; c < CW; ++c) v[c] += __uint_as_float(r[c]);
+            } else {
+              const float4* src =
+                  reinterpret_cast<const float4*>(ws_half + (size_t)s2 * (UT * BN)) +
+                  (size_t)(col0 / 4) * BM + row_in_tile;
+              float4 x[CW / 4];
+#pragma unroll
+              for (int c4 = 0; c4 < CW / 4; ++c4) x[c4] = __ldcg(src + (size_t)c4 * BM);
+#pragma unroll
+              for (int c4 = 0; c4 < CW / 4; ++c4) {
+                v[4 * c4] += x[c4].x;
+                v[4 * c4 + 1] += x[c4].y;
+                v[4 * c4 + 2] += x[c4].z;
+                v[4 * c4 + 3] += x[c4].w;
+              }
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] *= out_scale;
+        } else if (!split) {
           uint32_t r[32];
           if constexpr (CW == 32) {
             tmem_ld_32x32b_x32(t_row + col0, r);
@@ -630,6 +720,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         for (int blk = 0; blk < BN / 128; ++blk) {
 #pragma unroll 1
           for (int half = 0; half < 2; ++half) {
+            if (!owned(blk * 128)) continue;
             float g[32], uu[32];
             fetch(blk * 128 + half * 32, g);
             fetch(blk * 128 + 64 + half * 32, uu);
@@ -658,6 +749,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       } else {
 #pragma unroll 1
         for (int ch = 0; ch < BN / CW; ++ch) {
+          if (!owned(ch * CW)) continue;
           float r[32];
           fetch(ch * CW, r);
           const int j0 = uc.out_j0 + ch * CW;
@@ -690,10 +782,19 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         }
       }
       }  // M halves
-      if (!split) {
+      if (!split || dist) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_acc();
+      }
+      if (dist) {
+        // Every split of the tile has passed its wait once the counter reaches
+        // 2 x splits; the last one re-arms it for the next launch.
+        named_barrier_sync(1, 128);
+        if (etid == 0) {
+          const int old = atomicAdd(&counters[ci], 1);
+          if (old == 2 * splits - 1) counters[ci] = 0;
+        }
       }
     }
   }
@@ -873,14 +974,8 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   }
   static_assert(S::kTotal <= 232448, "shared memory budget");
   auto kernel = gemm_bf16_tc_kernel<BN, STAGES, SWAP, EPI, WF, MH>;
-  static bool attr_set = false;  // per instantiation; idempotent if raced
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    if (e != cudaSuccess)
-      throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    attr_set = true;
-  }
+  static bool attr_set[kMaxDevices] = {};  // per instantiation and device; idempotent if raced
+  set_smem_attr_once(kernel, S::kTotal, attr_set, "gemm_bf16_tc");
   CUtensorMap tp;
   if constexpr (WF == kWBf16) {
     tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, K, (uint64_t)ldp * 2, pbox,
@@ -916,14 +1011,8 @@ void launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int l
   using S = Smem<BN, STAGES, kWBf16, MH>;
   static_assert(S::kTotal <= 232448, "shared memory budget");
   auto kernel = gemm_bf16_tc_kernel<BN, STAGES, false, EPI, kWBf16, MH, true>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    if (e != cudaSuccess)
-      throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    attr_set = true;
-  }
+  static bool attr_set[kMaxDevices] = {};  // per instantiation and device; idempotent if raced
+  set_smem_attr_once(kernel, S::kTotal, attr_set, "gemm_bf16_tc");
   CUtensorMap tp = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, (uint64_t)lda * 2,
                                 BM, BK);
   CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
@@ -960,14 +1049,8 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
   using S = Smem<BN / 2, STAGES, kWBf16, 1>;
   static_assert(S::kTotal <= 232448, "shared memory budget");
   auto kernel = gemm_bf16_tc_kernel<BN, STAGES, false, EPI, kWBf16, 1, false, true>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    if (e != cudaSuccess)
-      throw std::runtime_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    attr_set = true;
-  }
+  static bool attr_set[kMaxDevices] = {};  // per instantiation and device; idempotent if raced
+  set_smem_attr_once(kernel, S::kTotal, attr_set, "gemm_bf16_tc");
   CUtensorMap tp = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, (uint64_t)lda * 2,
                                 BM, BK);
   CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
@@ -1025,7 +1108,7 @@ constexpr CfgInfo kCfgInfo[kCfgCount] = {
     {112, false, 2, false, false}, {64, false, 2, false, false},  {256, false, 1, true, false},
     {128, false, 1, true, false},  {128, false, 2, true, false},  {112, false, 2, true, false},
     {64, false, 2, true, false},   {256, false, 1, false, true},  {128, false, 1, false, true},
-    {192, false, 1, false, true},  {64, false, 1, false, true},
+    {192, false, 1, false, true},  {64, false, 1, false, true},   {96, false, 1, false, true},
 };
 
 int cfg_bn(int cfg) { return (cfg >= 0 && cfg < kCfgCount) ? kCfgInfo[cfg].bn : 0; }
@@ -1144,6 +1227,7 @@ GemmPlan gemm_bf16_plan(int M, int N, int K, int epi, int num_sm) {
       cands[nc++] = kCfgP2N256;
       cands[nc++] = kCfgP2N192;
       cands[nc++] = kCfgP2N128;
+      cands[nc++] = kCfgP2N96;
     }
   }
   const int num_kb = (K + 63) / 64;
@@ -1313,6 +1397,9 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
       case kCfgP2N128:
         return launch_pair<128, 8, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
                                              stream);
+      case kCfgP2N96:
+        return launch_pair<96, 9, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
+                                            stream);
       default:
         return launch_pair<64, 10, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
                                              stream);
@@ -1383,6 +1470,7 @@ bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, i
   // Normal (non-swap, single-CTA) tiles only: the collective phase needs the
   // whole grid resident (grid <= SMs) and the stage in row-major order.
   switch (cfg) {
+    case kCfgP2N96: cfg = kCfgN96; break;
     case kCfgN192: case kCfgN96: case kCfgSwap128: case kCfgP2N128: case kCfgP2N192:
     case kCfgClN128: cfg = kCfgN128; break;
     case kCfgSwap16: case kCfgSwap32: case kCfgSwap64: case kCfgP2N64: cfg = kCfgN64; break;

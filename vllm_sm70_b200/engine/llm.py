@@ -533,6 +533,10 @@ class LLM:
         batch; sample i > 0 goes to the first sample's ``more``."""
         import dataclasses
 
+        if on_tokens is not None:
+            # A flat sample index is not a prompt index, and one callback stream
+            # per prompt cannot carry several samples' tokens apart.
+            raise ValueError("on_tokens streaming supports n = 1 per prompt only")
         flat_p, flat_sp, owner = [], [], []
         for i, (p, sp) in enumerate(zip(prompts, params)):
             for j in range(max(1, sp.n)):
@@ -543,8 +547,8 @@ class LLM:
         outs = self.generate(flat_p, flat_sp, collect_stats, on_tokens, stream_interval)
         merged: list[RequestOutput] = []
         for i, o in zip(owner, outs):
+            o.request_id = i  # every sample reports its prompt's index
             if i == len(merged):
-                o.request_id = i
                 merged.append(o)
             else:
                 merged[i].more = (merged[i].more or []) + [o]

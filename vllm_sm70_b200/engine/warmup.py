@@ -39,7 +39,8 @@ CFGS = {0: (256, False, 128), 1: (128, False, 128), 2: (16, True, 128), 3: (32, 
         8: (128, True, 128), 9: (256, False, 256), 10: (224, False, 256), 11: (128, False, 256),
         12: (112, False, 256), 13: (64, False, 256),
         # CTA pairs (cta_group::2): 256-row tiles over two SMs
-        19: (256, False, 256), 20: (128, False, 256), 21: (192, False, 256), 22: (64, False, 256)}
+        19: (256, False, 256), 20: (128, False, 256), 21: (192, False, 256), 22: (64, False, 256),
+        23: (96, False, 256)}
 # cluster split-K configs (the K slices of a tile reduce through distributed
 # shared memory): cfg id -> (BN, BM); only tried with splits >= 2
 CLUSTER_CFGS = {14: (256, 128), 15: (128, 128), 16: (128, 256), 17: (112, 256), 18: (64, 256)}

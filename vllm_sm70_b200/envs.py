@@ -61,6 +61,8 @@ _reg("VLLM_B200_SKIP_EXT", "optin", False, "plugin",
 _reg("VLLM_B200_GEMM", "kill", True, "kernels", "tcgen05 BF16 GEMM (0 = torch.matmul).")
 _reg("VLLM_B200_GEMM_SILU_EPILOGUE", "kill", True, "kernels",
      "Fuse SiLU*up into the gate_up GEMM epilogue.")
+_reg("VLLM_B200_RMSNORM", "kill", True, "kernels",
+     "RMSNorm / fused add + RMSNorm kernels as vLLM's first IR-op provider.")
 _reg("VLLM_B200_ATTN", "kill", True, "kernels", "Paged attention kernels (0 = SDPA reference).")
 _reg("VLLM_B200_ROPE_KV", "kill", True, "kernels", "Fused RoPE + KV-cache write kernel.")
 _reg("VLLM_B200_FP8_GEMM", "kill", True, "kernels", "Block-FP8 tcgen05 GEMM.")
@@ -84,9 +86,10 @@ _reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
 _reg("VLLM_B200_CUDA_GRAPHS", "kill", True, "runtime", "Capture decode steps in CUDA graphs.")
 _reg("VLLM_B200_GRAPH_MAX_BS", "int", 512, "runtime", "Largest captured decode batch.")
 _reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tuning.")
-_reg("VLLM_B200_GEMM_LIBRARY", "kill", True, "runtime",
-     "Let the warm-up tuner route a plain bf16 GEMM shape to cuBLAS when it measures faster "
-     "than every tcgen05 plan (fused / quantised / grouped GEMMs never are).")
+_reg("VLLM_B200_GEMM_LIBRARY", "optin", False, "runtime",
+     "Baseline switch, off by default: let the warm-up tuner route a plain bf16 GEMM shape to "
+     "the vendor library (cuBLAS) when it measures faster than every tcgen05 plan. With it off "
+     "every GEMM of the models runs the tcgen05 kernels.")
 _reg("VLLM_B200_FUSED_GEMM_AR", "kill", True, "comm",
      "TP > 1: run each row-parallel GEMM (o_proj, down_proj) and the following all-reduce + "
      "residual + RMSNorm as one kernel (tcgen05 tiles, then the collective over NVLink peer "

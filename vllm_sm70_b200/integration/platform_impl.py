@@ -90,8 +90,15 @@ class B200CudaPlatform(CudaPlatform):
 
     @classmethod
     def get_default_ir_op_priority(cls, vllm_config):
-        # Keep vLLM's choice; the B200 models call their own fused kernels.
-        return super().get_default_ir_op_priority(vllm_config)
+        """vLLM's CUDA defaults with the "b200" RMSNorm providers first
+        (``integration/ir_ops.py``); kill switch ``VLLM_B200_RMSNORM=0``."""
+        prio = super().get_default_ir_op_priority(vllm_config)
+        if not envs.get("VLLM_B200_RMSNORM"):
+            return prio
+        from . import ir_ops
+
+        ir_ops.register()
+        return ir_ops.with_b200_first(prio)
 
     # ------------------------------------------------------------ U1
     @classmethod

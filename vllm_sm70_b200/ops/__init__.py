@@ -19,3 +19,8 @@ def register() -> None:
 
     if _ext.load():
         _fakes.register_all()
+    # RMSNorm of vLLM models: the "b200" IR-op provider (first in the
+    # platform's priority list).
+    from ..integration import ir_ops
+
+    ir_ops.register()

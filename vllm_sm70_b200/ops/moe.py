@@ -186,9 +186,43 @@ def experts_forward(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: Exp
     return out
 
 
+class TopKRoute:
+    """Route of one vLLM MoE layer on the B200 top-k kernel: softmax or
+    sigmoid scores, optional per-expert correction bias, top-k with ties to
+    the lower expert id, optional renormalisation (``moe_topk``)."""
+
+    def __init__(self, top_k: int, renorm: bool, use_sigmoid: bool, bias=None):
+        self.top_k, self.renorm, self.use_sigmoid, self.bias = top_k, renorm, use_sigmoid, bias
+
+    def try_route(self, hidden_states, router_logits=None):
+        if router_logits is None or not router_logits.is_cuda or router_logits.dim() != 2:
+            return None
+        lg = router_logits
+        if lg.dtype not in (torch.float32, torch.bfloat16):
+            lg = lg.float()
+        return topk(lg.contiguous(), self.top_k, self.use_sigmoid, self.renorm, self.bias)
+
+
 def make_route_for_runner(runner):
-    """U3 provider hook: this library routes only its own MoE layers; vLLM's
-    upstream ``MoERunner`` objects keep upstream routing."""
+    """U3 provider hook: a :class:`TopKRoute` for a vLLM ``MoERunner`` whose
+    router is plain (fused) top-k over softmax / sigmoid scores without EPLB,
+    grouped top-k or custom routing; ``None`` keeps vLLM's routing. Layers of
+    this library's own models carry ``b200_route`` already."""
     if getattr(runner, "b200_route", None) is not None:
         return runner.b200_route
-    return None
+    router = getattr(runner, "router", None)
+    if router is None or type(router).__name__ not in ("FusedTopKRouter", "FusedTopKBiasRouter"):
+        return None
+    if getattr(router, "eplb_state", None) is not None and getattr(
+            router.eplb_state, "logical_to_physical_map", None) is not None:
+        return None
+    scoring = str(getattr(router, "scoring_func", "softmax"))
+    if scoring not in ("softmax", "sigmoid"):
+        return None
+    k = int(getattr(router, "top_k", 0))
+    if not 1 <= k <= 16:
+        return None
+    bias = getattr(router, "e_score_correction_bias", None)
+    if bias is not None:
+        bias = bias.float().contiguous()
+    return TopKRoute(k, bool(getattr(router, "renormalize", True)), scoring == "sigmoid", bias)
