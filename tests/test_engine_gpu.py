@@ -39,7 +39,11 @@ def test_prefill_logits_match_fp32_reference(b200_ops):
     assert err < 3e-2, float(err)
 
 
-def test_graph_decode_equals_eager(b200_ops):
+def test_graph_decode_equals_eager(b200_ops, monkeypatch):
+    # Both engines must run the same GEMM plans: the warm-up tuner picks plans
+    # by timing, and two independent tunings can choose different split-K
+    # counts (a different fp32 summation order) for the same shape.
+    monkeypatch.setenv("VLLM_B200_WARMUP", "0")
     torch.manual_seed(1)
     prompts = [torch.randint(0, SMALL.vocab_size, (n,)) for n in (5, 64, 130, 17, 300)]
     sp = SamplingParams(max_tokens=24, ignore_eos=True)
