@@ -160,6 +160,45 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
       : "memory");
 }
 
+// Untiled bulk copy this CTA's shared memory -> global (both addresses 16-byte
+// aligned, size a multiple of 16), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void bulk_store(void* dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+// 2D tiled store shared -> global through a tensor map (out-of-range box
+// elements are not written), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+// Waits until at most one committed bulk group of this thread still reads
+// its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until every committed bulk group of this thread has completed (its
+// global writes performed).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy accesses with its async-proxy (bulk /
+// tensor copy) accesses of shared or global memory.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Tiled bulk prefetch of a 2D box into L2 (no shared-memory destination, no
 // completion); the later TMA load of the same box then hits L2.
 __device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t x, int32_t y) {

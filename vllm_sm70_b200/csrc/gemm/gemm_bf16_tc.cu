@@ -143,15 +143,19 @@ struct Smem {
   static constexpr int kRawBytes = BM * raw_row_bytes(WF);  // weight = P side (swap)
   static constexpr int kStageBytes = kPBytes + kQBytes + kRawBytes;
   static constexpr int kTileBytes = STAGES * kStageBytes;
+  // Output staging for the tensor-map store: 4 epilogue warps x 2 buffers x
+  // (32 rows x 32 bf16) = 16 KB.
+  static constexpr int kEpiBytes = 4 * 2 * 32 * 64;
   static constexpr int kBarBytes = 512;
-  static constexpr int kTotal = kTileBytes + kBarBytes + 1024;  // +1024 for manual alignment
+  static constexpr int kTotal = kTileBytes + kEpiBytes + kBarBytes + 1024;  // +1024: alignment
 };
 
 template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1, bool CL = false,
           bool PAIR = false>
 __global__ void __launch_bounds__(WF == kWBf16 ? kThreads : kThreadsQ, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
-                    const __grid_constant__ CUtensorMap tmap_q, __nv_bfloat16* __restrict__ C,
+                    const __grid_constant__ CUtensorMap tmap_q,
+                    const __grid_constant__ CUtensorMap tmap_c, __nv_bfloat16* __restrict__ C,
                     int ldc, int p_rows, int q_rows, int K, int splits, float* __restrict__ ws,
                     int* __restrict__ counters, unsigned int* err, const WQParams wq,
                     const GroupInfo grp, const int pm, const int pbox, const int qbox) {
@@ -185,13 +189,15 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::kTileBytes);
+  uint8_t* const epi_stage = smem + S::kTileBytes;  // [4 warps][2][32 rows x 64 B]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::kTileBytes + S::kEpiBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* dq_bar = empty_bar + STAGES;     // [STAGES] dequantised operand ready
   uint64_t* tfull_bar = dq_bar + STAGES;     // [2]
   uint64_t* tempty_bar = tfull_bar + 2;      // [2]
   uint64_t* done_bar = tempty_bar + 2;       // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* recv_bar = done_bar + 1;         // [1] split-K partials landed (bulk path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -218,6 +224,22 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   // from the workspace) instead of the last-arriving split reducing the whole
   // tile. Same summation order (split 0, 1, ...) as the serial path.
   const bool dist = splits > 1 && grp.E == 0 && num_units <= ustride;
+  // Bulk variant of the distributed reduction (plain epilogue): the partial
+  // chunks move between shared memory (the idle operand ring) and the
+  // workspace as 16 KB bulk copies instead of per-thread 16-byte accesses, so
+  // the exchange runs at copy-engine depth rather than at the few loads each
+  // epilogue thread can keep in flight. Needs the staged chunks to fit the ring.
+  constexpr int kCW = BN % 32 == 0 ? 32 : 16;
+  constexpr int kNCH = BN / kCW;
+  constexpr int kChunkBytes = BM * kCW * 4;
+  // Largest chunk count any split stages (the chunks it does not own) or
+  // receives (the other splits' partials of the chunks it owns); every split
+  // of a tile takes the same path.
+  const int bulk_stage = splits > 1 ? kNCH - kNCH / splits : 0;
+  const int bulk_recv = splits > 1 ? (kNCH + splits - 1) / splits * (splits - 1) : 0;
+  const bool bulk = dist && EPI == kEpiNone &&
+                    (size_t)MH * kChunkBytes * (bulk_stage > bulk_recv ? bulk_stage : bulk_recv) <=
+                        (size_t)S::kTileBytes;
   constexpr int kUsedCols = kNumAcc * kAccCols;
   constexpr uint32_t kTmemCols = (kUsedCols <= 32) ? 32 : (kUsedCols <= 64) ? 64
                                  : (kUsedCols <= 128) ? 128 : (kUsedCols <= 256) ? 256 : 512;
@@ -234,6 +256,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       mbar_init(&tempty_bar[b], PAIR ? 8 : 4);  // pair: both CTAs' epilogue warps
     }
     mbar_init(done_bar, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -241,6 +264,13 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     tma_prefetch_desc(&tmap_p);
     tma_prefetch_desc(&tmap_q);
   }
+  // Plain normal-mode bf16 tiles store through the tensor map: each epilogue
+  // warp stages its 32 rows x CW columns in shared memory (64-byte or 32-byte
+  // swizzle, matching the map) and one lane issues the tile store, so the
+  // global writes go out as whole row segments instead of 16-byte pieces of
+  // 32 different rows. Tiles narrower than 128 rows keep the direct stores
+  // (their rows past the tile belong to the next tile).
+  constexpr bool kTmaStoreKind = EPI == kEpiNone && !SWAP && WF == kWBf16 && !CL;
   if (warp == 1) {
     if constexpr (PAIR) {
       tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -499,6 +529,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     constexpr int CW = BN % 32 == 0 ? 32 : 16;  // columns per tcgen05.ld
     static_assert(BN % CW == 0, "tile width must be a multiple of 16");
     const float out_scale = wq.out_scale;
+    const bool tma_st = kTmaStoreKind && (PAIR || MH == 2 || p_rows_tile == BM);
+    int ebuf = 0;  // staging buffer of this warp's next tile store
     int local = 0;
     for (int u = unit0; u < num_units && !*abort_flag; u += ustride, ++local) {
       const int t = u / splits, sp = u - t * splits;
@@ -536,7 +568,93 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         return unit % splits == sp;
       };
       const int ci = PAIR ? 2 * t + (int)prank : t;  // arrival counter of this tile (half)
-      if (split && dist) {
+      // Bulk path: chunk ch is owned by split ch % splits; this split owns
+      // chunks sp, sp + splits, ...; received partials of owned chunk ch from
+      // split s2 sit in ring slot ((h * n_own + ch / splits) * (splits - 1) + s2'),
+      // s2' = s2 minus one past this split.
+      const int n_own = (kNCH - sp + splits - 1) / splits;
+      if (split && bulk) {
+        // Phase A: stage the chunks other splits own (rows swizzled by float4
+        // to spread shared-memory banks; the reader uses the same rule).
+        int slot = 0;
+#pragma unroll 1
+        for (int h = 0; h < MH; ++h) {
+          const uint32_t t_row = t_acc + h * kHalfCols;
+#pragma unroll 1
+          for (int ch = 0; ch < kNCH; ++ch) {
+            if (ch % splits == sp) continue;
+            uint32_t r[32];
+            if constexpr (kCW == 32) {
+              tmem_ld_32x32b_x32(t_row + ch * kCW, r);
+            } else {
+              tmem_ld_32x32b_x16(t_row + ch * kCW, *reinterpret_cast<uint32_t(*)[16]>(r));
+            }
+            tmem_wait_ld();
+            float4* dst = reinterpret_cast<float4*>(smem + (size_t)slot * kChunkBytes) +
+                          row_in_tile * (kCW / 4);
+#pragma unroll
+            for (int v = 0; v < kCW / 4; ++v)
+              dst[v ^ (row_in_tile & (kCW / 4 - 1))] =
+                  make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                              __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            ++slot;
+          }
+        }
+        fence_proxy_async_shared();
+        named_barrier_sync(1, 128);
+        if (etid == 0) {
+          B200_TL(10);
+          // Phase B: one thread copies the staged chunks out, publishes this
+          // split's arrival and waits for the others'.
+          slot = 0;
+          for (int h = 0; h < MH; ++h)
+            for (int ch = 0; ch < kNCH; ++ch) {
+              if (ch % splits == sp) continue;
+              bulk_store(ws_tile + (size_t)sp * (UT * BN) + (size_t)(hbase + h) * (BM * BN) +
+                             (size_t)ch * (BM * kCW),
+                         smem + (size_t)slot * kChunkBytes, kChunkBytes);
+              ++slot;
+            }
+          bulk_commit();
+          bulk_wait_all();
+          B200_TL(11);
+          fence_proxy_async_global();
+          __threadfence();
+          atomicAdd(&counters[ci], 1);
+          const bool ok = wait_geq_gpu(&counters[ci], splits, err);
+          B200_TL(12);
+          if (ok) {
+            // Phase C: fetch the other splits' partials of the owned chunks.
+            fence_proxy_async_global();
+            mbar_arrive_expect_tx(recv_bar,
+                                  (uint32_t)(MH * n_own * (splits - 1) * kChunkBytes));
+            slot = 0;
+            for (int h = 0; h < MH; ++h)
+              for (int ch = sp; ch < kNCH; ch += splits)
+                for (int s2 = 0; s2 < splits; ++s2) {
+                  if (s2 == sp) continue;
+                  bulk_load(smem + (size_t)slot * kChunkBytes,
+                            ws_tile + (size_t)s2 * (UT * BN) + (size_t)(hbase + h) * (BM * BN) +
+                                (size_t)ch * (BM * kCW),
+                            kChunkBytes, recv_bar);
+                  ++slot;
+                }
+          }
+          *last_flag = ok ? 1 : 0;
+        }
+        named_barrier_sync(1, 128);
+        const int arrived = *last_flag;
+        named_barrier_sync(1, 128);  // last_flag is rewritten below
+        const bool landed = arrived && mbar_wait(recv_bar, 0, err);
+        if (etid == 0) B200_TL(13);
+        if (!landed) {
+          *abort_flag = 1;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_acc();
+          break;
+        }
+      } else if (split && dist) {
         // Publish the chunks the other splits own (same workspace layout as
         // the serial path), then wait until every split of the tile has.
 #pragma unroll 1
@@ -635,7 +753,39 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       // Fetch 32 (or 16) tile columns of this thread's row: from TMEM, or the
       // fixed-order (split 0, 1, ...) sum of the partials.
       auto fetch = [&](int col0, float (&v)[32]) {
-        if (dist) {
+        if (bulk) {
+          uint32_t r[32];
+          if constexpr (CW == 32) {
+            tmem_ld_32x32b_x32(t_row + col0, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + col0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] = 0.f;
+          const int base = (h * n_own + (col0 / CW) / splits) * (splits - 1);
+          for (int s2 = 0; s2 < splits; ++s2) {
+            if (s2 == sp) {
+#pragma unroll
+              for (int c = 0; c < CW; ++c) v[c] += __uint_as_float(r[c]);
+            } else {
+              const float4* src =
+                  reinterpret_cast<const float4*>(
+                      smem + (size_t)(base + (s2 < sp ? s2 : s2 - 1)) * kChunkBytes) +
+                  row_in_tile * (CW / 4);
+#pragma unroll
+              for (int c4 = 0; c4 < CW / 4; ++c4) {
+                const float4 x = src[c4 ^ (row_in_tile & (CW / 4 - 1))];
+                v[4 * c4] += x.x;
+                v[4 * c4 + 1] += x.y;
+                v[4 * c4 + 2] += x.z;
+                v[4 * c4 + 3] += x.w;
+              }
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < CW; ++c) v[c] *= out_scale;
+        } else if (dist) {
           uint32_t r[32];
           if constexpr (CW == 32) {
             tmem_ld_32x32b_x32(t_row + col0, r);
@@ -753,6 +903,33 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           float r[32];
           fetch(ch * CW, r);
           const int j0 = uc.out_j0 + ch * CW;
+          if constexpr (kTmaStoreKind) {
+            if (tma_st) {
+              uint8_t* buf = epi_stage + (size_t)(q * 2 + ebuf) * 2048;
+              if (lane == 0) bulk_wait_read_le1();  // this buffer's previous store has read it
+              __syncwarp();
+#pragma unroll
+              for (int v = 0; v < CW / 8; ++v) {
+                uint4 pk;
+                pk.x = pack_bf16x2(r[8 * v + 0], r[8 * v + 1]);
+                pk.y = pack_bf16x2(r[8 * v + 2], r[8 * v + 3]);
+                pk.z = pack_bf16x2(r[8 * v + 4], r[8 * v + 5]);
+                pk.w = pack_bf16x2(r[8 * v + 6], r[8 * v + 7]);
+                // 16-byte unit v of row `lane`: 64-byte rows use the 64B
+                // swizzle (unit ^= (row >> 1) & 3), 32-byte rows the 32B one.
+                const int u = CW == 32 ? (v ^ ((lane >> 1) & 3)) : (v ^ ((lane >> 2) & 1));
+                *reinterpret_cast<uint4*>(buf + lane * (CW * 2) + u * 16) = pk;
+              }
+              fence_proxy_async_shared();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmap_c, buf, j0, i - lane);
+                bulk_commit();
+              }
+              ebuf ^= 1;
+              continue;
+            }
+          }
           if constexpr (!SWAP) {
             if (row_ok && i < uc.p_lim) {
               __nv_bfloat16* dst = C + (size_t)i * ldc + j0;
@@ -797,6 +974,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         }
       }
     }
+    // The staged tiles must be read out before shared memory goes away.
+    if (tma_st && lane == 0) bulk_wait_all();
   }
 
   if constexpr (CL) {
@@ -988,6 +1167,14 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   }
   CUtensorMap tq = make_tmap_2d(Q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, K,
                                 (uint64_t)ldq * 2, qbox, BK);
+  // Output map for the epilogue's tile stores (plain normal-mode bf16 only;
+  // other instantiations never read it and get the operand map instead).
+  constexpr int kCW = BN % 32 == 0 ? 32 : 16;
+  const CUtensorMap tc =
+      (EPI == kEpiNone && !SWAP && WF == kWBf16)
+          ? make_tmap_2d(C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, q_rows, (uint64_t)ldc * 2,
+                         32, kCW, kCW == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
+          : tq;
   int dev = 0;
   cudaGetDevice(&dev);
   const int p_stride = MH == 1 ? pm : BM * MH;
@@ -998,7 +1185,7 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   WQParams q = wq;
   if (WF == kWBf16) q.out_scale = 1.f;
   launch_pdl(kernel, dim3(grid), dim3(WF == kWBf16 ? kThreads : kThreadsQ), S::kTotal, stream,
-             nullptr, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits,
+             nullptr, tp, tq, tc, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits,
              ws, counters, err, q, grp, pm, pbox, qbox);
 }
 
@@ -1032,8 +1219,8 @@ void launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int l
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                     M, N, K, splits, (float*)nullptr, (int*)nullptr, err,
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, tq, reinterpret_cast<__nv_bfloat16*>(C),
+                                     ldc, M, N, K, splits, (float*)nullptr, (int*)nullptr, err,
                                      WQParams{}, GroupInfo{}, (int)BM, (int)BM, BN);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc cluster launch: ") + cudaGetErrorString(e));
@@ -1055,6 +1242,12 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
                                 BM, BK);
   CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
                                 BN / 2, BK);
+  constexpr int kCW = BN % 32 == 0 ? 32 : 16;
+  const CUtensorMap tc =
+      EPI == kEpiNone
+          ? make_tmap_2d(C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, (uint64_t)ldc * 2, 32, kCW,
+                         kCW == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
+          : tq;
   int dev = 0;
   cudaGetDevice(&dev);
   const long units = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * splits;
@@ -1086,8 +1279,8 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
   const long pairs = units < max_pairs[dev] ? units : max_pairs[dev];
   lc.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-                                     M, N, K, splits, ws, counters, err, WQParams{}, GroupInfo{},
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, tc, reinterpret_cast<__nv_bfloat16*>(C),
+                                     ldc, M, N, K, splits, ws, counters, err, WQParams{}, GroupInfo{},
                                      (int)BM, (int)BM, BN / 2);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc pair launch: ") + cudaGetErrorString(e));
