@@ -56,5 +56,20 @@ def test_cpu_forward_uses_reference_weight():
         lin = quant.make_linear(fmt, w)
         x = torch.randn(5, 256).to(torch.bfloat16)
         out = lin.forward(x)
-        ref = x.float() @ lin.reference_weight().t()
+        ref = lin.reference_forward(x)
         assert (out.float() - ref).abs().max() < 2e-2 * ref.abs().max() + 1e-3
+
+
+def test_fp8_act_quant_oracle():
+    """Per-token, 128-group e4m3 activation quantisation: scale = amax / 448,
+    the round trip stays within e4m3's half-ulp, zero groups stay zero, and
+    W8A16 (switch off) multiplies the unquantised activations."""
+    torch.manual_seed(4)
+    x = torch.randn(6, 300) * 5
+    x[1, :128] = 0
+    q, s = quant.quant_fp8_act_ref(x)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (6, 3)
+    assert torch.allclose(s[0, 0], x[0, :128].abs().max() / 448)
+    assert float(s[1, 0]) == 1.0 and q[1, :128].float().abs().max() == 0
+    back = quant.fp8_act_dequant_ref(x)
+    assert ((back - x).abs() <= x.abs() * 2 ** -4 + 1e-6).all()

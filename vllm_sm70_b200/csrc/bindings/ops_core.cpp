@@ -256,6 +256,67 @@ void gemm_grouped_out(at::Tensor& out, const at::Tensor& x, const at::Tensor& w_
                       device_status_ptr(x.get_device()), cur_stream());
 }
 
+// Block-scaled FP8 (W8A8): activation quantisation and the kind::f8f6f4 GEMMs.
+void quant_fp8_act(const at::Tensor& x, at::Tensor& xq, at::Tensor& sa) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_ROWMAJOR(x);
+  TORCH_CHECK(xq.is_cuda() && xq.element_size() == 1 && xq.dim() == 2 && xq.stride(1) == 1 &&
+                  xq.size(0) == x.size(0) && xq.size(1) == x.size(1), "quant_fp8_act: xq");
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.stride(1) == 1 &&
+                  sa.size(0) == (x.size(1) + 127) / 128 && sa.size(1) >= x.size(0),
+              "quant_fp8_act: sa must be fp32 [ceil(K/128), >= M]");
+  c10::cuda::CUDAGuard g(x.device());
+  quant_fp8_act_launch(x.data_ptr(), (int)x.stride(0), (int)x.size(0), (int)x.size(1),
+                       xq.data_ptr(), (int)xq.stride(0), sa.data_ptr<float>(), (int)sa.stride(0),
+                       cur_stream());
+}
+
+void gemm_fp8_out(at::Tensor& out, const at::Tensor& xq, const at::Tensor& sa,
+                  const at::Tensor& wq, const at::Tensor& sw, int64_t bn) {
+  CHECK_BF16(out); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(xq.is_cuda() && xq.element_size() == 1 && xq.dim() == 2 && xq.stride(1) == 1,
+              "gemm_fp8: xq must be 2-D e4m3 bytes");
+  TORCH_CHECK(wq.is_cuda() && wq.element_size() == 1 && wq.dim() == 2 && wq.stride(1) == 1 &&
+                  wq.size(1) == xq.size(1), "gemm_fp8: wq must be 2-D e4m3 bytes [N, K]");
+  const int M = (int)xq.size(0), K = (int)xq.size(1), N = (int)wq.size(0);
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.stride(1) == 1 &&
+                  sa.size(0) == (K + 127) / 128 && sa.size(1) >= M, "gemm_fp8: sa shape");
+  TORCH_CHECK(sw.scalar_type() == at::kFloat && sw.dim() == 2 && sw.stride(1) == 1 &&
+                  sw.size(0) == (N + 127) / 128 && sw.size(1) >= (K + 127) / 128,
+              "gemm_fp8: sw must be fp32 [ceil(N/128), ceil(K/128)]");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_fp8: out shape");
+  c10::cuda::CUDAGuard g(xq.device());
+  gemm_fp8_launch(xq.data_ptr(), sa.data_ptr<float>(), (int)sa.stride(0), wq.data_ptr(),
+                  sw.data_ptr<float>(), (int)sw.stride(0), out.data_ptr(), M, N, K,
+                  (int)xq.stride(0), (int)wq.stride(0), (int)out.stride(0), (int)bn,
+                  device_status_ptr(xq.get_device()), cur_stream());
+}
+
+void gemm_fp8_grouped_out(at::Tensor& out, const at::Tensor& xq, const at::Tensor& sa,
+                          const at::Tensor& w_stk, const at::Tensor& sw, int64_t E, int64_t N,
+                          const at::Tensor& row_off, at::Tensor& tile_off, int64_t bn) {
+  CHECK_BF16(out); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(xq.is_cuda() && xq.element_size() == 1 && xq.dim() == 2 && xq.stride(1) == 1,
+              "gemm_fp8_grouped: xq");
+  TORCH_CHECK(w_stk.element_size() == 1 && w_stk.dim() == 2 && w_stk.stride(1) == 1 &&
+                  w_stk.size(0) == E * N && w_stk.size(1) == xq.size(1), "gemm_fp8_grouped: W");
+  TORCH_CHECK(row_off.scalar_type() == at::kInt && tile_off.scalar_type() == at::kInt &&
+                  row_off.numel() >= E + 1 && tile_off.numel() >= E + 1,
+              "gemm_fp8_grouped: offsets");
+  const int rows = (int)xq.size(0), K = (int)xq.size(1);
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.stride(1) == 1 &&
+                  sa.size(0) == (K + 127) / 128 && sa.size(1) >= rows, "gemm_fp8_grouped: sa");
+  TORCH_CHECK(sw.scalar_type() == at::kFloat && sw.dim() == 2 && sw.stride(1) == 1 &&
+                  sw.size(0) == E * N / 128 && sw.size(1) >= (K + 127) / 128,
+              "gemm_fp8_grouped: sw must be fp32 [E * N / 128, ceil(K/128)]");
+  TORCH_CHECK(out.size(0) >= rows && out.size(1) == N, "gemm_fp8_grouped: out shape");
+  c10::cuda::CUDAGuard g(xq.device());
+  gemm_fp8_grouped_launch(xq.data_ptr(), sa.data_ptr<float>(), (int)sa.stride(0), w_stk.data_ptr(),
+                          sw.data_ptr<float>(), (int)sw.stride(0), out.data_ptr(), rows, (int)E,
+                          (int)N, K, (int)xq.stride(0), (int)w_stk.stride(0), (int)out.stride(0),
+                          row_off.data_ptr<int>(), tile_off.data_ptr<int>(), (int)bn,
+                          device_status_ptr(xq.get_device()), cur_stream());
+}
+
 void gumbel_argmax(at::Tensor& ids, at::Tensor& vals, const at::Tensor& logits,
                    const at::Tensor& temperature, const at::Tensor& seeds, int64_t offset,
                    int64_t id_offset, const c10::optional<at::Tensor>& row_offsets) {
@@ -645,6 +706,10 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("moe_combine(Tensor(a!) out, Tensor y, Tensor pos, Tensor w, Tensor? shared, float shared_scale) -> ()");
   m.def("gemm_grouped_out(Tensor(a!) out, Tensor x, Tensor w_stk, int E, int N, Tensor row_off, "
         "Tensor(b!) tile_off, int fmt, Tensor? scales, float out_scale, int bn=0) -> ()");
+  m.def("quant_fp8_act(Tensor x, Tensor(a!) xq, Tensor(b!) sa) -> ()");
+  m.def("gemm_fp8_out(Tensor(a!) out, Tensor xq, Tensor sa, Tensor wq, Tensor sw, int bn=0) -> ()");
+  m.def("gemm_fp8_grouped_out(Tensor(a!) out, Tensor xq, Tensor sa, Tensor w_stk, Tensor sw, "
+        "int E, int N, Tensor row_off, Tensor(b!) tile_off, int bn=0) -> ()");
   m.def("gumbel_argmax(Tensor(a!) ids, Tensor(b!) vals, Tensor logits, Tensor temperature, "
         "Tensor seeds, int offset, int id_offset, Tensor? row_offsets=None) -> ()");
   m.def("topk_candidates(Tensor(a!) vals, Tensor(b!) ids, Tensor logits, int K, int id_offset) -> ()");
@@ -696,6 +761,9 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("moe_combine", &b200::moe_combine);
   m.impl("gemm_grouped_out", &b200::gemm_grouped_out);
   m.impl("gemm_wq_out", &b200::gemm_wq_out);
+  m.impl("quant_fp8_act", &b200::quant_fp8_act);
+  m.impl("gemm_fp8_out", &b200::gemm_fp8_out);
+  m.impl("gemm_fp8_grouped_out", &b200::gemm_fp8_grouped_out);
   m.impl("dequant_weight", &b200::dequant_weight);
   m.impl("fused_add_rms_norm", &b200::fused_add_rms_norm);
   m.impl("rope_kv_write", &b200::rope_kv_write);

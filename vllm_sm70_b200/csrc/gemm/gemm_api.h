@@ -99,6 +99,25 @@ void gemm_wq_launch(const void* A, const void* Wraw, void* C, int M, int N, int 
                     int ld_raw, int ldc, int wf, const WQParams& wq, int bn, int splits,
                     unsigned int* err, cudaStream_t stream);
 
+// ---- Block-scaled FP8 (W8A8) on kind::f8f6f4 (gemm_fp8_tc.cu) ----
+// Per-token, 128-wide-group activation quantisation: xq e4m3 [M, K] (row
+// stride ldq bytes), sa fp32 [ceil(K/128)][ld_sa] (ld_sa >= M).
+void quant_fp8_act_launch(const void* x, int ldx, int M, int K, void* xq, int ldq, float* sa,
+                          int ld_sa, cudaStream_t stream);
+// C[M, N] (bf16) = dequant(Aq, sa) . dequant(Wq, sw)^T with exact fp32 scale
+// promotion per 128-wide K block; sw fp32 [ceil(N/128)][ld_sw]. bn <= 0:
+// automatic (128 x 128 tiles for M > 64, swap-AB tiles of 32 / 64 tokens below).
+void gemm_fp8_launch(const void* Aq, const float* sa, int ld_sa, const void* Wq, const float* sw,
+                     int ld_sw, void* C, int M, int N, int K, int lda, int ldw, int ldc, int bn,
+                     unsigned int* err, cudaStream_t stream);
+// Grouped (MoE) form over expert-sorted rows: C[r, :] = X[r] . W_e^T for r in
+// [row_off[e], row_off[e+1]); W stacked [E * N, K] e4m3 with sw [E * N / 128][ld_sw];
+// X e4m3 [rows, K] with sa [ceil(K/128)][ld_sa]. tile_off: int32 scratch [E + 1].
+void gemm_fp8_grouped_launch(const void* Xq, const float* sa, int ld_sa, const void* Wstk,
+                             const float* sw, int ld_sw, void* C, int rows, int E, int N, int K,
+                             int ldx, int ldw, int ldc, const int* row_off, int* tile_off, int bn,
+                             unsigned int* err, cudaStream_t stream);
+
 struct GemmPlan {
   int cfg;
   int splits;  // split-K factor (1 = none); partials reduced in-kernel, fixed order

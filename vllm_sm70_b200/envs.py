@@ -66,6 +66,10 @@ _reg("VLLM_B200_RMSNORM", "kill", True, "kernels",
 _reg("VLLM_B200_ATTN", "kill", True, "kernels", "Paged attention kernels (0 = SDPA reference).")
 _reg("VLLM_B200_ROPE_KV", "kill", True, "kernels", "Fused RoPE + KV-cache write kernel.")
 _reg("VLLM_B200_FP8_GEMM", "kill", True, "kernels", "Block-FP8 tcgen05 GEMM.")
+_reg("VLLM_B200_FP8_W8A8", "kill", True, "kernels",
+     "Block-FP8 weights run W8A8: activations quantised per token and 128-wide K group to e4m3, "
+     "kind::f8f6f4 tensor-core MMAs with exact fp32 scale promotion per K block. 0 = W8A16 "
+     "(weights dequantised to bf16 in the GEMM producer).")
 _reg("VLLM_B200_AWQ_GEMM", "kill", True, "kernels", "AWQ int4 GEMM.")
 _reg("VLLM_B200_NVFP4_GEMM", "kill", True, "kernels", "NVFP4 GEMM.")
 _reg("VLLM_B200_MOE", "kill", True, "kernels", "Grouped expert GEMM + router kernels.")

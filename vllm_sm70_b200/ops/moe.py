@@ -133,6 +133,20 @@ class MoEWorkspace:
         self.h = torch.empty(P, 2 * I, dtype=torch.bfloat16, device=device)
         self.act = torch.empty(P, I, dtype=torch.bfloat16, device=device)
         self.y = torch.empty(P, H, dtype=torch.bfloat16, device=device)
+        self.P, self.H, self.I = P, H, I
+        self._fp8 = None
+
+    def fp8_buffers(self):
+        """e4m3 activation rows and their K-group-major scales for the W8A8
+        expert GEMMs (allocated on first use, kept for later forwards)."""
+        if self._fp8 is None:
+            dev = self.x_perm.device
+            ld = max(4, (self.P + 3) // 4 * 4)
+            self._fp8 = (torch.empty(self.P, self.H, dtype=torch.uint8, device=dev),
+                         torch.empty((self.H + 127) // 128, ld, dtype=torch.float32, device=dev),
+                         torch.empty(self.P, self.I, dtype=torch.uint8, device=dev),
+                         torch.empty((self.I + 127) // 128, ld, dtype=torch.float32, device=dev))
+        return self._fp8
 
 
 def experts_forward_ref(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: ExpertWeights,
@@ -141,7 +155,17 @@ def experts_forward_ref(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew:
     w13, w2 = ew.dense_ref()
     T, k = ids.shape
     out = torch.zeros(T, ew.H, dtype=torch.float32, device=x.device)
-    xf = x.float()
+    w8a8 = ew.fmt == "fp8" and _q.w8a8_enabled()
+    if w8a8:
+        # W8A8: exact dequantised weights, and both GEMM inputs go through the
+        # per-token, 128-group e4m3 activation quantisation.
+        w13 = _wrap("fp8", ew.w13, ew.s13, 1.0, ew.E * 2 * ew.I, ew.H).exact_weight()
+        w13 = w13.view(ew.E, 2 * ew.I, ew.H)
+        w2 = _wrap("fp8", ew.w2, ew.s2, 1.0, ew.E * ew.H, ew.I).exact_weight()
+        w2 = w2.view(ew.E, ew.H, ew.I)
+        xf = _q.fp8_act_dequant_ref(x)
+    else:
+        xf = x.float()
     for t in range(T):
         for j in range(k):
             e = int(ids[t, j]) - e_base
@@ -149,7 +173,8 @@ def experts_forward_ref(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew:
                 continue
             h = w13[e] @ xf[t]
             g, u = h[: ew.I], h[ew.I:]
-            a = (g * torch.sigmoid(g) * u).to(torch.bfloat16).float()
+            a = (g * torch.sigmoid(g) * u).to(torch.bfloat16)
+            a = _q.fp8_act_dequant_ref(a[None])[0] if w8a8 else a.float()
             out[t] += float(w[t, j]) * (w2[e] @ a)
     return out
 
@@ -176,11 +201,23 @@ def experts_forward(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: Exp
     pos = ws.pos[:T]
     ops.moe_permute(ids, ew.E, e_base, x, xp, ws.counts, ws.offsets, ws.rank, pos, ws.src)
     fmt = FMT[ew.fmt]
-    ops.gemm_grouped_out(h, xp, ew.w13, ew.E, 2 * ew.I, ws.offsets, ws.tile_off, fmt, ew.s13,
-                         ew.g13, 0)
-    ops.silu_mul(act, h)
-    ops.gemm_grouped_out(y, act, ew.w2, ew.E, ew.H, ws.offsets, ws.tile_off, fmt, ew.s2,
-                         ew.g2, 0)
+    if ew.fmt == "fp8" and _q.w8a8_enabled():
+        # W8A8 grouped GEMMs on kind::f8f6f4 with per-K-block scale promotion.
+        xq, sa1, aq, sa2 = ws.fp8_buffers()
+        ops.quant_fp8_act(xp, xq[:P], sa1)
+        ops.gemm_fp8_grouped_out(h, xq[:P], sa1, ew.w13, ew.s13, ew.E, 2 * ew.I, ws.offsets,
+                                 ws.tile_off, 0)
+        ops.silu_mul(act, h)
+        ops.quant_fp8_act(act, aq[:P], sa2)
+        ops.gemm_fp8_grouped_out(y, aq[:P], sa2, ew.w2, ew.s2, ew.E, ew.H, ws.offsets,
+                                 ws.tile_off, 0)
+        launch_count.add(2)
+    else:
+        ops.gemm_grouped_out(h, xp, ew.w13, ew.E, 2 * ew.I, ws.offsets, ws.tile_off, fmt,
+                             ew.s13, ew.g13, 0)
+        ops.silu_mul(act, h)
+        ops.gemm_grouped_out(y, act, ew.w2, ew.E, ew.H, ws.offsets, ws.tile_off, fmt, ew.s2,
+                             ew.g2, 0)
     ops.moe_combine(out, y, pos, w, shared, 1.0)
     launch_count.add(8)  # count, offsets, scatter, 2x(tiles + GEMM), silu, combine
     return out

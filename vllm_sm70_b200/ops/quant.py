@@ -1,6 +1,12 @@
-"""Weight-only quantised linear layers: block-FP8 (W8A16), AWQ int4 (W4A16),
-NVFP4 (W4A16), on the tcgen05 GEMM with dequantisation fused into the
-producer (decode shapes, M <= 256) or dequantise-then-bf16-GEMM (prefill).
+"""Quantised linear layers: block-FP8 (W8A8 on kind::f8f6f4 tensor cores, or
+W8A16), AWQ int4 (W4A16), NVFP4 (W4A16), on the tcgen05 GEMMs.
+
+Block-FP8 runs W8A8 by default (``VLLM_B200_FP8_W8A8``): activations are
+quantised per token and 128-wide K group to e4m3 (fp32 scale = group amax /
+448), the GEMM multiplies e4m3 x e4m3 on the tensor cores and promotes each
+128-wide K block's partial sum into fp32 with both scales. The weight-only
+formats dequantise in the GEMM producer (decode shapes, M <= 256) or
+dequantise then run the bf16 GEMM (prefill).
 
 Checkpoint formats (HF safetensors) and the in-memory layouts:
 
@@ -101,6 +107,62 @@ def quantize_nvfp4(w: torch.Tensor, block: int = 16):
     return packed, bscale.contiguous(), float(gscale)
 
 
+def w8a8_enabled() -> bool:
+    return bool(envs.get("VLLM_B200_FP8_W8A8"))
+
+
+def quant_fp8_act_ref(x: torch.Tensor):
+    """CPU/GPU torch oracle of the activation quantiser: per row and 128-wide K
+    group, scale = amax / 448 (1 for an all-zero group), q = e4m3(x * 448 / amax)
+    rounded to nearest even after clamping to +-448. Returns (q [M, K] e4m3,
+    scale [M, ceil(K/128)] fp32) -- the same values the CUDA kernel writes."""
+    xf = x.float()
+    M, K = xf.shape
+    G = (K + 127) // 128
+    xp = torch.zeros(M, G * 128, dtype=torch.float32, device=xf.device)
+    xp[:, :K] = xf
+    g = xp.view(M, G, 128)
+    amax = g.abs().amax(-1)
+    pos = amax > 0
+    one = torch.ones_like(amax)
+    # Tensor / tensor: an IEEE division (a python-scalar divisor may be turned
+    # into a multiplication by its reciprocal, which rounds differently).
+    fmax = torch.full_like(amax, FP8_MAX)
+    scale = torch.where(pos, amax / fmax, one)
+    inv = torch.where(pos, fmax / torch.where(pos, amax, one), one)
+    q = (g * inv[..., None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q.view(M, G * 128)[:, :K].contiguous(), scale
+
+
+def fp8_act_dequant_ref(x: torch.Tensor) -> torch.Tensor:
+    """fp32 value of x after the W8A8 activation quantisation round trip."""
+    q, s = quant_fp8_act_ref(x)
+    return q.float() * s.repeat_interleave(128, 1)[:, : q.shape[1]]
+
+
+def quant_fp8_act(x: torch.Tensor):
+    """(xq uint8 [M, K] e4m3 bytes, sa fp32 [ceil(K/128), M']) on the CUDA kernel."""
+    M, K = x.shape
+    xq = torch.empty(M, K, dtype=torch.uint8, device=x.device)
+    sa = torch.empty((K + 127) // 128, max(4, (M + 3) // 4 * 4), dtype=torch.float32,
+                     device=x.device)
+    torch.ops._b200_C.quant_fp8_act(x, xq, sa)
+    launch_count.add(1)
+    return xq, sa
+
+
+def gemm_fp8(x: torch.Tensor, w_raw: torch.Tensor, sw: torch.Tensor,
+             out: torch.Tensor | None = None, bn: int = 0) -> torch.Tensor:
+    """W8A8 block-FP8 GEMM: ``x [M, K] bf16`` quantised on the fly, times the
+    e4m3 weight ``w_raw [N, K]`` with block scales ``sw [ceil(N/128), ceil(K/128)]``."""
+    if out is None:
+        out = torch.empty(x.shape[0], w_raw.shape[0], dtype=torch.bfloat16, device=x.device)
+    xq, sa = quant_fp8_act(x)
+    torch.ops._b200_C.gemm_fp8_out(out, xq, sa, w_raw, sw, bn)
+    launch_count.add(1)
+    return out
+
+
 # ------------------------------------------------------------------ linears
 class _WQLinear(Linear):
     fmt: str
@@ -142,6 +204,10 @@ class _WQLinear(Linear):
         """The dense weight this layer represents (fp32), for oracles."""
         return self.dequant_ref().float() * self.out_scale
 
+    def reference_forward(self, x: torch.Tensor) -> torch.Tensor:
+        """fp32 oracle of ``forward`` (weight-only formats: x times the dense weight)."""
+        return x.float() @ self.reference_weight().t()
+
     def weight_bytes(self):
         return self.raw.numel() + self.scales.numel() * self.scales.element_size()
 
@@ -160,6 +226,31 @@ class Fp8BlockLinear(_WQLinear):
         s = self.scales.repeat_interleave(128, 0).repeat_interleave(128, 1)
         s = s[: self.out_features, : self.in_features]
         return (q * s).to(torch.bfloat16)
+
+    def forward(self, x, out=None):
+        if w8a8_enabled():
+            if x.is_cuda and envs.get("VLLM_B200_FP8_GEMM"):
+                _ext.require()
+                return gemm_fp8(x, self.raw, self.scales, out)
+            if not x.is_cuda:
+                r = self.reference_forward(x).to(torch.bfloat16)
+                if out is None:
+                    return r
+                out.copy_(r)
+                return out
+        return super().forward(x, out)
+
+    def exact_weight(self) -> torch.Tensor:
+        """fp32 dequantised weight without the bf16 rounding of ``dequant_ref``
+        (what the W8A8 tensor-core path multiplies with)."""
+        q = self.raw.view(torch.float8_e4m3fn).float()
+        s = self.scales.repeat_interleave(128, 0).repeat_interleave(128, 1)
+        return q * s[: self.out_features, : self.in_features]
+
+    def reference_forward(self, x: torch.Tensor) -> torch.Tensor:
+        if w8a8_enabled():
+            return fp8_act_dequant_ref(x) @ self.exact_weight().t()
+        return super().reference_forward(x)
 
 
 class AwqLinear(_WQLinear):

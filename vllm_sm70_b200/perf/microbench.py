@@ -128,6 +128,31 @@ def bench_gemm(M, N, K, cfg=-1, splits=0, iters=20, flush=False, cublas=True, ep
     return res
 
 
+def bench_gemm_fp8(M, N, K, bn=0, iters=20, flush=False):
+    """W8A8 block-FP8 GEMM (kind::f8f6f4 + scale promotion) on pre-quantised
+    activations, plus the activation quantiser, vs the bf16 tcgen05 GEMM of
+    the same shape."""
+    from ..ops import linear, quant
+
+    w = torch.randn(N, K, device="cuda") * 0.05
+    lin = quant.make_linear("fp8", w)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    xq, sa = quant.quant_fp8_act(x)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ms = time_fn(lambda: torch.ops._b200_C.gemm_fp8_out(out, xq, sa, lin.raw, lin.scales, bn),
+                 iters, flush=flush)
+    ms_q = time_fn(lambda: torch.ops._b200_C.quant_fp8_act(x, xq, sa), iters, flush=flush)
+    wb = w.to(torch.bfloat16)
+    ms_bf16 = time_fn(lambda: linear.gemm(x, wb, out=out), iters, flush=flush)
+    pk = peaks()
+    flops = 2.0 * M * N * K
+    byts = M * K + N * K + 2.0 * M * N
+    return {"kernel": "gemm_fp8_w8a8", "M": M, "N": N, "K": K, "bn": bn, "ms": round(ms, 5),
+            "tflops": round(flops / ms / 1e9, 1), "gbs": round(byts / ms / 1e6, 1),
+            "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3),
+            "quant_ms": round(ms_q, 5), "bf16_gemm_ms": round(ms_bf16, 5), "peaks": pk["src"]}
+
+
 def bench_decode_attn(batch=256, ctx=1152, hq=32, hkv=8, d=128, bs=16, splits=1, iters=20,
                       seq_blocks=False):
     from ..ops import attention as A
@@ -177,8 +202,8 @@ def bench_prefill_attn(seqs=16, length=1024, hq=32, hkv=8, d=128, bs=16, iters=1
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "gemm-cublas", "decode-attn", "prefill-attn",
-                                     "all"])
+    ap.add_argument("case", choices=["gemm", "gemm-cublas", "gemm-fp8", "decode-attn",
+                                     "prefill-attn", "all"])
     ap.add_argument("--M", type=int, default=256)
     ap.add_argument("--N", type=int, default=6144)
     ap.add_argument("--K", type=int, default=4096)
@@ -216,6 +241,9 @@ def main(argv=None):
     elif args.case == "gemm":
         out.append(bench_gemm(args.M, args.N, args.K, args.cfg, args.splits, args.iters,
                               args.flush, not args.no_cublas, args.epi))
+    elif args.case == "gemm-fp8":
+        out.append(bench_gemm_fp8(args.M, args.N, args.K, max(0, args.cfg), args.iters,
+                                  args.flush))
     elif args.case == "gemm-cublas":
         a = torch.randn(args.M, args.K, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(args.N, args.K, device="cuda", dtype=torch.bfloat16)
