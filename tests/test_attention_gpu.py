@@ -34,9 +34,10 @@ def test_decode(b200_ops, d, hq, hkv, bs, rel_err):
 
 
 @pytest.mark.parametrize("splits", [2, 5])
-def test_decode_split_kv(b200_ops, splits, rel_err):
+@pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (256, 16, 2)])
+def test_decode_split_kv(b200_ops, splits, d, hq, hkv, rel_err):
     lens = [3, 700, 2100]
-    q, kc, vc, bt, sl, cu = _case([1] * 3, lens, 32, 8, 128, 16, seed=1)
+    q, kc, vc, bt, sl, cu = _case([1] * 3, lens, hq, hkv, d, 16, seed=1)
     out = torch.empty_like(q)
     T, H, D = q.shape
     po = torch.empty(splits, T, H, D, device="cuda")
@@ -58,9 +59,11 @@ def test_prefill_and_chunked(b200_ops, d, hq, hkv, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
-def test_spec_verify_rows(b200_ops, rel_err):
-    # 4 query tokens per request (k=3 draft + 1) through the decode variant.
-    q, kc, vc, bt, sl, cu = _case([4, 4], [50, 400], 32, 8, 128, 16, seed=3)
+@pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (256, 16, 2)])
+def test_spec_verify_rows(b200_ops, d, hq, hkv, rel_err):
+    # 4 query tokens per request (k=3 draft + 1) through the decode variant
+    # (D = 256: the Qwen3-Next gated-attention shape, 8 query heads per KV head).
+    q, kc, vc, bt, sl, cu = _case([4, 4], [50, 400], hq, hkv, d, 16, seed=3)
     out = torch.empty_like(q)
     A.paged_attention(out, q, kc, vc, bt, sl, cu, 4, 0.09, decode=True)
     ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 0.09)
@@ -76,9 +79,10 @@ def test_sinks_and_window(b200_ops, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
-def test_decode_sinks_window(b200_ops, rel_err):
-    q, kc, vc, bt, sl, cu = _case([1, 1, 1], [600, 40, 1300], 32, 8, 128, 16, seed=6)
-    sinks = torch.randn(32, device="cuda")
+@pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (256, 16, 2)])
+def test_decode_sinks_window(b200_ops, d, hq, hkv, rel_err):
+    q, kc, vc, bt, sl, cu = _case([1, 1, 1], [600, 40, 1300], hq, hkv, d, 16, seed=6)
+    sinks = torch.randn(hq, device="cuda")
     out = torch.empty_like(q)
     A.paged_attention(out, q, kc, vc, bt, sl, cu, 1, 0.1, window=256, sinks=sinks, decode=True)
     ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 0.1, window=256, sinks=sinks)

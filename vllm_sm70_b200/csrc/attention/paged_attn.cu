@@ -527,7 +527,9 @@ constexpr int decode_tma_smem() {
 // reserved per CTA); the register budget is capped to match.
 template <int D, int KT, int STAGES>
 constexpr int decode_tma_ctas() {
-  return (decode_tma_smem<D, KT, STAGES>() + 1024) * 3 <= 228 * 1024 ? 3 : 2;
+  return (decode_tma_smem<D, KT, STAGES>() + 1024) * 3 <= 228 * 1024   ? 3
+         : (decode_tma_smem<D, KT, STAGES>() + 1024) * 2 <= 228 * 1024 ? 2
+                                                                         : 1;
 }
 
 template <int D, int KT, int STAGES>
@@ -636,13 +638,17 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
 
   // -------------------------------------------------------------- consumers
   const int key_off = warp * KW;
-  uint32_t qf[D / 16][4];
-  {
-    const int r = (lane % 8) + ((lane / 8) % 2) * 8;
+  // Q fragments stay in registers up to D = 128; wider heads (D = 256, whose
+  // O accumulator alone takes 128 registers) re-read them from shared memory
+  // for every K/V tile.
+  constexpr bool kQReg = D <= 128;
+  const int q_r = (lane % 8) + ((lane / 8) % 2) * 8;
+  uint32_t qf[kQReg ? D / 16 : 1][4];
+  if constexpr (kQReg) {
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const int ch = kk * 2 + lane / 16;
-      ldmatrix_x4(smem_addr(sQ) + swz<D>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      ldmatrix_x4(smem_addr(sQ) + swz<D>(q_r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
     }
   }
   const int g = lane / 4, t4 = lane % 4;
@@ -684,14 +690,20 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     for (int n = 0; n < KW / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t qa[4];
+      if constexpr (kQReg) {
+        qa[0] = qf[kk][0]; qa[1] = qf[kk][1]; qa[2] = qf[kk][2]; qa[3] = qf[kk][3];
+      } else {
+        ldmatrix_x4(smem_addr(sQ) + swz<D>(q_r, kk * 2 + lane / 16), qa[0], qa[1], qa[2], qa[3]);
+      }
 #pragma unroll
       for (int n2 = 0; n2 < KW / 16; ++n2) {
         const int key = key_off + n2 * 16 + (lane % 8) + (lane / 16) * 8;
         const int ch = kk * 2 + (lane / 8) % 2;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(sK + tma_tile_off(key, ch, KT), b0, b1, b2, b3);
-        mma_bf16(s[2 * n2], qf[kk], b0, b1);
-        mma_bf16(s[2 * n2 + 1], qf[kk], b2, b3);
+        mma_bf16(s[2 * n2], qa, b0, b1);
+        mma_bf16(s[2 * n2 + 1], qa, b2, b3);
       }
     }
 
@@ -923,12 +935,15 @@ void paged_attention_launch(const AttnArgs& a, cudaStream_t stream) {
   if (!a.decode && fa_tc_enabled() && fa_tc_supported(a)) {
     fa_tc_launch(a, stream);
   } else if (a.decode && tma_ok && decode_tma_enabled() &&
-             (a.head_dim == 128 || a.head_dim == 64)) {
+             (a.head_dim == 128 || a.head_dim == 64 || a.head_dim == 256)) {
     // Two 64-key stages per CTA and three CTAs per SM measured faster than
     // three stages at two CTAs per SM (more consumer warps per SM keep the
-    // same bytes in flight).
+    // same bytes in flight). D = 256: one CTA per SM with three 64-key stages
+    // (192 KB of K/V in flight per SM).
     if (a.head_dim == 128)
       launch_decode_tma<128, 64, 2>(p, a, stream);
+    else if (a.head_dim == 256)
+      launch_decode_tma<256, 64, 3>(p, a, stream);
     else
       launch_decode_tma<64, 64, 4>(p, a, stream);
   } else if (a.head_dim == 128) {

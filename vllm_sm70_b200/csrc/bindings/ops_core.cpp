@@ -44,7 +44,8 @@ void launch_gemm(at::Tensor& out, const at::Tensor& a, const at::Tensor& w, int 
   gemm_bf16_launch_split(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, (int)a.stride(0),
                          (int)w.stride(0), (int)out.stride(0), epi, c, s, gemm_ws_ptr(dev),
                          gemm_workspace_bytes(dev), gemm_counters_ptr(dev),
-                         gemm_n_counters(dev), device_status_ptr(dev), cur_stream());
+                         gemm_n_counters(dev), device_status_ptr(dev), cur_stream(),
+                         /*ext_reduce=*/epi == kEpiNone);
 }
 
 void init_device(int64_t device) { (void)device_status_ptr((int)device); }

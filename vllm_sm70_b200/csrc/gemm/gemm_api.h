@@ -170,10 +170,13 @@ bool gemm_cfg_is_swap(int cfg);
 
 // Explicit-workspace variant: splits > 1 needs ws >= tiles*splits*128*BN*4
 // bytes and counters[tiles] zeroed (they are re-armed by the kernel).
+// ext_reduce: a one-round plain split may leave its fp32 partials in ws as
+// [splits][M][N] and sum them in a second kernel on the stream (needs
+// splits x M x N floats of workspace; opt-in with VLLM_B200_GEMM_EXT_REDUCE=1).
 void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,
                             int ldw, int ldc, int epi, int cfg, int splits, float* ws,
                             size_t ws_bytes, int* counters, int n_counters, unsigned int* err,
-                            cudaStream_t stream);
+                            cudaStream_t stream, bool ext_reduce = false);
 
 // Row-parallel GEMM fused with the TP all-reduce + residual add + RMSNorm in one
 // kernel: C = A W^T goes into this rank's symmetric stage (ar.stage_peer[rank]),

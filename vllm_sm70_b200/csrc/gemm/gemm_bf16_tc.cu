@@ -156,10 +156,12 @@ __global__ void __launch_bounds__(WF == kWBf16 ? kThreads : kThreadsQ, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     const __grid_constant__ CUtensorMap tmap_q,
                     const __grid_constant__ CUtensorMap tmap_c, __nv_bfloat16* __restrict__ C,
-                    int ldc, int p_rows, int q_rows, int K, int splits, float* __restrict__ ws,
+                    int ldc, int p_rows, int q_rows, int K, int splits_arg, float* __restrict__ ws,
                     int* __restrict__ counters, unsigned int* err, const WQParams wq,
                     const GroupInfo grp, const int pm, const int pbox, const int qbox) {
   unsigned long long* const tl = g_gemm_timeline;
+  // A negative split count asks for the external reduction (see `ext`).
+  const int splits = splits_arg < 0 ? -splits_arg : splits_arg;
 #define B200_TL(i) \
   do { if (tl) tl[(size_t)blockIdx.x * 16 + (i)] = globaltimer(); } while (0)
   if (threadIdx.x == 0) B200_TL(0);
@@ -223,7 +225,20 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   // the column chunks it owns (its own partial straight from TMEM, the others'
   // from the workspace) instead of the last-arriving split reducing the whole
   // tile. Same summation order (split 0, 1, ...) as the serial path.
-  const bool dist = splits > 1 && grp.E == 0 && num_units <= ustride;
+  // External split-K reduction: launched without arrival counters, the
+  // splits never meet in this kernel. Each writes its fp32 partial tile into
+  // the workspace laid out [split][M][N] (tensor map tmap_c, tile stores
+  // staged in the idle operand ring) and the reduction kernel that follows on
+  // the stream sums the partials in split order over every SM of the GPU,
+  // instead of the split CTAs exchanging them at a handful of loads in flight
+  // per thread. One round of units only (the ring must be idle).
+  constexpr bool kExtKind = EPI == kEpiNone && !SWAP && WF == kWBf16 && !CL && BN % 32 == 0 &&
+                            MH * BN * BM * 4 <= S::kTileBytes;
+  // The launcher asks for it only for one round of units and a workspace
+  // of splits x M x N floats.
+  const bool ext = kExtKind && splits_arg < -1 && ws != nullptr && grp.E == 0 &&
+                   num_units <= ustride;
+  const bool dist = splits > 1 && grp.E == 0 && num_units <= ustride && !ext;
   // Bulk variant of the distributed reduction (plain epilogue): the partial
   // chunks move between shared memory (the idle operand ring) and the
   // workspace as 16 KB bulk copies instead of per-thread 16-byte accesses, so
@@ -573,6 +588,42 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       // split s2 sit in ring slot ((h * n_own + ch / splits) * (splits - 1) + s2'),
       // s2' = s2 minus one past this split.
       const int n_own = (kNCH - sp + splits - 1) / splits;
+      if (ext) {
+        // Stage this warp's 32 rows of every 32-column chunk (fp32, 128-byte
+        // swizzle as the map expects), hand the accumulator back, then one
+        // lane per chunk issues its tile store (one warp-wide instruction).
+        constexpr int kChunks = MH * (BN / 32);
+        uint8_t* wst = smem + (size_t)q * kChunks * 4096;
+#pragma unroll 1
+        for (int h = 0; h < MH; ++h) {
+#pragma unroll 1
+          for (int ch = 0; ch < BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_acc + h * kHalfCols + ch * 32, r);
+            tmem_wait_ld();
+            float4* dst = reinterpret_cast<float4*>(wst + (size_t)(h * (BN / 32) + ch) * 4096) +
+                          lane * 8;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v ^ (lane & 7)] =
+                  make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                              __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          }
+        }
+        fence_proxy_async_shared();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release_acc();
+        if (lane < kChunks) {
+          const int h = lane / (BN / 32), ch = lane % (BN / 32);
+          tma_store_3d(&tmap_c, wst + (size_t)lane * 4096, uc.out_j0 + ch * 32,
+                       uc.out_i0 + (hbase + h) * BM + q * 32, sp);
+          bulk_commit();
+          bulk_wait_all();
+        }
+        __syncwarp();
+        continue;
+      }
       if (split && bulk) {
         // Phase A: stage the chunks other splits own (rows swizzled by float4
         // to spread shared-memory banks; the reader uses the same rule).
@@ -1138,10 +1189,11 @@ int tma_box_rows() {
 }
 
 template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1>
-void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, int K, int ldp,
+bool launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, int K, int ldp,
                 int ldq, int ldc, int splits, float* ws, int* counters, unsigned int* err,
                 cudaStream_t stream, const WQParams& wq = WQParams{},
-                const GroupInfo& grp = GroupInfo{}, int grid_units = 0, int pm = BM) {
+                const GroupInfo& grp = GroupInfo{}, int grid_units = 0, int pm = BM,
+                bool ext = false) {
   using S = Smem<BN, STAGES, WF, MH>;
   if (MH != 1 || WF != kWBf16 || grp.E > 0 || pm <= 0 || pm > BM) pm = BM;
   // TMA box rows per operand (bf16 operands only; 0 = one box per tile).
@@ -1170,11 +1222,15 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   // Output map for the epilogue's tile stores (plain normal-mode bf16 only;
   // other instantiations never read it and get the operand map instead).
   constexpr int kCW = BN % 32 == 0 ? 32 : 16;
-  const CUtensorMap tc =
+  const CUtensorMap tc_plain =
       (EPI == kEpiNone && !SWAP && WF == kWBf16)
           ? make_tmap_2d(C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, q_rows, (uint64_t)ldc * 2,
                          32, kCW, kCW == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
           : tq;
+  const CUtensorMap tc =
+      ext ? make_tmap_3d(ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)splits, p_rows, q_rows,
+                         (uint64_t)q_rows * 4, (uint64_t)p_rows * q_rows * 4, 1, 32, 32)
+          : tc_plain;
   int dev = 0;
   cudaGetDevice(&dev);
   const int p_stride = MH == 1 ? pm : BM * MH;
@@ -1182,18 +1238,23 @@ void launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
                                     : (long)((p_rows + p_stride - 1) / p_stride) *
                                           ((q_rows + BN - 1) / BN) * splits;
   const int grid = units < num_sms(dev) ? (int)units : num_sms(dev);
+  // One round (every unit resident at once) and the kernel's staging fits.
+  constexpr bool kExtFits = EPI == kEpiNone && !SWAP && WF == kWBf16 && BN % 32 == 0 &&
+                            MH * BN * BM * 4 <= S::kTileBytes;
+  const bool use_ext = kExtFits && ext && splits > 1 && units <= grid;
   WQParams q = wq;
   if (WF == kWBf16) q.out_scale = 1.f;
   launch_pdl(kernel, dim3(grid), dim3(WF == kWBf16 ? kThreads : kThreadsQ), S::kTotal, stream,
-             nullptr, tp, tq, tc, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows, q_rows, K, splits,
-             ws, counters, err, q, grp, pm, pbox, qbox);
+             nullptr, tp, tq, use_ext ? tc : tc_plain, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows,
+             q_rows, K, use_ext ? -splits : splits, ws, counters, err, q, grp, pm, pbox, qbox);
+  return use_ext;
 }
 
 // Cluster split-K: the `splits` K-slices of a tile run as one thread-block
 // cluster (one tile-split per CTA, grid = tiles * splits) and reduce through
 // distributed shared memory; no workspace or counters.
 template <int BN, int STAGES, int EPI, int MH>
-void launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
+bool launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
                int ldc, int splits, unsigned int* err, cudaStream_t stream) {
   using S = Smem<BN, STAGES, kWBf16, MH>;
   static_assert(S::kTotal <= 232448, "shared memory budget");
@@ -1224,15 +1285,16 @@ void launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int l
                                      WQParams{}, GroupInfo{}, (int)BM, (int)BM, BN);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc cluster launch: ") + cudaGetErrorString(e));
+  return false;
 }
 
 // CTA pairs: cluster of 2, grid = 2 x min(units, SMs / 2), each pair
 // persistent over (256 x BN tile, split) units; split-K through the workspace
 // with one arrival counter per tile half (needs 2 x tiles counters).
 template <int BN, int STAGES, int EPI>
-void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
+bool launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldw,
                  int ldc, int splits, float* ws, int* counters, unsigned int* err,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, bool ext = false) {
   using S = Smem<BN / 2, STAGES, kWBf16, 1>;
   static_assert(S::kTotal <= 232448, "shared memory budget");
   auto kernel = gemm_bf16_tc_kernel<BN, STAGES, false, EPI, kWBf16, 1, false, true>;
@@ -1243,11 +1305,15 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
   CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
                                 BN / 2, BK);
   constexpr int kCW = BN % 32 == 0 ? 32 : 16;
-  const CUtensorMap tc =
+  const CUtensorMap tc_plain =
       EPI == kEpiNone
           ? make_tmap_2d(C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, (uint64_t)ldc * 2, 32, kCW,
                          kCW == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B)
           : tq;
+  const CUtensorMap tc =
+      ext ? make_tmap_3d(ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)splits, M, N,
+                         (uint64_t)N * 4, (uint64_t)M * N * 4, 1, 32, 32)
+          : tc_plain;
   int dev = 0;
   cudaGetDevice(&dev);
   const long units = (long)((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * splits;
@@ -1277,13 +1343,18 @@ void launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
     max_pairs[dev] = n < num_sms(dev) / 2 ? n : num_sms(dev) / 2;
   }
   const long pairs = units < max_pairs[dev] ? units : max_pairs[dev];
+  // One round (every unit resident at once) and the kernel's staging fits.
+  constexpr bool kExtFits = EPI == kEpiNone && BN % 32 == 0 && BN * BM * 4 <= S::kTileBytes;
+  const bool use_ext = kExtFits && ext && splits > 1 && units <= pairs;
   lc.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, tc, reinterpret_cast<__nv_bfloat16*>(C),
-                                     ldc, M, N, K, splits, ws, counters, err, WQParams{}, GroupInfo{},
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, use_ext ? tc : tc_plain,
+                                     reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K,
+                                     use_ext ? -splits : splits, ws, counters, err, WQParams{}, GroupInfo{},
                                      (int)BM, (int)BM, BN / 2);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc pair launch: ") + cudaGetErrorString(e));
+  return use_ext;
 }
 
 struct CfgInfo {
@@ -1512,11 +1583,15 @@ float* gemm_ws_ptr(int device) { return g_split_ws[device].ws; }
 int* gemm_counters_ptr(int device) { return g_split_ws[device].counters; }
 int gemm_n_counters(int device) { return g_split_ws[device].n_counters; }
 
-void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,
-                            int ldw, int ldc, int epi, int cfg, int splits, float* ws,
-                            size_t ws_bytes, int* counters, int n_counters, unsigned int* err,
-                            cudaStream_t stream) {
-  if (M <= 0 || N <= 0 || K <= 0) return;
+namespace {
+
+// Returns true when the launched GEMM left its split-K partials in the
+// workspace for splitk_reduce_kernel (external reduction, `ext_req`).
+bool launch_split_impl(const void* A, const void* W, void* C, int M, int N, int K, int lda,
+                       int ldw, int ldc, int epi, int cfg, int splits, float* ws, size_t ws_bytes,
+                       int* counters, int n_counters, unsigned int* err, cudaStream_t stream,
+                       bool ext_req) {
+  if (M <= 0 || N <= 0 || K <= 0) return false;
   if (K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0)
     throw std::runtime_error("gemm_bf16: K and leading dims must be multiples of 8");
   if (N % 8 != 0 || ldc % 8 != 0) throw std::runtime_error("gemm_bf16: N, ldc must be multiples of 8");
@@ -1571,6 +1646,8 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
   const int pm = geo.tile_rows;
   float* wsp = splits > 1 ? ws : nullptr;
   int* cnt = splits > 1 ? counters : nullptr;
+  const bool ext = ext_req && splits > 1 && epi == kEpiNone && ws != nullptr &&
+                   (size_t)splits * M * N * sizeof(float) <= ws_bytes;
   if (cfg_pair(cfg) && epi == kEpiSiluMul) {
     if (N % 128 != 0) throw std::runtime_error("gemm_bf16 silu_mul: N must be a multiple of 128");
     if (cfg == kCfgP2N256)
@@ -1583,19 +1660,19 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
     switch (cfg) {
       case kCfgP2N256:
         return launch_pair<256, 6, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
-                                             stream);
+                                             stream, ext);
       case kCfgP2N192:
         return launch_pair<192, 7, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
-                                             stream);
+                                             stream, ext);
       case kCfgP2N128:
         return launch_pair<128, 8, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
-                                             stream);
+                                             stream, ext);
       case kCfgP2N96:
         return launch_pair<96, 9, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
-                                            stream);
+                                            stream, ext);
       default:
         return launch_pair<64, 10, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, err,
-                                             stream);
+                                             stream, ext);
     }
   }
   if (epi == kEpiSiluMul) {
@@ -1614,10 +1691,11 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
   }
 #define B200_NORMAL(BN_, ST_) \
   return launch_cfg<BN_, ST_, false, kEpiNone>(A, W, C, M, N, K, lda, ldw, ldc, splits, wsp, cnt, \
-                                               err, stream)
+                                               err, stream, WQParams{}, GroupInfo{}, 0, pm, ext)
 #define B200_TALL(BN_, ST_) \
   return launch_cfg<BN_, ST_, false, kEpiNone, kWBf16, 2>(A, W, C, M, N, K, lda, ldw, ldc, splits, \
-                                                          wsp, cnt, err, stream)
+                                                          wsp, cnt, err, stream, WQParams{},     \
+                                                          GroupInfo{}, 0, BM, ext)
 #define B200_SWAP(BN_, ST_) \
   return launch_cfg<BN_, ST_, true, kEpiNone>(W, A, C, N, M, K, ldw, lda, ldc, splits, wsp, cnt, \
                                               err, stream, WQParams{}, GroupInfo{}, 0, pm)
@@ -1640,7 +1718,72 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
 #undef B200_TALL
 #undef B200_NORMAL
 #undef B200_SWAP
+  return false;
 }
+
+// Opt-in (VLLM_B200_GEMM_EXT_REDUCE=1): measured on the Llama-3.1-8B decode
+// shapes it shortened the GEMM kernel's epilogue from about 8 to 3.6 us, but
+// the reduction kernel that follows took the difference back (qkv M = 256:
+// 29.6 vs 28.7 us per call; decode phase 3,227 vs 3,201 ms per bench step).
+bool ext_reduce_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLLM_B200_GEMM_EXT_REDUCE");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
+// C[m, n] = bf16(sum over s in order 0, 1, ... of ws[s][m][n]): the split
+// partials the GEMM left in the workspace; 8 columns per thread.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
+                                     __nv_bfloat16* __restrict__ C, int ldc) {
+  pdl_wait();
+  const long n8 = N / 8;
+  const long total = (long)M * n8;
+  for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long)gridDim.x * blockDim.x) {
+    const int m = (int)(idx / n8), c = (int)(idx - (long)m * n8) * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4* src = reinterpret_cast<const float4*>(ws + ((size_t)sp * M + m) * N + c);
+      const float4 a = __ldcg(src), b = __ldcg(src + 1);
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+      v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    uint4 pk;
+    pk.x = pack_bf16x2(v[0], v[1]);
+    pk.y = pack_bf16x2(v[2], v[3]);
+    pk.z = pack_bf16x2(v[4], v[5]);
+    pk.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(C + (size_t)m * ldc + c) = pk;
+  }
+}
+
+}  // namespace
+
+void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N, int K, int lda,
+                            int ldw, int ldc, int epi, int cfg, int splits, float* ws,
+                            size_t ws_bytes, int* counters, int n_counters, unsigned int* err,
+                            cudaStream_t stream, bool ext_reduce) {
+  const bool ext_req = ext_reduce && ext_reduce_enabled();
+  if (!launch_split_impl(A, W, C, M, N, K, lda, ldw, ldc, epi, cfg, splits, ws, ws_bytes,
+                         counters, n_counters, err, stream, ext_req))
+    return;
+  // The GEMM wrote split partials [splits][M][N]; splits as the launcher resolved them.
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int s = splits;
+  if (cfg < 0 || s <= 0) s = gemm_bf16_plan(M, N, K, epi, num_sms(dev)).splits;
+  if (s > kMaxSplits) s = kMaxSplits;
+  const int num_kb = (K + 63) / 64;
+  if (s > num_kb) s = num_kb;
+  const long total = (long)M * (N / 8);
+  const long blocks = (total + 255) / 256;
+  const int grid = (int)(blocks < 8L * num_sms(dev) ? blocks : 8L * num_sms(dev));
+  launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, stream, nullptr, ws, s, M, N,
+             reinterpret_cast<__nv_bfloat16*>(C), ldc);
+}
+
 
 bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, int lda, int ldw,
                             int cfg, int splits, const ArRmsNormParams& ar, unsigned int* err,
@@ -1726,8 +1869,8 @@ void gemm_wq_launch(const void* A, const void* Wraw, void* C, int M, int N, int 
   float* wsp = splits > 1 ? w.ws : nullptr;
   int* cnt = splits > 1 ? w.counters : nullptr;
 #define B200_WQ(BN_, ST_, WF_)                                                                  \
-  return launch_cfg<BN_, ST_, true, kEpiNone, WF_>(Wraw, A, C, N, M, K, ld_raw, lda, ldc, splits, \
-                                                   wsp, cnt, err, stream, wq)
+  return (void)launch_cfg<BN_, ST_, true, kEpiNone, WF_>(Wraw, A, C, N, M, K, ld_raw, lda, ldc,   \
+                                                         splits, wsp, cnt, err, stream, wq)
 #define B200_WQ_BN(WF_)                          \
   switch (bn) {                                  \
     case 16: B200_WQ(16, 6, WF_);                \
@@ -1780,8 +1923,9 @@ void gemm_grouped_launch(const void* X, const void* Wstk, void* C, int rows, int
   const int units = (int)(max_tiles < (1 << 30) ? max_tiles : (1 << 30));
   const int P = E * N;
 #define B200_G(BN_, ST_, WF_)                                                                   \
-  return launch_cfg<BN_, ST_, true, kEpiNone, WF_>(Wstk, X, C, P, rows, K, ldw, ldx, ldc, 1,       \
-                                                   nullptr, nullptr, err, stream, wq, g, units)
+  return (void)launch_cfg<BN_, ST_, true, kEpiNone, WF_>(Wstk, X, C, P, rows, K, ldw, ldx, ldc, 1, \
+                                                         nullptr, nullptr, err, stream, wq, g,   \
+                                                         units)
 #define B200_G_BN(WF_, S16, S64, S128, S256)                     \
   switch (bn) {                                                  \
     case 16: B200_G(16, S16, WF_);                               \
@@ -1808,7 +1952,7 @@ void gemm_bf16_launch(const void* A, const void* W, void* C, int M, int N, int K
   cudaGetDevice(&dev);
   const SplitWorkspace& w = g_split_ws[dev];
   gemm_bf16_launch_split(A, W, C, M, N, K, lda, ldw, ldc, epi, cfg, cfg < 0 ? 0 : 1, w.ws,
-                         w.ws_bytes, w.counters, w.n_counters, err, stream);
+                         w.ws_bytes, w.counters, w.n_counters, err, stream, /*ext_reduce=*/true);
 }
 
 }  // namespace b200

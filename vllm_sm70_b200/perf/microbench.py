@@ -220,6 +220,9 @@ def main(argv=None):
     ap.add_argument("--epi", type=int, default=0, help="gemm: 1 = fused SiLU*up epilogue")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays")
     ap.add_argument("--block", type=int, default=16, help="attention: KV-cache block size")
+    ap.add_argument("--d", type=int, default=128, help="attention: head dim")
+    ap.add_argument("--hq", type=int, default=32, help="attention: query heads")
+    ap.add_argument("--hkv", type=int, default=8, help="attention: KV heads")
     ap.add_argument("--seq-blocks", action="store_true",
                     help="decode-attn: sequential block table (default: random permutation)")
     args = ap.parse_args(argv)
@@ -252,7 +255,8 @@ def main(argv=None):
         out.append({"kernel": "cublas_bf16", "M": args.M, "N": args.N, "K": args.K,
                     "ms": round(ms, 5), "tflops": round(2.0 * args.M * args.N * args.K / ms / 1e9, 1)})
     elif args.case == "decode-attn":
-        out.append(bench_decode_attn(args.batch, args.ctx, bs=args.block,
+        out.append(bench_decode_attn(args.batch, args.ctx, hq=args.hq, hkv=args.hkv, d=args.d,
+                                     bs=args.block,
                                      splits=max(1, args.splits), iters=args.iters,
                                      seq_blocks=args.seq_blocks))
     elif args.case == "prefill-attn":
