@@ -594,25 +594,32 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         // lane per chunk issues its tile store (one warp-wide instruction).
         constexpr int kChunks = MH * (BN / 32);
         uint8_t* wst = smem + (size_t)q * kChunks * 4096;
+        // Two 32-column TMEM loads per wait: the load latency, not the bytes,
+        // bounds this loop.
+        auto stage_chunk = [&](int c, const uint32_t (&r)[32]) {
+          float4* dst = reinterpret_cast<float4*>(wst + (size_t)c * 4096) + lane * 8;
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            dst[v ^ (lane & 7)] =
+                make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                            __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        };
 #pragma unroll 1
         for (int h = 0; h < MH; ++h) {
 #pragma unroll 1
-          for (int ch = 0; ch < BN / 32; ++ch) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_acc + h * kHalfCols + ch * 32, r);
+          for (int ch = 0; ch < BN / 32; ch += 2) {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(t_acc + h * kHalfCols + ch * 32, r0);
+            if (ch + 1 < BN / 32) tmem_ld_32x32b_x32(t_acc + h * kHalfCols + (ch + 1) * 32, r1);
             tmem_wait_ld();
-            float4* dst = reinterpret_cast<float4*>(wst + (size_t)(h * (BN / 32) + ch) * 4096) +
-                          lane * 8;
-#pragma unroll
-            for (int v = 0; v < 8; ++v)
-              dst[v ^ (lane & 7)] =
-                  make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                              __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            stage_chunk(h * (BN / 32) + ch, r0);
+            if (ch + 1 < BN / 32) stage_chunk(h * (BN / 32) + ch + 1, r1);
           }
         }
         fence_proxy_async_shared();
         tc_fence_before();
         __syncwarp();
+        if (etid == 0) B200_TL(10);
         if (lane == 0) release_acc();
         if (lane < kChunks) {
           const int h = lane / (BN / 32), ch = lane % (BN / 32);
@@ -622,6 +629,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           bulk_wait_all();
         }
         __syncwarp();
+        if (etid == 0) B200_TL(11);
         continue;
       }
       if (split && bulk) {

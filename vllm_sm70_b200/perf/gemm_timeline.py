@@ -15,7 +15,7 @@ import json
 import torch
 
 STAMPS = ["entry", "setup", "first_tma", "first_stage", "last_mma", "first_acc", "epi_done",
-          "exit", "partial_written", "fenced", "bulk_staged", "bulk_stored", "splits_arrived",
+          "exit", "partial_written", "fenced", "staged", "stored", "splits_arrived",
           "bulk_received"]
 SLOTS = 16
 
