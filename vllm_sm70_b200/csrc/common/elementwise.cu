@@ -22,8 +22,8 @@ __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
                                 int I, int ld_x, int ld_o, int block) {
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.y;
-  const int i8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int t = blockIdx.x;  // rows on x: grid.y is limited to 65535
+  const int i8 = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
   if (i8 >= I) return;
   const __nv_bfloat16* g =
       x + (size_t)t * ld_x + (block > 0 ? (i8 / block) * 2 * block + i8 % block : i8);
@@ -66,7 +66,7 @@ void silu_mul_launch(void* out, const void* x, int T, int I, int ld_x, int ld_o,
   if (I % 8) throw std::runtime_error("silu_mul: I % 8 != 0");
   if (block < 0 || block % 8 || (block > 0 && I % block))
     throw std::runtime_error("silu_mul: interleave block must be a multiple of 8 dividing I");
-  dim3 grid((I / 8 + 127) / 128, T);
+  dim3 grid(T, (I / 8 + 127) / 128);
   launch_pdl(silu_mul_kernel, grid, dim3(128), 0, stream, nullptr, (__nv_bfloat16*)out,
              (const __nv_bfloat16*)x, I, ld_x, ld_o, block);
 }
