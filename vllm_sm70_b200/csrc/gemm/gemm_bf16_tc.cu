@@ -502,6 +502,14 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       const int rot = kb_rotation(t, nk, num_m);
       for (int it = 0; it < nk; ++it) {
         const int kb = kb0 + (it + rot) % nk;
+        // The 8 rows' scales do not depend on the TMA copy: issue their loads
+        // first so that their latency overlaps the wait for the weight bytes.
+        typename DqScale<WF>::type sc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int n = uc.p_row + (dt >> 3) + 16 * j;
+          sc[j] = dq_scale<WF>(wq, n < p_rows ? n : 0, kb, c);
+        }
         if (!mbar_wait(&full_bar[stage], phase, err)) {
           *abort_flag = 1;
           break;
@@ -513,7 +521,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
           const int r = (dt >> 3) + 16 * j;  // tile row 0..127
           const int n = uc.p_row + r;        // weight row (stacked for grouped)
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (n < p_rows) v = dequant8<WF>(raw + r * raw_row_bytes(WF), c, wq, n, kb);
+          if (n < p_rows) v = dequant8_s<WF>(raw + r * raw_row_bytes(WF), c, sc[j]);
           *reinterpret_cast<uint4*>(spp + r * 128 + ((c ^ (r & 7)) << 4)) = v;
         }
         // Generic-proxy smem writes -> visible to the tensor core (async proxy).
