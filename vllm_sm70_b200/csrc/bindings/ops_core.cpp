@@ -602,6 +602,89 @@ void ar_rmsnorm(const std::vector<int64_t>& stage_ptrs, const std::vector<int64_
   ar_rmsnorm_launch(p, (int)grid, cur_stream());
 }
 
+// Expert-parallel exchange over peer memory. `bufs` lists, per rank, the
+// addresses of (recv_x, recv_meta, back_y, pad) from the symmetric-memory
+// rendezvous: bufs[4 * r + i].
+static EpParams make_ep(const std::vector<int64_t>& bufs, int64_t rank, int64_t H, int64_t k,
+                        int64_t E_local, int64_t T_cap, int64_t timeout_ms, int device) {
+  const int W = (int)bufs.size() / 4;
+  TORCH_CHECK((int)bufs.size() == 4 * W && W >= 2 && W <= kMaxRanks, "ep: 4 buffers per rank, 2..8 ranks");
+  TORCH_CHECK(rank >= 0 && rank < W, "ep: bad rank");
+  EpParams p{};
+  for (int q = 0; q < W; ++q) {
+    TORCH_CHECK((bufs[4 * q] | bufs[4 * q + 1] | bufs[4 * q + 2] | bufs[4 * q + 3]) % 16 == 0,
+                "ep: 16B alignment");
+    p.recv_x_peer[q] = reinterpret_cast<__nv_bfloat16*>(bufs[4 * q]);
+    p.recv_meta_peer[q] = reinterpret_cast<int*>(bufs[4 * q + 1]);
+    p.back_y_peer[q] = reinterpret_cast<__nv_bfloat16*>(bufs[4 * q + 2]);
+    p.pad_peer[q] = reinterpret_cast<uint32_t*>(bufs[4 * q + 3]);
+  }
+  p.recv_x_local = p.recv_x_peer[rank];
+  p.recv_meta_local = p.recv_meta_peer[rank];
+  p.back_y_local = p.back_y_peer[rank];
+  p.pad_local = p.pad_peer[rank];
+  p.rank = (int)rank;
+  p.world = W;
+  p.H = (int)H;
+  p.k = (int)k;
+  p.E_local = (int)E_local;
+  p.T_cap = (int)T_cap;
+  p.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  p.err = device_status_ptr(device);
+  return p;
+}
+
+void ep_dispatch(const std::vector<int64_t>& bufs, int64_t rank, int64_t E_local, int64_t T_cap,
+                 int64_t timeout_ms, const at::Tensor& x, const at::Tensor& ids,
+                 const at::Tensor& w, at::Tensor& slot, at::Tensor& send_count) {
+  CHECK_CUDA(x); CHECK_BF16(x);
+  TORCH_CHECK(x.is_contiguous() && ids.is_contiguous() && w.is_contiguous(), "ep_dispatch: contiguous");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && w.scalar_type() == at::kFloat &&
+                  slot.scalar_type() == at::kInt && send_count.scalar_type() == at::kInt,
+              "ep_dispatch: dtypes");
+  const int T = (int)x.size(0), k = (int)ids.size(1);
+  const EpParams p = make_ep(bufs, rank, x.size(1), k, E_local, T_cap, timeout_ms, x.get_device());
+  TORCH_CHECK(slot.numel() >= (int64_t)T * p.world && send_count.numel() >= p.world, "ep_dispatch: scratch");
+  c10::cuda::CUDAGuard g(x.device());
+  ep_dispatch_launch(p, x.data_ptr(), ids.data_ptr<int>(), w.data_ptr<float>(), T,
+                     slot.data_ptr<int>(), send_count.data_ptr<int>(), cur_stream());
+}
+
+void ep_receive(const std::vector<int64_t>& bufs, int64_t rank, int64_t E_local, int64_t T_cap,
+                int64_t timeout_ms, at::Tensor& xc, at::Tensor& idc, at::Tensor& wc,
+                at::Tensor& row_src, at::Tensor& n_rows) {
+  CHECK_BF16(xc);
+  const int n_max = (int)xc.size(0), k = (int)idc.size(1);
+  TORCH_CHECK(idc.size(0) >= n_max && wc.size(0) >= n_max && row_src.numel() >= n_max,
+              "ep_receive: buffers");
+  const EpParams p = make_ep(bufs, rank, xc.size(1), k, E_local, T_cap, timeout_ms, xc.get_device());
+  c10::cuda::CUDAGuard g(xc.device());
+  ep_receive_launch(p, xc.data_ptr(), idc.data_ptr<int>(), wc.data_ptr<float>(),
+                    row_src.data_ptr<int>(), n_rows.data_ptr<int>(), n_max, cur_stream());
+}
+
+void ep_return(const std::vector<int64_t>& bufs, int64_t rank, int64_t E_local, int64_t T_cap,
+               int64_t timeout_ms, int64_t k, const at::Tensor& y, const at::Tensor& row_src,
+               const at::Tensor& n_rows) {
+  CHECK_BF16(y);
+  const EpParams p = make_ep(bufs, rank, y.size(1), k, E_local, T_cap, timeout_ms, y.get_device());
+  c10::cuda::CUDAGuard g(y.device());
+  ep_return_launch(p, y.data_ptr(), row_src.data_ptr<int>(), n_rows.data_ptr<int>(),
+                   (int)y.size(0), cur_stream());
+}
+
+void ep_finish(const std::vector<int64_t>& bufs, int64_t rank, int64_t E_local, int64_t T_cap,
+               int64_t timeout_ms, int64_t k, const at::Tensor& slot,
+               const c10::optional<at::Tensor>& shared, at::Tensor& out) {
+  CHECK_BF16(out);
+  TORCH_CHECK(out.is_contiguous(), "ep_finish: out contiguous");
+  if (shared) TORCH_CHECK(shared->is_contiguous() && shared->sizes() == out.sizes(), "ep_finish: shared");
+  const EpParams p = make_ep(bufs, rank, out.size(1), k, E_local, T_cap, timeout_ms, out.get_device());
+  c10::cuda::CUDAGuard g(out.device());
+  ep_finish_launch(p, slot.data_ptr<int>(), (int)out.size(0),
+                   shared ? shared->data_ptr() : nullptr, out.data_ptr(), cur_stream());
+}
+
 // Row-parallel GEMM x @ lin_w^T into this rank's stage, fused in one kernel
 // with the all-reduce + residual add + RMSNorm. Returns false when the
 // shape / tile is not taken (nothing launched; the caller runs the unfused pair).
@@ -734,6 +817,14 @@ TORCH_LIBRARY(_b200_C, m) {
       "paged_attention(Tensor(a!) out, Tensor q, Tensor k_cache, Tensor v_cache, "
       "Tensor block_table, Tensor seq_lens, Tensor cu_q, int max_q_len, float scale, int window, "
       "Tensor? sinks, bool decode, int num_splits, Tensor? part_o, Tensor? part_ml) -> ()");
+  m.def("ep_dispatch(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, Tensor x, "
+        "Tensor ids, Tensor w, Tensor(a!) slot, Tensor(b!) send_count) -> ()");
+  m.def("ep_receive(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, Tensor(a!) xc, "
+        "Tensor(b!) idc, Tensor(c!) wc, Tensor(d!) row_src, Tensor(e!) n_rows) -> ()");
+  m.def("ep_return(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, Tensor y, "
+        "Tensor row_src, Tensor n_rows) -> ()");
+  m.def("ep_finish(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, "
+        "Tensor slot, Tensor? shared, Tensor(a!) out) -> ()");
   m.def("ar_rmsnorm(int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, int[] flag_ptrs, int rank, "
         "int T, int H, Tensor w, float eps, int timeout_ms, int grid) -> ()");
   m.def("gemm_ar_rmsnorm(Tensor x, Tensor lin_w, int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, "
@@ -763,6 +854,10 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("gemm_grouped_out", &b200::gemm_grouped_out);
   m.impl("gemm_wq_out", &b200::gemm_wq_out);
   m.impl("quant_fp8_act", &b200::quant_fp8_act);
+  m.impl("ep_dispatch", &b200::ep_dispatch);
+  m.impl("ep_receive", &b200::ep_receive);
+  m.impl("ep_return", &b200::ep_return);
+  m.impl("ep_finish", &b200::ep_finish);
   m.impl("gemm_fp8_out", &b200::gemm_fp8_out);
   m.impl("gemm_fp8_grouped_out", &b200::gemm_fp8_grouped_out);
   m.impl("dequant_weight", &b200::dequant_weight);

@@ -25,4 +25,35 @@ struct ArRmsNormParams {
 
 void ar_rmsnorm_launch(const ArRmsNormParams& p, int grid, cudaStream_t stream);
 
+// Expert-parallel token exchange over peer memory (ep_a2a.cu). Buffers per
+// rank (symmetric): recv_x [W][T_cap][H] bf16, recv_meta [W][T_cap][2k] int32,
+// back_y [W][T_cap][H] bf16, pad [64] uint32.
+struct EpParams {
+  __nv_bfloat16* recv_x_peer[kMaxRanks];
+  int* recv_meta_peer[kMaxRanks];
+  __nv_bfloat16* back_y_peer[kMaxRanks];
+  uint32_t* pad_peer[kMaxRanks];
+  const __nv_bfloat16* recv_x_local;
+  const int* recv_meta_local;
+  const __nv_bfloat16* back_y_local;
+  uint32_t* pad_local;
+  int rank, world, H, k, E_local, T_cap;
+  unsigned long long timeout_ns;
+  unsigned int* err;
+};
+// Source side: slot[T][W] and send_count[W] (local scratch), rows + routing
+// stored into the destinations' recv buffers, epoch flag raised.
+void ep_dispatch_launch(const EpParams& p, const void* x, const int* ids, const float* w, int T,
+                        int* slot, int* send_count, cudaStream_t stream);
+// Destination side: waits for every source, compacts received rows into
+// xc [n_max, H] / idc, wc [n_max, k] / row_src [n_max]; *n_rows = rows received.
+void ep_receive_launch(const EpParams& p, void* xc, int* idc, float* wc, int* row_src,
+                       int* n_rows, int n_max, cudaStream_t stream);
+// Destination side: partial rows y [n_rows, H] back to their sources.
+void ep_return_launch(const EpParams& p, const void* y, const int* row_src, const int* n_rows,
+                      int n_max, cudaStream_t stream);
+// Source side: out[t] = bf16(sum over destinations in rank order + shared[t]).
+void ep_finish_launch(const EpParams& p, const int* slot, int T, const void* shared, void* out,
+                      cudaStream_t stream);
+
 }  // namespace b200

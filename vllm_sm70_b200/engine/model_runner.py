@@ -140,7 +140,7 @@ class ModelRunner:
                         cu_q=self.cu_q[: b + 1], max_q_len=1, decode=True, num_splits=ns,
                         part_o=po, part_ml=pml, state_slots=self.slot_ids[:b])
         if self.ep is not None:
-            self.ep.step(True)
+            self.ep.step(True, b)
         h = self.model.forward(self.ids[:b], meta, self.kv)
         if self.filtering:
             nxt = self.model.sample_filtered(h, self.temperature[:b], self.top_k[:b],
@@ -313,7 +313,7 @@ class ModelRunner:
                         block_table=h2d(bt_rows), seq_lens=h2d(seq_lens), cu_q=h2d(cu),
                         max_q_len=int(q_len.max()), decode=False, state_slots=state_slots)
         if self.ep is not None:
-            self.ep.step(True)
+            self.ep.step(True, int(toks.numel()))
         return self.model.forward(ids_d, meta, self.kv), cu, h2d
 
     def _sample_last(self, pieces, h, cu, h2d) -> None:

@@ -128,9 +128,10 @@ class B200CudaPlatform(CudaPlatform):
         at least two waves of CTAs over the SMs."""
         import torch
 
-        sms = 148
-        if device is not None and torch.cuda.is_available():
-            sms = torch.cuda.get_device_properties(device).multi_processor_count
+        sms = 148  # B200, when no GPU is visible (CPU-side planning)
+        if torch.cuda.is_available():
+            dev = device if device is not None else torch.cuda.current_device()
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
         for bv in (64, 32, 16, 8):
             if bv > BV:
                 continue

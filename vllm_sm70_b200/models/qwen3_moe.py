@@ -152,6 +152,8 @@ class Qwen3MoeModel(LlamaModel):
 
     def reserve_workspace(self, max_tokens: int) -> None:
         self._ws(max_tokens)
+        if self.ep_a2a is not None:
+            self.ep_a2a.reserve(max_tokens, self.cfg.hidden_size)
 
     def mlp(self, li, L, x, out):
         from .. import ops

@@ -34,6 +34,10 @@ NO_FAKE = {
     "build_prefill_meta": "host-side metadata builder (CPU tensors, data-dependent sizes)",
     "ar_rmsnorm": "NVLink collective over peer pointers (eager / CUDA-graph only)",
     "gemm_ar_rmsnorm": "GEMM + NVLink collective over peer pointers (eager / CUDA-graph only)",
+    "ep_dispatch": "expert-parallel exchange over peer pointers (eager only)",
+    "ep_receive": "expert-parallel exchange over peer pointers (eager only)",
+    "ep_return": "expert-parallel exchange over peer pointers (eager only)",
+    "ep_finish": "expert-parallel exchange over peer pointers (eager only)",
 }
 
 _done = False

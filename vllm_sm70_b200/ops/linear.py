@@ -43,9 +43,13 @@ def configure_workspace(device: int, ws_bytes: int = DEFAULT_WS_BYTES,
     _ws_configured.add(device)
 
 
-def plan(M: int, N: int, K: int, epi: int = 0, num_sm: int = 148) -> tuple[int, int]:
-    """(tile config, split-K) chosen by the native planner."""
+def plan(M: int, N: int, K: int, epi: int = 0, num_sm: int | None = None) -> tuple[int, int]:
+    """(tile config, split-K) chosen by the native planner (for the current
+    device's SM count unless ``num_sm`` is given)."""
     _ext.require()
+    if num_sm is None:
+        num_sm = (torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+                  if torch.cuda.is_available() else 148)
     c, s = torch.ops._b200_C.gemm_bf16_plan(M, N, K, epi, num_sm)
     return int(c), int(s)
 

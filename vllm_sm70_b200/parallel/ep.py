@@ -19,15 +19,19 @@ Per MoE block, on every rank of the EP group:
             expert-slice path, whose all-reduce sums the bf16 partials in
             rank order.
 
-Transport (this module): ``torch.distributed.all_to_all_single`` over the EP
-group -- NCCL on GPUs, gloo on CPU -- after a count exchange, with the row
-payload (hidden bytes + routing) packed into one tensor so a block costs
-three collectives (counts, dispatch, combine). This is the baseline path;
-the split sizes live on the host, so the MoE block is not graph-captured in
-this mode.
+Transport: on GPUs, ``EPPeer`` -- this library's own kernels storing the rows
+straight into the owners' symmetric buffers over NVLink and the partial rows
+back into their sources' (csrc/comm/ep_a2a.cu: no host round trip, no NCCL
+call inside the block; bit-identical results to the baseline). Otherwise
+``torch.distributed.all_to_all_single`` over the EP group -- NCCL on GPUs,
+gloo on CPU -- after a count exchange, with the row payload (hidden bytes +
+routing) packed into one tensor so a block costs three collectives (counts,
+dispatch, combine): the baseline path (``VLLM_B200_FUSED_EP_A2A=0``), whose
+split sizes live on the host.
 
 Lock-step: every forward on every rank is preceded by one ``step()`` vote
-over the CPU group. A rank with no work of its own votes "idle" and runs
+over the CPU group (which also shares every rank's token count: the peer
+path sizes its receive buffers from their sum). A rank with no work of its own votes "idle" and runs
 ``idle_pass`` -- every MoE block with zero local tokens, which still serves
 the tokens other ranks send to its experts -- until a vote finds no rank
 active. So all ranks enter the same collectives in the same order.
@@ -44,6 +48,8 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from ..utils import launch_count
+
 
 @dataclass
 class DispatchPlan:
@@ -53,9 +59,91 @@ class DispatchPlan:
     recv: list[int]          # rows received from each rank
 
 
+@dataclass
+class PeerPlan:
+    T: int                   # local tokens
+    n_max: int               # rows of the compacted receive buffers
+
+
+class EPPeer:
+    """Token exchange over peer memory (kernels in csrc/comm/ep_a2a.cu).
+
+    Symmetric buffers over the EP group, allocated once (a collective: every
+    rank constructs this with the same sizes): recv rows / routing / returned
+    partial rows for ``T_cap`` tokens per source rank, plus a signal pad.
+    Peer addresses come from the symmetric-memory rendezvous; only this
+    library's kernels touch them, with plain NVLink loads and stores."""
+
+    def __init__(self, ps, E_local: int, top_k: int, hidden: int, T_cap: int):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from .. import envs
+
+        self.W, self.rank, self.E_local, self.k, self.H = ps.ep_size, ps.ep_rank, E_local, top_k, hidden
+        self.T_cap = T_cap
+        dev = ps.device
+        W = self.W
+
+        def alloc(n, dt):
+            t = symm_mem.empty(n, dtype=dt, device=dev)
+            return t, symm_mem.rendezvous(t, ps.ep_group)
+
+        self.recv_x, hx = alloc(W * T_cap * hidden, torch.bfloat16)
+        self.recv_meta, hm = alloc(W * T_cap * 2 * top_k, torch.int32)
+        self.back_y, hy = alloc(W * T_cap * hidden, torch.bfloat16)
+        self.pad, hp = alloc(64, torch.int32)
+        self.pad.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+        self._handles = (hx, hm, hy, hp)
+        self.bufs = []
+        for r in range(W):
+            self.bufs += [int(hx.buffer_ptrs[r]), int(hm.buffer_ptrs[r]), int(hy.buffer_ptrs[r]),
+                          int(hp.buffer_ptrs[r])]
+        self.timeout_ms = int(envs.get("VLLM_B200_COMM_TIMEOUT_MS"))
+        self.slot = torch.empty(T_cap * W, dtype=torch.int32, device=dev)
+        self.send_count = torch.empty(W, dtype=torch.int32, device=dev)
+        self.n_rows = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._recv = None
+
+    def _recv_buffers(self, n_max: int, device):
+        if self._recv is None or self._recv[0].shape[0] < n_max:
+            n = max(n_max, 64)
+            self._recv = (torch.empty(n, self.H, dtype=torch.bfloat16, device=device),
+                          torch.empty(n, self.k, dtype=torch.int32, device=device),
+                          torch.empty(n, self.k, dtype=torch.float32, device=device),
+                          torch.empty(n, dtype=torch.int32, device=device))
+        return tuple(b[:n_max] for b in self._recv)
+
+    def _args(self):
+        return (self.bufs, self.rank, self.E_local, self.T_cap, self.timeout_ms)
+
+    def dispatch(self, x, w, ids, n_max: int):
+        ops = torch.ops._b200_C
+        T = x.shape[0]
+        ops.ep_dispatch(*self._args(), x.contiguous(), ids.to(torch.int32).contiguous(),
+                        w.float().contiguous(), self.slot, self.send_count)
+        xc, idc, wc, rs = self._recv_buffers(n_max, x.device)
+        ops.ep_receive(*self._args(), xc, idc, wc, rs, self.n_rows)
+        self._row_src = rs
+        launch_count.add(3)
+        return xc, wc, idc, PeerPlan(T, n_max)
+
+    def combine(self, yr, plan: PeerPlan, shared=None, out=None):
+        ops = torch.ops._b200_C
+        if out is None:
+            out = torch.empty(plan.T, self.H, dtype=yr.dtype, device=yr.device)
+        ops.ep_return(*self._args(), self.k, yr.contiguous(), self._row_src, self.n_rows)
+        sh = shared.contiguous() if shared is not None else None
+        ops.ep_finish(*self._args(), self.k, self.slot, sh, out)
+        launch_count.add(2)
+        return out
+
+
 class EPAllToAll:
     def __init__(self, ps, num_experts: int, top_k: int):
         assert ps.ep_size > 1 and num_experts % ps.ep_size == 0, (ps.ep_size, num_experts)
+        self.ps = ps
         self.W = ps.ep_size
         self.rank = ps.ep_rank
         self.group = ps.ep_group
@@ -64,13 +152,32 @@ class EPAllToAll:
         self.k = top_k
         self.sent_rows = 0       # rows dispatched by this rank (statistics)
         self.recv_rows = 0       # rows served by this rank's experts
+        self.peer: EPPeer | None = None
+        self.t_sum = 0           # tokens of all ranks in the current forward
+        self.t_max = 0
+
+    def reserve(self, max_tokens: int, hidden: int) -> None:
+        """Allocate the peer-memory transport for up to ``max_tokens`` tokens per
+        rank and forward (collective: every rank calls it with the same size)."""
+        from .. import envs
+
+        if (self.peer is None and torch.cuda.is_available() and self.ps.device.type == "cuda"
+                and envs.get("VLLM_B200_FUSED_EP_A2A")):
+            self.peer = EPPeer(self.ps, self.E_local, self.k, hidden, max_tokens)
 
     # -------------------------------------------------------------- lock-step
-    def step(self, active: bool) -> int:
-        """Vote before a forward; returns how many ranks are active in it."""
-        t = torch.tensor([1 if active else 0], dtype=torch.int64)
-        dist.all_reduce(t, group=self.cpu_group)
-        return int(t.item())
+    def step(self, active: bool, tokens: int = 0) -> int:
+        """Vote before a forward; returns how many ranks are active in it, and
+        records the sum / maximum of the ranks' token counts."""
+        t = torch.tensor([1 if active else 0, int(tokens)], dtype=torch.int64)
+        got = [torch.zeros_like(t) for _ in range(self.W)]
+        dist.all_gather(got, t, group=self.cpu_group)
+        self.t_sum = sum(int(g[1]) for g in got)
+        self.t_max = max(int(g[1]) for g in got)
+        return sum(int(g[0]) for g in got)
+
+    def _use_peer(self, x) -> bool:
+        return self.peer is not None and x.is_cuda and self.t_max <= self.peer.T_cap
 
     # -------------------------------------------------------------- transport
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
@@ -80,7 +187,11 @@ class EPAllToAll:
     def dispatch(self, x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor):
         """``x [T, H]``, routing ``w [T, k]`` fp32 / ``ids [T, k]`` int32 ->
         (received rows ``[N, H]``, their weights ``[N, k]``, ids ``[N, k]``,
-        plan)."""
+        plan). On the peer path N is an upper bound (the vote's token sum);
+        rows past the received ones carry expert id -1 (no expert)."""
+        if self._use_peer(x):
+            n_max = max(1, min(self.t_sum, self.W * self.peer.T_cap))
+            return self.peer.dispatch(x, w, ids, n_max)
         T, H = x.shape
         k = self.k
         dev = x.device
@@ -114,6 +225,8 @@ class EPAllToAll:
                 out: torch.Tensor | None = None) -> torch.Tensor:
         """Partial outputs of the received rows back to their source ranks;
         ``out[t] = round(sum over destinations in rank order + shared)``."""
+        if isinstance(plan, PeerPlan):
+            return self.peer.combine(yr, plan, shared, out)
         H = yr.shape[1]
         ys = torch.empty(sum(plan.send), H, dtype=yr.dtype, device=yr.device)
         self._a2a(ys, yr.contiguous(), plan.send, plan.recv)

@@ -30,15 +30,18 @@ SIGNAL_WORDS = 64  # uint32 words per rank: ready[W], done[W], epoch, done_targe
 
 class FusedArRmsNorm:
     def __init__(self, ps, max_tokens: int, hidden: int, dtype=torch.bfloat16,
-                 grid_cap: int = 132):
+                 grid_cap: int | None = None):
         import torch.distributed._symmetric_memory as symm_mem
 
         assert ps.tp_size in (2, 4, 8), ps.tp_size
         self.ps = ps
         self.T_max = max_tokens
         self.H = hidden
-        self.grid_cap = grid_cap
         dev = ps.device
+        # One CTA per SM at most (the whole grid must be resident: it spins on
+        # peer flags).
+        self.grid_cap = grid_cap or (torch.cuda.get_device_properties(dev).multi_processor_count
+                                     if dev.type == "cuda" else 148)
         group = ps.tp_group
 
         def alloc(n, dt):
