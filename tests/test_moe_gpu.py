@@ -41,7 +41,11 @@ def test_experts_forward(b200_ops, fmt, T):
     out = moe.experts_forward(x, w, ids, ew, ws)
     ref = moe.experts_forward_ref(x, w, ids, ew)
     err = float((out.float() - ref).abs().max() / ref.abs().max())
-    assert err < 3e-2, (fmt, T, err)
+    # NVFP4 W4A4 quantises the SiLU*up activations to e2m1 (steps of 25-50 %):
+    # a last-bit difference between the kernel's and the oracle's intermediate
+    # can move an element to the next e2m1 step, so its envelope is wider.
+    tol = 6e-2 if fmt == "nvfp4" else 3e-2
+    assert err < tol, (fmt, T, err)
     out2 = moe.experts_forward(x, w, ids, ew, ws)
     assert torch.equal(out, out2)
 

@@ -198,25 +198,27 @@ void moe_topk(at::Tensor& w, at::Tensor& ids, const at::Tensor& logits, int64_t 
 // Expert-sort the (token, slot) pairs of experts [e_base, e_base + E).
 void moe_permute(const at::Tensor& ids, int64_t E, int64_t e_base, const c10::optional<at::Tensor>& x,
                  const c10::optional<at::Tensor>& x_perm, at::Tensor& counts, at::Tensor& offsets,
-                 at::Tensor& rank_scratch, at::Tensor& pos, at::Tensor& src_row) {
+                 at::Tensor& rank_scratch, at::Tensor& pos, at::Tensor& src_row, int64_t align) {
   CHECK_CUDA(ids);
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.dim() == 2 && ids.is_contiguous(), "ids [T, k] int32");
   const int T = (int)ids.size(0), k = (int)ids.size(1);
   TORCH_CHECK(counts.numel() >= E && offsets.numel() >= E + 1, "moe_permute: counts/offsets");
-  TORCH_CHECK(rank_scratch.numel() >= T * k && pos.numel() >= T * k && src_row.numel() >= T * k,
+  TORCH_CHECK(align >= 1, "moe_permute: align >= 1");
+  const int64_t padded = (int64_t)T * k + E * (align - 1);
+  TORCH_CHECK(rank_scratch.numel() >= T * k && pos.numel() >= T * k && src_row.numel() >= padded,
               "moe_permute: scratch sizes");
   int H = 0;
   if (x) {
     CHECK_BF16((*x));
     TORCH_CHECK(x_perm && x->is_contiguous() && x_perm->is_contiguous(), "moe_permute: x / x_perm");
     H = (int)x->size(1);
-    TORCH_CHECK(H % 8 == 0 && x_perm->size(1) == H && x_perm->size(0) >= T * k, "moe_permute: H");
+    TORCH_CHECK(H % 8 == 0 && x_perm->size(1) == H && x_perm->size(0) >= padded, "moe_permute: H");
   }
   c10::cuda::CUDAGuard g(ids.device());
   moe_permute_launch(ids.data_ptr<int>(), T, k, (int)E, (int)e_base, x ? x->data_ptr() : nullptr, H,
                      x_perm ? x_perm->data_ptr() : nullptr, counts.data_ptr<int>(),
                      offsets.data_ptr<int>(), rank_scratch.data_ptr<int>(), pos.data_ptr<int>(),
-                     src_row.data_ptr<int>(), cur_stream());
+                     src_row.data_ptr<int>(), cur_stream(), (int)align);
 }
 
 void moe_combine(at::Tensor& out, const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w,
@@ -316,6 +318,60 @@ void gemm_fp8_grouped_out(at::Tensor& out, const at::Tensor& xq, const at::Tenso
                           (int)N, K, (int)xq.stride(0), (int)w_stk.stride(0), (int)out.stride(0),
                           row_off.data_ptr<int>(), tile_off.data_ptr<int>(), (int)bn,
                           device_status_ptr(xq.get_device()), cur_stream());
+}
+
+// NVFP4 W4A4 (kind::mxf4nvf4): activation quantisation and the GEMMs. Scale
+// tensors are bytes in the 128-row x 4-scale atom order [rows/128][K/64][512].
+void quant_nvfp4_act(const at::Tensor& x, at::Tensor& xq, at::Tensor& sf, at::Tensor& rs) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_ROWMAJOR(x);
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 64 == 0, "quant_nvfp4_act: K % 64");
+  TORCH_CHECK(xq.element_size() == 1 && xq.dim() == 2 && xq.size(0) >= M && xq.size(1) == K / 2 &&
+                  xq.stride(1) == 1, "quant_nvfp4_act: xq [M, K/2] bytes");
+  TORCH_CHECK(sf.element_size() == 1 && sf.is_contiguous() &&
+                  sf.numel() >= (M + 127) / 128 * (K / 64) * 512, "quant_nvfp4_act: sf atoms");
+  TORCH_CHECK(rs.scalar_type() == at::kFloat && rs.numel() >= M, "quant_nvfp4_act: rs");
+  c10::cuda::CUDAGuard g(x.device());
+  quant_nvfp4_act_launch(x.data_ptr(), (int)x.stride(0), (int)M, (int)K, xq.data_ptr(),
+                         (int)xq.stride(0), sf.data_ptr(), rs.data_ptr<float>(), cur_stream());
+}
+
+void gemm_nvfp4_out(at::Tensor& out, const at::Tensor& xq, const at::Tensor& sfa,
+                    const at::Tensor& rs, const at::Tensor& wq, const at::Tensor& sfw, double g,
+                    int64_t swap) {
+  CHECK_BF16(out); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(xq.element_size() == 1 && wq.element_size() == 1 && xq.dim() == 2 && wq.dim() == 2 &&
+                  xq.stride(1) == 1 && wq.stride(1) == 1 && xq.size(1) == wq.size(1),
+              "gemm_nvfp4: packed operands [rows, K/2]");
+  const int M = (int)xq.size(0), N = (int)wq.size(0), K = (int)xq.size(1) * 2;
+  TORCH_CHECK(sfa.numel() >= (int64_t)(M + 127) / 128 * (K / 64) * 512 &&
+                  sfw.numel() >= (int64_t)(N + 127) / 128 * (K / 64) * 512, "gemm_nvfp4: scale atoms");
+  TORCH_CHECK(rs.scalar_type() == at::kFloat && rs.numel() >= M, "gemm_nvfp4: rs");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_nvfp4: out shape");
+  c10::cuda::CUDAGuard gd(xq.device());
+  gemm_nvfp4_launch(xq.data_ptr(), sfa.data_ptr(), rs.data_ptr<float>(), wq.data_ptr(),
+                    sfw.data_ptr(), (float)g, out.data_ptr(), M, N, K, (int)xq.stride(0),
+                    (int)wq.stride(0), (int)out.stride(0), (int)swap,
+                    device_status_ptr(xq.get_device()), cur_stream());
+}
+
+void gemm_nvfp4_grouped_out(at::Tensor& out, const at::Tensor& xq, const at::Tensor& sfx,
+                            const at::Tensor& rs, const at::Tensor& w_stk, const at::Tensor& sfw,
+                            double g, int64_t E, int64_t N, const at::Tensor& row_off,
+                            at::Tensor& tile_off) {
+  CHECK_BF16(out); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(xq.element_size() == 1 && w_stk.element_size() == 1 && xq.size(1) == w_stk.size(1) &&
+                  w_stk.size(0) == E * N, "gemm_nvfp4_grouped: operands");
+  TORCH_CHECK(row_off.scalar_type() == at::kInt && tile_off.scalar_type() == at::kInt &&
+                  row_off.numel() >= E + 1 && tile_off.numel() >= E + 1, "gemm_nvfp4_grouped: offsets");
+  const int rows = (int)xq.size(0), K = (int)xq.size(1) * 2;
+  TORCH_CHECK(out.size(0) >= rows && out.size(1) == N, "gemm_nvfp4_grouped: out shape");
+  c10::cuda::CUDAGuard gd(xq.device());
+  gemm_nvfp4_grouped_launch(xq.data_ptr(), sfx.data_ptr(), rs.data_ptr<float>(), w_stk.data_ptr(),
+                            sfw.data_ptr(), (float)g, out.data_ptr(), rows, (int)E, (int)N, K,
+                            (int)xq.stride(0), (int)w_stk.stride(0), (int)out.stride(0),
+                            row_off.data_ptr<int>(), tile_off.data_ptr<int>(),
+                            device_status_ptr(xq.get_device()), cur_stream());
 }
 
 void gumbel_argmax(at::Tensor& ids, at::Tensor& vals, const at::Tensor& logits,
@@ -786,7 +842,13 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("moe_topk(Tensor(a!) w, Tensor(b!) ids, Tensor logits, int k, bool use_sigmoid, bool renorm, "
         "Tensor? bias) -> ()");
   m.def("moe_permute(Tensor ids, int E, int e_base, Tensor? x, Tensor(a!)? x_perm, Tensor(b!) counts, "
-        "Tensor(c!) offsets, Tensor(d!) rank_scratch, Tensor(e!) pos, Tensor(f!) src_row) -> ()");
+        "Tensor(c!) offsets, Tensor(d!) rank_scratch, Tensor(e!) pos, Tensor(f!) src_row, "
+        "int align=1) -> ()");
+  m.def("quant_nvfp4_act(Tensor x, Tensor(a!) xq, Tensor(b!) sf, Tensor(c!) rs) -> ()");
+  m.def("gemm_nvfp4_out(Tensor(a!) out, Tensor xq, Tensor sfa, Tensor rs, Tensor wq, Tensor sfw, "
+        "float g, int swap=-1) -> ()");
+  m.def("gemm_nvfp4_grouped_out(Tensor(a!) out, Tensor xq, Tensor sfx, Tensor rs, Tensor w_stk, "
+        "Tensor sfw, float g, int E, int N, Tensor row_off, Tensor(b!) tile_off) -> ()");
   m.def("moe_combine(Tensor(a!) out, Tensor y, Tensor pos, Tensor w, Tensor? shared, float shared_scale) -> ()");
   m.def("gemm_grouped_out(Tensor(a!) out, Tensor x, Tensor w_stk, int E, int N, Tensor row_off, "
         "Tensor(b!) tile_off, int fmt, Tensor? scales, float out_scale, int bn=0) -> ()");
@@ -854,6 +916,9 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("gemm_grouped_out", &b200::gemm_grouped_out);
   m.impl("gemm_wq_out", &b200::gemm_wq_out);
   m.impl("quant_fp8_act", &b200::quant_fp8_act);
+  m.impl("quant_nvfp4_act", &b200::quant_nvfp4_act);
+  m.impl("gemm_nvfp4_out", &b200::gemm_nvfp4_out);
+  m.impl("gemm_nvfp4_grouped_out", &b200::gemm_nvfp4_grouped_out);
   m.impl("ep_dispatch", &b200::ep_dispatch);
   m.impl("ep_receive", &b200::ep_receive);
   m.impl("ep_return", &b200::ep_return);

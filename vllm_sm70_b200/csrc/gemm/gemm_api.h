@@ -118,6 +118,22 @@ void gemm_fp8_grouped_launch(const void* Xq, const float* sa, int ld_sa, const v
                              int ldx, int ldw, int ldc, const int* row_off, int* tile_off, int bn,
                              unsigned int* err, cudaStream_t stream);
 
+// ---- NVFP4 W4A4 on kind::mxf4nvf4 (gemm_nvfp4_tc.cu) ----
+// Scale tensors (bytes) are in atom order [rows/128][K/64][512]: row r's 4
+// scales of 64-k group kg at ((r/128) * K/64 + kg) * 512 + (r%32)*16 + ((r%128)/32)*4.
+// Activations: xq [M, K/2] packed e2m1, sf atoms, rs [M] per-token fp32 scales.
+void quant_nvfp4_act_launch(const void* x, int ldx, int M, int K, void* xq, int ldq, void* sf,
+                            float* rs, cudaStream_t stream);
+// C = rs[m] * g * (Aq . Wq^T with both block scales); swap < 0: automatic.
+void gemm_nvfp4_launch(const void* Aq, const void* sfa, const float* rs, const void* Wq,
+                       const void* sfw, float g, void* C, int M, int N, int K, int lda, int ldw,
+                       int ldc, int swap, unsigned int* err, cudaStream_t stream);
+// Grouped over expert-sorted rows whose expert blocks start at multiples of 128.
+void gemm_nvfp4_grouped_launch(const void* Xq, const void* sfx, const float* rs, const void* Wstk,
+                               const void* sfw, float g, void* C, int rows, int E, int N, int K,
+                               int ldx, int ldw, int ldc, const int* row_off, int* tile_off,
+                               unsigned int* err, cudaStream_t stream);
+
 struct GemmPlan {
   int cfg;
   int splits;  // split-K factor (1 = none); partials reduced in-kernel, fixed order

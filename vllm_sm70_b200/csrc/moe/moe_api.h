@@ -8,9 +8,11 @@ void moe_topk_launch(const void* logits, bool bf16, int ld, int T, int E, int k,
                      bool renorm, const float* bias, float* w, int* ids, cudaStream_t stream);
 
 // ids [T*k] global expert ids; experts [e_base, e_base + E) are local.
+// align > 1: every local expert's rows start at a multiple of `align` in x_perm
+// (x_perm / src_row then need T*k + E*(align-1) rows).
 void moe_permute_launch(const int* ids, int T, int k, int E, int e_base, const void* x, int H,
                         void* x_perm, int* counts, int* offsets, int* rank_scratch, int* pos,
-                        int* src_row, cudaStream_t stream);
+                        int* src_row, cudaStream_t stream, int align = 1);
 
 void moe_combine_launch(const void* y, const int* pos, const float* w, int T, int k, int H,
                         const void* shared, float shared_scale, void* out, cudaStream_t stream);

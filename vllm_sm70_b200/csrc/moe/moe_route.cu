@@ -141,12 +141,16 @@ __global__ void expert_count_kernel(const int* __restrict__ ids, int pairs, int*
   if (threadIdx.x == 0) counts[e - e_base] = running;
 }
 
-__global__ void offsets_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets) {
+// Expert start offsets; with align > 1 every expert's block starts at a
+// multiple of `align` rows (the NVFP4 grouped GEMM reads its activation
+// scales in 128-row atoms).
+__global__ void offsets_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets,
+                               int align) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     int acc = 0;
     for (int e = 0; e < E; ++e) {
       offsets[e] = acc;
-      acc += counts[e];
+      acc += (counts[e] + align - 1) / align * align;
     }
     offsets[E] = acc;
   }
@@ -216,11 +220,11 @@ void moe_topk_launch(const void* logits, bool bf16, int ld, int T, int E, int k,
 
 void moe_permute_launch(const int* ids, int T, int k, int E, int e_base, const void* x, int H,
                         void* x_perm, int* counts, int* offsets, int* rank_scratch, int* pos,
-                        int* src_row, cudaStream_t stream) {
+                        int* src_row, cudaStream_t stream, int align) {
   const int pairs = T * k;
   if (E <= 0) return;
   expert_count_kernel<<<E, 256, 0, stream>>>(ids, pairs, counts, rank_scratch, E, e_base);
-  offsets_kernel<<<1, 32, 0, stream>>>(counts, E, offsets);
+  offsets_kernel<<<1, 32, 0, stream>>>(counts, E, offsets, align < 1 ? 1 : align);
   if (pairs > 0)
     scatter_kernel<<<pairs, 128, 0, stream>>>(ids, rank_scratch, offsets, pairs, k, E, e_base,
                                                (const __nv_bfloat16*)x, H,

@@ -72,6 +72,10 @@ _reg("VLLM_B200_FP8_W8A8", "kill", True, "kernels",
      "(weights dequantised to bf16 in the GEMM producer).")
 _reg("VLLM_B200_AWQ_GEMM", "kill", True, "kernels", "AWQ int4 GEMM.")
 _reg("VLLM_B200_NVFP4_GEMM", "kill", True, "kernels", "NVFP4 GEMM.")
+_reg("VLLM_B200_NVFP4_W4A4", "kill", True, "kernels",
+     "NVFP4 weights run W4A4: activations quantised per token (fp32 row scale) and 16-element "
+     "block (e4m3 scale) to e2m1, kind::mxf4nvf4 tensor-core MMAs with the block scales in TMEM. "
+     "0 = W4A16 (weights dequantised to bf16 in the GEMM producer).")
 _reg("VLLM_B200_MOE", "kill", True, "kernels", "Grouped expert GEMM + router kernels.")
 _reg("VLLM_B200_ROUTER", "kill", True, "kernels", "Fused MoE router (U3 provider).")
 _reg("VLLM_B200_SAMPLER", "kill", True, "kernels", "Hidden-state sampler (U4 provider).")

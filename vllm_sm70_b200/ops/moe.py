@@ -98,12 +98,24 @@ class ExpertWeights:
         return (a.reference_weight().view(self.E, 2 * self.I, self.H),
                 b.reference_weight().view(self.E, self.H, self.I))
 
+    def nvfp4_atoms(self):
+        """Block scales of w13 / w2 in the tensor-core atom order (cached)."""
+        if getattr(self, "_atoms", None) is None:
+            self._atoms = (_q.nvfp4_sf_atoms(self.s13.view(torch.uint8)),
+                           _q.nvfp4_sf_atoms(self.s2.view(torch.uint8)))
+        return self._atoms
+
     def bytes(self) -> int:
         n = self.w13.numel() * self.w13.element_size() + self.w2.numel() * self.w2.element_size()
         for s in (self.s13, self.s2):
             if s is not None:
                 n += s.numel() * s.element_size()
         return n
+
+
+def _w4a4(ew) -> bool:
+    return (ew.fmt == "nvfp4" and _q.w4a4_enabled() and ew.H % 256 == 0 and ew.I % 256 == 0
+            and (2 * ew.I) % 128 == 0 and ew.H % 128 == 0)
 
 
 def _wrap(fmt, raw, scales, gscale, N, K):
@@ -134,7 +146,31 @@ class MoEWorkspace:
         self.act = torch.empty(P, I, dtype=torch.bfloat16, device=device)
         self.y = torch.empty(P, H, dtype=torch.bfloat16, device=device)
         self.P, self.H, self.I = P, H, I
+        self.E_local = E_local
         self._fp8 = None
+        self._fp4 = None
+
+    def nvfp4_buffers(self):
+        """Padded-permutation buffers for the W4A4 grouped GEMMs (every expert's
+        rows start at a multiple of 128): rows P + E * 127."""
+        if self._fp4 is None:
+            dev = self.x_perm.device
+            Pp = self.P + self.E_local * 127
+            H, I = self.H, self.I
+            bf = dict(dtype=torch.bfloat16, device=dev)
+            u8 = dict(dtype=torch.uint8, device=dev)
+            f32 = dict(dtype=torch.float32, device=dev)
+            self._fp4 = dict(
+                Pp=Pp, x=torch.empty(Pp, H, **bf), h=torch.empty(Pp, 2 * I, **bf),
+                act=torch.empty(Pp, I, **bf), y=torch.empty(Pp, H, **bf),
+                src=torch.empty(Pp, dtype=torch.int32, device=dev),
+                xq=torch.empty(Pp, H // 2, **u8),
+                xsf=torch.empty((Pp + 127) // 128 * (H // 64) * 512, **u8),
+                xrs=torch.empty(Pp, **f32),
+                aq=torch.empty(Pp, I // 2, **u8),
+                asf=torch.empty((Pp + 127) // 128 * (I // 64) * 512, **u8),
+                ars=torch.empty(Pp, **f32))
+        return self._fp4
 
     def fp8_buffers(self):
         """e4m3 activation rows and their K-group-major scales for the W8A8
@@ -155,6 +191,25 @@ def experts_forward_ref(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew:
     w13, w2 = ew.dense_ref()
     T, k = ids.shape
     out = torch.zeros(T, ew.H, dtype=torch.float32, device=x.device)
+    if _w4a4(ew):
+        # W4A4: exact e2m1 x e4m3 weights times the global scales, and both GEMM
+        # inputs through the per-token NVFP4 activation quantisation.
+        w13 = (_wrap("nvfp4", ew.w13, ew.s13, 1.0, ew.E * 2 * ew.I, ew.H).exact_weight()
+               * ew.g13).view(ew.E, 2 * ew.I, ew.H)
+        w2 = (_wrap("nvfp4", ew.w2, ew.s2, 1.0, ew.E * ew.H, ew.I).exact_weight()
+              * ew.g2).view(ew.E, ew.H, ew.I)
+        xf = _q.nvfp4_act_dequant_ref(x)
+        for t in range(T):
+            for j in range(k):
+                e = int(ids[t, j]) - e_base
+                if e < 0 or e >= ew.E:
+                    continue
+                # The kernels round h to bf16 before SiLU*up (the GEMM output).
+                h = (w13[e] @ xf[t]).to(torch.bfloat16).float()
+                g, u = h[: ew.I], h[ew.I:]
+                a = (g * torch.sigmoid(g) * u).to(torch.bfloat16)
+                out[t] += float(w[t, j]) * (w2[e] @ _q.nvfp4_act_dequant_ref(a[None])[0])
+        return out
     w8a8 = ew.fmt == "fp8" and _q.w8a8_enabled()
     if w8a8:
         # W8A8: exact dequantised weights, and both GEMM inputs go through the
@@ -201,6 +256,26 @@ def experts_forward(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: Exp
     pos = ws.pos[:T]
     ops.moe_permute(ids, ew.E, e_base, x, xp, ws.counts, ws.offsets, ws.rank, pos, ws.src)
     fmt = FMT[ew.fmt]
+    if _w4a4(ew):
+        # W4A4 grouped GEMMs on kind::mxf4nvf4: a padded permutation (expert
+        # blocks start at multiples of 128 rows) so the activation scale atoms
+        # of a 128-row token tile belong to one expert.
+        b = ws.nvfp4_buffers()
+        Pp = P + ew.E * 127
+        xpp, hp, ap, yp = b["x"][:Pp], b["h"][:Pp], b["act"][:Pp], b["y"][:Pp]
+        ops.moe_permute(ids, ew.E, e_base, x, xpp, ws.counts, ws.offsets, ws.rank, pos,
+                        b["src"][:Pp], 128)
+        s13, s2 = ew.nvfp4_atoms()
+        ops.quant_nvfp4_act(xpp, b["xq"][:Pp], b["xsf"], b["xrs"])
+        ops.gemm_nvfp4_grouped_out(hp, b["xq"][:Pp], b["xsf"], b["xrs"], ew.w13, s13, ew.g13,
+                                   ew.E, 2 * ew.I, ws.offsets, ws.tile_off)
+        ops.silu_mul(ap, hp)
+        ops.quant_nvfp4_act(ap, b["aq"][:Pp], b["asf"], b["ars"])
+        ops.gemm_nvfp4_grouped_out(yp, b["aq"][:Pp], b["asf"], b["ars"], ew.w2, s2, ew.g2,
+                                   ew.E, ew.H, ws.offsets, ws.tile_off)
+        ops.moe_combine(out, yp, pos, w, shared, 1.0)
+        launch_count.add(9)
+        return out
     if ew.fmt == "fp8" and _q.w8a8_enabled():
         # W8A8 grouped GEMMs on kind::f8f6f4 with per-K-block scale promotion.
         xq, sa1, aq, sa2 = ws.fp8_buffers()

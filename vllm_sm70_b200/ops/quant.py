@@ -163,6 +163,75 @@ def gemm_fp8(x: torch.Tensor, w_raw: torch.Tensor, sw: torch.Tensor,
     return out
 
 
+# ------------------------------------------------------------------ NVFP4 W4A4
+def w4a4_enabled() -> bool:
+    return bool(envs.get("VLLM_B200_NVFP4_W4A4"))
+
+
+def nvfp4_sf_atoms(sf: torch.Tensor) -> torch.Tensor:
+    """Block scales ``[N, K/16]`` (e4m3 bytes, row-major) -> the tensor-core
+    atom order ``[ceil(N/128)][K/64][512]``: row r's 4 scales of 64-k group
+    kg at byte (r % 32) * 16 + ((r % 128) / 32) * 4 + j. Padded rows get 0."""
+    N, G = sf.shape
+    assert G % 4 == 0, "K must be a multiple of 64"
+    Np = (N + 127) // 128 * 128
+    s = torch.zeros(Np, G, dtype=torch.uint8, device=sf.device)
+    s[:N] = sf.view(torch.uint8)
+    # [nb, m1, m0, kg, j] -> [nb, kg, m0, m1, j]
+    s = s.view(Np // 128, 4, 32, G // 4, 4).permute(0, 3, 2, 1, 4).contiguous()
+    return s.view(-1)
+
+
+def _e2m1_round(y: torch.Tensor) -> torch.Tensor:
+    """Round to the nearest e2m1 value (ties to the even mantissa), saturating
+    at +-6: the rounding of ``cvt.rn.satfinite.e2m1x2.f32``."""
+    a = y.abs()
+    r = torch.where(a <= 0.25, 0.0,
+        torch.where(a < 0.75, 0.5,
+        torch.where(a <= 1.25, 1.0,
+        torch.where(a < 1.75, 1.5,
+        torch.where(a <= 2.5, 2.0,
+        torch.where(a < 3.5, 3.0,
+        torch.where(a <= 5.0, 4.0, 6.0)))))))
+    return torch.copysign(r, y)
+
+
+def quant_nvfp4_act_ref(x: torch.Tensor):
+    """Torch oracle of the W4A4 activation quantiser: per row rs = amax / 2688
+    (448 * 6; 1 for a zero row), per 16-element block s = e4m3(amax_blk / 6 /
+    rs), values e2m1(x / (s * rs)). Returns (e2m1 values [M, K] fp32, block
+    scales [M, K/16] as fp32 of the e4m3 bytes, rs [M])."""
+    xf = x.float()
+    M, K = xf.shape
+    amax = xf.abs().amax(1)
+    one = torch.ones_like(amax)
+    rs = torch.where(amax > 0, amax / torch.full_like(amax, 2688.0), one)
+    blocks = xf.view(M, K // 16, 16)
+    bmax = blocks.abs().amax(-1)
+    s = (bmax / torch.full_like(bmax, 6.0)) / rs[:, None]
+    s8 = s.clamp(max=FP8_MAX).to(torch.float8_e4m3fn)
+    sdec = s8.float() * rs[:, None]
+    inv = torch.where(sdec > 0, torch.ones_like(sdec) / torch.where(sdec > 0, sdec, 1.0), 0.0)
+    q = _e2m1_round(blocks * inv[..., None]).view(M, K)
+    return q, s8.float(), rs
+
+
+def nvfp4_act_dequant_ref(x: torch.Tensor) -> torch.Tensor:
+    q, s, rs = quant_nvfp4_act_ref(x)
+    return q * (s * rs[:, None]).repeat_interleave(16, 1)
+
+
+def quant_nvfp4_act(x: torch.Tensor):
+    """(xq [M, K/2] packed e2m1, scale atoms, rs [M]) on the CUDA kernel."""
+    M, K = x.shape
+    xq = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device)
+    sf = torch.empty((M + 127) // 128 * (K // 64) * 512, dtype=torch.uint8, device=x.device)
+    rs = torch.empty(max(M, 1), dtype=torch.float32, device=x.device)
+    torch.ops._b200_C.quant_nvfp4_act(x, xq, sf, rs)
+    launch_count.add(1)
+    return xq, sf, rs
+
+
 # ------------------------------------------------------------------ linears
 class _WQLinear(Linear):
     fmt: str
@@ -301,6 +370,47 @@ class Nvfp4Linear(_WQLinear):
         if with_global:
             w = (w.float() * self.out_scale).to(torch.bfloat16)
         return w
+
+    def exact_weight(self) -> torch.Tensor:
+        """fp32 e2m1 x e4m3 block scale (no global scale, no bf16 rounding)."""
+        N, K = self.out_features, self.in_features
+        lut = E2M1.to(self.raw.device)
+        q = torch.stack([lut[(self.raw & 0xF).long()], lut[(self.raw >> 4).long()]], -1).view(N, K)
+        return q * self.scales.view(torch.float8_e4m3fn).float().repeat_interleave(16, 1)
+
+    def sf_atoms(self) -> torch.Tensor:
+        if getattr(self, "_atoms", None) is None or self._atoms.device != self.raw.device:
+            self._atoms = nvfp4_sf_atoms(self.scales)
+        return self._atoms
+
+    def _w4a4(self, x) -> bool:
+        return (w4a4_enabled() and self.in_features % 256 == 0 and
+                self.out_features % 8 == 0)
+
+    def forward(self, x, out=None):
+        if self._w4a4(x):
+            if x.is_cuda and envs.get("VLLM_B200_NVFP4_GEMM"):
+                _ext.require()
+                if out is None:
+                    out = torch.empty(x.shape[0], self.out_features, dtype=torch.bfloat16,
+                                      device=x.device)
+                xq, sf, rs = quant_nvfp4_act(x)
+                torch.ops._b200_C.gemm_nvfp4_out(out, xq, sf, rs, self.raw, self.sf_atoms(),
+                                                 self.out_scale, -1)
+                launch_count.add(1)
+                return out
+            if not x.is_cuda:
+                r = self.reference_forward(x).to(torch.bfloat16)
+                if out is None:
+                    return r
+                out.copy_(r)
+                return out
+        return super().forward(x, out)
+
+    def reference_forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._w4a4(x):
+            return (nvfp4_act_dequant_ref(x) @ self.exact_weight().t()) * self.out_scale
+        return super().reference_forward(x)
 
 
 def merge_nvfp4_parts(ws, ss, gs):
