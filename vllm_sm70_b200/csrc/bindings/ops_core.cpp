@@ -322,7 +322,8 @@ void gemm_fp8_grouped_out(at::Tensor& out, const at::Tensor& xq, const at::Tenso
 
 // NVFP4 W4A4 (kind::mxf4nvf4): activation quantisation and the GEMMs. Scale
 // tensors are bytes in the 128-row x 4-scale atom order [rows/128][K/64][512].
-void quant_nvfp4_act(const at::Tensor& x, at::Tensor& xq, at::Tensor& sf, at::Tensor& rs) {
+void quant_nvfp4_act(const at::Tensor& x, at::Tensor& xq, at::Tensor& sf, at::Tensor& rs,
+                     const c10::optional<at::Tensor>& n_rows) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_ROWMAJOR(x);
   const int64_t M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 64 == 0, "quant_nvfp4_act: K % 64");
@@ -333,7 +334,8 @@ void quant_nvfp4_act(const at::Tensor& x, at::Tensor& xq, at::Tensor& sf, at::Te
   TORCH_CHECK(rs.scalar_type() == at::kFloat && rs.numel() >= M, "quant_nvfp4_act: rs");
   c10::cuda::CUDAGuard g(x.device());
   quant_nvfp4_act_launch(x.data_ptr(), (int)x.stride(0), (int)M, (int)K, xq.data_ptr(),
-                         (int)xq.stride(0), sf.data_ptr(), rs.data_ptr<float>(), cur_stream());
+                         (int)xq.stride(0), sf.data_ptr(), rs.data_ptr<float>(), cur_stream(),
+                         n_rows ? n_rows->data_ptr<int>() : nullptr);
 }
 
 void gemm_nvfp4_out(at::Tensor& out, const at::Tensor& xq, const at::Tensor& sfa,
@@ -797,12 +799,15 @@ void argmax(at::Tensor& ids, const c10::optional<at::Tensor>& vals, const at::Te
                 vals ? vals->data_ptr<float>() : nullptr, (int)id_offset, cur_stream());
 }
 
-void silu_mul(at::Tensor& out, const at::Tensor& x, int64_t block) {
+void silu_mul(at::Tensor& out, const at::Tensor& x, int64_t block,
+              const c10::optional<at::Tensor>& n_rows) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "silu_mul: 2-D rows");
+  if (n_rows) TORCH_CHECK(n_rows->scalar_type() == at::kInt, "silu_mul: n_rows int32");
   c10::cuda::CUDAGuard g(x.device());
   silu_mul_launch(out.data_ptr(), x.data_ptr(), (int)x.size(0), (int)(x.size(1) / 2),
-                  (int)x.stride(0), (int)out.stride(0), cur_stream(), (int)block);
+                  (int)x.stride(0), (int)out.stride(0), cur_stream(), (int)block,
+                  n_rows ? n_rows->data_ptr<int>() : nullptr);
 }
 
 void embedding(at::Tensor& out, const at::Tensor& ids, const at::Tensor& table,
@@ -844,7 +849,8 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("moe_permute(Tensor ids, int E, int e_base, Tensor? x, Tensor(a!)? x_perm, Tensor(b!) counts, "
         "Tensor(c!) offsets, Tensor(d!) rank_scratch, Tensor(e!) pos, Tensor(f!) src_row, "
         "int align=1) -> ()");
-  m.def("quant_nvfp4_act(Tensor x, Tensor(a!) xq, Tensor(b!) sf, Tensor(c!) rs) -> ()");
+  m.def("quant_nvfp4_act(Tensor x, Tensor(a!) xq, Tensor(b!) sf, Tensor(c!) rs, "
+        "Tensor? n_rows=None) -> ()");
   m.def("gemm_nvfp4_out(Tensor(a!) out, Tensor xq, Tensor sfa, Tensor rs, Tensor wq, Tensor sfw, "
         "float g, int swap=-1) -> ()");
   m.def("gemm_nvfp4_grouped_out(Tensor(a!) out, Tensor xq, Tensor sfx, Tensor rs, Tensor w_stk, "
@@ -894,7 +900,7 @@ TORCH_LIBRARY(_b200_C, m) {
         "-> bool");
   m.def("kv_cache_write(Tensor k, Tensor v, Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor slots) -> ()");
   m.def("argmax(Tensor(a!) ids, Tensor(b!)? vals, Tensor logits, int id_offset) -> ()");
-  m.def("silu_mul(Tensor(a!) out, Tensor x, int block=0) -> ()");
+  m.def("silu_mul(Tensor(a!) out, Tensor x, int block=0, Tensor? n_rows=None) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor ids, Tensor table, int vocab_start) -> ()");
 }
 

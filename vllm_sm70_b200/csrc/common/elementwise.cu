@@ -19,10 +19,11 @@ namespace {
 // `block` columns ([g0..g_b-1, u0..u_b-1, g_b.., ...], the layout of the
 // fused-epilogue gate_up weights); out [T, I]
 __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
-                                int I, int ld_x, int ld_o, int block) {
+                                int I, int ld_x, int ld_o, int block, const int* __restrict__ n_rows) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;  // rows on x: grid.y is limited to 65535
+  if (n_rows != nullptr && t >= *n_rows) return;  // rows past the device-side count
   const int i8 = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
   if (i8 >= I) return;
   const __nv_bfloat16* g =
@@ -61,14 +62,14 @@ __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int64_t*
 }  // namespace
 
 void silu_mul_launch(void* out, const void* x, int T, int I, int ld_x, int ld_o,
-                     cudaStream_t stream, int block) {
+                     cudaStream_t stream, int block, const int* n_rows) {
   if (T <= 0) return;
   if (I % 8) throw std::runtime_error("silu_mul: I % 8 != 0");
   if (block < 0 || block % 8 || (block > 0 && I % block))
     throw std::runtime_error("silu_mul: interleave block must be a multiple of 8 dividing I");
   dim3 grid(T, (I / 8 + 127) / 128);
   launch_pdl(silu_mul_kernel, grid, dim3(128), 0, stream, nullptr, (__nv_bfloat16*)out,
-             (const __nv_bfloat16*)x, I, ld_x, ld_o, block);
+             (const __nv_bfloat16*)x, I, ld_x, ld_o, block, n_rows);
 }
 
 void embedding_launch(void* out, const int64_t* ids, const void* table, int T, int H,

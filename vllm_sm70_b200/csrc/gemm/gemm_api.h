@@ -122,8 +122,10 @@ void gemm_fp8_grouped_launch(const void* Xq, const float* sa, int ld_sa, const v
 // Scale tensors (bytes) are in atom order [rows/128][K/64][512]: row r's 4
 // scales of 64-k group kg at ((r/128) * K/64 + kg) * 512 + (r%32)*16 + ((r%128)/32)*4.
 // Activations: xq [M, K/2] packed e2m1, sf atoms, rs [M] per-token fp32 scales.
+// n_rows (device, optional): rows at or past *n_rows are skipped (padded
+// MoE permutations whose used length is only known on the device).
 void quant_nvfp4_act_launch(const void* x, int ldx, int M, int K, void* xq, int ldq, void* sf,
-                            float* rs, cudaStream_t stream);
+                            float* rs, cudaStream_t stream, const int* n_rows = nullptr);
 // C = rs[m] * g * (Aq . Wq^T with both block scales); swap < 0: automatic.
 void gemm_nvfp4_launch(const void* Aq, const void* sfa, const float* rs, const void* Wq,
                        const void* sfw, float g, void* C, int M, int N, int K, int lda, int ldw,

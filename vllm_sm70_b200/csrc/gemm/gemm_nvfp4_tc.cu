@@ -342,9 +342,10 @@ gemm_nvfp4_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
 // up to the 128-row atom boundary get zero scales. One CTA per row.
 __global__ void __launch_bounds__(128) quant_nvfp4_act_kernel(
     const __nv_bfloat16* __restrict__ x, int ldx, int M, int K, uint8_t* __restrict__ xq,
-    int ldq, uint8_t* __restrict__ sf, float* __restrict__ rs) {
+    int ldq, uint8_t* __restrict__ sf, float* __restrict__ rs, const int* __restrict__ n_rows) {
   pdl_wait();
   const int m = blockIdx.x;
+  if (n_rows != nullptr && m >= *n_rows) return;
   const int nblk = K / 16;
   const int kgs = K / 64;
   __shared__ float red[4];
@@ -442,14 +443,14 @@ void check_nvfp4(int K, int ldq_bytes, int ldw_bytes, int ldc) {
 }  // namespace
 
 void quant_nvfp4_act_launch(const void* x, int ldx, int M, int K, void* xq, int ldq, void* sf,
-                            float* rs, cudaStream_t stream) {
+                            float* rs, cudaStream_t stream, const int* n_rows) {
   if (M <= 0) return;
   if (K % 64 != 0) throw std::runtime_error("quant_nvfp4_act: K must be a multiple of 64");
   if (ldx % 8 != 0 || ldq % 8 != 0) throw std::runtime_error("quant_nvfp4_act: row strides");
   const int rows = (M + 127) / 128 * 128;  // whole atoms: padded rows get zero scales
   launch_pdl(quant_nvfp4_act_kernel, dim3(rows), dim3(128), 0, stream, nullptr,
              reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, reinterpret_cast<uint8_t*>(xq),
-             ldq, reinterpret_cast<uint8_t*>(sf), rs);
+             ldq, reinterpret_cast<uint8_t*>(sf), rs, n_rows);
 }
 
 void gemm_nvfp4_launch(const void* Aq, const void* sfa, const float* rs, const void* Wq,

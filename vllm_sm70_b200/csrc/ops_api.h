@@ -31,7 +31,7 @@ void argmax_launch(const void* logits, bool is_bf16, int rows, int V, int ld, in
 // block = 0: x = [gate | up]; block > 0: gate / up interleaved in blocks of
 // `block` columns.
 void silu_mul_launch(void* out, const void* x, int T, int I, int ld_x, int ld_o,
-                     cudaStream_t stream, int block = 0);
+                     cudaStream_t stream, int block = 0, const int* n_rows = nullptr);
 void embedding_launch(void* out, const int64_t* ids, const void* table, int T, int H,
                       int64_t vocab_start, int64_t vocab_end, cudaStream_t stream);
 

@@ -266,11 +266,12 @@ def experts_forward(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, ew: Exp
         ops.moe_permute(ids, ew.E, e_base, x, xpp, ws.counts, ws.offsets, ws.rank, pos,
                         b["src"][:Pp], 128)
         s13, s2 = ew.nvfp4_atoms()
-        ops.quant_nvfp4_act(xpp, b["xq"][:Pp], b["xsf"], b["xrs"])
+        used = ws.offsets[ew.E:ew.E + 1]  # padded rows in use (device)
+        ops.quant_nvfp4_act(xpp, b["xq"][:Pp], b["xsf"], b["xrs"], used)
         ops.gemm_nvfp4_grouped_out(hp, b["xq"][:Pp], b["xsf"], b["xrs"], ew.w13, s13, ew.g13,
                                    ew.E, 2 * ew.I, ws.offsets, ws.tile_off)
-        ops.silu_mul(ap, hp)
-        ops.quant_nvfp4_act(ap, b["aq"][:Pp], b["asf"], b["ars"])
+        ops.silu_mul(ap, hp, 0, used)
+        ops.quant_nvfp4_act(ap, b["aq"][:Pp], b["asf"], b["ars"], used)
         ops.gemm_nvfp4_grouped_out(yp, b["aq"][:Pp], b["asf"], b["ars"], ew.w2, s2, ew.g2,
                                    ew.E, ew.H, ws.offsets, ws.tile_off)
         ops.moe_combine(out, yp, pos, w, shared, 1.0)
