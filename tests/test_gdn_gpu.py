@@ -77,3 +77,84 @@ def test_gated_rmsnorm(b200_ops):
     ref = gdn.gated_rmsnorm_ref(o, z, w, 4, 1e-6)
     gdn.gated_rmsnorm(o, z, w, 4, 1e-6)
     assert _rel(o, ref) < 2e-2
+
+
+def _gdn_ref_fast(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV):
+    """fp32 oracle vectorised over heads (token loop only): long sequences."""
+    import torch.nn.functional as F
+
+    T = q.shape[0]
+    DK = q.shape[1] // HK
+    DV = v.shape[1] // HV
+    o = torch.empty(T, HV * DV, dtype=torch.float32, device=q.device)
+    rep = HV // HK
+    for s in range(len(slots)):
+        t0, t1 = int(cu[s]), int(cu[s + 1])
+        slot = int(slots[s])
+        S = (state[slot].clone() if slot >= 0 else torch.zeros(HV, DV, DK, device=q.device))
+        qs = q[t0:t1].float().view(-1, HK, DK).repeat_interleave(rep, 1)
+        ks = k[t0:t1].float().view(-1, HK, DK).repeat_interleave(rep, 1)
+        qs = qs / (qs.pow(2).sum(-1, keepdim=True) + 1e-6).sqrt() * DK ** -0.5
+        ks = ks / (ks.pow(2).sum(-1, keepdim=True) + 1e-6).sqrt()
+        g = -torch.exp(A_log)[None] * F.softplus(a[t0:t1].float() + dt_bias[None])
+        beta = torch.sigmoid(b[t0:t1].float())
+        vs = v[t0:t1].float().view(-1, HV, DV)
+        for t in range(t1 - t0):
+            S = S * torch.exp(g[t])[:, None, None]
+            kt = ks[t]
+            u = torch.einsum("hvk,hk->hv", S, kt)
+            S = S + beta[t][:, None, None] * torch.einsum("hv,hk->hvk", vs[t] - u, kt)
+            o[t0 + t] = torch.einsum("hvk,hk->hv", S, qs[t]).reshape(-1)
+        if slot >= 0:
+            state[slot] = S
+    return o
+
+
+@pytest.mark.parametrize("HK,HV", [(2, 4), (16, 32)])
+def test_gdn_chunked_prefill_matches_recurrence(b200_ops, HK, HV):
+    """Chunked (64-token WY/UT) prefill vs the fp32 token-serial oracle: chunk
+    boundaries, partial chunks, carried-in states, slot < 0, state write-back."""
+    torch.manual_seed(5)
+    D = 128
+    lens = [1, 63, 64, 65, 300, 200]
+    T = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), device="cuda", dtype=torch.int32)
+    slots = torch.tensor([0, 1, -1, 2, 3, 4], device="cuda", dtype=torch.int32)
+    q = torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(T, HV * D, device="cuda", dtype=torch.bfloat16)
+    a = torch.randn(T, HV, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(T, HV, device="cuda", dtype=torch.bfloat16)
+    A_log = torch.randn(HV, device="cuda") * 0.5
+    dt = torch.randn(HV, device="cuda") * 0.5
+    st = torch.randn(5, HV, D, D, device="cuda") * 0.1
+    st_ref = st.clone()
+    o = gdn.gdn_recurrent(q, k, v, a, b, A_log, dt, st, cu, slots, HK, HV, chunked=True)
+    orf = _gdn_ref_fast(q, k, v, a, b, A_log, dt, st_ref, cu, slots, HK, HV)
+    torch.cuda.synchronize()
+    assert _rel(o, orf) < 3e-2
+    assert _rel(st, st_ref) < 3e-2
+
+
+def test_gdn_chunked_long_sequence(b200_ops):
+    """8192 tokens (the Qwen3-Next prompt length) in one sequence: the chunked
+    kernel stays on the fp32 recurrence over 128 chunks of carried state."""
+    torch.manual_seed(6)
+    HK, HV, D, T = 1, 2, 128, 8192
+    cu = torch.tensor([0, T], device="cuda", dtype=torch.int32)
+    slots = torch.tensor([0], device="cuda", dtype=torch.int32)
+    q = torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(T, HV * D, device="cuda", dtype=torch.bfloat16)
+    a = torch.randn(T, HV, device="cuda", dtype=torch.bfloat16) - 2
+    b = torch.randn(T, HV, device="cuda", dtype=torch.bfloat16)
+    A_log = torch.randn(HV, device="cuda") * 0.5 - 1
+    dt = torch.randn(HV, device="cuda") * 0.5
+    st = torch.zeros(1, HV, D, D, device="cuda")
+    st_ref = st.clone()
+    o = gdn.gdn_recurrent(q, k, v, a, b, A_log, dt, st, cu, slots, HK, HV, reset_state=True,
+                          chunked=True)
+    orf = _gdn_ref_fast(q, k, v, a, b, A_log, dt, st_ref, cu, slots, HK, HV)
+    torch.cuda.synchronize()
+    assert _rel(o, orf) < 3e-2
+    assert _rel(st, st_ref) < 3e-2

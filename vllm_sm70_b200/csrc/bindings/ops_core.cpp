@@ -443,7 +443,7 @@ void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, cons
                    const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
                    const at::Tensor& dt_bias, at::Tensor& state, const at::Tensor& cu,
                    const at::Tensor& slots, int64_t HK, int64_t HV, bool reset_state,
-                   bool write_state) {
+                   bool write_state, bool chunked) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(a); CHECK_BF16(b);
   CHECK_BF16(o);
   TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
@@ -464,7 +464,12 @@ void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, cons
   p.HK = (int)HK; p.HV = (int)HV; p.reset_state = reset_state ? 1 : 0;
   p.write_state = write_state ? 1 : 0;
   c10::cuda::CUDAGuard g(q.device());
-  gdn_recurrent_launch(p, (int)slots.numel(), DK, DV, cur_stream());
+  if (chunked) {
+    TORCH_CHECK(gdn_chunk_supported(DK, DV), "gdn: the chunked form needs DK = DV = 128");
+    gdn_chunk_launch(p, (int)slots.numel(), DK, DV, cur_stream());
+  } else {
+    gdn_recurrent_launch(p, (int)slots.numel(), DK, DV, cur_stream());
+  }
 }
 
 void gated_rmsnorm(at::Tensor& o, const at::Tensor& z, const at::Tensor& w, int64_t H, double eps) {
@@ -871,7 +876,7 @@ TORCH_LIBRARY(_b200_C, m) {
         "Tensor cu, Tensor slots, bool silu, bool write_state=True) -> ()");
   m.def("gdn_recurrent(Tensor(a!) o, Tensor q, Tensor k, Tensor v, Tensor a, Tensor b, "
         "Tensor A_log, Tensor dt_bias, Tensor(b!) state, Tensor cu, Tensor slots, int HK, int HV, "
-        "bool reset_state, bool write_state=True) -> ()");
+        "bool reset_state, bool write_state=True, bool chunked=False) -> ()");
   m.def("gated_rmsnorm(Tensor(a!) o, Tensor z, Tensor w, int H, float eps) -> ()");
   m.def("rejection_sample(Tensor(a!) out_tokens, Tensor(b!) num_out, Tensor target_logits, "
         "Tensor draft_logits, Tensor draft_ids, Tensor temperature, Tensor seeds, int offset) -> ()");

@@ -27,6 +27,10 @@ void causal_conv1d_launch(const void* x, int ldx, const void* w, const void* bia
                           int ldy, float* state, const int* cu, const int* slots, int nseq, int C,
                           int W, bool silu, bool write_state, cudaStream_t stream);
 void gdn_recurrent_launch(const GdnParams& p, int nseq, int dk, int dv, cudaStream_t stream);
+// Chunked (WY / UT form, 64-token chunks) gated delta rule for prefill:
+// same parameters and state semantics as gdn_recurrent_launch (DK = DV = 128).
+bool gdn_chunk_supported(int dk, int dv);
+void gdn_chunk_launch(const GdnParams& p, int nseq, int dk, int dv, cudaStream_t stream);
 void gated_rmsnorm_launch(void* o, int ldo, const void* z, int ldz, const void* w, int T, int H,
                           int D, float eps, cudaStream_t stream);
 

@@ -81,6 +81,9 @@ _reg("VLLM_B200_ROUTER", "kill", True, "kernels", "Fused MoE router (U3 provider
 _reg("VLLM_B200_SAMPLER", "kill", True, "kernels", "Hidden-state sampler (U4 provider).")
 _reg("VLLM_B200_GREEDY_FASTPATH", "kill", True, "kernels", "Vocab-parallel greedy top-1.")
 _reg("VLLM_B200_GDN", "kill", True, "kernels", "Gated-DeltaNet kernels.")
+_reg("VLLM_B200_GDN_CHUNK", "kill", True, "kernels",
+     "Gated-DeltaNet prefill in 64-token chunks (WY/UT form on the tensor cores) instead of "
+     "the token-serial recurrence (head dims 128).")
 # -- collectives ----------------------------------------------------------
 _reg("VLLM_B200_FUSED_AR_RMSNORM", "kill", True, "comm",
      "Fused all-reduce + residual + RMSNorm over NVLink peer memory (0 = NCCL + norm).")

@@ -320,7 +320,7 @@ class Qwen3NextModel(Qwen3MoeModel):
         v = conv_out[:, 2 * HK * DK:]
         o = gdn_ops.gdn_recurrent(q, k, v, a, b, L["A_log"], L["dt_bias"],
                                   self.gdn_state[lin_idx], meta.cu_q, slots, HK, HV,
-                                  write_state=write)
+                                  write_state=write, chunked=not meta.decode)
         gdn_ops.gated_rmsnorm(o, z, L["gnorm"], HV, self.cfg.rms_eps)
         return L["out"].forward(o, out=comm.row_parallel_out(T, x.shape[1]))
 

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .. import _ext
+from .. import _ext, envs
 from ..utils import launch_count
 
 
@@ -94,14 +94,24 @@ def causal_conv1d(x, w, bias, state, cu, slots, silu=True, out=None, write_state
     return out
 
 
+def chunk_ok(q, v, HK, HV) -> bool:
+    """The chunked (64-token WY/UT) prefill kernel takes head dims 128."""
+    return (q.is_cuda and envs.get("VLLM_B200_GDN_CHUNK") and q.shape[1] // HK == 128
+            and v.shape[1] // HV == 128)
+
+
 def gdn_recurrent(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV, reset_state=False,
-                  out=None, write_state=True):
+                  out=None, write_state=True, chunked=False):
+    """Gated delta rule over varlen sequences. ``chunked``: prefill through the
+    chunked tensor-core kernel when it takes the shape (same state semantics);
+    decode / verify steps stay token-serial."""
     if out is None:
         out = torch.empty(q.shape[0], v.shape[1], dtype=torch.bfloat16, device=q.device)
     if q.is_cuda:
         _ext.require()
         torch.ops._b200_C.gdn_recurrent(out, q, k, v, a, b, A_log, dt_bias, state, cu, slots,
-                                        HK, HV, reset_state, write_state)
+                                        HK, HV, reset_state, write_state,
+                                        bool(chunked) and chunk_ok(q, v, HK, HV))
         launch_count.add(1)
     else:
         st = state if write_state else state.clone()
