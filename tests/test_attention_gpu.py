@@ -121,16 +121,21 @@ def test_stale_cache_rows_nan(b200_ops, bs, decode, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
-def test_rope_kv_write(b200_ops, rel_err):
+@pytest.mark.parametrize("d,rot,norm", [(128, 128, True), (128, 128, False), (64, 64, True),
+                                         (256, 256, True), (256, 64, True)])
+def test_rope_kv_write(b200_ops, rel_err, d, rot, norm):
+    """Full-width rotation runs the 16-byte-access kernel (D/16 threads per
+    head), partial rotation the warp-per-head kernel; both against the fp32
+    reference, V copied bit-exactly."""
     torch.manual_seed(5)
-    T, hq, hkv, d, bs = 37, 8, 2, 128, 16
+    T, hq, hkv, bs = 37, 8, 2, 16
     qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda", dtype=torch.bfloat16)
     pos = torch.randint(0, 500, (T,), device="cuda")
     slots = torch.randperm(64 * bs, device="cuda")[:T]
     slots[3] = -1
-    cs = A.rope_cos_sin(d, 1024, 5e5, device="cuda")
-    qn = torch.randn(d, device="cuda", dtype=torch.bfloat16)
-    kn = torch.randn(d, device="cuda", dtype=torch.bfloat16)
+    cs = A.rope_cos_sin(rot, 1024, 5e5, device="cuda")
+    qn = torch.randn(d, device="cuda", dtype=torch.bfloat16) if norm else None
+    kn = torch.randn(d, device="cuda", dtype=torch.bfloat16) if norm else None
     kc = torch.zeros(64, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
     qkv2, kc2, vc2 = qkv.clone(), kc.clone(), vc.clone()

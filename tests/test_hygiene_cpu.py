@@ -33,3 +33,17 @@ def test_no_planning_note_references_or_closed_calls():
     bad = [str(p) for p in SOURCES if NOTES.search(p.read_text(errors="ignore"))
            or BATCHED.search(p.read_text(errors="ignore"))]
     assert bad == []
+
+
+def test_native_env_knobs_registered():
+    """Every VLLM_B200_* variable the native library reads is documented in
+    the Python registry (envs.py), like the ones read from Python."""
+    from vllm_sm70_b200 import envs
+
+    names = set()
+    for p in SOURCES:
+        if p.suffix in (".cu", ".cuh", ".h", ".cpp"):
+            names.update(re.findall(r'getenv\("(VLLM_B200_[A-Z0-9_]+)"\)', p.read_text()))
+    assert names, "no native knobs found"
+    missing = sorted(n for n in names if n not in envs._REGISTRY)
+    assert missing == []

@@ -95,6 +95,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: pairs with the release of a remote
+// arrive (mbar_arrive_cluster) from another CTA of the cluster.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.
 // Returns false (and records kErrMbarTimeout) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
@@ -103,6 +117,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0) {
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        if (err) atomicCAS(err, kErrNone, kErrMbarTimeout);
+        return false;
+      }
+      if (err && *(volatile unsigned int*)err != kErrNone) return false;
+    }
+  }
+}
+
+// Bounded mbar_wait with cluster-scope acquire (see mbar_try_wait_cluster).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  unsigned int* err) {
+  const unsigned long long t0 = globaltimer();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
       if (globaltimer() - t0 > kWaitTimeoutNs) {
         if (err) atomicCAS(err, kErrNone, kErrMbarTimeout);
@@ -162,6 +193,20 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
 
 // Untiled bulk copy this CTA's shared memory -> global (both addresses 16-byte
 // aligned, size a multiple of 16), tracked by the issuing thread's bulk group.
+// Bulk copy from this CTA's shared memory into another CTA's shared memory
+// of the cluster (no multicast): `dst_cluster` and the completion barrier
+// `bar_cluster` are shared::cluster addresses in the destination CTA; the
+// destination barrier's transaction count drops by `bytes` when they land.
+// Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void* smem_src,
+                                                     uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(smem_u32(smem_src)), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_store(void* dst, const void* smem_src, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
                    reinterpret_cast<uint64_t>(dst)),

@@ -132,8 +132,14 @@ __device__ __forceinline__ UnitCoord unit_coord(int t, int num_m, int num_n, con
 // with gemm_set_timeline): 16 %globaltimer slots per CTA -- entry, set-up
 // done, first TMA issued, first operand stage ready, last MMA issued, first
 // accumulator ready, epilogue done, exit, then the split-K epilogue phases
-// (partial written, fenced).
+// (partial written, fenced). Buffer layout: kTlCtas launch counters (one per
+// block index), then kTlSeqs x kTlCtas rows of 16 stamps. Each CTA takes its
+// block's next launch number, so a chain of launches with the same grid
+// keeps every launch's stamps (row = launch % kTlSeqs).
 __device__ unsigned long long* g_gemm_timeline = nullptr;
+constexpr int kSerialSplitFlag = 1 << 16;  // or-ed into the split count
+constexpr int kTlCtas = 256;
+constexpr int kTlSeqs = 64;
 
 template <int BN, int STAGES, int WF = kWBf16, int MH = 1>
 struct Smem {
@@ -159,11 +165,19 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                     int ldc, int p_rows, int q_rows, int K, int splits_arg, float* __restrict__ ws,
                     int* __restrict__ counters, unsigned int* err, const WQParams wq,
                     const GroupInfo grp, const int pm, const int pbox, const int qbox) {
-  unsigned long long* const tl = g_gemm_timeline;
-  // A negative split count asks for the external reduction (see `ext`).
-  const int splits = splits_arg < 0 ? -splits_arg : splits_arg;
+  // Timeline row of this CTA (thread 0 until set-up, then every thread).
+  unsigned long long* tl_row = nullptr;
+  if (threadIdx.x == 0 && g_gemm_timeline != nullptr && blockIdx.x < kTlCtas) {
+    unsigned long long* const tl = g_gemm_timeline;
+    const unsigned long long seq = atomicAdd(&tl[blockIdx.x], 1ull) % kTlSeqs;
+    tl_row = tl + kTlCtas + (seq * kTlCtas + blockIdx.x) * 16;
+  }
+  // A negative split count asks for the external reduction (see `ext`);
+  // kSerialSplitFlag asks for the serial reduction (see `dist`).
+  const bool serial_req = splits_arg > 0 && (splits_arg & kSerialSplitFlag) != 0;
+  const int splits = (splits_arg < 0 ? -splits_arg : splits_arg) & (kSerialSplitFlag - 1);
 #define B200_TL(i) \
-  do { if (tl) tl[(size_t)blockIdx.x * 16 + (i)] = globaltimer(); } while (0)
+  do { if (tl_row) tl_row[(i)] = globaltimer(); } while (0)
   if (threadIdx.x == 0) B200_TL(0);
   // Programmatic dependent launch: grouped tile lists and quantised
   // operands are read by every role, so those launches wait up front; plain
@@ -188,6 +202,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   constexpr int kAccCols = MH == 1 ? BN : MH * kHalfCols;
   constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
   using S = Smem<QR, STAGES, WF, MH>;
+  static_assert((3 * STAGES + 6) * 8 + 32 <= S::kBarBytes, "barrier / slot area");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -202,6 +217,8 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  unsigned long long** tl_slot = reinterpret_cast<unsigned long long**>(tmem_slot + 4);
+  uint64_t* free_bar = reinterpret_cast<uint64_t*>(tmem_slot + 6);  // cluster split: peers idle
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -238,7 +255,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   // of splits x M x N floats.
   const bool ext = kExtKind && splits_arg < -1 && ws != nullptr && grp.E == 0 &&
                    num_units <= ustride;
-  const bool dist = splits > 1 && grp.E == 0 && num_units <= ustride && !ext;
+  // Serial instead (requested): the last split to arrive sums the tile; the
+  // others leave as soon as their partials are stored, freeing their SMs for
+  // the next kernel's CTAs (which start streaming their weights early).
+  const bool dist = splits > 1 && grp.E == 0 && num_units <= ustride && !ext && !serial_req;
   // Bulk variant of the distributed reduction (plain epilogue): the partial
   // chunks move between shared memory (the idle operand ring) and the
   // workspace as 16 KB bulk copies instead of per-thread 16-byte accesses, so
@@ -272,7 +292,9 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     }
     mbar_init(done_bar, 1);
     mbar_init(recv_bar, 1);
+    mbar_init(free_bar, splits > 1 ? splits - 1 : 1);
     *abort_flag = 0;
+    *tl_slot = tl_row;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -297,11 +319,13 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   }
   tc_fence_before();
   __syncthreads();
-  // Pair: the peer's TMA completions and barrier arrivals target this CTA's
-  // barriers, so both CTAs' initialisation must be visible first.
-  if constexpr (PAIR) cluster_sync_all();
+  // Pair / cluster split: the peers' TMA completions, bulk copies and barrier
+  // arrivals target this CTA's barriers, so every CTA's initialisation must
+  // be visible first.
+  if constexpr (PAIR || CL) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  tl_row = *tl_slot;
   if (threadIdx.x == 0) {
     B200_TL(1);
     pdl_trigger();
@@ -313,7 +337,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     // A bulk-tensor instruction costs its warp a few hundred ns, so the L2
     // warm-up and the initial pipeline fill go out lane-parallel (one k-block
     // per lane); the steady-state loop issues from lane 0.
-    auto load_stage = [&](const UnitCoord& uc, int kb, int stage) {
+    // parts: bit 0 = P tiles, bit 1 = Q tiles, bit 2 = arm the stage's barrier
+    // with the whole stage's bytes (bf16 operands only; quantised stages
+    // always load whole).
+    auto load_stage = [&](const UnitCoord& uc, int kb, int stage, int parts = 7) {
       uint8_t* spp = smem + stage * S::kStageBytes;
       if constexpr (kQuant) {
         // Activations (Q side, bf16) + the raw weight tile; the P operand is
@@ -328,27 +355,33 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         if constexpr (PAIR) {
           // Both CTAs' halves complete on the leader's barrier, which
           // expects the bytes of the whole pair.
-          if (leader)
+          if (leader && (parts & 4))
             mbar_arrive_expect_tx(&full_bar[stage],
                                   (uint32_t)(2 * (BM * BK * 2 + S::kQBytes)));
           const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0u);
-          for (int r = 0; r < BM; r += pbox)
-            tma_load_2d_pair(spp + r * (BK * 2), &tmap_p, fb, kb * BK,
-                             uc.p_row + (int)prank * BM + r);
-          for (int r = 0; r < QR; r += qbox)
-            tma_load_2d_pair(spp + S::kPBytes + r * (BK * 2), &tmap_q, fb, kb * BK,
-                             uc.q_row + (int)prank * QR + r);
+          if (parts & 1)
+            for (int r = 0; r < BM; r += pbox)
+              tma_load_2d_pair(spp + r * (BK * 2), &tmap_p, fb, kb * BK,
+                               uc.p_row + (int)prank * BM + r);
+          if (parts & 2)
+            for (int r = 0; r < QR; r += qbox)
+              tma_load_2d_pair(spp + S::kPBytes + r * (BK * 2), &tmap_q, fb, kb * BK,
+                               uc.q_row + (int)prank * QR + r);
         } else {
-          mbar_arrive_expect_tx(&full_bar[stage],
-                                (uint32_t)(MH * p_rows_tile * BK * 2 + S::kQBytes));
+          if (parts & 4)
+            mbar_arrive_expect_tx(&full_bar[stage],
+                                  (uint32_t)(MH * p_rows_tile * BK * 2 + S::kQBytes));
+          if (parts & 1) {
 #pragma unroll
-          for (int h = 0; h < MH; ++h)
-            for (int r = 0; r < p_rows_tile; r += pbox)
-              tma_load_2d(spp + h * S::kHalfBytes + r * (BK * 2), &tmap_p, &full_bar[stage],
-                          kb * BK, uc.p_row + h * BM + r);
-          for (int r = 0; r < BN; r += qbox)
-            tma_load_2d(spp + S::kPBytes + r * (BK * 2), &tmap_q, &full_bar[stage], kb * BK,
-                        uc.q_row + r);
+            for (int h = 0; h < MH; ++h)
+              for (int r = 0; r < p_rows_tile; r += pbox)
+                tma_load_2d(spp + h * S::kHalfBytes + r * (BK * 2), &tmap_p, &full_bar[stage],
+                            kb * BK, uc.p_row + h * BM + r);
+          }
+          if (parts & 2)
+            for (int r = 0; r < BN; r += qbox)
+              tma_load_2d(spp + S::kPBytes + r * (BK * 2), &tmap_q, &full_bar[stage], kb * BK,
+                          uc.q_row + r);
         }
       }
     };
@@ -359,11 +392,16 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
       const int nk = kb1 - kb0;
       const int rot = kb_rotation(t, nk, num_m);
+      if constexpr (!kQuant) pre = max(0, min(nk, STAGES));
       if (!early_wait) {
-        // Before waiting for the previous kernel: pull the weight tiles of
-        // this CTA's first 2 x STAGES k-blocks into L2.
-        const int npf = min(nk, 2 * STAGES);
-        for (int it = lane; it < npf; it += 32) {
+        // Before waiting for the previous kernel (weights are never written
+        // by an earlier kernel): issue the weight tiles of the first-round
+        // stages straight into the ring, each stage's barrier armed with the
+        // whole stage's bytes, and pull the weights of the next STAGES
+        // k-blocks into L2. Only the activation tiles wait for the previous
+        // kernel's results.
+        constexpr int kW = SWAP ? 1 : 2, kA = SWAP ? 2 : 1;
+        for (int it = pre + lane; it < min(nk, 2 * STAGES); it += 32) {
           const int kb = kb0 + (it + rot) % nk;
           if constexpr (SWAP) {
             for (int r = 0; r < p_rows_tile; r += pbox)
@@ -373,10 +411,11 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
               tma_prefetch_l2_2d(&tmap_q, kb * BK, uc.q_row + (int)prank * QR + r);
           }
         }
+        if (lane < pre) load_stage(uc, kb0 + (lane + rot) % nk, lane, 4 | kW);
+        if (lane == 0 && pre > 0) B200_TL(2);
         pdl_wait();
-      }
-      if constexpr (!kQuant) {
-        pre = max(0, min(nk, STAGES));
+        if (lane < pre) load_stage(uc, kb0 + (lane + rot) % nk, lane, kA);
+      } else if constexpr (!kQuant) {
         if (lane < pre) load_stage(uc, kb0 + (lane + rot) % nk, lane);
         if (lane == 0 && pre > 0) B200_TL(2);
       }
@@ -1045,7 +1084,158 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     if (tma_st && lane == 0) bulk_wait_all();
   }
 
+  // Cluster split-K by bulk copies (plain epilogue, 128-row tiles): the tile's
+  // 32-column chunks are dealt round-robin to the splits (chunk ch belongs to
+  // split ch % splits, the cluster rank). Each CTA stages the chunks it does
+  // not own in its idle operand ring, grouped by owner; tells every peer that
+  // its own ring is idle and its receive barrier armed (remote arrive); once
+  // all peers have said so, one thread copies each owner's group into that
+  // owner's receive area with a single shared::cta -> shared::cluster bulk
+  // copy. Every CTA then sums its owned chunks over the splits in split order
+  // (its own partial straight from TMEM) and stores bf16 tiles through the
+  // output tensor map. Ring use per CTA: the staged chunks, then the received
+  // ones: (chunks - owned) + (splits - 1) x owned chunks of 16 KB.
+  constexpr bool kClBulkKind = CL && EPI == kEpiNone && MH == 1 && BN % 32 == 0;
+  constexpr int kClChunks = BN / 32;
+  constexpr int kClChunkBytes = BM * 32 * 4;
+  const int cl_need = kClChunks - kClChunks / (splits > 0 ? splits : 1) +
+                      (splits - 1) * ((kClChunks + splits - 1) / (splits > 0 ? splits : 1));
+  const bool cl_bulk = kClBulkKind && splits > 1 &&
+                       (size_t)cl_need * kClChunkBytes <= (size_t)S::kTileBytes;
+  if constexpr (kClBulkKind) {
+  if (cl_bulk && warp >= 2) {
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    const int etid = threadIdx.x - 64;
+    const int sp = (int)cluster_ctarank();
+    const int ns = splits;
+    const int t = (int)blockIdx.x / ns;
+    const UnitCoord uc = unit_coord<BN>(t, num_m, num_n, grp, p_rows, q_rows, p_tile);
+    const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16);
+    auto n_own_of = [&](int d) { return (kClChunks - d + ns - 1) / ns; };
+    const int my_own = n_own_of(sp);
+    // Receive area of CTA d: right after its staged chunks, [source][owned chunk].
+    auto recv_chunk = [&](int d, int src_slot, int k) {
+      return (kClChunks - n_own_of(d)) + src_slot * n_own_of(d) + k;
+    };
+    auto put = [&](int slot, const uint32_t (&r)[32]) {
+      float4* dst = reinterpret_cast<float4*>(smem + (size_t)slot * kClChunkBytes) +
+                    row_in_tile * 8;
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        dst[v ^ (row_in_tile & 7)] =
+            make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                        __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+    };
+    if (cl_ok) {
+      // Stage the chunks the other splits own, grouped by owner (two TMEM
+      // loads in flight per wait).
+      int slot = 0;
+#pragma unroll 1
+      for (int d = 0; d < ns; ++d) {
+        if (d == sp) continue;
+#pragma unroll 1
+        for (int ch = d; ch < kClChunks; ch += 2 * ns) {
+          uint32_t r0[32], r1[32];
+          const bool two = ch + ns < kClChunks;
+          tmem_ld_32x32b_x32(t_acc + ch * 32, r0);
+          if (two) tmem_ld_32x32b_x32(t_acc + (ch + ns) * 32, r1);
+          tmem_wait_ld();
+          put(slot++, r0);
+          if (two) put(slot++, r1);
+        }
+      }
+    }
+    fence_proxy_async_shared();
+    named_barrier_sync(1, 128);
+    if (etid == 0) {
+      bool ok = cl_ok;
+      if (ok) {
+        mbar_arrive_expect_tx(recv_bar, (uint32_t)((ns - 1) * my_own * kClChunkBytes));
+        for (int d = 0; d < ns; ++d)
+          if (d != sp) mbar_arrive_cluster(mapa_shared(smem_u32(free_bar), (uint32_t)d));
+        ok = mbar_wait_cluster(free_bar, 0, err);
+        B200_TL(10);
+      }
+      if (ok) {
+        int off = 0;
+        for (int d = 0; d < ns; ++d) {
+          const int nd = n_own_of(d);
+          if (d == sp || nd == 0) continue;  // (more splits than chunks: d owns none)
+          const int src_slot = sp < d ? sp : sp - 1;
+          const uint32_t dst = mapa_shared(
+              smem_u32(smem + (size_t)recv_chunk(d, src_slot, 0) * kClChunkBytes), (uint32_t)d);
+          bulk_copy_to_cluster(dst, smem + (size_t)off * kClChunkBytes,
+                               (uint32_t)(nd * kClChunkBytes),
+                               mapa_shared(smem_u32(recv_bar), (uint32_t)d));
+          off += nd;
+        }
+      }
+      *last_flag = ok ? 1 : 0;
+    }
+    named_barrier_sync(1, 128);
+    const bool ok = *last_flag != 0 && mbar_wait(recv_bar, 0, err);
+    if (etid == 0) B200_TL(13);
+    if (!ok) {
+      *abort_flag = 1;
+    } else {
+      tc_fence_after();
+      int ebuf = 0;
+#pragma unroll 1
+      for (int k = 0; k < my_own; ++k) {
+        const int ch = sp + k * ns;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_acc + ch * 32, r);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = 0.f;
+        for (int s2 = 0; s2 < ns; ++s2) {
+          if (s2 == sp) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) v[c] += __uint_as_float(r[c]);
+          } else {
+            const float4* src =
+                reinterpret_cast<const float4*>(
+                    smem + (size_t)recv_chunk(sp, s2 < sp ? s2 : s2 - 1, k) * kClChunkBytes) +
+                row_in_tile * 8;
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 x = src[c4 ^ (row_in_tile & 7)];
+              v[4 * c4] += x.x;
+              v[4 * c4 + 1] += x.y;
+              v[4 * c4 + 2] += x.z;
+              v[4 * c4 + 3] += x.w;
+            }
+          }
+        }
+        // bf16 tile store through the output map (64-byte rows, 64B swizzle).
+        uint8_t* buf = epi_stage + (size_t)(q * 2 + ebuf) * 2048;
+        if (lane == 0) bulk_wait_read_le1();
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 pk;
+          pk.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
+          pk.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
+          pk.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
+          pk.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
+          *reinterpret_cast<uint4*>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) = pk;
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_c, buf, uc.out_j0 + ch * 32, uc.out_i0 + q * 32);
+          bulk_commit();
+        }
+        ebuf ^= 1;
+      }
+      if (lane == 0) bulk_wait_all();
+    }
+  }
+  }
   if constexpr (CL) {
+  if (!cl_bulk) {
     // -------------------------------------------------- cluster reduction
     // Rows of the tile are dealt out to the cluster's CTAs (CTA d owns rows
     // [d * R, (d + 1) * R)). Barrier 1: every CTA's MMAs are complete, so the
@@ -1160,13 +1350,15 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
       }
     }
   }
+  }
 
   if (threadIdx.x == 64) B200_TL(6);
   tc_fence_before();
   __syncthreads();
-  // Pair: no CTA may leave while its peer can still signal its barriers or
-  // read its shared memory; the TMEM release is collective over the pair.
-  if constexpr (PAIR) cluster_sync_all();
+  // Pair / cluster split: no CTA may leave while a peer can still signal its
+  // barriers or copy into or out of its shared memory; the TMEM release is
+  // collective over a pair.
+  if constexpr (PAIR || CL) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     if constexpr (PAIR) tmem_dealloc_pair(tmem_base, kTmemCols);
@@ -1202,6 +1394,20 @@ int tma_box_rows() {
     return e ? std::atoi(e) : 0;
   }();
   return v;
+}
+
+// Split-K reduction mode: VLLM_B200_GEMM_SERIAL_SPLIT=1 makes the last split
+// to arrive sum each tile (the others exit early); default: the splits of a
+// tile that are resident together share the reduction.
+bool serial_split_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLLM_B200_GEMM_SERIAL_SPLIT");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+int split_arg(int splits) {
+  return (splits > 1 && serial_split_enabled()) ? (splits | kSerialSplitFlag) : splits;
 }
 
 template <int BN, int STAGES, bool SWAP, int EPI, int WF = kWBf16, int MH = 1>
@@ -1262,7 +1468,8 @@ bool launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   if (WF == kWBf16) q.out_scale = 1.f;
   launch_pdl(kernel, dim3(grid), dim3(WF == kWBf16 ? kThreads : kThreadsQ), S::kTotal, stream,
              nullptr, tp, tq, use_ext ? tc : tc_plain, reinterpret_cast<__nv_bfloat16*>(C), ldc, p_rows,
-             q_rows, K, use_ext ? -splits : splits, ws, counters, err, q, grp, pm, pbox, qbox);
+             q_rows, K, use_ext ? -splits : split_arg(splits), ws, counters, err, q, grp, pm,
+             pbox, qbox);
   return use_ext;
 }
 
@@ -1281,6 +1488,13 @@ bool launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int l
                                 BM, BK);
   CUtensorMap tq = make_tmap_2d(W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, (uint64_t)ldw * 2,
                                 BN, BK);
+  // Output map for the bulk-copy reduction's tile stores (32 rows x 32 bf16,
+  // 64-byte swizzle); other instantiations never read it.
+  const CUtensorMap tc =
+      (EPI == kEpiNone && MH == 1 && BN % 32 == 0)
+          ? make_tmap_2d(C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, (uint64_t)ldc * 2, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_64B)
+          : tq;
   const long tiles = (long)((M + BM * MH - 1) / (BM * MH)) * ((N + BN - 1) / BN);
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3((unsigned)(tiles * splits), 1, 1);
@@ -1296,7 +1510,7 @@ bool launch_cl(const void* A, const void* W, void* C, int M, int N, int K, int l
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, tq, reinterpret_cast<__nv_bfloat16*>(C),
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, tc, reinterpret_cast<__nv_bfloat16*>(C),
                                      ldc, M, N, K, splits, (float*)nullptr, (int*)nullptr, err,
                                      WQParams{}, GroupInfo{}, (int)BM, (int)BM, BN);
   if (e != cudaSuccess)
@@ -1366,7 +1580,8 @@ bool launch_pair(const void* A, const void* W, void* C, int M, int N, int K, int
   lc.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&lc, kernel, tp, tq, use_ext ? tc : tc_plain,
                                      reinterpret_cast<__nv_bfloat16*>(C), ldc, M, N, K,
-                                     use_ext ? -splits : splits, ws, counters, err, WQParams{}, GroupInfo{},
+                                     use_ext ? -splits : split_arg(splits), ws, counters, err,
+                                     WQParams{}, GroupInfo{},
                                      (int)BM, (int)BM, BN / 2);
   if (e != cudaSuccess)
     throw std::runtime_error(std::string("gemm_bf16_tc pair launch: ") + cudaGetErrorString(e));

@@ -61,6 +61,19 @@ _reg("VLLM_B200_SKIP_EXT", "optin", False, "plugin",
 _reg("VLLM_B200_GEMM", "kill", True, "kernels", "tcgen05 BF16 GEMM (0 = torch.matmul).")
 _reg("VLLM_B200_GEMM_SILU_EPILOGUE", "kill", True, "kernels",
      "Fuse SiLU*up into the gate_up GEMM epilogue.")
+# Read by the native library (std::getenv, once per process):
+_reg("VLLM_B200_ATTN_DECODE_TMA", "kill", True, "kernels",
+     "TMA-fed paged decode / spec-verify attention (0 = the cp.async kernel).")
+_reg("VLLM_B200_ATTN_PREFILL_TC", "kill", True, "kernels",
+     "tcgen05 prefill attention (0 = the mma.sync kernel).")
+_reg("VLLM_B200_GEMM_EXT_REDUCE", "optin", False, "kernels",
+     "Split-K GEMMs write fp32 partials to a [split][M][N] workspace and a reduction kernel "
+     "sums them (measured slower than the in-kernel reduction at decode sizes).")
+_reg("VLLM_B200_GEMM_SERIAL_SPLIT", "optin", False, "kernels",
+     "Split-K GEMMs: the last split to arrive sums each tile and the others exit early "
+     "(measured slower in decode-step chains than the shared reduction).")
+_reg("VLLM_B200_GEMM_TMA_BOX", "int", 0, "kernels",
+     "Rows per TMA box of the bf16 GEMM operands (0 = one box per tile; profiling aid).")
 _reg("VLLM_B200_RMSNORM", "kill", True, "kernels",
      "RMSNorm / fused add + RMSNorm kernels as vLLM's first IR-op provider.")
 _reg("VLLM_B200_ATTN", "kill", True, "kernels", "Paged attention kernels (0 = SDPA reference).")

@@ -1,17 +1,20 @@
-"""Decode-step driver for a per-kernel breakdown of the serving loop.
+"""Decode-step (or prefill-chunk) driver for a per-kernel breakdown of the serving loop.
 
 Builds the engine on random-init Llama-3.1-8B weights, prefills ``--requests``
 prompts of ``--prompt-len`` tokens and runs ``--decode-steps`` batched decode
 steps inside an NVTX range named ``decode`` (eager launches, so a profiler sees
-every kernel of the step as its own launch). Prints the decode milliseconds per
-step measured with CUDA events. Under a one-metric launch list:
+every kernel of the step as its own launch); every prefill chunk runs inside a
+range named ``prefill``. Prints the decode milliseconds per step measured with
+CUDA events. Under a one-metric launch list:
 
     ncu --nvtx --nvtx-include "decode/" --metrics gpu__time_duration.sum \\
         --clock-control none --csv --log-file launches.csv \\
         python -m vllm_sm70_b200.perf.decode_profile
 
 then ``python -m vllm_sm70_b200.perf.decode_profile --summarize launches.csv``
-groups the captured launches by kernel and prints each one's share.
+groups the captured launches by kernel and prints each one's share. With
+``--nvtx-include "prefill/"`` (and ``--summarize ... --per prefill-chunks``
+set to the number of chunks captured) the same list covers prefill chunks.
 """
 from __future__ import annotations
 
@@ -71,13 +74,20 @@ def main(argv=None):
               seed=0, enforce_eager=True)
     runner = llm.runner
     inner = runner.decode
+    inner_pf = runner.prefill
 
     def decode(n_rows, steps):
         torch.cuda.nvtx.range_push("decode")
         inner(n_rows, steps)
         torch.cuda.nvtx.range_pop()
 
+    def prefill(pieces):
+        torch.cuda.nvtx.range_push("prefill")
+        inner_pf(pieces)
+        torch.cuda.nvtx.range_pop()
+
     runner.decode = decode
+    runner.prefill = prefill
     g = torch.Generator().manual_seed(7)
     prompts = torch.randint(0, 128000, (R, P), generator=g)
     sp = SamplingParams(max_tokens=S + 1, temperature=0.0, ignore_eos=True)

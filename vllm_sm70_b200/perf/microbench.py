@@ -153,6 +153,112 @@ def bench_gemm_fp8(M, N, K, bn=0, iters=20, flush=False):
             "quant_ms": round(ms_q, 5), "bf16_gemm_ms": round(ms_bf16, 5), "peaks": pk["src"]}
 
 
+def bench_gemm_nvfp4(M, N, K, iters=20, flush=False):
+    """NVFP4 W4A4 GEMM (kind::mxf4nvf4, block-16 e4m3 scales in TMEM) on
+    pre-quantised activations, plus the activation quantiser, vs the bf16
+    tcgen05 GEMM of the same shape."""
+    from ..ops import linear, quant
+
+    w = torch.randn(N, K, device="cuda") * 0.02
+    lin = quant.make_linear("nvfp4", w)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    xq, sf, rs = quant.quant_nvfp4_act(x)
+    atoms = lin.sf_atoms()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ms = time_fn(lambda: torch.ops._b200_C.gemm_nvfp4_out(out, xq, sf, rs, lin.raw, atoms,
+                                                          lin.out_scale, -1), iters, flush=flush)
+    ms_q = time_fn(lambda: torch.ops._b200_C.quant_nvfp4_act(x, xq, sf, rs), iters, flush=flush)
+    wb = w.to(torch.bfloat16)
+    ms_bf16 = time_fn(lambda: linear.gemm(x, wb, out=out), iters, flush=flush)
+    pk = peaks()
+    flops = 2.0 * M * N * K
+    byts = M * K / 2 + N * K / 2 + 2.0 * M * N
+    return {"kernel": "gemm_nvfp4_w4a4", "M": M, "N": N, "K": K, "ms": round(ms, 5),
+            "tflops": round(flops / ms / 1e9, 1), "gbs": round(byts / ms / 1e6, 1),
+            "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3),
+            "quant_ms": round(ms_q, 5), "bf16_gemm_ms": round(ms_bf16, 5), "peaks": pk["src"]}
+
+
+def bench_gdn_chunk(nseq=4, length=8192, hk=16, hv=32, d=128, iters=5, serial=True):
+    """Gated-DeltaNet prefill: the 64-token chunked WY/UT kernel vs the
+    token-serial recurrence on the same inputs (Qwen3-Next head shape)."""
+    from ..ops import gdn
+
+    T = nseq * length
+    cu = torch.arange(nseq + 1, device="cuda", dtype=torch.int32) * length
+    slots = torch.arange(nseq, device="cuda", dtype=torch.int32)
+    q = torch.randn(T, hk * d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(T, hk * d, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(T, hv * d, device="cuda", dtype=torch.bfloat16)
+    a = torch.randn(T, hv, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(T, hv, device="cuda", dtype=torch.bfloat16)
+    A_log = torch.randn(hv, device="cuda") * 0.5
+    dt = torch.randn(hv, device="cuda") * 0.5
+    st = torch.zeros(nseq, hv, d, d, device="cuda")
+    out = torch.empty(T, hv * d, device="cuda", dtype=torch.bfloat16)
+
+    def run(chunked):
+        gdn.gdn_recurrent(q, k, v, a, b, A_log, dt, st, cu, slots, hk, hv, True, out, True,
+                          chunked)
+
+    ms = time_fn(lambda: run(True), iters)
+    r = {"kernel": "gdn_chunk", "nseq": nseq, "len": length, "hk": hk, "hv": hv, "d": d,
+         "ms": round(ms, 4)}
+    if serial:
+        r["serial_ms"] = round(time_fn(lambda: run(False), max(1, iters // 2)), 4)
+    return r
+
+
+def bench_moe(T=16384, E=128, k=8, H=2048, I=768, fmt="fp8", iters=10):
+    """One MoE expert layer (top-k routing, permutation, grouped expert GEMMs,
+    SiLU*up, weighted combine) on Qwen3-30B-A3B shapes, random routing."""
+    from ..ops import moe
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w13 = torch.randn(E, 2 * I, H, device="cuda", generator=g) * 0.05
+    w2 = torch.randn(E, H, I, device="cuda", generator=g) * 0.05
+    ew = moe.ExpertWeights.from_dense(fmt, w13, w2)
+    del w13, w2
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w, ids = moe.topk(torch.randn(T, E, device="cuda"), k)
+    ws = moe.MoEWorkspace(T, k, E, H, I, "cuda")
+    ms = time_fn(lambda: moe.experts_forward(x, w, ids, ew, ws), iters, flush=True)
+    flops = 2.0 * T * k * (2 * I * H + H * I)
+    return {"kernel": "moe_experts", "fmt": fmt, "T": T, "E": E, "k": k, "H": H, "I": I,
+            "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1)}
+
+
+def bench_rope_kv(T=16384, hq=32, hkv=8, d=128, bs=16, iters=20):
+    """Fused RoPE + paged KV write on a [T, (hq + 2 hkv) d] QKV tensor."""
+    from ..ops import attention as A
+
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda", dtype=torch.bfloat16)
+    pos = torch.arange(T, device="cuda") % 4096
+    nb = (T + bs - 1) // bs
+    slots = torch.arange(T, device="cuda")
+    cs = A.rope_cos_sin(d, 4096, 5e5, device="cuda")
+    kc = torch.empty(nb, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
+    vc = torch.empty_like(kc)
+    ms = time_fn(lambda: A.rope_kv_write(qkv, pos, cs, kc, vc, slots, hq, hkv), iters, flush=True)
+    byts = T * (hq + 2 * hkv) * d * 2 + T * (hq + hkv) * d * 2 + 2 * T * hkv * d * 2
+    pk = peaks()
+    return {"kernel": "rope_kv", "T": T, "ms": round(ms, 5), "gbs": round(byts / ms / 1e6, 1),
+            "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}
+
+
+def bench_rms_norm(T=16384, H=4096, iters=20):
+    """Fused residual add + RMSNorm (in place) on [T, H] bf16 rows."""
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(H, device="cuda", dtype=torch.bfloat16)
+    ms = time_fn(lambda: torch.ops._b200_C.fused_add_rms_norm(x, r, w, 1e-5), iters, flush=True)
+    byts = 4.0 * T * H * 2
+    pk = peaks()
+    return {"kernel": "fused_add_rms_norm", "T": T, "H": H, "ms": round(ms, 5),
+            "gbs": round(byts / ms / 1e6, 1), "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 3),
+            "peaks": pk["src"]}
+
+
 def bench_decode_attn(batch=256, ctx=1152, hq=32, hkv=8, d=128, bs=16, splits=1, iters=20,
                       seq_blocks=False):
     from ..ops import attention as A
@@ -202,8 +308,9 @@ def bench_prefill_attn(seqs=16, length=1024, hq=32, hkv=8, d=128, bs=16, iters=1
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "gemm-cublas", "gemm-fp8", "decode-attn",
-                                     "prefill-attn", "all"])
+    ap.add_argument("case", choices=["gemm", "gemm-cublas", "gemm-fp8", "gemm-nvfp4",
+                                     "decode-attn", "prefill-attn", "gdn-chunk", "rope-kv",
+                                     "rms-norm", "moe", "all"])
     ap.add_argument("--M", type=int, default=256)
     ap.add_argument("--N", type=int, default=6144)
     ap.add_argument("--K", type=int, default=4096)
@@ -223,6 +330,7 @@ def main(argv=None):
     ap.add_argument("--d", type=int, default=128, help="attention: head dim")
     ap.add_argument("--hq", type=int, default=32, help="attention: query heads")
     ap.add_argument("--hkv", type=int, default=8, help="attention: KV heads")
+    ap.add_argument("--fmt", default="fp8", help="moe: expert weight format")
     ap.add_argument("--seq-blocks", action="store_true",
                     help="decode-attn: sequential block table (default: random permutation)")
     args = ap.parse_args(argv)
@@ -247,6 +355,17 @@ def main(argv=None):
     elif args.case == "gemm-fp8":
         out.append(bench_gemm_fp8(args.M, args.N, args.K, max(0, args.cfg), args.iters,
                                   args.flush))
+    elif args.case == "gemm-nvfp4":
+        out.append(bench_gemm_nvfp4(args.M, args.N, args.K, args.iters, args.flush))
+    elif args.case == "gdn-chunk":
+        out.append(bench_gdn_chunk(args.seqs, args.len, iters=args.iters,
+                                   serial=not args.no_cublas))
+    elif args.case == "rope-kv":
+        out.append(bench_rope_kv(args.M, args.hq, args.hkv, args.d, args.block, args.iters))
+    elif args.case == "moe":
+        out.append(bench_moe(args.M, fmt=args.fmt, iters=args.iters))
+    elif args.case == "rms-norm":
+        out.append(bench_rms_norm(args.M, args.K, args.iters))
     elif args.case == "gemm-cublas":
         a = torch.randn(args.M, args.K, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(args.N, args.K, device="cuda", dtype=torch.bfloat16)
