@@ -243,3 +243,73 @@ def test_fused_gemm_ar_rmsnorm_bitwise(b200_ops):
     if world < 2:
         pytest.skip("needs 2+ GPUs")
     _mp.run(_fused_gemm_body, world, timeout=600)
+
+
+def _xchg_body(rank, world):
+    """Sampler exchange over peer memory vs the NCCL all-gather + merge:
+    greedy top-1 ids equal (ties across ranks, NaN rows, repeated calls
+    alternating receive halves, CUDA-graph replays) and the candidate gather
+    equals the rank-order concatenation."""
+    import torch.distributed as dist
+
+    from vllm_sm70_b200.ops import sampling
+    from vllm_sm70_b200.parallel import symm, state
+
+    ps = _setup(rank, world)
+    dev = ps.device
+    x = symm.TpExchange(ps, 512, 64)
+    for it, rows in enumerate([1, 37, 256, 512, 5, 256, 129]):
+        g = torch.Generator(device=dev).manual_seed(900 + it)
+        vals_all = torch.randn(world, rows, device=dev, generator=g)
+        ids_all = torch.randint(0, 1 << 20, (world, rows), device=dev, generator=g,
+                                dtype=torch.int32)
+        if rows > 4:
+            vals_all[:, 2] = 1.5  # tie across every rank -> lowest id
+            vals_all[world - 1, 3] = float("nan")  # NaN wins
+        got = x.top1(vals_all[rank].contiguous(), ids_all[rank].contiguous())
+        ref = sampling.merge_rank_top1(vals_all, ids_all.long())
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), f"top1 rows={rows}"
+        C = 64 if rows <= 256 else 16
+        v_all = torch.randn(world, rows, C, device=dev, generator=g)
+        i_all = torch.randint(0, 1 << 20, (world, rows, C), device=dev, generator=g,
+                              dtype=torch.int32)
+        ov, oi = x.gather(v_all[rank].contiguous(), i_all[rank].contiguous())
+        torch.cuda.synchronize()
+        assert torch.equal(ov, torch.cat(list(v_all), dim=1)), f"gather v rows={rows}"
+        assert torch.equal(oi, torch.cat(list(i_all), dim=1)), f"gather i rows={rows}"
+        assert int(torch.ops._b200_C.read_status(dev.index, True)) == 0
+    # CUDA graph: the device-side epoch advances per replay.
+    rows = 64
+    vin = torch.empty(rows, device=dev)
+    iin = torch.empty(rows, device=dev, dtype=torch.int32)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        x.top1(vin, iin)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = x.top1(vin, iin)
+    for it in range(5):
+        g = torch.Generator(device=dev).manual_seed(1900 + it)
+        vals_all = torch.randn(world, rows, device=dev, generator=g)
+        ids_all = torch.randint(0, 1 << 20, (world, rows), device=dev, generator=g,
+                                dtype=torch.int32)
+        vin.copy_(vals_all[rank])
+        iin.copy_(ids_all[rank])
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, sampling.merge_rank_top1(vals_all, ids_all.long())), it
+    del graph
+    torch.cuda.synchronize()
+    dist.barrier()
+    state.shutdown()
+
+
+def test_sampler_exchange_matches_nccl(b200_ops):
+    world = _world()
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    _mp.run(_xchg_body, world, timeout=600)

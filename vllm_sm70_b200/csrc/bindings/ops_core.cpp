@@ -195,6 +195,30 @@ void moe_topk(at::Tensor& w, at::Tensor& ids, const at::Tensor& logits, int64_t 
                   cur_stream());
 }
 
+// Fused router: fp32 logits of x [T, H] against wr [E, H] and the top-k in
+// one kernel. logits [>= T, E] fp32 scratch; tile_ctr [>= ceil(T/8)] int32,
+// zero before the first call (the kernel leaves it zero).
+void moe_router(at::Tensor& w, at::Tensor& ids, const at::Tensor& x, const at::Tensor& wr,
+                int64_t k, bool use_sigmoid, bool renorm, const c10::optional<at::Tensor>& bias,
+                at::Tensor& logits, at::Tensor& tile_ctr) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(wr);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && wr.dim() == 2 && wr.is_contiguous() &&
+              wr.size(1) == x.size(1), "moe_router: x [T, H], wr [E, H]");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
+              (reinterpret_cast<uintptr_t>(wr.data_ptr()) & 15) == 0, "moe_router: 16B-aligned rows");
+  const int64_t T = x.size(0), E = wr.size(0);
+  TORCH_CHECK(w.scalar_type() == at::kFloat && ids.scalar_type() == at::kInt &&
+              w.numel() >= T * k && ids.numel() >= T * k, "moe_router: outputs");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.numel() >= T * E, "moe_router: logits scratch");
+  TORCH_CHECK(tile_ctr.scalar_type() == at::kInt && tile_ctr.numel() >= (T + 7) / 8,
+              "moe_router: tile counters");
+  c10::cuda::CUDAGuard g(x.device());
+  moe_router_launch(x.data_ptr(), (int)x.stride(0), wr.data_ptr(), (int)T, (int)E, (int)x.size(1),
+                    (int)k, use_sigmoid, renorm, bias ? bias->data_ptr<float>() : nullptr,
+                    logits.data_ptr<float>(), tile_ctr.data_ptr<int>(), w.data_ptr<float>(),
+                    ids.data_ptr<int>(), cur_stream());
+}
+
 // Expert-sort the (token, slot) pairs of experts [e_base, e_base + E).
 void moe_permute(const at::Tensor& ids, int64_t E, int64_t e_base, const c10::optional<at::Tensor>& x,
                  const c10::optional<at::Tensor>& x_perm, at::Tensor& counts, at::Tensor& offsets,
@@ -748,6 +772,62 @@ void ep_finish(const std::vector<int64_t>& bufs, int64_t rank, int64_t E_local, 
                    shared ? shared->data_ptr() : nullptr, out.data_ptr(), cur_stream());
 }
 
+// Vocab-parallel sampler exchange over peer memory. bufs = [recv, pad] per
+// rank. mode 0: src0 = values [rows] fp32, src1 = ids [rows] int32 ->
+// out0 = merged ids [rows] int32. mode 1: src0 / src1 = values / ids
+// [rows, C] -> out0 = values [rows, W*C] fp32, out1 = ids [rows, W*C] int32.
+void tp_exchange(const std::vector<int64_t>& bufs, int64_t rank, int64_t cap, int64_t mode,
+                 const at::Tensor& src0, const at::Tensor& src1, at::Tensor& out0,
+                 const c10::optional<at::Tensor>& out1, int64_t timeout_ms) {
+  const int W = (int)bufs.size() / 2;
+  TORCH_CHECK((int)bufs.size() == 2 * W && (W == 2 || W == 4 || W == 8),
+              "tp_exchange: [recv, pad] per rank, 2, 4 or 8 ranks");
+  TORCH_CHECK(rank >= 0 && rank < W, "tp_exchange: bad rank");
+  CHECK_CUDA(src0); CHECK_CUDA(src1); CHECK_CUDA(out0);
+  TORCH_CHECK(src0.is_contiguous() && src1.is_contiguous() && out0.is_contiguous(),
+              "tp_exchange: contiguous tensors");
+  TORCH_CHECK(src0.scalar_type() == at::kFloat && src1.scalar_type() == at::kInt,
+              "tp_exchange: src0 fp32 values, src1 int32 ids");
+  TORCH_CHECK(src0.sizes() == src1.sizes(), "tp_exchange: values / ids shapes differ");
+  TpExchangeParams p{};
+  for (int q = 0; q < W; ++q) {
+    TORCH_CHECK(bufs[2 * q] % 16 == 0 && bufs[2 * q + 1] % 16 == 0, "tp_exchange: 16B alignment");
+    p.recv_peer[q] = reinterpret_cast<uint8_t*>(bufs[2 * q]);
+    p.pad_peer[q] = reinterpret_cast<uint32_t*>(bufs[2 * q + 1]);
+  }
+  p.recv_local = p.recv_peer[rank];
+  p.pad_local = p.pad_peer[rank];
+  p.rank = (int)rank;
+  p.world = W;
+  p.mode = (int)mode;
+  p.cap = cap;
+  p.src0 = src0.data_ptr();
+  p.n0 = src0.numel() * 4;
+  p.src1 = src1.data_ptr();
+  p.n1 = src1.numel() * 4;
+  if (mode == kTpXchgTop1) {
+    TORCH_CHECK(src0.dim() == 1 && out0.scalar_type() == at::kInt && out0.numel() == src0.numel(),
+                "tp_exchange top1: values / ids [rows], out int32 [rows]");
+    p.rows = (int)src0.numel();
+    p.C = 1;
+    p.out_ids = out0.data_ptr<int>();
+  } else {
+    TORCH_CHECK(mode == kTpXchgGather, "tp_exchange: mode 0 (top-1) or 1 (gather)");
+    TORCH_CHECK(src0.dim() == 2 && out1.has_value(), "tp_exchange gather: [rows, C] and two outputs");
+    p.rows = (int)src0.size(0);
+    p.C = (int)src0.size(1);
+    TORCH_CHECK(out0.scalar_type() == at::kFloat && out0.numel() == (int64_t)W * src0.numel() &&
+                out1->scalar_type() == at::kInt && out1->numel() == out0.numel() &&
+                out1->is_contiguous(), "tp_exchange gather: outputs [rows, W*C] fp32 / int32");
+    p.out_v = out0.data_ptr<float>();
+    p.out_i = out1->data_ptr<int>();
+  }
+  p.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  p.err = device_status_ptr(out0.get_device());
+  c10::cuda::CUDAGuard g(out0.device());
+  tp_exchange_launch(p, cur_stream());
+}
+
 // Row-parallel GEMM x @ lin_w^T into this rank's stage, fused in one kernel
 // with the all-reduce + residual add + RMSNorm. Returns false when the
 // shape / tile is not taken (nothing launched; the caller runs the unfused pair).
@@ -851,6 +931,8 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("dequant_weight(Tensor(a!) out, Tensor w_raw, int fmt, Tensor scales) -> ()");
   m.def("moe_topk(Tensor(a!) w, Tensor(b!) ids, Tensor logits, int k, bool use_sigmoid, bool renorm, "
         "Tensor? bias) -> ()");
+  m.def("moe_router(Tensor(a!) w, Tensor(b!) ids, Tensor x, Tensor wr, int k, bool use_sigmoid, "
+        "bool renorm, Tensor? bias, Tensor(c!) logits, Tensor(d!) tile_ctr) -> ()");
   m.def("moe_permute(Tensor ids, int E, int e_base, Tensor? x, Tensor(a!)? x_perm, Tensor(b!) counts, "
         "Tensor(c!) offsets, Tensor(d!) rank_scratch, Tensor(e!) pos, Tensor(f!) src_row, "
         "int align=1) -> ()");
@@ -896,6 +978,8 @@ TORCH_LIBRARY(_b200_C, m) {
         "Tensor(b!) idc, Tensor(c!) wc, Tensor(d!) row_src, Tensor(e!) n_rows) -> ()");
   m.def("ep_return(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, Tensor y, "
         "Tensor row_src, Tensor n_rows) -> ()");
+  m.def("tp_exchange(int[] bufs, int rank, int cap, int mode, Tensor src0, Tensor src1, "
+        "Tensor(a!) out0, Tensor(b!)? out1, int timeout_ms) -> ()");
   m.def("ep_finish(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, "
         "Tensor slot, Tensor? shared, Tensor(a!) out) -> ()");
   m.def("ar_rmsnorm(int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, int[] flag_ptrs, int rank, "
@@ -922,6 +1006,7 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("topk_candidates", &b200::topk_candidates);
   m.impl("sample_candidates", &b200::sample_candidates);
   m.impl("moe_topk", &b200::moe_topk);
+  m.impl("moe_router", &b200::moe_router);
   m.impl("moe_permute", &b200::moe_permute);
   m.impl("moe_combine", &b200::moe_combine);
   m.impl("gemm_grouped_out", &b200::gemm_grouped_out);
@@ -934,6 +1019,7 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("ep_receive", &b200::ep_receive);
   m.impl("ep_return", &b200::ep_return);
   m.impl("ep_finish", &b200::ep_finish);
+  m.impl("tp_exchange", &b200::tp_exchange);
   m.impl("gemm_fp8_out", &b200::gemm_fp8_out);
   m.impl("gemm_fp8_grouped_out", &b200::gemm_fp8_grouped_out);
   m.impl("dequant_weight", &b200::dequant_weight);

@@ -56,4 +56,28 @@ void ep_return_launch(const EpParams& p, const void* y, const int* row_src, cons
 void ep_finish_launch(const EpParams& p, const int* slot, int T, const void* shared, void* out,
                       cudaStream_t stream);
 
+// Vocab-parallel sampler exchange over peer memory (tp_exchange.cu). Buffers
+// per rank (symmetric): recv [2][W][cap] bytes, pad [W + 3] uint32. The
+// message is src0 (n0 bytes) followed by src1 (n1 bytes), 4-byte words.
+constexpr int kTpXchgTop1 = 0;    // src0 = values [rows] fp32, src1 = ids [rows] int32
+constexpr int kTpXchgGather = 1;  // src0 = values [rows, C] fp32, src1 = ids [rows, C] int32
+struct TpExchangeParams {
+  uint8_t* recv_peer[kMaxRanks];
+  uint32_t* pad_peer[kMaxRanks];
+  const uint8_t* recv_local;
+  uint32_t* pad_local;
+  int rank, world, mode, rows, C;
+  long long cap;
+  const void* src0;
+  long long n0;
+  const void* src1;
+  long long n1;
+  int* out_ids;  // kTpXchgTop1: [rows]
+  float* out_v;  // kTpXchgGather: [rows, W * C]
+  int* out_i;
+  unsigned long long timeout_ns;
+  unsigned int* err;
+};
+void tp_exchange_launch(const TpExchangeParams& p, cudaStream_t stream);
+
 }  // namespace b200

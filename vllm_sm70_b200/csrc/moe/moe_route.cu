@@ -1,6 +1,8 @@
 // MoE routing kernels: router top-k, deterministic token->expert permutation,
 // and the weighted combine.
 //
+//   moe_router    x [T, H] bf16, router weight [E, H] -> fp32 logits and the
+//                 top-k below in one kernel (small T: decode steps).
 //   moe_topk      logits [T, E] (bf16/fp32) -> softmax or sigmoid scores,
 //                 top-k (ties -> lower expert id, NaN -> 0), optional
 //                 renormalisation; weights fp32 [T, k], ids int32 [T, k].
@@ -23,6 +25,7 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 #include <stdexcept>
+#include <string>
 
 #include "moe/moe_api.h"
 
@@ -40,16 +43,15 @@ __device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloat16* p, size
 template <>
 __device__ __forceinline__ float ldf<float>(const float* p, size_t i) { return p[i]; }
 
-// One warp per token. Each lane scans E/32 experts; k rounds of warp argmax.
+// One warp selects one token's experts: softmax (max-subtracted) or sigmoid
+// scores, k rounds of warp argmax over the experts not yet taken (ties to the
+// lower id, NaN logits score 0, `bias` only shifts the selection key), then
+// the optional renormalisation; lane 0 writes the row.
 template <typename T>
-__global__ void topk_kernel(const T* __restrict__ logits, int ld, int Tn, int E, int k,
-                            bool use_sigmoid, bool renorm, const float* __restrict__ bias,
-                            float* __restrict__ w_out, int* __restrict__ id_out) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+__device__ void warp_topk(const T* __restrict__ row, int E, int k, bool use_sigmoid, bool renorm,
+                          const float* __restrict__ bias, float* __restrict__ w_row,
+                          int* __restrict__ id_row) {
   const int lane = threadIdx.x % 32;
-  if (warp >= Tn) return;
-  const T* row = logits + (size_t)warp * ld;
-  // softmax denominator (max-subtracted) or sigmoid scores
   float mx = -INFINITY;
   for (int e = lane; e < E; e += 32) {
     float v = ldf(row, e);
@@ -104,10 +106,120 @@ __global__ void topk_kernel(const T* __restrict__ logits, int ld, int Tn, int E,
   if (lane == 0) {
     const float inv = (renorm && taken_sum > 0.f) ? 1.f / taken_sum : 1.f;
     for (int j = 0; j < k; ++j) {
-      w_out[(size_t)warp * k + j] = sel_w[j] * inv;
-      id_out[(size_t)warp * k + j] = sel_id[j];
+      w_row[j] = sel_w[j] * inv;
+      id_row[j] = sel_id[j];
     }
   }
+}
+
+// One warp per token.
+template <typename T>
+__global__ void topk_kernel(const T* __restrict__ logits, int ld, int Tn, int E, int k,
+                            bool use_sigmoid, bool renorm, const float* __restrict__ bias,
+                            float* __restrict__ w_out, int* __restrict__ id_out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  if (warp >= Tn) return;
+  warp_topk(logits + (size_t)warp * ld, E, k, use_sigmoid, renorm, bias,
+            w_out + (size_t)warp * k, id_out + (size_t)warp * k);
+}
+
+// Fused router for small token counts: logits = x @ wr^T in fp32 and the
+// top-k selection in one kernel. Grid (token tiles of kRtTok, expert chunks
+// of 32); 8 warps, warp w computes experts chunk * 32 + 4w .. + 3 for the
+// tile's tokens (x tile staged in shared memory, each lane 8 columns of H
+// per step, fixed summation order), a 31-shuffle reduce-scatter leaves
+// (token, expert) = lane's sum in that lane. Every CTA stores its fp32
+// logits; the last CTA of a token tile (arrival counter, re-armed by that
+// CTA) runs warp_topk for the tile's tokens on them. Deterministic: the
+// logits do not depend on which CTA arrives last.
+constexpr int kRtTok = 8;
+
+__global__ void __launch_bounds__(256) router_kernel(
+    const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ wr, int Tn,
+    int E, int H, int k, bool use_sigmoid, bool renorm, const float* __restrict__ bias,
+    float* __restrict__ logits, int* __restrict__ tile_ctr, float* __restrict__ w_out,
+    int* __restrict__ id_out) {
+  extern __shared__ uint4 xs4[];  // [kRtTok][H / 8]
+  __shared__ int s_last;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int t0 = blockIdx.x * kRtTok;
+  const int nt = min(kRtTok, Tn - t0);
+  const int hv = H / 8;
+  for (int i = threadIdx.x; i < kRtTok * hv; i += blockDim.x) {
+    const int t = i / hv, c = i - t * hv;
+    xs4[i] = t < nt ? *reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * ldx + c * 8)
+                    : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int e0 = blockIdx.y * 32 + warp * 4;
+  float acc[kRtTok * 4];
+#pragma unroll
+  for (int i = 0; i < kRtTok * 4; ++i) acc[i] = 0.f;
+  for (int c = lane; c < hv; c += 32) {
+    float wf[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + j;
+      const uint4 u = e < E ? *reinterpret_cast<const uint4*>(wr + (size_t)e * H + c * 8)
+                            : make_uint4(0, 0, 0, 0);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
+        wf[j][2 * q] = f.x;
+        wf[j][2 * q + 1] = f.y;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kRtTok; ++t) {
+      const uint4 u = xs4[t * hv + c];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+      float xf[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
+        xf[2 * q] = f.x;
+        xf[2 * q + 1] = f.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float a = acc[t * 4 + j];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) a = fmaf(xf[q], wf[j][q], a);
+        acc[t * 4 + j] = a;
+      }
+    }
+  }
+  // Reduce-scatter over the warp: afterwards lane l holds the sum of acc[l].
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = upper ? acc[i] : acc[i + o];
+      const float keep = upper ? acc[i + o] : acc[i];
+      acc[i] = keep + __shfl_xor_sync(0xffffffff, send, o);
+    }
+  }
+  {
+    const int t = lane / 4, e = e0 + (lane & 3);
+    if (t < nt && e < E) logits[(size_t)(t0 + t) * E + e] = acc[0];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(&tile_ctr[blockIdx.x], 1);
+    s_last = old == (int)gridDim.y - 1;
+    if (s_last) tile_ctr[blockIdx.x] = 0;  // re-arm for the next launch
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (!s_last) return;
+  __threadfence();
+  if (warp < nt)
+    warp_topk(logits + (size_t)(t0 + warp) * E, E, k, use_sigmoid, renorm, bias,
+              w_out + (size_t)(t0 + warp) * k, id_out + (size_t)(t0 + warp) * k);
 }
 
 // One CTA per expert: counts the (token, slot) pairs routed to it and their
@@ -216,6 +328,37 @@ void moe_topk_launch(const void* logits, bool bf16, int ld, int T, int E, int k,
   else
     topk_kernel<float><<<blocks, threads, 0, stream>>>((const float*)logits, ld, T, E, k, sigmoid,
                                                        renorm, bias, w, ids);
+}
+
+void moe_router_launch(const void* x, int ldx, const void* wr, int T, int E, int H, int k,
+                       bool sigmoid, bool renorm, const float* bias, float* logits,
+                       int* tile_ctr, float* w, int* ids, cudaStream_t stream) {
+  if (T <= 0) return;
+  if (k > kMaxK || k > E) throw std::runtime_error("moe_router: k must be <= 16 and <= E");
+  if (H % 8) throw std::runtime_error("moe_router: H must be a multiple of 8");
+  const size_t smem = (size_t)kRtTok * H * 2;
+  if (smem > 96 * 1024) throw std::runtime_error("moe_router: hidden size too large");
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)((T + kRtTok - 1) / kRtTok), (unsigned)((E + 31) / 32), 1);
+  lc.blockDim = dim3(256, 1, 1);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&lc, router_kernel, (const __nv_bfloat16*)x, ldx,
+                                     (const __nv_bfloat16*)wr, T, E, H, k, sigmoid, renorm, bias,
+                                     logits, tile_ctr, w, ids);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("moe_router: ") + cudaGetErrorString(e));
 }
 
 void moe_permute_launch(const int* ids, int T, int k, int E, int e_base, const void* x, int H,

@@ -206,6 +206,9 @@ class LLM:
 
             comm.set_fused_ar_rmsnorm(symm.FusedArRmsNorm(
                 ps, max(max_num_batched_tokens, max_num_seqs), self.cfg.hidden_size))
+            # Sampler rows: decode rows, or (1 + k) verify rows per sequence.
+            comm.set_tp_exchange(symm.TpExchange(ps, max_num_seqs * (1 + max(3, int(speculative_k))),
+                                                 64))
         self.spec_k = int(speculative_k)
         if self.spec_k > 0 and self.ep is not None:
             raise NotImplementedError("speculative decoding with the all-to-all EP layout")

@@ -74,6 +74,11 @@ _reg("VLLM_B200_GEMM_SERIAL_SPLIT", "optin", False, "kernels",
      "(measured slower in decode-step chains than the shared reduction).")
 _reg("VLLM_B200_GEMM_TMA_BOX", "int", 0, "kernels",
      "Rows per TMA box of the bf16 GEMM operands (0 = one box per tile; profiling aid).")
+_reg("VLLM_B200_FUSED_ROUTER", "kill", True, "kernels",
+     "MoE router logits (fp32) and top-k in one kernel for small batches (0 = router GEMM "
+     "+ top-k kernel).")
+_reg("VLLM_B200_FUSED_ROUTER_MAX_TOKENS", "int", 1024, "kernels",
+     "Largest token count routed by the fused router kernel.")
 _reg("VLLM_B200_RMSNORM", "kill", True, "kernels",
      "RMSNorm / fused add + RMSNorm kernels as vLLM's first IR-op provider.")
 _reg("VLLM_B200_ATTN", "kill", True, "kernels", "Paged attention kernels (0 = SDPA reference).")
@@ -103,6 +108,9 @@ _reg("VLLM_B200_FUSED_AR_RMSNORM", "kill", True, "comm",
 _reg("VLLM_B200_FUSED_GEMM_RS", "kill", True, "comm", "Fused GEMM -> reduce-scatter.")
 _reg("VLLM_B200_FUSED_AG_GEMM", "kill", True, "comm", "Fused all-gather -> GEMM.")
 _reg("VLLM_B200_FUSED_EP_A2A", "kill", True, "comm", "Fused EP dispatch / combine.")
+_reg("VLLM_B200_FUSED_SAMPLER_XCHG", "kill", True, "comm",
+     "Vocab-parallel sampling at TP > 1: exchange the greedy (value, id) pairs / top-k "
+     "candidates over NVLink peer memory in one kernel (0 = NCCL all-gather + merge).")
 _reg("VLLM_B200_NVLS", "optin", False, "comm", "Use NVLS multimem reductions where supported.")
 _reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
      "Bound (ms) for every device-side flag wait in fused collectives.")

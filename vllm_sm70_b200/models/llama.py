@@ -473,8 +473,7 @@ class LlamaModel:
             lg = penalize(lg.float(), self.vocab_start).contiguous()
         v, i = ops.sampling.topk_candidates(lg, C, self.vocab_start)
         if self.ps.tp_size > 1:
-            v = pstate.tp_all_gather(v, dim=1)
-            i = pstate.tp_all_gather(i, dim=1)
+            v, i = comm.gather_candidates(v, i)
         return ops.sampling.sample_candidates(v, i, temperature, top_k, top_p, seeds, 0)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:

@@ -156,16 +156,11 @@ class Qwen3MoeModel(LlamaModel):
             self.ep_a2a.reserve(max_tokens, self.cfg.hidden_size)
 
     def mlp(self, li, L, x, out):
-        from .. import ops
-
         cfg = self.cfg
         T = x.shape[0]
-        logits = ops.gemm(x, L["router"]) if x.is_cuda else (x.float() @ L["router"].float().t())
         ws = self._ws(T) if x.is_cuda else None
-        w = ws.w[:T] if ws else None
-        ids = ws.ids[:T] if ws else None
-        w, ids = moe_ops.topk(logits, cfg.top_k, use_sigmoid=self.router_sigmoid,
-                              renorm=cfg.norm_topk_prob, w=w, ids=ids)
+        w, ids = moe_ops.route(x, L["router"], cfg.top_k, use_sigmoid=self.router_sigmoid,
+                               renorm=cfg.norm_topk_prob, ws=ws)
         shared = None
         if "shared_gate_up" in L:
             sh = L["shared_down"].forward(L["shared_gate_up"].forward(x))

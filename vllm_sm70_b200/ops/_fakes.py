@@ -38,6 +38,7 @@ NO_FAKE = {
     "ep_receive": "expert-parallel exchange over peer pointers (eager only)",
     "ep_return": "expert-parallel exchange over peer pointers (eager only)",
     "ep_finish": "expert-parallel exchange over peer pointers (eager only)",
+    "tp_exchange": "peer-memory collective (raw pointer lists)",
 }
 
 _done = False

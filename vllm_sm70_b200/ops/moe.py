@@ -21,7 +21,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .. import _ext
+from .. import _ext, envs
 from ..utils import launch_count
 from . import linear as _lin
 from . import quant as _q
@@ -58,6 +58,39 @@ def topk(logits: torch.Tensor, k: int, use_sigmoid: bool = False, renorm: bool =
         w.copy_(ww)
         ids.copy_(ii)
     return w, ids
+
+
+def router_ref(x: torch.Tensor, wr: torch.Tensor, k: int, use_sigmoid: bool = False,
+               renorm: bool = True):
+    """fp32 router logits and the top-k selection (oracle of :func:`route`)."""
+    return topk_ref(x.float() @ wr.float().t(), k, use_sigmoid, renorm)
+
+
+def route(x: torch.Tensor, wr: torch.Tensor, k: int, use_sigmoid: bool = False,
+          renorm: bool = True, ws: "MoEWorkspace | None" = None):
+    """Router logits ``x @ wr^T`` and the top-k experts per token: (weights
+    fp32 [T, k], ids int32 [T, k]). Up to ``VLLM_B200_FUSED_ROUTER_MAX_TOKENS``
+    tokens (decode steps) one fused kernel computes fp32 logits and selects;
+    larger batches run the tcgen05 GEMM (bf16 logits) and the top-k kernel.
+    Reference parity: the fused router (``sm70/csrc/router/flint_router.cuh:
+    1-186``)."""
+    T = x.shape[0]
+    w = ws.w[:T] if ws is not None else None
+    ids = ws.ids[:T] if ws is not None else None
+    if not x.is_cuda:
+        ww, ii = router_ref(x, wr, k, use_sigmoid, renorm)
+        return ww, ii
+    if (ws is not None and envs.get("VLLM_B200_FUSED_ROUTER")
+            and 0 < T <= envs.get("VLLM_B200_FUSED_ROUTER_MAX_TOKENS") and T <= ws.max_tokens
+            and x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.shape[1] * 16 <= 96 * 1024):
+        _ext.require()
+        lg, ctr = ws.router_buffers(wr.shape[0])
+        torch.ops._b200_C.moe_router(w, ids, x, wr.contiguous(), k, use_sigmoid, renorm, None,
+                                     lg, ctr)
+        launch_count.add(1)
+        return w, ids
+    logits = _lin.gemm(x, wr)
+    return topk(logits, k, use_sigmoid=use_sigmoid, renorm=renorm, w=w, ids=ids)
 
 
 @dataclass
@@ -149,6 +182,15 @@ class MoEWorkspace:
         self.E_local = E_local
         self._fp8 = None
         self._fp4 = None
+
+    def router_buffers(self, E: int):
+        """fp32 logits scratch [max_tokens, E] and the per-tile arrival
+        counters of the fused router (zero; the kernel leaves them zero)."""
+        if getattr(self, "_rt", None) is None or self._rt[0].shape[1] != E:
+            dev = self.w.device
+            self._rt = (torch.empty(self.max_tokens, E, dtype=torch.float32, device=dev),
+                        torch.zeros((self.max_tokens + 7) // 8, dtype=torch.int32, device=dev))
+        return self._rt
 
     def nvfp4_buffers(self):
         """Padded-permutation buffers for the W4A4 grouped GEMMs (every expert's

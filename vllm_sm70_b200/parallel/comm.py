@@ -20,7 +20,20 @@ import torch.distributed as dist
 from .. import envs, ops
 from . import state as pstate
 
-_fused = {"ar_rmsnorm": None}
+_fused = {"ar_rmsnorm": None, "tp_exchange": None}
+
+
+def set_tp_exchange(impl) -> None:
+    """Install the sampler exchange over peer memory (a
+    ``parallel.symm.TpExchange`` or None)."""
+    _fused["tp_exchange"] = impl
+
+
+def tp_exchange():
+    impl = _fused["tp_exchange"]
+    if impl is None or not envs.get("VLLM_B200_FUSED_SAMPLER_XCHG"):
+        return None
+    return impl
 
 
 def set_fused_ar_rmsnorm(impl) -> None:
@@ -99,14 +112,38 @@ def linear_all_reduce_add_rms_norm(lin, x: torch.Tensor, residual: torch.Tensor,
 
 def greedy_merge(vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
     """Gather per-rank (max value, id) pairs and pick the global top-1 in rank
-    order with the shared tie rule. Reference parity: F12 greedy
-    (``sm70/vllm_sm70/sample_greedy.py:293-328``)."""
+    order with the shared tie rule: one peer-memory kernel when the sampler
+    exchange is installed (rows within its capacity), else an NCCL all-gather
+    and the merge kernel. Reference parity: F12 greedy
+    (``sm70/vllm_sm70/sample_greedy.py:293-328``) and the P2P top-1 exchange
+    (``sm70/csrc/custom_ar/top1_custom_ar.cu:52-101``)."""
     st = pstate.get()
     if st.tp_size == 1:
         return ids
+    impl = tp_exchange()
+    if impl is not None and ids.is_cuda:
+        out = impl.top1(vals, ids)
+        if out is not None:
+            return out
     rows = ids.shape[0]
     packed = torch.stack([vals.float(), ids.float()], 0)  # ids < 2^24 are exact in fp32
     allp = torch.empty(st.tp_size * 2, rows, dtype=torch.float32, device=ids.device)
     dist.all_gather_into_tensor(allp, packed.contiguous(), group=st.tp_group)
     allp = allp.view(st.tp_size, 2, rows)
     return ops.sampling.merge_rank_top1(allp[:, 0], allp[:, 1].to(torch.int64))
+
+
+def gather_candidates(v: torch.Tensor, i: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The ranks' per-row candidate lists ``[rows, C]`` concatenated in rank
+    order along the candidate dimension: one peer-memory kernel when the
+    sampler exchange is installed, else two NCCL all-gathers. Reference
+    parity: the candidate gather (``sm70/vllm_sm70/sample.py:308-309``)."""
+    st = pstate.get()
+    if st.tp_size == 1:
+        return v, i
+    impl = tp_exchange()
+    if impl is not None and v.is_cuda:
+        r = impl.gather(v, i)
+        if r is not None:
+            return r
+    return pstate.tp_all_gather(v, dim=1), pstate.tp_all_gather(i, dim=1)

@@ -120,3 +120,62 @@ class FusedArRmsNorm:
         launch_count.add(1)
         self.calls += 1
         return self.out_view(T), rv
+
+
+class TpExchange:
+    """Symmetric buffers of the vocab-parallel sampler exchange
+    (``_b200_C::tp_exchange``): per rank a receive buffer of two halves x W
+    slots of ``cap`` bytes and a signal pad. One kernel stores this rank's
+    (value, id) pairs or top-C candidate lists into every rank's slot and
+    merges (greedy) or concatenates (candidates) in rank order on every rank.
+    ``rows_max`` bounds the rows per call (larger calls use NCCL)."""
+
+    def __init__(self, ps, rows_max: int, cands: int):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        assert ps.tp_size in (2, 4, 8), ps.tp_size
+        self.ps = ps
+        self.rows_max = rows_max
+        self.cands = cands
+        self.cap = ((rows_max * max(1, cands) * 8 + 15) // 16) * 16
+        W = ps.tp_size
+        dev = ps.device
+        self.recv = symm_mem.empty(2 * W * self.cap, dtype=torch.uint8, device=dev)
+        hr = symm_mem.rendezvous(self.recv, ps.tp_group)
+        self.pad = symm_mem.empty(16, dtype=torch.int32, device=dev)
+        hp = symm_mem.rendezvous(self.pad, ps.tp_group)
+        self.pad.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+        self.bufs = []
+        for q in range(W):
+            self.bufs += [int(hr.buffer_ptrs[q]), int(hp.buffer_ptrs[q])]
+        self._handles = (hr, hp)
+        self.timeout_ms = int(envs.get("VLLM_B200_COMM_TIMEOUT_MS"))
+
+    def top1(self, vals: torch.Tensor, ids: torch.Tensor) -> torch.Tensor | None:
+        """Global greedy ids [rows] int32 from this rank's (value, id) pairs."""
+        rows = ids.shape[0]
+        if rows > self.rows_max or rows * 8 > self.cap:
+            return None
+        out = torch.empty(rows, dtype=torch.int32, device=ids.device)
+        torch.ops._b200_C.tp_exchange(self.bufs, self.ps.tp_rank, self.cap, 0,
+                                      vals.float().contiguous(), ids.int().contiguous(), out,
+                                      None, self.timeout_ms)
+        launch_count.add(1)
+        return out
+
+    def gather(self, v: torch.Tensor, i: torch.Tensor):
+        """(values [rows, W*C] fp32, ids [rows, W*C] int32): the ranks'
+        candidate lists [rows, C] concatenated in rank order."""
+        rows, C = v.shape
+        if rows * C * 8 > self.cap:
+            return None
+        W = self.ps.tp_size
+        ov = torch.empty(rows, W * C, dtype=torch.float32, device=v.device)
+        oi = torch.empty(rows, W * C, dtype=torch.int32, device=v.device)
+        torch.ops._b200_C.tp_exchange(self.bufs, self.ps.tp_rank, self.cap, 1,
+                                      v.float().contiguous(), i.int().contiguous(), ov, oi,
+                                      self.timeout_ms)
+        launch_count.add(1)
+        return ov, oi
