@@ -127,10 +127,10 @@ _reg("VLLM_B200_FUSED_GEMM_AR", "kill", True, "comm",
      "residual + RMSNorm as one kernel (tcgen05 tiles, then the collective over NVLink peer "
      "memory) instead of a GEMM followed by the collective kernel, for token counts of at "
      "least VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS.")
-_reg("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS", "int", 1024, "comm",
+_reg("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS", "int", 1, "comm",
      "Smallest token count that takes the fused GEMM + all-reduce kernel (measured at TP2 on "
-     "Llama-3.1-8B shapes: faster for 16384-token prefill chunks, slower than the vendor GEMM + "
-     "collective kernel at 256-row decode steps).")
+     "Llama-3.1-8B shapes with every GEMM on the tcgen05 kernels: the fused kernel is as fast or "
+     "faster at 256-row decode steps and 16384-token prefill chunks).")
 _reg("VLLM_B200_PREFIX_CACHING", "optin", False, "runtime",
      "Reuse the KV of full prompt blocks across requests with the same token prefix "
      "(LLM(enable_prefix_caching=...) overrides).")
