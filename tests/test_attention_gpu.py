@@ -59,6 +59,23 @@ def test_prefill_and_chunked(b200_ops, d, hq, hkv, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
+@pytest.mark.parametrize("d,hq,hkv,bs", [(128, 32, 8, 16), (256, 16, 2, 16), (256, 16, 2, 64),
+                                         (256, 16, 2, 128)])
+def test_prefill_long_tcgen05(b200_ops, d, hq, hkv, bs, rel_err):
+    """Multi-tile causal prefill and chunked prefill through the tcgen05
+    kernel (head_dim 256: 64-key tiles; block size 128 exceeds its tile and
+    takes the mma.sync kernel), against the fp32 oracle."""
+    lens_q = [700, 300, 129]
+    lens_ctx = [700, 900, 129]
+    q, kc, vc, bt, sl, cu = _case(lens_q, lens_ctx, hq, hkv, d, bs, seed=12)
+    out = torch.empty_like(q)
+    A.paged_attention(out, q, kc, vc, bt, sl, cu, max(lens_q), 1 / math.sqrt(d))
+    ref = A.paged_attention_ref(q, kc, vc, bt, sl, cu, 1 / math.sqrt(d))
+    assert torch.isfinite(out.float()).all()
+    assert rel_err(out, ref) < 2e-2
+    assert int(torch.ops._b200_C.read_status(0, True)) == 0
+
+
 @pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (256, 16, 2)])
 def test_spec_verify_rows(b200_ops, d, hq, hkv, rel_err):
     # 4 query tokens per request (k=3 draft + 1) through the decode variant
@@ -101,14 +118,15 @@ def test_decode_interleaved_cache(b200_ops, bs, rel_err):
     assert rel_err(out, ref) < 2e-2
 
 
-@pytest.mark.parametrize("bs", [16, 128])
+@pytest.mark.parametrize("d,hq,hkv,bs", [(128, 32, 8, 16), (128, 32, 8, 128), (256, 16, 2, 16),
+                                         (256, 16, 2, 64)])
 @pytest.mark.parametrize("decode", [True, False])
-def test_stale_cache_rows_nan(b200_ops, bs, decode, rel_err):
+def test_stale_cache_rows_nan(b200_ops, d, hq, hkv, bs, decode, rel_err):
     """Cache rows past each sequence end hold NaN (stale contents of a
     recycled block): masking and V-row zeroing keep them out of the output."""
     lens = [1, 17, 300, 129]
     lens_q = [1] * 4 if decode else [1, 17, 44, 129]
-    q, kc, vc, bt, sl, cu = _case(lens_q, lens, 32, 8, 128, bs, seed=8)
+    q, kc, vc, bt, sl, cu = _case(lens_q, lens, hq, hkv, d, bs, seed=8)
     for i, L in enumerate(lens):
         if L % bs:
             blk = int(bt[i, (L - 1) // bs])

@@ -1,5 +1,7 @@
 // Prefill / chunked-prefill paged attention on the 5th-generation tensor
-// cores (head_dim 128, bf16, causal with optional sliding window and sinks).
+// cores (head_dim 128 or 256, bf16, causal with optional sliding window and
+// sinks). Head_dim 256 (Qwen3-Next full attention) runs 64-key tiles: FN and
+// the ring depth come from FaCfg; the description below is for head_dim 128.
 //
 // One CTA owns 128 query rows of one (sequence, KV head): GQA-packed rows
 // r -> token t0 + r / G, head kvh * G + r % G, so every K/V tile is read once
@@ -48,17 +50,31 @@
 namespace b200 {
 namespace {
 
-constexpr int FD = 128;                // head dim
 constexpr int FM = 128;                // query rows per CTA
-constexpr int FN = 128;                // keys per tile
-constexpr int FNS = 3;                 // K/V ring stages
-constexpr int kHalf = 128 * 128;       // 128 rows x 64 bf16
-constexpr int kQBytes = 2 * kHalf;     // Q: two 64-column halves
-constexpr int kKVBytes = 4 * kHalf;    // K halves, then V halves
 constexpr int kBarBytes = 256;
-constexpr int kFaSmem = kQBytes + FNS * kKVBytes + kBarBytes + 1024;
 constexpr int kFaThreads = 224;
-constexpr uint32_t kTmemColsFa = 512;  // S0 | S1 | O | P0 | P1 (P: 64 columns each)
+constexpr uint32_t kTmemColsFa = 512;
+
+// Tile geometry per head dim: head_dim 128 streams 128-key tiles through a
+// 3-stage ring; head_dim 256 uses 64-key tiles and 2 stages so that S0 | S1
+// (2 FN) + O (FD) + P0 | P1 (FN) columns fit TMEM and Q (64 KB) + the ring
+// fit shared memory. Rows of every operand are 64 bf16 = 128 bytes (128-byte
+// swizzle); a row of FD values is FD / 64 such chunks.
+template <int D_>
+struct FaCfg {
+  static constexpr int FD = D_;
+  static constexpr int FN = D_ == 128 ? 128 : 64;
+  static constexpr int FNS = D_ == 128 ? 3 : 2;
+  static constexpr int kDC = FD / 64;             // 64-column chunks per row
+  static constexpr int kQChunk = FM * 128;        // Q: 128 rows x 64 bf16
+  static constexpr int kKVChunk = FN * 128;       // K or V: FN keys x 64 bf16
+  static constexpr int kQBytes = kDC * kQChunk;
+  static constexpr int kKBytes = kDC * kKVChunk;  // K (then V) of one tile
+  static constexpr int kKVBytes = 2 * kKBytes;
+  static constexpr int kSmem = kQBytes + FNS * kKVBytes + kBarBytes + 1024;
+  static_assert(2 * FN + FD + FN <= (int)kTmemColsFa, "TMEM columns");
+  static_assert(kSmem <= 232448, "shared memory");
+};
 
 struct FaParams {
   const int* block_table;
@@ -88,9 +104,14 @@ __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+template <int D_>
 __global__ void __launch_bounds__(kFaThreads, 1)
 fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
              const __grid_constant__ CUtensorMap tmv, const FaParams p) {
+  using Cfg = FaCfg<D_>;
+  constexpr int FD = Cfg::FD, FN = Cfg::FN, FNS = Cfg::FNS, kDC = Cfg::kDC;
+  constexpr int kQChunk = Cfg::kQChunk, kKVChunk = Cfg::kKVChunk, kQBytes = Cfg::kQBytes;
+  constexpr int kKBytes = Cfg::kKBytes, kKVBytes = Cfg::kKVBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -176,7 +197,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     FA_TL(1);
   }
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tS = tmem_base, tO = tmem_base + 256, tP = tmem_base + 384;
+  const uint32_t tS = tmem_base, tO = tmem_base + 2 * FN, tP = tO + FD;
   const int BS = p.block_size;
   const int blk_last = (seq_len - 1) >> p.block_shift;
 
@@ -187,8 +208,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
     const int nb = FN / BS;
     if (!is_v && lane == 0) {
       mbar_arrive_expect_tx(q_full, (uint32_t)kQBytes);
-      tma_load_3d(sQ, &tmq, q_full, 0, kvh * G, q0 + t0);
-      tma_load_3d(sQ + kHalf, &tmq, q_full, 64, kvh * G, q0 + t0);
+#pragma unroll
+      for (int c = 0; c < kDC; ++c)
+        tma_load_3d(sQ + c * kQChunk, &tmq, q_full, c * 64, kvh * G, q0 + t0);
     }
     // Cache-block ids are fetched ahead: one warp-wide load covers `per`
     // tiles (lane L: tile L / nb, block L % nb), and the next group's load is
@@ -218,20 +240,20 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       if (lane == 0) {
         ok = mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ph ^ 1u, p.err) ? 1 : 0;
         FA_TLJ(j, is_v ? 1 : 0);
-        if (ok) mbar_arrive_expect_tx(fullb, (uint32_t)(2 * kHalf));
+        if (ok) mbar_arrive_expect_tx(fullb, (uint32_t)kKBytes);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) return false;
-      uint8_t* dst = sKV + st * kKVBytes + (is_v ? 2 * kHalf : 0);
+      uint8_t* dst = sKV + st * kKVBytes + (is_v ? kKBytes : 0);
       const CUtensorMap* tm = is_v ? &tmv : &tmk;
       // One (cache block, column half) per lane: a bulk-tensor instruction
       // costs the issuing warp a few hundred ns plus a little per active
-      // lane, so the tile's 2 * nb boxes go out as one warp-wide instruction.
+      // lane, so the tile's kDC * nb boxes go out as one warp-wide instruction.
       const int bi = lane % nb;
       const int blk = __shfl_sync(0xffffffffu, ids, (j % per) * nb + bi);
-      if (lane < 2 * nb) {
+      if (lane < kDC * nb) {
         const int h = lane / nb;
-        tma_load_3d(dst + h * kHalf + bi * BS * 128, tm, fullb, h * 64, kvh * BS, blk);
+        tma_load_3d(dst + h * kKVChunk + bi * BS * 128, tm, fullb, h * 64, kvh * BS, blk);
       }
       return true;
     };
@@ -252,11 +274,11 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
           return false;
         FA_TLJ(i, 3);
         tc_fence_after();
-        const uint32_t sv = smem_u32(sKV + st * kKVBytes + 2 * kHalf);
+        const uint32_t sv = smem_u32(sKV + st * kKVBytes + kKBytes);
 #pragma unroll
         for (int s = 0; s < FN / 16; ++s) {
           const uint64_t bv = umma_desc_sw128_mn(sv + s * 16 * 128, p.v_lbo, p.v_sbo);
-          umma_f16_ts(tO, tP + pb * 64 + s * 8, bv, idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tP + pb * (FN / 2) + s * 8, bv, idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
         }
         umma_commit(&p_free[pb]);
         umma_commit(&v_empty[st]);
@@ -276,9 +298,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         const uint32_t sq = smem_u32(sQ);
         const uint32_t sk = smem_u32(sKV + stage * kKVBytes);
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-          const uint64_t aq = umma_desc_sw128(sq + kb * kHalf);
-          const uint64_t bk = umma_desc_sw128(sk + kb * kHalf);
+        for (int kb = 0; kb < kDC; ++kb) {
+          const uint64_t aq = umma_desc_sw128(sq + kb * kQChunk);
+          const uint64_t bk = umma_desc_sw128(sk + kb * kKVChunk);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             umma_f16(tS + sb * FN, aq + (uint64_t)(2 * k), bk + (uint64_t)(2 * k), idesc_s,
@@ -329,7 +351,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       const int lo = key_lo - kbase, hi = key_hi - kbase;  // in-tile bounds
       const bool masked = __any_sync(0xffffffffu, lo > 0 || hi < FN - 1);
       const uint32_t s_row = tS + lane_base + sb * FN;
-      const uint32_t p_row = tP + lane_base + pb * 64;
+      const uint32_t p_row = tP + lane_base + pb * (FN / 2);
       // One sweep over the row's 128 raw scores, 64 per TMEM wait. With
       // WRITE: P = exp2(S * scale - mu) packed as bf16 pairs into this row's
       // lane of the P buffer (key 2c, 2c+1 -> column c), row sum into *rs.
@@ -342,7 +364,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         const float mu_eff = mu == -INFINITY ? 0.f : mu;
         const uint64_t nmu2 = f32x2_pack(-mu_eff, -mu_eff);
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < FN / 64; ++h) {
           uint32_t r[2][32];
           tmem_ld_32x32b_x32(s_row + h * 64, r[0]);
           tmem_ld_32x32b_x32(s_row + h * 64 + 32, r[1]);
@@ -411,7 +433,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < FD / 32; ++c) {
             uint32_t o[32];
             tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);
             tmem_wait_ld();
@@ -432,11 +454,12 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
       if (j == n_tiles - 1 && kbase + FN > seq_len &&
           __all_sync(0xffffffffu, mbar_wait(&v_full[j % FNS], (uint32_t)((j / FNS) & 1), p.err))) {
         // Zero the V rows past the sequence end (stale cache-block contents).
-        uint8_t* sv = sKV + (j % FNS) * kKVBytes + 2 * kHalf;
+        uint8_t* sv = sKV + (j % FNS) * kKVBytes + kKBytes;
         const int first_bad = max(0, seq_len - kbase);
-        for (int idx = stid; idx < (FN - first_bad) * 16; idx += 128) {
-          const int key = first_bad + idx / 16, c16 = idx % 16;
-          *reinterpret_cast<uint4*>(sv + (c16 >> 3) * kHalf + sw_off(key, c16 & 7)) =
+        constexpr int kU = FD / 8;  // 16-byte units per key row
+        for (int idx = stid; idx < (FN - first_bad) * kU; idx += 128) {
+          const int key = first_bad + idx / kU, c16 = idx % kU;
+          *reinterpret_cast<uint4*>(sv + (c16 >> 3) * kKVChunk + sw_off(key, c16 & 7)) =
               make_uint4(0, 0, 0, 0);
         }
         // Generic-proxy writes -> visible to the tensor core.
@@ -461,7 +484,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
         const float inv = denom > 0.f ? 1.f / denom : 0.f;
         __nv_bfloat16* dst = p.out + (size_t)(q0 + t0 + t) * p.o_stride_t + (size_t)head * FD;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < FD / 32; ++c) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);  // warp-collective: every lane
           tmem_wait_ld();
@@ -511,15 +534,19 @@ bool fa_tc_enabled() {
 
 bool fa_tc_supported(const AttnArgs& a) {
   const int G = a.Hkv > 0 ? a.Hq / a.Hkv : 0;
-  return !a.decode && a.head_dim == FD && a.num_blocks > 0 && G > 0 && FM % G == 0 &&
-         a.block_size >= 16 && a.block_size <= FN && (FN % a.block_size) == 0 &&
-         a.q_stride_t % 8 == 0;
+  if (a.head_dim != 128 && a.head_dim != 256) return false;
+  const int FN = a.head_dim == 128 ? FaCfg<128>::FN : FaCfg<256>::FN;
+  return !a.decode && a.num_blocks > 0 && G > 0 && FM % G == 0 && a.block_size >= 16 &&
+         a.block_size <= FN && (FN % a.block_size) == 0 && a.q_stride_t % 8 == 0;
 }
 
-void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
-  auto kernel = fa_tc_kernel;
+template <int D_>
+void fa_tc_launch_d(const AttnArgs& a, cudaStream_t stream) {
+  using Cfg = FaCfg<D_>;
+  constexpr int FD = Cfg::FD;
+  auto kernel = fa_tc_kernel<D_>;
   static bool attr[kMaxDevices] = {};
-  set_smem_attr_once(kernel, kFaSmem, attr, "fa_tc");
+  set_smem_attr_once(kernel, Cfg::kSmem, attr, "fa_tc");
   const int G = a.Hq / a.Hkv;
   const int BS = a.block_size;
   const long long blk_stride = a.kv_block_stride > 0 ? a.kv_block_stride
@@ -556,13 +583,19 @@ void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   p.err = device_status_ptr(dev);
   // V as an MN-major B operand: the next 64-column block of V is a whole
-  // 128-row half (16 KB) away, the next group of 8 keys one 1024-byte atom.
-  p.v_lbo = (uint32_t)kHalf;
+  // FN-key chunk (FN x 128 bytes) away, the next group of 8 keys one
+  // 1024-byte atom.
+  p.v_lbo = (uint32_t)Cfg::kKVChunk;
   p.v_sbo = 1024u;
   const int max_qt = (a.max_q_len * G + FM - 1) / FM;
   if (max_qt <= 0 || a.num_seqs <= 0) return;
-  launch_pdl(kernel, dim3(max_qt, a.num_seqs, a.Hkv), dim3(kFaThreads), kFaSmem, stream, nullptr,
+  launch_pdl(kernel, dim3(max_qt, a.num_seqs, a.Hkv), dim3(kFaThreads), Cfg::kSmem, stream, nullptr,
              tq, tk, tv, p);
+}
+
+void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {
+  if (a.head_dim == 256) fa_tc_launch_d<256>(a, stream);
+  else fa_tc_launch_d<128>(a, stream);
 }
 
 }  // namespace b200

@@ -379,7 +379,8 @@ def main(argv=None):
                                      splits=max(1, args.splits), iters=args.iters,
                                      seq_blocks=args.seq_blocks))
     elif args.case == "prefill-attn":
-        out.append(bench_prefill_attn(args.seqs, args.len, bs=args.block, iters=args.iters))
+        out.append(bench_prefill_attn(args.seqs, args.len, hq=args.hq, hkv=args.hkv, d=args.d,
+                                      bs=args.block, iters=args.iters))
     else:
         for (M, N, K) in [(16384, 6144, 4096), (16384, 4096, 4096), (16384, 28672, 4096),
                           (16384, 4096, 14336), (256, 6144, 4096), (256, 4096, 4096),
