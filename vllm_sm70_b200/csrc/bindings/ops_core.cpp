@@ -656,10 +656,22 @@ void paged_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_c
 
 // Fused TP all-reduce + residual add + RMSNorm over peer-mapped symmetric
 // buffers (addresses from the symmetric-memory rendezvous, one per rank).
+// Multicast addresses [stage, res, out] (NVLS) or an empty list.
+static void set_mc(ArRmsNormParams& p, const std::vector<int64_t>& mc_ptrs) {
+  TORCH_CHECK(mc_ptrs.empty() || mc_ptrs.size() == 3, "ar_rmsnorm: mc_ptrs = [stage, res, out]");
+  if (mc_ptrs.size() == 3) {
+    TORCH_CHECK((mc_ptrs[0] | mc_ptrs[1] | mc_ptrs[2]) % 16 == 0 && mc_ptrs[0] && mc_ptrs[1] &&
+                mc_ptrs[2], "ar_rmsnorm: multicast addresses");
+    p.mc_stage = reinterpret_cast<const __nv_bfloat16*>(mc_ptrs[0]);
+    p.mc_res = reinterpret_cast<__nv_bfloat16*>(mc_ptrs[1]);
+    p.mc_out = reinterpret_cast<__nv_bfloat16*>(mc_ptrs[2]);
+  }
+}
+
 void ar_rmsnorm(const std::vector<int64_t>& stage_ptrs, const std::vector<int64_t>& res_ptrs,
                 const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& flag_ptrs,
                 int64_t rank, int64_t T, int64_t H, const at::Tensor& w, double eps,
-                int64_t timeout_ms, int64_t grid) {
+                int64_t timeout_ms, int64_t grid, const std::vector<int64_t>& mc_ptrs) {
   const int W = (int)stage_ptrs.size();
   TORCH_CHECK(W == 2 || W == 4 || W == 8, "ar_rmsnorm: world size must be 2, 4 or 8");
   TORCH_CHECK((int)res_ptrs.size() == W && (int)out_ptrs.size() == W && (int)flag_ptrs.size() == W,
@@ -685,6 +697,7 @@ void ar_rmsnorm(const std::vector<int64_t>& stage_ptrs, const std::vector<int64_
   p.eps = (float)eps;
   p.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
   p.err = device_status_ptr(w.get_device());
+  set_mc(p, mc_ptrs);
   c10::cuda::CUDAGuard g(w.device());
   ar_rmsnorm_launch(p, (int)grid, cur_stream());
 }
@@ -835,7 +848,8 @@ bool gemm_ar_rmsnorm(const at::Tensor& x, const at::Tensor& lin_w,
                      const std::vector<int64_t>& stage_ptrs, const std::vector<int64_t>& res_ptrs,
                      const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& flag_ptrs,
                      int64_t rank, const at::Tensor& w, double eps, int64_t timeout_ms,
-                     int64_t cfg, int64_t splits) {
+                     int64_t cfg, int64_t splits,
+                     const std::vector<int64_t>& mc_ptrs) {
   const int W = (int)stage_ptrs.size();
   TORCH_CHECK(W == 2 || W == 4 || W == 8, "gemm_ar_rmsnorm: world size must be 2, 4 or 8");
   TORCH_CHECK((int)res_ptrs.size() == W && (int)out_ptrs.size() == W && (int)flag_ptrs.size() == W,
@@ -865,6 +879,7 @@ bool gemm_ar_rmsnorm(const at::Tensor& x, const at::Tensor& lin_w,
   p.eps = (float)eps;
   p.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
   p.err = device_status_ptr(x.get_device());
+  set_mc(p, mc_ptrs);
   c10::cuda::CUDAGuard g(x.device());
   return gemm_ar_rmsnorm_launch(x.data_ptr(), lin_w.data_ptr(), (int)T, (int)H, (int)K,
                                 (int)x.stride(0), (int)lin_w.stride(0), (int)cfg, (int)splits, p,
@@ -983,10 +998,10 @@ TORCH_LIBRARY(_b200_C, m) {
   m.def("ep_finish(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, "
         "Tensor slot, Tensor? shared, Tensor(a!) out) -> ()");
   m.def("ar_rmsnorm(int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, int[] flag_ptrs, int rank, "
-        "int T, int H, Tensor w, float eps, int timeout_ms, int grid) -> ()");
+        "int T, int H, Tensor w, float eps, int timeout_ms, int grid, int[] mc_ptrs=[]) -> ()");
   m.def("gemm_ar_rmsnorm(Tensor x, Tensor lin_w, int[] stage_ptrs, int[] res_ptrs, int[] out_ptrs, "
-        "int[] flag_ptrs, int rank, Tensor w, float eps, int timeout_ms, int cfg, int splits) "
-        "-> bool");
+        "int[] flag_ptrs, int rank, Tensor w, float eps, int timeout_ms, int cfg, int splits, "
+        "int[] mc_ptrs=[]) -> bool");
   m.def("kv_cache_write(Tensor k, Tensor v, Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor slots) -> ()");
   m.def("argmax(Tensor(a!) ids, Tensor(b!)? vals, Tensor logits, int id_offset) -> ()");
   m.def("silu_mul(Tensor(a!) out, Tensor x, int block=0, Tensor? n_rows=None) -> ()");

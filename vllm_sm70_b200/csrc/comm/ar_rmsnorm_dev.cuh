@@ -15,6 +15,9 @@
 //           fp32, one bf16 round, + residual (bf16 round), RMSNorm (sum of
 //           squares in the block-size-independent order of rowsum.cuh), and the
 //           new residual / normalised rows stored into EVERY rank's buffers.
+//           NVLS variant (multicast addresses given): the switch sums the W
+//           partials (fp32 accumulation in the switch, order unspecified, one
+//           bf16 result) and one multimem.st writes every rank's copy.
 //   end   : every CTA release-adds 1 to done[rank] on every peer; CTA 0 waits
 //           until done[p] reaches the cumulative CTA count of all launches
 //           (rank-uniform grids), then bumps the epoch -- so no rank reuses
@@ -61,6 +64,28 @@ __device__ __forceinline__ bool wait_geq(const uint32_t* p, uint32_t target, uns
     }
   }
   return true;
+}
+
+// NVLS (NVLink SHARP) accesses through a multicast address: the switch sums
+// the 16 bytes of every rank's copy (fp32 accumulation, bf16 result), or
+// writes 16 bytes to every rank's copy.
+__device__ __forceinline__ uint4 multimem_ld_add_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ void multimem_st_16(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// Orders this thread's accesses through the unicast and multicast aliases of
+// the same memory.
+__device__ __forceinline__ void fence_proxy_alias() {
+  asm volatile("fence.proxy.alias;" ::: "memory");
 }
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
@@ -113,6 +138,7 @@ __device__ bool start_barrier(const ArRmsNormParams& p, uint32_t epoch, bool gat
     *s_ok = ok;
   }
   __syncthreads();
+  if (p.mc_stage != nullptr) fence_proxy_alias();  // stages were written through unicast
   return *s_ok != 0;
 }
 
@@ -132,16 +158,22 @@ __device__ void rows_phase(const ArRmsNormParams& p, float* part, float* bcast) 
       const int i = tid + k * blockDim.x;
       if (i < nvec) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        uint4 parts[W];
+        if (p.mc_stage != nullptr) {
+          // In-switch sum of every rank's partial (bf16 result of an fp32 sum).
+          unpack8(multimem_ld_add_bf16x8(reinterpret_cast<const uint4*>(
+                      p.mc_stage + (size_t)row * H) + i), acc);
+        } else {
+          uint4 parts[W];
 #pragma unroll
-        for (int q = 0; q < W; ++q)
-          parts[q] = __ldcv(reinterpret_cast<const uint4*>(p.stage_peer[q] + (size_t)row * H) + i);
+          for (int q = 0; q < W; ++q)
+            parts[q] = __ldcv(reinterpret_cast<const uint4*>(p.stage_peer[q] + (size_t)row * H) + i);
 #pragma unroll
-        for (int q = 0; q < W; ++q) {  // rank order
-          float f[8];
-          unpack8(parts[q], f);
+          for (int q = 0; q < W; ++q) {  // rank order
+            float f[8];
+            unpack8(parts[q], f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += f[e];
+            for (int e = 0; e < 8; ++e) acc[e] += f[e];
+          }
         }
         float res[8];
         unpack8(*(reinterpret_cast<const uint4*>(p.res_local + (size_t)row * H) + i), res);
@@ -156,9 +188,13 @@ __device__ void rows_phase(const ArRmsNormParams& p, float* part, float* bcast) 
 #pragma unroll
         for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
         part[i] = ss;
+        if (p.mc_res != nullptr) {
+          multimem_st_16(reinterpret_cast<uint4*>(p.mc_res + (size_t)row * H) + i, rs);
+        } else {
 #pragma unroll
-        for (int q = 0; q < W; ++q)
-          *(reinterpret_cast<uint4*>(p.res_peer[q] + (size_t)row * H) + i) = rs;
+          for (int q = 0; q < W; ++q)
+            *(reinterpret_cast<uint4*>(p.res_peer[q] + (size_t)row * H) + i) = rs;
+        }
       }
     }
     // Row sum of squares in the block-size-independent order.
@@ -174,9 +210,13 @@ __device__ void rows_phase(const ArRmsNormParams& p, float* part, float* bcast) 
         for (int e = 0; e < 8; ++e)
           o[e] = __bfloat162float(__float2bfloat16_rn(v[k][e] * inv)) * wf[e];
         const uint4 ov = pack8(o);
+        if (p.mc_out != nullptr) {
+          multimem_st_16(reinterpret_cast<uint4*>(p.mc_out + (size_t)row * H) + i, ov);
+        } else {
 #pragma unroll
-        for (int q = 0; q < W; ++q)
-          *(reinterpret_cast<uint4*>(p.out_peer[q] + (size_t)row * H) + i) = ov;
+          for (int q = 0; q < W; ++q)
+            *(reinterpret_cast<uint4*>(p.out_peer[q] + (size_t)row * H) + i) = ov;
+        }
       }
     }
   }
@@ -185,6 +225,7 @@ __device__ void rows_phase(const ArRmsNormParams& p, float* part, float* bcast) 
 template <int W>
 __device__ void end_barrier(const ArRmsNormParams& p, uint32_t epoch) {
   uint32_t* pad = p.flags_local;
+  if (p.mc_out != nullptr) fence_proxy_alias();  // multicast stores before the release below
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();

@@ -17,6 +17,13 @@ struct ArRmsNormParams {
   uint32_t* flags_local;                       // this rank's signal pad
   const __nv_bfloat16* res_local;              // this rank's residual (== res_peer[rank])
   const __nv_bfloat16* w;                      // RMSNorm weight [H]
+  // NVLS: multicast addresses of the stage / residual / output buffers (all
+  // null: plain peer loads and stores). With them, each owned row is summed in
+  // the switch (multimem.ld_reduce, fp32 accumulation, one bf16 result) and
+  // stored to every rank with one multimem.st.
+  const __nv_bfloat16* mc_stage;
+  __nv_bfloat16* mc_res;
+  __nv_bfloat16* mc_out;
   int rank, world, T, H;
   float eps;
   unsigned long long timeout_ns;

@@ -111,7 +111,13 @@ _reg("VLLM_B200_FUSED_EP_A2A", "kill", True, "comm", "Fused EP dispatch / combin
 _reg("VLLM_B200_FUSED_SAMPLER_XCHG", "kill", True, "comm",
      "Vocab-parallel sampling at TP > 1: exchange the greedy (value, id) pairs / top-k "
      "candidates over NVLink peer memory in one kernel (0 = NCCL all-gather + merge).")
-_reg("VLLM_B200_NVLS", "optin", False, "comm", "Use NVLS multimem reductions where supported.")
+_reg("VLLM_B200_NVLS", "optin", False, "comm",
+     "Fused all-reduce + RMSNorm through NVLS: multimem.ld_reduce sums each owned row in the "
+     "NVSwitch (fp32 accumulation, order unspecified: not bitwise equal to the rank-order sum) "
+     "and multimem.st writes every rank's copy, when the symmetric buffers have multicast "
+     "addresses and TP >= VLLM_B200_NVLS_MIN_RANKS.")
+_reg("VLLM_B200_NVLS_MIN_RANKS", "int", 4, "comm",
+     "Smallest TP size that takes the NVLS all-reduce (VLLM_B200_NVLS=1).")
 _reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
      "Bound (ms) for every device-side flag wait in fused collectives.")
 # -- runtime --------------------------------------------------------------

@@ -28,6 +28,10 @@ logger = logging.getLogger("vllm.b200.symm")
 SIGNAL_WORDS = 64  # uint32 words per rank: ready[W], done[W], epoch, done_target, arrive
 
 
+def nvls_min_ranks() -> int:
+    return int(envs.get("VLLM_B200_NVLS_MIN_RANKS"))
+
+
 class FusedArRmsNorm:
     def __init__(self, ps, max_tokens: int, hidden: int, dtype=torch.bfloat16,
                  grid_cap: int | None = None):
@@ -61,6 +65,24 @@ class FusedArRmsNorm:
         self.out_ptrs = [int(p) for p in ho.buffer_ptrs]
         self.flag_ptrs = [int(p) for p in hf.buffer_ptrs]
         self._handles = (hs, hr, ho, hf)
+        # NVLS: multicast addresses of the three data buffers when the fabric
+        # offers them (NVSwitch) and VLLM_B200_NVLS=1; the decision must be
+        # rank-uniform, so it is agreed over the CPU group.
+        self.mc_ptrs: list[int] = []
+        want = bool(envs.get("VLLM_B200_NVLS")) and ps.tp_size >= nvls_min_ranks()
+        ok = False
+        if want and dev.type == "cuda":
+            try:
+                ok = bool(symm_mem._SymmetricMemory.has_multicast_support(
+                    symm_mem.DeviceType.CUDA, dev.index)) and all(
+                        int(h.multicast_ptr) != 0 for h in (hs, hr, ho))
+            except (AttributeError, RuntimeError):
+                ok = False
+        vote = torch.tensor([1 if ok else 0], dtype=torch.int32)
+        dist.all_reduce(vote, op=dist.ReduceOp.MIN, group=ps.cpu_group)
+        if int(vote.item()) == 1:
+            self.mc_ptrs = [int(hs.multicast_ptr), int(hr.multicast_ptr), int(ho.multicast_ptr)]
+            logger.info("fused all-reduce + RMSNorm: NVLS multicast (W=%d)", ps.tp_size)
         self.timeout_ms = int(envs.get("VLLM_B200_COMM_TIMEOUT_MS"))
         self.calls = 0
 
@@ -95,7 +117,7 @@ class FusedArRmsNorm:
             rv.copy_(residual)
         torch.ops._b200_C.ar_rmsnorm(self.stage_ptrs, self.res_ptrs, self.out_ptrs,
                                      self.flag_ptrs, self.ps.tp_rank, T, self.H, w, eps,
-                                     self.timeout_ms, self.grid(T))
+                                     self.timeout_ms, self.grid(T), self.mc_ptrs)
         launch_count.add(1)
         self.calls += 1
         return self.out_view(T), rv
@@ -114,7 +136,8 @@ class FusedArRmsNorm:
             rv.copy_(residual)
         ok = torch.ops._b200_C.gemm_ar_rmsnorm(x, lin_w, self.stage_ptrs, self.res_ptrs,
                                                self.out_ptrs, self.flag_ptrs, self.ps.tp_rank,
-                                               w, eps, self.timeout_ms, cfg, splits)
+                                               w, eps, self.timeout_ms, cfg, splits,
+                                               self.mc_ptrs)
         if not ok:
             return None
         launch_count.add(1)
