@@ -515,6 +515,8 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CU
 #undef FA_TLJ
 }
 
+#include "attention/fa_tc_pp.cuh"
+
 }  // namespace
 
 void fa_tc_set_timeline(unsigned long long* buf) {
@@ -539,6 +541,9 @@ bool fa_tc_supported(const AttnArgs& a) {
   return !a.decode && a.num_blocks > 0 && G > 0 && FM % G == 0 && a.block_size >= 16 &&
          a.block_size <= FN && (FN % a.block_size) == 0 && a.q_stride_t % 8 == 0;
 }
+
+bool fa_pingpong_enabled();
+int fa_exp2_split();
 
 template <int D_>
 void fa_tc_launch_d(const AttnArgs& a, cudaStream_t stream) {
@@ -587,10 +592,40 @@ void fa_tc_launch_d(const AttnArgs& a, cudaStream_t stream) {
   // 1024-byte atom.
   p.v_lbo = (uint32_t)Cfg::kKVChunk;
   p.v_sbo = 1024u;
+  if (D_ == 128 && fa_pingpong_enabled()) {
+    // Two 128-row Q tiles per CTA (fa_tc_pp_kernel): Q boxes as above.
+    const int max_qt2 = (a.max_q_len * G + 2 * FM - 1) / (2 * FM);
+    if (max_qt2 <= 0 || a.num_seqs <= 0) return;
+    const int split = fa_exp2_split();
+    auto kpp = split == 2 ? fa_tc_pp_kernel<2> : split == 1 ? fa_tc_pp_kernel<1>
+                                                           : fa_tc_pp_kernel<0>;
+    static bool attr_pp[3][kMaxDevices] = {};
+    set_smem_attr_once(kpp, kPpSmem, attr_pp[split], "fa_tc_pp");
+    launch_pdl(kpp, dim3(max_qt2, a.num_seqs, a.Hkv), dim3(kPpThreads), kPpSmem, stream, nullptr,
+               tq, tk, tv, p);
+    return;
+  }
   const int max_qt = (a.max_q_len * G + FM - 1) / FM;
   if (max_qt <= 0 || a.num_seqs <= 0) return;
   launch_pdl(kernel, dim3(max_qt, a.num_seqs, a.Hkv), dim3(kFaThreads), Cfg::kSmem, stream, nullptr,
              tq, tk, tv, p);
+}
+
+int fa_exp2_split() {
+  static const int v = [] {
+    const char* e = std::getenv("VLLM_B200_ATTN_EXP2_SPLIT");
+    const int x = e ? std::atoi(e) : 1;  // measured best: a quarter on the FMA pipe
+    return x < 0 ? 0 : (x > 2 ? 2 : x);
+  }();
+  return v;
+}
+
+bool fa_pingpong_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLLM_B200_ATTN_PINGPONG");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
 }
 
 void fa_tc_launch(const AttnArgs& a, cudaStream_t stream) {

@@ -66,6 +66,13 @@ _reg("VLLM_B200_ATTN_DECODE_TMA", "kill", True, "kernels",
      "TMA-fed paged decode / spec-verify attention (0 = the cp.async kernel).")
 _reg("VLLM_B200_ATTN_PREFILL_TC", "kill", True, "kernels",
      "tcgen05 prefill attention (0 = the mma.sync kernel).")
+_reg("VLLM_B200_ATTN_EXP2_SPLIT", "int", 1, "kernels",
+     "Ping-pong prefill attention: share of the softmax exponentials of mask-free tiles "
+     "computed on the FMA pipe (0 none, 1 a quarter, 2 half; measured at 4 x 8192: 2.41 / "
+     "2.22 / 2.36 ms).")
+_reg("VLLM_B200_ATTN_PINGPONG", "kill", True, "kernels",
+     "tcgen05 prefill attention, head_dim 128: two 128-row Q tiles per CTA with one softmax "
+     "warpgroup each (0 = one Q tile per CTA).")
 _reg("VLLM_B200_GEMM_EXT_REDUCE", "optin", False, "kernels",
      "Split-K GEMMs write fp32 partials to a [split][M][N] workspace and a reduction kernel "
      "sums them (measured slower than the in-kernel reduction at decode sizes).")
