@@ -373,3 +373,72 @@ def test_fused_ar_rmsnorm_nvls(b200_ops):
     if world < 2:
         pytest.skip("needs 2+ GPUs")
     _mp.run(_nvls_body, world, timeout=600)
+
+
+def _ag_body(rank, world):
+    """All-gather -> GEMM in one kernel vs NCCL all-gather then the same GEMM
+    plan: bitwise equal, over several shapes, repeated calls (alternating
+    gather halves), split-K and CUDA-graph replays."""
+    import torch.distributed as dist
+
+    from vllm_sm70_b200.ops import linear
+    from vllm_sm70_b200.parallel import symm, state
+
+    ps = _setup(rank, world)
+    dev = ps.device
+    linear.configure_workspace(dev.index)
+    K = 4096
+    ag = symm.AgGemm(ps, 4096, K)
+    for it, (T, N, cfg, sp) in enumerate([(256, 6144, -1, 0), (1024, 1536, -1, 0),
+                                          (4096, 3072, -1, 0), (256, 6144, 0, 3),
+                                          (2048, 2048, 11, 1), (64 * world, 1024, -1, 0)]):
+        g = torch.Generator(device=dev).manual_seed(700 + it)
+        x_all = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        rpr = T // world
+        shard = x_all[rank * rpr:(rank + 1) * rpr].contiguous()
+        got = ag(shard, w, cfg=cfg, splits=sp)
+        gathered = torch.empty(T, K, device=dev, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(gathered, shard, group=ps.tp_group)
+        ref = linear.gemm(gathered, w, cfg=cfg, splits=sp) if cfg >= 0 else None
+        torch.cuda.synchronize()
+        assert torch.equal(gathered, x_all)
+        if ref is not None:
+            assert torch.equal(got, ref), f"ag gemm bitwise T={T} N={N} cfg={cfg}"
+        dense = (x_all.float() @ w.float().t())
+        err = ((got.float() - dense).norm() / dense.norm()).item()
+        assert err < 1e-2, (T, N, err)
+        assert int(torch.ops._b200_C.read_status(dev.index, True)) == 0
+    # CUDA graph: the device-side epoch advances per replay.
+    T, N = 512, 2048
+    shard = torch.empty(T // world, K, device=dev, dtype=torch.bfloat16)
+    w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+    out = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ag(shard, w, out=out, cfg=0, splits=1)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ag(shard, w, out=out, cfg=0, splits=1)
+    for it in range(4):
+        g = torch.Generator(device=dev).manual_seed(900 + it)
+        x_all = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+        shard.copy_(x_all[rank * (T // world):(rank + 1) * (T // world)])
+        graph.replay()
+        ref = linear.gemm(x_all, w, cfg=0, splits=1)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), f"graph replay {it}"
+    del graph
+    torch.cuda.synchronize()
+    dist.barrier()
+    state.shutdown()
+
+
+def test_all_gather_gemm_matches_nccl(b200_ops):
+    world = _world()
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    _mp.run(_ag_body, world, timeout=600)

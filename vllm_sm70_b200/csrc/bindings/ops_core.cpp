@@ -785,6 +785,43 @@ void ep_finish(const std::vector<int64_t>& bufs, int64_t rank, int64_t E_local, 
                    shared ? shared->data_ptr() : nullptr, out.data_ptr(), cur_stream());
 }
 
+// All-gather -> GEMM: out [T, N] = concat over ranks of shard [T/W, K] (rank
+// order) times w [N, K]^T, the gather done inside the GEMM through the
+// symmetric buffers xfull (each [2][t_max][K] bf16) and pads (16 words).
+void gemm_ag(const at::Tensor& w, at::Tensor& out, const at::Tensor& shard,
+             const std::vector<int64_t>& xfull_ptrs, const std::vector<int64_t>& pad_ptrs,
+             int64_t rank, int64_t t_max, int64_t cfg, int64_t splits, int64_t timeout_ms) {
+  const int W = (int)xfull_ptrs.size();
+  TORCH_CHECK(W >= 2 && W <= kMaxRanks && (int)pad_ptrs.size() == W, "gemm_ag: 2..8 ranks");
+  TORCH_CHECK(rank >= 0 && rank < W, "gemm_ag: bad rank");
+  CHECK_CUDA(shard); CHECK_BF16(shard); CHECK_BF16(w); CHECK_BF16(out);
+  TORCH_CHECK(shard.dim() == 2 && shard.is_contiguous() && w.dim() == 2 && w.stride(1) == 1 &&
+              w.size(1) == shard.size(1), "gemm_ag: shard [T/W, K] contiguous, w [N, K]");
+  const int64_t rpr = shard.size(0), K = shard.size(1), T = rpr * W, N = w.size(0);
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == T && out.size(1) == N && out.stride(1) == 1,
+              "gemm_ag: out [T, N]");
+  TORCH_CHECK(T <= t_max && K % 8 == 0 && (reinterpret_cast<uintptr_t>(shard.data_ptr()) & 15) == 0,
+              "gemm_ag: T <= t_max, K % 8, 16B-aligned shard");
+  AgParams ag{};
+  for (int q = 0; q < W; ++q) {
+    TORCH_CHECK(xfull_ptrs[q] % 16 == 0 && pad_ptrs[q] % 16 == 0, "gemm_ag: 16B alignment");
+    ag.xfull_peer[q] = reinterpret_cast<uint8_t*>(xfull_ptrs[q]);
+    ag.pad_peer[q] = reinterpret_cast<uint32_t*>(pad_ptrs[q]);
+  }
+  ag.pad_local = ag.pad_peer[rank];
+  ag.shard = shard.data_ptr();
+  ag.rank = (int)rank;
+  ag.world = W;
+  ag.rows_per_rank = (int)rpr;
+  ag.t_max = (int)t_max;
+  ag.K = (int)K;
+  ag.timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  unsigned int* err = device_status_ptr(shard.get_device());
+  c10::cuda::CUDAGuard g(shard.device());
+  gemm_ag_launch(w.data_ptr(), out.data_ptr(), (int)T, (int)N, (int)K, (int)w.stride(0),
+                 (int)out.stride(0), (int)cfg, (int)splits, ag, err, cur_stream());
+}
+
 // Vocab-parallel sampler exchange over peer memory. bufs = [recv, pad] per
 // rank. mode 0: src0 = values [rows] fp32, src1 = ids [rows] int32 ->
 // out0 = merged ids [rows] int32. mode 1: src0 / src1 = values / ids
@@ -993,6 +1030,8 @@ TORCH_LIBRARY(_b200_C, m) {
         "Tensor(b!) idc, Tensor(c!) wc, Tensor(d!) row_src, Tensor(e!) n_rows) -> ()");
   m.def("ep_return(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, Tensor y, "
         "Tensor row_src, Tensor n_rows) -> ()");
+  m.def("gemm_ag(Tensor w, Tensor(a!) out, Tensor shard, int[] xfull_ptrs, int[] pad_ptrs, "
+        "int rank, int t_max, int cfg=-1, int splits=0, int timeout_ms=2000) -> ()");
   m.def("tp_exchange(int[] bufs, int rank, int cap, int mode, Tensor src0, Tensor src1, "
         "Tensor(a!) out0, Tensor(b!)? out1, int timeout_ms) -> ()");
   m.def("ep_finish(int[] bufs, int rank, int E_local, int T_cap, int timeout_ms, int k, "
@@ -1035,6 +1074,7 @@ TORCH_LIBRARY_IMPL(_b200_C, CUDA, m) {
   m.impl("ep_return", &b200::ep_return);
   m.impl("ep_finish", &b200::ep_finish);
   m.impl("tp_exchange", &b200::tp_exchange);
+  m.impl("gemm_ag", &b200::gemm_ag);
   m.impl("gemm_fp8_out", &b200::gemm_fp8_out);
   m.impl("gemm_fp8_grouped_out", &b200::gemm_fp8_grouped_out);
   m.impl("dequant_weight", &b200::dequant_weight);

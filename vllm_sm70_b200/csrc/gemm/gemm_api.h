@@ -65,6 +65,25 @@ __host__ __device__ constexpr int raw_row_bytes(int wf) {
   return wf == kWFp8 ? 64 : (wf == kWBf16 ? 0 : 32);
 }
 
+// All-gather -> GEMM: this rank's row shard is copied into every rank's gather
+// buffer by the GEMM's epilogue warps (before their first accumulator), and the
+// producer TMA-loads each A tile from the local gather buffer once the ranks
+// whose rows it covers have raised their ready flag (world 0: off). Gather
+// buffers hold two halves of t_max rows, used by alternate epochs; pad words:
+// ready[8], arrive, done, epoch.
+struct AgParams {
+  uint8_t* xfull_peer[kMaxRanks] = {};  // every rank's gather buffer [2][t_max][K] bf16
+  uint32_t* pad_peer[kMaxRanks] = {};   // every rank's signal pad
+  uint32_t* pad_local = nullptr;
+  const void* shard = nullptr;          // this rank's rows [rows_per_rank][K] bf16
+  int rank = 0, world = 0;
+  int rows_per_rank = 0;
+  int t_max = 0;
+  int K = 0;
+  unsigned long long timeout_ns = 0;
+};
+constexpr int kAgPadReady = 0, kAgPadArrive = 8, kAgPadDone = 9, kAgPadEpoch = 10;
+
 struct WQParams {
   const float* scales_f32 = nullptr;                // kWFp8
   const __nv_bfloat162* scale_zero = nullptr;       // kWAwq
@@ -72,6 +91,7 @@ struct WQParams {
   int scale_ld = 0;                                 // elements per scale row
   float out_scale = 1.f;                            // kWNvfp4 global scale
   ArRmsNormParams ar{};                             // kEpiArNorm: the collective after the GEMM
+  AgParams ag{};                                    // all-gather -> GEMM (plain normal-mode tiles)
 };
 
 // Grouped (MoE) GEMM: per-expert tiles read from device arrays.
@@ -200,6 +220,10 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
 // kernel: C = A W^T goes into this rank's symmetric stage (ar.stage_peer[rank]),
 // then the same CTAs run the collective over NVLink peer memory. N == ar.H,
 // M == ar.T. Returns false (nothing launched) for shapes it does not take.
+// All-gather -> GEMM (AgParams): C[T, N] = gather(x shards)[T, K] . W^T.
+void gemm_ag_launch(const void* W, void* C, int T, int N, int K, int ldw, int ldc, int cfg,
+                    int splits, const AgParams& ag, unsigned int* err, cudaStream_t stream);
+
 bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, int lda, int ldw,
                             int cfg, int splits, const ArRmsNormParams& ar, unsigned int* err,
                             cudaStream_t stream);

@@ -183,7 +183,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   // operands are read by every role, so those launches wait up front; plain
   // bf16 launches wait in the producer only, after warming L2 with the first
   // weight tiles (weights are never written by an earlier kernel).
-  const bool early_wait = grp.E > 0 || WF != kWBf16;
+  // All-gather -> GEMM (plain normal-mode tiles only; see AgParams).
+  constexpr bool kAgKind = EPI == kEpiNone && !SWAP && WF == kWBf16 && !CL && !PAIR;
+  const bool ag_on = kAgKind && wq.ag.world > 0;
+  const bool early_wait = grp.E > 0 || WF != kWBf16 || ag_on;
   if (early_wait) pdl_wait();
   static_assert(WF == kWBf16 || SWAP, "quantised weights use the swap-AB (weight = P) form");
   static_assert(MH == 1 || (!SWAP && WF == kWBf16), "tall tiles: normal-mode bf16 only");
@@ -202,7 +205,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   constexpr int kAccCols = MH == 1 ? BN : MH * kHalfCols;
   constexpr int kNumAcc = 2 * kAccCols <= 512 ? 2 : 1;
   using S = Smem<QR, STAGES, WF, MH>;
-  static_assert((3 * STAGES + 6) * 8 + 32 <= S::kBarBytes, "barrier / slot area");
+  static_assert((3 * STAGES + 6) * 8 + 40 <= S::kBarBytes, "barrier / slot area");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -219,6 +222,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
   unsigned long long** tl_slot = reinterpret_cast<unsigned long long**>(tmem_slot + 4);
   uint64_t* free_bar = reinterpret_cast<uint64_t*>(tmem_slot + 6);  // cluster split: peers idle
+  uint32_t* ag_epoch_slot = tmem_slot + 8;  // all-gather: this launch's epoch
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -293,6 +297,9 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     mbar_init(done_bar, 1);
     mbar_init(recv_bar, 1);
     mbar_init(free_bar, splits > 1 ? splits - 1 : 1);
+    // (all-gather: the previous launch, which bumped the epoch, has completed:
+    // early_wait put the PDL wait above)
+    *ag_epoch_slot = ag_on ? *(volatile uint32_t*)(wq.ag.pad_local + kAgPadEpoch) + 1u : 0u;
     *abort_flag = 0;
     *tl_slot = tl_row;
     fence_barrier_init();
@@ -326,6 +333,9 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   tl_row = *tl_slot;
+  const uint32_t ag_e = *ag_epoch_slot;
+  // Gather-buffer rows of this epoch's half (A tile coordinates are offset by it).
+  const int ag_off = ag_on ? (int)(ag_e & 1u) * wq.ag.t_max : 0;
   if (threadIdx.x == 0) {
     B200_TL(1);
     pdl_trigger();
@@ -376,7 +386,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
             for (int h = 0; h < MH; ++h)
               for (int r = 0; r < p_rows_tile; r += pbox)
                 tma_load_2d(spp + h * S::kHalfBytes + r * (BK * 2), &tmap_p, &full_bar[stage],
-                            kb * BK, uc.p_row + h * BM + r);
+                            kb * BK, ag_off + uc.p_row + h * BM + r);
           }
           if (parts & 2)
             for (int r = 0; r < BN; r += qbox)
@@ -384,6 +394,25 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
                           uc.q_row + r);
         }
       }
+    };
+    // All-gather: before a unit's first A tile, wait (bounded) until every
+    // rank whose rows the tile covers has published them into this rank's
+    // gather buffer, then order those peer writes before the tensor-copy reads.
+    uint32_t ag_seen = 0;  // ranks already seen ready in this launch
+    auto ag_wait = [&](const UnitCoord& uc) -> bool {
+      if (!ag_on) return true;
+      const int rpr = wq.ag.rows_per_rank;
+      const int r0 = uc.p_row, r1 = min(p_rows, uc.p_row + MH * BM) - 1;
+      if (r1 < r0) return true;
+      const int c0 = r0 / rpr, c1 = min(wq.ag.world - 1, r1 / rpr);
+      for (int c = c0; c <= c1; ++c) {
+        if ((ag_seen >> c) & 1u) continue;
+        if (!ardev::wait_geq(wq.ag.pad_local + kAgPadReady + c, ag_e, err, wq.ag.timeout_ns))
+          return false;
+        ag_seen |= 1u << c;
+      }
+      fence_proxy_async_global();
+      return true;
     };
     int pre = 0;  // k-blocks of the first unit issued lane-parallel
     if (unit0 < num_units) {
@@ -416,6 +445,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         pdl_wait();
         if (lane < pre) load_stage(uc, kb0 + (lane + rot) % nk, lane, kA);
       } else if constexpr (!kQuant) {
+        if (!ag_wait(uc)) {
+          *abort_flag = 1;
+          pre = 0;
+        }
         if (lane < pre) load_stage(uc, kb0 + (lane + rot) % nk, lane);
         if (lane == 0 && pre > 0) B200_TL(2);
       }
@@ -432,6 +465,10 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int nk = kb1 - kb0;
         const int rot = kb_rotation(t, nk, num_m);
+        if (!first && !ag_wait(uc)) {
+          *abort_flag = 1;
+          break;
+        }
         for (int it = first ? pre : 0; it < nk; ++it) {
           const int kb = kb0 + (it + rot) % nk;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err)) {
@@ -593,6 +630,33 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     const float out_scale = wq.out_scale;
     const bool tma_st = kTmaStoreKind && (PAIR || MH == 2 || p_rows_tile == BM);
     int ebuf = 0;  // staging buffer of this warp's next tile store
+    if (ag_on) {
+      // All-gather: copy this rank's rows into slot `rank` of this epoch's half
+      // of every rank's gather buffer (16-byte stores over NVLink), while the
+      // producer and the tensor core start on the rows already here. The last
+      // CTA to finish publishes the rank's ready flag on every rank.
+      const AgParams& ag = wq.ag;
+      const size_t nvec = (size_t)ag.rows_per_rank * ag.K / 8;
+      const size_t dst0 = ((size_t)(ag_e & 1u) * ag.t_max + (size_t)ag.rank * ag.rows_per_rank) *
+                          ag.K / 8;
+      const uint4* src = reinterpret_cast<const uint4*>(ag.shard);
+      for (size_t i = (size_t)blockIdx.x * 128 + etid; i < nvec; i += (size_t)gridDim.x * 128) {
+        const uint4 v = src[i];
+        for (int q2 = 0; q2 < ag.world; ++q2)
+          reinterpret_cast<uint4*>(ag.xfull_peer[q2])[dst0 + i] = v;
+      }
+      __threadfence_system();
+      named_barrier_sync(1, 128);
+      if (etid == 0) {
+        const uint32_t n = atomicAdd(ag.pad_local + kAgPadArrive, 1u) + 1u;
+        if (n == gridDim.x) {
+          atomicExch(ag.pad_local + kAgPadArrive, 0u);  // re-arm for the next launch
+          __threadfence_system();
+          for (int q2 = 0; q2 < ag.world; ++q2)
+            ardev::st_release_sys(ag.pad_peer[q2] + kAgPadReady + ag.rank, ag_e);
+        }
+      }
+    }
     int local = 0;
     for (int u = unit0; u < num_units && !*abort_flag; u += ustride, ++local) {
       const int t = u / splits, sp = u - t * splits;
@@ -1365,6 +1429,14 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmap_p,
     else tmem_dealloc(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0) B200_TL(7);
+  if (ag_on && threadIdx.x == 0) {
+    // Every CTA is past its waits: the last one hands the next launch its epoch.
+    const uint32_t n = atomicAdd(wq.ag.pad_local + kAgPadDone, 1u) + 1u;
+    if (n == gridDim.x) {
+      atomicExch(wq.ag.pad_local + kAgPadDone, 0u);
+      atomicExch(wq.ag.pad_local + kAgPadEpoch, ag_e);
+    }
+  }
   if constexpr (EPI == kEpiArNorm) {
     // Fused TP collective: every tile of this rank's stage is stored once all
     // CTAs have arrived; the same CTAs then all-reduce, add the residual and
@@ -1415,7 +1487,7 @@ bool launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
                 int ldq, int ldc, int splits, float* ws, int* counters, unsigned int* err,
                 cudaStream_t stream, const WQParams& wq = WQParams{},
                 const GroupInfo& grp = GroupInfo{}, int grid_units = 0, int pm = BM,
-                bool ext = false) {
+                bool ext = false, int p_map_rows = 0) {
   using S = Smem<BN, STAGES, WF, MH>;
   if (MH != 1 || WF != kWBf16 || grp.E > 0 || pm <= 0 || pm > BM) pm = BM;
   // TMA box rows per operand (bf16 operands only; 0 = one box per tile).
@@ -1431,8 +1503,10 @@ bool launch_cfg(const void* P, const void* Q, void* C, int p_rows, int q_rows, i
   set_smem_attr_once(kernel, S::kTotal, attr_set, "gemm_bf16_tc");
   CUtensorMap tp;
   if constexpr (WF == kWBf16) {
-    tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_rows, K, (uint64_t)ldp * 2, pbox,
-                      BK);
+    // (p_map_rows: the map spans more rows than are tiled -- the two halves
+    // of an all-gather buffer)
+    tp = make_tmap_2d(P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p_map_rows > 0 ? p_map_rows : p_rows,
+                      K, (uint64_t)ldp * 2, pbox, BK);
   } else {
     // Raw quantised rows: K * bytes-per-element bytes, box = 128 rows x one k-block.
     const int rb = raw_row_bytes(WF);
@@ -2015,6 +2089,54 @@ void gemm_bf16_launch_split(const void* A, const void* W, void* C, int M, int N,
              reinterpret_cast<__nv_bfloat16*>(C), ldc);
 }
 
+
+// All-gather -> GEMM: C[T, N] = gather(shards)[T, K] . W^T with the gather
+// inside the GEMM (AgParams). Tiles are plain normal-mode tiles (128 x 256 or
+// 128 x 128, or the 256-row tall ones), split-K as planned.
+void gemm_ag_launch(const void* W, void* C, int T, int N, int K, int ldw, int ldc, int cfg,
+                    int splits, const AgParams& ag, unsigned int* err, cudaStream_t stream) {
+  if (ag.world < 2 || ag.world > kMaxRanks || T != ag.rows_per_rank * ag.world || T > ag.t_max ||
+      K != ag.K || K % 8 != 0)
+    throw std::runtime_error("gemm_ag: bad shape / world");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cfg < 0) {
+    const GemmPlan pl = gemm_bf16_plan(T, N, K, kEpiNone, num_sms(dev));
+    cfg = pl.cfg;
+    if (splits <= 0) splits = pl.splits;
+  }
+  if (splits <= 0) splits = 1;
+  // The gather needs plain normal-mode tiles.
+  if (cfg == kCfgM2N224 || cfg == kCfgM2N112 || cfg == kCfgP2N256 || cfg == kCfgClM2N128 ||
+      cfg == kCfgClM2N112)
+    cfg = kCfgM2N128;
+  else if (cfg == kCfgM2N64 || cfg == kCfgClM2N64)
+    cfg = kCfgM2N128;
+  else if (cfg != kCfgN256 && cfg != kCfgN128 && cfg != kCfgM2N256 && cfg != kCfgM2N128)
+    cfg = kCfgN128;
+  SplitWorkspace& ws = g_split_ws[dev];
+  SplitGeometry geo = gemm_split_geometry(T, N, K, cfg, splits, num_sms(dev));
+  if (splits > 1 && (ws.ws == nullptr || geo.ws_bytes > ws.ws_bytes || geo.counters > ws.n_counters))
+    splits = 1;
+  float* wsp = splits > 1 ? ws.ws : nullptr;
+  int* cnt = splits > 1 ? ws.counters : nullptr;
+  WQParams wq{};
+  wq.ag = ag;
+  const void* P = ag.xfull_peer[ag.rank];
+  const int map_rows = 2 * ag.t_max;
+#define B200_AG(BN_, ST_, MH_)                                                                   \
+  launch_cfg<BN_, ST_, false, kEpiNone, kWBf16, MH_>(P, W, C, T, N, K, K, ldw, ldc, splits, wsp, \
+                                                    cnt, err, stream, wq, GroupInfo{}, 0, BM,   \
+                                                    false, map_rows);                           \
+  return
+  switch (cfg) {
+    case kCfgN256: B200_AG(256, 4, 1);
+    case kCfgM2N256: B200_AG(256, 3, 2);
+    case kCfgM2N128: B200_AG(128, 4, 2);
+    default: B200_AG(128, 6, 1);
+  }
+#undef B200_AG
+}
 
 bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, int lda, int ldw,
                             int cfg, int splits, const ArRmsNormParams& ar, unsigned int* err,

@@ -39,6 +39,7 @@ NO_FAKE = {
     "ep_return": "expert-parallel exchange over peer pointers (eager only)",
     "ep_finish": "expert-parallel exchange over peer pointers (eager only)",
     "tp_exchange": "peer-memory collective (raw pointer lists)",
+    "gemm_ag": "all-gather -> GEMM over peer memory (raw pointer lists)",
 }
 
 _done = False

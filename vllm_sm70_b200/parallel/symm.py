@@ -202,3 +202,45 @@ class TpExchange:
                                       self.timeout_ms)
         launch_count.add(1)
         return ov, oi
+
+
+class AgGemm:
+    """Column-parallel all-gather -> GEMM (``_b200_C::gemm_ag``): each rank
+    holds a row shard ``[T / W, K]`` of the input; one kernel per rank copies
+    its shard into every rank's symmetric gather buffer (two halves of
+    ``t_max`` rows used by alternate epochs) and multiplies the gathered rows
+    by its weight shard, each tile starting as soon as the ranks it reads from
+    have published their rows. Reference parity: the per-tile flag-publish /
+    peer-load pattern of the reference's dormant tile all-reduce epilogue
+    (``sm70/csrc/turbomind/lmdeploy/src/turbomind/kernels/gemm/epilogue.h:347-560``)."""
+
+    def __init__(self, ps, t_max: int, K: int, dtype=torch.bfloat16):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        assert ps.tp_size in (2, 4, 8), ps.tp_size
+        self.ps, self.t_max, self.K = ps, t_max, K
+        dev = ps.device
+        self.xfull = symm_mem.empty(2 * t_max * K, dtype=dtype, device=dev)
+        hx = symm_mem.rendezvous(self.xfull, ps.tp_group)
+        self.pad = symm_mem.empty(16, dtype=torch.int32, device=dev)
+        hp = symm_mem.rendezvous(self.pad, ps.tp_group)
+        self.pad.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=ps.cpu_group)
+        self.xfull_ptrs = [int(p) for p in hx.buffer_ptrs]
+        self.pad_ptrs = [int(p) for p in hp.buffer_ptrs]
+        self._handles = (hx, hp)
+        self.timeout_ms = int(envs.get("VLLM_B200_COMM_TIMEOUT_MS"))
+
+    def admits(self, T: int, K: int) -> bool:
+        return K == self.K and 0 < T <= self.t_max and T % self.ps.tp_size == 0
+
+    def __call__(self, shard: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+                 cfg: int = -1, splits: int = 0) -> torch.Tensor:
+        T = shard.shape[0] * self.ps.tp_size
+        if out is None:
+            out = torch.empty(T, w.shape[0], dtype=shard.dtype, device=shard.device)
+        torch.ops._b200_C.gemm_ag(w, out, shard.contiguous(), self.xfull_ptrs, self.pad_ptrs,
+                                  self.ps.tp_rank, self.t_max, cfg, splits, self.timeout_ms)
+        launch_count.add(1)
+        return out
