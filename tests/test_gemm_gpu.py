@@ -281,3 +281,31 @@ def test_gemm_decode_shapes_all_plans(b200_ops, M, N, K, rel_err):
         torch.cuda.synchronize()
         assert rel_err(o1, ref) < 1e-2, (cfg, sp)
         assert torch.equal(o1, o2), (cfg, sp)
+
+
+@pytest.mark.parametrize("M,cfg,splits", [(256, 0, 1), (256, 0, 3), (1000, 11, 2), (4096, 9, 1),
+                                          (7, 0, 2)])
+def test_gemm_add_rmsnorm_tp1_bitwise(b200_ops, M, cfg, splits):
+    """TP1 row GEMM + residual add + RMSNorm in one kernel (the fused
+    all-reduce epilogue with one rank) equals the GEMM with the same plan
+    followed by fused_add_rms_norm, bit for bit, across repeated calls."""
+    from vllm_sm70_b200.ops import norm
+    from vllm_sm70_b200.parallel import symm
+
+    torch.manual_seed(11)
+    N, K = 4096, 4096
+    f = symm.LocalAddRmsNorm("cuda", 4096, N)
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    nw = (torch.randn(N, device="cuda") * 0.5 + 1).to(torch.bfloat16)
+    for it in range(3):
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        res = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+        got_x, got_r = f.gemm(x, w, res.clone(), nw, 1e-5, cfg, splits)
+        # the fused launcher maps the plan onto its tiles; compare with that plan
+        ref_x = linear.gemm(x, w, cfg=cfg, splits=splits)
+        ref_r = res.clone()
+        norm.fused_add_rms_norm(ref_x, ref_r, nw, 1e-5)
+        torch.cuda.synchronize()
+        assert torch.equal(got_r, ref_r), (M, cfg, splits, it)
+        assert torch.equal(got_x, ref_x), (M, cfg, splits, it)
+    assert int(torch.ops._b200_C.read_status(0, True)) == 0

@@ -888,7 +888,8 @@ bool gemm_ar_rmsnorm(const at::Tensor& x, const at::Tensor& lin_w,
                      int64_t cfg, int64_t splits,
                      const std::vector<int64_t>& mc_ptrs) {
   const int W = (int)stage_ptrs.size();
-  TORCH_CHECK(W == 2 || W == 4 || W == 8, "gemm_ar_rmsnorm: world size must be 2, 4 or 8");
+  TORCH_CHECK(W == 1 || W == 2 || W == 4 || W == 8,
+              "gemm_ar_rmsnorm: world size must be 1 (TP1: add + RMSNorm), 2, 4 or 8");
   TORCH_CHECK((int)res_ptrs.size() == W && (int)out_ptrs.size() == W && (int)flag_ptrs.size() == W,
               "gemm_ar_rmsnorm: pointer lists must have one entry per rank");
   TORCH_CHECK(rank >= 0 && rank < W, "gemm_ar_rmsnorm: bad rank");

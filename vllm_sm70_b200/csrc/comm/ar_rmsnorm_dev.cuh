@@ -259,6 +259,7 @@ __device__ void run(const ArRmsNormParams& p, bool gated, float* part, float* bc
 __device__ __forceinline__ void run_any(const ArRmsNormParams& p, bool gated, float* part,
                                         float* bcast, int* s_ok) {
   switch (p.world) {
+    case 1: run<1>(p, gated, part, bcast, s_ok); break;  // residual add + RMSNorm after a GEMM (TP1)
     case 2: run<2>(p, gated, part, bcast, s_ok); break;
     case 4: run<4>(p, gated, part, bcast, s_ok); break;
     case 8: run<8>(p, gated, part, bcast, s_ok); break;

@@ -2144,7 +2144,7 @@ bool gemm_ar_rmsnorm_launch(const void* A, const void* W, int M, int N, int K, i
   if (M <= 0 || N <= 0 || K <= 0) return true;
   if (M != ar.T || N != ar.H || K % 8 != 0 || lda % 8 != 0 || ldw % 8 != 0 || N % 8 != 0)
     return false;
-  if ((ar.world != 2 && ar.world != 4 && ar.world != 8) ||
+  if ((ar.world != 1 && ar.world != 2 && ar.world != 4 && ar.world != 8) ||
       N / 8 > ardev::kMaxVec * kThreads)
     return false;
   int dev = 0;

@@ -201,6 +201,14 @@ class LLM:
                                   num_kv_blocks, self.device,
                                   use_graphs=not enforce_eager and self.ep is None,
                                   num_sms=num_sms)
+        if (self.device.type == "cuda" and ps.tp_size == 1 and self.ep is None
+                and envs.get("VLLM_B200_FUSED_GEMM_NORM")):
+            from ..parallel import comm, symm
+
+            # Held by the engine too: its captured graphs bake in these buffers.
+            self._local_norm = symm.LocalAddRmsNorm(
+                self.device, max(max_num_batched_tokens, max_num_seqs), self.cfg.hidden_size)
+            comm.set_local_gemm_norm(self._local_norm)
         if self.device.type == "cuda" and ps.tp_size > 1:
             from ..parallel import comm, symm
 

@@ -140,6 +140,11 @@ _reg("VLLM_B200_FUSED_GEMM_AR", "kill", True, "comm",
      "residual + RMSNorm as one kernel (tcgen05 tiles, then the collective over NVLink peer "
      "memory) instead of a GEMM followed by the collective kernel, for token counts of at "
      "least VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS.")
+_reg("VLLM_B200_FUSED_GEMM_NORM", "optin", False, "kernels",
+     "TP1: run each row GEMM (o_proj, down_proj) and the residual add + RMSNorm after it as one "
+     "kernel (the fused all-reduce epilogue with one rank). Off: measured slower on the "
+     "headline (9,383 vs 10,233 tok/s, same box) -- the fused launcher is limited to non-pair "
+     "tiles and its grid barrier costs more than the norm kernel it removes.")
 _reg("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS", "int", 1, "comm",
      "Smallest token count that takes the fused GEMM + all-reduce kernel (measured at TP2 on "
      "Llama-3.1-8B shapes with every GEMM on the tcgen05 kernels: the fused kernel is as fast or "

@@ -20,7 +20,20 @@ import torch.distributed as dist
 from .. import envs, ops
 from . import state as pstate
 
-_fused = {"ar_rmsnorm": None, "tp_exchange": None}
+_fused = {"ar_rmsnorm": None, "tp_exchange": None, "local_gemm_norm": None}
+
+
+def set_local_gemm_norm(impl) -> None:
+    """Install the TP1 GEMM + residual add + RMSNorm kernel path (a
+    ``parallel.symm.LocalAddRmsNorm`` or None)."""
+    _fused["local_gemm_norm"] = impl
+
+
+def local_gemm_norm():
+    impl = _fused["local_gemm_norm"]
+    if impl is None or not envs.get("VLLM_B200_FUSED_GEMM_NORM"):
+        return None
+    return impl
 
 
 def set_tp_exchange(impl) -> None:
@@ -62,7 +75,7 @@ def row_parallel_out(T: int, H: int, dtype=torch.bfloat16, device=None) -> torch
 def adopt_residual(residual: torch.Tensor) -> torch.Tensor:
     """Move the residual stream into the fused path's symmetric buffer (once
     per forward) so the fused kernel updates it in place on every rank."""
-    impl = fused_ar_rmsnorm()
+    impl = fused_ar_rmsnorm() if pstate.get().tp_size > 1 else local_gemm_norm()
     T = residual.shape[0]
     if impl is not None and impl.admits(T) and impl.H == residual.shape[1]:
         rv = impl.res_view(T)
@@ -97,6 +110,15 @@ def linear_all_reduce_add_rms_norm(lin, x: torch.Tensor, residual: torch.Tensor,
     otherwise the GEMM writes the stage and the collective follows."""
     st = pstate.get()
     T, H = x.shape[0], getattr(lin, "out_features", None)
+    if st.tp_size == 1:
+        impl = local_gemm_norm()
+        lw = getattr(lin, "w", None)
+        if (impl is not None and type(lin).__name__ == "DenseLinear" and lw is not None
+                and lw.dtype == torch.bfloat16 and x.is_cuda and x.stride(1) == 1
+                and residual.is_cuda):
+            r = impl.gemm(x, lw, residual, w, eps)
+            if r is not None:
+                return r
     if (st.tp_size > 1 and envs.get("VLLM_B200_FUSED_GEMM_AR")
             and T >= envs.get("VLLM_B200_FUSED_GEMM_AR_MIN_TOKENS")):
         impl = fused_ar_rmsnorm()

@@ -244,3 +244,54 @@ class AgGemm:
                                   self.ps.tp_rank, self.t_max, cfg, splits, self.timeout_ms)
         launch_count.add(1)
         return out
+
+
+class LocalAddRmsNorm:
+    """TP1: a row GEMM (o_proj, down_proj) fused with the residual add and
+    RMSNorm that follow it, in one kernel -- the fused all-reduce epilogue of
+    :class:`FusedArRmsNorm` with a single rank: every CTA stores its tiles
+    into the stage, the CTAs meet at a grid-wide flag barrier (the grid is
+    resident) and then add the residual and normalise the rows. Plain device
+    buffers (no peers); the same interface as FusedArRmsNorm's GEMM path, and
+    the same bits as the GEMM followed by ``fused_add_rms_norm``."""
+
+    def __init__(self, device, max_tokens: int, hidden: int, dtype=torch.bfloat16):
+        self.T_max, self.H = max_tokens, hidden
+        self.stage = torch.empty(max_tokens * hidden, dtype=dtype, device=device)
+        self.res = torch.empty(max_tokens * hidden, dtype=dtype, device=device)
+        self.out = torch.empty(max_tokens * hidden, dtype=dtype, device=device)
+        self.flags = torch.zeros(SIGNAL_WORDS, dtype=torch.int32, device=device)
+        self.stage_ptrs = [self.stage.data_ptr()]
+        self.res_ptrs = [self.res.data_ptr()]
+        self.out_ptrs = [self.out.data_ptr()]
+        self.flag_ptrs = [self.flags.data_ptr()]
+        self.timeout_ms = int(envs.get("VLLM_B200_COMM_TIMEOUT_MS"))
+        self.calls = 0
+
+    def admits(self, T: int) -> bool:
+        return 0 < T <= self.T_max
+
+    def res_view(self, T: int) -> torch.Tensor:
+        return self.res[: T * self.H].view(T, self.H)
+
+    def out_view(self, T: int) -> torch.Tensor:
+        return self.out[: T * self.H].view(T, self.H)
+
+    def gemm(self, x: torch.Tensor, lin_w: torch.Tensor, residual: torch.Tensor,
+             w: torch.Tensor, eps: float, cfg: int = -1, splits: int = 0):
+        """(normalised rows, new residual) as views of the buffers, or None
+        when not taken (the caller runs the GEMM and fused_add_rms_norm)."""
+        T = x.shape[0]
+        if not self.admits(T) or lin_w.shape[0] != self.H:
+            return None
+        rv = self.res_view(T)
+        if residual.data_ptr() != rv.data_ptr():
+            rv.copy_(residual)
+        ok = torch.ops._b200_C.gemm_ar_rmsnorm(x, lin_w, self.stage_ptrs, self.res_ptrs,
+                                               self.out_ptrs, self.flag_ptrs, 0, w, eps,
+                                               self.timeout_ms, cfg, splits, [])
+        if not ok:
+            return None
+        launch_count.add(1)
+        self.calls += 1
+        return self.out_view(T), rv
