@@ -1,6 +1,9 @@
 """Spawn helpers for multi-process tests: every child gets RANK/WORLD_SIZE/
-MASTER_* (127.0.0.1, a free port), the parent joins with a deadline and kills
-stragglers, so a protocol deadlock fails the test instead of hanging it."""
+MASTER_* (127.0.0.1), the parent joins with a deadline and kills stragglers,
+so a protocol deadlock fails the test instead of hanging it. The parent hosts
+the rendezvous store on a port it has already bound and every child attaches
+to it as a client (as under torchrun's agent), so no child races another
+process for a free port."""
 import os
 import socket
 import traceback
@@ -16,7 +19,8 @@ def free_port() -> int:
 
 def _entry(rank, world, port, fn, args, q):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
-                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      TORCHELASTIC_USE_AGENT_STORE="True")
     try:
         fn(rank, world, *args)
         q.put((rank, None))
@@ -25,9 +29,16 @@ def _entry(rank, world, port, fn, args, q):
 
 
 def run(fn, world: int, args=(), timeout: float = 300.0):
+    import datetime
+
+    import torch.distributed as dist
+
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = free_port()
+    # The store server binds port 0 itself: the port is held from the start.
+    store = dist.TCPStore("127.0.0.1", 0, world, is_master=True, wait_for_workers=False,
+                          timeout=datetime.timedelta(seconds=timeout))
+    port = store.port
     procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q)) for r in range(world)]
     for p in procs:
         p.start()
