@@ -163,18 +163,23 @@ def run_ours(args) -> dict:
     from vllm_sm70_b200.utils import launch_count
 
     world, rank = _dist_setup()
-    dp = args.layout == "dp-ep" and world > 1  # each rank serves its share of the requests
+    dp = args.layout == "dp-ep" and world > 1  # each replica serves its share of the requests
+    tp_in = args.tp if dp else 1  # dp-ep: TP ranks inside a replica (the TP x EP layout)
+    if dp and world % tp_in:
+        raise SystemExit(f"--tp {tp_in} does not divide the world size {world}")
+    n_rep = world // tp_in if dp else 1
     if dp:
-        ps = pstate.init(tp_size=1, ep_size=world)
+        ps = pstate.init(tp_size=tp_in, ep_size=world)
     else:
         ps = pstate.init(tp_size=args.gpus if world > 1 else 1)
-    share = (lambda p: p[rank::world].contiguous()) if dp else (lambda p: p)
+    rep = rank // tp_in  # contiguous ranks form a replica and pass the same prompts
+    share = (lambda p: p[rep::n_rep].contiguous()) if dp else (lambda p: p)
     llm = LLM(PRESET, tensor_parallel_size=ps.tp_size,
-              max_num_seqs=(N_REQ + world - 1) // world if dp else N_REQ,
+              max_num_seqs=(N_REQ + n_rep - 1) // n_rep if dp else N_REQ,
               max_model_len=PROMPT + OUT + (SPEC_K + 1 if SPEC_K else 0),
               block_size=args.block_size, max_num_batched_tokens=args.chunk,
               load_format="dummy", seed=0, speculative_k=SPEC_K,
-              data_parallel_size=world if dp else 1, enable_expert_parallel=dp)
+              data_parallel_size=n_rep if dp else 1, enable_expert_parallel=dp)
     warm = [share(make_prompts(1000 + i)).pin_memory() for i in range(args.warmup)]
     timed = [share(make_prompts(2000 + i)).pin_memory() for i in range(args.steps)]
     prompts = timed[0]
@@ -211,8 +216,8 @@ def run_ours(args) -> dict:
     dev_ms = _max_over_ranks(dev_ms)
     wall = _max_over_ranks(wall)
     n_out = sum(len(o.output_token_ids) for o in outs) * args.steps
-    if dp:  # every rank served its own share: the job's tokens are the sum
-        n_out = int(_sum_over_ranks(float(n_out)))
+    if dp:  # every replica served its own share: the job's tokens are the sum
+        n_out = int(_sum_over_ranks(float(n_out) if rank % tp_in == 0 else 0.0))
     value = n_out / (dev_ms / 1e3)
     e2e = n_out / wall
     res = {
@@ -223,7 +228,8 @@ def run_ours(args) -> dict:
         "dtype": "bf16", "data": "synthetic (uniform-random prompt ids, random-init weights std 0.02)",
         "config": {"model": MODEL, "global_batch": N_REQ, "seq_len": PROMPT,
                    "output_len": OUT,
-                   "parallelism": f"dp{args.gpus}-ep{args.gpus}" if dp else f"tp{args.gpus}",
+                   "parallelism": (f"dp{n_rep}-tp{tp_in}-ep{world}" if tp_in > 1 else
+                                   f"dp{world}-ep{world}") if dp else f"tp{args.gpus}",
                    "temperature": TEMPERATURE, "speculative_k": SPEC_K,
                    "l2": "inputs larger than L2 (16 GB of weights streamed per step)",
                    "block_size": args.block_size, "prefill_chunk_tokens": args.chunk},
@@ -425,6 +431,9 @@ def main(argv=None):
     ap.add_argument("--layout", choices=["tp", "dp-ep"], default="tp",
                     help="N > 1: tensor parallel (MoE experts sliced over the TP group), or "
                          "data-parallel attention with all-to-all expert parallelism")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="dp-ep only: tensor-parallel ranks inside each data-parallel replica "
+                         "(TP x EP: experts over all ranks, attention and dense GEMMs over TP)")
     args = ap.parse_args(argv)
     if args.verbose:
         import logging

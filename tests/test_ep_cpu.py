@@ -161,3 +161,48 @@ def test_dp_ep_engine_equals_single_process(tmp_path, arch, world):
         else:
             assert rec["again"] == []
     assert [got[i] for i in range(len(ref))] == ref
+
+
+def _tpxep_body(rank, world, tp, path, out_file):
+    from pathlib import Path
+
+    from vllm_sm70_b200.engine import LLM
+    from vllm_sm70_b200.parallel import state
+
+    state.init(tp_size=tp, ep_size=world, backend="gloo", timeout_s=120)
+    dp = world // tp
+    llm = LLM(path, load_format="safetensors", tensor_parallel_size=tp, data_parallel_size=dp,
+              enable_expert_parallel=True, **KW)
+    assert llm.model.ep_a2a is not None and llm.model.E_local == 8 // world
+    d = rank // tp  # contiguous ranks form a replica; its ranks serve the same prompts
+    mine = list(range(d, len(_prompts()), dp))
+    toks = _greedy(llm, mine)
+    Path(f"{out_file}.{rank}").write_text(json.dumps({"ids": mine, "toks": toks}))
+    llm.shutdown()
+    state.shutdown()
+
+
+@pytest.mark.parametrize("arch", ["qwen3_moe", "qwen3_next"])
+def test_tp_x_ep_engine_equals_single_process(tmp_path, arch):
+    """TP x EP (two replicas of TP 2 on four ranks, experts over all four):
+    inside a replica the tokens are replicated, each TP rank dispatches a
+    disjoint slice through the expert exchange and the TP all-reduce after
+    the block sums the slices with the shared-expert partials; the greedy
+    tokens equal one process serving every prompt."""
+    from vllm_sm70_b200.engine import LLM
+    from vllm_sm70_b200.models.config import ModelConfig
+
+    cfg, hf = _model(arch)
+    if arch == "qwen3_next":
+        # TP 2 shards the shared expert: keep each shard at one 64-row gate/up block
+        hf = dict(hf, shared_expert_intermediate_size=128)
+        cfg = ModelConfig.from_hf(hf)
+    single = LLM(cfg, **KW)
+    path = _write(tmp_path, hf, single.model.hf_state_dict())
+    ref = _greedy(single, range(len(_prompts())))
+    world, tp = 4, 2
+    _mp.run(_tpxep_body, world, args=(tp, path, str(tmp_path / "tpep")), timeout=300)
+    for r in range(world):
+        rec = json.loads((tmp_path / f"tpep.{r}").read_text())
+        for i, t in zip(rec["ids"], rec["toks"]):
+            assert t == ref[i], (arch, r, i)

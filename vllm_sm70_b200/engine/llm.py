@@ -12,9 +12,11 @@ finishes; finished requests release their slot and blocks and waiting ones
 are admitted. Under ``torchrun`` every rank constructs the same ``LLM`` and
 runs the same schedule (decisions depend only on rank-uniform inputs).
 
-Data parallelism (``data_parallel_size = world size``, TP 1 per replica):
-every rank holds a whole replica and ``generate`` serves that rank's own
-prompts. With ``enable_expert_parallel`` an MoE model splits its experts over
+Data parallelism (``data_parallel_size`` replicas of ``tensor_parallel_size``
+ranks each, world = dp x tp; contiguous ranks form a replica): the ranks of a
+replica hold its TP shards and ``generate`` serves that replica's prompts (the
+replica's ranks pass the same prompts). TP > 1 inside a replica is the MoE
+TP x EP layout. With ``enable_expert_parallel`` an MoE model splits its experts over
 the ranks and exchanges tokens in every MoE block (``parallel/ep.py``); each
 forward is then preceded by a vote over the ranks, and a rank that runs out
 of work keeps serving idle passes until every rank is done, so all ranks take
@@ -163,13 +165,17 @@ class LLM:
         ps = pstate.get() if pstate._STATE is not None else None
         dp = int(data_parallel_size)
         if dp > 1:
-            if (tensor_parallel_size or 1) != 1:
-                raise NotImplementedError("data parallelism runs TP 1 inside each replica")
-            ep = dp if enable_expert_parallel else 1
-            if ps is None or ps.tp_size != 1 or ps.world_size != dp or ps.ep_size != ep:
-                ps = pstate.init(tp_size=1, ep_size=ep)
-            if ps.world_size != dp:
-                raise ValueError(f"data_parallel_size {dp} != world size {ps.world_size}")
+            tp = int(tensor_parallel_size or 1)
+            if tp > 1 and not enable_expert_parallel:
+                raise NotImplementedError("data parallelism with TP > 1 inside each replica is "
+                                          "the MoE TP x EP layout (enable_expert_parallel)")
+            world = dp * tp
+            ep = world if enable_expert_parallel else 1
+            if ps is None or ps.tp_size != tp or ps.world_size != world or ps.ep_size != ep:
+                ps = pstate.init(tp_size=tp, ep_size=ep)
+            if ps.world_size != world:
+                raise ValueError(f"data_parallel_size {dp} x tensor_parallel_size {tp} != "
+                                 f"world size {ps.world_size}")
         elif ps is None or (tensor_parallel_size and ps.tp_size != tensor_parallel_size):
             ps = pstate.init(tp_size=tensor_parallel_size)
         self.ps = ps

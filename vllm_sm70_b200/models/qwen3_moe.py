@@ -34,7 +34,7 @@ class Qwen3MoeModel(LlamaModel):
         super().__init__(cfg, device, dtype, ps)
         ps = self.ps
         self.ep_a2a = None
-        if ps.tp_size == 1 and ps.ep_size > 1:  # data-parallel attention, all-to-all MoE
+        if ps.ep_size > 1:  # data-parallel attention (TP inside each replica), EP over all ranks
             from ..parallel.ep import EPAllToAll
 
             self.ep_a2a = EPAllToAll(ps, cfg.num_experts, cfg.top_k)
@@ -177,16 +177,41 @@ class Qwen3MoeModel(LlamaModel):
     def _ep_moe(self, L, x, w, ids, shared, out):
         """Dispatch -> local experts -> combine (data-parallel attention). Rows
         travel in the model dtype on every rank (the idle pass's too), so the
-        byte counts of the exchange agree whatever dtype a layer hands in."""
+        byte counts of the exchange agree whatever dtype a layer hands in.
+
+        With TP inside the replica (TP x EP), the tokens are replicated over the
+        TP group: TP rank r dispatches only its slice [T r / tp, T (r+1) / tp)
+        and writes the routed result into those rows of an output that holds
+        this rank's shared-expert partial sum (or zero) everywhere; the TP
+        all-reduce that follows the block then sums the disjoint slices and the
+        shared-expert partials -- it doubles as the all-gather."""
         ep = self.ep_a2a
         dt = x.dtype
+        tp, r = self.ps.tp_size, self.ps.tp_rank
+        if tp > 1:
+            T = x.shape[0]
+            lo, hi = T * r // tp, T * (r + 1) // tp
+            y = self._ep_exchange(L, x[lo:hi], w[lo:hi], ids[lo:hi], None, None)
+            full = out if out is not None else torch.empty(T, self.cfg.hidden_size, dtype=dt,
+                                                           device=x.device)
+            if shared is not None:
+                full.copy_(shared)
+            else:
+                full.zero_()
+            if hi > lo:
+                full[lo:hi] += y.to(dt)
+            return full
+        res = self._ep_exchange(L, x, w, ids, shared, out)
+        return res if res.dtype == dt else res.to(dt)
+
+    def _ep_exchange(self, L, x, w, ids, shared, out):
+        ep = self.ep_a2a
         xr, wr, idr, plan = ep.dispatch(x.to(self.dtype), w, ids)
         yr = xr.new_empty(xr.shape[0], self.cfg.hidden_size)
         if xr.shape[0]:
             ws = self._ws(xr.shape[0]) if xr.is_cuda else None
             moe_ops.experts_forward(xr, wr, idr, L["experts"], ws, self.e_base, None, yr)
-        res = ep.combine(yr, plan, shared, out)
-        return res if res.dtype == dt else res.to(dt)
+        return ep.combine(yr, plan, shared, out)
 
     def ep_idle_pass(self) -> None:
         """A forward without local tokens: every MoE block still serves the
