@@ -158,3 +158,43 @@ def test_gdn_chunked_long_sequence(b200_ops):
     torch.cuda.synchronize()
     assert _rel(o, orf) < 3e-2
     assert _rel(st, st_ref) < 3e-2
+
+
+@pytest.mark.parametrize("chunked", [False, True])
+def test_gdn_paged_state_and_fresh_sequences(b200_ops, chunked):
+    """State slots padded apart (vLLM's paged hybrid cache: slot stride past
+    the dense [HV, DV, DK] block) and per-sequence ``has_init`` (False: start
+    from zero, still store the final state): both kernels vs the fp32 oracle
+    on a dense copy; slots nobody owns and the padding floats stay untouched."""
+    torch.manual_seed(7)
+    HK, HV, D = 2, 4, 128
+    lens = [70, 1, 33, 5]
+    T = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), device="cuda", dtype=torch.int32)
+    slots = torch.tensor([4, 1, 2, -1], device="cuda", dtype=torch.int32)
+    has_init = torch.tensor([True, False, True, False], device="cuda")
+    q = torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(T, HK * D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(T, HV * D, device="cuda", dtype=torch.bfloat16)
+    a = torch.randn(T, HV, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(T, HV, device="cuda", dtype=torch.bfloat16)
+    A_log = torch.randn(HV, device="cuda") * 0.5
+    dt = torch.randn(HV, device="cuda") * 0.5
+    blk, pad, nslot = HV * D * D, 12, 5
+    store = torch.randn(nslot * (blk + pad), device="cuda") * 0.1
+    st = store.as_strided((nslot, HV, D, D), (blk + pad, D * D, D, 1))
+    st_ref = st.clone()  # dense
+    st_ref[1].zero_()  # slot 1's sequence has no initial state
+    before = store.clone()
+    o = gdn.gdn_recurrent(q, k, v, a, b, A_log, dt, st, cu, slots, HK, HV, chunked=chunked,
+                          has_init=has_init)
+    orf = _gdn_ref_fast(q, k, v, a, b, A_log, dt, st_ref, cu, slots, HK, HV)
+    torch.cuda.synchronize()
+    tol = 3e-2 if chunked else 2e-2
+    assert _rel(o, orf) < tol
+    for s in (4, 1, 2):
+        assert _rel(st[s], st_ref[s]) < tol
+    for s in (0, 3):  # no sequence owns them
+        assert torch.equal(st[s], before.as_strided(st.shape, st.stride())[s])
+    gaps = store.view(nslot, blk + pad)[:, blk:]
+    assert torch.equal(gaps, before.view(nslot, blk + pad)[:, blk:])

@@ -467,16 +467,35 @@ void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, cons
                    const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
                    const at::Tensor& dt_bias, at::Tensor& state, const at::Tensor& cu,
                    const at::Tensor& slots, int64_t HK, int64_t HV, bool reset_state,
-                   bool write_state, bool chunked) {
+                   bool write_state, bool chunked, const c10::optional<at::Tensor>& has_init) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_BF16(k); CHECK_BF16(v); CHECK_BF16(a); CHECK_BF16(b);
   CHECK_BF16(o);
   TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
               "gdn: fp32 A_log / dt_bias");
-  TORCH_CHECK(state.scalar_type() == at::kFloat && state.is_contiguous() && state.dim() == 4,
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.dim() == 4,
               "gdn: state [slots, HV, DV, DK] fp32");
   const int DK = (int)(q.size(1) / HK), DV = (int)(v.size(1) / HV);
   TORCH_CHECK(state.size(1) == HV && state.size(2) == DV && state.size(3) == DK, "gdn: state dims");
+  // Slots may be padded apart (paged state); each slot's [HV, DV, DK] block is dense and
+  // every slot starts on 16 bytes (the kernels read the state as float4 / float2).
+  TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == DK && state.stride(1) == (int64_t)DV * DK &&
+                  state.stride(0) >= (int64_t)HV * DV * DK && state.stride(0) % 4 == 0 &&
+                  reinterpret_cast<uintptr_t>(state.data_ptr()) % 16 == 0,
+              "gdn: each state slot must be a dense 16-byte aligned [HV, DV, DK] block");
+  TORCH_CHECK(cu.scalar_type() == at::kInt && slots.scalar_type() == at::kInt &&
+                  cu.is_contiguous() && slots.is_contiguous() && cu.numel() >= slots.numel() + 1,
+              "gdn: cu [nseq + 1] / slots [nseq] int32");
+  const unsigned char* init_ptr = nullptr;
+  if (has_init.has_value()) {
+    const at::Tensor& hi = *has_init;
+    TORCH_CHECK(hi.is_cuda() && (hi.scalar_type() == at::kBool || hi.scalar_type() == at::kByte) &&
+                    hi.is_contiguous() && hi.numel() == slots.numel(),
+                "gdn: has_init [nseq] bool");
+    init_ptr = reinterpret_cast<const unsigned char*>(hi.data_ptr());
+  }
   TORCH_CHECK(a.stride(0) == b.stride(0) && a.stride(1) == 1 && b.stride(1) == 1, "gdn: a/b layout");
+  TORCH_CHECK(q.stride(1) == 1 && k.stride(1) == 1 && v.stride(1) == 1 && o.stride(1) == 1,
+              "gdn: q / k / v / o rows must have unit inner stride");
   GdnParams p{};
   p.q = (const __nv_bfloat16*)q.data_ptr(); p.k = (const __nv_bfloat16*)k.data_ptr();
   p.v = (const __nv_bfloat16*)v.data_ptr(); p.a = (const __nv_bfloat16*)a.data_ptr();
@@ -487,6 +506,8 @@ void gdn_recurrent(at::Tensor& o, const at::Tensor& q, const at::Tensor& k, cons
   p.ldab = (int)a.stride(0); p.ldo = (int)o.stride(0);
   p.HK = (int)HK; p.HV = (int)HV; p.reset_state = reset_state ? 1 : 0;
   p.write_state = write_state ? 1 : 0;
+  p.ld_state = state.stride(0);
+  p.has_init = init_ptr;
   c10::cuda::CUDAGuard g(q.device());
   if (chunked) {
     TORCH_CHECK(gdn_chunk_supported(DK, DV), "gdn: the chunked form needs DK = DV = 128");
@@ -1011,7 +1032,7 @@ TORCH_LIBRARY(_b200_C, m) {
         "Tensor cu, Tensor slots, bool silu, bool write_state=True) -> ()");
   m.def("gdn_recurrent(Tensor(a!) o, Tensor q, Tensor k, Tensor v, Tensor a, Tensor b, "
         "Tensor A_log, Tensor dt_bias, Tensor(b!) state, Tensor cu, Tensor slots, int HK, int HV, "
-        "bool reset_state, bool write_state=True, bool chunked=False) -> ()");
+        "bool reset_state, bool write_state=True, bool chunked=False, Tensor? has_init=None) -> ()");
   m.def("gated_rmsnorm(Tensor(a!) o, Tensor z, Tensor w, int H, float eps) -> ()");
   m.def("rejection_sample(Tensor(a!) out_tokens, Tensor(b!) num_out, Tensor target_logits, "
         "Tensor draft_logits, Tensor draft_ids, Tensor temperature, Tensor seeds, int offset) -> ()");

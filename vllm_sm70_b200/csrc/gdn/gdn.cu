@@ -78,8 +78,10 @@ __global__ void __launch_bounds__(DV) gdn_recurrent_kernel(const GdnParams p) {
   __shared__ float sq[DK], sk[DK];
   __shared__ float sgb[2];
   float S[DK];
-  float* st = slot >= 0 ? p.state + (((size_t)slot * p.HV + h) * DV + j) * DK : nullptr;
-  if (st && !p.reset_state) {
+  const size_t lds = p.ld_state ? (size_t)p.ld_state : (size_t)p.HV * DV * DK;
+  float* st = slot >= 0 ? p.state + (size_t)slot * lds + ((size_t)h * DV + j) * DK : nullptr;
+  const bool fresh = p.reset_state || (p.has_init != nullptr && p.has_init[s] == 0);
+  if (st && !fresh) {
 #pragma unroll
     for (int i = 0; i < DK; i += 4) {
       const float4 v = *reinterpret_cast<const float4*>(st + i);

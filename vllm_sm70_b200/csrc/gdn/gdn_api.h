@@ -14,13 +14,16 @@ struct GdnParams {
   const float* A_log;      // [HV]
   const float* dt_bias;    // [HV]
   __nv_bfloat16* o;        // [T, HV*DV]
-  float* state;            // [slots, HV, DV, DK] fp32
+  float* state;            // [slots, HV, DV, DK] fp32; slot stride ld_state
   const int* cu;           // [nseq + 1]
   const int* slots;        // [nseq] state slot (< 0: no state)
   int ldq, ldk, ldv, ldab, ldo;
   int HK, HV;
   int reset_state;         // 1: start every sequence from a zero state
   int write_state = 1;     // 0: read the state but do not store it (spec verify)
+  long long ld_state = 0;  // floats between state slots (0: dense, HV * DV * DK)
+  const unsigned char* has_init = nullptr;  // [nseq] 0: this sequence starts from a zero
+                                            // state (null: every sequence reads its slot)
 };
 
 void causal_conv1d_launch(const void* x, int ldx, const void* w, const void* bias, void* y,

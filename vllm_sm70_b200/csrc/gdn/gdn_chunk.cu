@@ -142,13 +142,15 @@ __global__ void __launch_bounds__(128, 2) gdn_chunk_kernel(const GdnParams p) {
   // State rows [32 warp, +32): S[mt][nt][4] in C-fragment layout
   // (row = 32 warp + 16 mt + g8 (+8), col = 8 nt + 2 t4 (+1)).
   float S[2][16][4];
-  float* gst = slot >= 0 ? p.state + ((size_t)slot * p.HV + h) * kD * kD : nullptr;
+  const size_t lds = p.ld_state ? (size_t)p.ld_state : (size_t)p.HV * kD * kD;
+  float* gst = slot >= 0 ? p.state + (size_t)slot * lds + (size_t)h * kD * kD : nullptr;
+  const bool fresh = p.reset_state || (p.has_init != nullptr && p.has_init[s] == 0);
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
       const int r = warp * 32 + mt * 16 + g8, c = nt * 8 + 2 * t4;
-      if (gst != nullptr && !p.reset_state) {
+      if (gst != nullptr && !fresh) {
         const float2 lo = *reinterpret_cast<const float2*>(gst + (size_t)r * kD + c);
         const float2 hi = *reinterpret_cast<const float2*>(gst + (size_t)(r + 8) * kD + c);
         S[mt][nt][0] = lo.x; S[mt][nt][1] = lo.y; S[mt][nt][2] = hi.x; S[mt][nt][3] = hi.y;

@@ -43,7 +43,7 @@ def causal_conv1d_ref(x, w, bias, state, cu, slots, silu=True):
 
 
 def gdn_recurrent_ref(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV,
-                      reset_state=False):
+                      reset_state=False, has_init=None):
     T = q.shape[0]
     DK = q.shape[1] // HK
     DV = v.shape[1] // HV
@@ -51,9 +51,10 @@ def gdn_recurrent_ref(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV,
     for s in range(len(slots)):
         t0, t1 = int(cu[s]), int(cu[s + 1])
         slot = int(slots[s])
+        fresh = reset_state or (has_init is not None and not bool(has_init[s]))
         for h in range(HV):
             hk = h // (HV // HK)
-            S = (torch.zeros(DV, DK, device=q.device) if (slot < 0 or reset_state)
+            S = (torch.zeros(DV, DK, device=q.device) if (slot < 0 or fresh)
                  else state[slot, h].clone())
             for t in range(t0, t1):
                 qt = q[t, hk * DK:(hk + 1) * DK].float()
@@ -101,22 +102,26 @@ def chunk_ok(q, v, HK, HV) -> bool:
 
 
 def gdn_recurrent(q, k, v, a, b, A_log, dt_bias, state, cu, slots, HK, HV, reset_state=False,
-                  out=None, write_state=True, chunked=False):
+                  out=None, write_state=True, chunked=False, has_init=None):
     """Gated delta rule over varlen sequences. ``chunked``: prefill through the
     chunked tensor-core kernel when it takes the shape (same state semantics);
-    decode / verify steps stay token-serial."""
+    decode / verify steps stay token-serial.
+
+    ``state`` [slots, HV, DV, DK] fp32 may have padded slots (each slot's block
+    dense, as in a paged state cache); ``has_init`` [nseq] bool: sequences with
+    False start from a zero state (and still store their final state)."""
     if out is None:
         out = torch.empty(q.shape[0], v.shape[1], dtype=torch.bfloat16, device=q.device)
     if q.is_cuda:
         _ext.require()
         torch.ops._b200_C.gdn_recurrent(out, q, k, v, a, b, A_log, dt_bias, state, cu, slots,
                                         HK, HV, reset_state, write_state,
-                                        bool(chunked) and chunk_ok(q, v, HK, HV))
+                                        bool(chunked) and chunk_ok(q, v, HK, HV), has_init)
         launch_count.add(1)
     else:
         st = state if write_state else state.clone()
         out.copy_(gdn_recurrent_ref(q, k, v, a, b, A_log, dt_bias, st, cu, slots, HK, HV,
-                                    reset_state).to(out.dtype))
+                                    reset_state, has_init).to(out.dtype))
     return out
 
 
