@@ -87,9 +87,16 @@ def can_serve(md, ssm_state: torch.Tensor, d: GdnDims) -> bool:
     return state_ok(ssm_state, d)
 
 
+def _capturing(t: torch.Tensor) -> bool:
+    return t.is_cuda and torch.cuda.is_current_stream_capturing()
+
+
 def _fp32(layer, name: str) -> torch.Tensor:
     """fp32 copy of a per-head gate parameter, refreshed when the parameter
-    is rewritten (weight loading copies into it in place)."""
+    is rewritten (weight loading copies into it in place). Never stored while
+    a CUDA graph is being captured: captured kernels do not run, so a cache
+    filled then would hold garbage for later eager calls (the graph itself
+    recomputes the cast on every replay)."""
     p = getattr(layer, name)
     if p.dtype == torch.float32:
         return p.detach()
@@ -97,7 +104,10 @@ def _fp32(layer, name: str) -> torch.Tensor:
     cache = layer.__dict__.setdefault("_b200_fp32", {})
     hit = cache.get(name)
     if hit is None or hit[0] != key:
-        hit = (key, p.detach().float().contiguous())
+        val = p.detach().float().contiguous()
+        if _capturing(val):
+            return val
+        hit = (key, val)
         cache[name] = hit
     return hit[1]
 
@@ -116,12 +126,15 @@ _CU: dict = {}
 
 
 def _decode_cu(n: int, device) -> torch.Tensor:
-    """[0, 1, ..., n] (one token per decode row), cached per device; sized
-    past any captured decode batch, so the eager profiling pass allocates it
-    before graph capture."""
+    """[0, 1, ..., n] (one token per decode row), cached per device and sized
+    past any captured decode batch (vLLM's eager warm-up pass before each
+    capture fills it); under capture a missing cache is computed in the graph
+    and not stored."""
     c = _CU.get(device)
     if c is None or c.numel() < n + 1:
         c = torch.arange(max(n + 1, 16384), dtype=torch.int32, device=device)
+        if _capturing(c):
+            return c[: n + 1]
         _CU[device] = c
     return c[: n + 1]
 
