@@ -132,10 +132,15 @@ class ExpertWeights:
                 b.reference_weight().view(self.E, self.H, self.I))
 
     def nvfp4_atoms(self):
-        """Block scales of w13 / w2 in the tensor-core atom order (cached)."""
+        """Block scales of w13 / w2 in the tensor-core atom order (cached; not
+        stored while a CUDA graph is captured -- captured kernels do not run,
+        so such a cache would be garbage for later eager calls)."""
         if getattr(self, "_atoms", None) is None:
-            self._atoms = (_q.nvfp4_sf_atoms(self.s13.view(torch.uint8)),
-                           _q.nvfp4_sf_atoms(self.s2.view(torch.uint8)))
+            atoms = (_q.nvfp4_sf_atoms(self.s13.view(torch.uint8)),
+                     _q.nvfp4_sf_atoms(self.s2.view(torch.uint8)))
+            if self.s13.is_cuda and torch.cuda.is_current_stream_capturing():
+                return atoms
+            self._atoms = atoms
         return self._atoms
 
     def bytes(self) -> int:
