@@ -406,3 +406,40 @@ def test_n_samples_ids_and_streaming_guard():
     assert all(m.request_id == o.request_id for o in outs for m in (o.more or []))
     with pytest.raises(ValueError, match="n = 1"):
         llm.generate([list(range(20, 30))], sp, on_tokens=lambda *a: None)
+
+
+def test_stop_token_retires_request_early(monkeypatch):
+    """A request whose output reaches a stop token retires at the end of that
+    decode burst instead of decoding on to ``max_tokens``: its tokens equal the
+    full run cut after the stop, it runs at most one burst of decode steps
+    past it, its slot is reused by waiting requests, and the outputs carry
+    vLLM's finish reasons ("stop" with the token id, else "length").
+    ``min_tokens`` keeps earlier stops from ending it."""
+    from vllm_sm70_b200.engine.llm import _truncate_at_stop
+
+    llm = _llm()
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (9, 14, 5, 22, 11, 8)]
+    full = llm.generate(prompts, SamplingParams(max_tokens=40, ignore_eos=True))
+    assert all(o.outputs[0].finish_reason == "length" for o in full)
+    assert full[0].outputs[0].stop_reason is None
+    t0 = full[0].output_token_ids
+    stop = t0[5]
+    k = t0.index(stop)
+    sp = SamplingParams(max_tokens=40, stop_token_ids=[stop])
+    one = llm.generate([prompts[0]], sp)[0]
+    assert one.output_token_ids == t0[: k + 1]
+    assert one.finish_reason == "stop" and one.outputs[0].stop_reason == stop
+    assert llm.last_stats.decode_steps <= 16  # one burst, not 39 steps
+    # six requests on four slots: retired slots take the waiting prompts
+    many = llm.generate(prompts, sp)
+    for f, o in zip(full, many):
+        assert o.output_token_ids == _truncate_at_stop(f.output_token_ids, sp)
+        assert o.finish_reason == ("stop" if stop in f.output_token_ids else "length")
+    # min_tokens: the first stop does not count
+    sp2 = SamplingParams(max_tokens=40, stop_token_ids=[stop], min_tokens=k + 1)
+    assert llm.generate([prompts[0]], sp2)[0].output_token_ids == _truncate_at_stop(t0, sp2)
+    # 0 turns the scan off: same tokens, every request decodes to max_tokens
+    monkeypatch.setenv("VLLM_B200_STOP_CHECK_STEPS", "0")
+    off = llm.generate([prompts[0]], sp)[0]
+    assert off.output_token_ids == t0[: k + 1] and llm.last_stats.decode_steps == 39

@@ -66,6 +66,8 @@ class _Req:
     prompt_logprobs: list | None = None
     stream_stopped: bool = False   # a stop token was streamed: nothing more follows
     aborted: bool = False          # cancelled by the caller (online mode)
+    scanned: int = 0               # output tokens already searched for a stop token
+    stop_hit: bool = False         # a stop token was generated: retire at the burst's end
 
 
 @dataclass
@@ -91,26 +93,56 @@ def _filters(p: SamplingParams) -> bool:
     return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p)
 
 
+def _can_stop(p: SamplingParams) -> bool:
+    """Whether a stop token can end the request before ``max_tokens``."""
+    return not p.ignore_eos and bool(p.stop_token_ids)
+
+
+def _stop_index(tokens, p: SamplingParams, start: int = 0) -> int | None:
+    """Index of the first stop token at or after ``start`` that may end the
+    output (its count exceeds ``min_tokens``), or None."""
+    if not _can_stop(p):
+        return None
+    stops = set(p.stop_token_ids)
+    for i in range(max(start, p.min_tokens), len(tokens)):
+        if tokens[i] in stops:
+            return i
+    return None
+
+
 def _truncate_at_stop(tokens: list[int], p: SamplingParams) -> list[int]:
     """Cut the output after the first stop token (kept, like vLLM's token ids)
     unless the request ignores EOS. Decode runs whole bursts on the device, so
-    tokens past a stop are computed and dropped here."""
-    if p.ignore_eos or not p.stop_token_ids:
-        return tokens
-    stops = set(p.stop_token_ids)
-    for i, t in enumerate(tokens):
-        if t in stops and i + 1 > p.min_tokens:
-            return tokens[: i + 1]
-    return tokens
+    tokens of the burst past a stop are computed and dropped here."""
+    i = _stop_index(tokens, p)
+    return tokens if i is None else tokens[: i + 1]
+
+
+def _finish_reason(tokens: list[int], p: SamplingParams, text_cut: str | None):
+    """vLLM's (finish_reason, stop_reason) of a complete output: ("stop", the
+    stop token id or the stop string) when a stop ended it, else ("length",
+    None)."""
+    if text_cut is not None:
+        return "stop", text_cut
+    if tokens and _can_stop(p) and len(tokens) > p.min_tokens \
+            and tokens[-1] in set(p.stop_token_ids):
+        return "stop", int(tokens[-1])
+    return "length", None
 
 
 def _cut_at_stop_string(tokens: list[int], p: SamplingParams, decode) -> tuple[list[int], str]:
     """(tokens, text) cut at the first stop string that ends after
     ``min_tokens`` tokens: the tokens up to the one that completes it, the
     text up to its start (or its end with ``include_stop_str_in_output``)."""
+    return _match_stop_string(tokens, p, decode)[:2]
+
+
+def _match_stop_string(tokens: list[int], p: SamplingParams, decode):
+    """:func:`_cut_at_stop_string` plus the stop string that matched (None
+    when none did)."""
     text = decode(tokens)
     if not p.stop:
-        return tokens, text
+        return tokens, text, None
     best = None
     for st in p.stop:
         at = text.find(st) if st else -1
@@ -128,13 +160,13 @@ def _cut_at_stop_string(tokens: list[int], p: SamplingParams, decode) -> tuple[l
             k = lo
             if k > p.min_tokens:
                 if best is None or at < best[0]:
-                    best = (at, end, k)
+                    best = (at, end, k, st)
                 break
             at = text.find(st, at + 1)
     if best is None:
-        return tokens, text
-    at, end, k = best
-    return tokens[:k], text[: end if p.include_stop_str_in_output else at]
+        return tokens, text, None
+    at, end, k, st = best
+    return tokens[:k], text[: end if p.include_stop_str_in_output else at], st
 
 
 class LLM:
@@ -465,8 +497,10 @@ class LLM:
 
     @staticmethod
     def _output(r: "_Req") -> RequestOutput:
-        return RequestOutput(r.rid, r.prompt.tolist(), r.out, True, logprobs=r.logprobs,
-                             prompt_logprobs=r.prompt_logprobs)
+        o = RequestOutput(r.rid, r.prompt.tolist(), r.out, True, logprobs=r.logprobs,
+                          prompt_logprobs=r.prompt_logprobs)
+        o.finish_reason, o.stop_reason = _finish_reason(r.out, r.params, None)
+        return o
 
     def _logprobs_of(self, r: "_Req") -> tuple[list | None, list | None]:
         """(output, prompt) log-prob lists of a finished request that asked
@@ -598,12 +632,10 @@ class LLM:
             for r, row in zip(rs, rows_h):
                 upto = min(r.generated, r.params.max_tokens)
                 new = [] if r.stream_stopped else row[r.streamed:upto].tolist()
-                if new and not r.params.ignore_eos and r.params.stop_token_ids:
-                    stops = set(r.params.stop_token_ids)
-                    for j, t in enumerate(new):
-                        if t in stops:
-                            new, r.stream_stopped = new[: j + 1], True
-                            break
+                if new:
+                    j = _stop_index(row[:upto].tolist(), r.params, r.streamed)
+                    if j is not None:
+                        new, r.stream_stopped = new[: j + 1 - r.streamed], True
                 r.streamed = upto
                 if new or final:
                     on_tokens(r.rid, new, final)
@@ -622,6 +654,32 @@ class LLM:
         pending_first: list[tuple[object, list[_Req]]] = []
         decode_events: list[tuple[object, list[_Req], int]] = []
         prefill_spans: list[tuple[object, object]] = []
+        stop_every = max(0, int(envs.get("VLLM_B200_STOP_CHECK_STEPS")))
+
+        def scan_stops(rs) -> None:
+            """Search the not-yet-scanned output tokens of requests that can
+            end on a stop token (one device-to-host copy of the new columns);
+            a hit retires the request now instead of at ``max_tokens``, which
+            frees its slot and KV blocks for waiting requests. Every rank sees
+            the same tokens, so TP ranks decide alike."""
+            rs = [r for r in rs if not r.stop_hit and _can_stop(r.params)
+                  and r.scanned < min(r.generated, r.params.max_tokens)]
+            if not stop_every or not rs:
+                return
+            lo = min(r.scanned for r in rs)
+            hi = max(min(r.generated, r.params.max_tokens) for r in rs)
+            idx = torch.tensor([r.slot for r in rs], device=self.device)
+            cols = runner.out_tokens.index_select(0, idx)[:, lo:hi].cpu()
+            for r, row in zip(rs, cols):
+                upto = min(r.generated, r.params.max_tokens)
+                first = max(r.scanned, r.params.min_tokens)
+                stops = set(r.params.stop_token_ids)
+                if any(int(t) in stops for t in row[first - lo:upto - lo].tolist()):
+                    r.stop_hit = True
+                r.scanned = upto
+
+        def finished(r) -> bool:
+            return r.generated >= r.params.max_tokens or r.aborted or r.stop_hit
 
         def cancel(rid) -> None:
             """Abort a request wherever it is: queued, mid-prefill or decoding
@@ -762,7 +820,8 @@ class LLM:
                     break  # one chunk, then a decode burst of the running requests
             # ---- decode until the next request finishes
             live = [r for r in running if not r.done]
-            finished_now = [r for r in live if r.generated >= r.params.max_tokens or r.aborted]
+            scan_stops(live)  # a first token (from prefill) may already stop
+            finished_now = [r for r in live if finished(r)]
             if not live:
                 continue  # (interleaved) only prompts mid-prefill
             if not finished_now and self.spec_k:
@@ -775,7 +834,8 @@ class LLM:
                 stats.spec_slots += len(live)
                 if self.spec_hook is not None:
                     self.spec_hook(len(live), sum(int(n[r.slot]) for r in live))
-                finished_now = [r for r in live if r.generated >= r.params.max_tokens or r.aborted]
+                scan_stops(live)
+                finished_now = [r for r in live if finished(r)]
                 if cuda and finished_now:
                     e = ev()
                     e.record()
@@ -784,6 +844,8 @@ class LLM:
                 steps = min(r.params.max_tokens - r.generated for r in live)
                 if stream_interval > 0:
                     steps = min(steps, stream_interval)
+                if stop_every and any(_can_stop(r.params) for r in live):
+                    steps = min(steps, stop_every)
                 n_rows = max(r.slot for r in live) + 1
                 if self.watchdog is not None:
                     self.watchdog.check()
@@ -793,7 +855,8 @@ class LLM:
                 stats.decode_steps += steps
                 for r in live:
                     r.generated += steps
-                finished_now = [r for r in live if r.generated >= r.params.max_tokens or r.aborted]
+                scan_stops(live)
+                finished_now = [r for r in live if finished(r)]
                 if cuda:
                     e = ev()
                     e.record()
@@ -859,8 +922,10 @@ class LLM:
         if tok is not None:  # vLLM's RequestOutput.text (and stop strings)
             dec = lambda ids: tok.decode(ids, skip_special_tokens=True)  # noqa: E731
             for o, r in zip(outs, reqs):
-                o.output_token_ids, o.text = _cut_at_stop_string(o.output_token_ids, r.params,
-                                                                 dec)
+                o.output_token_ids, o.text, hit = _match_stop_string(o.output_token_ids,
+                                                                     r.params, dec)
+                if hit is not None:
+                    o.finish_reason, o.stop_reason = "stop", hit
         elif any(r.params.stop for r in reqs):
             raise ValueError("stop strings need a tokenizer (LLM(..., tokenizer=...))")
         return outs

@@ -38,6 +38,7 @@ class CompletionOutput:
     token_ids: list[int]
     logprobs: list | None = None
     finish_reason: str | None = None
+    stop_reason: int | str | None = None
 
 
 @dataclass
@@ -55,6 +56,10 @@ class RequestOutput:
     prompt_logprobs: list | None = None
     text: str | None = None        # the decoded output, when the engine has a tokenizer
     more: list | None = None       # samples 2..n (RequestOutput each) when n > 1
+    # vLLM's reasons: "stop" (a stop token or string ended the output; stop_reason
+    # is that token id or string) or "length" (max_tokens reached)
+    finish_reason: str | None = None
+    stop_reason: int | str | None = None
 
     @property
     def outputs(self) -> list[CompletionOutput]:
@@ -62,6 +67,7 @@ class RequestOutput:
         entry per sample."""
         out = []
         for i, o in enumerate([self] + list(self.more or [])):
-            reason = "abort" if o.error == "aborted" else ("error" if o.error else None)
-            out.append(CompletionOutput(i, o.text, o.output_token_ids, o.logprobs, reason))
+            reason = "abort" if o.error == "aborted" else ("error" if o.error else o.finish_reason)
+            out.append(CompletionOutput(i, o.text, o.output_token_ids, o.logprobs, reason,
+                                        None if o.error else o.stop_reason))
         return out

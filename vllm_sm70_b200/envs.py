@@ -131,6 +131,10 @@ _reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
 _reg("VLLM_B200_CUDA_GRAPHS", "kill", True, "runtime", "Capture decode steps in CUDA graphs.")
 _reg("VLLM_B200_GRAPH_MAX_BS", "int", 512, "runtime", "Largest captured decode batch.")
 _reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tuning.")
+_reg("VLLM_B200_STOP_CHECK_STEPS", "int", 16, "runtime",
+     "Longest decode burst while a running request can end on a stop token: its new "
+     "tokens are checked after each burst and a stopped request retires (0 = run "
+     "every request to max_tokens and cut the output at the stop afterwards).")
 _reg("VLLM_B200_GEMM_LIBRARY", "optin", False, "runtime",
      "Baseline switch, off by default: let the warm-up tuner route a plain bf16 GEMM shape to "
      "the vendor library (cuBLAS) when it measures faster than every tcgen05 plan. With it off "
