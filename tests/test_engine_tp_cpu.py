@@ -55,6 +55,15 @@ def _minp():
     return SamplingParams(max_tokens=6, temperature=1.0, min_p=0.5, seed=9)
 
 
+def _biased():
+    """logit_bias and allowed_token_ids with ids in both vocab shards (vocab
+    1024 at TP2: [0, 512) and [512, 1024))."""
+    from vllm_sm70_b200.engine import SamplingParams
+
+    return SamplingParams(max_tokens=6, logit_bias={7: 3.0, 700: 5.0, 1000: -2.0},
+                          allowed_token_ids=[3, 7, 100, 511, 512, 700, 1000, 1023])
+
+
 def _pen_body(rank, world, path, out_file):
     from pathlib import Path
 
@@ -66,6 +75,7 @@ def _pen_body(rank, world, path, out_file):
     sp = SamplingParams(max_tokens=6, repetition_penalty=1.7, frequency_penalty=0.5)
     toks = [o.output_token_ids for o in llm.generate(_prompts(), sp)]
     toks += [o.output_token_ids for o in llm.generate(_prompts(), _minp())]
+    toks += [o.output_token_ids for o in llm.generate(_prompts(), _biased())]
     if rank == 0:
         Path(out_file).write_text(json.dumps(toks))
     llm.shutdown()
@@ -73,9 +83,9 @@ def _pen_body(rank, world, path, out_file):
 
 
 def test_tp2_penalties_equal_tp1_cpu(tmp_path):
-    """Sampling penalties and min_p on vocab-parallel logit shards (each rank
-    rewrites its own slice; min_p's row maximum is reduced over the shards)
-    give the TP1 tokens."""
+    """Sampling penalties, min_p, logit_bias and allowed_token_ids on
+    vocab-parallel logit shards (each rank rewrites its own slice; min_p's row
+    maximum is reduced over the shards) give the TP1 tokens."""
     from vllm_sm70_b200.engine import LLM, SamplingParams
 
     _checkpoint(tmp_path)
@@ -85,4 +95,7 @@ def test_tp2_penalties_equal_tp1_cpu(tmp_path):
     sp = SamplingParams(max_tokens=6, repetition_penalty=1.7, frequency_penalty=0.5)
     want = [o.output_token_ids for o in one.generate(_prompts(), sp)]
     want += [o.output_token_ids for o in one.generate(_prompts(), _minp())]
+    biased = [o.output_token_ids for o in one.generate(_prompts(), _biased())]
+    assert all(set(t) <= set(_biased().allowed_token_ids) for t in biased)
+    want += biased
     assert json.loads(out_file.read_text()) == want

@@ -440,3 +440,15 @@ def test_health_reports_a_dead_engine():
             assert r.status_code == 500
             h = c.get("/health")
             assert h.status_code == 503 and "device lost" in h.json()["error"]
+
+
+def test_logit_bias_request_fields():
+    """OpenAI ``logit_bias`` (string token ids, bias clamped to [-100, 100])
+    and vLLM's ``allowed_token_ids`` reach the sampling parameters."""
+    from vllm_sm70_b200.entrypoints.openai_server import _params
+
+    sp = _params({"logit_bias": {"5": 3.5, "9": -250}, "allowed_token_ids": [5, 9, 11]}, None)
+    assert sp.logit_bias == {5: 3.5, 9: -100.0}
+    assert sp.allowed_token_ids == [5, 9, 11]
+    sp = _params({}, None)
+    assert sp.logit_bias is None and sp.allowed_token_ids is None

@@ -4,6 +4,7 @@ distribution proportional to softmax over the kept set), and the engine
 routes requests with top-k / top-p through it: top_k = 1 and a vanishing
 top_p reduce to greedy decoding, a fixed seed is reproducible, and greedy
 requests batched with filtered ones are unchanged."""
+import pytest
 import torch
 
 from vllm_sm70_b200.engine import SamplingParams
@@ -141,3 +142,51 @@ def test_min_p_keeps_only_likely_tokens():
     greedy = [o.output_token_ids for o in llm.generate(_prompts(), SamplingParams(max_tokens=5))]
     top = SamplingParams(max_tokens=5, temperature=2.0, min_p=1.0, seed=3)
     assert [o.output_token_ids for o in llm.generate(_prompts(), top)] == greedy
+
+
+def test_logit_bias_and_allowed_token_ids():
+    """``allowed_token_ids`` limits greedy decoding to the set and
+    ``logit_bias`` is added to the logits (vLLM's order: mask, then bias, then
+    penalties); both equal a dense reference that applies them, requests
+    without them in the same batch are unchanged, a large bias forces its
+    token, and ids outside the vocabulary are refused."""
+    from ._llama_ref import llama_logits
+
+    llm = _llm()
+    p = _prompts()[1]
+    plain = llm.generate([p], SamplingParams(max_tokens=6))[0].output_token_ids
+
+    def dense(n, allowed=None, bias=None, rep=1.0):
+        ids, out = p.clone(), []
+        for _ in range(n):
+            lg = llama_logits(llm.model, ids)[-1].clone()
+            if allowed is not None:
+                keep = torch.zeros_like(lg, dtype=torch.bool)
+                keep[allowed] = True
+                lg = torch.where(keep, lg, torch.full_like(lg, float("-inf")))
+            for t, v in (bias or {}).items():
+                lg[t] += v
+            seen = torch.zeros_like(lg, dtype=torch.bool)
+            seen[ids] = True
+            lg = torch.where(seen, torch.where(lg > 0, lg / rep, lg * rep), lg)
+            t = int(lg.argmax())
+            out.append(t)
+            ids = torch.cat([ids, torch.tensor([t])])
+        return out
+
+    allowed = [3, 17, 42, 99, 250, 511]
+    got = llm.generate([p, p], [SamplingParams(max_tokens=6, allowed_token_ids=allowed),
+                                SamplingParams(max_tokens=6)])
+    assert got[0].output_token_ids == dense(6, allowed=allowed)
+    assert set(got[0].output_token_ids) <= set(allowed)
+    assert got[1].output_token_ids == plain
+    bias = {plain[0]: -1e4, 77: 3.0}
+    sp = SamplingParams(max_tokens=6, logit_bias=bias, repetition_penalty=1.5)
+    got = llm.generate([p], sp)[0].output_token_ids
+    assert got == dense(6, bias=bias, rep=1.5) and plain[0] not in got
+    forced = llm.generate([p], SamplingParams(max_tokens=3, logit_bias={123: 1e4}))[0]
+    assert forced.output_token_ids == [123] * 3
+    for bad in (dict(allowed_token_ids=[512]), dict(allowed_token_ids=[]),
+                dict(logit_bias={-1: 1.0})):
+        with pytest.raises(ValueError):
+            llm.generate([p], SamplingParams(max_tokens=2, **bad))

@@ -84,12 +84,24 @@ class GenerateStats:
 
 def _penalized(p: SamplingParams) -> bool:
     return (p.repetition_penalty != 1.0 or p.presence_penalty != 0.0
-            or p.frequency_penalty != 0.0 or p.min_p > 0.0)
+            or p.frequency_penalty != 0.0 or p.min_p > 0.0 or bool(p.logit_bias)
+            or p.allowed_token_ids is not None)
+
+
+def _check_token_ids(p: SamplingParams, vocab: int) -> None:
+    """vLLM's argument checks of the token-id fields of a request."""
+    if p.allowed_token_ids is not None:
+        if not p.allowed_token_ids:
+            raise ValueError("allowed_token_ids is empty")
+        if any(not 0 <= int(t) < vocab for t in p.allowed_token_ids):
+            raise ValueError(f"allowed_token_ids out of the vocabulary [0, {vocab})")
+    if p.logit_bias and any(not 0 <= int(t) < vocab for t in p.logit_bias):
+        raise ValueError(f"logit_bias token id out of the vocabulary [0, {vocab})")
 
 
 def _filters(p: SamplingParams) -> bool:
     """Whether the request needs the candidate sampling path (top-k / top-p,
-    or sampling penalties)."""
+    sampling penalties, min_p, logit_bias or allowed_token_ids)."""
     return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p)
 
 
@@ -565,9 +577,12 @@ class LLM:
                   else [sampling_params] * len(prompts))
         if any(p.n > 1 for p in params) and feed is None:
             return self._generate_n(prompts, params, collect_stats, on_tokens, stream_interval)
+        for p in params:
+            _check_token_ids(p, self.cfg.vocab_size)
         filtering = any(_filters(p) for p in params)
         if filtering and self.spec_k:
-            raise NotImplementedError("top-k / top-p with speculative decoding")
+            raise NotImplementedError("top-k / top-p / penalties / logit_bias / "
+                                      "allowed_token_ids with speculative decoding")
         reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
         runner = self.runner
         runner.filtering = filtering
@@ -710,9 +725,15 @@ class LLM:
                     cancel(item[1])
                     continue
                 rid, ids, sp = item
+                try:
+                    _check_token_ids(sp, self.cfg.vocab_size)
+                except ValueError as e:  # fail this request alone
+                    on_finish(RequestOutput(rid, list(ids), [], True, error=str(e)))
+                    continue
                 if _filters(sp):
                     if self.spec_k:
-                        raise NotImplementedError("top-k / top-p with speculative decoding")
+                        raise NotImplementedError("top-k / top-p / penalties / logit_bias / "
+                                                  "allowed_token_ids with speculative decoding")
                     runner.filtering = True
                     runner.penalties = runner.penalties or _penalized(sp)
                 waiting.append(_Req(rid, torch.as_tensor(ids, dtype=torch.int64), sp))
@@ -759,7 +780,8 @@ class LLM:
                                     seed & 0x7FFFFFFFFFFFFFFF, sp.top_k, sp.top_p,
                                     sp.repetition_penalty, sp.presence_penalty,
                                     sp.frequency_penalty,
-                                    r.prompt if runner.penalties else None, sp.min_p)
+                                    r.prompt if runner.penalties else None, sp.min_p,
+                                    sp.logit_bias, sp.allowed_token_ids)
                 admitted.append(r)
             if not admitted and not running and not prefilling:
                 if not waiting:  # (online) every new request was refused above

@@ -74,6 +74,11 @@ class ModelRunner:
         self.freq_pen = torch.zeros(B, dtype=torch.float32, device=dev)
         self.min_p = torch.zeros(B, dtype=torch.float32, device=dev)
         self.prompt_ids: torch.Tensor | None = None  # [B, max_model_len], -1 padded
+        # logit_bias / allowed_token_ids: per-slot sparse rows (token id, -1 =
+        # unused), allocated on first use and widened to the longest request
+        self.bias_ids: torch.Tensor | None = None    # [B, nb] int64
+        self.bias_vals: torch.Tensor | None = None   # [B, nb] fp32
+        self.allow_ids: torch.Tensor | None = None   # [B, na] int64; a row of -1 = no limit
         self.penalties = False
         # Decode graphs always sample through the temperature path: rows with
         # T <= 0 reduce to the exact greedy argmax.
@@ -158,15 +163,34 @@ class ModelRunner:
         self.seq_lens[:b] += act
 
     def _penalizer(self, rows: torch.Tensor):
-        """Logit rewrite of the sampling penalties for batch slots ``rows``
-        (None when no request in flight uses them): repetition over prompt and
-        output tokens (divide positive logits, multiply negative ones),
-        presence and frequency over output tokens (subtract per occurrence)."""
+        """Logit rewrite for batch slots ``rows`` (None when no request in
+        flight needs one), in vLLM's order: ``allowed_token_ids`` (every other
+        token to -inf), ``logit_bias`` (added), then the penalties --
+        repetition over prompt and output tokens (divide positive logits,
+        multiply negative ones), presence and frequency over output tokens
+        (subtract per occurrence) -- and last the ``min_p`` cut."""
         if not self.penalties:
             return None
 
+        def sparse(ids_t, vals, vs, V):
+            """Dense [b, V] sum of per-row (token id, value) pairs that fall
+            in this rank's vocab shard [vs, vs + V)."""
+            ids = ids_t.index_select(0, rows)
+            loc = ids - vs
+            ok = (ids >= 0) & (loc >= 0) & (loc < V)
+            out = torch.zeros(ids.shape[0], V, device=ids.device)
+            out.scatter_add_(1, loc.clamp(0, V - 1), torch.where(ok, vals, torch.zeros_like(vals)))
+            return out
+
         def apply(lg: torch.Tensor, vs: int) -> torch.Tensor:
             b, V = lg.shape
+            if self.allow_ids is not None:
+                a = self.allow_ids.index_select(0, rows)
+                keep = sparse(self.allow_ids, torch.ones(a.shape, device=lg.device), vs, V) > 0
+                limited = (a >= 0).any(1)
+                lg = torch.where(limited[:, None] & ~keep, torch.full_like(lg, float("-inf")), lg)
+            if self.bias_ids is not None:
+                lg = lg + sparse(self.bias_ids, self.bias_vals.index_select(0, rows), vs, V)
             outs = self.out_tokens.index_select(0, rows).long()
             pos = self.out_pos.index_select(0, rows)
             ok = torch.arange(outs.shape[1], device=lg.device)[None, :] < pos[:, None]
@@ -261,7 +285,9 @@ class ModelRunner:
     def set_sampling(self, slot: int, temperature: float, seed: int, top_k: int = -1,
                      top_p: float = 1.0, repetition_penalty: float = 1.0,
                      presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
-                     prompt: torch.Tensor | None = None, min_p: float = 0.0) -> None:
+                     prompt: torch.Tensor | None = None, min_p: float = 0.0,
+                     logit_bias: dict | None = None,
+                     allowed_token_ids: list | None = None) -> None:
         self.temperature[slot] = float(temperature)
         self.seeds[slot] = int(seed)
         self.top_k[slot] = int(top_k) if top_k > 0 else -1
@@ -270,12 +296,42 @@ class ModelRunner:
         self.pres_pen[slot] = float(presence_penalty)
         self.freq_pen[slot] = float(frequency_penalty)
         self.min_p[slot] = float(min_p)
+        bias = sorted((int(t), float(v)) for t, v in (logit_bias or {}).items())
+        self.bias_ids, self.bias_vals = self._sparse_row(
+            self.bias_ids, self.bias_vals, slot, [t for t, _ in bias], [v for _, v in bias])
+        self.allow_ids, _ = self._sparse_row(self.allow_ids, None, slot,
+                                             sorted({int(t) for t in allowed_token_ids or []}))
         if prompt is not None:  # the prompt's tokens count for the repetition penalty
             if self.prompt_ids is None:
                 self.prompt_ids = torch.full((self.B, self.max_model_len), -1, dtype=torch.int64,
                                              device=self.device)
             self.prompt_ids[slot].fill_(-1)
             self.prompt_ids[slot, : prompt.numel()] = prompt.to(self.device)
+
+    def _sparse_row(self, ids_t, vals_t, slot: int, ids: list, vals: list | None = None):
+        """Write ``slot``'s row of a per-slot sparse table (ids padded with -1,
+        values with 0), allocating the table on first use and widening it to
+        the longest row; a slot without entries only clears its row."""
+        n = len(ids)
+        if ids_t is None and n == 0:
+            return ids_t, vals_t
+        if ids_t is None or ids_t.shape[1] < n:
+            w = max(n, 2 * (0 if ids_t is None else ids_t.shape[1]), 8)
+            new_ids = torch.full((self.B, w), -1, dtype=torch.int64, device=self.device)
+            new_vals = torch.zeros(self.B, w, dtype=torch.float32, device=self.device)
+            if ids_t is not None:
+                new_ids[:, : ids_t.shape[1]] = ids_t
+                if vals_t is not None:
+                    new_vals[:, : vals_t.shape[1]] = vals_t
+            ids_t, vals_t = new_ids, (new_vals if vals is not None else None)
+        ids_t[slot].fill_(-1)
+        if n:
+            ids_t[slot, :n] = torch.tensor(ids, dtype=torch.int64).to(self.device)
+        if vals_t is not None:
+            vals_t[slot].zero_()
+            if n:
+                vals_t[slot, :n] = torch.tensor(vals, dtype=torch.float32).to(self.device)
+        return ids_t, vals_t
 
     def prefill(self, pieces: list[tuple[int, torch.Tensor, int, bool, int]]) -> None:
         """``pieces``: (slot, token ids [n] int64 CPU, ctx_start, is_last, total_len)."""

@@ -22,6 +22,8 @@ class SamplingParams:
     repetition_penalty: float = 1.0      # > 1 discourages prompt / output tokens
     presence_penalty: float = 0.0        # subtracted once per token present in the output
     frequency_penalty: float = 0.0       # subtracted per occurrence in the output
+    logit_bias: dict[int, float] | None = None   # {token id: added to its logit}
+    allowed_token_ids: list[int] | None = None   # only these tokens can be sampled
     logprobs: int | None = None          # per output token: its log-prob + the top-N
     prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 

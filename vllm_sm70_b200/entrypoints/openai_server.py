@@ -392,6 +392,10 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
         stop_ids.append(int(eos))
     top_k = body.get("top_k")
     mt = body.get("max_completion_tokens", body.get("max_tokens"))
+    bias = body.get("logit_bias")
+    if bias is not None:  # OpenAI: {"token id": bias in [-100, 100]}
+        bias = {int(t): min(100.0, max(-100.0, float(v))) for t, v in dict(bias).items()}
+    allowed = body.get("allowed_token_ids")  # vLLM's extra field
     return SamplingParams(max_tokens=16 if mt is None else int(mt),
                           logprobs=n_lp, prompt_logprobs=prompt_lp,
                           temperature=float(body.get("temperature", 1.0)),
@@ -401,7 +405,9 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           min_p=float(body.get("min_p", 0.0)),
                           presence_penalty=float(body.get("presence_penalty", 0.0)),
                           frequency_penalty=float(body.get("frequency_penalty", 0.0)),
-                          seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids)
+                          seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids,
+                          logit_bias=bias or None,
+                          allowed_token_ids=None if allowed is None else [int(t) for t in allowed])
 
 
 def _apply_stop_strings(text: str, stop) -> tuple[str, bool]:
