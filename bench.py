@@ -36,6 +36,7 @@ N_REQ, PROMPT, OUT = 256, 1024, 256  # the headline workload; --requests/--promp
 # --output-len exist only for profiling runs and mark the JSON line "profiling"
 BASELINE_VALUE = None  # no published number exists for this config
 PRESET, TEMPERATURE, SPEC_K = "llama-3.1-8b", 0.0, 0
+PROFILING = False  # set by --requests / --prompt-len / --output-len
 
 # The other benchmark configurations of this project (--config): preset, workload, sampling.
 WORKLOADS = {
@@ -243,6 +244,8 @@ def run_ours(args) -> dict:
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
+    if PROFILING:
+        res["profiling"] = True
     if rank == 0:
         print(json.dumps(res), flush=True)
     llm.shutdown()
@@ -438,7 +441,7 @@ def main(argv=None):
     if args.verbose:
         import logging
         logging.basicConfig(level=logging.INFO, stream=sys.stderr)
-    global N_REQ, PROMPT, OUT, MODEL, PRESET, TEMPERATURE, SPEC_K
+    global N_REQ, PROMPT, OUT, MODEL, PRESET, TEMPERATURE, SPEC_K, PROFILING
     wl = WORKLOADS[args.config]
     N_REQ, PROMPT, OUT, MODEL = wl["requests"], wl["prompt"], wl["output"], wl["model"]
     PRESET, TEMPERATURE, SPEC_K = wl["preset"], wl["temperature"], wl["spec_k"]
@@ -450,6 +453,7 @@ def main(argv=None):
         N_REQ = args.requests or N_REQ
         PROMPT = args.prompt_len or PROMPT
         OUT = args.output_len or OUT
+        PROFILING = True
         print("warning: non-default workload; the JSON line is for profiling only",
               file=sys.stderr)
     if args.warmup < 3:

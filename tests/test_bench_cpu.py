@@ -23,3 +23,19 @@ def test_online_mode_tiny(monkeypatch, capsys):
     assert res["requests"] == 6 and res["profiling"] is True
     assert res["value"] > 0 and res["p50_ttft_ms"] is not None and res["p90_tpot_ms"] is not None
     assert '"metric": "online serving' in capsys.readouterr().out
+
+
+def test_profiling_flags_mark_the_line(monkeypatch):
+    """--requests / --prompt-len / --output-len change the workload and mark
+    the JSON line as profiling; the default headline workload does not."""
+    import bench
+
+    for name in ("N_REQ", "PROMPT", "OUT", "MODEL", "PRESET", "TEMPERATURE", "SPEC_K",
+                 "PROFILING"):  # main() rewrites these module globals: restore them after
+        monkeypatch.setattr(bench, name, getattr(bench, name))
+    seen = []
+    monkeypatch.setattr(bench, "run_ours", lambda args: seen.append(
+        (bench.N_REQ, bench.PROMPT, bench.OUT, bench.PROFILING)))
+    bench.main(["--steps", "1"])
+    bench.main(["--requests", "8", "--output-len", "4"])
+    assert seen == [(256, 1024, 256, False), (8, 1024, 4, True)]
