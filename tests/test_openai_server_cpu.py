@@ -451,4 +451,5 @@ def test_logit_bias_request_fields():
     assert sp.logit_bias == {5: 3.5, 9: -100.0}
     assert sp.allowed_token_ids == [5, 9, 11]
     sp = _params({}, None)
-    assert sp.logit_bias is None and sp.allowed_token_ids is None
+    assert sp.logit_bias is None and sp.allowed_token_ids is None and sp.min_tokens == 0
+    assert _params({"min_tokens": 3}, None).min_tokens == 3

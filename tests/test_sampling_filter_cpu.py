@@ -190,3 +190,29 @@ def test_logit_bias_and_allowed_token_ids():
                 dict(logit_bias={-1: 1.0})):
         with pytest.raises(ValueError):
             llm.generate([p], SamplingParams(max_tokens=2, **bad))
+
+
+def test_min_tokens_masks_stop_tokens():
+    """vLLM's ``min_tokens``: the stop tokens cannot be sampled until that
+    many output tokens exist (a dense reference that masks them agrees), and
+    the first stop after that ends the request."""
+    from ._llama_ref import llama_logits
+
+    llm = _llm()
+    p = _prompts()[0]
+    plain = llm.generate([p], SamplingParams(max_tokens=12, ignore_eos=True))[0].output_token_ids
+    stop = plain[0]
+    sp = SamplingParams(max_tokens=12, stop_token_ids=[stop], min_tokens=4)
+    got = llm.generate([p, p], [sp, SamplingParams(max_tokens=12, ignore_eos=True)])
+    ids, want = p.clone(), []
+    for i in range(12):
+        lg = llama_logits(llm.model, ids)[-1].clone()
+        if i < 4:
+            lg[stop] = float("-inf")
+        t = int(lg.argmax())
+        want.append(t)
+        ids = torch.cat([ids, torch.tensor([t])])
+        if t == stop:
+            break
+    assert got[0].output_token_ids == want and stop not in want[:4]
+    assert got[1].output_token_ids == plain

@@ -82,10 +82,15 @@ class GenerateStats:
     spec_slots: int = 0    # (row, step) pairs; spec_tokens / spec_slots = tokens per step
 
 
-def _penalized(p: SamplingParams) -> bool:
+def _penalized(p: SamplingParams, spec: bool = False) -> bool:
+    """Whether the request rewrites its logits before sampling. ``min_tokens``
+    masks the stop tokens until that many tokens exist (vLLM's rule), except
+    under speculative decoding, where stops before ``min_tokens`` are only
+    ignored."""
     return (p.repetition_penalty != 1.0 or p.presence_penalty != 0.0
             or p.frequency_penalty != 0.0 or p.min_p > 0.0 or bool(p.logit_bias)
-            or p.allowed_token_ids is not None)
+            or p.allowed_token_ids is not None
+            or (not spec and p.min_tokens > 0 and _can_stop(p)))
 
 
 def _check_token_ids(p: SamplingParams, vocab: int) -> None:
@@ -99,10 +104,10 @@ def _check_token_ids(p: SamplingParams, vocab: int) -> None:
         raise ValueError(f"logit_bias token id out of the vocabulary [0, {vocab})")
 
 
-def _filters(p: SamplingParams) -> bool:
+def _filters(p: SamplingParams, spec: bool = False) -> bool:
     """Whether the request needs the candidate sampling path (top-k / top-p,
     sampling penalties, min_p, logit_bias or allowed_token_ids)."""
-    return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p)
+    return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p, spec)
 
 
 def _can_stop(p: SamplingParams) -> bool:
@@ -579,14 +584,15 @@ class LLM:
             return self._generate_n(prompts, params, collect_stats, on_tokens, stream_interval)
         for p in params:
             _check_token_ids(p, self.cfg.vocab_size)
-        filtering = any(_filters(p) for p in params)
+        spec = bool(self.spec_k)
+        filtering = any(_filters(p, spec) for p in params)
         if filtering and self.spec_k:
             raise NotImplementedError("top-k / top-p / penalties / logit_bias / "
                                       "allowed_token_ids with speculative decoding")
         reqs = [_Req(i, prompts[i], params[i]) for i in range(len(prompts))]
         runner = self.runner
         runner.filtering = filtering
-        runner.penalties = any(_penalized(p) for p in params)
+        runner.penalties = any(_penalized(p, spec) for p in params)
         try:
             return self._generate(reqs, on_tokens, int(stream_interval), feed, on_finish)
         finally:
@@ -730,12 +736,12 @@ class LLM:
                 except ValueError as e:  # fail this request alone
                     on_finish(RequestOutput(rid, list(ids), [], True, error=str(e)))
                     continue
-                if _filters(sp):
+                if _filters(sp, bool(self.spec_k)):
                     if self.spec_k:
                         raise NotImplementedError("top-k / top-p / penalties / logit_bias / "
                                                   "allowed_token_ids with speculative decoding")
                     runner.filtering = True
-                    runner.penalties = runner.penalties or _penalized(sp)
+                    runner.penalties = runner.penalties or _penalized(sp, bool(self.spec_k))
                 waiting.append(_Req(rid, torch.as_tensor(ids, dtype=torch.int64), sp))
             return True
 
@@ -781,7 +787,9 @@ class LLM:
                                     sp.repetition_penalty, sp.presence_penalty,
                                     sp.frequency_penalty,
                                     r.prompt if runner.penalties else None, sp.min_p,
-                                    sp.logit_bias, sp.allowed_token_ids)
+                                    sp.logit_bias, sp.allowed_token_ids,
+                                    sp.min_tokens if _can_stop(sp) and not self.spec_k else 0,
+                                    sp.stop_token_ids)
                 admitted.append(r)
             if not admitted and not running and not prefilling:
                 if not waiting:  # (online) every new request was refused above

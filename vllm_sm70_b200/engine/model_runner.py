@@ -79,6 +79,9 @@ class ModelRunner:
         self.bias_ids: torch.Tensor | None = None    # [B, nb] int64
         self.bias_vals: torch.Tensor | None = None   # [B, nb] fp32
         self.allow_ids: torch.Tensor | None = None   # [B, na] int64; a row of -1 = no limit
+        # min_tokens: the stop tokens are masked while fewer tokens exist
+        self.min_tokens = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.stop_ids: torch.Tensor | None = None    # [B, ns] int64
         self.penalties = False
         # Decode graphs always sample through the temperature path: rows with
         # T <= 0 reduce to the exact greedy argmax.
@@ -165,7 +168,8 @@ class ModelRunner:
     def _penalizer(self, rows: torch.Tensor):
         """Logit rewrite for batch slots ``rows`` (None when no request in
         flight needs one), in vLLM's order: ``allowed_token_ids`` (every other
-        token to -inf), ``logit_bias`` (added), then the penalties --
+        token to -inf), ``logit_bias`` (added), the stop tokens to -inf while
+        fewer than ``min_tokens`` tokens exist, then the penalties --
         repetition over prompt and output tokens (divide positive logits,
         multiply negative ones), presence and frequency over output tokens
         (subtract per occurrence) -- and last the ``min_p`` cut."""
@@ -191,6 +195,11 @@ class ModelRunner:
                 lg = torch.where(limited[:, None] & ~keep, torch.full_like(lg, float("-inf")), lg)
             if self.bias_ids is not None:
                 lg = lg + sparse(self.bias_ids, self.bias_vals.index_select(0, rows), vs, V)
+            if self.stop_ids is not None:
+                early = self.out_pos.index_select(0, rows) < self.min_tokens.index_select(0, rows)
+                st = self.stop_ids.index_select(0, rows)
+                hit = sparse(self.stop_ids, torch.ones(st.shape, device=lg.device), vs, V) > 0
+                lg = torch.where(early[:, None] & hit, torch.full_like(lg, float("-inf")), lg)
             outs = self.out_tokens.index_select(0, rows).long()
             pos = self.out_pos.index_select(0, rows)
             ok = torch.arange(outs.shape[1], device=lg.device)[None, :] < pos[:, None]
@@ -287,7 +296,8 @@ class ModelRunner:
                      presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
                      prompt: torch.Tensor | None = None, min_p: float = 0.0,
                      logit_bias: dict | None = None,
-                     allowed_token_ids: list | None = None) -> None:
+                     allowed_token_ids: list | None = None, min_tokens: int = 0,
+                     stop_token_ids: list | None = None) -> None:
         self.temperature[slot] = float(temperature)
         self.seeds[slot] = int(seed)
         self.top_k[slot] = int(top_k) if top_k > 0 else -1
@@ -301,6 +311,10 @@ class ModelRunner:
             self.bias_ids, self.bias_vals, slot, [t for t, _ in bias], [v for _, v in bias])
         self.allow_ids, _ = self._sparse_row(self.allow_ids, None, slot,
                                              sorted({int(t) for t in allowed_token_ids or []}))
+        self.min_tokens[slot] = int(min_tokens)
+        self.stop_ids, _ = self._sparse_row(
+            self.stop_ids, None, slot,
+            sorted({int(t) for t in stop_token_ids or []}) if min_tokens > 0 else [])
         if prompt is not None:  # the prompt's tokens count for the repetition penalty
             if self.prompt_ids is None:
                 self.prompt_ids = torch.full((self.B, self.max_model_len), -1, dtype=torch.int64,

@@ -406,7 +406,7 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           presence_penalty=float(body.get("presence_penalty", 0.0)),
                           frequency_penalty=float(body.get("frequency_penalty", 0.0)),
                           seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids,
-                          logit_bias=bias or None,
+                          min_tokens=int(body.get("min_tokens", 0)), logit_bias=bias or None,
                           allowed_token_ids=None if allowed is None else [int(t) for t in allowed])
 
 
