@@ -453,3 +453,22 @@ def test_logit_bias_request_fields():
     sp = _params({}, None)
     assert sp.logit_bias is None and sp.allowed_token_ids is None and sp.min_tokens == 0
     assert _params({"min_tokens": 3}, None).min_tokens == 3
+
+
+def test_structured_output_request_fields():
+    """response_format (json_object / json_schema), vLLM's structured_outputs
+    object and the guided_* fields become StructuredOutputsParams."""
+    from vllm_sm70_b200.entrypoints.openai_server import _params
+
+    schema = {"type": "object", "properties": {"a": {"type": "integer"}}}
+    so = _params({"response_format": {"type": "json_schema",
+                                      "json_schema": {"name": "x", "schema": schema}}}, None)
+    assert so.structured_outputs.json == schema
+    assert _params({"response_format": {"type": "json_object"}},
+                   None).structured_outputs.json_object is True
+    assert _params({"response_format": {"type": "text"}}, None).structured_outputs is None
+    assert _params({"structured_outputs": {"choice": ["a", "b"]}},
+                   None).structured_outputs.choice == ["a", "b"]
+    assert _params({"guided_regex": "[0-9]+"}, None).structured_outputs.regex == "[0-9]+"
+    with pytest.raises(ValueError):
+        _params({"response_format": {"type": "json_schema", "json_schema": {}}}, None)

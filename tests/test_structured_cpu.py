@@ -1,0 +1,116 @@
+"""Structured outputs on CPU: greedy decoding under a grammar equals a dense
+reference that masks the logits with an independent xgrammar matcher; every
+output is accepted by its grammar (choice, regex, JSON schema, EBNF, JSON
+object); requests without a grammar in the same batch are unchanged; a
+completed grammar retires the request; bad grammars are refused."""
+import json
+
+import pytest
+import torch
+
+from vllm_sm70_b200.engine import LLM, SamplingParams, StructuredOutputsParams
+
+from ._llama_ref import llama_logits
+from .test_engine_cpu import TINY
+
+xgr = pytest.importorskip("xgrammar")
+
+
+def _tokenizer():
+    """Byte-level tokenizer of the tiny model's 512-token vocabulary: the 256
+    bytes, an end-of-sequence token (256) and unused specials."""
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    chars = sorted(pre_tokenizers.ByteLevel.alphabet())
+    tk = Tokenizer(models.BPE(vocab={c: i for i, c in enumerate(chars)}, merges=[]))
+    tk.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    tk.decoder = decoders.ByteLevel()
+    tk.add_special_tokens(["<eos>"] + [f"<x{i}>" for i in range(512 - 257)])
+    return PreTrainedTokenizerFast(tokenizer_object=tk, eos_token="<eos>")
+
+
+TOK = _tokenizer()
+
+
+def _llm():
+    return LLM(TINY, max_num_seqs=4, max_model_len=160, block_size=16, dtype=torch.float32,
+               enforce_eager=True, max_num_batched_tokens=64, tokenizer=TOK)
+
+
+def _dense_guided(llm, prompt, so, n):
+    """Greedy decoding with the grammar's mask applied to a dense forward."""
+    g = llm._grammars().compile(so)
+    m = xgr.GrammarMatcher(g)
+    bm = xgr.allocate_token_bitmask(1, TINY.vocab_size)
+    ids, out = prompt.clone(), []
+    for _ in range(n):
+        m.fill_next_token_bitmask(bm, 0)
+        lg = llama_logits(llm.model, ids)[-1].clone()
+        for t in range(lg.numel()):
+            if not (int(bm[0, t // 32]) >> (t % 32)) & 1:
+                lg[t] = float("-inf")
+        t = int(lg.argmax())
+        out.append(t)
+        assert m.accept_token(t)
+        ids = torch.cat([ids, torch.tensor([t])])
+        if m.is_terminated():
+            break
+    return out
+
+
+def _prompt(n=9, seed=5):
+    return torch.randint(0, 256, (n,), generator=torch.Generator().manual_seed(seed))
+
+
+def test_guided_greedy_equals_dense_reference():
+    llm = _llm()
+    p = _prompt()
+    eos = TOK.eos_token_id
+    so = StructuredOutputsParams(choice=["alpha", "beta", "gamma"])
+    plain = llm.generate([p], SamplingParams(max_tokens=10, ignore_eos=True))[0]
+    got = llm.generate([p, p], [SamplingParams(max_tokens=20, structured_outputs=so),
+                                SamplingParams(max_tokens=10, ignore_eos=True)])
+    want = _dense_guided(llm, p, so, 20)
+    assert got[0].output_token_ids == want and want[-1] == eos
+    assert got[0].outputs[0].text in ("alpha", "beta", "gamma")
+    assert got[0].outputs[0].finish_reason == "stop"
+    assert got[1].output_token_ids == plain.output_token_ids
+
+
+@pytest.mark.parametrize("so,check", [
+    (StructuredOutputsParams(regex=r"[0-9]{3}-[a-z]{2}"),
+     lambda t: len(t) == 6 and t[:3].isdigit() and t[3] == "-" and t[4:].isalpha()),
+    (StructuredOutputsParams(json={"type": "object", "properties": {
+        "ok": {"type": "boolean"}, "n": {"type": "integer", "minimum": 0, "maximum": 9}},
+        "required": ["ok", "n"], "additionalProperties": False}),
+     lambda t: set(json.loads(t)) == {"ok", "n"} and isinstance(json.loads(t)["ok"], bool)),
+    (StructuredOutputsParams(grammar='root ::= ("yes" | "no") " " [0-9]'),
+     lambda t: t.split(" ")[0] in ("yes", "no") and t[-1].isdigit()),
+])
+def test_outputs_follow_their_grammar(so, check):
+    """Sampled (temperature 1) outputs complete and satisfy the grammar."""
+    llm = _llm()
+    sp = SamplingParams(max_tokens=60, temperature=1.0, seed=3, structured_outputs=so,
+                        stop_token_ids=[TOK.eos_token_id])
+    for o in llm.generate([_prompt(7, s) for s in range(3)], sp):
+        assert o.outputs[0].finish_reason == "stop", o.outputs[0].text
+        assert check(o.outputs[0].text), o.outputs[0].text
+        m = xgr.GrammarMatcher(llm._grammars().compile(so))
+        assert all(m.accept_token(t) for t in o.output_token_ids) and m.is_terminated()
+
+
+def test_json_object_and_refusals():
+    llm = _llm()
+    so = StructuredOutputsParams(json_object=True)
+    o = llm.generate([_prompt()], SamplingParams(max_tokens=100, structured_outputs=so))[0]
+    m = xgr.GrammarMatcher(llm._grammars().compile(so))
+    assert all(m.accept_token(t) for t in o.output_token_ids)  # a prefix of a JSON object
+    assert o.outputs[0].text.startswith("{")
+    for bad in (StructuredOutputsParams(), StructuredOutputsParams(regex="a", choice=["b"]),
+                StructuredOutputsParams(json="{not json"), StructuredOutputsParams(choice=[])):
+        with pytest.raises(ValueError):
+            llm.generate([_prompt()], SamplingParams(max_tokens=4, structured_outputs=bad))
+    no_tok = LLM(TINY, max_num_seqs=2, max_model_len=64, dtype=torch.float32, enforce_eager=True)
+    with pytest.raises(ValueError, match="tokenizer"):
+        no_tok.generate([_prompt()], SamplingParams(max_tokens=4, structured_outputs=so))

@@ -67,6 +67,7 @@ class _Req:
     stream_stopped: bool = False   # a stop token was streamed: nothing more follows
     aborted: bool = False          # cancelled by the caller (online mode)
     scanned: int = 0               # output tokens already searched for a stop token
+    guide: object = None           # structured outputs: the grammar state (structured.Guide)
     stop_hit: bool = False         # a stop token was generated: retire at the burst's end
 
 
@@ -89,7 +90,7 @@ def _penalized(p: SamplingParams, spec: bool = False) -> bool:
     ignored."""
     return (p.repetition_penalty != 1.0 or p.presence_penalty != 0.0
             or p.frequency_penalty != 0.0 or p.min_p > 0.0 or bool(p.logit_bias)
-            or p.allowed_token_ids is not None
+            or p.allowed_token_ids is not None or p.structured_outputs is not None
             or (not spec and p.min_tokens > 0 and _can_stop(p)))
 
 
@@ -106,7 +107,7 @@ def _check_token_ids(p: SamplingParams, vocab: int) -> None:
 
 def _filters(p: SamplingParams, spec: bool = False) -> bool:
     """Whether the request needs the candidate sampling path (top-k / top-p,
-    sampling penalties, min_p, logit_bias or allowed_token_ids)."""
+    sampling penalties, min_p, logit_bias, allowed_token_ids or a grammar)."""
     return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p, spec)
 
 
@@ -202,6 +203,7 @@ class LLM:
         # directory for transformers.AutoTokenizer, or None (then the checkpoint
         # directory's tokenizer is tried on first use)
         self._tokenizer = tokenizer
+        self._grammar_compiler = None  # structured outputs (built on first use)
         self._tokenizer_src = None  # a checkpoint directory that ships tokenizer files
         if isinstance(model, str):
             from pathlib import Path
@@ -517,7 +519,30 @@ class LLM:
         o = RequestOutput(r.rid, r.prompt.tolist(), r.out, True, logprobs=r.logprobs,
                           prompt_logprobs=r.prompt_logprobs)
         o.finish_reason, o.stop_reason = _finish_reason(r.out, r.params, None)
+        if r.guide is not None and r.guide.done and not r.guide.failed \
+                and o.finish_reason == "length":
+            o.finish_reason = "stop"  # the grammar ended on its own stop token
+        if r.guide is not None and r.guide.failed:
+            o.error = "structured output: a sampled token broke the grammar"
         return o
+
+    def _grammars(self):
+        """The structured-output grammar compiler (built on first use)."""
+        if self._grammar_compiler is None:
+            tok = self.tokenizer
+            if tok is None:
+                raise ValueError("structured outputs need a tokenizer (LLM(..., tokenizer=...))")
+            from .structured import GrammarCompiler
+
+            self._grammar_compiler = GrammarCompiler(tok, self.cfg.vocab_size)
+        return self._grammar_compiler
+
+    def _check_request(self, p: SamplingParams) -> None:
+        """Argument checks of one request (ValueError): token ids in the
+        vocabulary, and a structured-output grammar that compiles."""
+        _check_token_ids(p, self.cfg.vocab_size)
+        if p.structured_outputs is not None:
+            self._grammars().compile(p.structured_outputs)
 
     def _logprobs_of(self, r: "_Req") -> tuple[list | None, list | None]:
         """(output, prompt) log-prob lists of a finished request that asked
@@ -583,7 +608,7 @@ class LLM:
         if any(p.n > 1 for p in params) and feed is None:
             return self._generate_n(prompts, params, collect_stats, on_tokens, stream_interval)
         for p in params:
-            _check_token_ids(p, self.cfg.vocab_size)
+            self._check_request(p)
         spec = bool(self.spec_k)
         filtering = any(_filters(p, spec) for p in params)
         if filtering and self.spec_k:
@@ -699,6 +724,26 @@ class LLM:
                     r.stop_hit = True
                 r.scanned = upto
 
+        def advance_guides(rs) -> None:
+            """Feed the new tokens of structured-output requests to their
+            grammar matchers and upload each one's next allow-list row; a
+            matcher that reached its grammar's end retires the request."""
+            rs = [r for r in rs if r.guide is not None and not r.guide.done
+                  and r.guide.accepted < min(r.generated, r.params.max_tokens)]
+            if not rs:
+                return
+            lo = min(r.guide.accepted for r in rs)
+            hi = max(min(r.generated, r.params.max_tokens) for r in rs)
+            idx = torch.tensor([r.slot for r in rs], device=self.device)
+            cols = runner.out_tokens.index_select(0, idx)[:, lo:hi].cpu()
+            for r, row in zip(rs, cols):
+                upto = min(r.generated, r.params.max_tokens)
+                r.guide.advance(row[r.guide.accepted - lo:upto - lo].tolist())
+                if r.guide.done:
+                    r.stop_hit = True
+                else:
+                    runner.set_guide_row(r.slot, r.guide.next_row())
+
         def finished(r) -> bool:
             return r.generated >= r.params.max_tokens or r.aborted or r.stop_hit
 
@@ -732,7 +777,7 @@ class LLM:
                     continue
                 rid, ids, sp = item
                 try:
-                    _check_token_ids(sp, self.cfg.vocab_size)
+                    self._check_request(sp)
                 except ValueError as e:  # fail this request alone
                     on_finish(RequestOutput(rid, list(ids), [], True, error=str(e)))
                     continue
@@ -790,6 +835,11 @@ class LLM:
                                     sp.logit_bias, sp.allowed_token_ids,
                                     sp.min_tokens if _can_stop(sp) and not self.spec_k else 0,
                                     sp.stop_token_ids)
+                if sp.structured_outputs is not None:
+                    r.guide = self._grammars().matcher(sp.structured_outputs)
+                    runner.set_guide_row(r.slot, r.guide.next_row())
+                else:
+                    runner.set_guide_row(r.slot, None)
                 admitted.append(r)
             if not admitted and not running and not prefilling:
                 if not waiting:  # (online) every new request was refused above
@@ -850,6 +900,7 @@ class LLM:
                     break  # one chunk, then a decode burst of the running requests
             # ---- decode until the next request finishes
             live = [r for r in running if not r.done]
+            advance_guides(live)
             scan_stops(live)  # a first token (from prefill) may already stop
             finished_now = [r for r in live if finished(r)]
             if not live:
@@ -864,6 +915,7 @@ class LLM:
                 stats.spec_slots += len(live)
                 if self.spec_hook is not None:
                     self.spec_hook(len(live), sum(int(n[r.slot]) for r in live))
+                advance_guides(live)
                 scan_stops(live)
                 finished_now = [r for r in live if finished(r)]
                 if cuda and finished_now:
@@ -876,6 +928,8 @@ class LLM:
                     steps = min(steps, stream_interval)
                 if stop_every and any(_can_stop(r.params) for r in live):
                     steps = min(steps, stop_every)
+                if any(r.guide is not None for r in live):
+                    steps = 1  # the next allow-list depends on this step's token
                 n_rows = max(r.slot for r in live) + 1
                 if self.watchdog is not None:
                     self.watchdog.check()
@@ -885,6 +939,7 @@ class LLM:
                 stats.decode_steps += steps
                 for r in live:
                     r.generated += steps
+                advance_guides(live)
                 scan_stops(live)
                 finished_now = [r for r in live if finished(r)]
                 if cuda:
@@ -903,6 +958,8 @@ class LLM:
                 emit(finished_now, outs_h, final=True)
                 for r, row in zip(finished_now, outs_h):
                     n_out = min(r.generated, r.params.max_tokens)
+                    if r.guide is not None and r.guide.done:
+                        n_out = min(n_out, r.guide.accepted + int(r.guide.failed))
                     r.out = _truncate_at_stop(row[:n_out].tolist(), r.params)
                     r.done = True
                     runner.alloc.free(r.blocks)

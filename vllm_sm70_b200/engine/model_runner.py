@@ -26,6 +26,7 @@ from .. import envs
 from ..utils import launch_count
 from ..models.layers import AttnMeta, KVCache
 from .block_manager import build_prefill_meta, make_allocator
+from .structured import mask_logits
 
 
 def default_capture_sizes(max_bs: int) -> list[int]:
@@ -82,6 +83,9 @@ class ModelRunner:
         # min_tokens: the stop tokens are masked while fewer tokens exist
         self.min_tokens = torch.zeros(B, dtype=torch.int64, device=dev)
         self.stop_ids: torch.Tensor | None = None    # [B, ns] int64
+        # structured outputs: per-slot allow-list bitmask of the next token
+        # (engine/structured.py), allocated on first use; -1 rows allow all
+        self.guide: torch.Tensor | None = None       # [B, ceil(vocab / 32)] int32
         self.penalties = False
         # Decode graphs always sample through the temperature path: rows with
         # T <= 0 reduce to the exact greedy argmax.
@@ -167,7 +171,8 @@ class ModelRunner:
 
     def _penalizer(self, rows: torch.Tensor):
         """Logit rewrite for batch slots ``rows`` (None when no request in
-        flight needs one), in vLLM's order: ``allowed_token_ids`` (every other
+        flight needs one), in vLLM's order: the structured-output grammar's
+        allow-list and ``allowed_token_ids`` (every other
         token to -inf), ``logit_bias`` (added), the stop tokens to -inf while
         fewer than ``min_tokens`` tokens exist, then the penalties --
         repetition over prompt and output tokens (divide positive logits,
@@ -188,6 +193,8 @@ class ModelRunner:
 
         def apply(lg: torch.Tensor, vs: int) -> torch.Tensor:
             b, V = lg.shape
+            if self.guide is not None:
+                lg = mask_logits(lg, self.guide.index_select(0, rows), vs)
             if self.allow_ids is not None:
                 a = self.allow_ids.index_select(0, rows)
                 keep = sparse(self.allow_ids, torch.ones(a.shape, device=lg.device), vs, V) > 0
@@ -321,6 +328,18 @@ class ModelRunner:
                                              device=self.device)
             self.prompt_ids[slot].fill_(-1)
             self.prompt_ids[slot, : prompt.numel()] = prompt.to(self.device)
+
+    def set_guide_row(self, slot: int, row: torch.Tensor | None) -> None:
+        """Allow-list bitmask of ``slot``'s next token ([1, words] int32, from
+        the request's grammar matcher), or None to lift the limit."""
+        if row is None:
+            if self.guide is not None:
+                self.guide[slot].fill_(-1)
+            return
+        if self.guide is None:
+            self.guide = torch.full((self.B, row.shape[-1]), -1, dtype=torch.int32,
+                                    device=self.device)
+        self.guide[slot].copy_(row.reshape(-1), non_blocking=False)
 
     def _sparse_row(self, ids_t, vals_t, slot: int, ids: list, vals: list | None = None):
         """Write ``slot``'s row of a per-slot sparse table (ids padded with -1,

@@ -4,6 +4,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 
+from .structured import StructuredOutputsParams
+
 
 @dataclass
 class SamplingParams:
@@ -24,6 +26,7 @@ class SamplingParams:
     frequency_penalty: float = 0.0       # subtracted per occurrence in the output
     logit_bias: dict[int, float] | None = None   # {token id: added to its logit}
     allowed_token_ids: list[int] | None = None   # only these tokens can be sampled
+    structured_outputs: StructuredOutputsParams | None = None  # grammar-constrained output
     logprobs: int | None = None          # per output token: its log-prob + the top-N
     prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 

@@ -396,6 +396,7 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
     if bias is not None:  # OpenAI: {"token id": bias in [-100, 100]}
         bias = {int(t): min(100.0, max(-100.0, float(v))) for t, v in dict(bias).items()}
     allowed = body.get("allowed_token_ids")  # vLLM's extra field
+    guided = _structured(body)
     return SamplingParams(max_tokens=16 if mt is None else int(mt),
                           logprobs=n_lp, prompt_logprobs=prompt_lp,
                           temperature=float(body.get("temperature", 1.0)),
@@ -407,7 +408,36 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           frequency_penalty=float(body.get("frequency_penalty", 0.0)),
                           seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids,
                           min_tokens=int(body.get("min_tokens", 0)), logit_bias=bias or None,
-                          allowed_token_ids=None if allowed is None else [int(t) for t in allowed])
+                          allowed_token_ids=None if allowed is None else [int(t) for t in allowed],
+                          structured_outputs=guided)
+
+
+def _structured(body: dict):
+    """Structured-output request of a body: OpenAI ``response_format``
+    (``json_object``, or ``json_schema`` with its ``schema``), vLLM's
+    ``structured_outputs`` object (json / regex / choice / grammar /
+    json_object) and its older ``guided_json`` / ``guided_regex`` /
+    ``guided_choice`` / ``guided_grammar`` fields; None when there is none."""
+    from ..engine.structured import StructuredOutputsParams
+
+    so = body.get("structured_outputs")
+    if so:
+        keys = ("json", "regex", "choice", "grammar", "json_object")
+        return StructuredOutputsParams(**{k: so[k] for k in keys if k in so})
+    for field, kw in (("guided_json", "json"), ("guided_regex", "regex"),
+                      ("guided_choice", "choice"), ("guided_grammar", "grammar")):
+        if body.get(field) is not None:
+            return StructuredOutputsParams(**{kw: body[field]})
+    rf = body.get("response_format") or {}
+    if rf.get("type") == "json_object":
+        return StructuredOutputsParams(json_object=True)
+    if rf.get("type") == "json_schema":
+        js = rf.get("json_schema") or {}
+        schema = js.get("schema", js.get("json_schema"))
+        if schema is None:
+            raise ValueError("response_format json_schema needs a schema")
+        return StructuredOutputsParams(json=schema)
+    return None
 
 
 def _apply_stop_strings(text: str, stop) -> tuple[str, bool]:
