@@ -114,3 +114,26 @@ def test_json_object_and_refusals():
     no_tok = LLM(TINY, max_num_seqs=2, max_model_len=64, dtype=torch.float32, enforce_eager=True)
     with pytest.raises(ValueError, match="tokenizer"):
         no_tok.generate([_prompt()], SamplingParams(max_tokens=4, structured_outputs=so))
+
+
+def test_online_mode_guided_requests():
+    """Continuous batching (requests arrive through a feed, prefill chunks
+    interleave with decode): a grammar request gives the offline tokens; an
+    invalid grammar fails that request alone."""
+    llm = _llm()
+    so = StructuredOutputsParams(choice=["alpha", "beta", "gamma"])
+    sp = SamplingParams(max_tokens=20, structured_outputs=so)
+    p = _prompt()
+    offline = llm.generate([p], sp)[0].output_token_ids
+    items = [[(0, p, sp), (1, _prompt(70, 2), SamplingParams(max_tokens=6, ignore_eos=True)),
+              (2, p, SamplingParams(max_tokens=4, structured_outputs=StructuredOutputsParams(
+                  json="{bad")))]]
+    done = {}
+
+    def feed(block):
+        return items.pop(0) if items else None
+
+    llm.generate([], feed=feed, on_finish=lambda o: done.__setitem__(o.request_id, o))
+    assert done[0].output_token_ids == offline and done[0].error is None
+    assert len(done[1].output_token_ids) == 6
+    assert done[2].error and "structured_outputs" in done[2].error
