@@ -137,3 +137,46 @@ def test_online_mode_guided_requests():
     assert done[0].output_token_ids == offline and done[0].error is None
     assert len(done[1].output_token_ids) == 6
     assert done[2].error and "structured_outputs" in done[2].error
+
+
+def test_server_response_format_and_forced_tool_choice(monkeypatch):
+    """Through the OpenAI chat endpoint: ``response_format`` json_schema
+    replies parse against the schema; a named ``tool_choice`` returns that
+    function's call with schema-valid arguments; "required" returns a
+    non-empty list of calls of offered functions."""
+    from fastapi.testclient import TestClient
+
+    from vllm_sm70_b200.entrypoints.openai_server import build_app
+
+    # compact JSON: a random-weight model would otherwise emit whitespace forever
+    monkeypatch.setenv("VLLM_B200_STRUCTURED_ANY_WHITESPACE", "0")
+    tok = _tokenizer()
+    tok.chat_template = "{% for m in messages %}{{ m['content'] }}{% endfor %}"
+    llm = LLM(TINY, max_num_seqs=4, max_model_len=200, block_size=16, dtype=torch.float32,
+              enforce_eager=True, max_num_batched_tokens=64)
+    schema = {"type": "object", "properties": {"city": {"type": "string", "enum": ["Paris", "Rome"]},
+                                               "days": {"type": "integer", "minimum": 1,
+                                                        "maximum": 7}},
+              "required": ["city", "days"], "additionalProperties": False}
+    tools = [{"type": "function", "function": {"name": "forecast", "parameters": schema}},
+             {"type": "function", "function": {"name": "ping", "parameters": {
+                 "type": "object", "properties": {}, "additionalProperties": False}}}]
+    body = {"messages": [{"role": "user", "content": "weather?"}], "max_tokens": 80,
+            "temperature": 0.0}
+    with TestClient(build_app(llm, tok, "tiny")) as c:
+        r = c.post("/v1/chat/completions", json={**body, "response_format": {
+            "type": "json_schema", "json_schema": {"name": "w", "schema": schema}}}).json()
+        obj = json.loads(r["choices"][0]["message"]["content"])
+        assert obj["city"] in ("Paris", "Rome") and 1 <= obj["days"] <= 7
+        r = c.post("/v1/chat/completions", json={**body, "tools": tools, "tool_choice": {
+            "type": "function", "function": {"name": "forecast"}}}).json()["choices"][0]
+        call = r["message"]["tool_calls"][0]["function"]
+        assert r["message"]["content"] is None and call["name"] == "forecast"
+        assert json.loads(call["arguments"])["city"] in ("Paris", "Rome")
+        r = c.post("/v1/chat/completions", json={**body, "max_tokens": 150, "tools": tools,
+                                                 "tool_choice": "required"}).json()["choices"][0]
+        calls = r["message"]["tool_calls"]
+        assert calls and all(x["function"]["name"] in ("forecast", "ping") for x in calls)
+        bad = c.post("/v1/chat/completions", json={**body, "tools": tools, "tool_choice": {
+            "type": "function", "function": {"name": "nope"}}})
+        assert bad.status_code == 400

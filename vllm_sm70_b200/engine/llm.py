@@ -111,6 +111,16 @@ def _filters(p: SamplingParams, spec: bool = False) -> bool:
     return p.top_k not in (-1, 0) or p.top_p < 1.0 or _penalized(p, spec)
 
 
+def chat_token_ids(tokenizer, messages, **kw) -> list[int]:
+    """Token ids of ``tokenizer.apply_chat_template(messages, tokenize=True,
+    **kw)``. Newer transformers return a mapping with ``input_ids`` (one
+    conversation) instead of the id list."""
+    out = tokenizer.apply_chat_template(messages, tokenize=True, **kw)
+    if hasattr(out, "keys"):
+        out = out["input_ids"]
+    return [int(t) for t in out]
+
+
 def _can_stop(p: SamplingParams) -> bool:
     """Whether a stop token can end the request before ``max_tokens``."""
     return not p.ignore_eos and bool(p.stop_token_ids)
@@ -407,7 +417,7 @@ class LLM:
         kw = dict(chat_template_kwargs or {})
         if tools:
             kw["tools"] = tools
-        ids = [list(tok.apply_chat_template(c, add_generation_prompt=True, tokenize=True, **kw))
+        ids = [chat_token_ids(tok, c, add_generation_prompt=True, **kw)
                for c in convs]
         return self.generate(ids, sampling_params)
 
@@ -534,8 +544,21 @@ class LLM:
                 raise ValueError("structured outputs need a tokenizer (LLM(..., tokenizer=...))")
             from .structured import GrammarCompiler
 
-            self._grammar_compiler = GrammarCompiler(tok, self.cfg.vocab_size)
+            try:
+                self._grammar_compiler = GrammarCompiler(tok, self.cfg.vocab_size)
+            except Exception as e:  # noqa: BLE001 - xgrammar cannot read this tokenizer
+                raise ValueError(f"structured outputs: unsupported tokenizer ({e})") from e
         return self._grammar_compiler
+
+    def get_tokenizer(self):
+        """vLLM's ``LLM.get_tokenizer``."""
+        return self.tokenizer
+
+    def set_tokenizer(self, tokenizer) -> None:
+        """vLLM's ``LLM.set_tokenizer``: text prompts, output text, stop
+        strings and structured-output grammars use ``tokenizer`` from now on."""
+        self._tokenizer, self._tokenizer_src = tokenizer, None
+        self._grammar_compiler = None
 
     def _check_request(self, p: SamplingParams) -> None:
         """Argument checks of one request (ValueError): token ids in the

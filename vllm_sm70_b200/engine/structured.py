@@ -37,9 +37,10 @@ class StructuredOutputsParams:
     choice: list[str] | None = None       # the output is one of these strings
     grammar: str | None = None            # EBNF (xgrammar / GBNF syntax)
     json_object: bool | None = None       # any JSON object
+    disable_any_whitespace: bool = False  # JSON without optional whitespace
 
     def key(self) -> tuple:
-        """(kind, canonical text): one compiled grammar per key."""
+        """(kind, canonical text, compact JSON): one compiled grammar per key."""
         set_ = [(k, v) for k, v in (("json", self.json), ("regex", self.regex),
                                     ("choice", self.choice), ("grammar", self.grammar),
                                     ("json_object", self.json_object)) if v not in (None, False)]
@@ -47,13 +48,20 @@ class StructuredOutputsParams:
             raise ValueError("structured_outputs needs exactly one of json, regex, choice, "
                              "grammar, json_object")
         kind, v = set_[0]
+        compact = bool(self.disable_any_whitespace) or not _any_whitespace()
         if kind == "json":
-            return kind, v if isinstance(v, str) else _json.dumps(v, sort_keys=True)
+            return kind, v if isinstance(v, str) else _json.dumps(v, sort_keys=True), compact
         if kind == "choice":
             if not v:
                 raise ValueError("structured_outputs.choice is empty")
-            return kind, "|".join(re.escape(str(c)) for c in v)
-        return kind, "" if kind == "json_object" else str(v)
+            return kind, "|".join(re.escape(str(c)) for c in v), compact
+        return kind, "" if kind == "json_object" else str(v), compact
+
+
+def _any_whitespace() -> bool:
+    from .. import envs
+
+    return bool(envs.get("VLLM_B200_STRUCTURED_ANY_WHITESPACE"))
 
 
 def bitmask_words(vocab_size: int) -> int:
@@ -81,15 +89,17 @@ class GrammarCompiler:
         if g is not None:
             self._cache.move_to_end(key)
             return g
-        kind, text = key
+        kind, text, compact = key
         c = self._compiler
         try:
             if kind == "json":
-                g = c.compile_json_schema(text)
+                g = c.compile_json_schema(text, any_whitespace=not compact)
             elif kind in ("regex", "choice"):
                 g = c.compile_regex(text)
             elif kind == "grammar":
                 g = c.compile_grammar(text)
+            elif compact:  # any JSON object, no optional whitespace
+                g = c.compile_json_schema('{"type": "object"}', any_whitespace=False)
             else:
                 g = c.compile_builtin_json_grammar()
         except Exception as e:  # noqa: BLE001 - xgrammar raises several types

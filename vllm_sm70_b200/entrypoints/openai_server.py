@@ -43,6 +43,7 @@ import threading
 import time
 import uuid
 
+from ..engine.llm import chat_token_ids
 from ..engine.sampling_params import SamplingParams
 
 STREAM_INTERVAL = 8  # decode steps per streamed chunk
@@ -412,6 +413,30 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           structured_outputs=guided)
 
 
+def _forced_tool_schema(body: dict):
+    """(kind, JSON schema) of the reply a forced ``tool_choice`` demands, as
+    vLLM builds it: a named function -> its ``parameters`` object; "required"
+    -> a non-empty array of {"name", "parameters"} over the offered tools;
+    None for "auto" / "none" / no tools."""
+    choice = body.get("tool_choice")
+    tools = [t.get("function", t) for t in body.get("tools") or []]
+    if not tools or choice in (None, "auto", "none"):
+        return None
+    params = lambda f: f.get("parameters") or {"type": "object"}  # noqa: E731
+    if choice == "required":
+        return "required", {"type": "array", "minItems": 1, "items": {"anyOf": [
+            {"type": "object", "properties": {"name": {"type": "string", "enum": [f["name"]]},
+                                              "parameters": params(f)},
+             "required": ["name", "parameters"]} for f in tools]}}
+    if isinstance(choice, dict):
+        name = (choice.get("function") or {}).get("name")
+        for f in tools:
+            if f.get("name") == name:
+                return ("named", name), params(f)
+        raise ValueError(f"tool_choice names an unknown function: {name}")
+    raise ValueError(f"tool_choice {choice!r} is not supported")
+
+
 def _structured(body: dict):
     """Structured-output request of a body: OpenAI ``response_format``
     (``json_object``, or ``json_schema`` with its ``schema``), vLLM's
@@ -422,7 +447,7 @@ def _structured(body: dict):
 
     so = body.get("structured_outputs")
     if so:
-        keys = ("json", "regex", "choice", "grammar", "json_object")
+        keys = ("json", "regex", "choice", "grammar", "json_object", "disable_any_whitespace")
         return StructuredOutputsParams(**{k: so[k] for k in keys if k in so})
     for field, kw in (("guided_json", "json"), ("guided_regex", "regex"),
                       ("guided_choice", "choice"), ("guided_grammar", "grammar")):
@@ -482,6 +507,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
     from .metrics import ServerMetrics
 
     metrics = ServerMetrics(model_name)
+    if tokenizer is not None and hasattr(llm, "set_tokenizer") and llm.tokenizer is None:
+        llm.set_tokenizer(tokenizer)  # structured-output grammars need it too
     ps = getattr(llm, "ps", None)
     dp = ps is not None and ps.world_size > 1 and ps.tp_size == 1
     batcher = (DPBatcher(llm, max_batch, ps.cpu_group, metrics) if dp
@@ -629,10 +656,10 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         if "messages" in body:
             if tokenizer is None or not hasattr(tokenizer, "apply_chat_template"):
                 raise HTTPException(400, "chat needs a tokenizer with a chat template")
-            ids = list(tokenizer.apply_chat_template(
-                body["messages"], add_generation_prompt=bool(body.get("add_generation_prompt",
-                                                                      True)),
-                tokenize=True, **(body.get("chat_template_kwargs") or {})))
+            ids = chat_token_ids(
+                tokenizer, body["messages"],
+                add_generation_prompt=bool(body.get("add_generation_prompt", True)),
+                **(body.get("chat_template_kwargs") or {}))
         else:
             ids = encode(body.get("prompt"))
         return {"tokens": ids, "count": len(ids), "max_model_len": llm.runner.max_model_len}
@@ -765,11 +792,23 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             sp = _params(body, tokenizer, chat=True)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
+        try:
+            forced = _forced_tool_schema(body)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        if forced is not None:  # the reply is the call's JSON, constrained by its schema
+            import dataclasses
+
+            from ..engine.structured import StructuredOutputsParams
+
+            if body.get("stream"):
+                raise HTTPException(400, "a forced tool_choice is served without streaming")
+            sp = dataclasses.replace(sp, structured_outputs=StructuredOutputsParams(
+                json=forced[1]))
         kwargs = body.get("chat_template_kwargs") or {}
         tools = body.get("tools") if body.get("tool_choice", "auto") != "none" else None
         tpl = dict(kwargs, tools=tools) if tools else kwargs
-        ids = list(tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True,
-                                                 tokenize=True, **tpl))
+        ids = chat_token_ids(tokenizer, body["messages"], add_generation_prompt=True, **tpl)
         if body.get("stream"):
             return stream_chat(ids, sp, kwargs, body.get("stop"),
                                bool((body.get("stream_options") or {}).get("include_usage")))
@@ -778,7 +817,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                                           for spj in _samples(sp, int(body.get("n", 1)))])
         except ValueError as e:  # a request the engine could not serve
             raise HTTPException(400, str(e)) from e
-        choices = [chat_choice(k, o, sp, kwargs, body.get("stop"), bool(tools))
+        choices = [chat_choice(k, o, sp, kwargs, body.get("stop"), bool(tools), forced)
                    for k, o in enumerate(outs)]
         n_out = sum(len(o.output_token_ids) for o in outs)
         return {"id": f"chatcmpl-{uuid.uuid4().hex}", "object": "chat.completion",
@@ -786,7 +825,7 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out,
                           "total_tokens": len(ids) + n_out}}
 
-    def chat_choice(index, o, sp, kwargs, stop, tools=False) -> dict:
+    def chat_choice(index, o, sp, kwargs, stop, tools=False, forced=None) -> dict:
         raw = tokenizer.decode(o.output_token_ids, skip_special_tokens=False)
         last = o.output_token_ids[-1] if o.output_token_ids else None
         stopped = last is not None and last in sp.stop_token_ids
@@ -804,7 +843,13 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         content, hit = _apply_stop_strings(content, stop)
         msg["content"] = content
         finish = "stop" if (stopped or hit) else "length"
-        if tools:  # the request offered tools: <tool_call> blocks become tool_calls
+        if forced is not None and not o.error:
+            from ..integration.tool_calls import forced_tool_calls
+
+            calls = forced_tool_calls(forced, content)
+            if calls:
+                msg["content"], msg["tool_calls"] = None, calls
+        elif tools:  # the request offered tools: <tool_call> blocks become tool_calls
             from ..integration.tool_calls import parse_tool_calls
 
             rest, calls = parse_tool_calls(content)
@@ -876,6 +921,8 @@ def main(argv=None) -> None:
             tok = AutoTokenizer.from_pretrained(args.tokenizer or args.model)
         except Exception:  # noqa: BLE001 - token-id prompts still work
             tok = None
+    if tok is not None:  # every rank compiles structured-output grammars against it
+        llm.set_tokenizer(tok)
     ps = pstate.get()
     group = ps.cpu_group if ps.tp_size > 1 else None
     if ps.tp_size > 1 and ps.tp_rank != 0:

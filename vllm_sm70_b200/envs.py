@@ -131,6 +131,9 @@ _reg("VLLM_B200_COMM_TIMEOUT_MS", "int", 2000, "comm",
 _reg("VLLM_B200_CUDA_GRAPHS", "kill", True, "runtime", "Capture decode steps in CUDA graphs.")
 _reg("VLLM_B200_GRAPH_MAX_BS", "int", 512, "runtime", "Largest captured decode batch.")
 _reg("VLLM_B200_WARMUP", "kill", True, "runtime", "Pre-capture GEMM warm-up / tuning.")
+_reg("VLLM_B200_STRUCTURED_ANY_WHITESPACE", "kill", True, "runtime",
+     "JSON grammars of structured outputs allow optional whitespace (0 = compact JSON for "
+     "every request, like a request's disable_any_whitespace).")
 _reg("VLLM_B200_STOP_CHECK_STEPS", "int", 16, "runtime",
      "Longest decode burst while a running request can end on a stop token: its new "
      "tokens are checked after each burst and a stopped request retires (0 = run "

@@ -87,3 +87,23 @@ def parse_tool_calls(text: str) -> tuple[str | None, list[dict]]:
             break
     content = "".join(keep).strip()
     return (content or None), calls
+
+
+def forced_tool_calls(forced, text: str) -> list[dict]:
+    """OpenAI ``tool_calls`` of a reply generated under a forced
+    ``tool_choice`` (the grammar made it the call's JSON): a named function's
+    arguments object, or the "required" array of {"name", "parameters"}.
+    Empty when the text is not complete JSON (the reply hit ``max_tokens``)."""
+    kind, _schema = forced
+    try:
+        obj = json.loads(text)
+    except ValueError:
+        return []
+
+    def call(name, args):
+        return {"id": f"call_{uuid.uuid4().hex[:24]}", "type": "function",
+                "function": {"name": name, "arguments": json.dumps(args)}}
+
+    if kind == "required":
+        return [call(c["name"], c.get("parameters", {})) for c in obj]
+    return [call(kind[1], obj)]
