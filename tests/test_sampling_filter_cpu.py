@@ -216,3 +216,37 @@ def test_min_tokens_masks_stop_tokens():
             break
     assert got[0].output_token_ids == want and stop not in want[:4]
     assert got[1].output_token_ids == plain
+
+
+def test_bad_words_match_dense_reference():
+    """vLLM's ``bad_words``: the last token of a word is banned whenever the
+    output ends with the rest of it (a one-token word is banned outright);
+    greedy tokens equal a dense reference applying that rule."""
+    from ._llama_ref import llama_logits
+
+    class CsvTok:  # "5,9" -> [5, 9]
+        def encode(self, text, add_special_tokens=False):
+            return [int(x) for x in text.strip().split(",") if x]
+
+        def decode(self, ids, skip_special_tokens=True):
+            return ",".join(map(str, ids))
+
+    llm = _llm()
+    llm.set_tokenizer(CsvTok())
+    p = _prompts()[2]
+    plain = llm.generate([p], SamplingParams(max_tokens=12, ignore_eos=True))[0].output_token_ids
+    words = [[plain[2]], [plain[4], plain[5]], [plain[0], plain[1], plain[6]]]
+    sp = SamplingParams(max_tokens=12, ignore_eos=True,
+                        bad_words=[",".join(map(str, w)) for w in words])
+    got = llm.generate([p, p], [sp, SamplingParams(max_tokens=12, ignore_eos=True)])
+    ids, want = p.clone(), []
+    for _ in range(12):
+        lg = llama_logits(llm.model, ids)[-1].clone()
+        for w in words:
+            if len(w) - 1 <= len(want) and (len(w) == 1 or want[-(len(w) - 1):] == w[:-1]):
+                lg[w[-1]] = float("-inf")
+        t = int(lg.argmax())
+        want.append(t)
+        ids = torch.cat([ids, torch.tensor([t])])
+    assert got[0].output_token_ids == want and plain[2] not in want and want != plain
+    assert got[1].output_token_ids == plain

@@ -91,6 +91,7 @@ def _penalized(p: SamplingParams, spec: bool = False) -> bool:
     return (p.repetition_penalty != 1.0 or p.presence_penalty != 0.0
             or p.frequency_penalty != 0.0 or p.min_p > 0.0 or bool(p.logit_bias)
             or p.allowed_token_ids is not None or p.structured_outputs is not None
+            or bool(p.bad_words)
             or (not spec and p.min_tokens > 0 and _can_stop(p)))
 
 
@@ -566,6 +567,37 @@ class LLM:
         _check_token_ids(p, self.cfg.vocab_size)
         if p.structured_outputs is not None:
             self._grammars().compile(p.structured_outputs)
+        self._bad_word_ids(p)
+
+    def _bad_word_ids(self, p: SamplingParams) -> list[list[int]]:
+        """Token sequences of a request's ``bad_words``, vLLM's way: each word
+        as it starts the text and, when the tokenizer gives it a different
+        first token of the same length, as it follows a space."""
+        if not p.bad_words:
+            return []
+        tok = self.tokenizer
+        if tok is None:
+            raise ValueError("bad_words need a tokenizer (LLM(..., tokenizer=...))")
+
+        def enc(text):
+            try:
+                return [int(t) for t in tok.encode(text, add_special_tokens=False)]
+            except TypeError:  # tokenizers without the keyword
+                return [int(t) for t in tok.encode(text)]
+
+        out = []
+        for w in p.bad_words:
+            bare = enc(w.lstrip())
+            if not bare:
+                continue
+            out.append(bare)
+            spaced = enc(" " + w.lstrip())
+            if spaced and spaced[0] != bare[0] and len(spaced) == len(bare):
+                out.append(spaced)
+        if any(not 0 <= t < self.cfg.vocab_size for w in out for t in w):
+            raise ValueError(f"bad_words encode to ids outside the vocabulary [0, "
+                             f"{self.cfg.vocab_size})")
+        return out
 
     def _logprobs_of(self, r: "_Req") -> tuple[list | None, list | None]:
         """(output, prompt) log-prob lists of a finished request that asked
@@ -858,6 +890,7 @@ class LLM:
                                     sp.logit_bias, sp.allowed_token_ids,
                                     sp.min_tokens if _can_stop(sp) and not self.spec_k else 0,
                                     sp.stop_token_ids)
+                runner.set_bad_words(r.slot, self._bad_word_ids(sp))
                 if sp.structured_outputs is not None:
                     r.guide = self._grammars().matcher(sp.structured_outputs)
                     runner.set_guide_row(r.slot, r.guide.next_row())

@@ -86,6 +86,10 @@ class ModelRunner:
         # structured outputs: per-slot allow-list bitmask of the next token
         # (engine/structured.py), allocated on first use; -1 rows allow all
         self.guide: torch.Tensor | None = None       # [B, ceil(vocab / 32)] int32
+        # bad_words: per slot, token sequences right-aligned in [B, words, L]
+        # (-1 pads the front and unused words): the last token of a word is
+        # banned when the output ends with the rest of it
+        self.bad_words: torch.Tensor | None = None
         self.penalties = False
         # Decode graphs always sample through the temperature path: rows with
         # T <= 0 reduce to the exact greedy argmax.
@@ -195,6 +199,8 @@ class ModelRunner:
             b, V = lg.shape
             if self.guide is not None:
                 lg = mask_logits(lg, self.guide.index_select(0, rows), vs)
+            if self.bad_words is not None:
+                lg = self._ban_bad_words(lg, rows, vs)
             if self.allow_ids is not None:
                 a = self.allow_ids.index_select(0, rows)
                 keep = sparse(self.allow_ids, torch.ones(a.shape, device=lg.device), vs, V) > 0
@@ -328,6 +334,47 @@ class ModelRunner:
                                              device=self.device)
             self.prompt_ids[slot].fill_(-1)
             self.prompt_ids[slot, : prompt.numel()] = prompt.to(self.device)
+
+    def _ban_bad_words(self, lg: torch.Tensor, rows: torch.Tensor, vs: int) -> torch.Tensor:
+        """-inf for the last token of every bad word whose preceding tokens
+        are the last output tokens of the row (vLLM's rule; output tokens
+        only, so a word longer than the output so far + 1 cannot match)."""
+        b, V = lg.shape
+        bw = self.bad_words.index_select(0, rows)                  # [b, W, L]
+        L = bw.shape[2]
+        last = bw[:, :, L - 1]
+        hit = last >= 0
+        if L > 1:
+            pos = self.out_pos.index_select(0, rows)
+            idx = pos[:, None] - (L - 1) + torch.arange(L - 1, device=lg.device)[None, :]
+            tail = self.out_tokens.index_select(0, rows).long().gather(1, idx.clamp_min(0))
+            tail = torch.where(idx >= 0, tail, torch.full_like(tail, -2))   # [b, L-1]
+            pref = bw[:, :, : L - 1]
+            hit &= ((pref < 0) | (pref == tail[:, None, :])).all(2)
+        loc = last - vs
+        hit &= (loc >= 0) & (loc < V)
+        ban = torch.zeros(b, V, device=lg.device)
+        ban.scatter_add_(1, loc.clamp(0, V - 1), hit.float())
+        return torch.where(ban > 0, torch.full_like(lg, float("-inf")), lg)
+
+    def set_bad_words(self, slot: int, words: list[list[int]] | None) -> None:
+        """Token sequences of ``slot``'s bad words (None / empty: none)."""
+        words = [list(w) for w in words or [] if w]
+        if self.bad_words is None and not words:
+            return
+        W = max(len(words), 1 if self.bad_words is None else self.bad_words.shape[1])
+        L = max([len(w) for w in words] + [1 if self.bad_words is None else
+                                           self.bad_words.shape[2]])
+        if self.bad_words is None or self.bad_words.shape[1:] != (W, L):
+            t = torch.full((self.B, W, L), -1, dtype=torch.int64, device=self.device)
+            if self.bad_words is not None:
+                _, w0, l0 = self.bad_words.shape
+                t[:, :w0, L - l0:] = self.bad_words
+            self.bad_words = t
+        row = torch.full((W, L), -1, dtype=torch.int64)
+        for i, w in enumerate(words):
+            row[i, L - len(w):] = torch.tensor(w, dtype=torch.int64)
+        self.bad_words[slot].copy_(row.to(self.device))
 
     def set_guide_row(self, slot: int, row: torch.Tensor | None) -> None:
         """Allow-list bitmask of ``slot``'s next token ([1, words] int32, from

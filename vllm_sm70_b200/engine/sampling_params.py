@@ -27,6 +27,7 @@ class SamplingParams:
     logit_bias: dict[int, float] | None = None   # {token id: added to its logit}
     allowed_token_ids: list[int] | None = None   # only these tokens can be sampled
     structured_outputs: StructuredOutputsParams | None = None  # grammar-constrained output
+    bad_words: list[str] | None = None   # words whose last token is banned after their prefix
     logprobs: int | None = None          # per output token: its log-prob + the top-N
     prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 

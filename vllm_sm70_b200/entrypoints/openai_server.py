@@ -410,7 +410,8 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           seed=body.get("seed"), ignore_eos=ignore_eos, stop_token_ids=stop_ids,
                           min_tokens=int(body.get("min_tokens", 0)), logit_bias=bias or None,
                           allowed_token_ids=None if allowed is None else [int(t) for t in allowed],
-                          structured_outputs=guided)
+                          structured_outputs=guided,
+                          bad_words=list(body["bad_words"]) if body.get("bad_words") else None)
 
 
 def _forced_tool_schema(body: dict):
