@@ -439,3 +439,36 @@ def test_stop_token_retires_request_early(monkeypatch):
     monkeypatch.setenv("VLLM_B200_STOP_CHECK_STEPS", "0")
     off = llm.generate([prompts[0]], sp)[0]
     assert off.output_token_ids == t0[: k + 1] and llm.last_stats.decode_steps == 39
+
+
+def test_truncate_prompt_and_text_options():
+    """``truncate_prompt_tokens`` serves the prompt's last k tokens (offline
+    and online); ``detokenize=False`` leaves the text empty;
+    ``skip_special_tokens`` reaches the tokenizer."""
+    calls = []
+
+    class Tok:
+        def encode(self, text):
+            return [ord(c) - 96 for c in text]
+
+        def decode(self, ids, skip_special_tokens=True):
+            calls.append(skip_special_tokens)
+            return "".join(chr(97 + i % 26) for i in ids)
+
+    llm = _llm(tokenizer=Tok())
+    g = torch.Generator().manual_seed(9)
+    p = torch.randint(0, 512, (40,), generator=g)
+    sp = SamplingParams(max_tokens=4, ignore_eos=True)
+    tail = llm.generate([p[-12:]], sp)[0]
+    cut = llm.generate([p], SamplingParams(max_tokens=4, ignore_eos=True,
+                                           truncate_prompt_tokens=12))[0]
+    assert cut.output_token_ids == tail.output_token_ids and cut.prompt_token_ids == p[-12:].tolist()
+    done = {}
+    items = [[(0, p, SamplingParams(max_tokens=4, ignore_eos=True, truncate_prompt_tokens=12))]]
+    llm.generate([], feed=lambda block: items.pop(0) if items else None,
+                 on_finish=lambda o: done.__setitem__(o.request_id, o))
+    assert done[0].output_token_ids == tail.output_token_ids
+    assert llm.generate([p], SamplingParams(max_tokens=2, detokenize=False))[0].text is None
+    calls.clear()
+    llm.generate([p], SamplingParams(max_tokens=2, skip_special_tokens=False))
+    assert calls and not any(calls)

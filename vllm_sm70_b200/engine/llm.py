@@ -660,6 +660,8 @@ class LLM:
                                        dtype=torch.int64) for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
+        prompts = [p[-sp.truncate_prompt_tokens:] if sp.truncate_prompt_tokens
+                   and sp.truncate_prompt_tokens > 0 else p for p, sp in zip(prompts, params)]
         if any(p.n > 1 for p in params) and feed is None:
             return self._generate_n(prompts, params, collect_stats, on_tokens, stream_interval)
         for p in params:
@@ -842,7 +844,10 @@ class LLM:
                                                   "allowed_token_ids with speculative decoding")
                     runner.filtering = True
                     runner.penalties = runner.penalties or _penalized(sp, bool(self.spec_k))
-                waiting.append(_Req(rid, torch.as_tensor(ids, dtype=torch.int64), sp))
+                ids = torch.as_tensor(ids, dtype=torch.int64)
+                if sp.truncate_prompt_tokens and sp.truncate_prompt_tokens > 0:
+                    ids = ids[-sp.truncate_prompt_tokens:]
+                waiting.append(_Req(rid, ids, sp))
             return True
 
         feed_open = online
@@ -1063,10 +1068,15 @@ class LLM:
         self.last_stats = stats
         tok = self.tokenizer if outs else None
         if tok is not None:  # vLLM's RequestOutput.text (and stop strings)
-            dec = lambda ids: tok.decode(ids, skip_special_tokens=True)  # noqa: E731
             for o, r in zip(outs, reqs):
-                o.output_token_ids, o.text, hit = _match_stop_string(o.output_token_ids,
-                                                                     r.params, dec)
+                sp = r.params
+                if not sp.detokenize and not sp.stop:
+                    continue
+                dec = lambda ids, skip=sp.skip_special_tokens: tok.decode(  # noqa: E731
+                    ids, skip_special_tokens=skip)
+                o.output_token_ids, o.text, hit = _match_stop_string(o.output_token_ids, sp, dec)
+                if not sp.detokenize:
+                    o.text = None
                 if hit is not None:
                     o.finish_reason, o.stop_reason = "stop", hit
         elif any(r.params.stop for r in reqs):

@@ -28,6 +28,9 @@ class SamplingParams:
     allowed_token_ids: list[int] | None = None   # only these tokens can be sampled
     structured_outputs: StructuredOutputsParams | None = None  # grammar-constrained output
     bad_words: list[str] | None = None   # words whose last token is banned after their prefix
+    truncate_prompt_tokens: int | None = None  # keep only the prompt's last k tokens
+    detokenize: bool = True              # fill RequestOutput.text (needs a tokenizer)
+    skip_special_tokens: bool = True     # ... without special tokens
     logprobs: int | None = None          # per output token: its log-prob + the top-N
     prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 

@@ -411,7 +411,9 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           min_tokens=int(body.get("min_tokens", 0)), logit_bias=bias or None,
                           allowed_token_ids=None if allowed is None else [int(t) for t in allowed],
                           structured_outputs=guided,
-                          bad_words=list(body["bad_words"]) if body.get("bad_words") else None)
+                          bad_words=list(body["bad_words"]) if body.get("bad_words") else None,
+                          truncate_prompt_tokens=body.get("truncate_prompt_tokens"),
+                          skip_special_tokens=bool(body.get("skip_special_tokens", True)))
 
 
 def _forced_tool_schema(body: dict):
