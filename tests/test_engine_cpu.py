@@ -472,3 +472,53 @@ def test_truncate_prompt_and_text_options():
     calls.clear()
     llm.generate([p], SamplingParams(max_tokens=2, skip_special_tokens=False))
     assert calls and not any(calls)
+
+
+def _dense_beam_search(model, prompt, W, n, eos, lp_pen=1.0):
+    """Independent beam search on a dense forward (vLLM's scoring rule)."""
+    from ._llama_ref import llama_logits
+
+    def score(toks, cum):
+        k = len(toks) - (1 if toks[-1] == eos else 0)
+        return cum / (k ** lp_pen)
+
+    beams, done = [(prompt.tolist(), 0.0)], []
+    for _ in range(n):
+        cands = []
+        for toks, cum in beams:
+            lg = llama_logits(model, torch.tensor(toks))[-1].double()
+            lsm = lg - torch.logsumexp(lg, 0)
+            v, i = lsm.topk(2 * W)
+            for lp, t in zip(v.tolist(), i.tolist()):
+                (done if t == eos else cands).append((toks + [t], cum + lp))
+        beams = sorted(cands, key=lambda b: score(*b), reverse=True)[:W]
+    return [b[0] for b in sorted(done + beams, key=lambda b: score(*b), reverse=True)[:W]]
+
+
+def test_beam_search_matches_dense_reference():
+    """``LLM.beam_search`` keeps the beams a dense-forward beam search keeps
+    (same candidates, vLLM's length-normalised score), EOS-ended beams
+    included; beam width 1 is greedy decoding."""
+    from vllm_sm70_b200.engine import BeamSearchParams
+
+    class Tok:
+        eos_token_id = 7
+
+        def encode(self, text):
+            return [ord(c) - 96 for c in text]
+
+        def decode(self, ids, skip_special_tokens=True):
+            return "".join(chr(97 + i % 26) for i in ids)
+
+    llm = _llm(tokenizer=Tok())
+    g = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (6, 11)]
+    outs = llm.beam_search(prompts, BeamSearchParams(beam_width=3, max_tokens=5))
+    for p, o in zip(prompts, outs):
+        want = _dense_beam_search(llm.model, p, 3, 5, eos=7)
+        assert [s.tokens for s in o.sequences] == want
+        assert o.sequences[0].text == Tok().decode(want[0][p.numel():])
+    one = llm.beam_search(prompts[:1], BeamSearchParams(beam_width=1, max_tokens=4,
+                                                        ignore_eos=True))[0].sequences[0]
+    greedy = llm.generate(prompts[:1], SamplingParams(max_tokens=4, ignore_eos=True))[0]
+    assert one.tokens[prompts[0].numel():] == greedy.output_token_ids

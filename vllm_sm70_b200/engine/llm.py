@@ -551,6 +551,13 @@ class LLM:
                 raise ValueError(f"structured outputs: unsupported tokenizer ({e})") from e
         return self._grammar_compiler
 
+    def beam_search(self, prompts, params):
+        """vLLM's ``LLM.beam_search``: ``params`` a ``BeamSearchParams``;
+        one ``BeamSearchOutput`` (best ``beam_width`` sequences) per prompt."""
+        from .beam_search import beam_search
+
+        return beam_search(self, prompts, params)
+
     def get_tokenizer(self):
         """vLLM's ``LLM.get_tokenizer``."""
         return self.tokenizer
