@@ -522,3 +522,23 @@ def test_beam_search_matches_dense_reference():
                                                         ignore_eos=True))[0].sequences[0]
     greedy = llm.generate(prompts[:1], SamplingParams(max_tokens=4, ignore_eos=True))[0]
     assert one.tokens[prompts[0].numel():] == greedy.output_token_ids
+
+
+def test_priority_scheduling_admits_low_values_first():
+    """LLM(scheduling_policy="priority"): with one batch slot, requests are
+    served lowest priority value first (arrival order on ties), with the
+    same tokens as in arrival order; priority needs the policy."""
+    import pytest
+
+    order = []
+    llm = _llm(max_num_seqs=1, scheduling_policy="priority")
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, 512, (n,), generator=g) for n in (5, 9, 7, 4)]
+    sp = SamplingParams(max_tokens=3, ignore_eos=True)
+    fifo = llm.generate(prompts, sp)
+    outs = llm.generate(prompts, sp, priority=[3, 1, 3, 0],
+                        on_tokens=lambda i, ids, fin: fin and order.append(i))
+    assert order == [3, 1, 0, 2]
+    assert [o.output_token_ids for o in outs] == [o.output_token_ids for o in fifo]
+    with pytest.raises(ValueError):
+        _llm().generate(prompts, sp, priority=[0, 0, 0, 0])

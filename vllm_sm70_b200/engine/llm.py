@@ -208,13 +208,19 @@ class LLM:
                  tune_gemm: bool = True, gemm_lut_path: str | None = None,
                  speculative_k: int = 0, enable_prefix_caching: bool | None = None,
                  data_parallel_size: int = 1, enable_expert_parallel: bool = False,
-                 prefix_cache_dir: str | None = None, tokenizer=None):
+                 prefix_cache_dir: str | None = None, tokenizer=None,
+                 scheduling_policy: str = "fcfs"):
         self.cfg: ModelConfig = resolve(model)
         # tokenizer: an object with encode / decode (/ apply_chat_template), a
         # directory for transformers.AutoTokenizer, or None (then the checkpoint
         # directory's tokenizer is tried on first use)
         self._tokenizer = tokenizer
         self._grammar_compiler = None  # structured outputs (built on first use)
+        if scheduling_policy not in ("fcfs", "priority"):
+            raise ValueError(f"scheduling_policy must be fcfs or priority, not {scheduling_policy}")
+        # priority: waiting requests are admitted lowest priority value first
+        # (ties in arrival order); running requests are never preempted
+        self.scheduling_policy = scheduling_policy
         self._tokenizer_src = None  # a checkpoint directory that ships tokenizer files
         if isinstance(model, str):
             from pathlib import Path
@@ -633,7 +639,7 @@ class LLM:
     def generate(self, prompt_token_ids, sampling_params: SamplingParams | list | None = None,
                  collect_stats: bool = True, on_tokens=None,
                  stream_interval: int = 0, feed=None, on_finish=None,
-                 use_tqdm: bool = False) -> list[RequestOutput]:
+                 use_tqdm: bool = False, priority: list[int] | None = None) -> list[RequestOutput]:
         """Serve the prompts to completion; returns one output per prompt.
 
         Streaming: ``on_tokens(request_index, new_token_ids, finished)`` is
@@ -667,6 +673,14 @@ class LLM:
                                        dtype=torch.int64) for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
+        if priority is not None:
+            import dataclasses
+
+            if self.scheduling_policy != "priority":
+                raise ValueError("priority needs LLM(scheduling_policy='priority')")
+            if len(priority) != len(prompts):
+                raise ValueError("one priority per prompt")
+            params = [dataclasses.replace(sp, priority=int(q)) for sp, q in zip(params, priority)]
         prompts = [p[-sp.truncate_prompt_tokens:] if sp.truncate_prompt_tokens
                    and sp.truncate_prompt_tokens > 0 else p for p, sp in zip(prompts, params)]
         if any(p.n > 1 for p in params) and feed is None:
@@ -865,6 +879,10 @@ class LLM:
                     continue
             # ---- admission
             admitted: list[_Req] = []
+            if self.scheduling_policy == "priority" and len(waiting) > 1:
+                order = sorted(waiting, key=lambda q: q.params.priority)  # stable: arrival ties
+                waiting.clear()
+                waiting.extend(order)
             while waiting and free_slots:
                 r = waiting[0]
                 L = r.prompt.numel()

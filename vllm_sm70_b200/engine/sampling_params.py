@@ -31,6 +31,9 @@ class SamplingParams:
     truncate_prompt_tokens: int | None = None  # keep only the prompt's last k tokens
     detokenize: bool = True              # fill RequestOutput.text (needs a tokenizer)
     skip_special_tokens: bool = True     # ... without special tokens
+    # vLLM's per-request ``priority`` (lower = sooner) under
+    # LLM(scheduling_policy="priority"); generate(priority=[...]) sets it
+    priority: int = 0
     logprobs: int | None = None          # per output token: its log-prob + the top-N
     prompt_logprobs: int | None = None   # per prompt token (the first has none) + top-N
 

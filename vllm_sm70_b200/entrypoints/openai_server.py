@@ -413,7 +413,8 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
                           structured_outputs=guided,
                           bad_words=list(body["bad_words"]) if body.get("bad_words") else None,
                           truncate_prompt_tokens=body.get("truncate_prompt_tokens"),
-                          skip_special_tokens=bool(body.get("skip_special_tokens", True)))
+                          skip_special_tokens=bool(body.get("skip_special_tokens", True)),
+                          priority=int(body.get("priority", 0)))
 
 
 def _forced_tool_schema(body: dict):
