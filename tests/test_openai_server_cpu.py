@@ -96,7 +96,7 @@ def test_stop_string_and_unsupported(client):
     r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 8, "temperature": 0.0,
                                               "ignore_eos": True, "stop": ["\\u0000"]})
     assert r.status_code == 200
-    for bad in ({"n": 17}, {"n": 2, "stream": True}, {"logprobs": 21},
+    for bad in ({"n": 17}, {"logprobs": 21},
                 {"logprobs": 1, "stream": True},
                 {"stream": True, "prompt": ["a", "b"]}):
         body = {"prompt": [1, 2, 3], "max_tokens": 2, **bad}
@@ -472,3 +472,19 @@ def test_structured_output_request_fields():
     assert _params({"guided_regex": "[0-9]+"}, None).structured_outputs.regex == "[0-9]+"
     with pytest.raises(ValueError):
         _params({"response_format": {"type": "json_schema", "json_schema": {}}}, None)
+
+
+def test_stream_completion_n_samples(client):
+    """``n`` > 1 streams every sample as chunks tagged with its choice index;
+    each sample's tokens equal the unstreamed n-sample reply's."""
+    body = {"prompt": "many", "max_tokens": 11, "temperature": 1.0, "seed": 5, "n": 3,
+            "ignore_eos": True}
+    whole = client.post("/v1/completions", json=body).json()["choices"]
+    ev = _events(client, "/v1/completions", {**body, "stream": True})
+    got = {}
+    for e in ev:
+        c = e["choices"][0]
+        got.setdefault(c["index"], []).extend(c["token_ids"])
+    assert sorted(got) == [0, 1, 2]
+    assert [got[k] for k in range(3)] == [c["token_ids"] for c in whole]
+    assert sum(e["choices"][0]["finish_reason"] == "length" for e in ev) == 3

@@ -373,8 +373,8 @@ def _params(body: dict, tokenizer, chat: bool = False) -> SamplingParams:
     n = int(body.get("n", 1))
     if not 1 <= n <= MAX_N:
         raise ValueError(f"n must be in [1, {MAX_N}]")
-    if n > 1 and body.get("stream"):
-        raise ValueError("streaming serves n = 1")
+    if n > 1 and body.get("stream") and chat:
+        raise ValueError("chat streaming serves n = 1")
     if chat:
         n_lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
         prompt_lp = None
@@ -561,14 +561,17 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
         fut = batcher.submit(prompt_ids, sp)
         return await asyncio.wrap_future(fut)
 
-    def start_stream(prompt_ids, sp) -> asyncio.Queue:
+    def start_stream(prompt_ids, sp, q=None, tag=None) -> asyncio.Queue:
         """Submit a streamed request; its (new ids, finished) pieces arrive on
-        the returned queue."""
+        the returned queue -- ``q`` if given, as (tag, new ids, finished) when
+        a ``tag`` is given (several samples on one queue)."""
         loop = asyncio.get_running_loop()
-        q: asyncio.Queue = asyncio.Queue()
-        fut = batcher.submit(prompt_ids, sp,
-                             lambda ids, fin: loop.call_soon_threadsafe(q.put_nowait, (ids, fin)))
+        q = asyncio.Queue() if q is None else q
+        item = (lambda ids, fin: (ids, fin)) if tag is None else (lambda ids, fin: (tag, ids, fin))
+        fut = batcher.submit(prompt_ids, sp, lambda ids, fin: loop.call_soon_threadsafe(
+            q.put_nowait, item(ids, fin)))
         q.rid = getattr(fut, "rid", None)
+        q.rids = getattr(q, "rids", []) + [q.rid]
         return q
 
     async def guarded(gen, q):
@@ -580,39 +583,43 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
                 yield item
             done = True
         finally:
-            if not done and q.rid is not None:
-                batcher.abort(q.rid)
+            for rid in (getattr(q, "rids", None) or [q.rid]) if not done else []:
+                if rid is not None:
+                    batcher.abort(rid)
 
-    def stream_completion(prompt_ids, sp, stop, usage=False):
-        q = start_stream(prompt_ids, sp)
+    def stream_completion(prompt_ids, sp, stop, usage=False, n=1):
+        """Server-sent events of one prompt's ``n`` samples; each chunk is
+        one sample's new tokens, tagged with the sample's choice index."""
+        q: asyncio.Queue = asyncio.Queue()
+        for k, spk in enumerate(_samples(sp, n)):
+            start_stream(prompt_ids, spk, q, k)
         rid, made = f"cmpl-{uuid.uuid4().hex}", int(time.time())
 
         async def events():
-            ts = _TextStream(decode) if tokenizer is not None else None
-            hit = stopped = False
-            n_gen = 0
-            while True:
-                ids, fin = await q.get()
+            ts = [_TextStream(decode) if tokenizer is not None else None for _ in range(n)]
+            hit, stopped = [False] * n, [False] * n
+            n_gen, open_ = 0, n
+            while open_:
+                k, ids, fin = await q.get()
                 if ids is None:
                     yield _sse({"error": {"message": "generation failed"}})
                     break
                 if ids and ids[-1] in sp.stop_token_ids:
-                    stopped = True
+                    stopped[k] = True
                 text = None
-                if ts is not None:
-                    text = "" if hit else ts.push(ids, fin)
-                    if not hit and stop:
-                        cut, hit = _apply_stop_strings(ts.sent, stop)
-                        if hit:  # drop what follows the stop string
-                            text = text[: max(0, len(text) - (len(ts.sent) - len(cut)))]
-                choice = {"index": 0, "text": text, "token_ids": ids,
-                          "finish_reason": ("stop" if (stopped or hit) else "length") if fin
-                          else None}
+                if ts[k] is not None:
+                    text = "" if hit[k] else ts[k].push(ids, fin)
+                    if not hit[k] and stop:
+                        cut, hit[k] = _apply_stop_strings(ts[k].sent, stop)
+                        if hit[k]:  # drop what follows the stop string
+                            text = text[: max(0, len(text) - (len(ts[k].sent) - len(cut)))]
+                choice = {"index": k, "text": text, "token_ids": ids,
+                          "finish_reason": ("stop" if (stopped[k] or hit[k]) else "length")
+                          if fin else None}
                 yield _sse({"id": rid, "object": "text_completion", "created": made,
                             "model": model_name, "choices": [choice]})
                 n_gen += len(ids)
-                if fin:
-                    break
+                open_ -= bool(fin)
             if usage:
                 yield _sse({"id": rid, "object": "text_completion", "created": made,
                             "model": model_name, "choices": [],
@@ -694,7 +701,8 @@ def build_app(llm, tokenizer=None, model_name: str = "model", reasoning_parser: 
             if len(ids) != 1:
                 raise HTTPException(400, "streaming serves one prompt per request")
             return stream_completion(ids[0], sp, body.get("stop"),
-                                     bool((body.get("stream_options") or {}).get("include_usage")))
+                                     bool((body.get("stream_options") or {}).get("include_usage")),
+                                     int(body.get("n", 1)))
         n = int(body.get("n", 1))
         jobs = [(pi, spj) for pi in range(len(ids)) for spj in _samples(sp, n)]
         try:
