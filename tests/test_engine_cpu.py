@@ -542,3 +542,23 @@ def test_priority_scheduling_admits_low_values_first():
     assert [o.output_token_ids for o in outs] == [o.output_token_ids for o in fifo]
     with pytest.raises(ValueError):
         _llm().generate(prompts, sp, priority=[0, 0, 0, 0])
+
+
+def test_vllm_prompt_dicts():
+    """vLLM's TokensPrompt / TextPrompt dicts are accepted, alone or in a list."""
+    from vllm.inputs import TokensPrompt
+
+    class Tok:
+        def encode(self, text):
+            return [ord(c) - 96 for c in text]
+
+        def decode(self, ids, skip_special_tokens=True):
+            return "".join(chr(97 + i % 26) for i in ids)
+
+    llm = _llm(tokenizer=Tok())
+    sp = SamplingParams(max_tokens=3, ignore_eos=True)
+    ids = [5, 9, 14, 3]
+    want = llm.generate([ids], sp)[0].output_token_ids
+    assert llm.generate(TokensPrompt(prompt_token_ids=ids), sp)[0].output_token_ids == want
+    both = llm.generate([{"prompt_token_ids": ids}, {"prompt": "eint"}], sp)
+    assert both[0].output_token_ids == want and both[1].prompt_token_ids == [5, 9, 14, 20]

@@ -52,14 +52,14 @@ def beam_score(tokens: list[int], cum_logprob: float, eos: int | None,
 
 
 def beam_search(llm, prompts, params: BeamSearchParams) -> list[BeamSearchOutput]:
-    """``prompts``: token-id lists / tensors or strings (needs a tokenizer)."""
+    """``prompts``: token-id lists / tensors, strings (needs a tokenizer) or
+    vLLM's prompt dicts."""
     W = int(params.beam_width)
     if W < 1 or params.max_tokens < 1:
         raise ValueError("beam_width and max_tokens must be >= 1")
     tok = llm.tokenizer
     eos = None if params.ignore_eos or tok is None else getattr(tok, "eos_token_id", None)
-    starts = [list(llm._encode(p)) if isinstance(p, str) else [int(t) for t in p]
-              for p in prompts]
+    starts = [[int(t) for t in llm._prompt_ids(p)] for p in prompts]
     beams = [[BeamSearchSequence(list(s))] for s in starts]
     done: list[list[BeamSearchSequence]] = [[] for _ in starts]
     sp = SamplingParams(max_tokens=1, logprobs=2 * W, temperature=params.temperature,

@@ -557,6 +557,18 @@ class LLM:
                 raise ValueError(f"structured outputs: unsupported tokenizer ({e})") from e
         return self._grammar_compiler
 
+    def _prompt_ids(self, p):
+        """Token ids of one prompt: ids, text, or vLLM's prompt dicts
+        (``TokensPrompt`` {"prompt_token_ids": ...} / ``TextPrompt``
+        {"prompt": ...})."""
+        if isinstance(p, dict):
+            if "prompt_token_ids" in p:
+                return list(p["prompt_token_ids"])
+            if "prompt" in p:
+                return self._encode(p["prompt"])
+            raise ValueError("a prompt dict needs prompt_token_ids or prompt")
+        return self._encode(p) if isinstance(p, str) else p
+
     def beam_search(self, prompts, params):
         """vLLM's ``LLM.beam_search``: ``params`` a ``BeamSearchParams``;
         one ``BeamSearchOutput`` (best ``beam_width`` sequences) per prompt."""
@@ -662,15 +674,15 @@ class LLM:
         the same requests in the same calls (rank 0 broadcasts them)."""
         if sampling_params is None:
             sampling_params = SamplingParams()
-        if isinstance(prompt_token_ids, str) or (
+        if isinstance(prompt_token_ids, (str, dict)) or (
                 isinstance(prompt_token_ids, (list, tuple)) and prompt_token_ids
                 and isinstance(prompt_token_ids[0], int)):
-            prompt_token_ids = [prompt_token_ids]  # one prompt (text or token ids)
+            prompt_token_ids = [prompt_token_ids]  # one prompt (text, token ids or a dict)
         if isinstance(prompt_token_ids, torch.Tensor):
             prompts = [row for row in prompt_token_ids.to(torch.int64)]
         else:
-            prompts = [torch.as_tensor(self._encode(p) if isinstance(p, str) else p,
-                                       dtype=torch.int64) for p in prompt_token_ids]
+            prompts = [torch.as_tensor(self._prompt_ids(p), dtype=torch.int64)
+                       for p in prompt_token_ids]
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
         if priority is not None:
