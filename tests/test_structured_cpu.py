@@ -180,3 +180,24 @@ def test_server_response_format_and_forced_tool_choice(monkeypatch):
         bad = c.post("/v1/chat/completions", json={**body, "tools": tools, "tool_choice": {
             "type": "function", "function": {"name": "nope"}}})
         assert bad.status_code == 400
+
+
+def test_llm_chat_template_options():
+    """LLM.chat takes vLLM's chat_template, add_generation_prompt and
+    continue_final_message (the reply extends the last assistant message)."""
+    llm = _llm()
+    tpl = ("{% for m in messages %}<{{ m['role'] }}>{{ m['content'] }}{% endfor %}"
+           "{% if add_generation_prompt %}<assistant>{% endif %}")
+    sp = SamplingParams(max_tokens=2, ignore_eos=True)
+    msgs = [{"role": "user", "content": "hi"}]
+    enc = lambda t: TOK.encode(t, add_special_tokens=False)  # noqa: E731
+    o = llm.chat(msgs, sp, chat_template=tpl)[0]
+    assert o.prompt_token_ids == enc("<user>hi<assistant>")
+    o = llm.chat(msgs, sp, chat_template=tpl, add_generation_prompt=False)[0]
+    assert o.prompt_token_ids == enc("<user>hi")
+    cont = msgs + [{"role": "assistant", "content": "Sure"}]
+    o = llm.chat(cont, sp, chat_template=tpl, add_generation_prompt=False,
+                 continue_final_message=True)[0]
+    assert o.prompt_token_ids == enc("<user>hi<assistant>Sure")
+    with pytest.raises(ValueError):
+        llm.chat(cont, sp, chat_template=tpl, continue_final_message=True)

@@ -413,7 +413,9 @@ class LLM:
         return list(tok.encode(text))
 
     def chat(self, messages, sampling_params: SamplingParams | None = None,
-             chat_template_kwargs: dict | None = None, tools=None) -> list[RequestOutput]:
+             chat_template_kwargs: dict | None = None, tools=None, use_tqdm: bool = False,
+             chat_template: str | None = None, add_generation_prompt: bool = True,
+             continue_final_message: bool = False) -> list[RequestOutput]:
         """vLLM's ``LLM.chat``: one conversation (a list of ``{"role",
         "content"}`` messages) or a list of them, through the tokenizer's
         chat template with the generation prompt appended."""
@@ -424,7 +426,13 @@ class LLM:
         kw = dict(chat_template_kwargs or {})
         if tools:
             kw["tools"] = tools
-        ids = [chat_token_ids(tok, c, add_generation_prompt=True, **kw)
+        if chat_template is not None:
+            kw["chat_template"] = chat_template
+        if continue_final_message:  # the reply extends the last (assistant) message
+            if add_generation_prompt:
+                raise ValueError("continue_final_message needs add_generation_prompt=False")
+            kw["continue_final_message"] = True
+        ids = [chat_token_ids(tok, c, add_generation_prompt=add_generation_prompt, **kw)
                for c in convs]
         return self.generate(ids, sampling_params)
 
